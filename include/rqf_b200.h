@@ -1,0 +1,171 @@
+/*
+ * rqf_b200.h — C ABI of the B200 (sm_100a) backend for the RQF complex
+ * linear-recurrence scan family.
+ *
+ * Every entry point takes raw device pointers, sizes and a CUDA stream, never
+ * allocates or frees device memory, and returns an int status (RQF_OK == 0).
+ * Complex tensors are interleaved re/im float32 (the memory layout of a
+ * contiguous torch.complex64 tensor, i.e. torch.view_as_real).  Per-channel
+ * coefficients (c1, c2, tap0, tap1) are complex (F,) vectors.
+ *
+ * Gradients follow PyTorch's conjugate-Wirtinger convention, e.g.
+ *   grad_c1 = sum_{b,t} conj(y[t-1]) * g[t],   grad_u = conj(c2) * g.
+ *
+ * Two memory layouts are served:
+ *   BTF  (batch, time, filters): filters innermost — the layout of
+ *        rqf_models/ops/chunked_scan_kernel.py:_triton_chunked_scan (:340)
+ *        and _triton_chunked_scan_prospective (:506).  No permutes are made.
+ *   FBT  (filters, batch, time): time innermost — the layout of
+ *        rqf_models/ops/fbt_scan_kernel.py:fbt_prospective_scan (:332),
+ *        fbt_recompute_scan (:667) and the selective kernels
+ *        rqf_models/ops/selective_scan_kernel.py (:491, :517).
+ *
+ * Saved context.  Forward kernels write one complex "carry" per (row, tile):
+ * the recurrence state entering that tile.  Backward kernels recompute the
+ * states from those carries instead of reading a saved output.  The caller
+ * owns the carry buffer (rqf_*_carry_count complex entries) between forward
+ * and backward.
+ *
+ * Scratch.  Forward and full-BPTT backward kernels chain tiles of a row with a
+ * decoupled look-back; they need a caller-provided scratch buffer of
+ * rqf_*_scratch_bytes() bytes (16-byte aligned), which the entry point clears
+ * with cudaMemsetAsync on the given stream before the launch.  Scratch may be
+ * reused by the next call on the same stream.
+ *
+ * Errors.  A look-back wait is bounded; when it runs out the kernel latches
+ * RQF_ERR_LOOKBACK_TIMEOUT into a per-device error word and returns.  Read it
+ * with rqf_read_device_error (synchronises the stream).
+ */
+#ifndef RQF_B200_H
+#define RQF_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *rqf_stream_t; /* identical to cudaStream_t */
+
+enum rqf_status {
+  RQF_OK = 0,
+  RQF_ERR_SHAPE = 1,            /* negative / inconsistent sizes            */
+  RQF_ERR_ALIGN = 2,            /* pointer alignment requirement violated   */
+  RQF_ERR_LOOKBACK_TIMEOUT = 3, /* bounded cross-tile wait gave up          */
+  RQF_ERR_LAUNCH = 4,           /* CUDA launch / memset error               */
+  RQF_ERR_ARGUMENT = 5,         /* null pointer or unsupported option       */
+  RQF_ERR_CAPACITY = 6          /* size beyond a fixed internal maximum     */
+};
+
+/* ---- library information -------------------------------------------- */
+int rqf_abi_version(void);
+const char *rqf_status_string(int status);
+
+/* Copy (and optionally clear) the device error word of the current device.
+ * Synchronises `stream`. */
+int rqf_read_device_error(int *out_code, int clear, rqf_stream_t stream);
+
+/* ---- sizes of saved context and scratch ------------------------------ */
+/* BTF kernels: tiles along time, rows = batch * filters. */
+int64_t rqf_btf_num_tiles(int64_t time);
+int64_t rqf_btf_carry_count(int64_t batch, int64_t time, int64_t filters);
+size_t rqf_btf_scratch_bytes(int64_t batch, int64_t time, int64_t filters);
+/* FBT kernels: rows = filters * batch, tiles along time. */
+int64_t rqf_fbt_num_tiles(int64_t time);
+int64_t rqf_fbt_carry_count(int64_t filters, int64_t batch, int64_t time);
+size_t rqf_fbt_scratch_bytes(int64_t filters, int64_t batch, int64_t time);
+
+/* ---- diagonal scan, (B,T,F) layout ----------------------------------- *
+ * Replaces rqf_models/ops/chunked_scan_kernel.py:_chunked_scan_forward_raw
+ * (:217) / _chunked_scan_kernel (:60):  y[t] = c1*y[t-1] + c2*u[t], y[-1]=0.
+ * u is complex (B,T,F) or, with u_is_real != 0, float32 (B,T,F) — the real
+ * input that rqf_models/ops/scan.py:sequential_scan (:290, :366) promotes to
+ * complex before the kernel; the result is identical. */
+int rqf_chunked_scan_forward(const float *c1, const float *c2, const void *u,
+                             int u_is_real, float *y, float *carries,
+                             void *scratch, int64_t batch, int64_t time,
+                             int64_t filters, rqf_stream_t stream);
+
+/* Replaces chunked_scan_kernel.py:_chunked_scan_backward_raw (:252) /
+ * _chunked_scan_backward_kernel (:122): g[t] = gy[t] + conj(c1) g[t+1];
+ * grad_u = conj(c2) g (real part only when u_is_real);
+ * grad_c1 = sum conj(y[t-1]) g[t];  grad_c2 = sum conj(u[t]) g[t].
+ * y[t-1] is recomputed from `carries`; grad_c1/grad_c2 are overwritten. */
+int rqf_chunked_scan_backward(const float *c1, const float *c2, const void *u,
+                              int u_is_real, const float *carries,
+                              const float *grad_y, void *grad_u, float *grad_c1,
+                              float *grad_c2, void *scratch, int64_t batch,
+                              int64_t time, int64_t filters,
+                              rqf_stream_t stream);
+
+/* ---- two-tap prospective scan, (B,T,F) layout ------------------------ *
+ * Replaces chunked_scan_kernel.py:_chunked_prospective_forward_raw (:442) /
+ * _chunked_prospective_kernel (:374):
+ *   y[t] = c1*y[t-1] + tap0*x[t] + tap1*x[t-1],  x[-1] = 0. */
+int rqf_chunked_prospective_forward(const float *c1, const float *tap0,
+                                    const float *tap1, const float *x, float *y,
+                                    float *carries, void *scratch,
+                                    int64_t batch, int64_t time,
+                                    int64_t filters, rqf_stream_t stream);
+
+/* Replaces _ChunkedProspectiveScanFunction.backward
+ * (chunked_scan_kernel.py:489-503), fused into one kernel:
+ *   grad_x[t] = conj(tap0) g[t] + conj(tap1) g[t+1];  grad_c1, grad_tap0,
+ *   grad_tap1 = sums of conj(y[t-1]) g, conj(x[t]) g, conj(x[t-1]) g. */
+int rqf_chunked_prospective_backward(
+    const float *c1, const float *tap0, const float *tap1, const float *x,
+    const float *carries, const float *grad_y, float *grad_x, float *grad_c1,
+    float *grad_tap0, float *grad_tap1, void *scratch, int64_t batch,
+    int64_t time, int64_t filters, rqf_stream_t stream);
+
+/* ---- two-tap prospective scan, (F,B,T) layout ------------------------ *
+ * Replaces fbt_scan_kernel.py:_fbt_prospective_kernel (:34) and
+ * _fbt_recompute_forward_kernel (:360).  Writes split-ReLU(y) when
+ * fuse_act != 0 (relu(Re y) + i relu(Im y)), else the raw state y. */
+int rqf_fbt_prospective_forward(const float *c1, const float *tap0,
+                                const float *tap1, const float *z, float *out,
+                                float *carries, void *scratch, int64_t filters,
+                                int64_t batch, int64_t time, int fuse_act,
+                                rqf_stream_t stream);
+
+/* Replaces fbt_scan_kernel.py:_fbt_prospective_backward_kernel (:113) and
+ * _fbt_recompute_backward_kernel (:439).  grad_out is the cotangent of the
+ * forward's output (of the split-ReLU output when fuse_act != 0; the mask is
+ * sign(y) > 0 per component, recomputed).  Writes grad_z and overwrites
+ * grad_c1 / grad_tap0 / grad_tap1 (complex (F,)). */
+int rqf_fbt_prospective_backward(const float *c1, const float *tap0,
+                                 const float *tap1, const float *z,
+                                 const float *carries, const float *grad_out,
+                                 float *grad_z, float *grad_c1,
+                                 float *grad_tap0, float *grad_tap1,
+                                 void *scratch, int64_t filters, int64_t batch,
+                                 int64_t time, int fuse_act,
+                                 rqf_stream_t stream);
+
+/* ---- TBPTT(1) two-tap surrogate backward ----------------------------- *
+ * The forward value of the reference's TBPTT(1) path equals the exact scan
+ * (rqf_models/backbones/rqf/block.py:_scan_two_tap_with_grad_mode :904-954),
+ * so the forward is rqf_chunked_prospective_forward (layout 0, BTF) or
+ * rqf_fbt_prospective_forward (layout 1, FBT).  This replaces the pointwise
+ * autograd of the one-step rebuild  C1*h[t-1].detach() + tap0*z[t] +
+ * tap1*zw[t-1]  (block.py:946-954) with one kernel, no temporal scan:
+ *   g        = grad_out (masked by split-ReLU'(y) when fuse_act)
+ *   grad_z   = conj(tap0) g[t]
+ *   grad_zw  = conj(tap1) g[t+1]  (cotangent of the lag source zw = z values)
+ *   grad_c1  = sum conj(y[t-1]) g[t], grad_tap0 = sum conj(z[t]) g[t],
+ *   grad_tap1 = sum conj(z[t-1]) g[t].
+ * dims = {batch, time, filters} for layout 0, {filters, batch, time} for 1. */
+int rqf_tbptt1_two_tap_backward(int layout, const float *c1, const float *tap0,
+                                const float *tap1, const float *z,
+                                const float *carries, const float *grad_out,
+                                float *grad_z, float *grad_zw, float *grad_c1,
+                                float *grad_tap0, float *grad_tap1,
+                                void *scratch, int64_t d0, int64_t d1,
+                                int64_t d2, int fuse_act, rqf_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RQF_B200_H */

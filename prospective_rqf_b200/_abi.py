@@ -1,0 +1,104 @@
+"""ctypes binding of librqf_b200.so (declarations: include/rqf_b200.h).
+
+This is the product's only route to the GPU kernels.  Loading fails loudly
+when the library is missing; there is no CPU fallback anywhere in the package.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import torch
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "librqf_b200.so"
+
+_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+_sz = ctypes.c_size_t
+
+# name -> (restype, argtypes); mirrors include/rqf_b200.h exactly.
+SIGNATURES: dict[str, tuple] = {
+    "rqf_abi_version": (_int, []),
+    "rqf_status_string": (ctypes.c_char_p, [_int]),
+    "rqf_read_device_error": (_int, [ctypes.POINTER(_int), _int, _p]),
+    "rqf_btf_num_tiles": (_i64, [_i64]),
+    "rqf_btf_carry_count": (_i64, [_i64, _i64, _i64]),
+    "rqf_btf_scratch_bytes": (_sz, [_i64, _i64, _i64]),
+    "rqf_fbt_num_tiles": (_i64, [_i64]),
+    "rqf_fbt_carry_count": (_i64, [_i64, _i64, _i64]),
+    "rqf_fbt_scratch_bytes": (_sz, [_i64, _i64, _i64]),
+    "rqf_chunked_scan_forward": (_int, [_p, _p, _p, _int, _p, _p, _p, _i64, _i64, _i64, _p]),
+    "rqf_chunked_scan_backward": (
+        _int, [_p, _p, _p, _int, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p]),
+    "rqf_chunked_prospective_forward": (_int, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p]),
+    "rqf_chunked_prospective_backward": (
+        _int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p]),
+    "rqf_fbt_prospective_forward": (
+        _int, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
+    "rqf_fbt_prospective_backward": (
+        _int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
+    "rqf_tbptt1_two_tap_backward": (
+        _int, [_int, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
+}
+
+_LIB = None
+
+
+class RQFError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+
+def load() -> ctypes.CDLL:
+    """Load librqf_b200.so (raises if it was not built)."""
+    global _LIB
+    if _LIB is None:
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with prospective_rqf_b200._build.build() "
+                "(the B200 backend has no CPU fallback)")
+        lib = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = lib
+    return _LIB
+
+
+def status_string(code: int) -> str:
+    return load().rqf_status_string(int(code)).decode()
+
+
+def check(code: int, what: str) -> None:
+    if code != 0:
+        raise RQFError(f"rqf_b200 {what} failed: {status_string(code)} (status {code})")
+
+
+def ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_of(t: torch.Tensor):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def read_device_error(device=None, clear: bool = True) -> int:
+    """Return (and by default clear) the device error word; synchronises."""
+    lib = load()
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    code = _int(0)
+    with torch.cuda.device(dev):
+        st = lib.rqf_read_device_error(ctypes.byref(code), int(clear),
+                                       ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream))
+    check(st, "rqf_read_device_error")
+    return int(code.value)
+
+
+def check_device_errors(device=None) -> None:
+    """Raise if any kernel latched an error (e.g. a bounded look-back wait ran out)."""
+    code = read_device_error(device, clear=True)
+    if code != 0:
+        raise RQFError(f"rqf_b200 device error: {status_string(code)} (status {code})")

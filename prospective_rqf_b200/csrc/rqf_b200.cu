@@ -1,0 +1,433 @@
+// C-ABI entry points of librqf_b200.so (declared in include/rqf_b200.h).
+//
+// The entry points validate sizes and alignment, clear the look-back part of
+// the caller's scratch with cudaMemsetAsync, pick the kernel instantiation and
+// launch on the caller's stream.  Nothing here allocates device memory.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/rqf_b200.h"
+#include "btf_scan.cuh"
+#include "fbt_scan.cuh"
+#include "reduce.cuh"
+
+using namespace rqf;
+
+namespace {
+
+constexpr int kAbiVersion = 1;
+constexpr int64_t kMaxTickets = 0x7fffffffLL;
+
+// BTF launch shapes: the forward uses 8 warps x 16 steps, the backward
+// 16 warps x 8 steps; both tile 128 time steps so they share the carries.
+constexpr int kBtfFwdWarps = 8, kBtfFwdK = 16;
+constexpr int kBtfBwdWarps = 16, kBtfBwdK = 8;
+static_assert(kBtfFwdWarps * kBtfFwdK == kBtfTile, "BTF forward tile");
+static_assert(kBtfBwdWarps * kBtfBwdK == kBtfTile, "BTF backward tile");
+
+inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+inline size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct Scratch {
+  size_t flags_off, flags_bytes, partials_off, total;
+};
+
+inline Scratch scratch_layout(int64_t rows, int64_t ntiles) {
+  Scratch s;
+  s.flags_bytes = (size_t)rows * (size_t)ntiles * 2 * sizeof(u64);
+  const size_t partial_bytes = (size_t)rows * (size_t)ntiles * 3 * sizeof(float2);
+  s.flags_off = 256;  // [0, 256): ticket counter
+  s.partials_off = s.flags_off + round256(s.flags_bytes);
+  s.total = s.partials_off + round256(partial_bytes);
+  return s;
+}
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+inline int launch_status() {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? RQF_OK : RQF_ERR_LAUNCH;
+}
+
+inline int zero_complex(float *p, int64_t n, cudaStream_t s) {
+  if (!p || n <= 0) return RQF_OK;
+  return cudaMemsetAsync(p, 0, (size_t)n * 2 * sizeof(float), s) == cudaSuccess ? RQF_OK
+                                                                               : RQF_ERR_LAUNCH;
+}
+
+inline int clear_lookback(void *scratch, const Scratch &lay, cudaStream_t s) {
+  return cudaMemsetAsync(scratch, 0, lay.flags_off + lay.flags_bytes, s) == cudaSuccess
+             ? RQF_OK
+             : RQF_ERR_LAUNCH;
+}
+
+template <typename T>
+inline T *at(void *base, size_t off) {
+  return reinterpret_cast<T *>(static_cast<char *>(base) + off);
+}
+
+// ------------------------------------------------------------- FBT
+int fbt_dims_ok(int64_t F, int64_t B, int64_t T) {
+  if (F < 0 || B < 0 || T < 0) return RQF_ERR_SHAPE;
+  if (B > 0x7fffffffLL) return RQF_ERR_SHAPE;
+  if (F * B > 0 && ceil_div(T, kFbtTile) * F * B > kMaxTickets) return RQF_ERR_SHAPE;
+  return RQF_OK;
+}
+
+FbtArgs fbt_args(const float *c1, const float *tap0, const float *tap1, const float *z,
+                 const float *gout, float *out, float *out2, float *carries, void *scratch,
+                 int64_t F, int64_t B, int64_t T) {
+  FbtArgs a;
+  a.c1 = reinterpret_cast<const float2 *>(c1);
+  a.tap0 = reinterpret_cast<const float2 *>(tap0);
+  a.tap1 = reinterpret_cast<const float2 *>(tap1);
+  a.z = reinterpret_cast<const float2 *>(z);
+  a.gout = reinterpret_cast<const float2 *>(gout);
+  a.out = reinterpret_cast<float2 *>(out);
+  a.out2 = reinterpret_cast<float2 *>(out2);
+  a.carries = reinterpret_cast<float2 *>(carries);
+  a.rows = F * B;
+  a.T = T;
+  a.batch = (int)B;
+  a.ntiles = (int)ceil_div(T, kFbtTile);
+  a.log2L = kFbtLog2Tile;
+  const Scratch lay = scratch_layout(a.rows, a.ntiles);
+  a.ticket = at<unsigned>(scratch, 0);
+  a.flags = at<u64>(scratch, lay.flags_off);
+  a.partials = at<float2>(scratch, lay.partials_off);
+  return a;
+}
+
+// ------------------------------------------------------------- BTF
+int btf_dims_ok(int64_t B, int64_t T, int64_t F) {
+  if (B < 0 || T < 0 || F < 0) return RQF_ERR_SHAPE;
+  if (B > 0 && F > 0 && ceil_div(T, kBtfTile) * B * ceil_div(F, 32) > kMaxTickets)
+    return RQF_ERR_SHAPE;
+  return RQF_OK;
+}
+
+BtfArgs btf_args(const float *c1, const float *c2, const float *tap1, const void *x,
+                 const float *gout, void *out, float *out2, float *carries, void *scratch,
+                 int64_t B, int64_t T, int64_t F) {
+  BtfArgs a;
+  a.c1 = reinterpret_cast<const float2 *>(c1);
+  a.c2 = reinterpret_cast<const float2 *>(c2);
+  a.tap1 = reinterpret_cast<const float2 *>(tap1);
+  a.x = x;
+  a.gout = reinterpret_cast<const float2 *>(gout);
+  a.out = out;
+  a.out2 = reinterpret_cast<float2 *>(out2);
+  a.carries = reinterpret_cast<float2 *>(carries);
+  a.B = B;
+  a.T = T;
+  a.F = F;
+  a.nfb = (int)ceil_div(F, 32);
+  a.ntiles = (int)ceil_div(T, kBtfTile);
+  a.log2L = kBtfLog2Tile;
+  const Scratch lay = scratch_layout(B * F, a.ntiles);
+  a.ticket = at<unsigned>(scratch, 0);
+  a.flags = at<u64>(scratch, lay.flags_off);
+  a.partials = at<float2>(scratch, lay.partials_off);
+  return a;
+}
+
+int btf_forward(int drive, const float *c1, const float *c2, const float *tap1, const void *x,
+                float *y, float *carries, void *scratch, int64_t B, int64_t T, int64_t F,
+                cudaStream_t stream) {
+  int st = btf_dims_ok(B, T, F);
+  if (st != RQF_OK) return st;
+  if (B == 0 || T == 0 || F == 0) return RQF_OK;
+  if (!c1 || !c2 || !x || !y || !carries || !scratch || (drive == kTwoTap && !tap1))
+    return RQF_ERR_ARGUMENT;
+  if (!aligned(c1, 8) || !aligned(c2, 8) || !aligned(y, 8) || !aligned(carries, 8) ||
+      !aligned(scratch, 16) || !aligned(x, drive == kReal ? 4 : 8) ||
+      (tap1 && !aligned(tap1, 8)))
+    return RQF_ERR_ALIGN;
+  BtfArgs a = btf_args(c1, c2, tap1, x, nullptr, y, nullptr, carries, scratch, B, T, F);
+  const Scratch lay = scratch_layout(B * F, a.ntiles);
+  if ((st = clear_lookback(scratch, lay, stream)) != RQF_OK) return st;
+  const unsigned grid = (unsigned)(B * a.nfb * a.ntiles);
+  const int nt = kBtfFwdWarps * 32;
+  if (drive == kReal)
+    btf_fwd_kernel<kBtfFwdWarps, kBtfFwdK, kReal><<<grid, nt, 0, stream>>>(a);
+  else if (drive == kPlain)
+    btf_fwd_kernel<kBtfFwdWarps, kBtfFwdK, kPlain><<<grid, nt, 0, stream>>>(a);
+  else
+    btf_fwd_kernel<kBtfFwdWarps, kBtfFwdK, kTwoTap><<<grid, nt, 0, stream>>>(a);
+  return launch_status();
+}
+
+int btf_backward(int drive, const float *c1, const float *c2, const float *tap1, const void *x,
+                 const float *carries, const float *gy, void *gx, float *o0, float *o1,
+                 float *o2, void *scratch, int64_t B, int64_t T, int64_t F,
+                 cudaStream_t stream) {
+  int st = btf_dims_ok(B, T, F);
+  if (st != RQF_OK) return st;
+  if (F == 0) return RQF_OK;
+  if (B == 0 || T == 0) {
+    if ((st = zero_complex(o0, F, stream)) != RQF_OK) return st;
+    if ((st = zero_complex(o1, F, stream)) != RQF_OK) return st;
+    return zero_complex(o2, F, stream);
+  }
+  if (!c1 || !c2 || !x || !carries || !gy || !gx || !scratch || (drive == kTwoTap && !tap1))
+    return RQF_ERR_ARGUMENT;
+  if (!aligned(c1, 8) || !aligned(c2, 8) || !aligned(gy, 8) || !aligned(carries, 8) ||
+      !aligned(scratch, 16) || !aligned(x, drive == kReal ? 4 : 8) ||
+      !aligned(gx, drive == kReal ? 4 : 8) || (tap1 && !aligned(tap1, 8)))
+    return RQF_ERR_ALIGN;
+  BtfArgs a = btf_args(c1, c2, tap1, x, gy, gx, nullptr, const_cast<float *>(carries), scratch,
+                       B, T, F);
+  const Scratch lay = scratch_layout(B * F, a.ntiles);
+  if ((st = clear_lookback(scratch, lay, stream)) != RQF_OK) return st;
+  const unsigned grid = (unsigned)(B * a.nfb * a.ntiles);
+  const int nt = kBtfBwdWarps * 32;
+  if (drive == kReal)
+    btf_bwd_kernel<kBtfBwdWarps, kBtfBwdK, kReal><<<grid, nt, 0, stream>>>(a);
+  else if (drive == kPlain)
+    btf_bwd_kernel<kBtfBwdWarps, kBtfBwdK, kPlain><<<grid, nt, 0, stream>>>(a);
+  else
+    btf_bwd_kernel<kBtfBwdWarps, kBtfBwdK, kTwoTap><<<grid, nt, 0, stream>>>(a);
+  if ((st = launch_status()) != RQF_OK) return st;
+  reduce_partials_kernel<<<(unsigned)F, 256, 0, stream>>>(
+      a.partials, reinterpret_cast<float2 *>(o0), reinterpret_cast<float2 *>(o1),
+      reinterpret_cast<float2 *>(o2), B, 1, F, a.ntiles);
+  return launch_status();
+}
+
+}  // namespace
+
+extern "C" {
+
+int rqf_abi_version(void) { return kAbiVersion; }
+
+const char *rqf_status_string(int status) {
+  switch (status) {
+    case RQF_OK:
+      return "ok";
+    case RQF_ERR_SHAPE:
+      return "invalid or unsupported shape";
+    case RQF_ERR_ALIGN:
+      return "pointer alignment requirement violated";
+    case RQF_ERR_LOOKBACK_TIMEOUT:
+      return "cross-tile look-back wait timed out";
+    case RQF_ERR_LAUNCH:
+      return "CUDA launch or memset failed";
+    case RQF_ERR_ARGUMENT:
+      return "null pointer or unsupported option";
+    case RQF_ERR_CAPACITY:
+      return "size exceeds the fixed internal maximum";
+    default:
+      return "unknown status";
+  }
+}
+
+int rqf_read_device_error(int *out_code, int clear, rqf_stream_t stream) {
+  if (!out_code) return RQF_ERR_ARGUMENT;
+  int h = 0;
+  if (cudaMemcpyFromSymbolAsync(&h, g_rqf_error, sizeof(int), 0, cudaMemcpyDeviceToHost,
+                                stream) != cudaSuccess)
+    return RQF_ERR_LAUNCH;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return RQF_ERR_LAUNCH;
+  if (clear) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbolAsync(g_rqf_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice,
+                                stream) != cudaSuccess)
+      return RQF_ERR_LAUNCH;
+    if (cudaStreamSynchronize(stream) != cudaSuccess) return RQF_ERR_LAUNCH;
+  }
+  *out_code = h;
+  return RQF_OK;
+}
+
+// ---------------------------------------------------------------- sizes
+int64_t rqf_btf_num_tiles(int64_t time) { return time <= 0 ? 0 : ceil_div(time, kBtfTile); }
+int64_t rqf_btf_carry_count(int64_t batch, int64_t time, int64_t filters) {
+  return batch * filters * rqf_btf_num_tiles(time);
+}
+size_t rqf_btf_scratch_bytes(int64_t batch, int64_t time, int64_t filters) {
+  if (batch <= 0 || time <= 0 || filters <= 0) return 256;
+  return scratch_layout(batch * filters, rqf_btf_num_tiles(time)).total;
+}
+int64_t rqf_fbt_num_tiles(int64_t time) { return time <= 0 ? 0 : ceil_div(time, kFbtTile); }
+int64_t rqf_fbt_carry_count(int64_t filters, int64_t batch, int64_t time) {
+  return filters * batch * rqf_fbt_num_tiles(time);
+}
+size_t rqf_fbt_scratch_bytes(int64_t filters, int64_t batch, int64_t time) {
+  if (batch <= 0 || time <= 0 || filters <= 0) return 256;
+  return scratch_layout(filters * batch, rqf_fbt_num_tiles(time)).total;
+}
+
+// --------------------------------------------------------- BTF scans
+int rqf_chunked_scan_forward(const float *c1, const float *c2, const void *u, int u_is_real,
+                             float *y, float *carries, void *scratch, int64_t batch,
+                             int64_t time, int64_t filters, rqf_stream_t stream) {
+  return btf_forward(u_is_real ? kReal : kPlain, c1, c2, nullptr, u, y, carries, scratch, batch,
+                     time, filters, stream);
+}
+
+int rqf_chunked_scan_backward(const float *c1, const float *c2, const void *u, int u_is_real,
+                              const float *carries, const float *grad_y, void *grad_u,
+                              float *grad_c1, float *grad_c2, void *scratch, int64_t batch,
+                              int64_t time, int64_t filters, rqf_stream_t stream) {
+  return btf_backward(u_is_real ? kReal : kPlain, c1, c2, nullptr, u, carries, grad_y, grad_u,
+                      grad_c1, grad_c2, nullptr, scratch, batch, time, filters, stream);
+}
+
+int rqf_chunked_prospective_forward(const float *c1, const float *tap0, const float *tap1,
+                                    const float *x, float *y, float *carries, void *scratch,
+                                    int64_t batch, int64_t time, int64_t filters,
+                                    rqf_stream_t stream) {
+  return btf_forward(kTwoTap, c1, tap0, tap1, x, y, carries, scratch, batch, time, filters,
+                     stream);
+}
+
+int rqf_chunked_prospective_backward(const float *c1, const float *tap0, const float *tap1,
+                                     const float *x, const float *carries, const float *grad_y,
+                                     float *grad_x, float *grad_c1, float *grad_tap0,
+                                     float *grad_tap1, void *scratch, int64_t batch,
+                                     int64_t time, int64_t filters, rqf_stream_t stream) {
+  return btf_backward(kTwoTap, c1, tap0, tap1, x, carries, grad_y, grad_x, grad_c1, grad_tap0,
+                      grad_tap1, scratch, batch, time, filters, stream);
+}
+
+// --------------------------------------------------------- FBT scans
+int rqf_fbt_prospective_forward(const float *c1, const float *tap0, const float *tap1,
+                                const float *z, float *out, float *carries, void *scratch,
+                                int64_t filters, int64_t batch, int64_t time, int fuse_act,
+                                rqf_stream_t stream) {
+  int st = fbt_dims_ok(filters, batch, time);
+  if (st != RQF_OK) return st;
+  if (filters == 0 || batch == 0 || time == 0) return RQF_OK;
+  if (!c1 || !tap0 || !tap1 || !z || !out || !carries || !scratch) return RQF_ERR_ARGUMENT;
+  if (!aligned(c1, 8) || !aligned(tap0, 8) || !aligned(tap1, 8) || !aligned(z, 8) ||
+      !aligned(out, 8) || !aligned(carries, 8) || !aligned(scratch, 16))
+    return RQF_ERR_ALIGN;
+  FbtArgs a = fbt_args(c1, tap0, tap1, z, nullptr, out, nullptr, carries, scratch, filters,
+                       batch, time);
+  const Scratch lay = scratch_layout(a.rows, a.ntiles);
+  if ((st = clear_lookback(scratch, lay, stream)) != RQF_OK) return st;
+  const bool vec = (time % 2 == 0) && aligned(z, 16) && aligned(out, 16);
+  const unsigned grid = (unsigned)(a.rows * a.ntiles);
+  if (vec) {
+    if (fuse_act)
+      fbt_fwd_kernel<kFbtThreads, kFbtK, true, true><<<grid, kFbtThreads, 0, stream>>>(a);
+    else
+      fbt_fwd_kernel<kFbtThreads, kFbtK, true, false><<<grid, kFbtThreads, 0, stream>>>(a);
+  } else {
+    if (fuse_act)
+      fbt_fwd_kernel<kFbtThreads, kFbtK, false, true><<<grid, kFbtThreads, 0, stream>>>(a);
+    else
+      fbt_fwd_kernel<kFbtThreads, kFbtK, false, false><<<grid, kFbtThreads, 0, stream>>>(a);
+  }
+  return launch_status();
+}
+
+int rqf_fbt_prospective_backward(const float *c1, const float *tap0, const float *tap1,
+                                 const float *z, const float *carries, const float *grad_out,
+                                 float *grad_z, float *grad_c1, float *grad_tap0,
+                                 float *grad_tap1, void *scratch, int64_t filters, int64_t batch,
+                                 int64_t time, int fuse_act, rqf_stream_t stream) {
+  int st = fbt_dims_ok(filters, batch, time);
+  if (st != RQF_OK) return st;
+  if (filters == 0) return RQF_OK;
+  if (batch == 0 || time == 0) {
+    if ((st = zero_complex(grad_c1, filters, stream)) != RQF_OK) return st;
+    if ((st = zero_complex(grad_tap0, filters, stream)) != RQF_OK) return st;
+    return zero_complex(grad_tap1, filters, stream);
+  }
+  if (!c1 || !tap0 || !tap1 || !z || !carries || !grad_out || !grad_z || !scratch)
+    return RQF_ERR_ARGUMENT;
+  if (!aligned(c1, 8) || !aligned(tap0, 8) || !aligned(tap1, 8) || !aligned(z, 8) ||
+      !aligned(grad_out, 8) || !aligned(grad_z, 8) || !aligned(carries, 8) ||
+      !aligned(scratch, 16))
+    return RQF_ERR_ALIGN;
+  FbtArgs a = fbt_args(c1, tap0, tap1, z, grad_out, grad_z, nullptr, const_cast<float *>(carries),
+                       scratch, filters, batch, time);
+  const Scratch lay = scratch_layout(a.rows, a.ntiles);
+  if ((st = clear_lookback(scratch, lay, stream)) != RQF_OK) return st;
+  const bool vec =
+      (time % 2 == 0) && aligned(z, 16) && aligned(grad_out, 16) && aligned(grad_z, 16);
+  const unsigned grid = (unsigned)(a.rows * a.ntiles);
+  if (vec) {
+    if (fuse_act)
+      fbt_bwd_kernel<kFbtThreads, kFbtK, true, true><<<grid, kFbtThreads, 0, stream>>>(a);
+    else
+      fbt_bwd_kernel<kFbtThreads, kFbtK, true, false><<<grid, kFbtThreads, 0, stream>>>(a);
+  } else {
+    if (fuse_act)
+      fbt_bwd_kernel<kFbtThreads, kFbtK, false, true><<<grid, kFbtThreads, 0, stream>>>(a);
+    else
+      fbt_bwd_kernel<kFbtThreads, kFbtK, false, false><<<grid, kFbtThreads, 0, stream>>>(a);
+  }
+  if ((st = launch_status()) != RQF_OK) return st;
+  reduce_partials_kernel<<<(unsigned)filters, 256, 0, stream>>>(
+      a.partials, reinterpret_cast<float2 *>(grad_c1), reinterpret_cast<float2 *>(grad_tap0),
+      reinterpret_cast<float2 *>(grad_tap1), batch, batch, 1, a.ntiles);
+  return launch_status();
+}
+
+// ------------------------------------------------------------ TBPTT(1)
+int rqf_tbptt1_two_tap_backward(int layout, const float *c1, const float *tap0,
+                                const float *tap1, const float *z, const float *carries,
+                                const float *grad_out, float *grad_z, float *grad_zw,
+                                float *grad_c1, float *grad_tap0, float *grad_tap1,
+                                void *scratch, int64_t d0, int64_t d1, int64_t d2, int fuse_act,
+                                rqf_stream_t stream) {
+  if (layout != 0 && layout != 1) return RQF_ERR_ARGUMENT;
+  const int64_t F = layout == 0 ? d2 : d0;
+  const int64_t B = layout == 0 ? d0 : d1;
+  const int64_t T = layout == 0 ? d1 : d2;
+  int st = layout == 0 ? btf_dims_ok(B, T, F) : fbt_dims_ok(F, B, T);
+  if (st != RQF_OK) return st;
+  if (F == 0) return RQF_OK;
+  if (B == 0 || T == 0) {
+    if ((st = zero_complex(grad_c1, F, stream)) != RQF_OK) return st;
+    if ((st = zero_complex(grad_tap0, F, stream)) != RQF_OK) return st;
+    return zero_complex(grad_tap1, F, stream);
+  }
+  if (!c1 || !tap0 || !tap1 || !z || !carries || !grad_out || !grad_z || !grad_zw || !scratch)
+    return RQF_ERR_ARGUMENT;
+  if (!aligned(c1, 8) || !aligned(tap0, 8) || !aligned(tap1, 8) || !aligned(z, 8) ||
+      !aligned(grad_out, 8) || !aligned(grad_z, 8) || !aligned(grad_zw, 8) ||
+      !aligned(carries, 8) || !aligned(scratch, 16))
+    return RQF_ERR_ALIGN;
+  if (layout == 0) {
+    BtfArgs a = btf_args(c1, tap0, tap1, z, grad_out, grad_z, grad_zw,
+                         const_cast<float *>(carries), scratch, B, T, F);
+    const unsigned grid = (unsigned)(B * a.nfb * a.ntiles);
+    const int nt = kBtfBwdWarps * 32;
+    if (fuse_act)
+      btf_tbptt_bwd_kernel<kBtfBwdWarps, kBtfBwdK, true><<<grid, nt, 0, stream>>>(a);
+    else
+      btf_tbptt_bwd_kernel<kBtfBwdWarps, kBtfBwdK, false><<<grid, nt, 0, stream>>>(a);
+    if ((st = launch_status()) != RQF_OK) return st;
+    reduce_partials_kernel<<<(unsigned)F, 256, 0, stream>>>(
+        a.partials, reinterpret_cast<float2 *>(grad_c1), reinterpret_cast<float2 *>(grad_tap0),
+        reinterpret_cast<float2 *>(grad_tap1), B, 1, F, a.ntiles);
+    return launch_status();
+  }
+  FbtArgs a = fbt_args(c1, tap0, tap1, z, grad_out, grad_z, grad_zw, const_cast<float *>(carries),
+                       scratch, F, B, T);
+  const bool vec = (T % 2 == 0) && aligned(z, 16) && aligned(grad_out, 16) &&
+                   aligned(grad_z, 16) && aligned(grad_zw, 16);
+  const unsigned grid = (unsigned)(a.rows * a.ntiles);
+  if (vec) {
+    if (fuse_act)
+      fbt_tbptt_bwd_kernel<kFbtThreads, kFbtK, true, true><<<grid, kFbtThreads, 0, stream>>>(a);
+    else
+      fbt_tbptt_bwd_kernel<kFbtThreads, kFbtK, true, false><<<grid, kFbtThreads, 0, stream>>>(a);
+  } else {
+    if (fuse_act)
+      fbt_tbptt_bwd_kernel<kFbtThreads, kFbtK, false, true><<<grid, kFbtThreads, 0, stream>>>(a);
+    else
+      fbt_tbptt_bwd_kernel<kFbtThreads, kFbtK, false, false>
+          <<<grid, kFbtThreads, 0, stream>>>(a);
+  }
+  if ((st = launch_status()) != RQF_OK) return st;
+  reduce_partials_kernel<<<(unsigned)F, 256, 0, stream>>>(
+      a.partials, reinterpret_cast<float2 *>(grad_c1), reinterpret_cast<float2 *>(grad_tap0),
+      reinterpret_cast<float2 *>(grad_tap1), B, B, 1, a.ntiles);
+  return launch_status();
+}
+
+}  // extern "C"

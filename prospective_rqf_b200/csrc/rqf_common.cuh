@@ -1,0 +1,333 @@
+// Device-side building blocks shared by the scan kernels:
+//   * complex float arithmetic on float2 (re, im),
+//   * the affine-pair composition used by every tile scan,
+//   * CTA-wide scans of (gate, value) pairs in forward and reverse time,
+//   * warp-private shared-memory transposes between the coalesced "striped"
+//     order of a global load and the "blocked" order (K consecutive time
+//     steps per thread) that the per-thread recurrence needs,
+//   * decoupled look-back flags with bounded waits and a device error latch.
+//
+// The recurrence y[t] = a[t]*y[t-1] + b[t] over a segment is the affine map
+// y_out = G*y_in + X with (G, X) the composition of the per-step pairs; the
+// composition of an earlier segment (g1, x1) followed by a later one (g2, x2)
+// is (g2*g1, g2*x1 + x2) — the operator of rqf_models/ops/scan.py:23-25 and
+// chunked_scan_kernel.py:_affine_combine (:50-57).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rqf {
+
+typedef unsigned long long u64;
+
+// ---------------------------------------------------------------- complex
+__device__ __forceinline__ float2 cz() { return make_float2(0.f, 0.f); }
+__device__ __forceinline__ float2 cone() { return make_float2(1.f, 0.f); }
+__device__ __forceinline__ float2 c_add(float2 a, float2 b) {
+  return make_float2(a.x + b.x, a.y + b.y);
+}
+__device__ __forceinline__ float2 c_conj(float2 a) { return make_float2(a.x, -a.y); }
+__device__ __forceinline__ float2 c_mul(float2 a, float2 b) {
+  return make_float2(fmaf(a.x, b.x, -a.y * b.y), fmaf(a.x, b.y, a.y * b.x));
+}
+// a*b + c
+__device__ __forceinline__ float2 c_fma(float2 a, float2 b, float2 c) {
+  return make_float2(fmaf(a.x, b.x, fmaf(-a.y, b.y, c.x)),
+                     fmaf(a.x, b.y, fmaf(a.y, b.x, c.y)));
+}
+// conj(a)*b + c
+__device__ __forceinline__ float2 c_cfma(float2 a, float2 b, float2 c) {
+  return make_float2(fmaf(a.x, b.x, fmaf(a.y, b.y, c.x)),
+                     fmaf(a.x, b.y, fmaf(-a.y, b.x, c.y)));
+}
+// split-ReLU: relu(Re) + i relu(Im)   (rqf_models/backbones/rqf/utils/activations.py:14-18)
+__device__ __forceinline__ float2 c_relu(float2 a) {
+  return make_float2(a.x > 0.f ? a.x : 0.f, a.y > 0.f ? a.y : 0.f);
+}
+// mask g by split-ReLU'(y): relu'(0) = 0, as fbt_scan_kernel.py:181-185
+__device__ __forceinline__ float2 c_relu_mask(float2 g, float2 y) {
+  return make_float2(y.x > 0.f ? g.x : 0.f, y.y > 0.f ? g.y : 0.f);
+}
+
+__device__ __forceinline__ float2 shfl_up2(float2 v, int d) {
+  return make_float2(__shfl_up_sync(0xffffffffu, v.x, d), __shfl_up_sync(0xffffffffu, v.y, d));
+}
+__device__ __forceinline__ float2 shfl_down2(float2 v, int d) {
+  return make_float2(__shfl_down_sync(0xffffffffu, v.x, d),
+                     __shfl_down_sync(0xffffffffu, v.y, d));
+}
+__device__ __forceinline__ float2 shfl_xor2(float2 v, int d) {
+  return make_float2(__shfl_xor_sync(0xffffffffu, v.x, d), __shfl_xor_sync(0xffffffffu, v.y, d));
+}
+
+// a^(2^s) in double precision: used for the per-tile gate lambda^L of a
+// time-invariant scan (L a power of two) so that the look-back multiplier
+// carries no fp32 accumulation of L products.
+__device__ __forceinline__ float2 c_pow2k(float2 a, int s) {
+  double re = a.x, im = a.y;
+  for (int i = 0; i < s; ++i) {
+    double nr = re * re - im * im;
+    double ni = 2.0 * re * im;
+    re = nr;
+    im = ni;
+  }
+  return make_float2((float)re, (float)im);
+}
+
+// ---------------------------------------------------------------- errors
+__device__ int g_rqf_error;  // first error code latched since the last clear
+
+__device__ __forceinline__ void latch_error(int code) { atomicCAS(&g_rqf_error, 0, code); }
+
+// ------------------------------------------------------- look-back flags
+// A published tile value is stored as 64-bit words (status << 32 | float bits)
+// so each word is single-copy atomic and carries its own status:
+//   0 = nothing yet, 1 = tile aggregate, 2 = inclusive prefix.
+constexpr unsigned kAggregate = 1u;
+constexpr unsigned kInclusive = 2u;
+// Upper bound of polls of one predecessor before giving up (~0.3 s).
+constexpr unsigned kSpinLimit = 1u << 20;
+constexpr int kErrLookbackTimeout = 3;
+
+__device__ __forceinline__ void st_relaxed_u64(u64 *p, u64 v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ u64 ld_relaxed_u64(const u64 *p) {
+  u64 v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ u64 pack_word(float v, unsigned status) {
+  return ((u64)status << 32) | (u64)__float_as_uint(v);
+}
+
+// Publish a complex value (2 words).
+__device__ __forceinline__ void flag_publish2(u64 *p, float2 v, unsigned status) {
+  st_relaxed_u64(p + 0, pack_word(v.x, status));
+  st_relaxed_u64(p + 1, pack_word(v.y, status));
+}
+// Publish (gate, value) (4 words).
+__device__ __forceinline__ void flag_publish4(u64 *p, float2 g, float2 v, unsigned status) {
+  st_relaxed_u64(p + 0, pack_word(g.x, status));
+  st_relaxed_u64(p + 1, pack_word(g.y, status));
+  st_relaxed_u64(p + 2, pack_word(v.x, status));
+  st_relaxed_u64(p + 3, pack_word(v.y, status));
+}
+
+// Exclusive prefix of the tile at processing position `pos` (pos >= 1) of a
+// row whose tiles all have the same time-invariant gate M (= lambda^L).
+// flags points at the row's 2-word slots, indexed by processing position.
+__device__ __forceinline__ float2 lookback_const(const u64 *flags, int pos, float2 M) {
+  float2 acc = cz(), mult = cone();
+  int i = pos - 1;
+  unsigned spins = 0, ns = 32;
+  while (i >= 0) {
+    const u64 w0 = ld_relaxed_u64(flags + 2 * i);
+    const u64 w1 = ld_relaxed_u64(flags + 2 * i + 1);
+    const unsigned s0 = (unsigned)(w0 >> 32), s1 = (unsigned)(w1 >> 32);
+    if (s0 == 0u || s0 != s1) {
+      if (++spins > kSpinLimit) {
+        latch_error(kErrLookbackTimeout);
+        break;
+      }
+      __nanosleep(ns);
+      ns = ns < 256u ? ns * 2u : 256u;
+      continue;
+    }
+    const float2 v = make_float2(__uint_as_float((unsigned)w0), __uint_as_float((unsigned)w1));
+    acc = c_fma(mult, v, acc);
+    if (s0 == kInclusive) break;
+    mult = c_mul(mult, M);
+    --i;
+    spins = 0;
+    ns = 32;
+  }
+  return acc;
+}
+
+// Same for tiles with their own gate aggregates (time-varying recurrences).
+__device__ __forceinline__ float2 lookback_pair(const u64 *flags, int pos) {
+  float2 acc = cz(), mult = cone();
+  int i = pos - 1;
+  unsigned spins = 0, ns = 32;
+  while (i >= 0) {
+    u64 w[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) w[q] = ld_relaxed_u64(flags + 4 * i + q);
+    const unsigned s = (unsigned)(w[0] >> 32);
+    bool ok = s != 0u;
+#pragma unroll
+    for (int q = 1; q < 4; ++q) ok = ok && ((unsigned)(w[q] >> 32) == s);
+    if (!ok) {
+      if (++spins > kSpinLimit) {
+        latch_error(kErrLookbackTimeout);
+        break;
+      }
+      __nanosleep(ns);
+      ns = ns < 256u ? ns * 2u : 256u;
+      continue;
+    }
+    const float2 g = make_float2(__uint_as_float((unsigned)w[0]), __uint_as_float((unsigned)w[1]));
+    const float2 v = make_float2(__uint_as_float((unsigned)w[2]), __uint_as_float((unsigned)w[3]));
+    acc = c_fma(mult, v, acc);
+    if (s == kInclusive) break;
+    mult = c_mul(mult, g);
+    --i;
+    spins = 0;
+    ns = 32;
+  }
+  return acc;
+}
+
+// --------------------------------------------------------- CTA scans
+// Scan of per-thread affine pairs (g, a) over the CTA in increasing thread
+// order.  Returns the exclusive composition (G, X) of all earlier threads and
+// the CTA total (Gt, At).  s_warp needs NT/32 float4 slots.  Contains one
+// __syncthreads(); every thread of the CTA must call it.
+template <int NT>
+__device__ __forceinline__ void cta_scan_fwd(float2 g, float2 a, float2 &G, float2 &X, float2 &Gt,
+                                             float2 &At, float4 *s_warp) {
+  constexpr int NW = NT / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float2 gp = shfl_up2(g, o), ap = shfl_up2(a, o);
+    if (lane >= o) {
+      a = c_fma(g, ap, a);
+      g = c_mul(g, gp);
+    }
+  }
+  float2 ge = shfl_up2(g, 1), ae = shfl_up2(a, 1);
+  if (lane == 0) {
+    ge = cone();
+    ae = cz();
+  }
+  if (lane == 31) s_warp[warp] = make_float4(g.x, g.y, a.x, a.y);
+  __syncthreads();
+  float2 Gw = cone(), Xw = cz();
+  float2 Gall = cone(), Xall = cz();
+#pragma unroll
+  for (int w = 0; w < NW; ++w) {
+    const float4 q = s_warp[w];
+    const float2 gw = make_float2(q.x, q.y), aw = make_float2(q.z, q.w);
+    if (w == warp) {
+      Gw = Gall;
+      Xw = Xall;
+    }
+    Xall = c_fma(gw, Xall, aw);
+    Gall = c_mul(gw, Gall);
+  }
+  X = c_fma(ge, Xw, ae);
+  G = c_mul(ge, Gw);
+  Gt = Gall;
+  At = Xall;
+}
+
+// Reverse-time counterpart: threads composed from the last to the first.
+// (G, X) composes all LATER threads; (Gt, At) is the CTA total.
+template <int NT>
+__device__ __forceinline__ void cta_scan_rev(float2 g, float2 a, float2 &G, float2 &X, float2 &Gt,
+                                             float2 &At, float4 *s_warp) {
+  constexpr int NW = NT / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float2 gp = shfl_down2(g, o), ap = shfl_down2(a, o);
+    if (lane + o < 32) {
+      a = c_fma(g, ap, a);
+      g = c_mul(g, gp);
+    }
+  }
+  float2 ge = shfl_down2(g, 1), ae = shfl_down2(a, 1);
+  if (lane == 31) {
+    ge = cone();
+    ae = cz();
+  }
+  if (lane == 0) s_warp[warp] = make_float4(g.x, g.y, a.x, a.y);
+  __syncthreads();
+  float2 Gw = cone(), Xw = cz();
+  float2 Gall = cone(), Xall = cz();
+#pragma unroll
+  for (int w = NW - 1; w >= 0; --w) {
+    const float4 q = s_warp[w];
+    const float2 gw = make_float2(q.x, q.y), aw = make_float2(q.z, q.w);
+    if (w == warp) {
+      Gw = Gall;
+      Xw = Xall;
+    }
+    Xall = c_fma(gw, Xall, aw);
+    Gall = c_mul(gw, Gall);
+  }
+  X = c_fma(ge, Xw, ae);
+  G = c_mul(ge, Gw);
+  Gt = Gall;
+  At = Xall;
+}
+
+// Sum a complex value over the CTA; the result is valid in thread 0.
+// s_red needs NT/32 float2 slots.  Contains one __syncthreads().
+template <int NT>
+__device__ __forceinline__ float2 cta_sum(float2 v, float2 *s_red) {
+  constexpr int NW = NT / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = c_add(v, shfl_xor2(v, o));
+  if (lane == 0) s_red[warp] = v;
+  __syncthreads();
+  float2 s = cz();
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int w = 0; w < NW; ++w) s = c_add(s, s_red[w]);
+  }
+  return s;
+}
+
+// --------------------------------------------- warp-private transposes
+// A warp owns 32*K consecutive complex samples.  "Striped": lane l holds the
+// float4 pairs v*32 + l (v < K/2) — what a coalesced 16-byte load returns.
+// "Blocked": lane l holds samples l*K .. l*K+K-1.  The XOR swizzle on the
+// float4 slot index keeps both access patterns free of bank conflicts for
+// K in {4, 8, 16}.
+template <int K>
+__device__ __forceinline__ int swz(int p) {
+  return p ^ ((p >> 3) & (K / 2 - 1));
+}
+
+template <int K>
+__device__ __forceinline__ void striped_to_blocked(float4 *wbuf, const float4 (&s)[K / 2],
+                                                   float2 (&b)[K], int lane) {
+#pragma unroll
+  for (int v = 0; v < K / 2; ++v) wbuf[swz<K>(v * 32 + lane)] = s[v];
+  __syncwarp();
+#pragma unroll
+  for (int m = 0; m < K / 2; ++m) {
+    const float4 q = wbuf[swz<K>(lane * (K / 2) + m)];
+    b[2 * m] = make_float2(q.x, q.y);
+    b[2 * m + 1] = make_float2(q.z, q.w);
+  }
+  __syncwarp();
+}
+
+template <int K>
+__device__ __forceinline__ void blocked_to_striped(float4 *wbuf, const float2 (&b)[K],
+                                                   float4 (&s)[K / 2], int lane) {
+#pragma unroll
+  for (int m = 0; m < K / 2; ++m)
+    wbuf[swz<K>(lane * (K / 2) + m)] =
+        make_float4(b[2 * m].x, b[2 * m].y, b[2 * m + 1].x, b[2 * m + 1].y);
+  __syncwarp();
+#pragma unroll
+  for (int v = 0; v < K / 2; ++v) s[v] = wbuf[swz<K>(v * 32 + lane)];
+  __syncwarp();
+}
+
+// Streaming 16-byte load / store (data is touched once per kernel).
+__device__ __forceinline__ float4 ld_stream4(const float2 *p) {
+  return __ldcs(reinterpret_cast<const float4 *>(p));
+}
+__device__ __forceinline__ void st_stream4(float2 *p, float4 v) {
+  __stcs(reinterpret_cast<float4 *>(p), v);
+}
+
+}  // namespace rqf

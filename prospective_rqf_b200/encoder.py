@@ -1,0 +1,212 @@
+"""Pure RQF encoder and complex readout driven by the B200 scan kernels.
+
+A restatement of the reference's channel-outermost Pure RQF stack — the
+callers on either side of the scan — so the training step can run (and be
+timed) without the reference tree:
+
+* ZOH prospective two-tap coefficients from log-space leaves
+  (rqf_models/backbones/rqf/filter.py:RQF, _init_log_space :303-340,
+  compute_two_tap_coefficients :510-664 ZOH branch, clamp_parameters :366-399,
+  _expm1_div_x_complex :21-50);
+* the (F,B,T) stack of rqf_models/backbones/rqf/pure.py:_forward_fbt_stack
+  (:510-536) and PureRQFBlock._forward_fbt (:212-243): input projection on the
+  tiny input axis, per block z = W @ h (complex GEMM), two-tap scan with the
+  split-ReLU fused (fbt_recompute_scan) or the raw state for a last block
+  without activation, complex skip h = out + h;
+* power-preserving W init (rqf_models/backbones/rqf/utils/init.py:33-65);
+* the per-timestep [Re; Im] MLP readout with mean-pooled logits
+  (train.py:ComplexReadoutClassifier :74-136), evaluated channel-first so the
+  (F,B,T) features need no (B,T,F) permute.
+
+TBPTT(1) blocks own their projection GEMM (as rqf_models/ops/selective_scan.py
+:_SelectiveLayerScan does for the selective path) so the lag-tap cotangent
+reaches W only, without the reference's second forward GEMM W(x.detach())
+(pure.py:184-187).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+from torch.autograd.function import once_differentiable
+
+from . import ops
+
+SPLIT_RELU_GAIN = 0.5     # utils/init.py RQF_ACTIVATION_GAINS["split_relu"]
+NOMINAL_FILTER_GAIN = 0.5  # utils/init.py NOMINAL_FILTER_GAIN
+
+
+def rqf_forward_std(n_in: int, activation_gain: float) -> float:
+    return 1.0 / math.sqrt(2.0 * n_in * NOMINAL_FILTER_GAIN * activation_gain)
+
+
+def _expm1_div_x(x: torch.Tensor, threshold: float = 1e-4) -> torch.Tensor:
+    """(e^x - 1)/x for complex x with the reference's 4th-order small branch."""
+    small = x.abs() < threshold
+    safe = torch.where(small, torch.ones_like(x), x)
+    direct = (torch.exp(x) - 1.0) / safe
+    taylor = 1.0 + x / 2 + x ** 2 / 6 + x ** 3 / 24 + x ** 4 / 120
+    return torch.where(small, taylor, direct)
+
+
+class RQFCoefficients(nn.Module):
+    """Log-space RQF leaves (resonant recipe, seq_duration set) and their ZOH
+    prospective two-tap coefficients (tau mode, rho = 1)."""
+
+    def __init__(self, num_filters: int, dt: float, tau: float, seq_duration: float,
+                 filter_max_freq_factor: float = 1.0, generator: torch.Generator | None = None):
+        super().__init__()
+        self.dt = float(dt)
+        self.tau = float(tau)
+        self.seq_duration = float(seq_duration)
+        lo = math.log(2 * math.pi * tau / seq_duration)
+        hi = math.log(2 * math.pi * filter_max_freq_factor)
+        u = torch.rand(num_filters, generator=generator)
+        log_theta = lo + u * (hi - lo)
+        theta = log_theta.exp()
+        gamma = (theta / (1.0 + theta)).clamp(1e-6, 1.0 - 1e-6)
+        self.log_theta = nn.Parameter(log_theta)
+        self.log_gamma = nn.Parameter(gamma.log())
+        # theta band [2 pi tau / T, 2 pi tau * (1/tau)] and gamma band [1e-6, 1 - 1e-6]
+        self._theta_bounds = (lo, math.log(2 * math.pi))
+        self._gamma_bounds = (math.log(1e-6), math.log(1.0 - 1e-6))
+
+    def two_tap(self) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        gamma = self.log_gamma.exp()
+        theta = self.log_theta.exp()
+        a = torch.complex(-gamma / self.tau, (theta / self.tau) * (1.0 - gamma)) * self.dt
+        c1 = torch.exp(a)
+        b_bar = (self.dt / self.tau) * _expm1_div_x(a)
+        extra = gamma * c1  # gamma * rho * C1 with rho = 1
+        tap0 = gamma * b_bar + extra
+        tap1 = -extra
+        return c1.to(torch.complex64), tap0.to(torch.complex64), tap1.to(torch.complex64)
+
+    @torch.no_grad()
+    def clamp_parameters(self) -> None:
+        self.log_theta.clamp_(*self._theta_bounds)
+        self.log_gamma.clamp_(*self._gamma_bounds)
+
+
+class _TBPTTLayer(torch.autograd.Function):
+    """z = W @ h, then the TBPTT(1) two-tap scan in (F,B,T).  The lag-tap
+    cotangent updates W only — the reference gets the same by feeding the lag
+    tap from a second GEMM W(x.detach()) (pure.py:184-187)."""
+
+    @staticmethod
+    def forward(ctx, h, W, C1, tap0, tap1, fuse_act):
+        F_in, B, T = h.shape
+        z = (W @ h.reshape(F_in, B * T)).reshape(W.shape[0], B, T)
+        y, saved = ops._fbt_forward(C1, tap0, tap1, z, bool(fuse_act))
+        ctx.save_for_backward(h, W, *saved)
+        ctx.fuse_act = bool(fuse_act)
+        return y
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, gy):
+        h, W, *saved = ctx.saved_tensors
+        z = saved[3]
+        gc1, gt0, gt1, gz, gzw = ops._tbptt_backward(saved, "fbt", tuple(z.shape), gy,
+                                                     ctx.fuse_act)
+        F_in, B, T = h.shape
+        need = ctx.needs_input_grad
+        gh = (W.mH @ gz.reshape(W.shape[0], B * T)).reshape(F_in, B, T) if need[0] else None
+        gW = (gz + gzw).reshape(W.shape[0], B * T) @ h.reshape(F_in, B * T).mH if need[1] else None
+        return gh, gW, gc1, gt0, gt1, None
+
+
+class PureRQFEncoderB200(nn.Module):
+    """Pure RQF encoder in (F,B,T) layout on the B200 scan kernels.
+
+    forward(x: (B,T,input_dims) real) -> complex (F,B,T) features."""
+
+    def __init__(self, input_dims: int = 1, hidden_dims: int = 128, num_layers: int = 6,
+                 samp_frequency: float = 16000.0, tau: float = 0.0003125,
+                 seq_duration: float = 1.0, skip_connection: bool = True,
+                 final_activation: bool = False, input_proj_bias: bool = False,
+                 scan_grad_mode: str = "full", seed: int = 0):
+        super().__init__()
+        if scan_grad_mode not in ("full", "tbptt1"):
+            raise ValueError(f"scan_grad_mode must be 'full' or 'tbptt1', got {scan_grad_mode!r}")
+        g = torch.Generator().manual_seed(seed)
+        self.hidden = hidden_dims
+        self.skip = skip_connection
+        self.final_activation = final_activation
+        self.scan_grad_mode = scan_grad_mode
+        self.input_proj = nn.Linear(input_dims, hidden_dims, bias=input_proj_bias)
+        dt = 1.0 / samp_frequency
+        self.rqf = nn.ModuleList(
+            RQFCoefficients(hidden_dims, dt, tau, seq_duration, generator=g)
+            for _ in range(num_layers))
+        ws = []
+        for i in range(num_layers):
+            std = rqf_forward_std(hidden_dims, 1.0 if i == 0 else SPLIT_RELU_GAIN)
+            re = torch.randn(hidden_dims, hidden_dims, generator=g) * std
+            im = torch.randn(hidden_dims, hidden_dims, generator=g) * std
+            ws.append(nn.Parameter(torch.complex(re, im)))
+        self.W = nn.ParameterList(ws)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        B, T, I = x.shape
+        x_cf = x.permute(2, 0, 1).reshape(I, B * T)
+        w_in, b_in = self.input_proj.weight, self.input_proj.bias
+        proj = w_in @ x_cf if b_in is None else torch.addmm(b_in[:, None], w_in, x_cf)
+        h = proj.reshape(-1, B, T).to(torch.complex64)
+        n = len(self.W)
+        for i in range(n):
+            act = self.final_activation or i + 1 < n
+            c1, t0, t1 = self.rqf[i].two_tap()
+            W = self.W[i]
+            if self.scan_grad_mode == "tbptt1":
+                out = _TBPTTLayer.apply(h, W, c1, t0, t1, act)
+            else:
+                z = (W @ h.reshape(W.shape[1], B * T)).reshape(W.shape[0], B, T)
+                out = (ops.fbt_recompute_scan(c1, t0, t1, z) if act
+                       else ops.fbt_prospective_scan(c1, t0, t1, z, False))
+            h = out + h if (self.skip and out.shape == h.shape) else out
+        return h
+
+    @torch.no_grad()
+    def clamp_parameters(self) -> None:
+        for r in self.rqf:
+            r.clamp_parameters()
+
+
+class ComplexReadout(nn.Module):
+    """Per-timestep MLP on [Re h; Im h] with mean-pooled logits
+    (train.py:ComplexReadoutClassifier, hidden_dims set)."""
+
+    def __init__(self, features: int, num_classes: int, hidden_dims: int = 256, seed: int = 1):
+        super().__init__()
+        g = torch.Generator().manual_seed(seed)
+        self.fc1 = nn.Linear(2 * features, hidden_dims)
+        self.fc2 = nn.Linear(hidden_dims, num_classes)
+        with torch.no_grad():
+            bound = 1.0 / math.sqrt(2 * features)
+            self.fc1.weight.uniform_(-bound, bound, generator=g)
+            self.fc1.bias.uniform_(-bound, bound, generator=g)
+            self.fc2.weight.normal_(0.0, 1e-3, generator=g)
+            self.fc2.bias.zero_()
+
+    def forward(self, h: torch.Tensor, per_step: bool = False) -> torch.Tensor:
+        F, B, T = h.shape
+        feats = torch.cat([h.real, h.imag], dim=0).reshape(2 * F, B * T)
+        hid = torch.relu(torch.addmm(self.fc1.bias[:, None], self.fc1.weight, feats))
+        logits = torch.addmm(self.fc2.bias[:, None], self.fc2.weight, hid)  # (C, B*T)
+        logits = logits.reshape(-1, B, T)
+        if per_step:
+            return logits.permute(1, 2, 0)  # (B, T, C)
+        return logits.mean(dim=2).t()  # (B, C)
+
+
+class RQFClassifier(nn.Module):
+    def __init__(self, encoder: PureRQFEncoderB200, num_classes: int, hidden_dims: int = 256):
+        super().__init__()
+        self.encoder = encoder
+        self.readout = ComplexReadout(encoder.hidden, num_classes, hidden_dims)
+
+    def forward(self, x: torch.Tensor, per_step: bool = False) -> torch.Tensor:
+        return self.readout(self.encoder(x), per_step=per_step)

@@ -1,0 +1,85 @@
+"""Route the reference's scan dispatch to this backend.
+
+``install()`` rebinds the module-level callables that the reference's own
+dispatch resolves at call time, so its selection logic (``ORGANICS_RQF_FBT``,
+``ORGANICS_SCAN_BACKEND``, the FBT eligibility checks of
+rqf_models/backbones/rqf/pure.py:194-210 / :500-508, the CUDA/Triton gates of
+rqf_models/ops/scan.py:359-372) stays exactly as it is; only the kernels
+behind it change.  ``uninstall()`` restores the originals.
+
+Call sites served (reference paths):
+  rqf_models/ops/scan.py:367, :509            -> _triton_chunked_scan
+  rqf_models/backbones/rqf/block.py:926-934   -> _triton_chunked_scan_prospective
+  rqf_models/backbones/rqf/pure.py:234-238    -> fbt_prospective_scan / fbt_recompute_scan
+  rqf_models/backbones/rqf/block.py:882, :904 -> TBPTT(1) fused surrogate on CUDA
+"""
+
+from __future__ import annotations
+
+import importlib
+
+from . import ops
+
+_SAVED: list[tuple[object, str, object]] = []
+
+_BINDINGS = [
+    ("rqf_models.ops.chunked_scan_kernel", "_triton_chunked_scan", ops._triton_chunked_scan),
+    ("rqf_models.ops.chunked_scan_kernel", "_triton_chunked_scan_prospective",
+     ops._triton_chunked_scan_prospective),
+    ("rqf_models.ops.scan", "_triton_chunked_scan", ops._triton_chunked_scan),
+    ("rqf_models.ops.fbt_scan_kernel", "fbt_prospective_scan", ops.fbt_prospective_scan),
+    ("rqf_models.ops.fbt_scan_kernel", "fbt_recompute_scan", ops.fbt_recompute_scan),
+    ("rqf_models.backbones.rqf.block", "_triton_chunked_scan_prospective",
+     ops._triton_chunked_scan_prospective),
+    ("rqf_models.backbones.rqf.pure", "fbt_prospective_scan", ops.fbt_prospective_scan),
+    ("rqf_models.backbones.rqf.pure", "fbt_recompute_scan", ops.fbt_recompute_scan),
+]
+
+
+def _tbptt_two_tap(orig):
+    def _scan_two_tap_with_grad_mode(self, u, C1, tap0, tap1, *, delayed_u=None):
+        if (self._use_tbptt1_scan_grad() and u.is_cuda and tap0.dim() == 1
+                and tap1.dim() == 1):
+            return ops.tbptt1_two_tap_scan(u, C1, tap0, tap1, delayed_u=delayed_u, layout="btf")
+        return orig(self, u, C1, tap0, tap1, delayed_u=delayed_u)
+
+    _scan_two_tap_with_grad_mode.__wrapped__ = orig
+    return _scan_two_tap_with_grad_mode
+
+
+def _tbptt_single_tap(orig):
+    def _scan_with_grad_mode(self, u, C1, C2):
+        if self._use_tbptt1_scan_grad() and u.is_cuda and C1.dim() == 1 and C2.dim() == 1:
+            return ops.tbptt1_scan(u, C1, C2)
+        return orig(self, u, C1, C2)
+
+    _scan_with_grad_mode.__wrapped__ = orig
+    return _scan_with_grad_mode
+
+
+def install() -> list[str]:
+    """Rebind the reference callables; returns the names that were patched."""
+    if _SAVED:
+        return [f"{getattr(m, '__name__', m)}.{n}" for m, n, _ in _SAVED]
+    patched = []
+    for mod_name, attr, fn in _BINDINGS:
+        mod = importlib.import_module(mod_name)
+        if hasattr(mod, attr):
+            _SAVED.append((mod, attr, getattr(mod, attr)))
+            setattr(mod, attr, fn)
+            patched.append(f"{mod_name}.{attr}")
+    block = importlib.import_module("rqf_models.backbones.rqf.block")
+    base = block.BaseRQFBlock
+    for attr, wrap in (("_scan_two_tap_with_grad_mode", _tbptt_two_tap),
+                       ("_scan_with_grad_mode", _tbptt_single_tap)):
+        orig = getattr(base, attr)
+        _SAVED.append((base, attr, orig))
+        setattr(base, attr, wrap(orig))
+        patched.append(f"rqf_models.backbones.rqf.block.BaseRQFBlock.{attr}")
+    return patched
+
+
+def uninstall() -> None:
+    while _SAVED:
+        obj, attr, orig = _SAVED.pop()
+        setattr(obj, attr, orig)

@@ -1,0 +1,421 @@
+"""B200 drop-in for the rqf_models.ops scan entry points.
+
+Each public callable keeps the name, signature, return convention and
+gradient convention (PyTorch conjugate-Wirtinger, ``None`` for inputs that do
+not need a gradient) of the reference callable it replaces; the compute runs
+in librqf_b200.so through the C ABI of include/rqf_b200.h.  There is no CPU
+or Triton fallback: non-CUDA inputs raise.
+
+Reference callables (paths inside the reference project):
+  _triton_chunked_scan              rqf_models/ops/chunked_scan_kernel.py:340
+  _triton_chunked_scan_prospective  rqf_models/ops/chunked_scan_kernel.py:506
+  fbt_prospective_scan              rqf_models/ops/fbt_scan_kernel.py:332
+  fbt_recompute_scan                rqf_models/ops/fbt_scan_kernel.py:667
+  sequential_scan / parallel_scan   rqf_models/ops/scan.py:290 / :435 (CUDA branch)
+  sequential_scan_abs               rqf_models/ops/scan.py:381
+New (no single reference callable; replaces the autograd surrogate of
+rqf_models/backbones/rqf/block.py:_scan_two_tap_with_grad_mode :904-954 and
+_scan_with_grad_mode :882-902):
+  tbptt1_two_tap_scan, tbptt1_scan
+"""
+
+from __future__ import annotations
+
+import os
+
+import torch
+from torch.autograd.function import once_differentiable
+
+from . import _abi, _timing
+
+_SYNC_CHECK = os.environ.get("RQF_B200_SYNC_CHECK", "0") == "1"
+
+__all__ = [
+    "_triton_chunked_scan",
+    "_triton_chunked_scan_prospective",
+    "fbt_prospective_scan",
+    "fbt_recompute_scan",
+    "tbptt1_two_tap_scan",
+    "tbptt1_scan",
+    "sequential_scan",
+    "parallel_scan",
+    "sequential_scan_abs",
+]
+
+
+# ------------------------------------------------------------------ helpers
+def _c64(t: torch.Tensor) -> torch.Tensor:
+    if t.dtype != torch.complex64:
+        t = t.to(torch.complex64)
+    return t.resolve_conj().resolve_neg().contiguous()
+
+
+def _require_cuda(*ts: torch.Tensor | None) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError(
+                "prospective_rqf_b200 runs on CUDA tensors only (no CPU fallback); "
+                f"got a tensor on {t.device}")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} and {t.device}")
+    return dev
+
+
+def _coef(t: torch.Tensor, n: int, name: str) -> torch.Tensor:
+    t = _c64(t)
+    if t.dim() != 1 or t.shape[0] != n:
+        raise ValueError(f"{name} must have shape ({n},), got {tuple(t.shape)}")
+    return t
+
+
+def _scratch(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def _carries(n: int, device) -> torch.Tensor:
+    return torch.empty(max(int(n), 1), dtype=torch.complex64, device=device)
+
+
+def _done(device) -> None:
+    if _SYNC_CHECK:
+        _abi.check_device_errors(device)
+
+
+def _shape3(x: torch.Tensor, what: str):
+    if x.dim() != 3:
+        raise ValueError(f"{what} must be 3-D, got shape {tuple(x.shape)}")
+    return tuple(int(s) for s in x.shape)
+
+
+# ------------------------------------------------------ (B,T,F) plain scan
+class _ChunkedScanFunction(torch.autograd.Function):
+    """y[t] = C1*y[t-1] + C2*u[t] on (B,T,F); saves C1, C2, u and one carry per
+    tile (chunked_scan_kernel.py:_ChunkedScanFunction :306-337 saves the full
+    output instead)."""
+
+    @staticmethod
+    def forward(ctx, C1, C2, u):
+        dev = _require_cuda(C1, C2, u)
+        real = not u.is_complex()
+        uu = u.to(torch.float32).contiguous() if real else _c64(u)
+        B, T, F = _shape3(uu, "u")
+        c1, c2 = _coef(C1, F, "C1"), _coef(C2, F, "C2")
+        lib = _abi.load()
+        y = torch.empty((B, T, F), dtype=torch.complex64, device=dev)
+        carries = _carries(lib.rqf_btf_carry_count(B, T, F), dev)
+        scratch = _scratch(lib.rqf_btf_scratch_bytes(B, T, F), dev)
+        with _timing.launch("rqf_chunked_scan_forward", B * T * F):
+            _abi.check(lib.rqf_chunked_scan_forward(
+                _abi.ptr(c1), _abi.ptr(c2), _abi.ptr(uu), int(real), _abi.ptr(y), _abi.ptr(carries),
+                _abi.ptr(scratch), B, T, F, _abi.stream_of(uu)), "rqf_chunked_scan_forward")
+        _done(dev)
+        ctx.save_for_backward(c1, c2, uu, carries)
+        ctx.real = real
+        return y
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_output):
+        c1, c2, uu, carries = ctx.saved_tensors
+        B, T, F = uu.shape
+        dev = uu.device
+        gy = _c64(grad_output)
+        lib = _abi.load()
+        gu = torch.empty_like(uu)
+        gc1 = torch.empty_like(c1)
+        gc2 = torch.empty_like(c2)
+        scratch = _scratch(lib.rqf_btf_scratch_bytes(B, T, F), dev)
+        with _timing.launch("rqf_chunked_scan_backward", B * T * F):
+            _abi.check(lib.rqf_chunked_scan_backward(
+                _abi.ptr(c1), _abi.ptr(c2), _abi.ptr(uu), int(ctx.real), _abi.ptr(carries),
+                _abi.ptr(gy), _abi.ptr(gu), _abi.ptr(gc1), _abi.ptr(gc2), _abi.ptr(scratch),
+                B, T, F, _abi.stream_of(gy)), "rqf_chunked_scan_backward")
+        _done(dev)
+        need = ctx.needs_input_grad
+        return (gc1 if need[0] else None, gc2 if need[1] else None, gu if need[2] else None)
+
+
+def _triton_chunked_scan(C1: torch.Tensor, C2: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    """x[n] = C1*x[n-1] + C2*u[n] on (batch, time, filters) — drop-in for
+    rqf_models/ops/chunked_scan_kernel.py:_triton_chunked_scan (:340).  A real
+    ``u`` is scanned without promotion (same values as scan.py:366's cast)."""
+    return _ChunkedScanFunction.apply(C1, C2, u)
+
+
+# ------------------------------------------------ (B,T,F) two-tap scan
+class _ChunkedProspectiveScanFunction(torch.autograd.Function):
+    """y[n] = C1 y[n-1] + tap0 x[n] + tap1 x[n-1] on (B,T,F)
+    (chunked_scan_kernel.py:_ChunkedProspectiveScanFunction :474-503)."""
+
+    @staticmethod
+    def forward(ctx, C1, tap0, tap1, x):
+        dev = _require_cuda(C1, tap0, tap1, x)
+        xx = _c64(x)
+        B, T, F = _shape3(xx, "x")
+        c1, t0, t1 = _coef(C1, F, "C1"), _coef(tap0, F, "tap0"), _coef(tap1, F, "tap1")
+        lib = _abi.load()
+        y = torch.empty((B, T, F), dtype=torch.complex64, device=dev)
+        carries = _carries(lib.rqf_btf_carry_count(B, T, F), dev)
+        scratch = _scratch(lib.rqf_btf_scratch_bytes(B, T, F), dev)
+        with _timing.launch("rqf_chunked_prospective_forward", B * T * F):
+            _abi.check(lib.rqf_chunked_prospective_forward(
+                _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1), _abi.ptr(xx), _abi.ptr(y), _abi.ptr(carries),
+                _abi.ptr(scratch), B, T, F, _abi.stream_of(xx)), "rqf_chunked_prospective_forward")
+        _done(dev)
+        ctx.save_for_backward(c1, t0, t1, xx, carries)
+        return y
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_output):
+        c1, t0, t1, xx, carries = ctx.saved_tensors
+        B, T, F = xx.shape
+        dev = xx.device
+        gy = _c64(grad_output)
+        lib = _abi.load()
+        gx = torch.empty_like(xx)
+        gc1, gt0, gt1 = torch.empty_like(c1), torch.empty_like(t0), torch.empty_like(t1)
+        scratch = _scratch(lib.rqf_btf_scratch_bytes(B, T, F), dev)
+        with _timing.launch("rqf_chunked_prospective_backward", B * T * F):
+            _abi.check(lib.rqf_chunked_prospective_backward(
+                _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1), _abi.ptr(xx), _abi.ptr(carries),
+                _abi.ptr(gy), _abi.ptr(gx), _abi.ptr(gc1), _abi.ptr(gt0), _abi.ptr(gt1),
+                _abi.ptr(scratch), B, T, F, _abi.stream_of(gy)), "rqf_chunked_prospective_backward")
+        _done(dev)
+        need = ctx.needs_input_grad
+        return (gc1 if need[0] else None, gt0 if need[1] else None, gt1 if need[2] else None,
+                gx if need[3] else None)
+
+
+def _triton_chunked_scan_prospective(C1, tap0, tap1, x):
+    """Fused two-tap prospective scan on (batch, time, filters) — drop-in for
+    rqf_models/ops/chunked_scan_kernel.py:_triton_chunked_scan_prospective (:506)."""
+    return _ChunkedProspectiveScanFunction.apply(C1, tap0, tap1, x)
+
+
+# ------------------------------------------------ (F,B,T) two-tap scan
+def _fbt_forward(C1, tap0, tap1, x_fbt, fuse_act: bool):
+    dev = _require_cuda(C1, tap0, tap1, x_fbt)
+    z = _c64(x_fbt)
+    F, B, T = _shape3(z, "x_fbt")
+    c1, t0, t1 = _coef(C1, F, "C1"), _coef(tap0, F, "tap0"), _coef(tap1, F, "tap1")
+    lib = _abi.load()
+    out = torch.empty((F, B, T), dtype=torch.complex64, device=dev)
+    carries = _carries(lib.rqf_fbt_carry_count(F, B, T), dev)
+    scratch = _scratch(lib.rqf_fbt_scratch_bytes(F, B, T), dev)
+    with _timing.launch("rqf_fbt_prospective_forward", B * T * F):
+        _abi.check(lib.rqf_fbt_prospective_forward(
+            _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1), _abi.ptr(z), _abi.ptr(out), _abi.ptr(carries),
+            _abi.ptr(scratch), F, B, T, int(bool(fuse_act)), _abi.stream_of(z)),
+            "rqf_fbt_prospective_forward")
+    _done(dev)
+    return out, (c1, t0, t1, z, carries)
+
+
+def _fbt_backward(saved, grad_output, fuse_act: bool):
+    c1, t0, t1, z, carries = saved
+    F, B, T = z.shape
+    dev = z.device
+    gy = _c64(grad_output)
+    lib = _abi.load()
+    gz = torch.empty_like(z)
+    gc1, gt0, gt1 = torch.empty_like(c1), torch.empty_like(t0), torch.empty_like(t1)
+    scratch = _scratch(lib.rqf_fbt_scratch_bytes(F, B, T), dev)
+    with _timing.launch("rqf_fbt_prospective_backward", B * T * F):
+        _abi.check(lib.rqf_fbt_prospective_backward(
+            _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1), _abi.ptr(z), _abi.ptr(carries), _abi.ptr(gy),
+            _abi.ptr(gz), _abi.ptr(gc1), _abi.ptr(gt0), _abi.ptr(gt1), _abi.ptr(scratch), F, B, T,
+            int(bool(fuse_act)), _abi.stream_of(gy)), "rqf_fbt_prospective_backward")
+    _done(dev)
+    return gc1, gt0, gt1, gz
+
+
+class _FBTProspectiveScan(torch.autograd.Function):
+    """(F,B,T) two-tap scan, split-ReLU output when ``fuse_act``
+    (fbt_scan_kernel.py:_FBTProspectiveScan :245-329).  Saves only the tile
+    carries; the backward recomputes the raw state."""
+
+    @staticmethod
+    def forward(ctx, C1, tap0, tap1, x_fbt, fuse_act):
+        out, saved = _fbt_forward(C1, tap0, tap1, x_fbt, bool(fuse_act))
+        ctx.save_for_backward(*saved)
+        ctx.fuse_act = bool(fuse_act)
+        return out
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_output):
+        gc1, gt0, gt1, gz = _fbt_backward(ctx.saved_tensors, grad_output, ctx.fuse_act)
+        need = ctx.needs_input_grad
+        return (gc1 if need[0] else None, gt0 if need[1] else None, gt1 if need[2] else None,
+                gz if need[3] else None, None)
+
+
+class _FBTRecompute(torch.autograd.Function):
+    """Split-ReLU (F,B,T) two-tap scan storing only per-tile carries
+    (fbt_scan_kernel.py:_FBTRecompute :575-664)."""
+
+    @staticmethod
+    def forward(ctx, C1, tap0, tap1, x_fbt):
+        out, saved = _fbt_forward(C1, tap0, tap1, x_fbt, True)
+        ctx.save_for_backward(*saved)
+        return out
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_output):
+        gc1, gt0, gt1, gz = _fbt_backward(ctx.saved_tensors, grad_output, True)
+        need = ctx.needs_input_grad
+        return (gc1 if need[0] else None, gt0 if need[1] else None, gt1 if need[2] else None,
+                gz if need[3] else None)
+
+
+def fbt_prospective_scan(C1, tap0, tap1, x_fbt, fuse_act: bool = False):
+    """Fused two-tap prospective scan in channel-outermost (filters, batch,
+    time) layout — drop-in for rqf_models/ops/fbt_scan_kernel.py:
+    fbt_prospective_scan (:332).  Returns split-ReLU(y) when ``fuse_act``,
+    else the raw state y."""
+    return _FBTProspectiveScan.apply(C1, tap0, tap1, x_fbt, fuse_act)
+
+
+def fbt_recompute_scan(C1, tap0, tap1, x_fbt):
+    """Split-ReLU two-tap scan with recompute-in-backward — drop-in for
+    rqf_models/ops/fbt_scan_kernel.py:fbt_recompute_scan (:667)."""
+    return _FBTRecompute.apply(C1, tap0, tap1, x_fbt)
+
+
+# ------------------------------------------------------------- TBPTT(1)
+class _TBPTT1TwoTap(torch.autograd.Function):
+    """Forward = the exact two-tap scan; backward = the TBPTT(1) surrogate of
+    block.py:_scan_two_tap_with_grad_mode (:938-954) in one pointwise kernel:
+    grad_u = conj(tap0) g (+ conj(tap1) g[t+1] when u is its own lag source),
+    grad_delayed_u[t] = conj(tap1) g[t+1], coefficient grads summed with the
+    recurrent state detached."""
+
+    @staticmethod
+    def forward(ctx, C1, tap0, tap1, u, delayed_u, layout, fuse_act):
+        if layout not in ("btf", "fbt"):
+            raise ValueError(f"layout must be 'btf' or 'fbt', got {layout!r}")
+        if layout == "btf" and fuse_act:
+            raise ValueError("fuse_act is supported for the (F,B,T) layout only")
+        if delayed_u is not None and delayed_u.shape != u.shape:
+            raise ValueError(
+                f"delayed_u must have shape {tuple(u.shape)}, got {tuple(delayed_u.shape)}")
+        dev = _require_cuda(C1, tap0, tap1, u, delayed_u)
+        lib = _abi.load()
+        if layout == "fbt":
+            out, saved = _fbt_forward(C1, tap0, tap1, u, bool(fuse_act))
+            c1, t0, t1, z, carries = saved
+            dims = tuple(z.shape)
+        else:
+            z = _c64(u)
+            B, T, F = _shape3(z, "u")
+            c1, t0, t1 = _coef(C1, F, "C1"), _coef(tap0, F, "tap0"), _coef(tap1, F, "tap1")
+            out = torch.empty((B, T, F), dtype=torch.complex64, device=dev)
+            carries = _carries(lib.rqf_btf_carry_count(B, T, F), dev)
+            scratch = _scratch(lib.rqf_btf_scratch_bytes(B, T, F), dev)
+            with _timing.launch("rqf_chunked_prospective_forward", B * T * F):
+                _abi.check(lib.rqf_chunked_prospective_forward(
+                    _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1), _abi.ptr(z), _abi.ptr(out),
+                    _abi.ptr(carries), _abi.ptr(scratch), B, T, F, _abi.stream_of(z)),
+                    "rqf_chunked_prospective_forward")
+            _done(dev)
+            dims = (B, T, F)
+        ctx.save_for_backward(c1, t0, t1, z, carries)
+        ctx.layout, ctx.fuse_act, ctx.dims = layout, bool(fuse_act), dims
+        ctx.has_lag = delayed_u is not None
+        return out
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_output):
+        gc1, gt0, gt1, gz, gzw = _tbptt_backward(ctx.saved_tensors, ctx.layout, ctx.dims,
+                                                 grad_output, ctx.fuse_act)
+        need = ctx.needs_input_grad
+        if ctx.has_lag:
+            gu, gd = gz, gzw
+        else:
+            gu, gd = gz.add_(gzw), None
+        return (gc1 if need[0] else None, gt0 if need[1] else None, gt1 if need[2] else None,
+                gu if need[3] else None, gd if (need[4] and gd is not None) else None, None, None)
+
+
+def _tbptt_backward(saved, layout, dims, grad_output, fuse_act):
+    """TBPTT(1) surrogate VJP kernel: returns (gc1, gtap0, gtap1, gz, gzw)."""
+    c1, t0, t1, z, carries = saved
+    dev = z.device
+    gy = _c64(grad_output)
+    lib = _abi.load()
+    gz = torch.empty_like(z)
+    gzw = torch.empty_like(z)
+    gc1, gt0, gt1 = torch.empty_like(c1), torch.empty_like(t0), torch.empty_like(t1)
+    d0, d1, d2 = dims
+    if layout == "fbt":
+        scratch = _scratch(lib.rqf_fbt_scratch_bytes(d0, d1, d2), dev)
+    else:
+        scratch = _scratch(lib.rqf_btf_scratch_bytes(d0, d1, d2), dev)
+    with _timing.launch("rqf_tbptt1_two_tap_backward", d0 * d1 * d2):
+        _abi.check(lib.rqf_tbptt1_two_tap_backward(
+            0 if layout == "btf" else 1, _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1),
+            _abi.ptr(z), _abi.ptr(carries), _abi.ptr(gy), _abi.ptr(gz), _abi.ptr(gzw),
+            _abi.ptr(gc1), _abi.ptr(gt0), _abi.ptr(gt1), _abi.ptr(scratch), d0, d1, d2,
+            int(bool(fuse_act)), _abi.stream_of(gy)), "rqf_tbptt1_two_tap_backward")
+    _done(dev)
+    return gc1, gt0, gt1, gz, gzw
+
+
+def tbptt1_two_tap_scan(u, C1, tap0, tap1, *, delayed_u=None, layout: str = "btf",
+                        fuse_act: bool = False):
+    """TBPTT(1) two-tap scan: forward value of the exact recurrence
+    h[n] = C1 h[n-1] + tap0 u[n] + tap1 u[n-1]; gradients of the one-step
+    rebuild with h[n-1] detached, as block.py:_scan_two_tap_with_grad_mode
+    (:904-954) builds them in autograd.  ``delayed_u`` is the lag-tap source
+    (e.g. W(x.detach())); ``layout`` "btf" (batch, time, filters) or "fbt"
+    (filters, batch, time); ``fuse_act`` applies split-ReLU (fbt only)."""
+    return _TBPTT1TwoTap.apply(C1, tap0, tap1, u, delayed_u, layout, fuse_act)
+
+
+def tbptt1_scan(u, C1, C2):
+    """TBPTT(1) single-tap scan x[n] = C1 x[n-1] + C2 u[n] with the surrogate
+    gradients of block.py:_scan_with_grad_mode (:882-902)."""
+    return _TBPTT1TwoTap.apply(C1, C2, torch.zeros_like(_c64(C2)), u, None, "btf", False)
+
+
+# --------------------------------------------- scan.py dispatch mirrors
+def _prepare(C1, C2, u, B):
+    if not C1.is_complex():
+        C1 = C1.to(torch.cfloat)
+    if not C2.is_complex():
+        C2 = C2.to(torch.cfloat)
+    num_filters = C1.shape[0]
+    if B is not None:
+        # (C2 ⊙ B) @ u == C2 * (B @ u): project, then scan with gain C2.
+        u_c = u.to(torch.cfloat) if not u.is_complex() else u
+        u = torch.einsum("nf,btf->btn", B.to(torch.cfloat), u_c)
+    elif u.shape[-1] == 1 and num_filters > 1:
+        u = u.expand(-1, -1, num_filters).contiguous()
+    return C1, C2, u
+
+
+def sequential_scan(C1, C2, u, B=None):
+    """CUDA branch of rqf_models/ops/scan.py:sequential_scan (:290-378):
+    x[n] = C1 x[n-1] + C2 u[n] (or (C2 ⊙ B) @ u[n]); real u is scanned
+    without materialising its zero imaginary part."""
+    C1, C2, u = _prepare(C1, C2, u, B)
+    return _triton_chunked_scan(C1, C2, u)
+
+
+def parallel_scan(C1, C2, u, B=None):
+    """CUDA branch of rqf_models/ops/scan.py:parallel_scan (:435-529); the
+    reference routes it to the same chunked kernel (:504-509)."""
+    return sequential_scan(C1, C2, u, B)
+
+
+def sequential_scan_abs(C1, C2, u, B=None):
+    """|sequential_scan(...)| (rqf_models/ops/scan.py:381-432)."""
+    return sequential_scan(C1, C2, u, B).abs()

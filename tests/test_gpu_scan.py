@@ -1,0 +1,362 @@
+"""GPU parity of the sm_100a scan kernels (through the C ABI) against the
+fp64 CPU oracle and the reference's golden vectors.
+
+Tolerances (written here, from the BASELINE contract): forward normwise max
+relative error <= 1e-4, gradients <= 1e-3, fp32 kernels vs fp64 oracle.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from _util import FWD_TOL, GRAD_TOL, assert_close, golden
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _device():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    import prospective_rqf_b200 as rqf
+
+    rqf.read_device_error(clear=True)
+    yield
+    rqf.check_device_errors()
+
+
+def rqf():
+    import prospective_rqf_b200
+
+    return prospective_rqf_b200
+
+
+def dev(a, dtype=torch.complex64, grad=False):
+    t = torch.from_numpy(np.ascontiguousarray(a)).to("cuda").to(dtype)
+    return t.requires_grad_(grad)
+
+
+def host(t):
+    return t.detach().cpu().numpy().astype(np.complex128)
+
+
+def crandn(rng, shape, scale=1.0):
+    return scale * (rng.standard_normal(shape) + 1j * rng.standard_normal(shape))
+
+
+def coeffs(rng, F, rmin=0.8, rmax=0.999):
+    mag = rng.uniform(rmin, rmax, F)
+    lam = mag * np.exp(1j * rng.uniform(0, 2 * np.pi, F))
+    return lam.astype(np.complex64).astype(np.complex128)
+
+
+def c64(a):
+    return np.asarray(a).astype(np.complex64).astype(np.complex128)
+
+
+# ----------------------------------------------------------- goldens
+def test_golden_scan_complex():
+    g = golden("scan_complex")
+    c1, c2, u = dev(g["c1"], grad=True), dev(g["c2"], grad=True), dev(g["u"], grad=True)
+    y = rqf()._triton_chunked_scan(c1, c2, u)
+    assert_close(host(y), g["y"], FWD_TOL, "y")
+    y.backward(dev(g["gy"]))
+    for t, k in ((c1, "gc1"), (c2, "gc2"), (u, "gu")):
+        assert_close(host(t.grad), g[k], GRAD_TOL, k)
+
+
+def test_golden_real_input_cfg1_style():
+    g = golden("scan_real_cfg1")
+    c1, c2 = dev(g["c1"], grad=True), dev(g["c2"], grad=True)
+    u = dev(g["u"], dtype=torch.float32, grad=True)
+    y = rqf().sequential_scan(c1, c2, u)
+    assert y.dtype == torch.complex64
+    assert_close(host(y), g["y"], FWD_TOL, "y")
+    (y.real ** 2 + y.imag ** 2).sum().backward()
+    assert u.grad.dtype == torch.float32
+    assert_close(host(c1.grad), g["gc1"], GRAD_TOL, "gc1")
+    assert_close(host(c2.grad), g["gc2"], GRAD_TOL, "gc2")
+    assert_close(u.grad.cpu().numpy(), g["gu"], GRAD_TOL, "gu")
+
+
+def test_golden_prospective_btf():
+    g = golden("prospective_btf")
+    ins = [dev(g[k], grad=True) for k in ("c1", "tap0", "tap1", "x")]
+    y = rqf()._triton_chunked_scan_prospective(*ins)
+    assert_close(host(y), g["y"], FWD_TOL, "y")
+    y.backward(dev(g["gy"]))
+    for t, k in zip(ins, ("gc1", "gt0", "gt1", "gx")):
+        assert_close(host(t.grad), g[k], GRAD_TOL, k)
+
+
+@pytest.mark.parametrize("name,fuse", [("fbt_split_relu", True), ("fbt_raw", False)])
+def test_golden_fbt(name, fuse):
+    g = golden(name)
+    ins = [dev(g[k], grad=True) for k in ("c1", "tap0", "tap1", "z")]
+    if fuse:
+        y = rqf().fbt_recompute_scan(*ins)
+    else:
+        y = rqf().fbt_prospective_scan(*ins, False)
+    assert_close(host(y), g["y"], FWD_TOL, "y")
+    y.backward(dev(g["gy"]))
+    for t, k in zip(ins, ("gc1", "gt0", "gt1", "gz")):
+        assert_close(host(t.grad), g[k], GRAD_TOL, k)
+
+
+def test_golden_tbptt():
+    g = golden("tbptt")
+    ins = [dev(g[k], grad=True) for k in ("c1", "tap0", "tap1", "u")]
+    lag = dev(g["u"], grad=True)
+    y = rqf().tbptt1_two_tap_scan(ins[3], ins[0], ins[1], ins[2], delayed_u=lag)
+    assert_close(host(y), g["y"], FWD_TOL, "y")
+    y.backward(dev(g["gy"]))
+    for t, k in zip(ins + [lag], ("gc1", "gt0", "gt1", "gu", "gd")):
+        assert_close(host(t.grad), g[k], GRAD_TOL, k)
+    ins2 = [dev(g[k], grad=True) for k in ("c1", "tap0", "tap1", "u")]
+    y2 = rqf().tbptt1_two_tap_scan(ins2[3], ins2[0], ins2[1], ins2[2])
+    y2.backward(dev(g["gy"]))
+    for t, k in zip(ins2, ("gc1_nolag", "gt0_nolag", "gt1_nolag", "gu_nolag")):
+        assert_close(host(t.grad), g[k], GRAD_TOL, k)
+
+
+# ------------------------------------------- (F,B,T) sweeps vs oracle
+FBT_T = [1, 2, 3, 31, 2047, 2048, 2049, 4097, 5001, 6144]
+
+
+@pytest.mark.parametrize("T", FBT_T)
+@pytest.mark.parametrize("fuse", [True, False])
+def test_fbt_vs_oracle(T, fuse):
+    rng = np.random.default_rng(1000 + T + int(fuse))
+    F, B = 3, 5
+    c1 = coeffs(rng, F)
+    t0, t1 = c64(crandn(rng, F, 0.5)), c64(crandn(rng, F, 0.5))
+    z = c64(crandn(rng, (F, B, T)))
+    gy = c64(crandn(rng, (F, B, T)))
+    ins = [dev(a, grad=True) for a in (c1, t0, t1, z)]
+    y = rqf().fbt_prospective_scan(*ins, fuse)
+    assert_close(host(y), oracle.two_tap_forward(c1, t0, t1, z, "fbt", fuse_act=fuse), FWD_TOL,
+                 "y")
+    y.backward(dev(gy))
+    ref = oracle.two_tap_backward(c1, t0, t1, z, gy, "fbt", fuse_act=fuse)
+    gz, gc1, gt0, gt1 = ref
+    for t, r, k in zip(ins, (gc1, gt0, gt1, gz), ("gc1", "gt0", "gt1", "gz")):
+        assert_close(host(t.grad), r, GRAD_TOL, k)
+
+
+def test_fbt_long_sequence_undamped_poles():
+    """T = 16000 with |C1| up to 1 - 2e-7 (the paper recipe's gamma -> 1e-6
+    edge) — the hardest case for cross-tile carry accuracy."""
+    rng = np.random.default_rng(7)
+    F, B, T = 8, 4, 16000
+    mag = np.concatenate([np.full(4, np.exp(-2e-7)), rng.uniform(0.9, 0.9999, 4)])
+    c1 = c64(mag * np.exp(1j * rng.uniform(0, np.pi, F)))
+    t0, t1 = c64(crandn(rng, F, 0.05)), c64(crandn(rng, F, 0.05))
+    z = c64(crandn(rng, (F, B, T)))
+    gy = c64(crandn(rng, (F, B, T)))
+    ins = [dev(a, grad=True) for a in (c1, t0, t1, z)]
+    y = rqf().fbt_recompute_scan(*ins)
+    assert_close(host(y), oracle.two_tap_forward(c1, t0, t1, z, "fbt", fuse_act=True), FWD_TOL,
+                 "y")
+    y.backward(dev(gy))
+    gz, gc1, gt0, gt1 = oracle.two_tap_backward(c1, t0, t1, z, gy, "fbt", fuse_act=True)
+    for t, r, k in zip(ins, (gc1, gt0, gt1, gz), ("gc1", "gt0", "gt1", "gz")):
+        assert_close(host(t.grad), r, GRAD_TOL, k)
+
+
+def test_fbt_full_size_linearity_and_adjoint():
+    """Config-2 shape (F=128, B=16, T=16000): size-independent properties of
+    the raw (linear) scan — linearity in z and the adjoint identity
+    Re<gy, J dz> == Re<J^H gy, dz> that the backward must satisfy."""
+    torch.manual_seed(0)
+    F, B, T = 128, 16, 16000
+    c1 = (torch.rand(F, device="cuda") * 0.1 + 0.9) * torch.exp(
+        1j * torch.rand(F, device="cuda") * 3.0)
+    c1 = c1.to(torch.complex64)
+    t0 = torch.randn(F, dtype=torch.complex64, device="cuda") * 0.1
+    t1 = torch.randn(F, dtype=torch.complex64, device="cuda") * 0.1
+    z1 = torch.randn(F, B, T, dtype=torch.complex64, device="cuda")
+    z2 = torch.randn(F, B, T, dtype=torch.complex64, device="cuda")
+    a, b = 0.7 - 0.2j, -1.3 + 0.4j
+    scan = rqf().fbt_prospective_scan
+    y12 = scan(c1, t0, t1, a * z1 + b * z2, False)
+    y1, y2 = scan(c1, t0, t1, z1, False), scan(c1, t0, t1, z2, False)
+    lin = (y12 - (a * y1 + b * y2)).abs().max() / y12.abs().max()
+    assert lin.item() < FWD_TOL
+    zz = z1.clone().requires_grad_(True)
+    y = scan(c1, t0, t1, zz, False)
+    gy = torch.randn_like(y)
+    (gz,) = torch.autograd.grad(y, zz, gy)
+    lhs = torch.sum(gy.conj() * y).real.double()  # <gy, J z1>
+    rhs = torch.sum(gz.conj() * z1).real.double()  # <J^H gy, z1>
+    assert abs(lhs - rhs).item() / abs(lhs).item() < GRAD_TOL
+
+
+def test_fbt_matches_btf_layout():
+    rng = np.random.default_rng(3)
+    B, T, F = 4, 3000, 40
+    c1 = coeffs(rng, F)
+    t0, t1 = c64(crandn(rng, F, 0.3)), c64(crandn(rng, F, 0.3))
+    x = dev(crandn(rng, (B, T, F)))
+    args = [dev(c1), dev(t0), dev(t1)]
+    y_btf = rqf()._triton_chunked_scan_prospective(*args, x)
+    y_fbt = rqf().fbt_prospective_scan(*args, x.permute(2, 0, 1).contiguous(), False)
+    err = (y_fbt.permute(1, 2, 0) - y_btf).abs().max() / y_btf.abs().max()
+    assert err.item() < FWD_TOL
+
+
+# ------------------------------------------- (B,T,F) sweeps vs oracle
+BTF_SHAPES = [(1, 1, 1), (2, 63, 5), (2, 128, 32), (3, 129, 33), (2, 1023, 8), (1, 777, 16),
+              (2, 4096, 96), (2, 16000, 32)]
+
+
+@pytest.mark.parametrize("B,T,F", BTF_SHAPES)
+def test_btf_plain_vs_oracle(B, T, F):
+    rng = np.random.default_rng(B * 100000 + T * 10 + F)
+    c1 = coeffs(rng, F)
+    c2 = c64(crandn(rng, F, 0.1))
+    u = c64(crandn(rng, (B, T, F)))
+    gy = c64(crandn(rng, (B, T, F)))
+    ins = [dev(a, grad=True) for a in (c1, c2, u)]
+    y = rqf()._triton_chunked_scan(*ins)
+    assert_close(host(y), oracle.chunked_scan(c1, c2, u), FWD_TOL, "y")
+    y.backward(dev(gy))
+    gc1, gc2, gu = oracle.chunked_scan_backward(c1, c2, u, gy)
+    for t, r, k in zip(ins, (gc1, gc2, gu), ("gc1", "gc2", "gu")):
+        assert_close(host(t.grad), r, GRAD_TOL, k)
+
+
+@pytest.mark.parametrize("B,T,F", BTF_SHAPES)
+def test_btf_prospective_vs_oracle(B, T, F):
+    rng = np.random.default_rng(7 + B * 100000 + T * 10 + F)
+    c1 = coeffs(rng, F)
+    t0, t1 = c64(crandn(rng, F, 0.5)), c64(crandn(rng, F, 0.5))
+    x = c64(crandn(rng, (B, T, F)))
+    gy = c64(crandn(rng, (B, T, F)))
+    ins = [dev(a, grad=True) for a in (c1, t0, t1, x)]
+    y = rqf()._triton_chunked_scan_prospective(*ins)
+    assert_close(host(y), oracle.two_tap_forward(c1, t0, t1, x, "btf"), FWD_TOL, "y")
+    y.backward(dev(gy))
+    gx, gc1, gt0, gt1 = oracle.two_tap_backward(c1, t0, t1, x, gy, "btf")
+    for t, r, k in zip(ins, (gc1, gt0, gt1, gx), ("gc1", "gt0", "gt1", "gx")):
+        assert_close(host(t.grad), r, GRAD_TOL, k)
+
+
+def test_btf_real_input_matches_promoted():
+    rng = np.random.default_rng(5)
+    B, T, F = 3, 500, 20
+    c1, c2 = coeffs(rng, F), c64(crandn(rng, F))
+    u = rng.standard_normal((B, T, F)).astype(np.float32)
+    ur = dev(u, dtype=torch.float32, grad=True)
+    uc = dev(u.astype(np.complex128), grad=True)
+    yr = rqf()._triton_chunked_scan(dev(c1), dev(c2), ur)
+    yc = rqf()._triton_chunked_scan(dev(c1), dev(c2), uc)
+    torch.testing.assert_close(yr, yc, rtol=1e-5, atol=1e-5)
+    gy = dev(crandn(rng, (B, T, F)))
+    yr.backward(gy)
+    yc.backward(gy)
+    torch.testing.assert_close(ur.grad, uc.grad.real, rtol=1e-5, atol=1e-5)
+
+
+def test_config1_exact_shapes():
+    """u real [32,161,128] ~ N(0,1), lambda = r e^{i theta},
+    r ~ U(0.90, 0.999), theta ~ U(0, pi), b ~ CN(0,1)/sqrt(2), y0 = 0; grads of
+    sum |y|^2 w.r.t. u, lambda and b."""
+    g = torch.Generator().manual_seed(0)
+    B, T, H = 32, 161, 128
+    u = torch.randn(B, T, H, generator=g)
+    r = 0.90 + 0.099 * torch.rand(H, generator=g)
+    th = torch.pi * torch.rand(H, generator=g)
+    lam = torch.polar(r, th)
+    b = torch.complex(torch.randn(H, generator=g), torch.randn(H, generator=g)) / np.sqrt(2.0)
+    ins = [lam.cuda().requires_grad_(True), b.cuda().requires_grad_(True),
+           u.cuda().requires_grad_(True)]
+    y = rqf().sequential_scan(*ins)
+    y_ref = oracle.chunked_scan(lam.numpy(), b.numpy(), u.numpy())
+    assert_close(host(y), y_ref, FWD_TOL, "y")
+    (y.real ** 2 + y.imag ** 2).sum().backward()
+    gc1, gc2, gu = oracle.chunked_scan_backward(lam.numpy(), b.numpy(), u.numpy(), 2.0 * y_ref)
+    assert_close(host(ins[0].grad), gc1, GRAD_TOL, "grad lambda")
+    assert_close(host(ins[1].grad), gc2, GRAD_TOL, "grad b")
+    assert_close(ins[2].grad.cpu().numpy(), gu.real, GRAD_TOL, "grad u")
+
+
+# ------------------------------------------------------- TBPTT(1)
+@pytest.mark.parametrize("layout", ["btf", "fbt"])
+@pytest.mark.parametrize("T", [1, 5, 2049, 3000])
+def test_tbptt_vs_oracle(layout, T):
+    rng = np.random.default_rng(T + (0 if layout == "btf" else 1))
+    F, B = 6, 3
+    shape = (B, T, F) if layout == "btf" else (F, B, T)
+    c1 = coeffs(rng, F)
+    t0, t1 = c64(crandn(rng, F, 0.5)), c64(crandn(rng, F, 0.5))
+    z = c64(crandn(rng, shape))
+    gy = c64(crandn(rng, shape))
+    for fuse in ([False] if layout == "btf" else [False, True]):
+        ins = [dev(a, grad=True) for a in (c1, t0, t1, z)]
+        lag = dev(z, grad=True)
+        y = rqf().tbptt1_two_tap_scan(ins[3], ins[0], ins[1], ins[2], delayed_u=lag,
+                                      layout=layout, fuse_act=fuse)
+        ref_y = oracle.two_tap_forward(c1, t0, t1, z, layout, fuse_act=fuse)
+        assert_close(host(y), ref_y, FWD_TOL, "y")
+        y.backward(dev(gy))
+        gz, gzw, gc1, gt0, gt1 = oracle.tbptt_backward(c1, t0, t1, z, gy, layout, fuse_act=fuse)
+        for t, r, k in zip(ins + [lag], (gc1, gt0, gt1, gz, gzw),
+                           ("gc1", "gt0", "gt1", "gz", "gzw")):
+            assert_close(host(t.grad), r, GRAD_TOL, f"{k} fuse={fuse}")
+
+
+# ------------------------------------------------------- edge cases
+def test_empty_shapes_give_zero_grads():
+    for shape in [(0, 10, 4), (2, 0, 4)]:
+        c1 = torch.full((4,), 0.9 + 0.1j, dtype=torch.complex64, device="cuda",
+                        requires_grad=True)
+        c2 = torch.ones(4, dtype=torch.complex64, device="cuda", requires_grad=True)
+        u = torch.zeros(shape, dtype=torch.complex64, device="cuda", requires_grad=True)
+        y = rqf()._triton_chunked_scan(c1, c2, u)
+        assert y.shape == shape
+        y.sum().abs().backward()
+        assert torch.count_nonzero(c1.grad).item() == 0
+        assert u.grad.shape == shape
+    z = torch.zeros((4, 0, 7), dtype=torch.complex64, device="cuda", requires_grad=True)
+    y = rqf().fbt_recompute_scan(c1, c1, c1, z)
+    assert y.shape == (4, 0, 7)
+
+
+def test_conj_and_noncontiguous_inputs():
+    rng = np.random.default_rng(11)
+    F, B, T = 4, 3, 300
+    c1 = coeffs(rng, F)
+    t0, t1 = c64(crandn(rng, F)), c64(crandn(rng, F))
+    z = c64(crandn(rng, (B, T, F)))
+    z_dev = dev(z).permute(2, 0, 1)  # non-contiguous (F,B,T) view
+    y = rqf().fbt_prospective_scan(dev(c1).conj(), dev(t0), dev(t1), z_dev, True)
+    ref = oracle.two_tap_forward(np.conj(c1), t0, t1, z.transpose(2, 0, 1), "fbt", fuse_act=True)
+    assert_close(host(y), ref, FWD_TOL, "y")
+
+
+def test_cpu_tensors_raise():
+    with pytest.raises(RuntimeError, match="CUDA"):
+        rqf().fbt_recompute_scan(torch.ones(2, dtype=torch.complex64),
+                                 torch.ones(2, dtype=torch.complex64),
+                                 torch.ones(2, dtype=torch.complex64),
+                                 torch.ones(2, 1, 3, dtype=torch.complex64))
+
+
+def test_repeated_calls_are_deterministic():
+    torch.manual_seed(3)
+    F, B, T = 16, 8, 7000
+    c1 = (0.95 * torch.exp(1j * torch.rand(F) * 3)).to(torch.complex64).cuda()
+    t0 = torch.randn(F, dtype=torch.complex64, device="cuda")
+    t1 = torch.randn(F, dtype=torch.complex64, device="cuda")
+    z = torch.randn(F, B, T, dtype=torch.complex64, device="cuda", requires_grad=True)
+    gy = torch.randn(F, B, T, dtype=torch.complex64, device="cuda")
+    outs = []
+    for _ in range(3):
+        c = c1.clone().requires_grad_(True)
+        y = rqf().fbt_recompute_scan(c, t0, t1, z)
+        gz, gc = torch.autograd.grad(y, (z, c), gy)
+        outs.append((y, gz, gc))
+    for y, gz, gc in outs[1:]:
+        assert torch.equal(y, outs[0][0])
+        assert torch.equal(gz, outs[0][1])
+        assert torch.equal(gc, outs[0][2])

@@ -1,0 +1,122 @@
+"""Host-side logic that needs no GPU: loud failure on CPU tensors (no
+fallback), argument checks, and the install() rebinding of the reference's
+dispatch names."""
+
+import os
+import sys
+import types
+from pathlib import Path
+
+import pytest
+import torch
+
+import prospective_rqf_b200 as rqf
+from prospective_rqf_b200 import integration, ops
+
+REFERENCE = Path(os.environ.get("RQF_REFERENCE", "/root/reference"))
+
+
+def c(*shape):
+    return torch.ones(*shape, dtype=torch.complex64)
+
+
+@pytest.mark.parametrize("fn,args", [
+    (rqf._triton_chunked_scan, (c(3), c(3), c(2, 5, 3))),
+    (rqf._triton_chunked_scan_prospective, (c(3), c(3), c(3), c(2, 5, 3))),
+    (rqf.fbt_prospective_scan, (c(3), c(3), c(3), c(3, 2, 5), True)),
+    (rqf.fbt_recompute_scan, (c(3), c(3), c(3), c(3, 2, 5))),
+    (rqf.sequential_scan, (c(3), c(3), torch.ones(2, 5, 3))),
+])
+def test_cpu_tensors_raise_no_fallback(fn, args):
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        fn(*args)
+
+
+def test_tbptt_rejects_bad_arguments():
+    with pytest.raises(ValueError):
+        rqf.tbptt1_two_tap_scan(c(2, 5, 3), c(3), c(3), c(3), layout="tbf")
+    with pytest.raises(ValueError):
+        rqf.tbptt1_two_tap_scan(c(2, 5, 3), c(3), c(3), c(3), layout="btf", fuse_act=True)
+    with pytest.raises(ValueError):
+        rqf.tbptt1_two_tap_scan(c(2, 5, 3), c(3), c(3), c(3), delayed_u=c(2, 4, 3))
+
+
+def _fake_reference(monkeypatch):
+    """Minimal stand-ins for the reference modules install() rebinds."""
+    names = {
+        "rqf_models": {},
+        "rqf_models.ops": {},
+        "rqf_models.ops.chunked_scan_kernel": {"_triton_chunked_scan": "orig",
+                                               "_triton_chunked_scan_prospective": "orig"},
+        "rqf_models.ops.scan": {"_triton_chunked_scan": "orig"},
+        "rqf_models.ops.fbt_scan_kernel": {"fbt_prospective_scan": "orig",
+                                           "fbt_recompute_scan": "orig"},
+        "rqf_models.backbones": {},
+        "rqf_models.backbones.rqf": {},
+        "rqf_models.backbones.rqf.block": {"_triton_chunked_scan_prospective": "orig"},
+        "rqf_models.backbones.rqf.pure": {"fbt_prospective_scan": "orig",
+                                          "fbt_recompute_scan": "orig"},
+    }
+    for name, attrs in names.items():
+        mod = types.ModuleType(name)
+        for k, v in attrs.items():
+            setattr(mod, k, v)
+        monkeypatch.setitem(sys.modules, name, mod)
+
+    class BaseRQFBlock:
+        def __init__(self, tbptt):
+            self.tbptt = tbptt
+
+        def _use_tbptt1_scan_grad(self):
+            return self.tbptt
+
+        def _scan_two_tap_with_grad_mode(self, u, C1, tap0, tap1, *, delayed_u=None):
+            return "reference-two-tap"
+
+        def _scan_with_grad_mode(self, u, C1, C2):
+            return "reference-single-tap"
+
+    sys.modules["rqf_models.backbones.rqf.block"].BaseRQFBlock = BaseRQFBlock
+    return BaseRQFBlock
+
+
+def test_install_rebinds_and_uninstall_restores(monkeypatch):
+    Block = _fake_reference(monkeypatch)
+    integration.uninstall()
+    try:
+        patched = rqf.install()
+        assert "rqf_models.ops.scan._triton_chunked_scan" in patched
+        assert sys.modules["rqf_models.ops.scan"]._triton_chunked_scan is ops._triton_chunked_scan
+        assert sys.modules["rqf_models.backbones.rqf.pure"].fbt_recompute_scan is \
+            ops.fbt_recompute_scan
+        assert sys.modules["rqf_models.backbones.rqf.block"]._triton_chunked_scan_prospective \
+            is ops._triton_chunked_scan_prospective
+        # TBPTT wrapper: CPU tensors keep the reference's own path.
+        blk = Block(tbptt=True)
+        assert blk._scan_two_tap_with_grad_mode(c(1, 2, 3), c(3), c(3), c(3)) == \
+            "reference-two-tap"
+        assert blk._scan_with_grad_mode(c(1, 2, 3), c(3), c(3)) == "reference-single-tap"
+    finally:
+        integration.uninstall()
+    assert sys.modules["rqf_models.ops.scan"]._triton_chunked_scan == "orig"
+    assert Block(tbptt=True)._scan_with_grad_mode(None, None, None) == "reference-single-tap"
+
+
+@pytest.mark.skipif(not (REFERENCE / "rqf_models").exists(), reason="reference tree absent")
+def test_install_against_the_reference_tree(monkeypatch):
+    monkeypatch.syspath_prepend(str(REFERENCE))
+    for name in list(sys.modules):
+        if name.startswith("rqf_models"):
+            monkeypatch.delitem(sys.modules, name)
+    integration.uninstall()
+    try:
+        patched = rqf.install()
+        import rqf_models.backbones.rqf.pure as pure
+        import rqf_models.ops.scan as scan
+
+        assert scan._triton_chunked_scan is ops._triton_chunked_scan
+        assert pure.fbt_recompute_scan is ops.fbt_recompute_scan
+        assert pure.fbt_prospective_scan is ops.fbt_prospective_scan
+        assert len(patched) == 10
+    finally:
+        integration.uninstall()
