@@ -43,6 +43,9 @@ def _lib():
         lib.rqfo_two_tap_forward.argtypes = [ci, i64, i64, i64, p, p, p, p, p, ci, ci]
         lib.rqfo_two_tap_backward.argtypes = [ci, i64, i64, i64, p, p, p, p, p, ci, p, p, p, p, ci]
         lib.rqfo_tbptt_backward.argtypes = [ci, i64, i64, i64, p, p, p, p, p, ci, p, p, p, p, p, ci]
+        lib.rqfo_two_tap_backward_masked.argtypes = [ci, i64, i64, i64, p, p, p, p, p, ci, p, p, p,
+                                                     p, p, ci]
+        lib.rqfo_two_tap_backward_masked.restype = ci
         lib.rqfo_max_threads.restype = ci
         for fn in (lib.rqfo_two_tap_forward, lib.rqfo_two_tap_backward, lib.rqfo_tbptt_backward):
             fn.restype = ci
@@ -86,9 +89,11 @@ def two_tap_forward(c1, tap0, tap1, x, layout: str = "btf", fuse_act: bool = Fal
 
 
 def two_tap_backward(c1, tap0, tap1, x, gy, layout: str = "btf", fuse_act: bool = False,
-                     nthreads: int | None = None):
+                     nthreads: int | None = None, mask=None):
     """Full-BPTT VJP of two_tap_forward: returns (gx, gc1, gtap0, gtap1)
-    (gtap1 is None when tap1 is None)."""
+    (gtap1 is None when tap1 is None).  With fuse_act, `mask` (bool array of
+    x.shape + (2,), [..., 0] for Re and [..., 1] for Im) overrides the sign
+    test of split-ReLU'."""
     c1, tap0 = _c128(c1), _c128(tap0)
     tap1 = None if tap1 is None else _c128(tap1)
     x, gy = _c128(x), _c128(gy)
@@ -98,12 +103,35 @@ def two_tap_backward(c1, tap0, tap1, x, gy, layout: str = "btf", fuse_act: bool 
     gt0 = np.zeros(nf, np.complex128)
     gt1 = None if tap1 is None else np.zeros(nf, np.complex128)
     d0, d1, d2 = x.shape
-    st = _lib().rqfo_two_tap_backward(_LAYOUT[layout], d0, d1, d2, _ptr(c1), _ptr(tap0),
-                                      _ptr(tap1), _ptr(x), _ptr(gy), int(fuse_act), _ptr(gx),
-                                      _ptr(gc1), _ptr(gt0), _ptr(gt1), _threads(nthreads))
+    m = None
+    if mask is not None:
+        m = np.ascontiguousarray(mask, dtype=np.uint8)
+        if m.shape != x.shape + (2,):
+            raise ValueError(f"mask must have shape {x.shape + (2,)}")
+    st = _lib().rqfo_two_tap_backward_masked(_LAYOUT[layout], d0, d1, d2, _ptr(c1), _ptr(tap0),
+                                             _ptr(tap1), _ptr(x), _ptr(gy), int(fuse_act),
+                                             _ptr(m), _ptr(gx), _ptr(gc1), _ptr(gt0), _ptr(gt1),
+                                             _threads(nthreads))
     if st:
         raise RuntimeError("oracle backward failed")
     return gx, gc1, gt0, gt1
+
+
+def relu_mask_from_output(act) -> np.ndarray:
+    """Split-ReLU decisions implied by a split-ReLU output (act > 0 per part)."""
+    act = np.asarray(act)
+    return np.stack([act.real > 0, act.imag > 0], axis=-1)
+
+
+def mask_disagreement(mask, y_ref) -> float:
+    """Largest |component| of the fp64 state where `mask` disagrees with its
+    sign, relative to max |y_ref| (0 when they agree everywhere)."""
+    ref = np.stack([y_ref.real > 0, y_ref.imag > 0], axis=-1)
+    bad = mask != ref
+    if not bad.any():
+        return 0.0
+    parts = np.stack([y_ref.real, y_ref.imag], axis=-1)
+    return float(np.max(np.abs(parts[bad])) / max(np.max(np.abs(parts)), 1e-300))
 
 
 def tbptt_backward(c1, tap0, tap1, x, gy, layout: str = "btf", fuse_act: bool = False,

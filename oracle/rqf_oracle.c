@@ -114,11 +114,29 @@ int rqfo_two_tap_forward(int layout, int64_t d0, int64_t d1, int64_t d2, const c
   return 0;
 }
 
-/* g_coef arrays: complex (F,). gx may alias nothing. */
+/* g_coef arrays: complex (F,).  When fuse_act and `mask` is non-NULL, the
+ * split-ReLU derivative is taken from mask (2 bytes per element: Re, Im;
+ * nonzero = active) instead of the sign of the recomputed state.  relu' is
+ * discontinuous at 0, so checks of an fp32 kernel at millions of elements
+ * pass the kernel's own forward decisions here and test separately that the
+ * decisions differ only where the state is within rounding of 0. */
+int rqfo_two_tap_backward_masked(int layout, int64_t d0, int64_t d1, int64_t d2, const cplx *c1,
+                                 const cplx *tap0, const cplx *tap1, const cplx *x,
+                                 const cplx *gy, int fuse_act, const unsigned char *mask,
+                                 cplx *gx, cplx *gc1, cplx *gt0, cplx *gt1, int nthreads);
+
 int rqfo_two_tap_backward(int layout, int64_t d0, int64_t d1, int64_t d2, const cplx *c1,
                           const cplx *tap0, const cplx *tap1, const cplx *x, const cplx *gy,
                           int fuse_act, cplx *gx, cplx *gc1, cplx *gt0, cplx *gt1,
                           int nthreads) {
+  return rqfo_two_tap_backward_masked(layout, d0, d1, d2, c1, tap0, tap1, x, gy, fuse_act, NULL,
+                                      gx, gc1, gt0, gt1, nthreads);
+}
+
+int rqfo_two_tap_backward_masked(int layout, int64_t d0, int64_t d1, int64_t d2, const cplx *c1,
+                                 const cplx *tap0, const cplx *tap1, const cplx *x,
+                                 const cplx *gy, int fuse_act, const unsigned char *mask,
+                                 cplx *gx, cplx *gc1, cplx *gt0, cplx *gt1, int nthreads) {
   const rows_t r = make_rows(layout, d0, d1, d2);
   set_threads(nthreads);
   cplx *part = (cplx *)calloc((size_t)(r.R > 0 ? r.R : 1) * 3, sizeof(cplx));
@@ -149,7 +167,15 @@ int rqfo_two_tap_backward(int layout, int64_t d0, int64_t d1, int64_t d2, const 
       cplx gnext = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
       for (int64_t t = r.T - 1; t >= 0; --t) {
         const cplx gt = gy[off + t * r.ts];
-        const cplx gbar = fuse_act ? mask_c(gt, ybuf[t + 1]) : gt;
+        cplx gbar = gt;
+        if (fuse_act) {
+          if (mask) {
+            const unsigned char *m = mask + 2 * (off + t * r.ts);
+            gbar = (m[0] ? creal(gt) : 0.0) + I * (m[1] ? cimag(gt) : 0.0);
+          } else {
+            gbar = mask_c(gt, ybuf[t + 1]);
+          }
+        }
         const cplx g = gbar + conj(lam) * gnext;
         const cplx xt = x[off + t * r.ts];
         const cplx xp = t > 0 ? x[off + (t - 1) * r.ts] : 0.0;

@@ -95,9 +95,7 @@ __global__ void __launch_bounds__(NW * 32) btf_fwd_kernel(const BtfArgs a) {
   float2 y = cz();
 #pragma unroll
   for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
-  float2 gK = lam;
-#pragma unroll
-  for (int s = 1; s < K; s <<= 1) gK = c_mul(gK, gK);
+  const float2 gK = c_pow2k(lam, (K == 8) ? 3 : (K == 16) ? 4 : 2);
   s_agg[warp][lane] = make_float4(gK.x, gK.y, y.x, y.y);
   __syncthreads();
   float2 Gw = cone(), Xw = cz(), Xall = cz();
@@ -187,9 +185,7 @@ __global__ void __launch_bounds__(NW * 32) btf_bwd_kernel(const BtfArgs a) {
   float2 y = cz();
 #pragma unroll
   for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
-  float2 gK = lam;
-#pragma unroll
-  for (int s = 1; s < K; s <<= 1) gK = c_mul(gK, gK);
+  const float2 gK = c_pow2k(lam, (K == 8) ? 3 : (K == 16) ? 4 : 2);
   // reverse local aggregate of the adjoint
   const float2 mu = c_conj(lam);
   float2 h = cz();
@@ -316,9 +312,7 @@ __global__ void __launch_bounds__(NW * 32) btf_tbptt_bwd_kernel(const BtfArgs a)
   float2 y = cz();
 #pragma unroll
   for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
-  float2 gK = lam;
-#pragma unroll
-  for (int s = 1; s < K; s <<= 1) gK = c_mul(gK, gK);
+  const float2 gK = c_pow2k(lam, (K == 8) ? 3 : (K == 16) ? 4 : 2);
   s_agg[warp][lane] = make_float4(gK.x, gK.y, y.x, y.y);
   __syncthreads();
   float2 Gw = cone(), Xw = cz(), Xall = cz();

@@ -1,0 +1,288 @@
+// Persistent row-sequential variant of the (F,B,T) two-tap scan, used when
+// there are at least as many rows as resident CTAs (3 and
+// 5 have 2k-8k rows of 16k samples).
+//
+// Each CTA owns rows blockIdx.x, blockIdx.x + gridDim.x, ... and walks each
+// row tile by tile, keeping the recurrence carry on chip between tiles, so no
+// inter-CTA communication (tickets, flags, look-back) is needed.  Because the
+// state entering a tile is known before the tile is scanned, it is folded into
+// the first thread's aggregate (cta_scan_entry_*), which removes the per-thread
+// gate powers of the look-back kernels.  The memory system is kept busy by an
+// S-stage cp.async pipeline: while tile i is computed, the inputs of the next
+// S-1 tiles (possibly of the next rows) are in flight into swizzled shared
+// memory.  Work cursors are advanced incrementally (no integer division in the
+// loop).
+//
+// Same tile length and per-tile carries as fbt_scan.cuh, so the forward and
+// backward of either variant pair up.
+#pragma once
+
+#include "fbt_scan.cuh"
+
+namespace rqf {
+
+constexpr int kRowsFwdStages = 3;
+constexpr int kRowsBwdStages = 2;  // 2 x 32 KB stages: 3 CTAs per SM
+
+template <int NT, int K, int NIN, int S>
+constexpr size_t fbt_rows_smem_bytes() {
+  return (size_t)S * NIN * NT * (K / 2) * sizeof(float4);
+}
+
+// Work cursor over (row, tile) items of this CTA.
+struct RowCursor {
+  int row, j, stage;
+  __device__ __forceinline__ void advance(int ntiles, int G, int S) {
+    if (++j == ntiles) {
+      j = 0;
+      row += G;
+    }
+    stage = (stage + 1 == S) ? 0 : stage + 1;
+  }
+};
+
+// Power table for the row being issued into stage `s`: copied from the
+// previous stage for later tiles of the same row, built in double precision
+// for a row's first tile.  Called by one thread, in issue order.
+template <int S>
+__device__ __forceinline__ void stage_table(float2 (*s_pw)[kPowTable], int s, bool first_tile,
+                                            const float2 *c1, int f) {
+  if (!first_tile) {
+    const int sp = (s + S - 1) % S;
+#pragma unroll
+    for (int i = 0; i < kPowTable; ++i) s_pw[s][i] = s_pw[sp][i];
+  } else {
+    pow2_table(c1[f], s_pw[s], kPowTable);
+  }
+}
+
+template <int K>
+__device__ __forceinline__ void fbt_issue_tile(float4 *wbuf, const float2 *row, int wstart, int T,
+                                               int lane) {
+#pragma unroll
+  for (int v = 0; v < K / 2; ++v) {
+    const int t = wstart + 2 * (v * 32 + lane);
+    const bool in = t < T;
+    cp_async16(&wbuf[swz<K>(v * 32 + lane)], row + (in ? t : 0), in);
+  }
+}
+
+template <int K>
+__device__ __forceinline__ void fbt_store_tile(float4 *wbuf, const float2 (&o)[K], float2 *row,
+                                               int wstart, int T, int lane) {
+#pragma unroll
+  for (int m = 0; m < K / 2; ++m)
+    wbuf[swz<K>(lane * (K / 2) + m)] =
+        make_float4(o[2 * m].x, o[2 * m].y, o[2 * m + 1].x, o[2 * m + 1].y);
+  __syncwarp();
+#pragma unroll
+  for (int v = 0; v < K / 2; ++v) {
+    const int t = wstart + 2 * (v * 32 + lane);
+    if (t < T) st_stream4(row + t, wbuf[swz<K>(v * 32 + lane)]);
+  }
+}
+
+// ------------------------------------------------------------ forward
+template <int NT, int K, int S, bool FUSE_ACT>
+__global__ void __launch_bounds__(NT) fbt_fwd_rows_kernel(const FbtArgs a) {
+  constexpr int NW = NT / 32, L = NT * K, LK = (K == 4) ? 2 : (K == 8) ? 3 : 4;
+  constexpr int WSZ = 16 * K;  // float4 slots per warp region
+  extern __shared__ __align__(16) float4 dsm[];
+  __shared__ float2 s_pw[S][kPowTable];
+  __shared__ float2 s_warp[NW];
+  __shared__ float2 s_zlast;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = gridDim.x, rows = (int)a.rows, T = (int)a.T, ntiles = a.ntiles;
+  const int wofs = warp * 32 * K;
+
+  RowCursor ic{(int)blockIdx.x, 0, 0};  // next item to issue
+  auto issue = [&]() {
+    if (ic.row < rows) {
+      fbt_issue_tile<K>(dsm + (size_t)ic.stage * NW * WSZ + warp * WSZ,
+                        a.z + (size_t)ic.row * T, ic.j * L + wofs, T, lane);
+      if (tid == 0) stage_table<S>(s_pw, ic.stage, ic.j == 0, a.c1, ic.row / a.batch);
+      ic.advance(ntiles, G, S);
+    }
+    cp_async_commit();
+  };
+
+#pragma unroll
+  for (int s = 0; s < S - 1; ++s) issue();
+  RowCursor pc{(int)blockIdx.x, 0, 0};  // item being processed
+  float2 carry = cz(), lam = cz(), t0 = cz(), t1 = cz(), lanepow = cz();
+  while (pc.row < rows) {
+    cp_async_wait<S - 2>();
+    __syncthreads();
+    issue();
+    const float2 *pw = s_pw[pc.stage];
+    if (pc.j == 0) {  // new row: per-row constants
+      const int f = pc.row / a.batch;
+      lam = pw[0];
+      t0 = a.tap0[f];
+      t1 = a.tap1[f];
+      lanepow = pow_from_table<false>(pw, LK, lane);
+      carry = cz();
+    }
+    float4 *wbuf = dsm + (size_t)pc.stage * NW * WSZ + warp * WSZ;
+    float2 z[K];
+    read_blocked<K>(wbuf, z, lane);
+    float2 zp = shfl_up2(z[K - 1], 1);
+    if (lane == 0) {
+      if (warp > 0)
+        zp = read_sample<K>(wbuf - WSZ, 32 * K - 1);
+      else
+        zp = (pc.j > 0) ? s_zlast : cz();
+    }
+    float2 b[K];
+    b[0] = c_fma(t1, zp, c_mul(t0, z[0]));
+#pragma unroll
+    for (int k = 1; k < K; ++k) b[k] = c_fma(t1, z[k - 1], c_mul(t0, z[k]));
+    float2 y = cz();
+#pragma unroll
+    for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
+    float2 e, At;
+    cta_scan_entry_fwd<NT, LK>(y, carry, pw, lanepow, e, At, s_warp);
+    if (tid == NT - 1) s_zlast = z[K - 1];
+    if (tid == 0) a.carries[(size_t)pc.row * ntiles + pc.j] = carry;
+    carry = At;  // entry of the next tile of this row
+    float2 o[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      e = c_fma(lam, e, b[k]);
+      o[k] = FUSE_ACT ? c_relu(e) : e;
+    }
+    fbt_store_tile<K>(wbuf, o, a.out + (size_t)pc.row * T, pc.j * L + wofs, T, lane);
+    pc.advance(ntiles, G, S);
+  }
+  cp_async_wait<0>();
+}
+
+// ------------------------------------------------ full-BPTT backward
+// Tiles of a row in reverse time order; the adjoint carry g[tile end] stays
+// on chip.  Coefficient-gradient partial sums accumulate over the whole row
+// and are written once per row: partials[row*3 + {0,1,2}].
+template <int NT, int K, int S, bool FUSE_ACT>
+__global__ void __launch_bounds__(NT, 3) fbt_bwd_rows_kernel(const FbtArgs a) {
+  constexpr int NW = NT / 32, L = NT * K, LK = (K == 4) ? 2 : (K == 8) ? 3 : 4;
+  constexpr int WSZ = 16 * K;
+  extern __shared__ __align__(16) float4 dsm[];  // [S][2 inputs][NW][WSZ]
+  __shared__ float2 s_pw[S][kPowTable];
+  __shared__ float2 s_meta[S][2];  // {entry carry C, z sample before the tile}
+  __shared__ float2 s_warp_f[NW];
+  __shared__ float2 s_warp_r[NW];
+  __shared__ float2 s_red[3][NW];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = gridDim.x, rows = (int)a.rows, T = (int)a.T, ntiles = a.ntiles;
+  const int wofs = warp * 32 * K;
+  constexpr size_t stage_sz = (size_t)2 * NW * WSZ;
+
+  // j counts processed tiles of the row; the tile index in time is ntiles-1-j.
+  RowCursor ic{(int)blockIdx.x, 0, 0};
+  auto issue = [&]() {
+    if (ic.row < rows) {
+      const int jt = ntiles - 1 - ic.j;
+      float4 *base = dsm + ic.stage * stage_sz;
+      const size_t roff = (size_t)ic.row * T;
+      fbt_issue_tile<K>(base + warp * WSZ, a.z + roff, jt * L + wofs, T, lane);
+      fbt_issue_tile<K>(base + (NW + warp) * WSZ, a.gout + roff, jt * L + wofs, T, lane);
+      if (tid == 0) {
+        const int t0 = jt * L;
+        cp_async8(&s_meta[ic.stage][0], a.carries + (size_t)ic.row * ntiles + jt, true);
+        cp_async8(&s_meta[ic.stage][1], a.z + roff + (t0 > 0 ? t0 - 1 : 0), t0 > 0);
+        stage_table<S>(s_pw, ic.stage, ic.j == 0, a.c1, ic.row / a.batch);
+      }
+      ic.advance(ntiles, G, S);
+    }
+    cp_async_commit();
+  };
+
+#pragma unroll
+  for (int s = 0; s < S - 1; ++s) issue();
+  RowCursor pc{(int)blockIdx.x, 0, 0};
+  float2 dcarry = cz(), lam = cz(), t0 = cz(), t1 = cz(), lpow_f = cz(), lpow_r = cz();
+  float2 acc_c1 = cz(), acc_t0 = cz(), acc_t1 = cz();
+  while (pc.row < rows) {
+    cp_async_wait<S - 2>();
+    __syncthreads();
+    issue();
+    const int s = pc.stage;
+    const int jt = ntiles - 1 - pc.j;
+    const float2 *pw = s_pw[s];
+    if (pc.j == 0) {
+      const int f = pc.row / a.batch;
+      lam = pw[0];
+      t0 = a.tap0[f];
+      t1 = a.tap1[f];
+      lpow_f = pow_from_table<false>(pw, LK, lane);
+      lpow_r = pow_from_table<true>(pw, LK, 31 - lane);
+      dcarry = cz();
+    }
+    float4 *zbuf = dsm + s * stage_sz + warp * WSZ;
+    float4 *gbuf = dsm + s * stage_sz + (NW + warp) * WSZ;
+    float2 z[K], go[K];
+    read_blocked<K>(zbuf, z, lane);
+    read_blocked<K>(gbuf, go, lane);
+    float2 zp = shfl_up2(z[K - 1], 1);
+    if (lane == 0) zp = warp > 0 ? read_sample<K>(zbuf - WSZ, 32 * K - 1) : s_meta[s][1];
+
+    float2 b[K];
+    b[0] = c_fma(t1, zp, c_mul(t0, z[0]));
+#pragma unroll
+    for (int k = 1; k < K; ++k) b[k] = c_fma(t1, z[k - 1], c_mul(t0, z[k]));
+    float2 y = cz();
+#pragma unroll
+    for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
+    float2 e, At;
+    cta_scan_entry_fwd<NT, LK>(y, s_meta[s][0], pw, lpow_f, e, At, s_warp_f);
+    float2 yprev[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      yprev[k] = e;
+      e = c_fma(lam, e, b[k]);
+      b[k] = FUSE_ACT ? c_relu_mask(go[k], e) : go[k];
+    }
+    const float2 mu = c_conj(lam);
+    float2 h = cz();
+#pragma unroll
+    for (int k = K - 1; k >= 0; --k) h = c_fma(mu, h, b[k]);
+    float2 gnext, Art;
+    cta_scan_entry_rev<NT, LK>(h, dcarry, pw, lpow_r, gnext, Art, s_warp_r);
+    dcarry = Art;  // g at this tile's first sample: right entry of the tile before it
+    float2 gz[K];
+#pragma unroll
+    for (int k = K - 1; k >= 0; --k) {
+      const float2 g = c_fma(mu, gnext, b[k]);
+      gz[k] = c_cfma(t1, gnext, c_cfma(t0, g, cz()));
+      acc_c1 = c_cfma(yprev[k], g, acc_c1);
+      acc_t0 = c_cfma(z[k], g, acc_t0);
+      acc_t1 = c_cfma(k > 0 ? z[k - 1] : zp, g, acc_t1);
+      gnext = g;
+    }
+    fbt_store_tile<K>(gbuf, gz, a.out + (size_t)pc.row * T, jt * L + wofs, T, lane);
+    if (jt == 0) {  // row finished: deterministic CTA reduction of the row's sums
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        acc_c1 = c_add(acc_c1, shfl_xor2(acc_c1, o));
+        acc_t0 = c_add(acc_t0, shfl_xor2(acc_t0, o));
+        acc_t1 = c_add(acc_t1, shfl_xor2(acc_t1, o));
+      }
+      if (lane == 0) {
+        s_red[0][warp] = acc_c1;
+        s_red[1][warp] = acc_t0;
+        s_red[2][warp] = acc_t1;
+      }
+      __syncthreads();
+      if (tid < 3) {
+        float2 sum = cz();
+#pragma unroll
+        for (int w = 0; w < NW; ++w) sum = c_add(sum, s_red[tid][w]);
+        a.partials[(size_t)pc.row * 3 + tid] = sum;
+      }
+      acc_c1 = acc_t0 = acc_t1 = cz();
+    }
+    pc.advance(ntiles, G, S);
+  }
+  cp_async_wait<0>();
+}
+
+}  // namespace rqf

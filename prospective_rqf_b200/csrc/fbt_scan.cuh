@@ -45,6 +45,7 @@ constexpr int kFbtThreads = 256;
 constexpr int kFbtK = 8;
 constexpr int kFbtTile = kFbtThreads * kFbtK;  // 2048 samples
 constexpr int kFbtLog2Tile = 11;
+constexpr int kPowTable = 12;  // lambda^(2^i), i <= log2(tile)
 
 // Load the K samples [tfirst, tfirst+K) of this thread (blocked order).
 template <int K, bool VEC>
@@ -89,24 +90,22 @@ __device__ __forceinline__ void fbt_store(float2 *__restrict__ row, int64_t wsta
   }
 }
 
-template <int K>
-__device__ __forceinline__ float2 c_pow_k(float2 lam) {
-  float2 g = lam;
-#pragma unroll
-  for (int s = 1; s < K; s <<= 1) g = c_mul(g, g);
-  return g;
-}
-
 // ------------------------------------------------------------ forward
 template <int NT, int K, bool VEC, bool FUSE_ACT>
 __global__ void __launch_bounds__(NT) fbt_fwd_kernel(const FbtArgs a) {
   constexpr int NW = NT / 32, L = NT * K;
+  constexpr int LK = (K == 4) ? 2 : (K == 8) ? 3 : 4;
   __shared__ __align__(16) float4 s_buf[NW][16 * K];
-  __shared__ float4 s_warp[NW];
+  __shared__ float2 s_warp[NW];
+  __shared__ float2 s_pw[kPowTable];
   __shared__ unsigned s_ticket;
   __shared__ float2 s_carry;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) s_ticket = atomicAdd(a.ticket, 1u);
+  if (tid == 0) {
+    const unsigned t = atomicAdd(a.ticket, 1u);
+    s_ticket = t;
+    pow2_table(a.c1[(t / (unsigned)a.ntiles) / a.batch], s_pw, kPowTable);
+  }
   __syncthreads();
   const unsigned tk = s_ticket;
   const int64_t row = tk / (unsigned)a.ntiles;
@@ -130,8 +129,8 @@ __global__ void __launch_bounds__(NT) fbt_fwd_kernel(const FbtArgs a) {
 #pragma unroll
   for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
 
-  float2 G, X, Gt, At;
-  cta_scan_fwd<NT>(c_pow_k<K>(lam), y, G, X, Gt, At, s_warp);
+  float2 G, X, At;
+  cta_scan_const_fwd<NT, LK>(y, s_pw, G, X, At, s_warp);
 
   if (tid == 0) {
     u64 *fl = a.flags + row * (int64_t)a.ntiles * 2;
@@ -141,7 +140,7 @@ __global__ void __launch_bounds__(NT) fbt_fwd_kernel(const FbtArgs a) {
       if (has_next) flag_publish2(fl, At, kInclusive);
     } else {
       if (has_next) flag_publish2(fl + 2 * j, At, kAggregate);
-      const float2 M = c_pow2k(lam, a.log2L);
+      const float2 M = s_pw[a.log2L];
       C = lookback_const(fl, j, M);
       if (has_next) flag_publish2(fl + 2 * j, c_fma(M, C, At), kInclusive);
     }
@@ -164,14 +163,20 @@ template <int NT, int K, bool VEC, bool FUSE_ACT>
 __global__ void __launch_bounds__(NT) fbt_bwd_kernel(const FbtArgs a) {
   constexpr int NW = NT / 32;
   constexpr int L = NT * K;
+  constexpr int LK = (K == 4) ? 2 : (K == 8) ? 3 : 4;
   __shared__ __align__(16) float4 s_buf[NW][16 * K];
-  __shared__ float4 s_warp_f[NW];
-  __shared__ float4 s_warp_r[NW];
+  __shared__ float2 s_warp_f[NW];
+  __shared__ float2 s_warp_r[NW];
+  __shared__ float2 s_pw[kPowTable];
   __shared__ float2 s_red[3][NW];
   __shared__ unsigned s_ticket;
   __shared__ float2 s_entry;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) s_ticket = atomicAdd(a.ticket, 1u);
+  if (tid == 0) {
+    const unsigned t = atomicAdd(a.ticket, 1u);
+    s_ticket = t;
+    pow2_table(a.c1[(t / (unsigned)a.ntiles) / a.batch], s_pw, kPowTable);
+  }
   __syncthreads();
   const unsigned tk = s_ticket;
   const int64_t row = tk / (unsigned)a.ntiles;
@@ -199,9 +204,8 @@ __global__ void __launch_bounds__(NT) fbt_bwd_kernel(const FbtArgs a) {
   float2 y = cz();
 #pragma unroll
   for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
-  const float2 lamK = c_pow_k<K>(lam);
-  float2 G, X, Gt, At;
-  cta_scan_fwd<NT>(lamK, y, G, X, Gt, At, s_warp_f);
+  float2 G, X, At;
+  cta_scan_const_fwd<NT, LK>(y, s_pw, G, X, At, s_warp_f);
   float2 e = c_fma(G, C, X);
   float2 yprev[K];  // y[t-1] per sample; reuse b[] storage for the masked cotangent
 #pragma unroll
@@ -216,8 +220,8 @@ __global__ void __launch_bounds__(NT) fbt_bwd_kernel(const FbtArgs a) {
   float2 h = cz();
 #pragma unroll
   for (int k = K - 1; k >= 0; --k) h = c_fma(mu, h, b[k]);
-  float2 Gr, Xr, Grt, Art;
-  cta_scan_rev<NT>(c_conj(lamK), h, Gr, Xr, Grt, Art, s_warp_r);
+  float2 Gr, Xr, Art;
+  cta_scan_const_rev<NT, LK>(h, s_pw, Gr, Xr, Art, s_warp_r);
   if (tid == 0) {
     u64 *fl = a.flags + row * (int64_t)a.ntiles * 2;
     const bool has_next = p + 1 < a.ntiles;
@@ -226,7 +230,7 @@ __global__ void __launch_bounds__(NT) fbt_bwd_kernel(const FbtArgs a) {
       if (has_next) flag_publish2(fl, Art, kInclusive);
     } else {
       if (has_next) flag_publish2(fl + 2 * p, Art, kAggregate);
-      const float2 M = c_pow2k(mu, a.log2L);
+      const float2 M = c_conj(s_pw[a.log2L]);
       D = lookback_const(fl, p, M);
       if (has_next) flag_publish2(fl + 2 * p, c_fma(M, D, Art), kInclusive);
     }
@@ -277,11 +281,14 @@ template <int NT, int K, bool VEC, bool FUSE_ACT>
 __global__ void __launch_bounds__(NT) fbt_tbptt_bwd_kernel(const FbtArgs a) {
   constexpr int NW = NT / 32;
   constexpr int L = NT * K;
+  constexpr int LK = (K == 4) ? 2 : (K == 8) ? 3 : 4;
   __shared__ __align__(16) float4 s_buf[NW][16 * K];
-  __shared__ float4 s_warp_f[NW];
+  __shared__ float2 s_warp_f[NW];
+  __shared__ float2 s_pw[kPowTable];
   __shared__ float2 s_first[NW + 1];
   __shared__ float2 s_red[3][NW];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) pow2_table(a.c1[(blockIdx.x / (unsigned)a.ntiles) / a.batch], s_pw, kPowTable);
   const int64_t row = blockIdx.x / (unsigned)a.ntiles;
   const int j = (int)(blockIdx.x - (unsigned)(row * a.ntiles));
   const int f = (int)(row / a.batch);
@@ -305,8 +312,9 @@ __global__ void __launch_bounds__(NT) fbt_tbptt_bwd_kernel(const FbtArgs a) {
   float2 y = cz();
 #pragma unroll
   for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
-  float2 G, X, Gt, At;
-  cta_scan_fwd<NT>(c_pow_k<K>(lam), y, G, X, Gt, At, s_warp_f);
+  __syncthreads();  // s_pw
+  float2 G, X, At;
+  cta_scan_const_fwd<NT, LK>(y, s_pw, G, X, At, s_warp_f);
   float2 e = c_fma(G, C, X);
   float2 yprev[K];
 #pragma unroll

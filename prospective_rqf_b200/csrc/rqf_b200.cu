@@ -8,6 +8,7 @@
 
 #include "../../include/rqf_b200.h"
 #include "btf_scan.cuh"
+#include "fbt_rows.cuh"
 #include "fbt_scan.cuh"
 #include "reduce.cuh"
 
@@ -47,6 +48,34 @@ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline int launch_status() {
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? RQF_OK : RQF_ERR_LAUNCH;
+}
+
+// Resident CTAs of a persistent kernel on the current device (sets its dynamic
+// shared-memory limit first).  Returns 0 when the kernel cannot be resident.
+template <typename Kern>
+int64_t resident_ctas(Kern kernel, int threads, size_t smem) {
+  int dev = 0, sms = 0, per_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) !=
+      cudaSuccess)
+    return 0;
+  return (int64_t)sms * per_sm;
+}
+
+// Persistent row-sequential launch when every resident CTA gets at least one
+// whole row; returns false (nothing launched) when the look-back tile kernels
+// should be used instead.
+template <typename Kern>
+bool launch_rows(Kern kernel, size_t smem, const FbtArgs &a, cudaStream_t stream) {
+  if (a.T > 0x7fffffffLL || a.rows > 0x7fffffffLL) return false;  // 32-bit cursors
+  const int64_t g = resident_ctas(kernel, kFbtThreads, smem);
+  if (g <= 0 || a.rows < g) return false;
+  kernel<<<(unsigned)g, kFbtThreads, smem, stream>>>(a);
+  return true;
 }
 
 inline int zero_complex(float *p, int64_t n, cudaStream_t s) {
@@ -304,9 +333,18 @@ int rqf_fbt_prospective_forward(const float *c1, const float *tap0, const float 
     return RQF_ERR_ALIGN;
   FbtArgs a = fbt_args(c1, tap0, tap1, z, nullptr, out, nullptr, carries, scratch, filters,
                        batch, time);
+  const bool vec = (time % 2 == 0) && aligned(z, 16) && aligned(out, 16);
+  if (vec) {
+    constexpr size_t smem = fbt_rows_smem_bytes<kFbtThreads, kFbtK, 1, kRowsFwdStages>();
+    const bool done =
+        fuse_act ? launch_rows(fbt_fwd_rows_kernel<kFbtThreads, kFbtK, kRowsFwdStages, true>, smem,
+                               a, stream)
+                 : launch_rows(fbt_fwd_rows_kernel<kFbtThreads, kFbtK, kRowsFwdStages, false>,
+                               smem, a, stream);
+    if (done) return launch_status();
+  }
   const Scratch lay = scratch_layout(a.rows, a.ntiles);
   if ((st = clear_lookback(scratch, lay, stream)) != RQF_OK) return st;
-  const bool vec = (time % 2 == 0) && aligned(z, 16) && aligned(out, 16);
   const unsigned grid = (unsigned)(a.rows * a.ntiles);
   if (vec) {
     if (fuse_act)
@@ -343,10 +381,25 @@ int rqf_fbt_prospective_backward(const float *c1, const float *tap0, const float
     return RQF_ERR_ALIGN;
   FbtArgs a = fbt_args(c1, tap0, tap1, z, grad_out, grad_z, nullptr, const_cast<float *>(carries),
                        scratch, filters, batch, time);
-  const Scratch lay = scratch_layout(a.rows, a.ntiles);
-  if ((st = clear_lookback(scratch, lay, stream)) != RQF_OK) return st;
   const bool vec =
       (time % 2 == 0) && aligned(z, 16) && aligned(grad_out, 16) && aligned(grad_z, 16);
+  if (vec) {
+    constexpr size_t smem = fbt_rows_smem_bytes<kFbtThreads, kFbtK, 2, kRowsBwdStages>();
+    const bool done =
+        fuse_act ? launch_rows(fbt_bwd_rows_kernel<kFbtThreads, kFbtK, kRowsBwdStages, true>, smem,
+                               a, stream)
+                 : launch_rows(fbt_bwd_rows_kernel<kFbtThreads, kFbtK, kRowsBwdStages, false>,
+                               smem, a, stream);
+    if (done) {
+      if ((st = launch_status()) != RQF_OK) return st;
+      reduce_partials_kernel<<<(unsigned)filters, 256, 0, stream>>>(
+          a.partials, reinterpret_cast<float2 *>(grad_c1), reinterpret_cast<float2 *>(grad_tap0),
+          reinterpret_cast<float2 *>(grad_tap1), batch, batch, 1, 1);
+      return launch_status();
+    }
+  }
+  const Scratch lay = scratch_layout(a.rows, a.ntiles);
+  if ((st = clear_lookback(scratch, lay, stream)) != RQF_OK) return st;
   const unsigned grid = (unsigned)(a.rows * a.ntiles);
   if (vec) {
     if (fuse_act)

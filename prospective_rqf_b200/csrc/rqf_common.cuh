@@ -265,6 +265,156 @@ __device__ __forceinline__ void cta_scan_rev(float2 g, float2 a, float2 &G, floa
   At = Xall;
 }
 
+// ------------------------------------------- time-invariant CTA scans
+// For a constant gate lambda the composition of n steps has gate lambda^n.
+// Building lambda^n by repeated multiplication of one rounded lambda^K makes
+// its phase error grow linearly with n (255 products per 2048-sample tile),
+// which breaks fp32 parity for undamped poles (|lambda| -> 1) over long
+// sequences.  Instead every power is taken from a table pw[i] = lambda^(2^i)
+// built in double precision, so each power carries at most log2(n) roundings.
+
+// Fill pw[0..n) with lambda^(2^i) (one thread; double precision squaring).
+__device__ __forceinline__ void pow2_table(float2 lam, float2 *pw, int n) {
+  double re = lam.x, im = lam.y;
+  for (int i = 0; i < n; ++i) {
+    pw[i] = make_float2((float)re, (float)im);
+    const double nr = re * re - im * im;
+    const double ni = 2.0 * re * im;
+    re = nr;
+    im = ni;
+  }
+}
+
+// lambda^(2^s * n) from the table (conjugated when CONJ).
+template <bool CONJ>
+__device__ __forceinline__ float2 pow_from_table(const float2 *pw, int s, unsigned n) {
+  float2 r = cone();
+  for (int i = 0; n; ++i, n >>= 1)
+    if (n & 1u) r = c_mul(r, CONJ ? c_conj(pw[s + i]) : pw[s + i]);
+  return r;
+}
+
+// Forward scan of per-thread aggregates `a` (K samples each, zero entry) with
+// the constant gate lambda: returns the exclusive composition (G, X) of the
+// earlier threads (G = lambda^(K*tid)) and the CTA total value At.
+template <int NT, int LK>
+__device__ __forceinline__ void cta_scan_const_fwd(float2 a, const float2 *pw, float2 &G, float2 &X,
+                                                   float2 &At, float2 *s_warp) {
+  constexpr int NW = NT / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int d = 0; d < 5; ++d) {
+    const int o = 1 << d;
+    const float2 v = shfl_up2(a, o);
+    if (lane >= o) a = c_fma(pw[LK + d], v, a);
+  }
+  float2 ae = shfl_up2(a, 1);
+  if (lane == 0) ae = cz();
+  if (lane == 31) s_warp[warp] = a;
+  __syncthreads();
+  const float2 gw = pw[LK + 5];  // lambda^(32K)
+  float2 Xw = cz(), Xall = cz();
+#pragma unroll
+  for (int w = 0; w < NW; ++w) {
+    if (w == warp) Xw = Xall;
+    Xall = c_fma(gw, Xall, s_warp[w]);
+  }
+  X = c_fma(pow_from_table<false>(pw, LK, lane), Xw, ae);
+  G = pow_from_table<false>(pw, LK, threadIdx.x);
+  At = Xall;
+}
+
+// Reverse-time counterpart with gate conj(lambda): (G, X) compose the LATER
+// threads (G = conj(lambda)^(K*(NT-1-tid))); At is the CTA total.
+template <int NT, int LK>
+__device__ __forceinline__ void cta_scan_const_rev(float2 a, const float2 *pw, float2 &G, float2 &X,
+                                                   float2 &At, float2 *s_warp) {
+  constexpr int NW = NT / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int d = 0; d < 5; ++d) {
+    const int o = 1 << d;
+    const float2 v = shfl_down2(a, o);
+    if (lane + o < 32) a = c_fma(c_conj(pw[LK + d]), v, a);
+  }
+  float2 ae = shfl_down2(a, 1);
+  if (lane == 31) ae = cz();
+  if (lane == 0) s_warp[warp] = a;
+  __syncthreads();
+  const float2 gw = c_conj(pw[LK + 5]);
+  float2 Xw = cz(), Xall = cz();
+#pragma unroll
+  for (int w = NW - 1; w >= 0; --w) {
+    if (w == warp) Xw = Xall;
+    Xall = c_fma(gw, Xall, s_warp[w]);
+  }
+  X = c_fma(pow_from_table<true>(pw, LK, 31 - lane), Xw, ae);
+  G = pow_from_table<true>(pw, LK, NT - 1 - threadIdx.x);
+  At = Xall;
+}
+
+// Scans for the row-sequential kernels, where the state entering the tile is
+// known before the scan: it is folded into the first thread's aggregate, so
+// the scan directly yields each thread's entry state E and the state after the
+// tile At, and no per-thread power lambda^(K*tid) is needed.  lanepow is
+// lambda^(K*lane) (forward) or conj(lambda)^(K*(31-lane)) (reverse), cached
+// per row by the caller.
+template <int NT, int LK>
+__device__ __forceinline__ void cta_scan_entry_fwd(float2 a, float2 entry, const float2 *pw,
+                                                   float2 lanepow, float2 &E, float2 &At,
+                                                   float2 *s_warp) {
+  constexpr int NW = NT / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) a = c_fma(pw[LK], entry, a);
+#pragma unroll
+  for (int d = 0; d < 5; ++d) {
+    const int o = 1 << d;
+    const float2 v = shfl_up2(a, o);
+    if (lane >= o) a = c_fma(pw[LK + d], v, a);
+  }
+  float2 ae = shfl_up2(a, 1);
+  if (lane == 0) ae = cz();
+  if (lane == 31) s_warp[warp] = a;
+  __syncthreads();
+  const float2 gw = pw[LK + 5];
+  float2 Xw = cz(), Xall = cz();
+#pragma unroll
+  for (int w = 0; w < NW; ++w) {
+    if (w == warp) Xw = Xall;
+    Xall = c_fma(gw, Xall, s_warp[w]);
+  }
+  E = threadIdx.x == 0 ? entry : c_fma(lanepow, Xw, ae);
+  At = Xall;
+}
+
+template <int NT, int LK>
+__device__ __forceinline__ void cta_scan_entry_rev(float2 a, float2 entry, const float2 *pw,
+                                                   float2 lanepow, float2 &E, float2 &At,
+                                                   float2 *s_warp) {
+  constexpr int NW = NT / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == NT - 1) a = c_fma(c_conj(pw[LK]), entry, a);
+#pragma unroll
+  for (int d = 0; d < 5; ++d) {
+    const int o = 1 << d;
+    const float2 v = shfl_down2(a, o);
+    if (lane + o < 32) a = c_fma(c_conj(pw[LK + d]), v, a);
+  }
+  float2 ae = shfl_down2(a, 1);
+  if (lane == 31) ae = cz();
+  if (lane == 0) s_warp[warp] = a;
+  __syncthreads();
+  const float2 gw = c_conj(pw[LK + 5]);
+  float2 Xw = cz(), Xall = cz();
+#pragma unroll
+  for (int w = NW - 1; w >= 0; --w) {
+    if (w == warp) Xw = Xall;
+    Xall = c_fma(gw, Xall, s_warp[w]);
+  }
+  E = threadIdx.x == NT - 1 ? entry : c_fma(lanepow, Xw, ae);
+  At = Xall;
+}
+
 // Sum a complex value over the CTA; the result is valid in thread 0.
 // s_red needs NT/32 float2 slots.  Contains one __syncthreads().
 template <int NT>
@@ -320,6 +470,49 @@ __device__ __forceinline__ void blocked_to_striped(float4 *wbuf, const float2 (&
 #pragma unroll
   for (int v = 0; v < K / 2; ++v) s[v] = wbuf[swz<K>(v * 32 + lane)];
   __syncwarp();
+}
+
+// ---------------------------------------------------- cp.async staging
+// Asynchronous global -> shared copies (the copy engine path that bypasses
+// registers).  `pred == false` zero-fills the destination without reading
+// global memory (the source address is still kept inside the tensor).
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool pred) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  const int n = pred ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(n)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async8(void *smem, const void *gmem, bool pred) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  const int n = pred ? 8 : 0;
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(s), "l"(gmem), "r"(n)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Read this thread's K blocked samples from a warp region written in the
+// swizzled striped order (see striped_to_blocked).
+template <int K>
+__device__ __forceinline__ void read_blocked(const float4 *wbuf, float2 (&b)[K], int lane) {
+#pragma unroll
+  for (int m = 0; m < K / 2; ++m) {
+    const float4 q = wbuf[swz<K>(lane * (K / 2) + m)];
+    b[2 * m] = make_float2(q.x, q.y);
+    b[2 * m + 1] = make_float2(q.z, q.w);
+  }
+}
+
+// Sample q (0 <= q < 32K) of a warp region stored in swizzled striped order.
+template <int K>
+__device__ __forceinline__ float2 read_sample(const float4 *wbuf, int q) {
+  const float4 v = wbuf[swz<K>(q >> 1)];
+  return (q & 1) ? make_float2(v.z, v.w) : make_float2(v.x, v.y);
 }
 
 // Streaming 16-byte load / store (data is touched once per kernel).

@@ -54,6 +54,30 @@ def c64(a):
     return np.asarray(a).astype(np.complex64).astype(np.complex128)
 
 
+# split-ReLU decisions of the fp32 kernel may differ from fp64 only where the
+# state is within rounding of zero (relu' is discontinuous there).
+MASK_EDGE = 1e-4
+
+
+def check_fbt(ins, y, gy, c1, t0, t1, z, fuse, layout="fbt"):
+    """Forward vs the fp64 oracle; backward vs the oracle VJP evaluated with
+    the kernel's own split-ReLU decisions (checked to differ from fp64 only
+    at |state| < MASK_EDGE * max|state|)."""
+    y_ref = oracle.two_tap_forward(c1, t0, t1, z, layout, fuse_act=fuse)
+    assert_close(host(y), y_ref, FWD_TOL, "y")
+    mask = None
+    if fuse:
+        mask = oracle.relu_mask_from_output(host(y))
+        raw_ref = oracle.two_tap_forward(c1, t0, t1, z, layout, fuse_act=False)
+        edge = oracle.mask_disagreement(mask, raw_ref)
+        assert edge < MASK_EDGE, f"split-ReLU decision differs at |state| = {edge:.2e} max"
+    y.backward(dev(gy))
+    gz, gc1, gt0, gt1 = oracle.two_tap_backward(c1, t0, t1, z, gy, layout, fuse_act=fuse,
+                                                mask=mask)
+    for t, r, k in zip(ins, (gc1, gt0, gt1, gz), ("gc1", "gt0", "gt1", "gz")):
+        assert_close(host(t.grad), r, GRAD_TOL, k)
+
+
 # ----------------------------------------------------------- goldens
 def test_golden_scan_complex():
     g = golden("scan_complex")
@@ -125,7 +149,7 @@ FBT_T = [1, 2, 3, 31, 2047, 2048, 2049, 4097, 5001, 6144]
 
 @pytest.mark.parametrize("T", FBT_T)
 @pytest.mark.parametrize("fuse", [True, False])
-def test_fbt_vs_oracle(T, fuse):
+def test_fbt_lookback_tiles_vs_oracle(T, fuse):
     rng = np.random.default_rng(1000 + T + int(fuse))
     F, B = 3, 5
     c1 = coeffs(rng, F)
@@ -134,19 +158,29 @@ def test_fbt_vs_oracle(T, fuse):
     gy = c64(crandn(rng, (F, B, T)))
     ins = [dev(a, grad=True) for a in (c1, t0, t1, z)]
     y = rqf().fbt_prospective_scan(*ins, fuse)
-    assert_close(host(y), oracle.two_tap_forward(c1, t0, t1, z, "fbt", fuse_act=fuse), FWD_TOL,
-                 "y")
-    y.backward(dev(gy))
-    ref = oracle.two_tap_backward(c1, t0, t1, z, gy, "fbt", fuse_act=fuse)
-    gz, gc1, gt0, gt1 = ref
-    for t, r, k in zip(ins, (gc1, gt0, gt1, gz), ("gc1", "gt0", "gt1", "gz")):
-        assert_close(host(t.grad), r, GRAD_TOL, k)
+    check_fbt(ins, y, gy, c1, t0, t1, z, fuse)
 
 
-def test_fbt_long_sequence_undamped_poles():
-    """T = 16000 with |C1| up to 1 - 2e-7 (the paper recipe's gamma -> 1e-6
-    edge) — the hardest case for cross-tile carry accuracy."""
-    rng = np.random.default_rng(7)
+# Row counts >= the resident CTAs of the persistent kernels (at most 3 per SM
+# on 148 SMs = 444) take the persistent row-sequential path; the sweep above
+# (15 rows) takes the look-back tile path.
+@pytest.mark.parametrize("T", [2, 2048, 2050, 6000])
+@pytest.mark.parametrize("fuse", [True, False])
+def test_fbt_persistent_rows_vs_oracle(T, fuse):
+    rng = np.random.default_rng(2000 + T + int(fuse))
+    F, B = 37, 16  # 592 rows
+    c1 = coeffs(rng, F)
+    t0, t1 = c64(crandn(rng, F, 0.5)), c64(crandn(rng, F, 0.5))
+    z = c64(crandn(rng, (F, B, T)))
+    gy = c64(crandn(rng, (F, B, T)))
+    ins = [dev(a, grad=True) for a in (c1, t0, t1, z)]
+    y = rqf().fbt_prospective_scan(*ins, fuse)
+    check_fbt(ins, y, gy, c1, t0, t1, z, fuse)
+
+
+def test_fbt_long_sequence_undamped_poles_lookback():
+    """Same hardest case through the look-back tile kernels (few rows)."""
+    rng = np.random.default_rng(8)
     F, B, T = 8, 4, 16000
     mag = np.concatenate([np.full(4, np.exp(-2e-7)), rng.uniform(0.9, 0.9999, 4)])
     c1 = c64(mag * np.exp(1j * rng.uniform(0, np.pi, F)))
@@ -155,12 +189,22 @@ def test_fbt_long_sequence_undamped_poles():
     gy = c64(crandn(rng, (F, B, T)))
     ins = [dev(a, grad=True) for a in (c1, t0, t1, z)]
     y = rqf().fbt_recompute_scan(*ins)
-    assert_close(host(y), oracle.two_tap_forward(c1, t0, t1, z, "fbt", fuse_act=True), FWD_TOL,
-                 "y")
-    y.backward(dev(gy))
-    gz, gc1, gt0, gt1 = oracle.two_tap_backward(c1, t0, t1, z, gy, "fbt", fuse_act=True)
-    for t, r, k in zip(ins, (gc1, gt0, gt1, gz), ("gc1", "gt0", "gt1", "gz")):
-        assert_close(host(t.grad), r, GRAD_TOL, k)
+    check_fbt(ins, y, gy, c1, t0, t1, z, True)
+
+
+def test_fbt_long_sequence_undamped_poles():
+    """T = 16000 with |C1| up to 1 - 2e-7 (the paper recipe's gamma -> 1e-6
+    edge) — the hardest case for cross-tile carry accuracy."""
+    rng = np.random.default_rng(7)
+    F, B, T = 8, 80, 16000  # 640 rows: persistent path
+    mag = np.concatenate([np.full(4, np.exp(-2e-7)), rng.uniform(0.9, 0.9999, 4)])
+    c1 = c64(mag * np.exp(1j * rng.uniform(0, np.pi, F)))
+    t0, t1 = c64(crandn(rng, F, 0.05)), c64(crandn(rng, F, 0.05))
+    z = c64(crandn(rng, (F, B, T)))
+    gy = c64(crandn(rng, (F, B, T)))
+    ins = [dev(a, grad=True) for a in (c1, t0, t1, z)]
+    y = rqf().fbt_recompute_scan(*ins)
+    check_fbt(ins, y, gy, c1, t0, t1, z, True)
 
 
 def test_fbt_full_size_linearity_and_adjoint():
