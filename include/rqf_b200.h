@@ -164,6 +164,32 @@ int rqf_tbptt1_two_tap_backward(int layout, const float *c1, const float *tap0,
                                 void *scratch, int64_t d0, int64_t d1,
                                 int64_t d2, int fuse_act, rqf_stream_t stream);
 
+/* ---- allocation-free variant of rqf_fbt_prospective_backward --------- *
+ * No counterpart in the reference.  For callers that cannot allocate device
+ * memory — e.g. code running inside a framework allocator's callback, a
+ * real-time loop that forbids cudaMalloc after start-up, or a host language
+ * binding that only hands over tensors it already owns — so they cannot
+ * provide the `scratch` buffer the other backward entry point needs.
+ *
+ * Same arguments and results as rqf_fbt_prospective_backward without
+ * `scratch`: the scratch lives in a fixed 4 MiB __device__ array inside this
+ * library (every GPU that loads the library holds it until process exit).
+ * Shapes whose scratch (rqf_fbt_scratch_bytes) exceeds 4 MiB are rejected
+ * with RQF_ERR_CAPACITY.  The first call on a device looks up the array's
+ * device address on that device (cudaGetSymbolAddress, once per device), so
+ * make the first call on each device outside any stream capture.  All calls
+ * share the one array and it keeps the last call's contents (the part that
+ * must start at zero is cleared on every call), so calls whose GPU work
+ * overlaps — on different streams, or from different host threads without
+ * ordering — race on it and must be serialised by the caller.  Allocates
+ * nothing: no cudaMalloc, cudaFree or allocating library routine. */
+int rqf_fbt_prospective_backward_noalloc(const float *c1, const float *tap0, const float *tap1,
+                                         const float *z, const float *carries,
+                                         const float *grad_out, float *grad_z, float *grad_c1,
+                                         float *grad_tap0, float *grad_tap1, int64_t filters,
+                                         int64_t batch, int64_t time, int fuse_act,
+                                         rqf_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -40,6 +40,8 @@ SIGNATURES: dict[str, tuple] = {
         _int, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "rqf_fbt_prospective_backward": (
         _int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
+    "rqf_fbt_prospective_backward_noalloc": (
+        _int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "rqf_tbptt1_two_tap_backward": (
         _int, [_int, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
 }

@@ -484,3 +484,5 @@ int rqf_tbptt1_two_tap_backward(int layout, const float *c1, const float *tap0,
 }
 
 }  // extern "C"
+
+#include "noalloc.cuh"
