@@ -257,16 +257,21 @@ def scan_roofline(timer_summary, hbm_peak, peak_kind, traffic):
         "bound": "hbm", "kernel": "scan fwd+bwd (" + ", ".join(sorted(per)) + ")",
         "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
         "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
-        "traffic": traffic, "per_kernel": per,
+        "traffic": traffic, "traffic_unit": "bytes per fwd+bwd launch pair (ncu)",
+        "alg_bytes_per_pair": int(sum(v["alg_bytes_per_launch"] for v in per.values())),
+        "per_kernel": per,
     }
 
 
 def load_traffic(workload):
+    """DRAM bytes (read + write) of one scan forward+backward launch pair from
+    the committed ncu capture (profiles/traffic.json), or None."""
     p = ROOT / "profiles" / "traffic.json"
     if not p.exists():
         return None
     try:
-        return json.loads(p.read_text()).get(workload)
+        entry = json.loads(p.read_text()).get(workload)
+        return None if entry is None else int(entry["bytes_per_launch_pair"])
     except Exception:
         return None
 
