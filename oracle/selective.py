@@ -44,12 +44,11 @@ def _phi_and_dphi(a):
     return A, phi, dphi
 
 
-def controllers(gl, dl, wl, bias, theta, groups, lo, span, step, opt, th_lo, th_hi):
-    """Per-element gamma, theta, gate and the link intermediates."""
+def controllers(gl, dl, wl, bias, theta, groups, lo, span, step, opt, th_lo, th_hi, shape):
+    """Per-element gamma, theta, gate and the link intermediates; shape is
+    (F, B, T)."""
     (has_gamma, has_warp, has_write, log_shift, g_scale, w_scale, _pros, _gh, w_sig, w_max,
      w_bias, bound) = opt
-    F = bias.shape[0]
-    shape = (F,) + tuple((gl if has_gamma else wl if has_write else dl).shape[1:])
     b = bias[:, None, None]
     aux = {}
     if has_gamma:
@@ -79,10 +78,17 @@ def controllers(gl, dl, wl, bias, theta, groups, lo, span, step, opt, th_lo, th_
     return gamma, th, gate, h, aux
 
 
+def options(raw) -> tuple:
+    """The reference's 12-tuple from a numeric array (bools, floats)."""
+    v = [float(x) for x in raw]
+    b = [bool(round(x)) for x in v]
+    return (b[0], b[1], b[2], b[3], v[4], v[5], b[6], b[7], b[8], v[9], v[10], b[11])
+
+
 def forward(z, gl, dl, wl, bias, theta, groups, lo, span, step, horizon, th_lo, th_hi, opt):
     """Returns (raw y, coefficient dict)."""
     gamma, th, gate, h, aux = controllers(gl, dl, wl, bias, theta, groups, lo, span, step, opt,
-                                          th_lo, th_hi)
+                                          th_lo, th_hi, z.shape)
     prospective, gamma_horizon = opt[6], opt[7]
     a = -gamma * h + 1j * (1.0 - gamma) * th * h
     A, phi, dphi = _phi_and_dphi(a)
@@ -184,4 +190,9 @@ def backward(z, y, co, gy, gx, gl, dl, wl, bias, theta, groups, lo, span, step, 
         dW = dgate * gate * (1.0 - gate / w_max) if w_sig else dgate
     dbias = dbias_e.sum(axis=(1, 2))
     dtheta = dtheta_e.sum(axis=(1, 2))
-    return dz, (dzw if truncated else dz), dG, dDg, dW, dbias, dtheta
+    # Full BPTT: z feeds both taps, so its cotangent is the total (dz and dzw
+    # are the same tensor, selective_scan_kernel.py:521); TBPTT(1): dz is the
+    # spatial part for x, dzw the total for the weight.
+    if truncated:
+        return dz, dzw, dG, dDg, dW, dbias, dtheta
+    return dzw, dzw, dG, dDg, dW, dbias, dtheta

@@ -242,6 +242,78 @@ def case_tbptt(out):
              gu_nolag=_np(gub))
 
 
+SELECTIVE_CASES = [
+    # (controller config, prospective, truncated, horizon mode)
+    ({}, True, False, "tau"),
+    ({"gamma_link": "log_shift"}, True, False, "tau"),
+    ({"gamma_control": False, "write_control": True}, True, False, "tau"),
+    ({"gamma_control": False, "write_control": True, "write_link": "affine"}, False, False, "tau"),
+    ({"gamma_control": False, "frequency_warp": "global"}, True, False, "tau"),
+    ({"frequency_warp": "grouped", "num_groups": 3, "write_control": True}, True, False, "tau"),
+    ({"frequency_warp": "grouped", "num_groups": 3, "write_control": True}, True, True, "tau"),
+    ({"frequency_warp": "global", "write_control": True, "gamma_link": "log_shift"}, True, False,
+     "gamma"),
+    ({"frequency_warp": "grouped", "num_groups": 3, "warp_bound": "none"}, False, True, "tau"),
+    ({"write_control": True}, True, True, "gamma"),
+]
+
+
+def case_selective(out, reference):
+    """Selective scan: the reference's reference_layer_scan (selective_scan.py
+    :71-104) in fp64 with autograd, on SelectiveScanInputs built by the
+    reference's own SelectiveController (the model/test helpers of
+    tests/test_selective_rqf.py).  Weight = identity so z = x; in truncated
+    mode the lag cotangent reaches only the weight gradient."""
+    import torch
+
+    sys.path.insert(0, os.path.join(reference, "tests"))
+    from rqf_models.ops.selective_scan import reference_layer_scan
+    from test_selective_rqf import inputs_for, make_model
+
+    fields = ("gamma_logits", "warp_logits", "write_logits", "bias", "theta")
+    for ci, (cfg, prospective, truncated, mode) in enumerate(SELECTIVE_CASES):
+        blk = make_model(cfg, active=True, num_layers=1, prospective_input=prospective,
+                         prospective_mode=mode, samp_frequency=100.0).blocks[0].double()
+        F = blk.W.shape[0]
+        B, T = 2, 37
+        g = torch.Generator().manual_seed(100 + ci)
+
+        def cplx(*shape):
+            return torch.complex(torch.randn(*shape, generator=g, dtype=torch.float64),
+                                 torch.randn(*shape, generator=g, dtype=torch.float64))
+
+        x = cplx(blk.W.shape[1], B, T)
+        with torch.no_grad():
+            inputs = inputs_for(blk, x)
+        leaves = {k: getattr(inputs, k).detach().clone().requires_grad_(True) for k in fields}
+        inp = inputs._replace(**leaves)
+        z = cplx(F, B, T).requires_grad_(True)
+        weight = torch.eye(F, dtype=torch.complex128).requires_grad_(True)
+        raw, act = reference_layer_scan(z, weight, inp, truncated=truncated, activate=True,
+                                        write_raw=True)
+        gy, gx = cplx(F, B, T), cplx(F, B, T)
+        loss = (gy.conj() * raw).real.sum() + (gx.conj() * act).real.sum()
+        loss.backward()
+
+        def arr(t):
+            return np.zeros(0) if t is None or t.numel() == 0 else _np(t)
+
+        opt = np.array([float(v) for v in inputs.options])
+        np.savez(out / f"selective_{ci}.npz", z=_np(z), gy=_np(gy), gx=_np(gx), raw=_np(raw),
+                 act=_np(act), dz=_np(z.grad), dweight=_np(weight.grad),
+                 gamma_logits=arr(inputs.gamma_logits), warp_logits=arr(inputs.warp_logits),
+                 write_logits=arr(inputs.write_logits), bias=_np(inputs.bias),
+                 theta=_np(inputs.theta),
+                 groups=np.zeros(0, np.int64) if inputs.groups is None else _np(inputs.groups),
+                 minimum=_np(inputs.minimum), span=_np(inputs.span), step=_np(inputs.step),
+                 horizon=_np(inputs.horizon), theta_minimum=_np(inputs.theta_minimum),
+                 theta_maximum=_np(inputs.theta_maximum), options=opt,
+                 truncated=np.array(truncated),
+                 dG=arr(leaves["gamma_logits"].grad), dD=arr(leaves["warp_logits"].grad),
+                 dW=arr(leaves["write_logits"].grad), dbias=_np(leaves["bias"].grad),
+                 dtheta=_np(leaves["theta"].grad))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("RQF_REFERENCE", ""))
@@ -263,6 +335,7 @@ def main():
     case_fbt(out, fuse_act=False)
     case_triton_btf(out)
     case_tbptt(out)
+    case_selective(out, args.reference)
     print("golden vectors written to", out)
 
 
