@@ -164,6 +164,53 @@ int rqf_tbptt1_two_tap_backward(int layout, const float *c1, const float *tap0,
                                 void *scratch, int64_t d0, int64_t d1,
                                 int64_t d2, int fuse_act, rqf_stream_t stream);
 
+/* ---- selective (input-dependent ZOH) scan, (F,B,T) layout ------------ *
+ * Replaces rqf_models/ops/selective_scan_kernel.py:selective_forward (:491) /
+ * _forward (:155) and selective_backward (:517) / _backward (:250) /
+ * _group_reduce (:465).  The options mirror the reference's 12-tuple
+ * (rqf_models/backbones/rqf/selective.py:249-262); the inputs mirror
+ * SelectiveScanInputs (rqf_models/ops/selective_scan.py:10-23). */
+typedef struct {
+  int has_gamma, has_warp, has_write, log_shift;
+  float gamma_scale, warp_scale;
+  int prospective, gamma_horizon, write_sigmoid;
+  float write_max, write_bias;
+  int bound_warp;
+} rqf_selective_options;
+
+typedef struct {
+  const float *gamma_logits; /* (F,B,T), or NULL without gamma control */
+  const float *warp_logits;  /* (num_groups,B,T), or NULL without warp  */
+  const float *write_logits; /* (F,B,T), or NULL without write control */
+  const float *bias, *theta; /* (F,) */
+  const int64_t *groups;     /* (F,) warp group per channel, or NULL  */
+  const float *minimum, *span, *step, *horizon, *theta_minimum, *theta_maximum; /* (F,) */
+  int64_t num_groups;
+} rqf_selective_inputs;
+
+int64_t rqf_selective_num_tiles(int64_t time);
+int64_t rqf_selective_carry_count(int64_t filters, int64_t batch, int64_t time);
+size_t rqf_selective_scratch_bytes(int64_t filters, int64_t batch, int64_t time, int has_warp);
+
+/* Writes raw (may be NULL) and split-ReLU(raw) `act` (may be NULL) as
+ * complex (F,B,T), and the per-tile entry states into `carries`. */
+int rqf_selective_forward(const float *z, const rqf_selective_inputs *inputs,
+                          const rqf_selective_options *options, float *raw, float *act,
+                          float *carries, int64_t filters, int64_t batch, int64_t time,
+                          rqf_stream_t stream);
+
+/* grad_raw / grad_act: cotangents of raw and act (either may be NULL).
+ * Outputs as selective_backward: dz (total drive cotangent in full BPTT, the
+ * spatial part in TBPTT(1)), dzw (TBPTT(1) only: total, for the weight; may
+ * be NULL otherwise), dgamma (F,B,T) / dwarp (num_groups,B,T) / dwrite (F,B,T)
+ * logit cotangents (NULL when the controller is off), dbias / dtheta (F,). */
+int rqf_selective_backward(const float *z, const rqf_selective_inputs *inputs,
+                           const rqf_selective_options *options, const float *carries,
+                           const float *grad_raw, const float *grad_act, int truncated,
+                           float *dz, float *dzw, float *dgamma, float *dwarp, float *dwrite,
+                           float *dbias, float *dtheta, void *scratch, int64_t filters,
+                           int64_t batch, int64_t time, rqf_stream_t stream);
+
 /* ---- allocation-free variant of rqf_fbt_prospective_backward --------- *
  * No counterpart in the reference.  For callers that cannot allocate device
  * memory — e.g. code running inside a framework allocator's callback, a

@@ -116,10 +116,11 @@ def forward(z, gl, dl, wl, bias, theta, groups, lo, span, step, horizon, th_lo, 
 
 
 def backward(z, y, co, gy, gx, gl, dl, wl, bias, theta, groups, lo, span, step, horizon,
-             th_lo, th_hi, opt, truncated):
+             th_lo, th_hi, opt, truncated, mask=None):
     """VJP of forward; gy/gx are the cotangents of raw / split-ReLU(raw) (or
     None).  Returns (dz, dzw, dG, dD_group, dW, dbias, dtheta) as the
-    reference's selective_backward does (dzw is dz when not truncated)."""
+    reference's selective_backward does (dzw is dz when not truncated).
+    `mask` (bool, z.shape + (2,)) overrides the split-ReLU decisions."""
     (has_gamma, has_warp, has_write, log_shift, g_scale, w_scale, prospective, gamma_horizon,
      w_sig, w_max, _wb, bound) = opt
     F, B, T = z.shape
@@ -127,7 +128,8 @@ def backward(z, y, co, gy, gx, gl, dl, wl, bias, theta, groups, lo, span, step, 
     if gy is not None:
         e = e + gy
     if gx is not None:
-        e = e + np.where(y.real > 0, gx.real, 0.0) + 1j * np.where(y.imag > 0, gx.imag, 0.0)
+        mr, mi = (y.real > 0, y.imag > 0) if mask is None else (mask[..., 0], mask[..., 1])
+        e = e + np.where(mr, gx.real, 0.0) + 1j * np.where(mi, gx.imag, 0.0)
     A, p, n = co["A"], co["p"], co["n"]
     d = np.zeros(z.shape, np.complex128)
     nxt = np.zeros((F, B), np.complex128)

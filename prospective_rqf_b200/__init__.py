@@ -18,6 +18,9 @@ from .ops import (
     fbt_prospective_scan,
     fbt_recompute_scan,
     parallel_scan,
+    selective_backward,
+    selective_forward,
+    selective_layer_scan,
     sequential_scan,
     sequential_scan_abs,
     tbptt1_scan,
@@ -35,6 +38,9 @@ __all__ = [
     "fbt_prospective_scan",
     "fbt_recompute_scan",
     "parallel_scan",
+    "selective_backward",
+    "selective_forward",
+    "selective_layer_scan",
     "sequential_scan",
     "sequential_scan_abs",
     "tbptt1_scan",

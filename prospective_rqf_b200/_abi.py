@@ -18,6 +18,29 @@ _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _int = ctypes.c_int
 _sz = ctypes.c_size_t
+_f32 = ctypes.c_float
+
+
+class SelectiveOptions(ctypes.Structure):
+    """rqf_selective_options (include/rqf_b200.h)."""
+
+    _fields_ = [("has_gamma", _int), ("has_warp", _int), ("has_write", _int),
+                ("log_shift", _int), ("gamma_scale", _f32), ("warp_scale", _f32),
+                ("prospective", _int), ("gamma_horizon", _int), ("write_sigmoid", _int),
+                ("write_max", _f32), ("write_bias", _f32), ("bound_warp", _int)]
+
+
+class SelectiveInputs(ctypes.Structure):
+    """rqf_selective_inputs (include/rqf_b200.h)."""
+
+    _fields_ = [("gamma_logits", _p), ("warp_logits", _p), ("write_logits", _p), ("bias", _p),
+                ("theta", _p), ("groups", _p), ("minimum", _p), ("span", _p), ("step", _p),
+                ("horizon", _p), ("theta_minimum", _p), ("theta_maximum", _p),
+                ("num_groups", _i64)]
+
+
+_pin = ctypes.POINTER(SelectiveInputs)
+_pop = ctypes.POINTER(SelectiveOptions)
 
 # name -> (restype, argtypes); mirrors include/rqf_b200.h exactly.
 SIGNATURES: dict[str, tuple] = {
@@ -42,6 +65,13 @@ SIGNATURES: dict[str, tuple] = {
         _int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "rqf_fbt_prospective_backward_noalloc": (
         _int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
+    "rqf_selective_num_tiles": (_i64, [_i64]),
+    "rqf_selective_carry_count": (_i64, [_i64, _i64, _i64]),
+    "rqf_selective_scratch_bytes": (_sz, [_i64, _i64, _i64, _int]),
+    "rqf_selective_forward": (_int, [_p, _pin, _pop, _p, _p, _p, _i64, _i64, _i64, _p]),
+    "rqf_selective_backward": (
+        _int, [_p, _pin, _pop, _p, _p, _p, _int, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64,
+               _i64, _p]),
     "rqf_tbptt1_two_tap_backward": (
         _int, [_int, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
 }

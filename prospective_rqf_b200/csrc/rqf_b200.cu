@@ -11,6 +11,7 @@
 #include "fbt_rows.cuh"
 #include "fbt_scan.cuh"
 #include "reduce.cuh"
+#include "selective.cuh"
 
 using namespace rqf;
 
@@ -480,6 +481,153 @@ int rqf_tbptt1_two_tap_backward(int layout, const float *c1, const float *tap0,
   reduce_partials_kernel<<<(unsigned)F, 256, 0, stream>>>(
       a.partials, reinterpret_cast<float2 *>(grad_c1), reinterpret_cast<float2 *>(grad_tap0),
       reinterpret_cast<float2 *>(grad_tap1), B, B, 1, a.ntiles);
+  return launch_status();
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------ selective
+namespace {
+
+SelArgs sel_args(const float *z, const rqf_selective_inputs *in, const rqf_selective_options *o,
+                 int64_t F, int64_t B, int64_t T) {
+  SelArgs a = {};
+  a.z = reinterpret_cast<const float2 *>(z);
+  a.G = o->has_gamma ? in->gamma_logits : nullptr;
+  a.D = o->has_warp ? in->warp_logits : nullptr;
+  a.W = o->has_write ? in->write_logits : nullptr;
+  a.bias = in->bias;
+  a.theta = in->theta;
+  a.groups = reinterpret_cast<const long long *>(in->groups);
+  a.lo = in->minimum;
+  a.span = in->span;
+  a.step = in->step;
+  a.horizon = in->horizon;
+  a.th_lo = in->theta_minimum;
+  a.th_hi = in->theta_maximum;
+  a.rows = (int)(F * B);
+  a.T = (int)T;
+  a.batch = (int)B;
+  a.ntiles = (int)ceil_div(T, kSelTile);
+  a.num_groups = (int)in->num_groups;
+  a.o.has_gamma = o->has_gamma;
+  a.o.has_warp = o->has_warp;
+  a.o.has_write = o->has_write;
+  a.o.log_shift = o->log_shift;
+  a.o.gamma_scale = o->gamma_scale;
+  a.o.warp_scale = o->warp_scale;
+  a.o.prospective = o->prospective;
+  a.o.gamma_horizon = o->gamma_horizon;
+  a.o.write_sigmoid = o->write_sigmoid;
+  a.o.write_max = o->write_max;
+  a.o.write_bias = o->write_bias;
+  a.o.bound_warp = o->bound_warp;
+  return a;
+}
+
+int sel_check(const float *z, const rqf_selective_inputs *in, const rqf_selective_options *o,
+              int64_t F, int64_t B, int64_t T) {
+  if (F < 0 || B < 0 || T < 0) return RQF_ERR_SHAPE;
+  if (F * B > 0x7fffffffLL || T > 0x7fffffffLL) return RQF_ERR_SHAPE;
+  if (!in || !o) return RQF_ERR_ARGUMENT;
+  if (F * B * T == 0) return RQF_OK;
+  if (!z || !in->bias || !in->theta || !in->minimum || !in->span || !in->step || !in->horizon ||
+      !in->theta_minimum || !in->theta_maximum)
+    return RQF_ERR_ARGUMENT;
+  if ((o->has_gamma && !in->gamma_logits) || (o->has_write && !in->write_logits) ||
+      (o->has_warp && (!in->warp_logits || !in->groups || in->num_groups < 1 ||
+                       in->num_groups > 32)))
+    return RQF_ERR_ARGUMENT;
+  if (!aligned(z, 8)) return RQF_ERR_ALIGN;
+  return RQF_OK;
+}
+
+template <typename Kern>
+unsigned sel_grid(Kern kernel, int64_t rows) {
+  const int64_t g = resident_ctas(kernel, kSelThreads, 0);
+  const int64_t n = g > 0 ? (g < rows ? g : rows) : (rows < 1024 ? rows : 1024);
+  return (unsigned)(n > 0 ? n : 1);
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t rqf_selective_num_tiles(int64_t time) { return time <= 0 ? 0 : ceil_div(time, kSelTile); }
+int64_t rqf_selective_carry_count(int64_t filters, int64_t batch, int64_t time) {
+  return filters * batch * rqf_selective_num_tiles(time);
+}
+size_t rqf_selective_scratch_bytes(int64_t filters, int64_t batch, int64_t time, int has_warp) {
+  if (filters <= 0 || batch <= 0 || time <= 0) return 256;
+  const size_t dd = has_warp ? round256((size_t)filters * batch * time * sizeof(float)) : 0;
+  return dd + round256((size_t)filters * batch * 2 * sizeof(float));
+}
+
+int rqf_selective_forward(const float *z, const rqf_selective_inputs *inputs,
+                          const rqf_selective_options *options, float *raw, float *act,
+                          float *carries, int64_t filters, int64_t batch, int64_t time,
+                          rqf_stream_t stream) {
+  int st = sel_check(z, inputs, options, filters, batch, time);
+  if (st != RQF_OK || filters * batch * time == 0) return st;
+  if ((!raw && !act) || !carries) return RQF_ERR_ARGUMENT;
+  if ((raw && !aligned(raw, 8)) || (act && !aligned(act, 8)) || !aligned(carries, 8))
+    return RQF_ERR_ALIGN;
+  SelArgs a = sel_args(z, inputs, options, filters, batch, time);
+  a.raw = reinterpret_cast<float2 *>(raw);
+  a.act = reinterpret_cast<float2 *>(act);
+  a.carries = reinterpret_cast<float2 *>(carries);
+  auto kern = sel_fwd_kernel<kSelThreads, kSelK>;
+  kern<<<sel_grid(kern, a.rows), kSelThreads, 0, stream>>>(a);
+  return launch_status();
+}
+
+int rqf_selective_backward(const float *z, const rqf_selective_inputs *inputs,
+                           const rqf_selective_options *options, const float *carries,
+                           const float *grad_raw, const float *grad_act, int truncated,
+                           float *dz, float *dzw, float *dgamma, float *dwarp, float *dwrite,
+                           float *dbias, float *dtheta, void *scratch, int64_t filters,
+                           int64_t batch, int64_t time, rqf_stream_t stream) {
+  int st = sel_check(z, inputs, options, filters, batch, time);
+  if (st != RQF_OK) return st;
+  if (filters * batch * time == 0) {
+    if (dbias && filters > 0 && cudaMemsetAsync(dbias, 0, filters * sizeof(float), stream))
+      return RQF_ERR_LAUNCH;
+    if (dtheta && filters > 0 && cudaMemsetAsync(dtheta, 0, filters * sizeof(float), stream))
+      return RQF_ERR_LAUNCH;
+    return RQF_OK;
+  }
+  if (!carries || !dz || !dbias || !dtheta || !scratch || (truncated && !dzw) ||
+      (options->has_gamma && !dgamma) || (options->has_warp && !dwarp) ||
+      (options->has_write && !dwrite))
+    return RQF_ERR_ARGUMENT;
+  if (!aligned(dz, 8) || (dzw && !aligned(dzw, 8)) || !aligned(carries, 8) ||
+      !aligned(scratch, 16) || (grad_raw && !aligned(grad_raw, 8)) ||
+      (grad_act && !aligned(grad_act, 8)))
+    return RQF_ERR_ALIGN;
+  SelArgs a = sel_args(z, inputs, options, filters, batch, time);
+  a.carries = const_cast<float2 *>(reinterpret_cast<const float2 *>(carries));
+  a.gy = reinterpret_cast<const float2 *>(grad_raw);
+  a.gx = reinterpret_cast<const float2 *>(grad_act);
+  a.dz = reinterpret_cast<float2 *>(dz);
+  a.dzw = reinterpret_cast<float2 *>(dzw);
+  a.dG = dgamma;
+  a.dW = dwrite;
+  a.truncated = truncated ? 1 : 0;
+  const size_t dd_bytes =
+      options->has_warp ? round256((size_t)filters * batch * time * sizeof(float)) : 0;
+  a.dD = options->has_warp ? static_cast<float *>(scratch) : nullptr;
+  a.partials = at<float>(scratch, dd_bytes);
+  auto kern = sel_bwd_kernel<kSelThreads, kSelK>;
+  kern<<<sel_grid(kern, a.rows), kSelThreads, 0, stream>>>(a);
+  if ((st = launch_status()) != RQF_OK) return st;
+  if (options->has_warp) {
+    const int64_t bt = batch * time;
+    sel_group_reduce_kernel<<<(unsigned)ceil_div(bt, 256), 256, 0, stream>>>(
+        a.dD, a.groups, dwarp, (int)filters, (int)inputs->num_groups, bt);
+    if ((st = launch_status()) != RQF_OK) return st;
+  }
+  sel_param_reduce_kernel<<<(unsigned)ceil_div(filters, 128), 128, 0, stream>>>(
+      a.partials, dbias, dtheta, (int)filters, (int)batch);
   return launch_status();
 }
 

@@ -415,6 +415,74 @@ __device__ __forceinline__ void cta_scan_entry_rev(float2 a, float2 entry, const
   At = Xall;
 }
 
+// Generic (time-varying gate) counterparts of cta_scan_entry_*: each thread
+// contributes the composition (g, a) of its K samples; the known entry state
+// is folded into the first thread (last thread in reverse).  s_warp needs
+// NT/32 float4 slots and must not be reused before the next __syncthreads.
+template <int NT>
+__device__ __forceinline__ void cta_scan_pair_entry_fwd(float2 g, float2 a, float2 entry,
+                                                        float2 &E, float2 &At, float4 *s_warp) {
+  constexpr int NW = NT / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) a = c_fma(g, entry, a);
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float2 gp = shfl_up2(g, o), ap = shfl_up2(a, o);
+    if (lane >= o) {
+      a = c_fma(g, ap, a);
+      g = c_mul(g, gp);
+    }
+  }
+  float2 ge = shfl_up2(g, 1), ae = shfl_up2(a, 1);
+  if (lane == 0) {
+    ge = cone();
+    ae = cz();
+  }
+  if (lane == 31) s_warp[warp] = make_float4(g.x, g.y, a.x, a.y);
+  __syncthreads();
+  float2 Xw = cz(), Xall = cz();
+#pragma unroll
+  for (int w = 0; w < NW; ++w) {
+    const float4 q = s_warp[w];
+    if (w == warp) Xw = Xall;
+    Xall = c_fma(make_float2(q.x, q.y), Xall, make_float2(q.z, q.w));
+  }
+  E = threadIdx.x == 0 ? entry : c_fma(ge, Xw, ae);
+  At = Xall;
+}
+
+template <int NT>
+__device__ __forceinline__ void cta_scan_pair_entry_rev(float2 g, float2 a, float2 entry,
+                                                        float2 &E, float2 &At, float4 *s_warp) {
+  constexpr int NW = NT / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == NT - 1) a = c_fma(g, entry, a);
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float2 gp = shfl_down2(g, o), ap = shfl_down2(a, o);
+    if (lane + o < 32) {
+      a = c_fma(g, ap, a);
+      g = c_mul(g, gp);
+    }
+  }
+  float2 ge = shfl_down2(g, 1), ae = shfl_down2(a, 1);
+  if (lane == 31) {
+    ge = cone();
+    ae = cz();
+  }
+  if (lane == 0) s_warp[warp] = make_float4(g.x, g.y, a.x, a.y);
+  __syncthreads();
+  float2 Xw = cz(), Xall = cz();
+#pragma unroll
+  for (int w = NW - 1; w >= 0; --w) {
+    const float4 q = s_warp[w];
+    if (w == warp) Xw = Xall;
+    Xall = c_fma(make_float2(q.x, q.y), Xall, make_float2(q.z, q.w));
+  }
+  E = threadIdx.x == NT - 1 ? entry : c_fma(ge, Xw, ae);
+  At = Xall;
+}
+
 // Sum a complex value over the CTA; the result is valid in thread 0.
 // s_red needs NT/32 float2 slots.  Contains one __syncthreads().
 template <int NT>

@@ -1,0 +1,475 @@
+// Selective (input-dependent ZOH) RQF scan in (F,B,T) layout.
+//
+// Per sample t of row (f, b) (rqf_models/ops/selective_scan.py:
+// selective_coefficients :26-68, reference_layer_scan :71-104):
+//   controllers  gamma = bias                         (no gamma control)
+//                      | lo + span * sigmoid(bias + G)   (sigmoid link)
+//                      | exp(bias + gscale * tanh(G))    (log-shift link)
+//                theta = Theta * exp(wscale * tanh(D[group(f)])), clamped to the
+//                        band when bounded
+//                gate  = wmax * sigmoid(W + wbias)  |  1 + W  |  1
+//   ZOH          a = (-gamma + i (1-gamma) theta) * h,  A = e^a,
+//                phi = (e^a - 1)/a,  p0 = gamma h phi
+//   prospective  lag = ratio * gamma * A,  p0 += lag,  n0 = -lag
+//                (ratio = 1/gamma in gamma-horizon mode, else horizon[f])
+//   recurrence   y[t] = A[t] y[t-1] + gate (p0 z[t] + n0 z[t-1])
+//
+// Work decomposition: persistent CTAs each walk whole rows tile by tile
+// (1024 samples, 4 per thread) with the carry on chip.  The in-tile scan
+// composes time-varying (A, u) pairs (warp shuffles + shared memory).  The
+// backward replays the controllers and the forward states of a tile from its
+// stored entry state, runs the reverse adjoint d[t] = e[t] + conj(A[t+1])
+// d[t+1] (skipped for TBPTT(1)), and fuses the whole coefficient VJP: dz, dzw,
+// the gamma / write logit cotangents, the per-channel warp cotangent (group-
+// reduced afterwards in fixed order) and per-row sums for bias and theta.
+// The reference recomputes the same quantities in its Triton _backward
+// (selective_scan_kernel.py:250-462) with one program per row.
+#pragma once
+
+#include "rqf_common.cuh"
+
+namespace rqf {
+
+struct SelOptions {  // layout of rqf_selective_options in include/rqf_b200.h
+  int has_gamma, has_warp, has_write, log_shift;
+  float gamma_scale, warp_scale;
+  int prospective, gamma_horizon, write_sigmoid;
+  float write_max, write_bias;
+  int bound_warp;
+};
+
+struct SelArgs {
+  const float2 *z;
+  const float *G, *D, *W;  // logits (F,B,T), (groups,B,T), (F,B,T); null when unused
+  const float *bias, *theta, *lo, *span, *step, *horizon, *th_lo, *th_hi;  // (F,)
+  const long long *groups;                                                  // (F,)
+  float2 *raw, *act;   // forward outputs (nullable)
+  float2 *carries;     // (rows, ntiles) entry states
+  const float2 *gy, *gx;
+  float2 *dz, *dzw;
+  float *dG, *dD, *dW;  // dD: per-channel (F,B,T) warp cotangent, group-reduced later
+  float *partials;      // (rows, 2): bias and theta sums
+  int rows, T, batch, ntiles, num_groups;
+  SelOptions o;
+  int truncated;
+};
+
+constexpr int kSelThreads = 256;
+constexpr int kSelK = 4;
+constexpr int kSelTile = kSelThreads * kSelK;  // 1024 samples
+
+struct SelChan {
+  float bias, theta, lo, span, h, horizon, th_lo, th_hi;
+  int group;
+};
+
+struct SelCtl {
+  float g, th, gate, sig, warp, scale;
+};
+
+struct SelCoef {
+  float2 a, A, phi, p0, n0;
+  float ratio;
+};
+
+__device__ __forceinline__ float sel_sigmoid(float x) { return 1.f / (1.f + expf(-x)); }
+
+__device__ __forceinline__ SelChan sel_chan(const SelArgs &a, int f) {
+  SelChan c;
+  c.bias = a.bias[f];
+  c.theta = a.theta[f];
+  c.lo = a.lo[f];
+  c.span = a.span[f];
+  c.h = a.step[f];
+  c.horizon = a.horizon[f];
+  c.th_lo = a.th_lo[f];
+  c.th_hi = a.th_hi[f];
+  c.group = 0;
+  if (a.o.has_warp) {
+    const long long g = a.groups[f];
+    if (g < 0 || g >= a.num_groups) {
+      latch_error(5);  // RQF_ERR_ARGUMENT: warp group out of range (read clamped to group 0)
+    } else {
+      c.group = (int)g;
+    }
+  }
+  return c;
+}
+
+__device__ __forceinline__ SelCtl sel_controller(const SelOptions &o, const SelChan &c, float gl,
+                                                 float dl, float wl) {
+  SelCtl r;
+  r.sig = 0.f;
+  r.warp = 0.f;
+  r.scale = 1.f;
+  r.g = c.bias;
+  if (o.has_gamma) {
+    if (o.log_shift) {
+      r.sig = tanhf(gl);
+      r.g = expf(c.bias + o.gamma_scale * r.sig);
+    } else {
+      r.sig = sel_sigmoid(c.bias + gl);
+      r.g = c.lo + c.span * r.sig;
+    }
+  }
+  r.th = c.theta;
+  if (o.has_warp) {
+    r.warp = tanhf(dl);
+    r.scale = expf(o.warp_scale * r.warp);
+    r.th = c.theta * r.scale;
+    if (o.bound_warp) r.th = fminf(fmaxf(r.th, c.th_lo), c.th_hi);
+  }
+  r.gate = 1.f;
+  if (o.has_write) r.gate = o.write_sigmoid ? o.write_max * sel_sigmoid(wl + o.write_bias) : 1.f + wl;
+  return r;
+}
+
+__device__ __forceinline__ SelCoef sel_coef(const SelOptions &o, const SelChan &c,
+                                            const SelCtl &k) {
+  SelCoef r;
+  const float ar = -k.g * c.h, ai = (1.f - k.g) * k.th * c.h;
+  float sn, cs;
+  sincosf(ai, &sn, &cs);
+  const float e = expf(ar);
+  r.a = make_float2(ar, ai);
+  r.A = make_float2(e * cs, e * sn);
+  const float den = ar * ar + ai * ai;
+  if (den < 1e-8f) {  // exprel Taylor series near 0: 1 + a/2 + a^2/6 + a^3/24
+    float2 s = c_fma(r.a, make_float2(1.f / 24.f, 0.f), make_float2(1.f / 6.f, 0.f));
+    s = c_fma(r.a, s, make_float2(0.5f, 0.f));
+    r.phi = c_fma(r.a, s, cone());
+  } else {
+    // e^a - 1 without cancellation: expm1(ar) cos(ai) - 2 sin^2(ai/2) + i e^ar sin(ai)
+    const float hs = sinf(0.5f * ai);
+    const float er = expm1f(ar) * cs - 2.f * hs * hs, ei = r.A.y;
+    r.phi = make_float2((er * ar + ei * ai) / den, (ei * ar - er * ai) / den);
+  }
+  const float gh = k.g * c.h;
+  r.p0 = make_float2(gh * r.phi.x, gh * r.phi.y);
+  r.n0 = cz();
+  r.ratio = 0.f;
+  if (o.prospective) {
+    r.ratio = o.gamma_horizon ? 1.f / k.g : c.horizon;
+    const float rg = r.ratio * k.g;
+    const float2 lag = make_float2(rg * r.A.x, rg * r.A.y);
+    r.p0 = c_add(r.p0, lag);
+    r.n0 = make_float2(-lag.x, -lag.y);
+  }
+  return r;
+}
+
+// exprel'(a) = (e^a - phi)/a with the Taylor series sum_k (k+1)/(k+2)! a^k
+// below |a|^2 < 1/64 (8 terms) and its cubic truncation below 1e-8.
+__device__ __forceinline__ float2 sel_dphi(float2 a, float2 A, float2 phi) {
+  const float den = a.x * a.x + a.y * a.y;
+  if (den < 1e-8f) {
+    float2 s = c_fma(a, make_float2(1.f / 8.f, 0.f), make_float2(1.f / 3.f, 0.f));
+    return c_fma(a, s, make_float2(0.5f, 0.f));
+  }
+  if (den < 0.015625f) {
+    const float c[8] = {1.f / 45360.f, 1.f / 5760.f, 1.f / 840.f, 1.f / 144.f,
+                        1.f / 30.f,    1.f / 8.f,    1.f / 3.f,   0.5f};
+    float2 s = make_float2(c[0], 0.f);
+#pragma unroll
+    for (int i = 1; i < 8; ++i) s = c_fma(a, s, make_float2(c[i], 0.f));
+    return s;
+  }
+  const float2 d = make_float2(A.x - phi.x, A.y - phi.y);
+  return make_float2((d.x * a.x + d.y * a.y) / den, (d.y * a.x - d.x * a.y) / den);
+}
+
+template <int K>
+__device__ __forceinline__ void sel_load_logits(const float *base, int t0, int T, float (&v)[K]) {
+#pragma unroll
+  for (int k = 0; k < K; ++k) v[k] = (base && t0 + k < T) ? __ldg(base + t0 + k) : 0.f;
+}
+
+// ------------------------------------------------------------ forward
+template <int NT, int K>
+__global__ void __launch_bounds__(NT) sel_fwd_kernel(const SelArgs a) {
+  constexpr int L = NT * K;
+  __shared__ float4 s_warp[2][NT / 32];  // double-buffered across consecutive tiles
+  const int tid = threadIdx.x;
+  const int T = a.T;
+  unsigned tcount = 0;
+  for (int row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const int f = row / a.batch, b = row - f * a.batch;
+    const SelChan c = sel_chan(a, f);
+    const float2 *zrow = a.z + (size_t)row * T;
+    const float *grow = a.o.has_gamma ? a.G + (size_t)row * T : nullptr;
+    const float *wrow = a.o.has_write ? a.W + (size_t)row * T : nullptr;
+    const float *drow = a.o.has_warp ? a.D + ((size_t)c.group * a.batch + b) * T : nullptr;
+    float2 carry = cz();
+    for (int j = 0; j < a.ntiles; ++j, ++tcount) {
+      const int t0 = j * L + tid * K;
+      float2 z[K];
+#pragma unroll
+      for (int k = 0; k < K; ++k) z[k] = (t0 + k < T) ? __ldcs(zrow + t0 + k) : cz();
+      const float2 zp = (t0 > 0 && t0 - 1 < T) ? zrow[t0 - 1] : cz();
+      float gl[K], dl[K], wl[K];
+      sel_load_logits<K>(grow, t0, T, gl);
+      sel_load_logits<K>(drow, t0, T, dl);
+      sel_load_logits<K>(wrow, t0, T, wl);
+      float2 A[K], u[K];
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const SelCtl ct = sel_controller(a.o, c, gl[k], dl[k], wl[k]);
+        const SelCoef co = sel_coef(a.o, c, ct);
+        const float2 p = make_float2(ct.gate * co.p0.x, ct.gate * co.p0.y);
+        const float2 n = make_float2(ct.gate * co.n0.x, ct.gate * co.n0.y);
+        const bool in = t0 + k < T;
+        A[k] = in ? co.A : cz();
+        u[k] = in ? c_fma(n, k > 0 ? z[k - 1] : zp, c_mul(p, z[k])) : cz();
+      }
+      float2 g = cone(), y = cz();
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        y = c_fma(A[k], y, u[k]);
+        g = c_mul(A[k], g);
+      }
+      float2 e, At;
+      cta_scan_pair_entry_fwd<NT>(g, y, carry, e, At, s_warp[tcount & 1]);
+      if (tid == 0) a.carries[(size_t)row * a.ntiles + j] = carry;
+      carry = At;
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        e = c_fma(A[k], e, u[k]);
+        if (t0 + k < T) {
+          if (a.raw) __stcs(a.raw + (size_t)row * T + t0 + k, e);
+          if (a.act) __stcs(a.act + (size_t)row * T + t0 + k, c_relu(e));
+        }
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------ backward
+template <int NT, int K>
+__global__ void __launch_bounds__(NT) sel_bwd_kernel(const SelArgs a) {
+  constexpr int NW = NT / 32, L = NT * K;
+  __shared__ float4 s_warp_f[NW];
+  __shared__ float4 s_warp_r[NW];
+  __shared__ float4 s_first[NW + 1];  // (A, gated n) of each warp's first sample
+  __shared__ float2 s_efirst[NW];     // e at each warp's first sample (TBPTT(1))
+  __shared__ float s_red[2][NW];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int T = a.T;
+  const bool prosp = a.o.prospective != 0;
+  for (int row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const int f = row / a.batch, b = row - f * a.batch;
+    const SelChan c = sel_chan(a, f);
+    const size_t roff = (size_t)row * T;
+    const float *grow = a.o.has_gamma ? a.G + roff : nullptr;
+    const float *wrow = a.o.has_write ? a.W + roff : nullptr;
+    const float *drow = a.o.has_warp ? a.D + ((size_t)c.group * a.batch + b) * T : nullptr;
+    float2 dcarry = cz();                   // d at the first sample of the next tile
+    float2 A_next = cz(), n_next = cz();    // A, gated n at that sample (0 past T)
+    float acc_bias = 0.f, acc_theta = 0.f;
+    for (int jr = a.ntiles - 1; jr >= 0; --jr) {
+      __syncthreads();  // shared slots of the previous tile are free
+      const int t0 = jr * L + tid * K;
+      float2 z[K], e[K];
+#pragma unroll
+      for (int k = 0; k < K; ++k) z[k] = (t0 + k < T) ? __ldcs(a.z + roff + t0 + k) : cz();
+      const float2 zp = (t0 > 0 && t0 - 1 < T) ? a.z[roff + t0 - 1] : cz();
+      float gl[K], dl[K], wl[K];
+      sel_load_logits<K>(grow, t0, T, gl);
+      sel_load_logits<K>(drow, t0, T, dl);
+      sel_load_logits<K>(wrow, t0, T, wl);
+      // forward replay of the tile from its stored entry state
+      float2 A[K], nn[K], u[K];
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const SelCtl ct = sel_controller(a.o, c, gl[k], dl[k], wl[k]);
+        const SelCoef co = sel_coef(a.o, c, ct);
+        const float2 p = make_float2(ct.gate * co.p0.x, ct.gate * co.p0.y);
+        const bool in = t0 + k < T;
+        nn[k] = in ? make_float2(ct.gate * co.n0.x, ct.gate * co.n0.y) : cz();
+        A[k] = in ? co.A : cz();
+        u[k] = in ? c_fma(nn[k], k > 0 ? z[k - 1] : zp, c_mul(p, z[k])) : cz();
+      }
+      float2 g = cone(), y = cz();
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        y = c_fma(A[k], y, u[k]);
+        g = c_mul(A[k], g);
+      }
+      float2 ent, At;
+      cta_scan_pair_entry_fwd<NT>(g, y, a.carries[(size_t)row * a.ntiles + jr], ent, At,
+                                  s_warp_f);
+      float2 yprev[K];
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        yprev[k] = ent;
+        ent = c_fma(A[k], ent, u[k]);
+        float2 ek = cz();
+        if (t0 + k < T) {
+          if (a.gy) ek = __ldcs(a.gy + roff + t0 + k);
+          if (a.gx) ek = c_add(ek, c_relu_mask(__ldcs(a.gx + roff + t0 + k), ent));
+        }
+        e[k] = ek;
+      }
+      // neighbours: (A, n) of the sample after each thread's last one
+      float2 An = make_float2(__shfl_down_sync(0xffffffffu, A[0].x, 1),
+                              __shfl_down_sync(0xffffffffu, A[0].y, 1));
+      float2 Nn = make_float2(__shfl_down_sync(0xffffffffu, nn[0].x, 1),
+                              __shfl_down_sync(0xffffffffu, nn[0].y, 1));
+      if (lane == 0) {
+        s_first[warp] = make_float4(A[0].x, A[0].y, nn[0].x, nn[0].y);
+        s_efirst[warp] = e[0];
+      }
+      if (tid == NT - 1) s_first[NW] = make_float4(A_next.x, A_next.y, n_next.x, n_next.y);
+      __syncthreads();
+      if (lane == 31) {
+        const float4 q = s_first[warp + 1];
+        An = make_float2(q.x, q.y);
+        Nn = make_float2(q.z, q.w);
+      }
+      // reverse adjoint over the tile
+      float2 dn;  // d at the sample after this thread's last one
+      float2 dcarry_next;
+      if (a.truncated) {  // no temporal adjoint: d = e
+        dn = shfl_down2(e[0], 1);
+        if (lane == 31) dn = warp + 1 < NW ? s_efirst[warp + 1] : dcarry;
+        dcarry_next = s_efirst[0];
+      } else {
+        float2 gr = cone(), h = cz();
+        float2 An_k = An;
+#pragma unroll
+        for (int k = K - 1; k >= 0; --k) {
+          const float2 m = c_conj(An_k);
+          h = c_fma(m, h, e[k]);
+          gr = c_mul(m, gr);
+          An_k = A[k];
+        }
+        float2 Art;
+        cta_scan_pair_entry_rev<NT>(gr, h, dcarry, dn, Art, s_warp_r);
+        dcarry_next = Art;
+      }
+      // per-sample coefficient VJP, in reverse order
+      float2 dnext = dn, A1 = An, N1 = Nn;
+#pragma unroll
+      for (int k = K - 1; k >= 0; --k) {
+        const int t = t0 + k;
+        const float2 d = a.truncated ? e[k] : c_fma(c_conj(A1), dnext, e[k]);
+        if (t < T) {
+          const SelCtl ct = sel_controller(a.o, c, gl[k], dl[k], wl[k]);
+          const SelCoef co = sel_coef(a.o, c, ct);
+          const float2 p = make_float2(ct.gate * co.p0.x, ct.gate * co.p0.y);
+          const float2 dzs = c_cfma(p, d, cz());
+          const float2 dzwv = prosp ? c_cfma(N1, dnext, dzs) : dzs;
+          __stcs(a.dz + roff + t, a.truncated ? dzs : dzwv);
+          if (a.truncated) __stcs(a.dzw + roff + t, dzwv);
+          const float2 zk = z[k], zpk = k > 0 ? z[k - 1] : zp;
+          const float2 dp = c_cfma(zk, d, cz());
+          const float2 dnv = c_cfma(zpk, d, cz());
+          float2 dA = c_cfma(yprev[k], d, cz());
+          const float dgate =
+              co.p0.x * dp.x + co.p0.y * dp.y + co.n0.x * dnv.x + co.n0.y * dnv.y;
+          const float2 dp0 = make_float2(ct.gate * dp.x, ct.gate * dp.y);
+          const float2 dn0 = make_float2(ct.gate * dnv.x, ct.gate * dnv.y);
+          float dgam = c.h * (co.phi.x * dp0.x + co.phi.y * dp0.y);
+          if (prosp) {
+            const float2 q = make_float2(dp0.x - dn0.x, dp0.y - dn0.y);
+            const float rg = co.ratio * ct.g;
+            dA = make_float2(fmaf(rg, q.x, dA.x), fmaf(rg, q.y, dA.y));
+            if (!a.o.gamma_horizon) dgam += co.ratio * (co.A.x * q.x + co.A.y * q.y);
+          }
+          const float2 dphi = sel_dphi(co.a, co.A, co.phi);
+          const float gh = ct.g * c.h;
+          const float2 da =
+              c_cfma(dphi, make_float2(gh * dp0.x, gh * dp0.y), c_cfma(co.A, dA, cz()));
+          dgam -= c.h * (da.x + ct.th * da.y);
+          float dth = (1.f - ct.g) * c.h * da.y;
+          float dbias_e = dgam;
+          if (a.o.has_gamma) {
+            if (a.o.log_shift) {
+              dbias_e = dgam * ct.g;
+              a.dG[roff + t] = dbias_e * a.o.gamma_scale * (1.f - ct.sig * ct.sig);
+            } else {
+              dbias_e = dgam * c.span * ct.sig * (1.f - ct.sig);
+              a.dG[roff + t] = dbias_e;
+            }
+          }
+          float dtheta_e = dth;
+          if (a.o.has_warp) {
+            if (a.o.bound_warp) {
+              const float un = c.theta * ct.scale;
+              dth = (un >= c.th_lo && un <= c.th_hi) ? dth : 0.f;
+            }
+            a.dD[roff + t] = dth * ct.th * a.o.warp_scale * (1.f - ct.warp * ct.warp);
+            dtheta_e = dth * ct.scale;
+          }
+          if (a.o.has_write)
+            a.dW[roff + t] =
+                a.o.write_sigmoid ? dgate * ct.gate * (1.f - ct.gate / a.o.write_max) : dgate;
+          acc_bias += dbias_e;
+          acc_theta += dtheta_e;
+        }
+        dnext = d;
+        A1 = A[k];
+        N1 = nn[k];
+      }
+      dcarry = dcarry_next;
+      {
+        const float4 q = s_first[0];
+        A_next = make_float2(q.x, q.y);
+        n_next = make_float2(q.z, q.w);
+      }
+    }
+    // row finished: deterministic CTA reduction of the bias / theta sums
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      acc_bias += __shfl_xor_sync(0xffffffffu, acc_bias, o);
+      acc_theta += __shfl_xor_sync(0xffffffffu, acc_theta, o);
+    }
+    __syncthreads();
+    if (lane == 0) {
+      s_red[0][warp] = acc_bias;
+      s_red[1][warp] = acc_theta;
+    }
+    __syncthreads();
+    if (tid < 2) {
+      float s = 0.f;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) s += s_red[tid][w];
+      a.partials[(size_t)row * 2 + tid] = s;
+    }
+  }
+}
+
+// dd_group[g, b, t] = sum over channels f of group g of dD[f, b, t], summed in
+// increasing f (deterministic); one thread per (b, t), up to 32 groups.
+__global__ void __launch_bounds__(256)
+    sel_group_reduce_kernel(const float *__restrict__ dD, const long long *__restrict__ groups,
+                            float *__restrict__ out, int F, int ngroups, int64_t BT) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= BT) return;
+  float acc[32];
+#pragma unroll
+  for (int g = 0; g < 32; ++g) acc[g] = 0.f;
+  for (int f = 0; f < F; ++f) {
+    const int g = (int)groups[f];
+    const float v = dD[(int64_t)f * BT + i];
+#pragma unroll
+    for (int q = 0; q < 32; ++q)
+      if (q == g) acc[q] += v;
+  }
+  for (int g = 0; g < ngroups; ++g) out[(int64_t)g * BT + i] = acc[g];
+}
+
+// dbias / dtheta from the per-row sums, summed in double over the batch.
+__global__ void sel_param_reduce_kernel(const float *__restrict__ partials, float *dbias,
+                                        float *dtheta, int F, int batch) {
+  const int f = blockIdx.x * blockDim.x + threadIdx.x;
+  if (f >= F) return;
+  double sb = 0.0, st = 0.0;
+  for (int b = 0; b < batch; ++b) {
+    sb += partials[((int64_t)f * batch + b) * 2];
+    st += partials[((int64_t)f * batch + b) * 2 + 1];
+  }
+  dbias[f] = (float)sb;
+  dtheta[f] = (float)st;
+}
+
+}  // namespace rqf

@@ -12,6 +12,7 @@ Call sites served (reference paths):
   rqf_models/backbones/rqf/block.py:926-934   -> _triton_chunked_scan_prospective
   rqf_models/backbones/rqf/pure.py:234-238    -> fbt_prospective_scan / fbt_recompute_scan
   rqf_models/backbones/rqf/block.py:882, :904 -> TBPTT(1) fused surrogate on CUDA
+  rqf_models/ops/selective_scan.py:119, :133   -> selective_forward / selective_backward
 """
 
 from __future__ import annotations
@@ -33,6 +34,8 @@ _BINDINGS = [
      ops._triton_chunked_scan_prospective),
     ("rqf_models.backbones.rqf.pure", "fbt_prospective_scan", ops.fbt_prospective_scan),
     ("rqf_models.backbones.rqf.pure", "fbt_recompute_scan", ops.fbt_recompute_scan),
+    ("rqf_models.ops.selective_scan_kernel", "selective_forward", ops.selective_forward),
+    ("rqf_models.ops.selective_scan_kernel", "selective_backward", ops.selective_backward),
 ]
 
 

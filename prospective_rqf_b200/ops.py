@@ -21,6 +21,7 @@ _scan_with_grad_mode :882-902):
 
 from __future__ import annotations
 
+import ctypes
 import os
 
 import torch
@@ -40,6 +41,9 @@ __all__ = [
     "sequential_scan",
     "parallel_scan",
     "sequential_scan_abs",
+    "selective_forward",
+    "selective_backward",
+    "selective_layer_scan",
 ]
 
 
@@ -419,3 +423,157 @@ def parallel_scan(C1, C2, u, B=None):
 def sequential_scan_abs(C1, C2, u, B=None):
     """|sequential_scan(...)| (rqf_models/ops/scan.py:381-432)."""
     return sequential_scan(C1, C2, u, B).abs()
+
+
+# ------------------------------------------------------ selective scan
+_SEL_FIELDS = ("gamma_logits", "warp_logits", "write_logits", "bias", "theta", "groups",
+               "minimum", "span", "step", "horizon", "theta_minimum", "theta_maximum")
+
+
+def _sel_options(opt) -> "_abi.SelectiveOptions":
+    o = _abi.SelectiveOptions()
+    (o.has_gamma, o.has_warp, o.has_write, o.log_shift) = (int(bool(v)) for v in opt[:4])
+    o.gamma_scale, o.warp_scale = float(opt[4]), float(opt[5])
+    o.prospective, o.gamma_horizon, o.write_sigmoid = (int(bool(v)) for v in opt[6:9])
+    o.write_max, o.write_bias = float(opt[9]), float(opt[10])
+    o.bound_warp = int(bool(opt[11]))
+    return o
+
+
+def _sel_tensors(inputs, device):
+    """Contiguous fp32 / int64 device tensors of a SelectiveScanInputs-like
+    13-tuple (rqf_models/ops/selective_scan.py:10-23) and its C struct."""
+    opt = inputs[12]
+    t = {}
+    for i, name in enumerate(_SEL_FIELDS):
+        v = inputs[i]
+        if v is None or (name.endswith("_logits") and v.numel() == 0):
+            t[name] = None
+        elif name == "groups":
+            t[name] = v.to(device=device, dtype=torch.int64).contiguous()
+        else:
+            t[name] = v.to(device=device, dtype=torch.float32).contiguous()
+    if not opt[0]:
+        t["gamma_logits"] = None
+    if not opt[1]:
+        t["warp_logits"], t["groups"] = None, None
+    if not opt[2]:
+        t["write_logits"] = None
+    s = _abi.SelectiveInputs()
+    for name in _SEL_FIELDS:
+        setattr(s, name, None if t[name] is None else t[name].data_ptr())
+    s.num_groups = int(t["warp_logits"].shape[0]) if t["warp_logits"] is not None else 0
+    return t, s, _sel_options(opt)
+
+
+def selective_forward(z, inputs, activate, write_raw, chunk=None):
+    """Fused input-dependent ZOH scan — drop-in for
+    rqf_models/ops/selective_scan_kernel.py:selective_forward (:491).
+    Returns (raw | None, act | None, entries); `entries` holds this backend's
+    per-tile entry states (opaque to the caller, passed back to
+    selective_backward); `chunk` is accepted and unused (fixed tiles)."""
+    dev = _require_cuda(z)
+    if not activate and not write_raw:
+        raise ValueError("selective scan requires at least one output")
+    zz = _c64(z)
+    F, B, T = _shape3(zz, "z")
+    keep, sin, sopt = _sel_tensors(inputs, dev)
+    lib = _abi.load()
+    raw = torch.empty_like(zz) if write_raw else None
+    act = torch.empty_like(zz) if activate else None
+    entries = torch.empty((F * B, max(int(lib.rqf_selective_num_tiles(T)), 1)),
+                          dtype=torch.complex64, device=dev)
+    with _timing.launch("rqf_selective_forward", F * B * T):
+        _abi.check(lib.rqf_selective_forward(
+            _abi.ptr(zz), ctypes.byref(sin), ctypes.byref(sopt), _abi.ptr(raw), _abi.ptr(act),
+            _abi.ptr(entries), F, B, T, _abi.stream_of(zz)), "rqf_selective_forward")
+    _done(dev)
+    del keep
+    return raw, act, entries
+
+
+def selective_backward(z, inputs, entries, gy, gx, activate, truncated, chunk=None):
+    """Fused backward — drop-in for selective_scan_kernel.py:selective_backward
+    (:517).  Returns (dz, dzw, dg, dd_group, dw, dbias, dtheta); dzw is dz
+    unless truncated (TBPTT(1)), as in the reference."""
+    dev = _require_cuda(z)
+    zz = _c64(z)
+    F, B, T = _shape3(zz, "z")
+    keep, sin, sopt = _sel_tensors(inputs, dev)
+    opt = inputs[12]
+    lib = _abi.load()
+    gyc = None if gy is None else _c64(gy)
+    gxc = None if gx is None else _c64(gx)
+    dz = torch.empty_like(zz)
+    dzw = torch.empty_like(zz) if truncated else dz
+    dg = torch.empty_like(keep["gamma_logits"]) if opt[0] else None
+    dd = torch.empty_like(keep["warp_logits"]) if opt[1] else None
+    dw = torch.empty_like(keep["write_logits"]) if opt[2] else None
+    dbias = torch.empty(F, dtype=torch.float32, device=dev)
+    dtheta = torch.empty(F, dtype=torch.float32, device=dev)
+    scratch = _scratch(lib.rqf_selective_scratch_bytes(F, B, T, int(bool(opt[1]))), dev)
+    with _timing.launch("rqf_selective_backward", F * B * T):
+        _abi.check(lib.rqf_selective_backward(
+            _abi.ptr(zz), ctypes.byref(sin), ctypes.byref(sopt), _abi.ptr(entries),
+            _abi.ptr(gyc), _abi.ptr(gxc), int(bool(truncated)), _abi.ptr(dz),
+            _abi.ptr(dzw if truncated else None), _abi.ptr(dg), _abi.ptr(dd), _abi.ptr(dw),
+            _abi.ptr(dbias), _abi.ptr(dtheta), _abi.ptr(scratch), F, B, T, _abi.stream_of(zz)),
+            "rqf_selective_backward")
+    _done(dev)
+    del keep
+    return dz, dzw, dg, dd, dw, dbias, dtheta
+
+
+class _SelectiveLayerScan(torch.autograd.Function):
+    """Owns the drive GEMM z = W @ x so the TBPTT(1) lag cotangent reaches W
+    only (rqf_models/ops/selective_scan.py:_SelectiveLayerScan :107-170)."""
+
+    @staticmethod
+    def forward(ctx, x, weight, *args):
+        *tensors, options, truncated, activate, write_raw, chunk = args
+        inputs = tuple(tensors) + (options,)
+        f_in, batch, time = x.shape
+        with torch.autocast(x.device.type, enabled=False):
+            z = (weight @ x.reshape(f_in, batch * time)).reshape(-1, batch, time)
+        raw, act, entries = selective_forward(z, inputs, activate, write_raw, chunk)
+        ctx.save_for_backward(x, weight, z, entries, *[t for t in tensors if t is not None])
+        ctx.none_mask = [t is None for t in tensors]
+        ctx.options, ctx.truncated = options, truncated
+        ctx.activate, ctx.chunk = activate, chunk
+        ctx.set_materialize_grads(False)
+        return raw, act
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_raw, grad_act):
+        x, weight, z, entries, *present = ctx.saved_tensors
+        it = iter(present)
+        tensors = [None if none else next(it) for none in ctx.none_mask]
+        inputs = tuple(tensors) + (ctx.options,)
+        dx_drive, dw_drive, dg, dd, dw, dbias, dtheta = selective_backward(
+            z, inputs, entries, grad_raw, grad_act, ctx.activate, ctx.truncated, ctx.chunk)
+        f_in = x.shape[0]
+        with torch.autocast(x.device.type, enabled=False):
+            dx = (weight.mH @ dx_drive.reshape(weight.shape[0], -1)).reshape_as(x)
+            dweight = dw_drive.reshape(weight.shape[0], -1) @ x.reshape(f_in, -1).mH
+        grads = (dx, dweight, dg, dd, dw, dbias, dtheta) + (None,) * 12
+        return tuple(g if need else None for g, need in zip(grads, ctx.needs_input_grad))
+
+
+def selective_layer_scan(x, weight, inputs, *, truncated: bool = False, activate: bool = True,
+                         write_raw: bool = True, use_kernel: bool = True, chunk=None):
+    """Complex (I,B,T) selective layer on the B200 kernels — mirrors
+    rqf_models/ops/selective_scan.py:selective_layer_scan (:173) for CUDA
+    complex64 inputs (the reference's kernel-eligible case).  Returns
+    (raw | None, act | None)."""
+    if not activate and not write_raw:
+        raise ValueError("selective scan requires at least one output")
+    if not use_kernel:
+        raise ValueError("use_kernel=False selects the reference's PyTorch path, which this "
+                         "backend does not provide")
+    if chunk is not None and (chunk < 1 or chunk & (chunk - 1)):
+        raise ValueError("chunk must be a positive power of two")
+    _require_cuda(x, weight)
+    tensors = [v.contiguous() if isinstance(v, torch.Tensor) else v for v in inputs[:-1]]
+    return _SelectiveLayerScan.apply(x.contiguous(), weight, *tensors, inputs[-1], truncated,
+                                     activate, write_raw, chunk)

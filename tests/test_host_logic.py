@@ -51,6 +51,8 @@ def _fake_reference(monkeypatch):
         "rqf_models.ops.scan": {"_triton_chunked_scan": "orig"},
         "rqf_models.ops.fbt_scan_kernel": {"fbt_prospective_scan": "orig",
                                            "fbt_recompute_scan": "orig"},
+        "rqf_models.ops.selective_scan_kernel": {"selective_forward": "orig",
+                                                 "selective_backward": "orig"},
         "rqf_models.backbones": {},
         "rqf_models.backbones.rqf": {},
         "rqf_models.backbones.rqf.block": {"_triton_chunked_scan_prospective": "orig"},
@@ -117,6 +119,9 @@ def test_install_against_the_reference_tree(monkeypatch):
         assert scan._triton_chunked_scan is ops._triton_chunked_scan
         assert pure.fbt_recompute_scan is ops.fbt_recompute_scan
         assert pure.fbt_prospective_scan is ops.fbt_prospective_scan
-        assert len(patched) == 10
+        import rqf_models.ops.selective_scan_kernel as sk
+
+        assert sk.selective_forward is ops.selective_forward
+        assert len(patched) == 12
     finally:
         integration.uninstall()
