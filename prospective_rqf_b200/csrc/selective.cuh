@@ -128,8 +128,11 @@ __device__ __forceinline__ SelCoef sel_coef(const SelOptions &o, const SelChan &
                                             const SelCtl &k) {
   SelCoef r;
   const float ar = -k.g * c.h, ai = (1.f - k.g) * k.th * c.h;
-  float sn, cs;
-  sincosf(ai, &sn, &cs);
+  // half-angle sincos gives sin(ai), cos(ai) and the cancellation-free
+  // 1 - cos(ai) = 2 sin^2(ai/2) from one call
+  float hs, hc;
+  sincosf(0.5f * ai, &hs, &hc);
+  const float sn = 2.f * hs * hc, one_m_cs = 2.f * hs * hs, cs = 1.f - one_m_cs;
   const float e = expf(ar);
   r.a = make_float2(ar, ai);
   r.A = make_float2(e * cs, e * sn);
@@ -139,10 +142,10 @@ __device__ __forceinline__ SelCoef sel_coef(const SelOptions &o, const SelChan &
     s = c_fma(r.a, s, make_float2(0.5f, 0.f));
     r.phi = c_fma(r.a, s, cone());
   } else {
-    // e^a - 1 without cancellation: expm1(ar) cos(ai) - 2 sin^2(ai/2) + i e^ar sin(ai)
-    const float hs = sinf(0.5f * ai);
-    const float er = expm1f(ar) * cs - 2.f * hs * hs, ei = r.A.y;
-    r.phi = make_float2((er * ar + ei * ai) / den, (ei * ar - er * ai) / den);
+    // e^a - 1 without cancellation: expm1(ar) cos(ai) - (1 - cos(ai)) + i e^ar sin(ai)
+    const float er = expm1f(ar) * cs - one_m_cs, ei = r.A.y;
+    const float inv = 1.f / den;
+    r.phi = make_float2((er * ar + ei * ai) * inv, (ei * ar - er * ai) * inv);
   }
   const float gh = k.g * c.h;
   r.p0 = make_float2(gh * r.phi.x, gh * r.phi.y);
@@ -175,7 +178,8 @@ __device__ __forceinline__ float2 sel_dphi(float2 a, float2 A, float2 phi) {
     return s;
   }
   const float2 d = make_float2(A.x - phi.x, A.y - phi.y);
-  return make_float2((d.x * a.x + d.y * a.y) / den, (d.y * a.x - d.x * a.y) / den);
+  const float inv = 1.f / den;
+  return make_float2((d.x * a.x + d.y * a.y) * inv, (d.y * a.x - d.x * a.y) * inv);
 }
 
 template <int K>
@@ -252,6 +256,10 @@ __global__ void __launch_bounds__(NT) sel_bwd_kernel(const SelArgs a) {
   __shared__ float4 s_first[NW + 1];  // (A, gated n) of each warp's first sample
   __shared__ float2 s_efirst[NW];     // e at each warp's first sample (TBPTT(1))
   __shared__ float s_red[2][NW];
+  // Per-sample controller / ZOH values of the replay, reused by the VJP so the
+  // transcendentals run once per sample: [field][k][thread] (conflict-free).
+  constexpr int kStash = 10;  // A.re, A.im, phi.re, phi.im, g, th, gate, sig, warp, scale
+  __shared__ float s_stash[kStash][K][NT];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int T = a.T;
   const bool prosp = a.o.prospective != 0;
@@ -287,6 +295,16 @@ __global__ void __launch_bounds__(NT) sel_bwd_kernel(const SelArgs a) {
         nn[k] = in ? make_float2(ct.gate * co.n0.x, ct.gate * co.n0.y) : cz();
         A[k] = in ? co.A : cz();
         u[k] = in ? c_fma(nn[k], k > 0 ? z[k - 1] : zp, c_mul(p, z[k])) : cz();
+        s_stash[0][k][tid] = co.A.x;
+        s_stash[1][k][tid] = co.A.y;
+        s_stash[2][k][tid] = co.phi.x;
+        s_stash[3][k][tid] = co.phi.y;
+        s_stash[4][k][tid] = ct.g;
+        s_stash[5][k][tid] = ct.th;
+        s_stash[6][k][tid] = ct.gate;
+        s_stash[7][k][tid] = ct.sig;
+        s_stash[8][k][tid] = ct.warp;
+        s_stash[9][k][tid] = ct.scale;
       }
       float2 g = cone(), y = cz();
 #pragma unroll
@@ -353,8 +371,27 @@ __global__ void __launch_bounds__(NT) sel_bwd_kernel(const SelArgs a) {
         const int t = t0 + k;
         const float2 d = a.truncated ? e[k] : c_fma(c_conj(A1), dnext, e[k]);
         if (t < T) {
-          const SelCtl ct = sel_controller(a.o, c, gl[k], dl[k], wl[k]);
-          const SelCoef co = sel_coef(a.o, c, ct);
+          SelCtl ct;
+          ct.g = s_stash[4][k][tid];
+          ct.th = s_stash[5][k][tid];
+          ct.gate = s_stash[6][k][tid];
+          ct.sig = s_stash[7][k][tid];
+          ct.warp = s_stash[8][k][tid];
+          ct.scale = s_stash[9][k][tid];
+          SelCoef co;
+          co.A = make_float2(s_stash[0][k][tid], s_stash[1][k][tid]);
+          co.phi = make_float2(s_stash[2][k][tid], s_stash[3][k][tid]);
+          co.a = make_float2(-ct.g * c.h, (1.f - ct.g) * ct.th * c.h);
+          const float gh0 = ct.g * c.h;
+          co.p0 = make_float2(gh0 * co.phi.x, gh0 * co.phi.y);
+          co.n0 = cz();
+          co.ratio = 0.f;
+          if (prosp) {
+            co.ratio = a.o.gamma_horizon ? 1.f / ct.g : c.horizon;
+            const float rg = co.ratio * ct.g;
+            co.p0 = make_float2(fmaf(rg, co.A.x, co.p0.x), fmaf(rg, co.A.y, co.p0.y));
+            co.n0 = make_float2(-rg * co.A.x, -rg * co.A.y);
+          }
           const float2 p = make_float2(ct.gate * co.p0.x, ct.gate * co.p0.y);
           const float2 dzs = c_cfma(p, d, cz());
           const float2 dzwv = prosp ? c_cfma(N1, dnext, dzs) : dzs;
