@@ -66,6 +66,14 @@ const char *rqf_status_string(int status);
  * Synchronises `stream`. */
 int rqf_read_device_error(int *out_code, int clear, rqf_stream_t stream);
 
+/* Diagnostic: run one look-back wait on a predecessor flag that nothing ever
+ * publishes, so the bounded wait runs out (about 0.3 s), latches
+ * RQF_ERR_LOOKBACK_TIMEOUT in the device error word and the kernel returns —
+ * the failure path of every cross-tile wait, without faulting or hanging the
+ * GPU.  `scratch` needs 256 bytes.  Read the result with
+ * rqf_read_device_error. */
+int rqf_selftest_lookback_timeout(void *scratch, rqf_stream_t stream);
+
 /* ---- sizes of saved context and scratch ------------------------------ */
 /* BTF kernels: tiles along time, rows = batch * filters. */
 int64_t rqf_btf_num_tiles(int64_t time);

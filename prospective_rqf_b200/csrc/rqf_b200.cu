@@ -96,6 +96,12 @@ inline T *at(void *base, size_t off) {
   return reinterpret_cast<T *>(static_cast<char *>(base) + off);
 }
 
+// One look-back wait on slot 0 of a cleared flag array: nothing publishes it,
+// so the bounded wait gives up, latches the timeout error and returns.
+__global__ void lookback_selftest_kernel(const u64 *flags, float2 *out) {
+  if (threadIdx.x == 0) *out = lookback_const(flags, 1, cone());
+}
+
 // ------------------------------------------------------------- FBT
 int fbt_dims_ok(int64_t F, int64_t B, int64_t T) {
   if (F < 0 || B < 0 || T < 0) return RQF_ERR_SHAPE;
@@ -267,6 +273,16 @@ int rqf_read_device_error(int *out_code, int clear, rqf_stream_t stream) {
   }
   *out_code = h;
   return RQF_OK;
+}
+
+int rqf_selftest_lookback_timeout(void *scratch, rqf_stream_t stream) {
+  if (!scratch) return RQF_ERR_ARGUMENT;
+  if (!aligned(scratch, 16)) return RQF_ERR_ALIGN;
+  if (cudaMemsetAsync(scratch, 0, 256, stream) != cudaSuccess) return RQF_ERR_LAUNCH;
+  u64 *flags = static_cast<u64 *>(scratch);
+  float2 *out = reinterpret_cast<float2 *>(static_cast<char *>(scratch) + 128);
+  lookback_selftest_kernel<<<1, 32, 0, stream>>>(flags, out);
+  return launch_status();
 }
 
 // ---------------------------------------------------------------- sizes
