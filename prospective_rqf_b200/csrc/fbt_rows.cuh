@@ -285,4 +285,145 @@ __global__ void __launch_bounds__(NT, 3) fbt_bwd_rows_kernel(const FbtArgs a) {
   cp_async_wait<0>();
 }
 
+// -------------------------------------------------- TBPTT(1) backward
+// No temporal adjoint, so tiles run in time order with only the forward
+// states replayed from the stored entry carries.  grad_zw[t] = conj(tap1) *
+// g[t+1] for the last sample of a tile needs g of the next tile's first
+// sample: the next tile (same CTA, next item) writes that one element.
+template <int NT, int K, int S, bool FUSE_ACT>
+__global__ void __launch_bounds__(NT, 3) fbt_tbptt_rows_kernel(const FbtArgs a) {
+  constexpr int NW = NT / 32, L = NT * K, LK = (K == 4) ? 2 : (K == 8) ? 3 : 4;
+  constexpr int WSZ = 16 * K;
+  extern __shared__ __align__(16) float4 dsm[];  // [S][2 inputs][NW][WSZ]
+  __shared__ float2 s_pw[S][kPowTable];
+  __shared__ float2 s_meta[S][2];  // {entry carry C, z sample before the tile}
+  __shared__ float2 s_warp_f[NW];
+  __shared__ float2 s_gfirst[NW];
+  __shared__ float2 s_red[3][NW];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = gridDim.x, rows = (int)a.rows, T = (int)a.T, ntiles = a.ntiles;
+  const int wofs = warp * 32 * K;
+  constexpr size_t stage_sz = (size_t)2 * NW * WSZ;
+
+  RowCursor ic{(int)blockIdx.x, 0, 0};
+  auto issue = [&]() {
+    if (ic.row < rows) {
+      float4 *base = dsm + ic.stage * stage_sz;
+      const size_t roff = (size_t)ic.row * T;
+      fbt_issue_tile<K>(base + warp * WSZ, a.z + roff, ic.j * L + wofs, T, lane);
+      fbt_issue_tile<K>(base + (NW + warp) * WSZ, a.gout + roff, ic.j * L + wofs, T, lane);
+      if (tid == 0) {
+        const int t0 = ic.j * L;
+        cp_async8(&s_meta[ic.stage][0], a.carries + (size_t)ic.row * ntiles + ic.j, true);
+        cp_async8(&s_meta[ic.stage][1], a.z + roff + (t0 > 0 ? t0 - 1 : 0), t0 > 0);
+        stage_table<S>(s_pw, ic.stage, ic.j == 0, a.c1, ic.row / a.batch);
+      }
+      ic.advance(ntiles, G, S);
+    }
+    cp_async_commit();
+  };
+
+#pragma unroll
+  for (int s = 0; s < S - 1; ++s) issue();
+  RowCursor pc{(int)blockIdx.x, 0, 0};
+  float2 lam = cz(), t0c = cz(), t1c = cz(), lpow = cz();
+  float2 acc_c1 = cz(), acc_t0 = cz(), acc_t1 = cz();
+  while (pc.row < rows) {
+    cp_async_wait<S - 2>();
+    __syncthreads();
+    issue();
+    const int s = pc.stage;
+    const float2 *pw = s_pw[s];
+    if (pc.j == 0) {
+      const int f = pc.row / a.batch;
+      lam = pw[0];
+      t0c = a.tap0[f];
+      t1c = a.tap1[f];
+      lpow = pow_from_table<false>(pw, LK, lane);
+    }
+    float4 *zbuf = dsm + s * stage_sz + warp * WSZ;
+    float4 *gbuf = dsm + s * stage_sz + (NW + warp) * WSZ;
+    const size_t roff = (size_t)pc.row * T;
+    const int tile0 = pc.j * L;
+    float2 z[K], go[K];
+    read_blocked<K>(zbuf, z, lane);
+    read_blocked<K>(gbuf, go, lane);
+    float2 zp = shfl_up2(z[K - 1], 1);
+    if (lane == 0) zp = warp > 0 ? read_sample<K>(zbuf - WSZ, 32 * K - 1) : s_meta[s][1];
+    float2 b[K];
+    b[0] = c_fma(t1c, zp, c_mul(t0c, z[0]));
+#pragma unroll
+    for (int k = 1; k < K; ++k) b[k] = c_fma(t1c, z[k - 1], c_mul(t0c, z[k]));
+    float2 y = cz();
+#pragma unroll
+    for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
+    float2 e, At;
+    cta_scan_entry_fwd<NT, LK>(y, s_meta[s][0], pw, lpow, e, At, s_warp_f);
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const float2 yp = e;
+      e = c_fma(lam, e, b[k]);
+      go[k] = FUSE_ACT ? c_relu_mask(go[k], e) : go[k];
+      acc_c1 = c_cfma(yp, go[k], acc_c1);
+      acc_t0 = c_cfma(z[k], go[k], acc_t0);
+      acc_t1 = c_cfma(k > 0 ? z[k - 1] : zp, go[k], acc_t1);
+    }
+    float2 gn = shfl_down2(go[0], 1);
+    if (lane == 0) s_gfirst[warp] = go[0];
+    __syncthreads();
+    if (lane == 31) gn = warp + 1 < NW ? s_gfirst[warp + 1] : cz();
+    float2 dz[K], dzw[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      dz[k] = c_cfma(t0c, go[k], cz());
+      dzw[k] = c_cfma(t1c, k + 1 < K ? go[k + 1] : gn, cz());
+    }
+    if (tid == 0 && pc.j > 0) __stcs(a.out2 + roff + tile0 - 1, c_cfma(t1c, go[0], cz()));
+    fbt_store_tile<K>(gbuf, dz, a.out + roff, tile0 + wofs, T, lane);
+    // grad_zw staged through the z region (every warp has read its z samples
+    // before the scan barrier).  The tile's last sample needs g of the next
+    // tile: unless this is the row's last tile, only the first half of that
+    // pair is stored here and the next tile stores the other.
+    const int last = tile0 + L - 1;
+#pragma unroll
+    for (int m = 0; m < K / 2; ++m)
+      zbuf[swz<K>(lane * (K / 2) + m)] =
+          make_float4(dzw[2 * m].x, dzw[2 * m].y, dzw[2 * m + 1].x, dzw[2 * m + 1].y);
+    __syncwarp();
+#pragma unroll
+    for (int v = 0; v < K / 2; ++v) {
+      const int t = tile0 + wofs + 2 * (v * 32 + lane);
+      if (t >= T) continue;
+      const float4 q = zbuf[swz<K>(v * 32 + lane)];
+      if (t + 1 == last && pc.j + 1 < ntiles)
+        __stcs(a.out2 + roff + t, make_float2(q.x, q.y));
+      else
+        st_stream4(a.out2 + roff + t, q);
+    }
+    if (pc.j + 1 == ntiles) {  // row finished
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        acc_c1 = c_add(acc_c1, shfl_xor2(acc_c1, o));
+        acc_t0 = c_add(acc_t0, shfl_xor2(acc_t0, o));
+        acc_t1 = c_add(acc_t1, shfl_xor2(acc_t1, o));
+      }
+      if (lane == 0) {
+        s_red[0][warp] = acc_c1;
+        s_red[1][warp] = acc_t0;
+        s_red[2][warp] = acc_t1;
+      }
+      __syncthreads();
+      if (tid < 3) {
+        float2 sum = cz();
+#pragma unroll
+        for (int w = 0; w < NW; ++w) sum = c_add(sum, s_red[tid][w]);
+        a.partials[(size_t)pc.row * 3 + tid] = sum;
+      }
+      acc_c1 = acc_t0 = acc_t1 = cz();
+    }
+    pc.advance(ntiles, G, S);
+  }
+  cp_async_wait<0>();
+}
+
 }  // namespace rqf

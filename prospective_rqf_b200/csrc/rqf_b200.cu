@@ -480,6 +480,21 @@ int rqf_tbptt1_two_tap_backward(int layout, const float *c1, const float *tap0,
                        scratch, F, B, T);
   const bool vec = (T % 2 == 0) && aligned(z, 16) && aligned(grad_out, 16) &&
                    aligned(grad_z, 16) && aligned(grad_zw, 16);
+  if (vec) {
+    constexpr size_t smem = fbt_rows_smem_bytes<kFbtThreads, kFbtK, 2, kRowsBwdStages>();
+    const bool done =
+        fuse_act ? launch_rows(fbt_tbptt_rows_kernel<kFbtThreads, kFbtK, kRowsBwdStages, true>,
+                               smem, a, stream)
+                 : launch_rows(fbt_tbptt_rows_kernel<kFbtThreads, kFbtK, kRowsBwdStages, false>,
+                               smem, a, stream);
+    if (done) {
+      if ((st = launch_status()) != RQF_OK) return st;
+      reduce_partials_kernel<<<(unsigned)F, 256, 0, stream>>>(
+          a.partials, reinterpret_cast<float2 *>(grad_c1), reinterpret_cast<float2 *>(grad_tap0),
+          reinterpret_cast<float2 *>(grad_tap1), B, B, 1, 1);
+      return launch_status();
+    }
+  }
   const unsigned grid = (unsigned)(a.rows * a.ntiles);
   if (vec) {
     if (fuse_act)

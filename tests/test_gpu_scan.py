@@ -349,6 +349,36 @@ def test_tbptt_vs_oracle(layout, T):
             assert_close(host(t.grad), r, GRAD_TOL, f"{k} fuse={fuse}")
 
 
+@pytest.mark.parametrize("T", [2, 2048, 2050, 5000])
+@pytest.mark.parametrize("fuse", [False, True])
+def test_tbptt_fbt_persistent_rows_vs_oracle(T, fuse):
+    """640 rows: the persistent TBPTT(1) kernel.  g is pointwise here, so the
+    oracle is evaluated on the cotangent pre-masked by the kernel's own
+    split-ReLU decisions (checked to differ from fp64 only near 0)."""
+    rng = np.random.default_rng(3000 + T + int(fuse))
+    F, B = 40, 16
+    c1 = coeffs(rng, F)
+    t0, t1 = c64(crandn(rng, F, 0.5)), c64(crandn(rng, F, 0.5))
+    z = c64(crandn(rng, (F, B, T)))
+    gy = c64(crandn(rng, (F, B, T)))
+    ins = [dev(a, grad=True) for a in (c1, t0, t1, z)]
+    lag = dev(z, grad=True)
+    y = rqf().tbptt1_two_tap_scan(ins[3], ins[0], ins[1], ins[2], delayed_u=lag, layout="fbt",
+                                  fuse_act=fuse)
+    ref_y = oracle.two_tap_forward(c1, t0, t1, z, "fbt", fuse_act=fuse)
+    assert_close(host(y), ref_y, FWD_TOL, "y")
+    g_ref = gy
+    if fuse:
+        mask = oracle.relu_mask_from_output(host(y))
+        raw_ref = oracle.two_tap_forward(c1, t0, t1, z, "fbt", fuse_act=False)
+        assert oracle.mask_disagreement(mask, raw_ref) < MASK_EDGE
+        g_ref = np.where(mask[..., 0], gy.real, 0.0) + 1j * np.where(mask[..., 1], gy.imag, 0.0)
+    y.backward(dev(gy))
+    gz, gzw, gc1, gt0, gt1 = oracle.tbptt_backward(c1, t0, t1, z, g_ref, "fbt", fuse_act=False)
+    for t, r, k in zip(ins + [lag], (gc1, gt0, gt1, gz, gzw), ("gc1", "gt0", "gt1", "gz", "gzw")):
+        assert_close(host(t.grad), r, GRAD_TOL, k)
+
+
 # ------------------------------------------------------- edge cases
 def test_empty_shapes_give_zero_grads():
     for shape in [(0, 10, 4), (2, 0, 4)]:
