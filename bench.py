@@ -35,17 +35,13 @@ import torch.distributed as dist
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-ALG_BYTES = {  # algorithmic bytes per scan element and launch kind
-    "rqf_fbt_prospective_forward": 16,
-    "rqf_fbt_prospective_backward": 24,
-    "rqf_tbptt1_two_tap_backward": 32,
-}
 KERNELS_PER_CALL = {  # kernels each C-ABI call launches (the backward adds the reduction)
     "rqf_fbt_prospective_forward": 1,
+    "rqf_fbt_block_forward": 1,
     "rqf_fbt_prospective_backward": 2,
     "rqf_tbptt1_two_tap_backward": 2,
 }
-FALLBACK_HBM_GBS = 6650.0
+SCAN_CALLS = tuple(KERNELS_PER_CALL)
 
 
 def parse():
@@ -60,11 +56,9 @@ def parse():
 
 
 def peaks():
-    p = ROOT / "MEASURED_PEAKS.json"
-    if p.exists():
-        d = json.loads(p.read_text())
-        return float(d["hbm_gbs"]), "measured"
-    return FALLBACK_HBM_GBS, "fallback"
+    from prospective_rqf_b200.microbench import hbm_peak
+
+    return hbm_peak()
 
 
 # ------------------------------------------------------------------ clocks
@@ -244,9 +238,9 @@ def scan_roofline(timer_summary, hbm_peak, peak_kind, traffic):
     tot_ms = 0.0
     per = {}
     for name, s in timer_summary.items():
-        if name not in ALG_BYTES:
+        if name not in SCAN_CALLS:
             continue
-        b = ALG_BYTES[name] * s["elements"]
+        b = s["alg_bytes"]
         per[name] = {"launches": s["launches"], "mean_ms": round(s["mean_ms"], 4),
                      "gbs": round(b / (s["total_ms"] * 1e-3) / 1e9, 1) if s["total_ms"] else None,
                      "alg_bytes_per_launch": int(b / max(s["launches"], 1))}

@@ -137,6 +137,17 @@ int rqf_fbt_prospective_forward(const float *c1, const float *tap0,
                                 int64_t batch, int64_t time, int fuse_act,
                                 rqf_stream_t stream);
 
+/* Pure RQF block forward with the complex skip connection fused:
+ *   out = act(y) + skip  (rqf_models/backbones/rqf/pure.py:_forward_fbt_stack
+ *   :535, h = out + h), y the two-tap scan above.  skip may be NULL (then this
+ *   is rqf_fbt_prospective_forward).  The backward is
+ *   rqf_fbt_prospective_backward on the output cotangent; the skip's
+ *   cotangent is that same cotangent. */
+int rqf_fbt_block_forward(const float *c1, const float *tap0, const float *tap1,
+                          const float *z, const float *skip, float *out, float *carries,
+                          void *scratch, int64_t filters, int64_t batch, int64_t time,
+                          int fuse_act, rqf_stream_t stream);
+
 /* Replaces fbt_scan_kernel.py:_fbt_prospective_backward_kernel (:113) and
  * _fbt_recompute_backward_kernel (:439).  grad_out is the cotangent of the
  * forward's output (of the split-ReLU output when fuse_act != 0; the mask is

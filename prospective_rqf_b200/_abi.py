@@ -62,6 +62,8 @@ SIGNATURES: dict[str, tuple] = {
         _int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p]),
     "rqf_fbt_prospective_forward": (
         _int, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
+    "rqf_fbt_block_forward": (
+        _int, [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "rqf_fbt_prospective_backward": (
         _int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "rqf_fbt_prospective_backward_noalloc": (

@@ -83,11 +83,14 @@ __device__ __forceinline__ void fbt_store_tile(float4 *wbuf, const float2 (&o)[K
 }
 
 // ------------------------------------------------------------ forward
-template <int NT, int K, int S, bool FUSE_ACT>
+// SKIP: the stage also carries the same tile of `skip`, added to the output
+// (the Pure RQF complex skip connection h = out + h, fused).
+template <int NT, int K, int S, bool FUSE_ACT, bool SKIP = false>
 __global__ void __launch_bounds__(NT) fbt_fwd_rows_kernel(const FbtArgs a) {
   constexpr int NW = NT / 32, L = NT * K, LK = (K == 4) ? 2 : (K == 8) ? 3 : 4;
   constexpr int WSZ = 16 * K;  // float4 slots per warp region
-  extern __shared__ __align__(16) float4 dsm[];
+  constexpr int NIN = SKIP ? 2 : 1;
+  extern __shared__ __align__(16) float4 dsm[];  // [S][NIN inputs][NW][WSZ]
   __shared__ float2 s_pw[S][kPowTable];
   __shared__ float2 s_warp[NW];
   __shared__ float2 s_zlast;
@@ -98,8 +101,11 @@ __global__ void __launch_bounds__(NT) fbt_fwd_rows_kernel(const FbtArgs a) {
   RowCursor ic{(int)blockIdx.x, 0, 0};  // next item to issue
   auto issue = [&]() {
     if (ic.row < rows) {
-      fbt_issue_tile<K>(dsm + (size_t)ic.stage * NW * WSZ + warp * WSZ,
+      fbt_issue_tile<K>(dsm + (size_t)ic.stage * NIN * NW * WSZ + warp * WSZ,
                         a.z + (size_t)ic.row * T, ic.j * L + wofs, T, lane);
+      if constexpr (SKIP)
+        fbt_issue_tile<K>(dsm + ((size_t)ic.stage * NIN + 1) * NW * WSZ + warp * WSZ,
+                          a.skip + (size_t)ic.row * T, ic.j * L + wofs, T, lane);
       if (tid == 0) stage_table<S>(s_pw, ic.stage, ic.j == 0, a.c1, ic.row / a.batch);
       ic.advance(ntiles, G, S);
     }
@@ -123,7 +129,7 @@ __global__ void __launch_bounds__(NT) fbt_fwd_rows_kernel(const FbtArgs a) {
       lanepow = pow_from_table<false>(pw, LK, lane);
       carry = cz();
     }
-    float4 *wbuf = dsm + (size_t)pc.stage * NW * WSZ + warp * WSZ;
+    float4 *wbuf = dsm + (size_t)pc.stage * NIN * NW * WSZ + warp * WSZ;
     float2 z[K];
     read_blocked<K>(wbuf, z, lane);
     float2 zp = shfl_up2(z[K - 1], 1);
@@ -150,6 +156,12 @@ __global__ void __launch_bounds__(NT) fbt_fwd_rows_kernel(const FbtArgs a) {
     for (int k = 0; k < K; ++k) {
       e = c_fma(lam, e, b[k]);
       o[k] = FUSE_ACT ? c_relu(e) : e;
+    }
+    if constexpr (SKIP) {
+      float2 sk[K];
+      read_blocked<K>(wbuf + NW * WSZ, sk, lane);
+#pragma unroll
+      for (int k = 0; k < K; ++k) o[k] = c_add(o[k], sk[k]);
     }
     fbt_store_tile<K>(wbuf, o, a.out + (size_t)pc.row * T, pc.j * L + wofs, T, lane);
     pc.advance(ntiles, G, S);

@@ -29,6 +29,7 @@ struct FbtArgs {
   const float2 *c1, *tap0, *tap1;  // (F,)
   const float2 *z;                 // (rows, T)
   const float2 *gout;              // (rows, T) cotangent (backward)
+  const float2 *skip;              // (rows, T) added to the forward output, or null
   float2 *out;                     // forward: act / raw; backward: grad_z
   float2 *out2;                    // TBPTT backward: grad_zw
   float2 *carries;                 // (rows, ntiles)
@@ -154,6 +155,12 @@ __global__ void __launch_bounds__(NT) fbt_fwd_kernel(const FbtArgs a) {
   for (int k = 0; k < K; ++k) {
     e = c_fma(lam, e, b[k]);
     o[k] = FUSE_ACT ? c_relu(e) : e;
+  }
+  if (a.skip) {
+    float2 sk[K];
+    fbt_load<K, VEC>(a.skip + row * a.T, wstart, tfirst, a.T, sk, s_buf[warp], lane);
+#pragma unroll
+    for (int k = 0; k < K; ++k) o[k] = c_add(o[k], sk[k]);
   }
   fbt_store<K, VEC>(a.out + row * a.T, wstart, tfirst, a.T, o, s_buf[warp], lane);
 }

@@ -119,6 +119,7 @@ FbtArgs fbt_args(const float *c1, const float *tap0, const float *tap1, const fl
   a.tap1 = reinterpret_cast<const float2 *>(tap1);
   a.z = reinterpret_cast<const float2 *>(z);
   a.gout = reinterpret_cast<const float2 *>(gout);
+  a.skip = nullptr;
   a.out = reinterpret_cast<float2 *>(out);
   a.out2 = reinterpret_cast<float2 *>(out2);
   a.carries = reinterpret_cast<float2 *>(carries);
@@ -341,23 +342,42 @@ int rqf_fbt_prospective_forward(const float *c1, const float *tap0, const float 
                                 const float *z, float *out, float *carries, void *scratch,
                                 int64_t filters, int64_t batch, int64_t time, int fuse_act,
                                 rqf_stream_t stream) {
+  return rqf_fbt_block_forward(c1, tap0, tap1, z, nullptr, out, carries, scratch, filters, batch,
+                               time, fuse_act, stream);
+}
+
+int rqf_fbt_block_forward(const float *c1, const float *tap0, const float *tap1, const float *z,
+                          const float *skip, float *out, float *carries, void *scratch,
+                          int64_t filters, int64_t batch, int64_t time, int fuse_act,
+                          rqf_stream_t stream) {
   int st = fbt_dims_ok(filters, batch, time);
   if (st != RQF_OK) return st;
   if (filters == 0 || batch == 0 || time == 0) return RQF_OK;
   if (!c1 || !tap0 || !tap1 || !z || !out || !carries || !scratch) return RQF_ERR_ARGUMENT;
   if (!aligned(c1, 8) || !aligned(tap0, 8) || !aligned(tap1, 8) || !aligned(z, 8) ||
-      !aligned(out, 8) || !aligned(carries, 8) || !aligned(scratch, 16))
+      !aligned(out, 8) || !aligned(carries, 8) || !aligned(scratch, 16) ||
+      (skip && !aligned(skip, 8)))
     return RQF_ERR_ALIGN;
   FbtArgs a = fbt_args(c1, tap0, tap1, z, nullptr, out, nullptr, carries, scratch, filters,
                        batch, time);
-  const bool vec = (time % 2 == 0) && aligned(z, 16) && aligned(out, 16);
+  a.skip = reinterpret_cast<const float2 *>(skip);
+  const bool vec =
+      (time % 2 == 0) && aligned(z, 16) && aligned(out, 16) && (!skip || aligned(skip, 16));
   if (vec) {
-    constexpr size_t smem = fbt_rows_smem_bytes<kFbtThreads, kFbtK, 1, kRowsFwdStages>();
-    const bool done =
-        fuse_act ? launch_rows(fbt_fwd_rows_kernel<kFbtThreads, kFbtK, kRowsFwdStages, true>, smem,
-                               a, stream)
-                 : launch_rows(fbt_fwd_rows_kernel<kFbtThreads, kFbtK, kRowsFwdStages, false>,
-                               smem, a, stream);
+    bool done;
+    if (skip) {
+      constexpr size_t smem = fbt_rows_smem_bytes<kFbtThreads, kFbtK, 2, kRowsBwdStages>();
+      done = fuse_act ? launch_rows(fbt_fwd_rows_kernel<kFbtThreads, kFbtK, kRowsBwdStages, true,
+                                                        true>, smem, a, stream)
+                      : launch_rows(fbt_fwd_rows_kernel<kFbtThreads, kFbtK, kRowsBwdStages,
+                                                        false, true>, smem, a, stream);
+    } else {
+      constexpr size_t smem = fbt_rows_smem_bytes<kFbtThreads, kFbtK, 1, kRowsFwdStages>();
+      done = fuse_act ? launch_rows(fbt_fwd_rows_kernel<kFbtThreads, kFbtK, kRowsFwdStages, true>,
+                                    smem, a, stream)
+                      : launch_rows(fbt_fwd_rows_kernel<kFbtThreads, kFbtK, kRowsFwdStages, false>,
+                                    smem, a, stream);
+    }
     if (done) return launch_status();
   }
   const Scratch lay = scratch_layout(a.rows, a.ntiles);

@@ -118,6 +118,41 @@ class _TBPTTLayer(torch.autograd.Function):
         return gh, gW, gc1, gt0, gt1, None
 
 
+class _PureBlock(torch.autograd.Function):
+    """One full-BPTT Pure RQF block in (F,B,T): z = W @ h, two-tap scan with
+    split-ReLU (or raw), and the complex skip h_out = out + h fused into the
+    scan's store (pure.py:_forward_fbt :212-243 and :535).  Backward: the
+    fused scan VJP on the output cotangent g, then one accumulating GEMM
+    gh = W^H gz + g (the skip's cotangent is g) and gW = gz h^H."""
+
+    @staticmethod
+    def forward(ctx, h, W, C1, tap0, tap1, fuse_act, skip):
+        F_in, B, T = h.shape
+        z = (W @ h.reshape(F_in, B * T)).reshape(W.shape[0], B, T)
+        out, saved = ops._fbt_forward(C1, tap0, tap1, z, bool(fuse_act), h if skip else None)
+        ctx.save_for_backward(h, W, *saved)
+        ctx.fuse_act, ctx.skip = bool(fuse_act), bool(skip)
+        return out
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, g):
+        h, W, *saved = ctx.saved_tensors
+        gc1, gt0, gt1, gz = ops._fbt_backward(saved, g, ctx.fuse_act)
+        F_in, B, T = h.shape
+        F_out = W.shape[0]
+        gz2 = gz.reshape(F_out, B * T)
+        need = ctx.needs_input_grad
+        gh = None
+        if need[0]:
+            if ctx.skip:
+                gh = torch.addmm(ops._c64(g).reshape(F_in, B * T), W.mH, gz2).reshape(F_in, B, T)
+            else:
+                gh = (W.mH @ gz2).reshape(F_in, B, T)
+        gW = gz2 @ h.reshape(F_in, B * T).mH if need[1] else None
+        return gh, gW, gc1, gt0, gt1, None, None
+
+
 class PureRQFEncoderB200(nn.Module):
     """Pure RQF encoder in (F,B,T) layout on the B200 scan kernels.
 
@@ -160,13 +195,12 @@ class PureRQFEncoderB200(nn.Module):
             act = self.final_activation or i + 1 < n
             c1, t0, t1 = self.rqf[i].two_tap()
             W = self.W[i]
+            skip = self.skip and W.shape[0] == W.shape[1]
             if self.scan_grad_mode == "tbptt1":
                 out = _TBPTTLayer.apply(h, W, c1, t0, t1, act)
+                h = out + h if skip else out
             else:
-                z = (W @ h.reshape(W.shape[1], B * T)).reshape(W.shape[0], B, T)
-                out = (ops.fbt_recompute_scan(c1, t0, t1, z) if act
-                       else ops.fbt_prospective_scan(c1, t0, t1, z, False))
-            h = out + h if (self.skip and out.shape == h.shape) else out
+                h = _PureBlock.apply(h, W, c1, t0, t1, act, skip)
         return h
 
     @torch.no_grad()

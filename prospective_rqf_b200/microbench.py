@@ -1,0 +1,164 @@
+"""Op-level timing of the scan kernels: one forward and one backward of a
+public op per iteration on seeded synthetic inputs, each C-ABI call timed with
+CUDA events on its launching stream, reported as milliseconds per launch and
+achieved algorithmic bandwidth against the measured HBM copy peak.
+
+    python -m prospective_rqf_b200.microbench --op fbt --F 256 --B 32 --T 16000
+
+Ops:
+  fbt        fbt_recompute_scan (split-ReLU fused), (F,B,T)
+  fbt_raw    fbt_prospective_scan without activation, (F,B,T)
+  fbt_skip   the Pure RQF block scan: split-ReLU output plus the fused skip
+             input (rqf_fbt_block_forward) and its backward
+  tbptt_fbt  tbptt1_two_tap_scan, (F,B,T), split-ReLU fused
+  tbptt_btf  tbptt1_two_tap_scan, (B,T,F)
+  btf        _triton_chunked_scan, complex input, (B,T,F)
+  btf_real   _triton_chunked_scan, real input, (B,T,F)
+  btf_pro    _triton_chunked_scan_prospective, (B,T,F)
+  selective  selective_forward + selective_backward with every controller on
+             (--groups warp groups, --truncated for the TBPTT(1) variant)
+
+Every tensor is at least --T x --B x --F complex64; the shapes used for the
+committed figures exceed the 126 MB L2, so the timings read HBM.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+from pathlib import Path
+
+import torch
+
+FALLBACK_HBM_GBS = 6650.0
+
+
+def hbm_peak() -> tuple[float, str]:
+    """(GB/s, "measured" | "fallback"): the STREAM-style copy bandwidth of this
+    pool's B200s if MEASURED_PEAKS.json sits beside the package."""
+    p = Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (ValueError, KeyError):
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def _coeffs(F, dev, g):
+    mag = 0.9 + 0.0999 * torch.rand(F, generator=g)
+    lam = torch.polar(mag, 2 * math.pi * torch.rand(F, generator=g)).to(torch.complex64)
+    t0 = (0.3 * torch.randn(F, dtype=torch.complex64, generator=g))
+    t1 = (0.3 * torch.randn(F, dtype=torch.complex64, generator=g))
+    return lam.to(dev), t0.to(dev), t1.to(dev)
+
+
+def make_case(op: str, F: int, B: int, T: int, groups: int = 8, truncated: bool = False):
+    """Returns run() performing one forward + backward of `op`."""
+    import prospective_rqf_b200 as rqf
+    from . import ops
+
+    dev = torch.device("cuda")
+    g = torch.Generator().manual_seed(0)
+    c1, t0, t1 = _coeffs(F, dev, g)
+
+    def crandn(*shape):
+        return torch.randn(*shape, dtype=torch.complex64, generator=g).to(dev)
+
+    if op == "selective":
+        G = groups
+        theta = (0.05 + 2 * torch.rand(F, generator=g)).to(dev)
+        inputs = (torch.randn(F, B, T, generator=g).to(dev), torch.randn(G, B, T, generator=g).to(dev),
+                  torch.randn(F, B, T, generator=g).to(dev), torch.randn(F, generator=g).to(dev),
+                  theta, torch.randint(0, G, (F,), generator=g).to(dev),
+                  torch.full((F,), 1e-6, device=dev), torch.full((F,), 1 - 2e-6, device=dev),
+                  torch.full((F,), 0.2, device=dev), torch.ones(F, device=dev), theta * 0.4,
+                  theta * 1.6,
+                  (True, True, True, False, 0.223, 0.223, True, False, True, 2.0, 0.0, True))
+        z = crandn(F, B, T)
+        gy, gx = crandn(F, B, T), crandn(F, B, T)
+
+        def run():
+            _, _, ent = rqf.selective_forward(z, inputs, True, True, None)
+            rqf.selective_backward(z, inputs, ent, gy, gx, True, truncated, None)
+        return run
+
+    if op == "fbt_skip":
+        z, h, gy = crandn(F, B, T), crandn(F, B, T), crandn(F, B, T)
+
+        def run():
+            out, saved = ops._fbt_forward(c1, t0, t1, z, True, h)
+            ops._fbt_backward(saved, gy, True)
+        return run
+
+    fbt = op in ("fbt", "fbt_raw", "tbptt_fbt")
+    shape = (F, B, T) if fbt else (B, T, F)
+    if op == "btf_real":
+        u = torch.randn(*shape, generator=g).to(dev)
+    else:
+        u = crandn(*shape)
+    u.requires_grad_(True)
+    gy = crandn(*shape)
+    fwd = {
+        "fbt": lambda: rqf.fbt_recompute_scan(c1, t0, t1, u),
+        "fbt_raw": lambda: rqf.fbt_prospective_scan(c1, t0, t1, u, False),
+        "tbptt_fbt": lambda: rqf.tbptt1_two_tap_scan(u, c1, t0, t1, layout="fbt", fuse_act=True),
+        "tbptt_btf": lambda: rqf.tbptt1_two_tap_scan(u, c1, t0, t1, layout="btf"),
+        "btf": lambda: rqf._triton_chunked_scan(c1, t0, u),
+        "btf_real": lambda: rqf._triton_chunked_scan(c1, t0, u),
+        "btf_pro": lambda: rqf._triton_chunked_scan_prospective(c1, t0, t1, u),
+    }[op]
+
+    def run():
+        y = fwd()
+        torch.autograd.grad(y, (u,), gy)
+    return run
+
+
+OPS = ("fbt", "fbt_raw", "fbt_skip", "tbptt_fbt", "tbptt_btf", "btf", "btf_real", "btf_pro",
+       "selective")
+
+
+def measure(op, F, B, T, iters=10, warmup=3, groups=8, truncated=False) -> dict:
+    import prospective_rqf_b200 as rqf
+    from . import _timing
+
+    run = make_case(op, F, B, T, groups, truncated)
+    for _ in range(warmup):
+        run()
+    torch.cuda.synchronize()
+    with _timing.KernelTimer() as tm:
+        for _ in range(iters):
+            run()
+    s = tm.summary()
+    rqf.check_device_errors()
+    peak, kind = hbm_peak()
+    kernels = {}
+    for name, v in s.items():
+        per = v["alg_bytes"] / max(v["launches"], 1)
+        gbs = per / (v["mean_ms"] * 1e-3) / 1e9 if v["mean_ms"] else 0.0
+        kernels[name] = {"launches": v["launches"], "mean_ms": round(v["mean_ms"], 4),
+                         "alg_bytes_per_launch": int(per), "gbs": round(gbs, 1),
+                         "frac": round(gbs / peak, 4)}
+    return {"op": op, "F": F, "B": B, "T": T, "iters": iters, "warmup": warmup,
+            "peak_gbs": peak, "peak_kind": kind, "kernels": kernels}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--op", choices=OPS, default="fbt")
+    ap.add_argument("--F", type=int, default=256)
+    ap.add_argument("--B", type=int, default=32)
+    ap.add_argument("--T", type=int, default=16000)
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--groups", type=int, default=8)
+    ap.add_argument("--truncated", action="store_true")
+    a = ap.parse_args(argv)
+    print(json.dumps(measure(a.op, a.F, a.B, a.T, a.iters, a.warmup, a.groups, a.truncated)),
+          flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -90,6 +90,11 @@ def _done(device) -> None:
         _abi.check_device_errors(device)
 
 
+def _nbytes(*tensors) -> int:
+    """Algorithmic bytes of one launch: each large operand read or written once."""
+    return sum(t.numel() * t.element_size() for t in tensors if t is not None)
+
+
 def _shape3(x: torch.Tensor, what: str):
     if x.dim() != 3:
         raise ValueError(f"{what} must be 3-D, got shape {tuple(x.shape)}")
@@ -113,7 +118,7 @@ class _ChunkedScanFunction(torch.autograd.Function):
         y = torch.empty((B, T, F), dtype=torch.complex64, device=dev)
         carries = _carries(lib.rqf_btf_carry_count(B, T, F), dev)
         scratch = _scratch(lib.rqf_btf_scratch_bytes(B, T, F), dev)
-        with _timing.launch("rqf_chunked_scan_forward", B * T * F):
+        with _timing.launch("rqf_chunked_scan_forward", B * T * F, _nbytes(uu, y)):
             _abi.check(lib.rqf_chunked_scan_forward(
                 _abi.ptr(c1), _abi.ptr(c2), _abi.ptr(uu), int(real), _abi.ptr(y), _abi.ptr(carries),
                 _abi.ptr(scratch), B, T, F, _abi.stream_of(uu)), "rqf_chunked_scan_forward")
@@ -134,7 +139,7 @@ class _ChunkedScanFunction(torch.autograd.Function):
         gc1 = torch.empty_like(c1)
         gc2 = torch.empty_like(c2)
         scratch = _scratch(lib.rqf_btf_scratch_bytes(B, T, F), dev)
-        with _timing.launch("rqf_chunked_scan_backward", B * T * F):
+        with _timing.launch("rqf_chunked_scan_backward", B * T * F, _nbytes(uu, gy, gu)):
             _abi.check(lib.rqf_chunked_scan_backward(
                 _abi.ptr(c1), _abi.ptr(c2), _abi.ptr(uu), int(ctx.real), _abi.ptr(carries),
                 _abi.ptr(gy), _abi.ptr(gu), _abi.ptr(gc1), _abi.ptr(gc2), _abi.ptr(scratch),
@@ -166,7 +171,7 @@ class _ChunkedProspectiveScanFunction(torch.autograd.Function):
         y = torch.empty((B, T, F), dtype=torch.complex64, device=dev)
         carries = _carries(lib.rqf_btf_carry_count(B, T, F), dev)
         scratch = _scratch(lib.rqf_btf_scratch_bytes(B, T, F), dev)
-        with _timing.launch("rqf_chunked_prospective_forward", B * T * F):
+        with _timing.launch("rqf_chunked_prospective_forward", B * T * F, _nbytes(xx, y)):
             _abi.check(lib.rqf_chunked_prospective_forward(
                 _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1), _abi.ptr(xx), _abi.ptr(y), _abi.ptr(carries),
                 _abi.ptr(scratch), B, T, F, _abi.stream_of(xx)), "rqf_chunked_prospective_forward")
@@ -185,7 +190,7 @@ class _ChunkedProspectiveScanFunction(torch.autograd.Function):
         gx = torch.empty_like(xx)
         gc1, gt0, gt1 = torch.empty_like(c1), torch.empty_like(t0), torch.empty_like(t1)
         scratch = _scratch(lib.rqf_btf_scratch_bytes(B, T, F), dev)
-        with _timing.launch("rqf_chunked_prospective_backward", B * T * F):
+        with _timing.launch("rqf_chunked_prospective_backward", B * T * F, _nbytes(xx, gy, gx)):
             _abi.check(lib.rqf_chunked_prospective_backward(
                 _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1), _abi.ptr(xx), _abi.ptr(carries),
                 _abi.ptr(gy), _abi.ptr(gx), _abi.ptr(gc1), _abi.ptr(gt0), _abi.ptr(gt1),
@@ -203,20 +208,27 @@ def _triton_chunked_scan_prospective(C1, tap0, tap1, x):
 
 
 # ------------------------------------------------ (F,B,T) two-tap scan
-def _fbt_forward(C1, tap0, tap1, x_fbt, fuse_act: bool):
-    dev = _require_cuda(C1, tap0, tap1, x_fbt)
+def _fbt_forward(C1, tap0, tap1, x_fbt, fuse_act: bool, skip=None):
+    """(F,B,T) two-tap scan; with `skip`, returns act(y) + skip (fused)."""
+    dev = _require_cuda(C1, tap0, tap1, x_fbt, skip)
     z = _c64(x_fbt)
     F, B, T = _shape3(z, "x_fbt")
     c1, t0, t1 = _coef(C1, F, "C1"), _coef(tap0, F, "tap0"), _coef(tap1, F, "tap1")
+    sk = None
+    if skip is not None:
+        sk = _c64(skip)
+        if sk.shape != z.shape:
+            raise ValueError(f"skip must have shape {tuple(z.shape)}, got {tuple(sk.shape)}")
     lib = _abi.load()
     out = torch.empty((F, B, T), dtype=torch.complex64, device=dev)
     carries = _carries(lib.rqf_fbt_carry_count(F, B, T), dev)
     scratch = _scratch(lib.rqf_fbt_scratch_bytes(F, B, T), dev)
-    with _timing.launch("rqf_fbt_prospective_forward", B * T * F):
-        _abi.check(lib.rqf_fbt_prospective_forward(
-            _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1), _abi.ptr(z), _abi.ptr(out), _abi.ptr(carries),
-            _abi.ptr(scratch), F, B, T, int(bool(fuse_act)), _abi.stream_of(z)),
-            "rqf_fbt_prospective_forward")
+    name = "rqf_fbt_prospective_forward" if sk is None else "rqf_fbt_block_forward"
+    with _timing.launch(name, B * T * F, _nbytes(z, sk, out)):
+        _abi.check(lib.rqf_fbt_block_forward(
+            _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1), _abi.ptr(z), _abi.ptr(sk), _abi.ptr(out),
+            _abi.ptr(carries), _abi.ptr(scratch), F, B, T, int(bool(fuse_act)),
+            _abi.stream_of(z)), "rqf_fbt_block_forward")
     _done(dev)
     return out, (c1, t0, t1, z, carries)
 
@@ -230,7 +242,7 @@ def _fbt_backward(saved, grad_output, fuse_act: bool):
     gz = torch.empty_like(z)
     gc1, gt0, gt1 = torch.empty_like(c1), torch.empty_like(t0), torch.empty_like(t1)
     scratch = _scratch(lib.rqf_fbt_scratch_bytes(F, B, T), dev)
-    with _timing.launch("rqf_fbt_prospective_backward", B * T * F):
+    with _timing.launch("rqf_fbt_prospective_backward", B * T * F, _nbytes(z, gy, gz)):
         _abi.check(lib.rqf_fbt_prospective_backward(
             _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1), _abi.ptr(z), _abi.ptr(carries), _abi.ptr(gy),
             _abi.ptr(gz), _abi.ptr(gc1), _abi.ptr(gt0), _abi.ptr(gt1), _abi.ptr(scratch), F, B, T,
@@ -323,7 +335,7 @@ class _TBPTT1TwoTap(torch.autograd.Function):
             out = torch.empty((B, T, F), dtype=torch.complex64, device=dev)
             carries = _carries(lib.rqf_btf_carry_count(B, T, F), dev)
             scratch = _scratch(lib.rqf_btf_scratch_bytes(B, T, F), dev)
-            with _timing.launch("rqf_chunked_prospective_forward", B * T * F):
+            with _timing.launch("rqf_chunked_prospective_forward", B * T * F, _nbytes(z, out)):
                 _abi.check(lib.rqf_chunked_prospective_forward(
                     _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1), _abi.ptr(z), _abi.ptr(out),
                     _abi.ptr(carries), _abi.ptr(scratch), B, T, F, _abi.stream_of(z)),
@@ -363,7 +375,7 @@ def _tbptt_backward(saved, layout, dims, grad_output, fuse_act):
         scratch = _scratch(lib.rqf_fbt_scratch_bytes(d0, d1, d2), dev)
     else:
         scratch = _scratch(lib.rqf_btf_scratch_bytes(d0, d1, d2), dev)
-    with _timing.launch("rqf_tbptt1_two_tap_backward", d0 * d1 * d2):
+    with _timing.launch("rqf_tbptt1_two_tap_backward", d0 * d1 * d2, _nbytes(z, gy, gz, gzw)):
         _abi.check(lib.rqf_tbptt1_two_tap_backward(
             0 if layout == "btf" else 1, _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1),
             _abi.ptr(z), _abi.ptr(carries), _abi.ptr(gy), _abi.ptr(gz), _abi.ptr(gzw),
@@ -483,7 +495,8 @@ def selective_forward(z, inputs, activate, write_raw, chunk=None):
     act = torch.empty_like(zz) if activate else None
     entries = torch.empty((F * B, max(int(lib.rqf_selective_num_tiles(T)), 1)),
                           dtype=torch.complex64, device=dev)
-    with _timing.launch("rqf_selective_forward", F * B * T):
+    nb = _nbytes(zz, keep["gamma_logits"], keep["warp_logits"], keep["write_logits"], raw, act)
+    with _timing.launch("rqf_selective_forward", F * B * T, nb):
         _abi.check(lib.rqf_selective_forward(
             _abi.ptr(zz), ctypes.byref(sin), ctypes.byref(sopt), _abi.ptr(raw), _abi.ptr(act),
             _abi.ptr(entries), F, B, T, _abi.stream_of(zz)), "rqf_selective_forward")
@@ -512,7 +525,9 @@ def selective_backward(z, inputs, entries, gy, gx, activate, truncated, chunk=No
     dbias = torch.empty(F, dtype=torch.float32, device=dev)
     dtheta = torch.empty(F, dtype=torch.float32, device=dev)
     scratch = _scratch(lib.rqf_selective_scratch_bytes(F, B, T, int(bool(opt[1]))), dev)
-    with _timing.launch("rqf_selective_backward", F * B * T):
+    nb = _nbytes(zz, keep["gamma_logits"], keep["warp_logits"], keep["write_logits"], gyc, gxc,
+                 dz, dzw if truncated else None, dg, dd, dw)
+    with _timing.launch("rqf_selective_backward", F * B * T, nb):
         _abi.check(lib.rqf_selective_backward(
             _abi.ptr(zz), ctypes.byref(sin), ctypes.byref(sopt), _abi.ptr(entries),
             _abi.ptr(gyc), _abi.ptr(gxc), int(bool(truncated)), _abi.ptr(dz),

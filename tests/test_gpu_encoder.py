@@ -1,0 +1,215 @@
+"""Encoder-level parity: the B200 Pure RQF stack (prospective_rqf_b200.encoder —
+fused skip blocks, ZOH two-tap coefficients, TBPTT(1) layers, readout)
+against an fp64 CPU restatement of the same model whose scans run through the
+fp64 oracle, on identical parameters and inputs.  Mirrors the reference's
+FBT-vs-standard encoder check (tests/test_scan_backends_parity.py:109-162).
+Tolerances: outputs 1e-4, parameter and input gradients 1e-3."""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from _util import FWD_TOL, GRAD_TOL, assert_close
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _device():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    import prospective_rqf_b200 as rqf
+
+    rqf.read_device_error(clear=True)
+    yield
+    rqf.check_device_errors()
+
+
+def _np(t):
+    return t.detach().resolve_conj().numpy()
+
+
+class _OracleScan(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, c1, t0, t1, z, act):
+        y = oracle.two_tap_forward(_np(c1), _np(t0), _np(t1), _np(z), "fbt", fuse_act=act)
+        ctx.save_for_backward(c1, t0, t1, z)
+        ctx.act = act
+        return torch.from_numpy(y)
+
+    @staticmethod
+    def backward(ctx, g):
+        c1, t0, t1, z = ctx.saved_tensors
+        gz, gc1, gt0, gt1 = oracle.two_tap_backward(_np(c1), _np(t0), _np(t1), _np(z), _np(g),
+                                                    "fbt", fuse_act=ctx.act)
+        f = torch.from_numpy
+        return f(gc1), f(gt0), f(gt1), f(gz), None
+
+
+class _OracleTBPTT(torch.autograd.Function):
+    """TBPTT(1): exact forward; surrogate grads, lag cotangent to W only."""
+
+    @staticmethod
+    def forward(ctx, h, W, c1, t0, t1, act):
+        F_in, B, T = h.shape
+        z = (W.detach() @ h.detach().reshape(F_in, B * T)).reshape(-1, B, T)
+        y = oracle.two_tap_forward(_np(c1), _np(t0), _np(t1), _np(z), "fbt", fuse_act=act)
+        ctx.save_for_backward(h, W, c1, t0, t1, z)
+        ctx.act = act
+        return torch.from_numpy(y)
+
+    @staticmethod
+    def backward(ctx, g):
+        h, W, c1, t0, t1, z = ctx.saved_tensors
+        gz, gzw, gc1, gt0, gt1 = oracle.tbptt_backward(_np(c1), _np(t0), _np(t1), _np(z),
+                                                       _np(g), "fbt", fuse_act=ctx.act)
+        gz, gzw = torch.from_numpy(gz), torch.from_numpy(gzw)
+        F_in, B, T = h.shape
+        gh = (W.mH @ gz.reshape(-1, B * T)).reshape(F_in, B, T)
+        gW = (gz + gzw).reshape(-1, B * T) @ h.reshape(F_in, B * T).mH
+        f = torch.from_numpy
+        return gh, gW, f(gc1), f(gt0), f(gt1), None
+
+
+def _two_tap(log_theta, log_gamma, dt, tau):
+    gamma, theta = log_gamma.exp(), log_theta.exp()
+    a = torch.complex(-gamma / tau, (theta / tau) * (1.0 - gamma)) * dt
+    c1 = torch.exp(a)
+    phi = torch.where(a.abs() < 1e-4, 1 + a / 2 + a ** 2 / 6 + a ** 3 / 24 + a ** 4 / 120,
+                      (torch.exp(a) - 1) / torch.where(a.abs() < 1e-4, torch.ones_like(a), a))
+    extra = gamma * c1
+    return c1, gamma * (dt / tau) * phi + extra, -extra
+
+
+def reference_forward(model, x, params):
+    enc = model.encoder
+    B, T, I = x.shape
+    h = (params["input_proj.weight"] @ x.permute(2, 0, 1).reshape(I, B * T)).reshape(-1, B, T)
+    h = h.to(torch.complex128)
+    n = len(enc.W)
+    for i in range(n):
+        r = enc.rqf[i]
+        c1, t0, t1 = _two_tap(params[f"rqf.{i}.log_theta"], params[f"rqf.{i}.log_gamma"], r.dt,
+                              r.tau)
+        W = params[f"W.{i}"]
+        act = enc.final_activation or i + 1 < n
+        skip = enc.skip and W.shape[0] == W.shape[1]
+        if enc.scan_grad_mode == "tbptt1":
+            out = _OracleTBPTT.apply(h, W, c1, t0, t1, act)
+        else:
+            z = (W @ h.reshape(W.shape[1], B * T)).reshape(W.shape[0], B, T)
+            out = _OracleScan.apply(c1, t0, t1, z, act)
+        h = out + h if skip else out
+    F = h.shape[0]
+    feats = torch.cat([h.real, h.imag], dim=0).reshape(2 * F, B * T)
+    hid = torch.relu(params["fc1.weight"] @ feats + params["fc1.bias"][:, None])
+    logits = (params["fc2.weight"] @ hid + params["fc2.bias"][:, None]).reshape(-1, B, T)
+    return logits.mean(dim=2).t()
+
+
+@pytest.mark.parametrize("mode,T", [("full", 3000), ("full", 1000), ("tbptt1", 2500)])
+def test_encoder_matches_fp64_restatement(mode, T):
+    from prospective_rqf_b200.train import StepConfig, build_model
+
+    torch.manual_seed(0)
+    cfg = StepConfig(batch=4, time=T, hidden=16, depth=3, num_classes=5, readout_hidden=32,
+                     scan_grad_mode=mode)
+    model = build_model(cfg, "cuda", seed=3)
+    # gamma spread over the recipe band so some poles are nearly undamped
+    with torch.no_grad():
+        for r in model.encoder.rqf:
+            r.log_gamma.copy_(torch.linspace(math.log(1e-3), math.log(0.9), 16))
+    g = torch.Generator().manual_seed(5)
+    x = (0.5 * torch.randn(cfg.batch, T, 1, generator=g)).clamp(-1, 1)
+    y = torch.randint(0, cfg.num_classes, (cfg.batch,), generator=g)
+
+    xg = x.cuda().requires_grad_(True)
+    loss = torch.nn.functional.cross_entropy(model(xg), y.cuda())
+    loss.backward()
+
+    names = {}
+    for name, p in model.named_parameters():
+        key = name.replace("encoder.", "").replace("readout.", "")
+        names[key] = p
+    params = {k: (p.detach().cpu().to(torch.complex128 if p.is_complex() else torch.float64)
+                  .requires_grad_(True)) for k, p in names.items()}
+    xr = x.double().requires_grad_(True)
+    logits_ref = reference_forward(model, xr, params)
+    loss_ref = torch.nn.functional.cross_entropy(logits_ref, y)
+    loss_ref.backward()
+
+    assert_close(model(x.cuda()).detach().cpu().double().numpy(), logits_ref.detach().numpy(),
+                 FWD_TOL, "logits")
+    assert abs(loss.item() - loss_ref.item()) <= FWD_TOL * max(1.0, abs(loss_ref.item()))
+    assert_close(xg.grad.cpu().double().numpy(), xr.grad.numpy(), GRAD_TOL, "grad x")
+    for k, p in names.items():
+        ref = params[k].grad
+        assert ref is not None, k
+        assert_close(p.grad.cpu().numpy().astype(np.complex128 if p.is_complex() else np.float64),
+                     ref.numpy(), GRAD_TOL, f"grad {k}")
+
+
+# ------------------------------------------- fused skip (rqf_fbt_block_forward)
+def _crandn(g, *shape):
+    return torch.randn(*shape, dtype=torch.complex64, generator=g)
+
+
+def _coef(g, F):
+    mag = 0.8 + 0.199 * torch.rand(F, generator=g)
+    lam = torch.polar(mag, 6.283 * torch.rand(F, generator=g)).to(torch.complex64)
+    return lam, 0.5 * _crandn(g, F), 0.5 * _crandn(g, F)
+
+
+# 15 rows take the look-back tile kernels; 640 rows (>= the resident CTAs of
+# every persistent forward kernel: 4 per SM x 148 without skip, 3 with) take
+# the row-sequential kernels.  Between those counts the plain and the skip
+# forward take different kernels, whose fp32 sums associate differently.
+@pytest.mark.parametrize("F,B,T", [(3, 5, 5001), (40, 16, 2050), (40, 16, 1)])
+@pytest.mark.parametrize("fuse", [True, False])
+def test_block_forward_fused_skip(F, B, T, fuse):
+    from prospective_rqf_b200 import ops
+
+    g = torch.Generator().manual_seed(F * 1000 + T + int(fuse))
+    c1, t0, t1 = (t.cuda() for t in _coef(g, F))
+    z, h = _crandn(g, F, B, T).cuda(), _crandn(g, F, B, T).cuda()
+    fused, saved = ops._fbt_forward(c1, t0, t1, z, fuse, h)
+    plain, _ = ops._fbt_forward(c1, t0, t1, z, fuse)
+    # same scan arithmetic, one fp32 add at the store: bit-identical
+    assert torch.equal(fused, plain + h)
+    ref = oracle.two_tap_forward(_np(c1.cpu()), _np(t0.cpu()), _np(t1.cpu()), _np(z.cpu()), "fbt",
+                                 fuse_act=fuse) + _np(h.cpu())
+    assert_close(_np(fused.cpu()), ref, FWD_TOL, "act(y) + skip")
+    assert saved[3].data_ptr() == z.data_ptr()  # the backward recomputes from z, not from out
+
+
+@pytest.mark.parametrize("F,B,T", [(4, 3, 3000), (40, 16, 2100)])
+@pytest.mark.parametrize("fuse,skip", [(True, True), (False, True), (True, False)])
+def test_pure_block_matches_unfused_composition(F, B, T, fuse, skip):
+    """_PureBlock (GEMM + fused scan/skip + one accumulating GEMM backward)
+    against W @ h -> fbt_prospective_scan -> + h composed by autograd."""
+    import prospective_rqf_b200 as rqf
+    from prospective_rqf_b200.encoder import _PureBlock
+
+    g = torch.Generator().manual_seed(F + B + T)
+    c1, t0, t1 = (t.cuda() for t in _coef(g, F))
+    W = (_crandn(g, F, F) / math.sqrt(2 * F)).cuda()
+    h = _crandn(g, F, B, T).cuda()
+    gy = _crandn(g, F, B, T).cuda()
+
+    leaves_a = [t.clone().requires_grad_(True) for t in (h, W, c1, t0, t1)]
+    out_a = _PureBlock.apply(*leaves_a, fuse, skip)
+    out_a.backward(gy)
+
+    leaves_b = [t.clone().requires_grad_(True) for t in (h, W, c1, t0, t1)]
+    hb, Wb, c1b, t0b, t1b = leaves_b
+    z = (Wb @ hb.reshape(F, B * T)).reshape(F, B, T)
+    out_b = rqf.fbt_prospective_scan(c1b, t0b, t1b, z, fuse)
+    if skip:
+        out_b = out_b + hb
+    out_b.backward(gy)
+
+    assert torch.equal(out_a, out_b)
+    for a, b, k in zip(leaves_a, leaves_b, ("h", "W", "c1", "tap0", "tap1")):
+        assert_close(_np(a.grad.cpu()), _np(b.grad.cpu()), 1e-5, f"grad {k}")
