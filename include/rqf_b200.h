@@ -55,7 +55,8 @@ enum rqf_status {
   RQF_ERR_LOOKBACK_TIMEOUT = 3, /* bounded cross-tile wait gave up          */
   RQF_ERR_LAUNCH = 4,           /* CUDA launch / memset error               */
   RQF_ERR_ARGUMENT = 5,         /* null pointer or unsupported option       */
-  RQF_ERR_CAPACITY = 6          /* size beyond a fixed internal maximum     */
+  RQF_ERR_CAPACITY = 6,         /* size beyond a fixed internal maximum     */
+  RQF_ERR_PIPELINE_TIMEOUT = 7  /* bounded tensor-core pipeline wait gave up */
 };
 
 /* ---- library information -------------------------------------------- */
@@ -255,6 +256,33 @@ int rqf_fbt_prospective_backward_noalloc(const float *c1, const float *tap0, con
                                          float *grad_tap0, float *grad_tap1, int64_t filters,
                                          int64_t batch, int64_t time, int fuse_act,
                                          rqf_stream_t stream);
+
+/* ---- complex projection GEMM of the Pure RQF block (tensor cores) ---- *
+ * Replaces the complex GEMM torch.matmul(W, h.reshape(d_model, batch*time))
+ * of rqf_models/backbones/rqf/pure.py:223 (PureRQFBlock._forward_fbt) and its
+ * input cotangent W^H gz (autograd of the same matmul; the reference runs both
+ * as cuBLAS fp32 complex GEMMs):
+ *
+ *   out[j, n] = sum_k op(W)[j, k] * x[k, n]  (+ acc[j, n])        complex64
+ *
+ * conj_transpose = 0: op(W) = W with W (m x k);  = 1: op(W) = W^H with W
+ * (k x m).  x is (k x n) with n contiguous ((F,B,T) activations, n = B*T);
+ * out and acc (nullable; may alias out) are (m x n).  Arithmetic: split TF32
+ * on the tensor cores (each fp32 operand split into two TF32 parts, three
+ * TF32 products per fp32 product, fp32 accumulation), fp32-comparable.
+ * Requirements: n even, x / out / acc 16-byte aligned, n < 2^30.
+ * `workspace` needs rqf_projection_workspace_bytes(m, k) bytes (16-byte
+ * aligned); it holds the split copy of op(W) and is free again when the
+ * launch completes.  The pipeline's waits are bounded: on expiry the kernel
+ * latches RQF_ERR_PIPELINE_TIMEOUT in the device error word. */
+size_t rqf_projection_workspace_bytes(int64_t m, int64_t k);
+/* Diagnostic: where the first expired wait of the projection pipeline gave
+ * up since the last clear (0 none, 1 producer, 2 transform, 3/4 MMA issuer,
+ * 5 epilogue, 6 shutdown drain); -1 on a CUDA error.  Synchronous. */
+int rqf_projection_timeout_site(int clear);
+int rqf_projection(const float *w, const float *x, const float *acc, float *out, int64_t m,
+                   int64_t k, int64_t n, int conj_transpose, void *workspace,
+                   rqf_stream_t stream);
 
 #ifdef __cplusplus
 }

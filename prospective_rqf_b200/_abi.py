@@ -77,6 +77,9 @@ SIGNATURES: dict[str, tuple] = {
                _i64, _p]),
     "rqf_tbptt1_two_tap_backward": (
         _int, [_int, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
+    "rqf_projection_workspace_bytes": (_sz, [_i64, _i64]),
+    "rqf_projection_timeout_site": (_int, [_int]),
+    "rqf_projection": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _int, _p, _p]),
 }
 
 _LIB = None

@@ -1,0 +1,517 @@
+// Complex projection GEMM of the Pure RQF block on the 5th-generation tensor
+// cores (tcgen05 + TMA + TMEM), in split TF32:
+//
+//   out[j, n] = sum_k op(W)[j, k] * X[k, n]   (+ acc[j, n])          complex64
+//
+// op(W) = W gives the block projection z = W h (rqf_models/backbones/rqf/
+// pure.py:223, a torch.matmul on the (d_model, batch*time) view); op(W) = W^H
+// gives its input cotangent W^H gz, and `acc` folds in the skip cotangent.
+// X is (K, N) with N contiguous: the (F,B,T) activations with N = B*T.
+//
+// Real formulation.  A' is the (2M x K) real matrix whose rows alternate
+// Re op(W)[j,:] and Im op(W)[j,:]; X' = view_as_real(X) is (K x 2N) with
+// columns alternating Re and Im.  P = A' X' holds the four real products of
+// each complex product, and
+//     Re out[j,n] = P[2j, 2n] - P[2j+1, 2n+1],   Im out[j,n] = P[2j, 2n+1] + P[2j+1, 2n].
+// Rows 2j and 2j+1 of a tile sit in adjacent TMEM lanes, i.e. adjacent
+// threads of one epilogue warp, which combine them with shuffles.
+//
+// Precision.  Every fp32 operand v is split as hi = rna_tf32(v),
+// lo = rna_tf32(v - hi), and the tile accumulates A_hi X_hi + A_hi X_lo +
+// A_lo X_hi in fp32: about 21 significant bits per operand against 11 for a
+// single TF32 product, i.e. fp32-comparable (the fp32 SIMT complex GEMM it
+// replaces keeps 24).  A' is split once per call by proj_prep_kernel; X' is
+// split in shared memory by four transform warps right after its TMA load,
+// so the activations cross HBM once.
+//
+// CTA (one per SM, persistent over output tiles of 128 A' rows x 256 X'
+// columns = 64 complex outputs x 128 samples):
+//   warp 0      TMA producer: A_hi, A_lo (K-major, 128-byte swizzle) and X'
+//               (MN-major, 128-byte swizzle of 32-byte atoms) stages
+//   warp 1      TMEM owner and MMA issuer (tcgen05.mma.cta_group::1.kind::tf32)
+//   warps 2..5  epilogue: TMEM -> registers, complex combine, (+acc), store
+//   warps 6..9  transform: X' stage -> hi (in place) and lo
+// Two smem stages of K = 32 and two TMEM accumulators (2 x 256 columns), so
+// the epilogue of one tile overlaps the MMAs of the next.  Every mbarrier wait
+// is bounded in time; on expiry the kernel latches RQF_ERR_PIPELINE_TIMEOUT,
+// every role stops, in-flight copies and MMAs are waited for (bounded) and
+// the TMEM is freed before exit.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "rqf_common.cuh"
+
+namespace rqf {
+namespace proj {
+
+constexpr int kBM = 128;              // A' rows per tile
+constexpr int kBN = 256;              // X' columns per tile
+constexpr int kBK = 32;               // K per stage: one 128-byte swizzle row of fp32
+constexpr int kUmmaK = 8;             // K of one tcgen05.mma kind::tf32
+constexpr int kStages = 2;
+constexpr int kAccBufs = 2;
+constexpr int kTmemCols = kBN * kAccBufs;  // 512: the whole TMEM of the SM
+constexpr int kThreads = 320;
+constexpr int kNBlocks = kBN / 32;    // 32-column (128-byte) blocks of an X' stage
+
+constexpr int kABytes = kBM * kBK * 4;            // 16 KB, one of A_hi / A_lo
+constexpr int kBBytes = kBK * kBN * 4;            // 32 KB, one of X_hi / X_lo
+constexpr int kStageBytes = 2 * kABytes + 2 * kBBytes;
+constexpr int kTxBytes = 2 * kABytes + kBBytes;   // bytes the TMA lands per stage
+constexpr int kBarBytes = 256;
+constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;  // + alignment slack
+
+constexpr int kErrPipelineTimeout = 7;            // RQF_ERR_PIPELINE_TIMEOUT
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
+
+// Where the first expired wait of the projection pipeline gave up (0 = none):
+// 1 producer/empty, 2 transform/full, 3 MMA/accumulator-drained, 4 MMA/ready,
+// 5 epilogue/accumulator-full, 6 shutdown drain.  Read by
+// rqf_projection_timeout_site().
+__device__ int g_proj_timeout_site;
+
+struct Params {
+  float2 *out;
+  const float2 *acc;   // may be null
+  long long M;         // complex output rows
+  long long N;         // complex samples
+  int K;               // complex reduction length
+  int m_tiles, n_tiles, k_blocks;
+  long long num_tiles;
+  int a_rows_pad;      // rows of the hi half of the split A' buffer
+};
+
+// ------------------------------------------------------------ PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase of `parity` to complete.  Returns false (and
+// raises the CTA's abort flag, latching the error once) when the time limit
+// passes or another role has already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
+                                          int site) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 31u) == 0u) {
+      if (*abort) return false;
+      if (global_ns() - t0 > kWaitLimitNs) {
+        latch_error(kErrPipelineTimeout);
+        atomicCAS(&g_proj_timeout_site, 0, site);
+        *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+// Wait used while shutting down: bounded, ignores the abort flag.
+__device__ __forceinline__ void mbar_drain(uint64_t *bar, uint32_t parity) {
+  const unsigned long long t0 = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_ns() - t0 > kWaitLimitNs) {
+      latch_error(kErrPipelineTimeout);
+      atomicCAS(&g_proj_timeout_site, 0, 6);
+      return;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tc_mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 32 lanes x 32 consecutive fp32 columns: thread i of the warp receives
+// columns [col, col+32) of TMEM lane (lane base + i).
+__device__ __forceinline__ void tc_ld_32x32b_x32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float tf32_rna(float v) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return __uint_as_float(r);
+}
+
+// Shared-memory matrix descriptor of tcgen05.mma: start, leading and stride
+// byte offsets in 16-byte units, descriptor version 1, swizzle mode.
+//   kSwizzle128B       (2): 16-byte chunks XOR-ed over 8 rows of 128 bytes —
+//                           the K-major A' tile (TMA CU_TENSOR_MAP_SWIZZLE_128B);
+//   kSwizzle128BBase32 (1): 32-byte chunks XOR-ed over 4 rows of 128 bytes —
+//                           what an MN-major 32-bit operand must use (the X'
+//                           tile; TMA CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B).
+constexpr uint64_t kSwizzle128B = 2, kSwizzle128BBase32 = 1;
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo,
+                                              uint64_t swizzle) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (swizzle << 61);
+}
+
+// Instruction descriptor: D fp32, A and B TF32, A K-major, B MN-major, M = 128, N = 256.
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (0u << 15) | (1u << 16) |
+                            ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+
+// ------------------------------------------------------------ weight split
+// A' rows alternate Re and Im of op(W)[j,:]; hi in rows [0, rows_pad), lo in
+// rows [rows_pad, 2 rows_pad) of a (2 rows_pad x k_pad) fp32 buffer, padding
+// zero.  op(W) = W for W (M x K); op(W) = W^H for W (K x M).
+__global__ void proj_prep_kernel(const float2 *__restrict__ W, float *__restrict__ a_split,
+                                 long long M, int K, int rows_pad, int k_pad, int conj_t) {
+  const long long total = (long long)rows_pad * k_pad;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / k_pad;
+    const int k = (int)(i - r * k_pad);
+    float v = 0.f;
+    if (r < 2 * M && k < K) {
+      const long long j = r >> 1;
+      if (!conj_t) {
+        const float2 w = W[j * K + k];
+        v = (r & 1) ? w.y : w.x;
+      } else {
+        const float2 w = W[(long long)k * M + j];
+        v = (r & 1) ? -w.y : w.x;
+      }
+    }
+    const float hi = tf32_rna(v);
+    a_split[i] = hi;
+    a_split[total + i] = tf32_rna(v - hi);
+  }
+}
+
+// ------------------------------------------------------------ main kernel
+__device__ __forceinline__ void tile_coords(long long tile, const Params &p, int &mt, int &nt) {
+  mt = (int)(tile % p.m_tiles);  // consecutive CTAs share an X' tile through L2
+  nt = (int)(tile / p.m_tiles);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmX,
+            const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
+  uint64_t *full = bars;                 // TMA landed            (1 arrival + tx)
+  uint64_t *ready = bars + kStages;      // X' split done         (4 transform warps)
+  uint64_t *empty = bars + 2 * kStages;  // MMAs done with stage  (tcgen05.commit)
+  uint64_t *accf = bars + 3 * kStages;   // accumulator complete  (tcgen05.commit)
+  uint64_t *acce = accf + kAccBufs;      // accumulator drained   (4 epilogue warps)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acce + kAccBufs);
+  volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&ready[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < kAccBufs; ++a) {
+      mbar_init(&accf[a], 1);
+      mbar_init(&acce[a], 4);
+    }
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmX);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (long long tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        int mt, nt;
+        tile_coords(tile, p, mt, nt);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort, 1)) {
+            ok = false;
+            break;
+          }
+          uint8_t *st = smem + stage * kStageBytes;
+          mbar_expect_tx(&full[stage], kTxBytes);
+          tma_load_2d(st, &tmA, &full[stage], kb * kBK, mt * kBM);
+          tma_load_2d(st + kABytes, &tmA, &full[stage], kb * kBK, p.a_rows_pad + mt * kBM);
+#pragma unroll
+          for (int i = 0; i < kNBlocks; ++i)
+            tma_load_2d(st + 2 * kABytes + i * (kBK * 128), &tmX, &full[stage],
+                        nt * kBN + i * 32, kb * kBK);
+          ++issued;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Wait for the copies still in flight (the last min(issued, kStages)).
+      for (int i = 0; i < kStages && i < issued; ++i) {
+        if (--stage < 0) {
+          stage = kStages - 1;
+          phase ^= 1u;
+        }
+        mbar_drain(&full[stage], phase);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      uint64_t *last = nullptr;
+      uint32_t last_parity = 0;
+      for (long long tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        if (!mbar_wait(&acce[acc], acc_phase ^ 1u, abort, 3)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kBN);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&ready[stage], phase, abort, 4)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = smem_u32(smem + stage * kStageBytes);
+          // A': K-major, 8-row groups 1024 B apart.  X': MN-major, 32-column
+          // (128-byte) blocks kBK*128 B apart (LBO), 4-row groups 512 B apart (SBO).
+          const uint64_t a_hi = smem_desc(st, 16, 1024, kSwizzle128B);
+          const uint64_t a_lo = smem_desc(st + kABytes, 16, 1024, kSwizzle128B);
+          const uint64_t b_hi = smem_desc(st + 2 * kABytes, kBK * 128, 512, kSwizzle128BBase32);
+          const uint64_t b_lo =
+              smem_desc(st + 2 * kABytes + kBBytes, kBK * 128, 512, kSwizzle128BBase32);
+#pragma unroll
+          for (int ks = 0; ks < kBK / kUmmaK; ++ks) {
+            // A advances 32 bytes along K inside its swizzle row; X' advances
+            // 8 rows (1024 bytes) per K step.
+            const uint64_t da = (uint64_t)(ks * (kUmmaK * 4) >> 4);
+            const uint64_t db = (uint64_t)(ks * (kUmmaK * 128) >> 4);
+            const uint32_t accum = (kb > 0 || ks > 0) ? 1u : 0u;
+            tc_mma_tf32(d_tmem, a_hi + da, b_hi + db, kIdesc, accum);
+            tc_mma_tf32(d_tmem, a_hi + da, b_lo + db, kIdesc, 1u);
+            tc_mma_tf32(d_tmem, a_lo + da, b_hi + db, kIdesc, 1u);
+          }
+          tc_commit(&empty[stage]);
+          last = &empty[stage];
+          last_parity = phase;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&accf[acc]);
+        if (++acc == kAccBufs) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // The MMAs read shared memory and write TMEM asynchronously: the last
+      // commit must land before the CTA frees either.
+      if (last != nullptr) mbar_drain(last, last_parity);
+    }
+  } else if (warp < 6) {
+    // ---------------------------------------------------------- epilogue
+    const int quarter = warp & 3;          // TMEM lanes this warp may read
+    const int row = quarter * 32 + lane;   // A' row within the tile
+    const bool odd = (row & 1) != 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (long long tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+      // every lane waits; the decision is made warp-uniform before the
+      // .sync.aligned TMEM loads
+      const bool ok = mbar_wait(&accf[acc], acc_phase, abort, 5);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      int mt, nt;
+      tile_coords(tile, p, mt, nt);
+      const long long j = (long long)mt * (kBM / 2) + (row >> 1);
+      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kBN);
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        float v[32];
+        tc_ld_32x32b_x32(tbase + (uint32_t)(c * 32), v);
+        float r[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) r[i] = __shfl_xor_sync(0xffffffffu, odd ? v[i] : v[16 + i], 1);
+        float2 z[8];
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+          const float pr_re = odd ? r[2 * s] : v[2 * s];
+          const float pr_im = odd ? r[2 * s + 1] : v[2 * s + 1];
+          const float pi_re = odd ? v[16 + 2 * s] : r[2 * s];
+          const float pi_im = odd ? v[16 + 2 * s + 1] : r[2 * s + 1];
+          z[s] = make_float2(pr_re - pi_im, pr_im + pi_re);
+        }
+        const long long n0 = (long long)nt * (kBN / 2) + c * 16 + (odd ? 8 : 0);
+        if (j < p.M && n0 < p.N) {
+          float2 *dst = p.out + j * p.N + n0;
+          const float2 *src = p.acc ? p.acc + j * p.N + n0 : nullptr;
+          if (n0 + 8 <= p.N) {
+            if (src) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float4 a = reinterpret_cast<const float4 *>(src)[q];
+                z[2 * q] = make_float2(z[2 * q].x + a.x, z[2 * q].y + a.y);
+                z[2 * q + 1] = make_float2(z[2 * q + 1].x + a.z, z[2 * q + 1].y + a.w);
+              }
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              reinterpret_cast<float4 *>(dst)[q] =
+                  make_float4(z[2 * q].x, z[2 * q].y, z[2 * q + 1].x, z[2 * q + 1].y);
+          } else {
+#pragma unroll
+            for (int s = 0; s < 8; ++s) {
+              if (n0 + s < p.N) {
+                float2 o = z[s];
+                if (src) o = make_float2(o.x + src[s].x, o.y + src[s].y);
+                dst[s] = o;
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce[acc]);
+      if (++acc == kAccBufs) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  } else {
+    // ---------------------------------------------------------- transform
+    const int t = threadIdx.x - 6 * 32;  // 0..127
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (long long tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&full[stage], phase, abort, 2));
+        if (!ok) break;
+        float4 *xb = reinterpret_cast<float4 *>(smem + stage * kStageBytes + 2 * kABytes);
+        float4 *xl = reinterpret_cast<float4 *>(smem + stage * kStageBytes + 2 * kABytes + kBBytes);
+#pragma unroll 4
+        for (int i = t; i < kBBytes / 16; i += 128) {
+          const float4 v = xb[i];
+          float4 h, l;
+          h.x = tf32_rna(v.x); l.x = tf32_rna(v.x - h.x);
+          h.y = tf32_rna(v.y); l.y = tf32_rna(v.y - h.y);
+          h.z = tf32_rna(v.z); l.z = tf32_rna(v.z - h.z);
+          h.w = tf32_rna(v.w); l.w = tf32_rna(v.w - h.w);
+          xb[i] = h;
+          xl[i] = l;
+        }
+        // generic-proxy smem writes -> visible to the tensor core (async proxy)
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ready[stage]);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  }
+
+  __syncwarp();  // lanes of warps 0 and 1 wait for their elected lane's loop
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+}  // namespace proj
+}  // namespace rqf

@@ -3,14 +3,19 @@
 // The entry points validate sizes and alignment, clear the look-back part of
 // the caller's scratch with cudaMemsetAsync, pick the kernel instantiation and
 // launch on the caller's stream.  Nothing here allocates device memory.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <mutex>
 
 #include "../../include/rqf_b200.h"
 #include "btf_scan.cuh"
 #include "fbt_rows.cuh"
 #include "fbt_scan.cuh"
 #include "reduce.cuh"
+#include "projection.cuh"
 #include "selective.cuh"
 
 using namespace rqf;
@@ -253,6 +258,8 @@ const char *rqf_status_string(int status) {
       return "null pointer or unsupported option";
     case RQF_ERR_CAPACITY:
       return "size exceeds the fixed internal maximum";
+    case RQF_ERR_PIPELINE_TIMEOUT:
+      return "tensor-core pipeline wait timed out";
     default:
       return "unknown status";
   }
@@ -685,3 +692,144 @@ int rqf_selective_backward(const float *z, const rqf_selective_inputs *inputs,
 }  // extern "C"
 
 #include "noalloc.cuh"
+
+// ------------------------------------------------ complex projection GEMM
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D fp32 tensor map: `inner` contiguous elements per row, `outer` rows
+// `row_bytes` apart; out-of-range elements load as zero.
+bool encode_map_2d(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer,
+                   uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                   CUtensorMapSwizzle swizzle) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = tensor_map_encoder();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t elem[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims, strides, box,
+            elem, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct ProjGeometry {
+  int64_t rows_pad, k_pad;
+};
+
+inline ProjGeometry proj_geometry(int64_t m, int64_t k) {
+  ProjGeometry g;
+  g.rows_pad = ceil_div(2 * m, proj::kBM) * proj::kBM;
+  g.k_pad = ceil_div(k, proj::kBK) * proj::kBK;
+  return g;
+}
+
+int proj_ctas_per_device() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  static std::mutex mu;
+  static bool configured[64] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(proj::proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             proj::kSmemBytes) != cudaSuccess)
+      return 0;
+    configured[dev] = true;
+  }
+  return sms;
+}
+
+}  // namespace
+
+extern "C" {
+
+int rqf_projection_timeout_site(int clear) {
+  int site = 0;
+  if (cudaMemcpyFromSymbol(&site, proj::g_proj_timeout_site, sizeof(int)) != cudaSuccess) return -1;
+  if (clear) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(proj::g_proj_timeout_site, &zero, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return site;
+}
+
+size_t rqf_projection_workspace_bytes(int64_t m, int64_t k) {
+  if (m <= 0 || k <= 0) return 0;
+  const ProjGeometry g = proj_geometry(m, k);
+  return (size_t)(2 * g.rows_pad * g.k_pad) * sizeof(float);
+}
+
+int rqf_projection(const float *w, const float *x, const float *acc, float *out, int64_t m,
+                   int64_t k, int64_t n, int conj_transpose, void *workspace,
+                   rqf_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (m < 0 || k < 0 || n < 0) return RQF_ERR_SHAPE;
+  if (m == 0 || n == 0) return RQF_OK;
+  if (out == nullptr || (k > 0 && (w == nullptr || x == nullptr || workspace == nullptr)))
+    return RQF_ERR_ARGUMENT;
+  const size_t out_bytes = (size_t)m * (size_t)n * sizeof(float2);
+  if (k == 0) {  // empty sum
+    const cudaError_t e = acc ? (acc == out ? cudaSuccess
+                                            : cudaMemcpyAsync(out, acc, out_bytes,
+                                                              cudaMemcpyDeviceToDevice, st))
+                              : cudaMemsetAsync(out, 0, out_bytes, st);
+    return e == cudaSuccess ? RQF_OK : RQF_ERR_LAUNCH;
+  }
+  // TMA: the X' row pitch (8n bytes) must be a multiple of 16, coordinates are int32.
+  if ((n & 1) != 0 || n >= (int64_t(1) << 30) || k > 0x7fffffffLL || m > (int64_t(1) << 40))
+    return RQF_ERR_SHAPE;
+  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(workspace, 16) ||
+      (acc != nullptr && !aligned(acc, 16)))
+    return RQF_ERR_ALIGN;
+  const ProjGeometry g = proj_geometry(m, k);
+  if (g.rows_pad > 0x3fffffffLL || g.k_pad > 0x7fffffffLL) return RQF_ERR_SHAPE;
+  const int sms = proj_ctas_per_device();
+  if (sms <= 0) return RQF_ERR_LAUNCH;
+
+  float *a_split = static_cast<float *>(workspace);
+  {
+    const int64_t total = g.rows_pad * g.k_pad;
+    const int64_t blocks = ceil_div(total, 256);
+    proj::proj_prep_kernel<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, st>>>(
+        reinterpret_cast<const float2 *>(w), a_split, m, (int)k, (int)g.rows_pad, (int)g.k_pad,
+        conj_transpose ? 1 : 0);
+    if (cudaGetLastError() != cudaSuccess) return RQF_ERR_LAUNCH;
+  }
+  CUtensorMap tmA, tmX;
+  if (!encode_map_2d(&tmA, a_split, (uint64_t)g.k_pad, (uint64_t)(2 * g.rows_pad),
+                     (uint64_t)g.k_pad * sizeof(float), proj::kBK, proj::kBM,
+                     CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map_2d(&tmX, x, (uint64_t)(2 * n), (uint64_t)k, (uint64_t)(2 * n) * sizeof(float),
+                     32, proj::kBK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
+    return RQF_ERR_LAUNCH;
+
+  proj::Params p;
+  p.out = reinterpret_cast<float2 *>(out);
+  p.acc = reinterpret_cast<const float2 *>(acc);
+  p.M = m;
+  p.N = n;
+  p.K = (int)k;
+  p.m_tiles = (int)(g.rows_pad / proj::kBM);
+  p.n_tiles = (int)ceil_div(2 * n, proj::kBN);
+  p.k_blocks = (int)(g.k_pad / proj::kBK);
+  p.num_tiles = (long long)p.m_tiles * p.n_tiles;
+  p.a_rows_pad = (int)g.rows_pad;
+  const long long grid = p.num_tiles < sms ? p.num_tiles : sms;
+  proj::proj_kernel<<<(unsigned)grid, proj::kThreads, proj::kSmemBytes, st>>>(tmA, tmX, p);
+  return launch_status();
+}
+
+}  // extern "C"

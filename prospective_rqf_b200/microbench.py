@@ -17,6 +17,10 @@ Ops:
   btf_pro    _triton_chunked_scan_prospective, (B,T,F)
   selective  selective_forward + selective_backward with every controller on
              (--groups warp groups, --truncated for the TBPTT(1) variant)
+  projection the block projection z = W h and its input cotangent W^H gz + g
+             (split-TF32 tcgen05 GEMM, W of F x F complex); reports TFLOP/s
+             (8 F^2 B T real flops per GEMM) beside the bandwidth
+  projection_torch  the same two GEMMs through torch.matmul (cuBLAS fp32)
 
 Every tensor is at least --T x --B x --F complex64; the shapes used for the
 committed figures exceed the 126 MB L2, so the timings read HBM.
@@ -84,6 +88,24 @@ def make_case(op: str, F: int, B: int, T: int, groups: int = 8, truncated: bool 
             rqf.selective_backward(z, inputs, ent, gy, gx, True, truncated, None)
         return run
 
+    if op in ("projection", "projection_torch"):
+        W = (crandn(F, F) / math.sqrt(2 * F))
+        h, gz, gh = crandn(F, B, T), crandn(F, B, T), crandn(F, B, T)
+
+        if op == "projection":
+            def run():
+                ops.projection(W, h)
+                ops.projection(W, gz, True, gh)
+        else:
+            from . import _timing
+
+            def run():
+                with _timing.launch("torch_matmul", F * B * T, 16 * F * B * T):
+                    W @ h.reshape(F, B * T)
+                with _timing.launch("torch_matmul_h", F * B * T, 24 * F * B * T):
+                    torch.addmm(gh.reshape(F, B * T), W.mH, gz.reshape(F, B * T))
+        return run
+
     if op == "fbt_skip":
         z, h, gy = crandn(F, B, T), crandn(F, B, T), crandn(F, B, T)
 
@@ -117,7 +139,7 @@ def make_case(op: str, F: int, B: int, T: int, groups: int = 8, truncated: bool 
 
 
 OPS = ("fbt", "fbt_raw", "fbt_skip", "tbptt_fbt", "tbptt_btf", "btf", "btf_real", "btf_pro",
-       "selective")
+       "selective", "projection", "projection_torch")
 
 
 def measure(op, F, B, T, iters=10, warmup=3, groups=8, truncated=False) -> dict:
@@ -141,6 +163,9 @@ def measure(op, F, B, T, iters=10, warmup=3, groups=8, truncated=False) -> dict:
         kernels[name] = {"launches": v["launches"], "mean_ms": round(v["mean_ms"], 4),
                          "alg_bytes_per_launch": int(per), "gbs": round(gbs, 1),
                          "frac": round(gbs / peak, 4)}
+        if op.startswith("projection") and v["mean_ms"]:
+            flops = 8.0 * F * F * B * T
+            kernels[name]["tflops"] = round(flops / (v["mean_ms"] * 1e-3) / 1e12, 1)
     return {"op": op, "F": F, "B": B, "T": T, "iters": iters, "warmup": warmup,
             "peak_gbs": peak, "peak_kind": kind, "kernels": kernels}
 

@@ -592,3 +592,52 @@ def selective_layer_scan(x, weight, inputs, *, truncated: bool = False, activate
     tensors = [v.contiguous() if isinstance(v, torch.Tensor) else v for v in inputs[:-1]]
     return _SelectiveLayerScan.apply(x.contiguous(), weight, *tensors, inputs[-1], truncated,
                                      activate, write_raw, chunk)
+
+
+# ------------------------------------------------ complex projection GEMM
+def projection(W: torch.Tensor, x: torch.Tensor, conj_transpose: bool = False,
+               acc: torch.Tensor | None = None) -> torch.Tensor:
+    """out = op(W) @ x (+ acc) with x (K, ...) complex64, the trailing dims
+    flattened to N: the Pure RQF block projection z = W h
+    (rqf_models/backbones/rqf/pure.py:223, torch.matmul on the
+    (d_model, batch*time) view) when op(W) = W with W (M, K), and its input
+    cotangent W^H gz when ``conj_transpose`` (W is then (K, M)).  ``acc``
+    (M, ...) is added in the epilogue (the skip cotangent).
+
+    Runs the split-TF32 tcgen05 GEMM of rqf_projection (fp32-comparable;
+    not differentiable itself — the callers own the autograd).  An odd N,
+    which the kernel's TMA row pitch cannot express, runs torch.matmul on
+    the GPU instead."""
+    dev = _require_cuda(W, x, acc)
+    w = _c64(W)
+    xx = _c64(x)
+    if w.dim() != 2 or xx.dim() < 1:
+        raise ValueError("projection expects a 2-D W and an x of at least 1 dimension")
+    K = int(xx.shape[0])
+    M = int(w.shape[1] if conj_transpose else w.shape[0])
+    if int(w.shape[0] if conj_transpose else w.shape[1]) != K:
+        raise ValueError(f"W {tuple(w.shape)} does not match x {tuple(xx.shape)}"
+                         f"{' (conj_transpose)' if conj_transpose else ''}")
+    tail = tuple(xx.shape[1:])
+    N = 1
+    for d in tail:
+        N *= int(d)
+    out_shape = (M,) + tail
+    a = None
+    if acc is not None:
+        a = _c64(acc)
+        if tuple(a.shape) != out_shape:
+            raise ValueError(f"acc must have shape {out_shape}, got {tuple(a.shape)}")
+    if N % 2 == 1:
+        opw = w.mH if conj_transpose else w
+        out = (opw @ xx.reshape(K, N)).reshape(out_shape)
+        return out if a is None else out.add_(a)
+    lib = _abi.load()
+    out = torch.empty(out_shape, dtype=torch.complex64, device=dev)
+    ws = _scratch(lib.rqf_projection_workspace_bytes(M, K), dev)
+    with _timing.launch("rqf_projection", M * N, _nbytes(xx, out, a)):
+        _abi.check(lib.rqf_projection(
+            _abi.ptr(w), _abi.ptr(xx), _abi.ptr(a), _abi.ptr(out), M, K, N,
+            int(bool(conj_transpose)), _abi.ptr(ws), _abi.stream_of(xx)), "rqf_projection")
+    _done(dev)
+    return out
