@@ -35,13 +35,15 @@ import torch.distributed as dist
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-KERNELS_PER_CALL = {  # kernels each C-ABI call launches (the backward adds the reduction)
-    "rqf_fbt_prospective_forward": 1,
+KERNELS_PER_CALL = {  # kernels each C-ABI call launches (the backward adds the reduction,
+    "rqf_fbt_prospective_forward": 1,  # the projection its weight split)
+    "rqf_projection": 2,
     "rqf_fbt_block_forward": 1,
     "rqf_fbt_prospective_backward": 2,
     "rqf_tbptt1_two_tap_backward": 2,
 }
-SCAN_CALLS = tuple(KERNELS_PER_CALL)
+SCAN_CALLS = ("rqf_fbt_prospective_forward", "rqf_fbt_block_forward",
+              "rqf_fbt_prospective_backward", "rqf_tbptt1_two_tap_backward")
 
 
 def parse():

@@ -27,6 +27,7 @@ reaches W only, without the reference's second forward GEMM W(x.detach())
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 import torch.nn as nn
@@ -35,6 +36,21 @@ from torch.autograd.function import once_differentiable
 from . import ops
 
 SPLIT_RELU_GAIN = 0.5     # utils/init.py RQF_ACTIVATION_GAINS["split_relu"]
+
+# "tc": the block projections run on the split-TF32 tcgen05 GEMM
+# (ops.projection); "torch": torch.matmul (cuBLAS fp32), as the reference does.
+PROJECTION = os.environ.get("RQF_B200_PROJECTION", "tc")
+
+
+def _project(W, h, conj_transpose=False, acc=None):
+    """op(W) @ h (+ acc) over the (d, batch*time) view of an (d, B, T) tensor."""
+    if PROJECTION == "tc" and h.is_cuda:
+        return ops.projection(W, h, conj_transpose, acc)
+    d, B, T = h.shape
+    opw = W.mH if conj_transpose else W
+    if acc is None:
+        return (opw @ h.reshape(d, B * T)).reshape(-1, B, T)
+    return torch.addmm(acc.reshape(-1, B * T), opw, h.reshape(d, B * T)).reshape(-1, B, T)
 NOMINAL_FILTER_GAIN = 0.5  # utils/init.py NOMINAL_FILTER_GAIN
 
 
@@ -97,8 +113,7 @@ class _TBPTTLayer(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, h, W, C1, tap0, tap1, fuse_act):
-        F_in, B, T = h.shape
-        z = (W @ h.reshape(F_in, B * T)).reshape(W.shape[0], B, T)
+        z = _project(W, h)
         y, saved = ops._fbt_forward(C1, tap0, tap1, z, bool(fuse_act))
         ctx.save_for_backward(h, W, *saved)
         ctx.fuse_act = bool(fuse_act)
@@ -113,7 +128,7 @@ class _TBPTTLayer(torch.autograd.Function):
                                                      ctx.fuse_act)
         F_in, B, T = h.shape
         need = ctx.needs_input_grad
-        gh = (W.mH @ gz.reshape(W.shape[0], B * T)).reshape(F_in, B, T) if need[0] else None
+        gh = _project(W, gz, conj_transpose=True) if need[0] else None
         gW = (gz + gzw).reshape(W.shape[0], B * T) @ h.reshape(F_in, B * T).mH if need[1] else None
         return gh, gW, gc1, gt0, gt1, None
 
@@ -123,12 +138,13 @@ class _PureBlock(torch.autograd.Function):
     split-ReLU (or raw), and the complex skip h_out = out + h fused into the
     scan's store (pure.py:_forward_fbt :212-243 and :535).  Backward: the
     fused scan VJP on the output cotangent g, then one accumulating GEMM
-    gh = W^H gz + g (the skip's cotangent is g) and gW = gz h^H."""
+    gh = W^H gz + g (the skip's cotangent is g) and gW = gz h^H.  The two
+    projections with the activations as operand (W h, W^H gz + g) run on the
+    split-TF32 tcgen05 GEMM; gW (a K = B*T reduction) stays a torch GEMM."""
 
     @staticmethod
     def forward(ctx, h, W, C1, tap0, tap1, fuse_act, skip):
-        F_in, B, T = h.shape
-        z = (W @ h.reshape(F_in, B * T)).reshape(W.shape[0], B, T)
+        z = _project(W, h)
         out, saved = ops._fbt_forward(C1, tap0, tap1, z, bool(fuse_act), h if skip else None)
         ctx.save_for_backward(h, W, *saved)
         ctx.fuse_act, ctx.skip = bool(fuse_act), bool(skip)
@@ -145,10 +161,7 @@ class _PureBlock(torch.autograd.Function):
         need = ctx.needs_input_grad
         gh = None
         if need[0]:
-            if ctx.skip:
-                gh = torch.addmm(ops._c64(g).reshape(F_in, B * T), W.mH, gz2).reshape(F_in, B, T)
-            else:
-                gh = (W.mH @ gz2).reshape(F_in, B, T)
+            gh = _project(W, gz, conj_transpose=True, acc=ops._c64(g) if ctx.skip else None)
         gW = gz2 @ h.reshape(F_in, B * T).mH if need[1] else None
         return gh, gW, gc1, gt0, gt1, None, None
 

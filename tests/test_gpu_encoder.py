@@ -186,11 +186,15 @@ def test_block_forward_fused_skip(F, B, T, fuse):
 
 @pytest.mark.parametrize("F,B,T", [(4, 3, 3000), (40, 16, 2100)])
 @pytest.mark.parametrize("fuse,skip", [(True, True), (False, True), (True, False)])
-def test_pure_block_matches_unfused_composition(F, B, T, fuse, skip):
+def test_pure_block_matches_unfused_composition(F, B, T, fuse, skip, monkeypatch):
     """_PureBlock (GEMM + fused scan/skip + one accumulating GEMM backward)
-    against W @ h -> fbt_prospective_scan -> + h composed by autograd."""
+    against W @ h -> fbt_prospective_scan -> + h composed by autograd, both
+    with torch's projection GEMM so the scan sees bit-identical z."""
     import prospective_rqf_b200 as rqf
+    from prospective_rqf_b200 import encoder
     from prospective_rqf_b200.encoder import _PureBlock
+
+    monkeypatch.setattr(encoder, "PROJECTION", "torch")
 
     g = torch.Generator().manual_seed(F + B + T)
     c1, t0, t1 = (t.cuda() for t in _coef(g, F))
@@ -213,3 +217,31 @@ def test_pure_block_matches_unfused_composition(F, B, T, fuse, skip):
     assert torch.equal(out_a, out_b)
     for a, b, k in zip(leaves_a, leaves_b, ("h", "W", "c1", "tap0", "tap1")):
         assert_close(_np(a.grad.cpu()), _np(b.grad.cpu()), 1e-5, f"grad {k}")
+
+
+@pytest.mark.parametrize("F,B,T", [(32, 4, 3000), (40, 16, 2100)])
+@pytest.mark.parametrize("fuse", [False, True])
+def test_pure_block_tc_projection_matches_torch(F, B, T, fuse, monkeypatch):
+    """The block with its projections on the split-TF32 tcgen05 GEMM against
+    the same block on torch's fp32 GEMM.  With the split-ReLU on, an fp32
+    rounding difference may flip relu' at a state within rounding of 0, so
+    only the forward is compared there."""
+    from prospective_rqf_b200 import encoder
+    from prospective_rqf_b200.encoder import _PureBlock
+
+    g = torch.Generator().manual_seed(F * 3 + T)
+    c1, t0, t1 = (t.cuda() for t in _coef(g, F))
+    W = (_crandn(g, F, F) / math.sqrt(2 * F)).cuda()
+    h = _crandn(g, F, B, T).cuda()
+    gy = _crandn(g, F, B, T).cuda()
+    res = {}
+    for mode in ("tc", "torch"):
+        monkeypatch.setattr(encoder, "PROJECTION", mode)
+        leaves = [t.clone().requires_grad_(True) for t in (h, W, c1, t0, t1)]
+        out = _PureBlock.apply(*leaves, fuse, True)
+        out.backward(gy)
+        res[mode] = (out.detach(), [l.grad for l in leaves])
+    assert_close(_np(res["tc"][0].cpu()), _np(res["torch"][0].cpu()), 1e-5, "out")
+    if not fuse:
+        for a, b, k in zip(res["tc"][1], res["torch"][1], ("h", "W", "c1", "tap0", "tap1")):
+            assert_close(_np(a.cpu()), _np(b.cpu()), 1e-4, f"grad {k}")
