@@ -38,6 +38,7 @@ sys.path.insert(0, str(ROOT))
 KERNELS_PER_CALL = {  # kernels each C-ABI call launches (the backward adds the reduction,
     "rqf_fbt_prospective_forward": 1,  # the projection its weight split)
     "rqf_projection": 2,
+    "rqf_projection_weight_grad": 2,
     "rqf_fbt_block_forward": 1,
     "rqf_fbt_prospective_backward": 2,
     "rqf_tbptt1_two_tap_backward": 2,

@@ -284,6 +284,20 @@ int rqf_projection(const float *w, const float *x, const float *acc, float *out,
                    int64_t k, int64_t n, int conj_transpose, void *workspace,
                    rqf_stream_t stream);
 
+/* Weight cotangent of the same projection (autograd of pure.py:223's matmul
+ * with respect to W; cuBLAS fp32 in the reference):
+ *
+ *   gw[j, i] = sum_n gz[j, n] * conj(x[i, n])                      complex64
+ *
+ * gz (m x n) and x (k x n) with n contiguous; gw (m x k).  Split TF32 on the
+ * tensor cores, the n reduction split over CTAs and the fp32 partial tiles
+ * summed in a fixed order (deterministic).  Requirements as rqf_projection;
+ * `workspace` needs rqf_projection_weight_grad_workspace_bytes(m, k, n) bytes
+ * on the current device (the split count follows its SM count). */
+size_t rqf_projection_weight_grad_workspace_bytes(int64_t m, int64_t k, int64_t n);
+int rqf_projection_weight_grad(const float *gz, const float *x, float *gw, int64_t m, int64_t k,
+                               int64_t n, void *workspace, rqf_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -26,12 +26,12 @@
 //
 // CTA (one per SM, persistent over output tiles of 128 A' rows x 256 X'
 // columns = 64 complex outputs x 128 samples):
-//   warp 0      TMA producer: A_hi, A_lo (K-major, 128-byte swizzle) and X'
+//   warp 0      TMA producer: A_hi, A_lo (K-major, 64-byte swizzle) and X'
 //               (MN-major, 128-byte swizzle of 32-byte atoms) stages
 //   warp 1      TMEM owner and MMA issuer (tcgen05.mma.cta_group::1.kind::tf32)
 //   warps 2..5  epilogue: TMEM -> registers, complex combine, (+acc), store
 //   warps 6..9  transform: X' stage -> hi (in place) and lo
-// Two smem stages of K = 32 and two TMEM accumulators (2 x 256 columns), so
+// Four smem stages of K = 16 and two TMEM accumulators (2 x 256 columns), so
 // the epilogue of one tile overlaps the MMAs of the next.  Every mbarrier wait
 // is bounded in time; on expiry the kernel latches RQF_ERR_PIPELINE_TIMEOUT,
 // every role stops, in-flight copies and MMAs are waited for (bounded) and
@@ -49,16 +49,16 @@ namespace proj {
 
 constexpr int kBM = 128;              // A' rows per tile
 constexpr int kBN = 256;              // X' columns per tile
-constexpr int kBK = 32;               // K per stage: one 128-byte swizzle row of fp32
+constexpr int kBK = 16;               // K per stage: one 64-byte swizzle row of fp32
 constexpr int kUmmaK = 8;             // K of one tcgen05.mma kind::tf32
-constexpr int kStages = 2;
+constexpr int kStages = 4;
 constexpr int kAccBufs = 2;
 constexpr int kTmemCols = kBN * kAccBufs;  // 512: the whole TMEM of the SM
 constexpr int kThreads = 320;
 constexpr int kNBlocks = kBN / 32;    // 32-column (128-byte) blocks of an X' stage
 
-constexpr int kABytes = kBM * kBK * 4;            // 16 KB, one of A_hi / A_lo
-constexpr int kBBytes = kBK * kBN * 4;            // 32 KB, one of X_hi / X_lo
+constexpr int kABytes = kBM * kBK * 4;            // 8 KB, one of A_hi / A_lo
+constexpr int kBBytes = kBK * kBN * 4;            // 16 KB, one of X_hi / X_lo
 constexpr int kStageBytes = 2 * kABytes + 2 * kBBytes;
 constexpr int kTxBytes = 2 * kABytes + kBBytes;   // bytes the TMA lands per stage
 constexpr int kBarBytes = 256;
@@ -198,6 +198,27 @@ __device__ __forceinline__ void tc_ld_32x32b_x32(uint32_t taddr, float (&v)[32])
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+// The inverse: thread i writes v to columns [col, col+32) of lane (base + i).
+// Completion is awaited with tcgen05.wait::st.
+__device__ __forceinline__ void tc_st_32x32b_x32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(
+          taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
 
 __device__ __forceinline__ float tf32_rna(float v) {
   uint32_t r;
@@ -207,12 +228,12 @@ __device__ __forceinline__ float tf32_rna(float v) {
 
 // Shared-memory matrix descriptor of tcgen05.mma: start, leading and stride
 // byte offsets in 16-byte units, descriptor version 1, swizzle mode.
-//   kSwizzle128B       (2): 16-byte chunks XOR-ed over 8 rows of 128 bytes —
-//                           the K-major A' tile (TMA CU_TENSOR_MAP_SWIZZLE_128B);
+//   kSwizzle64B        (4): 16-byte chunks XOR-ed over 8 rows of 64 bytes —
+//                           the K-major A' tile (TMA CU_TENSOR_MAP_SWIZZLE_64B);
 //   kSwizzle128BBase32 (1): 32-byte chunks XOR-ed over 4 rows of 128 bytes —
 //                           what an MN-major 32-bit operand must use (the X'
 //                           tile; TMA CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B).
-constexpr uint64_t kSwizzle128B = 2, kSwizzle128BBase32 = 1;
+constexpr uint64_t kSwizzle64B = 4, kSwizzle128BBase32 = 1;
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo,
                                               uint64_t swizzle) {
   return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
@@ -360,17 +381,18 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           }
           tc_fence_after();
           const uint32_t st = smem_u32(smem + stage * kStageBytes);
-          // A': K-major, 8-row groups 1024 B apart.  X': MN-major, 32-column
-          // (128-byte) blocks kBK*128 B apart (LBO), 4-row groups 512 B apart (SBO).
-          const uint64_t a_hi = smem_desc(st, 16, 1024, kSwizzle128B);
-          const uint64_t a_lo = smem_desc(st + kABytes, 16, 1024, kSwizzle128B);
+          // A': K-major 64-byte rows, 8-row groups 512 B apart.  X': MN-major,
+          // 32-column (128-byte) blocks kBK*128 B apart (LBO), 4-row groups
+          // 512 B apart (SBO).
+          const uint64_t a_hi = smem_desc(st, 16, 512, kSwizzle64B);
+          const uint64_t a_lo = smem_desc(st + kABytes, 16, 512, kSwizzle64B);
           const uint64_t b_hi = smem_desc(st + 2 * kABytes, kBK * 128, 512, kSwizzle128BBase32);
           const uint64_t b_lo =
               smem_desc(st + 2 * kABytes + kBBytes, kBK * 128, 512, kSwizzle128BBase32);
 #pragma unroll
           for (int ks = 0; ks < kBK / kUmmaK; ++ks) {
-            // A advances 32 bytes along K inside its swizzle row; X' advances
-            // 8 rows (1024 bytes) per K step.
+            // A advances 32 bytes along K inside its 64-byte swizzle row; X'
+            // advances 8 rows (1024 bytes) per K step.
             const uint64_t da = (uint64_t)(ks * (kUmmaK * 4) >> 4);
             const uint64_t db = (uint64_t)(ks * (kUmmaK * 128) >> 4);
             const uint32_t accum = (kb > 0 || ks > 0) ? 1u : 0u;
@@ -510,6 +532,315 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                  "r"(kTmemCols)
                  : "memory");
+  }
+}
+
+
+// ------------------------------------------------------------ weight gradient
+// gW[j, i] = sum_n gz[j, n] conj(h[i, n]): the weight cotangent of z = W h.
+// Over the interleaved samples k' = 2n + {0: Re, 1: Im},
+//   Re gW[j,i] = sum_k' gz'[j,k'] h'[i,k'],    Im gW[j,i] = sum_k' gz'[j,k'] h~'[i,k'],
+// with h~'[i,2n] = -Im h[i,n] and h~'[i,2n+1] = Re h[i,n].  A work tile of
+// 128 j x 128 i accumulates D[j][c] in TMEM: column c < 128 holds Re and
+// c >= 128 holds Im of gW[j, i0 + c mod 128].  The k' range is split over
+// CTAs (split-K); each CTA stores its fp32 partial tile and
+// proj_wgrad_reduce_kernel sums the partials in a fixed order (deterministic).
+// A = gz' is K-major as loaded (64-byte swizzle, split in place like X' of the
+// projection).  B = [h' ; h~'] must be MN-major for a 32-bit operand, so the
+// transform warps transpose the TMA-loaded h' tile into the 32-byte-atom
+// layout while splitting it, writing both halves as hi and lo parts.
+constexpr int kWgRows = 128;                     // j per tile (A rows) and i per tile
+constexpr int kWgStages = 4;
+constexpr int kWgABytes = kWgRows * kBK * 4;     // 8 KB: gz' raw -> hi (in place); + lo
+constexpr int kWgSrcBytes = kWgRows * kBK * 4;   // 8 KB: h' raw
+constexpr int kWgBBytes = kBK * kBN * 4;         // 16 KB: one of B_hi / B_lo
+constexpr int kWgStageBytes = 2 * kWgABytes + kWgSrcBytes + 2 * kWgBBytes;  // 56 KB
+constexpr int kWgTxBytes = kWgABytes + kWgSrcBytes;
+constexpr int kWgSmemBytes = kWgStages * kWgStageBytes + kBarBytes + 1024;
+// TMEM: columns [0, 256) the CTA's running total, [256, 512) the chunk
+// accumulator.  The tensor core's fp32 accumulate rounds with a bias that
+// grows with the number of accumulations into one accumulator (about 2e-4
+// relative after 10^4 of them, against ~5e-6 after 10^2), so the MMAs
+// accumulate kWgChunk k-blocks (6 per k-block) at a time and the epilogue
+// warps fold each chunk into the total with ordinary fp32 adds.
+constexpr int kWgTmemCols = 2 * kBN;
+constexpr int kWgChunk = 16;
+
+struct WgParams {
+  float2 *partials;          // [splits][m_tiles*128][ld] complex
+  long long M, K;            // gW is M x K (F_out x F_in)
+  int m_tiles, i_tiles, splits;
+  long long kblocks;         // ceil(2N / kBK)
+  int ld;                    // i_tiles * 128
+};
+
+// Byte offset of element (column c, row k) of an MN-major 32-byte-atom tile
+// whose 32-column blocks are kBK rows of 128 bytes.
+__device__ __forceinline__ uint32_t mn32_offset(int c, int k) {
+  return (uint32_t)((c >> 5) * (kBK * 128) + k * 128 + ((((c & 31) >> 3) ^ (k & 3)) << 5) +
+                    ((c & 7) << 2));
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmH,
+                  const WgParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kWgStages * kWgStageBytes);
+  uint64_t *full = bars;
+  uint64_t *ready = bars + kWgStages;
+  uint64_t *empty = bars + 2 * kWgStages;
+  uint64_t *accf = bars + 3 * kWgStages;  // chunk accumulated   (tcgen05.commit)
+  uint64_t *acce = accf + 1;              // chunk folded/drained (4 epilogue warps)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acce + 1);
+  volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tile = blockIdx.x / p.splits;
+  const int split = blockIdx.x - tile * p.splits;
+  const int mt = tile % p.m_tiles;
+  const int it = tile / p.m_tiles;
+  const long long kb0 = (long long)split * p.kblocks / p.splits;
+  const long long kb1 = (long long)(split + 1) * p.kblocks / p.splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kWgStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&ready[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accf, 1);
+    mbar_init(acce, 4);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_tmap(&tmG);
+    prefetch_tmap(&tmH);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kWgTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      int stage = 0, issued = 0;
+      uint32_t phase = 0;
+      for (long long kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort, 1)) break;
+        uint8_t *st = smem + stage * kWgStageBytes;
+        mbar_expect_tx(&full[stage], kWgTxBytes);
+        tma_load_2d(st, &tmG, &full[stage], (int)(kb * kBK), mt * kWgRows);
+        tma_load_2d(st + 2 * kWgABytes, &tmH, &full[stage], (int)(kb * kBK), it * kWgRows);
+        ++issued;
+        if (++stage == kWgStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      for (int i = 0; i < kWgStages && i < issued; ++i) {
+        if (--stage < 0) {
+          stage = kWgStages - 1;
+          phase ^= 1u;
+        }
+        mbar_drain(&full[stage], phase);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, cphase = 0;
+      bool ok = true;
+      uint64_t *last = nullptr;
+      uint32_t last_parity = 0;
+      const uint32_t d_tmem = tmem_base + (uint32_t)kBN;  // chunk accumulator
+      for (long long c0 = kb0; ok && c0 < kb1; c0 += kWgChunk) {
+        const long long c1 = c0 + kWgChunk < kb1 ? c0 + kWgChunk : kb1;
+        if (!mbar_wait(acce, cphase ^ 1u, abort, 3)) break;  // previous chunk read out
+        tc_fence_after();
+        for (long long kb = c0; kb < c1; ++kb) {
+          if (!mbar_wait(&ready[stage], phase, abort, 4)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = smem_u32(smem + stage * kWgStageBytes);
+          const uint64_t a_hi = smem_desc(st, 16, 512, kSwizzle64B);
+          const uint64_t a_lo = smem_desc(st + kWgABytes, 16, 512, kSwizzle64B);
+          const uint32_t bb = st + 2 * kWgABytes + kWgSrcBytes;
+          const uint64_t b_hi = smem_desc(bb, kBK * 128, 512, kSwizzle128BBase32);
+          const uint64_t b_lo = smem_desc(bb + kWgBBytes, kBK * 128, 512, kSwizzle128BBase32);
+#pragma unroll
+          for (int ks = 0; ks < kBK / kUmmaK; ++ks) {
+            const uint64_t da = (uint64_t)(ks * (kUmmaK * 4) >> 4);
+            const uint64_t db = (uint64_t)(ks * (kUmmaK * 128) >> 4);
+            const uint32_t accum = (kb > c0 || ks > 0) ? 1u : 0u;
+            tc_mma_tf32(d_tmem, a_hi + da, b_hi + db, kIdesc, accum);
+            tc_mma_tf32(d_tmem, a_hi + da, b_lo + db, kIdesc, 1u);
+            tc_mma_tf32(d_tmem, a_lo + da, b_hi + db, kIdesc, 1u);
+          }
+          tc_commit(&empty[stage]);
+          last = &empty[stage];
+          last_parity = phase;
+          if (++stage == kWgStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(accf);
+        last = accf;
+        last_parity = cphase;
+        cphase ^= 1u;
+      }
+      if (last != nullptr) mbar_drain(last, last_parity);
+    }
+  } else if (warp < 6) {
+    // ---------------------------------------------------------- epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16);
+    const long long nchunks = (kb1 - kb0 + kWgChunk - 1) / kWgChunk;
+    uint32_t cphase = 0;
+    bool ok = true;
+    for (long long q = 0; q < nchunks; ++q) {
+      ok = __all_sync(0xffffffffu, mbar_wait(accf, cphase, abort, 5));
+      if (!ok) break;
+      tc_fence_after();
+      if (q + 1 < nchunks) {
+        // total += chunk (the first chunk initialises the total)
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          float v[32];
+          tc_ld_32x32b_x32(tbase + (uint32_t)(kBN + c * 32), v);
+          if (q > 0) {
+            float t[32];
+            tc_ld_32x32b_x32(tbase + (uint32_t)(c * 32), t);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] += t[i];
+          }
+          tc_st_32x32b_x32(tbase + (uint32_t)(c * 32), v);
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      } else {
+        // last chunk: partial = total + chunk, Re in columns [0,128), Im in [128,256)
+        const long long j = (long long)mt * kWgRows + row;
+        float2 *dst = p.partials + ((long long)split * p.m_tiles * kWgRows + j) * p.ld +
+                      (long long)it * kWgRows;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float re[32], im[32];
+          tc_ld_32x32b_x32(tbase + (uint32_t)(kBN + c * 32), re);
+          tc_ld_32x32b_x32(tbase + (uint32_t)(kBN + 128 + c * 32), im);
+          if (q > 0) {
+            float t[32];
+            tc_ld_32x32b_x32(tbase + (uint32_t)(c * 32), t);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) re[i] += t[i];
+            tc_ld_32x32b_x32(tbase + (uint32_t)(128 + c * 32), t);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) im[i] += t[i];
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            reinterpret_cast<float4 *>(dst + c * 32)[i] =
+                make_float4(re[2 * i], im[2 * i], re[2 * i + 1], im[2 * i + 1]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acce);
+      cphase ^= 1u;
+    }
+  } else {
+    // ---------------------------------------------------------- transform
+    const int t = threadIdx.x - 6 * 32;  // 0..127: also the h' row this thread transposes
+    int stage = 0;
+    uint32_t phase = 0;
+    for (long long kb = kb0; kb < kb1; ++kb) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, abort, 2))) break;
+      uint8_t *st = smem + stage * kWgStageBytes;
+      float4 *ab = reinterpret_cast<float4 *>(st);
+      float4 *al = reinterpret_cast<float4 *>(st + kWgABytes);
+#pragma unroll
+      for (int i = t; i < kWgABytes / 16; i += 128) {
+        const float4 v = ab[i];
+        float4 h, l;
+        h.x = tf32_rna(v.x); l.x = tf32_rna(v.x - h.x);
+        h.y = tf32_rna(v.y); l.y = tf32_rna(v.y - h.y);
+        h.z = tf32_rna(v.z); l.z = tf32_rna(v.z - h.z);
+        h.w = tf32_rna(v.w); l.w = tf32_rna(v.w - h.w);
+        ab[i] = h;
+        al[i] = l;
+      }
+      // h' row t: 16 floats in four 16-byte chunks, 64-byte swizzle
+      // (chunk q of row r at q ^ ((r >> 1) & 3)).
+      const uint8_t *src = st + 2 * kWgABytes + t * 64;
+      float x[kBK];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 v = *reinterpret_cast<const float4 *>(src + ((q ^ ((t >> 1) & 3)) << 4));
+        x[4 * q] = v.x; x[4 * q + 1] = v.y; x[4 * q + 2] = v.z; x[4 * q + 3] = v.w;
+      }
+      uint8_t *bh = st + 2 * kWgABytes + kWgSrcBytes;
+      uint8_t *bl = bh + kWgBBytes;
+#pragma unroll
+      for (int k = 0; k < kBK; ++k) {
+        const float v = x[k];
+        const float sw = (k & 1) ? x[k - 1] : -x[k + 1];  // h~'
+        const float vh = tf32_rna(v), sh = tf32_rna(sw);
+        const uint32_t o1 = mn32_offset(t, k), o2 = mn32_offset(t + kWgRows, k);
+        *reinterpret_cast<float *>(bh + o1) = vh;
+        *reinterpret_cast<float *>(bl + o1) = tf32_rna(v - vh);
+        *reinterpret_cast<float *>(bh + o2) = sh;
+        *reinterpret_cast<float *>(bl + o2) = tf32_rna(sw - sh);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ready[stage]);
+      if (++stage == kWgStages) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(kWgTmemCols)
+                 : "memory");
+  }
+}
+
+// gW[j, i] = sum over splits of the partial tiles, in split order.
+__global__ void proj_wgrad_reduce_kernel(const float2 *__restrict__ partials,
+                                         float2 *__restrict__ gw, long long M, long long K,
+                                         int splits, long long rows_pad, int ld) {
+  const long long total = M * K;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const long long j = e / K, i = e - j * K;
+    double re = 0.0, im = 0.0;
+    for (int s = 0; s < splits; ++s) {
+      const float2 v = partials[((long long)s * rows_pad + j) * ld + i];
+      re += v.x;
+      im += v.y;
+    }
+    gw[e] = make_float2((float)re, (float)im);
   }
 }
 

@@ -811,7 +811,7 @@ int rqf_projection(const float *w, const float *x, const float *acc, float *out,
   CUtensorMap tmA, tmX;
   if (!encode_map_2d(&tmA, a_split, (uint64_t)g.k_pad, (uint64_t)(2 * g.rows_pad),
                      (uint64_t)g.k_pad * sizeof(float), proj::kBK, proj::kBM,
-                     CU_TENSOR_MAP_SWIZZLE_128B) ||
+                     CU_TENSOR_MAP_SWIZZLE_64B) ||
       !encode_map_2d(&tmX, x, (uint64_t)(2 * n), (uint64_t)k, (uint64_t)(2 * n) * sizeof(float),
                      32, proj::kBK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
     return RQF_ERR_LAUNCH;
@@ -829,6 +829,104 @@ int rqf_projection(const float *w, const float *x, const float *acc, float *out,
   p.a_rows_pad = (int)g.rows_pad;
   const long long grid = p.num_tiles < sms ? p.num_tiles : sms;
   proj::proj_kernel<<<(unsigned)grid, proj::kThreads, proj::kSmemBytes, st>>>(tmA, tmX, p);
+  return launch_status();
+}
+
+}  // extern "C"
+
+// ------------------------------------------------ projection weight gradient
+namespace {
+
+struct WgGeometry {
+  int m_tiles, i_tiles, splits;
+  int64_t kblocks;
+};
+
+inline WgGeometry wgrad_geometry(int64_t m, int64_t k, int64_t n, int sms) {
+  WgGeometry g;
+  g.m_tiles = (int)ceil_div(m, proj::kWgRows);
+  g.i_tiles = (int)ceil_div(k, proj::kWgRows);
+  g.kblocks = ceil_div(2 * n, proj::kBK);
+  const int64_t tiles = (int64_t)g.m_tiles * g.i_tiles;
+  int64_t splits = sms > 0 ? sms / tiles : 1;
+  if (splits < 1) splits = 1;
+  if (splits > g.kblocks) splits = g.kblocks;
+  g.splits = (int)splits;
+  return g;
+}
+
+int device_sms() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  return sms;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t rqf_projection_weight_grad_workspace_bytes(int64_t m, int64_t k, int64_t n) {
+  if (m <= 0 || k <= 0 || n <= 0) return 0;
+  const WgGeometry g = wgrad_geometry(m, k, n, device_sms());
+  return (size_t)g.splits * (size_t)g.m_tiles * proj::kWgRows * (size_t)g.i_tiles *
+         proj::kWgRows * sizeof(float2);
+}
+
+int rqf_projection_weight_grad(const float *gz, const float *x, float *gw, int64_t m, int64_t k,
+                               int64_t n, void *workspace, rqf_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (m < 0 || k < 0 || n < 0) return RQF_ERR_SHAPE;
+  if (m == 0 || k == 0) return RQF_OK;
+  if (gw == nullptr) return RQF_ERR_ARGUMENT;
+  if (n == 0) {
+    return cudaMemsetAsync(gw, 0, (size_t)m * (size_t)k * sizeof(float2), st) == cudaSuccess
+               ? RQF_OK
+               : RQF_ERR_LAUNCH;
+  }
+  if (gz == nullptr || x == nullptr || workspace == nullptr) return RQF_ERR_ARGUMENT;
+  if ((n & 1) != 0 || n >= (int64_t(1) << 30) || m > 0x7fffffffLL || k > 0x7fffffffLL)
+    return RQF_ERR_SHAPE;
+  if (!aligned(gz, 16) || !aligned(x, 16) || !aligned(workspace, 16)) return RQF_ERR_ALIGN;
+  const int sms = device_sms();
+  if (sms <= 0) return RQF_ERR_LAUNCH;
+  const WgGeometry g = wgrad_geometry(m, k, n, sms);
+  {
+    static std::mutex mu;
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 64 && !configured[dev]) {
+      if (cudaFuncSetAttribute(proj::proj_wgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               proj::kWgSmemBytes) != cudaSuccess)
+        return RQF_ERR_LAUNCH;
+      configured[dev] = true;
+    }
+  }
+  CUtensorMap tmG, tmH;
+  if (!encode_map_2d(&tmG, gz, (uint64_t)(2 * n), (uint64_t)m, (uint64_t)(2 * n) * sizeof(float),
+                     proj::kBK, proj::kWgRows, CU_TENSOR_MAP_SWIZZLE_64B) ||
+      !encode_map_2d(&tmH, x, (uint64_t)(2 * n), (uint64_t)k, (uint64_t)(2 * n) * sizeof(float),
+                     proj::kBK, proj::kWgRows, CU_TENSOR_MAP_SWIZZLE_64B))
+    return RQF_ERR_LAUNCH;
+  proj::WgParams p;
+  p.partials = static_cast<float2 *>(workspace);
+  p.M = m;
+  p.K = k;
+  p.m_tiles = g.m_tiles;
+  p.i_tiles = g.i_tiles;
+  p.splits = g.splits;
+  p.kblocks = g.kblocks;
+  p.ld = g.i_tiles * proj::kWgRows;
+  const int64_t grid = (int64_t)g.m_tiles * g.i_tiles * g.splits;
+  proj::proj_wgrad_kernel<<<(unsigned)grid, proj::kThreads, proj::kWgSmemBytes, st>>>(tmG, tmH, p);
+  if (cudaGetLastError() != cudaSuccess) return RQF_ERR_LAUNCH;
+  const int64_t total = m * k;
+  const int64_t blocks = ceil_div(total, 256);
+  proj::proj_wgrad_reduce_kernel<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, st>>>(
+      p.partials, reinterpret_cast<float2 *>(gw), m, k, g.splits,
+      (long long)g.m_tiles * proj::kWgRows, p.ld);
   return launch_status();
 }
 

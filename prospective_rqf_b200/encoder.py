@@ -42,6 +42,13 @@ SPLIT_RELU_GAIN = 0.5     # utils/init.py RQF_ACTIVATION_GAINS["split_relu"]
 PROJECTION = os.environ.get("RQF_B200_PROJECTION", "tc")
 
 
+def _weight_grad(gz, h):
+    """gz @ h^H over the (d, batch*time) views: the projection's weight cotangent."""
+    if PROJECTION == "tc" and gz.is_cuda:
+        return ops.projection_weight_grad(gz, h)
+    return gz.reshape(gz.shape[0], -1) @ h.reshape(h.shape[0], -1).mH
+
+
 def _project(W, h, conj_transpose=False, acc=None):
     """op(W) @ h (+ acc) over the (d, batch*time) view of an (d, B, T) tensor."""
     if PROJECTION == "tc" and h.is_cuda:
@@ -129,7 +136,7 @@ class _TBPTTLayer(torch.autograd.Function):
         F_in, B, T = h.shape
         need = ctx.needs_input_grad
         gh = _project(W, gz, conj_transpose=True) if need[0] else None
-        gW = (gz + gzw).reshape(W.shape[0], B * T) @ h.reshape(F_in, B * T).mH if need[1] else None
+        gW = _weight_grad(gz + gzw, h) if need[1] else None
         return gh, gW, gc1, gt0, gt1, None
 
 
@@ -138,9 +145,8 @@ class _PureBlock(torch.autograd.Function):
     split-ReLU (or raw), and the complex skip h_out = out + h fused into the
     scan's store (pure.py:_forward_fbt :212-243 and :535).  Backward: the
     fused scan VJP on the output cotangent g, then one accumulating GEMM
-    gh = W^H gz + g (the skip's cotangent is g) and gW = gz h^H.  The two
-    projections with the activations as operand (W h, W^H gz + g) run on the
-    split-TF32 tcgen05 GEMM; gW (a K = B*T reduction) stays a torch GEMM."""
+    gh = W^H gz + g (the skip's cotangent is g) and gW = gz h^H, all three on
+    the split-TF32 tcgen05 GEMMs (ops.projection, ops.projection_weight_grad)."""
 
     @staticmethod
     def forward(ctx, h, W, C1, tap0, tap1, fuse_act, skip):
@@ -155,14 +161,11 @@ class _PureBlock(torch.autograd.Function):
     def backward(ctx, g):
         h, W, *saved = ctx.saved_tensors
         gc1, gt0, gt1, gz = ops._fbt_backward(saved, g, ctx.fuse_act)
-        F_in, B, T = h.shape
-        F_out = W.shape[0]
-        gz2 = gz.reshape(F_out, B * T)
         need = ctx.needs_input_grad
         gh = None
         if need[0]:
             gh = _project(W, gz, conj_transpose=True, acc=ops._c64(g) if ctx.skip else None)
-        gW = gz2 @ h.reshape(F_in, B * T).mH if need[1] else None
+        gW = _weight_grad(gz, h) if need[1] else None
         return gh, gW, gc1, gt0, gt1, None, None
 
 

@@ -17,9 +17,9 @@ Ops:
   btf_pro    _triton_chunked_scan_prospective, (B,T,F)
   selective  selective_forward + selective_backward with every controller on
              (--groups warp groups, --truncated for the TBPTT(1) variant)
-  projection the block projection z = W h and its input cotangent W^H gz + g
-             (split-TF32 tcgen05 GEMM, W of F x F complex); reports TFLOP/s
-             (8 F^2 B T real flops per GEMM) beside the bandwidth
+  projection the block projection z = W h, its input cotangent W^H gz + g and
+             its weight cotangent gz h^H (split-TF32 tcgen05 GEMMs, W of F x F
+             complex); reports TFLOP/s (8 F^2 B T real flops per GEMM)
   projection_torch  the same two GEMMs through torch.matmul (cuBLAS fp32)
 
 Every tensor is at least --T x --B x --F complex64; the shapes used for the
@@ -96,6 +96,7 @@ def make_case(op: str, F: int, B: int, T: int, groups: int = 8, truncated: bool 
             def run():
                 ops.projection(W, h)
                 ops.projection(W, gz, True, gh)
+                ops.projection_weight_grad(gz, h)
         else:
             from . import _timing
 
@@ -104,6 +105,8 @@ def make_case(op: str, F: int, B: int, T: int, groups: int = 8, truncated: bool 
                     W @ h.reshape(F, B * T)
                 with _timing.launch("torch_matmul_h", F * B * T, 24 * F * B * T):
                     torch.addmm(gh.reshape(F, B * T), W.mH, gz.reshape(F, B * T))
+                with _timing.launch("torch_matmul_w", F * B * T, 16 * F * B * T):
+                    gz.reshape(F, B * T) @ h.reshape(F, B * T).mH
         return run
 
     if op == "fbt_skip":

@@ -641,3 +641,29 @@ def projection(W: torch.Tensor, x: torch.Tensor, conj_transpose: bool = False,
             int(bool(conj_transpose)), _abi.ptr(ws), _abi.stream_of(xx)), "rqf_projection")
     _done(dev)
     return out
+
+
+def projection_weight_grad(gz: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """gW = gz @ x^H over the flattened trailing dims: the weight cotangent of
+    the block projection z = W x (pure.py:223) given gz = dL/dz, with gz
+    (M, ...) and x (K, ...) complex64.  Split-TF32 tcgen05 GEMM with a split
+    reduction over samples summed in a fixed order
+    (rqf_projection_weight_grad); an odd sample count runs torch.matmul."""
+    dev = _require_cuda(gz, x)
+    g = _c64(gz)
+    xx = _c64(x)
+    M, K = int(g.shape[0]), int(xx.shape[0])
+    if tuple(g.shape[1:]) != tuple(xx.shape[1:]):
+        raise ValueError(f"gz {tuple(g.shape)} and x {tuple(xx.shape)} differ in trailing dims")
+    N = g.numel() // M if M else 0
+    if N % 2 == 1:
+        return g.reshape(M, N) @ xx.reshape(K, N).mH
+    lib = _abi.load()
+    gw = torch.empty((M, K), dtype=torch.complex64, device=dev)
+    ws = _scratch(lib.rqf_projection_weight_grad_workspace_bytes(M, K, N), dev)
+    with _timing.launch("rqf_projection_weight_grad", M * N, _nbytes(g, xx, gw)):
+        _abi.check(lib.rqf_projection_weight_grad(
+            _abi.ptr(g), _abi.ptr(xx), _abi.ptr(gw), M, K, N, _abi.ptr(ws),
+            _abi.stream_of(g)), "rqf_projection_weight_grad")
+    _done(dev)
+    return gw

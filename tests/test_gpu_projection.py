@@ -101,3 +101,55 @@ def test_projection_odd_n_uses_torch_and_matches():
     W, x = _crandn(g, 8, 16), _crandn(g, 16, 3, 5)
     out = ops.projection(W.cuda(), x.cuda())
     assert_close(out.cpu().numpy().astype(np.complex128), _ref(W, x, False), 1e-6, "odd N")
+
+
+# ------------------------------------------------ weight gradient gz @ x^H
+def _ref_wgrad(gz, x):
+    M, K = gz.shape[0], x.shape[0]
+    g = gz.cpu().to(torch.complex128).reshape(M, -1)
+    xx = x.cpu().to(torch.complex128).reshape(K, -1)
+    return (g @ xx.mH).numpy()
+
+
+WG_SHAPES = [(64, 32, 256), (37, 50, 1000), (128, 128, 4096), (5, 3, 2), (256, 256, 2 * 1111),
+             (200, 130, 64)]
+
+
+@pytest.mark.parametrize("M,K,N", WG_SHAPES)
+def test_weight_grad_vs_fp64(M, K, N):
+    from prospective_rqf_b200 import ops
+
+    g = torch.Generator().manual_seed(M * 131 + K * 7 + N)
+    gz, x = _crandn(g, M, N), _crandn(g, K, N)
+    gw = ops.projection_weight_grad(gz.cuda(), x.cuda())
+    assert gw.shape == (M, K)
+    ref = _ref_wgrad(gz, x)
+    e32 = rel_err((gz.cuda() @ x.cuda().mH).cpu().numpy(), ref)
+    assert_close(gw.cpu().numpy().astype(np.complex128), ref, max(PROJ_TOL, 3 * e32), "gz x^H")
+
+
+def test_weight_grad_full_layer_shape():
+    """Config-5 layer: gz, h of 256 x (32 x 16000), a reduction over 512,000
+    samples.  Against fp64 (the fp32 sum over the samples sets the error
+    floor, so the bound is tied to torch's own fp32 error) and deterministic."""
+    from prospective_rqf_b200 import ops
+
+    g = torch.Generator().manual_seed(9)
+    F, B, T = 256, 32, 16000
+    gz = torch.randn(F, B, T, dtype=torch.complex64, generator=g).cuda()
+    h = torch.randn(F, B, T, dtype=torch.complex64, generator=g).cuda()
+    gw = ops.projection_weight_grad(gz, h)
+    ref = (gz.reshape(F, -1).to(torch.complex128) @ h.reshape(F, -1).to(torch.complex128).mH)
+    ref = ref.cpu().numpy()
+    e32 = rel_err((gz.reshape(F, -1) @ h.reshape(F, -1).mH).cpu().numpy(), ref)
+    assert_close(gw.cpu().numpy().astype(np.complex128), ref, max(2e-5, 3 * e32), "full layer")
+    assert torch.equal(gw, ops.projection_weight_grad(gz, h))
+
+
+def test_weight_grad_odd_n_uses_torch():
+    from prospective_rqf_b200 import ops
+
+    g = torch.Generator().manual_seed(4)
+    gz, x = _crandn(g, 6, 3, 5), _crandn(g, 4, 3, 5)
+    gw = ops.projection_weight_grad(gz.cuda(), x.cuda())
+    assert_close(gw.cpu().numpy().astype(np.complex128), _ref_wgrad(gz, x), 1e-6, "odd N")
