@@ -16,13 +16,17 @@
 // Rows 2j and 2j+1 of a tile sit in adjacent TMEM lanes, i.e. adjacent
 // threads of one epilogue warp, which combine them with shuffles.
 //
-// Precision.  Every fp32 operand v is split as hi = rna_tf32(v),
-// lo = rna_tf32(v - hi), and the tile accumulates A_hi X_hi + A_hi X_lo +
-// A_lo X_hi in fp32: about 21 significant bits per operand against 11 for a
-// single TF32 product, i.e. fp32-comparable (the fp32 SIMT complex GEMM it
-// replaces keeps 24).  A' is split once per call by proj_prep_kernel; X' is
-// split in shared memory by four transform warps right after its TMA load,
-// so the activations cross HBM once.
+// Precision.  tcgen05.mma kind::tf32 converts its fp32 operands to TF32 by
+// truncation (round toward zero; measured on B200 by an in-bounds MMA of
+// values with low mantissa bits set against exact ones).  So the raw fp32
+// value v already serves as hi = trunc_tf32(v), and only lo =
+// rna_tf32(v - trunc_tf32(v)) is materialised; the tile accumulates
+// A_hi X_hi + A_hi X_lo + A_lo X_hi in fp32: about 21 significant bits per
+// operand against 10 for a single TF32 product, i.e. fp32-comparable (the
+// fp32 SIMT complex GEMM it replaces keeps 24).  A' is split once per call
+// by proj_prep_kernel; X' is split in shared memory by four transform warps
+// right after its TMA load (writing only the lo part), so the activations
+// cross HBM once.
 //
 // CTA (one per SM, persistent over output tiles of 128 A' rows x 256 X'
 // columns = 64 complex outputs x 128 samples):
@@ -30,7 +34,7 @@
 //               (MN-major, 128-byte swizzle of 32-byte atoms) stages
 //   warp 1      TMEM owner and MMA issuer (tcgen05.mma.cta_group::1.kind::tf32)
 //   warps 2..5  epilogue: TMEM -> registers, complex combine, (+acc), store
-//   warps 6..9  transform: X' stage -> hi (in place) and lo
+//   warps 6..9  transform: X' stage -> lo part (the raw stage is the hi part)
 // Four smem stages of K = 16 and two TMEM accumulators (2 x 256 columns), so
 // the epilogue of one tile overlaps the MMAs of the next.  Every mbarrier wait
 // is bounded in time; on expiry the kernel latches RQF_ERR_PIPELINE_TIMEOUT,
@@ -104,14 +108,18 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
                "r"(bytes)
                : "memory");
 }
+// try_wait with a suspend-time hint: a waiting warp sleeps in hardware (up to
+// the hint, in ns) instead of re-issuing the poll, leaving issue slots to
+// the transform and epilogue warps.
+constexpr uint32_t kSuspendHintNs = 1000000;
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.b32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
 }
@@ -126,7 +134,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 31u) == 0u) {
       if (*abort) return false;
-      if (global_ns() - t0 > kWaitLimitNs) {
+      if (global_ns() - t0 > kWaitLimitNs) {  // each poll sleeps at most kSuspendHintNs
         latch_error(kErrPipelineTimeout);
         atomicCAS(&g_proj_timeout_site, 0, site);
         *abort = 1;
@@ -225,6 +233,11 @@ __device__ __forceinline__ float tf32_rna(float v) {
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
   return __uint_as_float(r);
 }
+// The low part of the split: v minus the TF32 value the tensor core reads
+// for v (its truncation), rounded to TF32 so that it is read exactly.
+__device__ __forceinline__ float tf32_lo(float v) {
+  return tf32_rna(v - __uint_as_float(__float_as_uint(v) & 0xffffe000u));
+}
 
 // Shared-memory matrix descriptor of tcgen05.mma: start, leading and stride
 // byte offsets in 16-byte units, descriptor version 1, swizzle mode.
@@ -266,9 +279,8 @@ __global__ void proj_prep_kernel(const float2 *__restrict__ W, float *__restrict
         v = (r & 1) ? -w.y : w.x;
       }
     }
-    const float hi = tf32_rna(v);
-    a_split[i] = hi;
-    a_split[total + i] = tf32_rna(v - hi);
+    a_split[i] = v;  // read as trunc_tf32(v) by the tensor core
+    a_split[total + i] = tf32_lo(v);
   }
 }
 
@@ -503,14 +515,8 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         float4 *xl = reinterpret_cast<float4 *>(smem + stage * kStageBytes + 2 * kABytes + kBBytes);
 #pragma unroll 4
         for (int i = t; i < kBBytes / 16; i += 128) {
-          const float4 v = xb[i];
-          float4 h, l;
-          h.x = tf32_rna(v.x); l.x = tf32_rna(v.x - h.x);
-          h.y = tf32_rna(v.y); l.y = tf32_rna(v.y - h.y);
-          h.z = tf32_rna(v.z); l.z = tf32_rna(v.z - h.z);
-          h.w = tf32_rna(v.w); l.w = tf32_rna(v.w - h.w);
-          xb[i] = h;
-          xl[i] = l;
+          const float4 v = xb[i];  // stays in place as the hi part
+          xl[i] = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
         }
         // generic-proxy smem writes -> visible to the tensor core (async proxy)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -774,14 +780,8 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
       float4 *al = reinterpret_cast<float4 *>(st + kWgABytes);
 #pragma unroll
       for (int i = t; i < kWgABytes / 16; i += 128) {
-        const float4 v = ab[i];
-        float4 h, l;
-        h.x = tf32_rna(v.x); l.x = tf32_rna(v.x - h.x);
-        h.y = tf32_rna(v.y); l.y = tf32_rna(v.y - h.y);
-        h.z = tf32_rna(v.z); l.z = tf32_rna(v.z - h.z);
-        h.w = tf32_rna(v.w); l.w = tf32_rna(v.w - h.w);
-        ab[i] = h;
-        al[i] = l;
+        const float4 v = ab[i];  // stays in place as the hi part
+        al[i] = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
       }
       // h' row t: 16 floats in four 16-byte chunks, 64-byte swizzle
       // (chunk q of row r at q ^ ((r >> 1) & 3)).
@@ -798,12 +798,11 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
       for (int k = 0; k < kBK; ++k) {
         const float v = x[k];
         const float sw = (k & 1) ? x[k - 1] : -x[k + 1];  // h~'
-        const float vh = tf32_rna(v), sh = tf32_rna(sw);
         const uint32_t o1 = mn32_offset(t, k), o2 = mn32_offset(t + kWgRows, k);
-        *reinterpret_cast<float *>(bh + o1) = vh;
-        *reinterpret_cast<float *>(bl + o1) = tf32_rna(v - vh);
-        *reinterpret_cast<float *>(bh + o2) = sh;
-        *reinterpret_cast<float *>(bl + o2) = tf32_rna(sw - sh);
+        *reinterpret_cast<float *>(bh + o1) = v;
+        *reinterpret_cast<float *>(bl + o1) = tf32_lo(v);
+        *reinterpret_cast<float *>(bh + o2) = sw;
+        *reinterpret_cast<float *>(bl + o2) = tf32_lo(sw);
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
