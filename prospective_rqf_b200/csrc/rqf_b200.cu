@@ -600,6 +600,16 @@ int sel_check(const float *z, const rqf_selective_inputs *in, const rqf_selectiv
   return RQF_OK;
 }
 
+// 16-byte per-thread accesses need every per-sample row to start on a
+// 16-byte boundary: T a multiple of 4 and 16-byte aligned base pointers.
+int sel_vec(const SelArgs &a, int64_t T) {
+  if (T % 4 != 0) return 0;
+  const void *ptrs[] = {a.z, a.G, a.D, a.W, a.raw, a.act, a.gy, a.gx, a.dz, a.dzw, a.dG, a.dD, a.dW};
+  for (const void *p : ptrs)
+    if (p != nullptr && !aligned(p, 16)) return 0;
+  return 1;
+}
+
 template <typename Kern>
 unsigned sel_grid(Kern kernel, int64_t rows) {
   const int64_t g = resident_ctas(kernel, kSelThreads, 0);
@@ -618,7 +628,8 @@ int64_t rqf_selective_carry_count(int64_t filters, int64_t batch, int64_t time) 
 size_t rqf_selective_scratch_bytes(int64_t filters, int64_t batch, int64_t time, int has_warp) {
   if (filters <= 0 || batch <= 0 || time <= 0) return 256;
   const size_t dd = has_warp ? round256((size_t)filters * batch * time * sizeof(float)) : 0;
-  return dd + round256((size_t)filters * batch * 2 * sizeof(float));
+  const size_t order = has_warp ? round256((size_t)(filters + 33) * sizeof(int)) : 0;
+  return dd + round256((size_t)filters * batch * 2 * sizeof(float)) + order;
 }
 
 int rqf_selective_forward(const float *z, const rqf_selective_inputs *inputs,
@@ -634,6 +645,7 @@ int rqf_selective_forward(const float *z, const rqf_selective_inputs *inputs,
   a.raw = reinterpret_cast<float2 *>(raw);
   a.act = reinterpret_cast<float2 *>(act);
   a.carries = reinterpret_cast<float2 *>(carries);
+  a.vec = sel_vec(a, time);
   auto kern = sel_fwd_kernel<kSelThreads, kSelK>;
   kern<<<sel_grid(kern, a.rows), kSelThreads, 0, stream>>>(a);
   return launch_status();
@@ -675,13 +687,19 @@ int rqf_selective_backward(const float *z, const rqf_selective_inputs *inputs,
       options->has_warp ? round256((size_t)filters * batch * time * sizeof(float)) : 0;
   a.dD = options->has_warp ? static_cast<float *>(scratch) : nullptr;
   a.partials = at<float>(scratch, dd_bytes);
+  a.vec = sel_vec(a, time);
   auto kern = sel_bwd_kernel<kSelThreads, kSelK>;
   kern<<<sel_grid(kern, a.rows), kSelThreads, 0, stream>>>(a);
   if ((st = launch_status()) != RQF_OK) return st;
   if (options->has_warp) {
     const int64_t bt = batch * time;
-    sel_group_reduce_kernel<<<(unsigned)ceil_div(bt, 256), 256, 0, stream>>>(
-        a.dD, a.groups, dwarp, (int)filters, (int)inputs->num_groups, bt);
+    int *order = at<int>(scratch, dd_bytes + round256((size_t)filters * batch * 2 * sizeof(float)));
+    int *bounds = order + filters;
+    const int ng = (int)inputs->num_groups;
+    sel_group_order_kernel<<<1, 32 * ng, 0, stream>>>(a.groups, (int)filters, ng, order, bounds);
+    if ((st = launch_status()) != RQF_OK) return st;
+    sel_group_reduce_kernel<<<(unsigned)ceil_div(bt, 256), 256, 0, stream>>>(a.dD, order, bounds,
+                                                                              dwarp, ng, bt);
     if ((st = launch_status()) != RQF_OK) return st;
   }
   sel_param_reduce_kernel<<<(unsigned)ceil_div(filters, 128), 128, 0, stream>>>(

@@ -52,6 +52,7 @@ struct SelArgs {
   int rows, T, batch, ntiles, num_groups;
   SelOptions o;
   int truncated;
+  int vec;  // T % 4 == 0 and every per-sample tensor 16-byte aligned: 16-byte accesses
 };
 
 constexpr int kSelThreads = 256;
@@ -72,7 +73,52 @@ struct SelCoef {
   float ratio;
 };
 
-__device__ __forceinline__ float sel_sigmoid(float x) { return 1.f / (1.f + expf(-x)); }
+// Controller links on the hardware exponential (ex2-based __expf, ~2 ulp, as
+// the reference's Triton tl.exp) and the 2-ulp reciprocal.  tanh comes from
+// the identity tanh(x) = 1 - 2 / (e^{2x} + 1): absolute error ~1e-7, and the
+// controllers only use it additively (exponents, 1 - tanh^2).
+__device__ __forceinline__ float sel_rcp(float x) { return __fdividef(1.f, x); }
+__device__ __forceinline__ float sel_sigmoid(float x) { return sel_rcp(1.f + __expf(-x)); }
+__device__ __forceinline__ float sel_tanh(float x) {
+  const float e = __expf(2.f * x);
+  return e > 1e30f ? 1.f : fmaf(-2.f, sel_rcp(e + 1.f), 1.f);
+}
+// e^x - 1 without cancellation: the Maclaurin series through x^8/8! below
+// |x| = 0.35 (truncation < 0.35^9/9! ~ 2e-10), e^x - 1 on __expf above (where
+// e^x - 1 is at least 0.3 in magnitude, so no digits cancel).
+__device__ __forceinline__ float sel_expm1(float x) {
+  if (fabsf(x) < 0.35f) {
+    float p = fmaf(x, 1.f / 40320.f, 1.f / 5040.f);
+    p = fmaf(x, p, 1.f / 720.f);
+    p = fmaf(x, p, 1.f / 120.f);
+    p = fmaf(x, p, 1.f / 24.f);
+    p = fmaf(x, p, 1.f / 6.f);
+    p = fmaf(x, p, 0.5f);
+    return fmaf(x * x, p, x);
+  }
+  return __expf(x) - 1.f;
+}
+
+// sin and cos of the ZOH half angle.  Below pi/4 (every practical step: the
+// angle is (1 - gamma) theta h / 2) the Maclaurin series of sin and cos
+// through x^9 and x^10 — truncation below x^11/11! < 2e-9 — evaluated in
+// Horner form on x^2; larger angles take sincosf.
+__device__ __forceinline__ void sel_sincos_half(float x, float &sn, float &cs) {
+  if (fabsf(x) < 0.7853982f) {
+    const float x2 = x * x;
+    float ps = fmaf(x2, 1.f / 362880.f, -1.f / 5040.f);
+    ps = fmaf(x2, ps, 1.f / 120.f);
+    ps = fmaf(x2, ps, -1.f / 6.f);
+    sn = fmaf(x * x2, ps, x);
+    float pc = fmaf(x2, -1.f / 3628800.f, 1.f / 40320.f);
+    pc = fmaf(x2, pc, -1.f / 720.f);
+    pc = fmaf(x2, pc, 1.f / 24.f);
+    pc = fmaf(x2, pc, -0.5f);
+    cs = fmaf(x2, pc, 1.f);
+  } else {
+    sincosf(x, &sn, &cs);
+  }
+}
 
 __device__ __forceinline__ SelChan sel_chan(const SelArgs &a, int f) {
   SelChan c;
@@ -105,8 +151,8 @@ __device__ __forceinline__ SelCtl sel_controller(const SelOptions &o, const SelC
   r.g = c.bias;
   if (o.has_gamma) {
     if (o.log_shift) {
-      r.sig = tanhf(gl);
-      r.g = expf(c.bias + o.gamma_scale * r.sig);
+      r.sig = sel_tanh(gl);
+      r.g = __expf(c.bias + o.gamma_scale * r.sig);
     } else {
       r.sig = sel_sigmoid(c.bias + gl);
       r.g = c.lo + c.span * r.sig;
@@ -114,8 +160,8 @@ __device__ __forceinline__ SelCtl sel_controller(const SelOptions &o, const SelC
   }
   r.th = c.theta;
   if (o.has_warp) {
-    r.warp = tanhf(dl);
-    r.scale = expf(o.warp_scale * r.warp);
+    r.warp = sel_tanh(dl);
+    r.scale = __expf(o.warp_scale * r.warp);
     r.th = c.theta * r.scale;
     if (o.bound_warp) r.th = fminf(fmaxf(r.th, c.th_lo), c.th_hi);
   }
@@ -129,11 +175,11 @@ __device__ __forceinline__ SelCoef sel_coef(const SelOptions &o, const SelChan &
   SelCoef r;
   const float ar = -k.g * c.h, ai = (1.f - k.g) * k.th * c.h;
   // half-angle sincos gives sin(ai), cos(ai) and the cancellation-free
-  // 1 - cos(ai) = 2 sin^2(ai/2) from one call
+  // 1 - cos(ai) = 2 sin^2(ai/2) from one evaluation
   float hs, hc;
-  sincosf(0.5f * ai, &hs, &hc);
+  sel_sincos_half(0.5f * ai, hs, hc);
   const float sn = 2.f * hs * hc, one_m_cs = 2.f * hs * hs, cs = 1.f - one_m_cs;
-  const float e = expf(ar);
+  const float e = __expf(ar);
   r.a = make_float2(ar, ai);
   r.A = make_float2(e * cs, e * sn);
   const float den = ar * ar + ai * ai;
@@ -143,8 +189,8 @@ __device__ __forceinline__ SelCoef sel_coef(const SelOptions &o, const SelChan &
     r.phi = c_fma(r.a, s, cone());
   } else {
     // e^a - 1 without cancellation: expm1(ar) cos(ai) - (1 - cos(ai)) + i e^ar sin(ai)
-    const float er = expm1f(ar) * cs - one_m_cs, ei = r.A.y;
-    const float inv = 1.f / den;
+    const float er = sel_expm1(ar) * cs - one_m_cs, ei = r.A.y;
+    const float inv = sel_rcp(den);
     r.phi = make_float2((er * ar + ei * ai) * inv, (ei * ar - er * ai) * inv);
   }
   const float gh = k.g * c.h;
@@ -152,7 +198,7 @@ __device__ __forceinline__ SelCoef sel_coef(const SelOptions &o, const SelChan &
   r.n0 = cz();
   r.ratio = 0.f;
   if (o.prospective) {
-    r.ratio = o.gamma_horizon ? 1.f / k.g : c.horizon;
+    r.ratio = o.gamma_horizon ? sel_rcp(k.g) : c.horizon;
     const float rg = r.ratio * k.g;
     const float2 lag = make_float2(rg * r.A.x, rg * r.A.y);
     r.p0 = c_add(r.p0, lag);
@@ -178,14 +224,64 @@ __device__ __forceinline__ float2 sel_dphi(float2 a, float2 A, float2 phi) {
     return s;
   }
   const float2 d = make_float2(A.x - phi.x, A.y - phi.y);
-  const float inv = 1.f / den;
+  const float inv = sel_rcp(den);
   return make_float2((d.x * a.x + d.y * a.y) * inv, (d.y * a.x - d.x * a.y) * inv);
 }
 
-template <int K>
-__device__ __forceinline__ void sel_load_logits(const float *base, int t0, int T, float (&v)[K]) {
+// Per-thread groups of K = 4 consecutive samples [t0, t0 + 4) of one row:
+// 16-byte accesses when `vec` and the group lies inside the row, element-wise
+// (zero fill past T) otherwise.  Complex rows stream (read or written once).
+static_assert(kSelK == 4, "the vector accesses below move 4 samples per thread");
+__device__ __forceinline__ void sel_ld_f(const float *row, int t0, int T, bool vec,
+                                         float (&v)[kSelK]) {
+  if (row && vec && t0 + kSelK <= T) {
+    const float4 q = __ldg(reinterpret_cast<const float4 *>(row + t0));
+    v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+    return;
+  }
 #pragma unroll
-  for (int k = 0; k < K; ++k) v[k] = (base && t0 + k < T) ? __ldg(base + t0 + k) : 0.f;
+  for (int k = 0; k < kSelK; ++k) v[k] = (row && t0 + k < T) ? __ldg(row + t0 + k) : 0.f;
+}
+__device__ __forceinline__ void sel_ld_c(const float2 *row, int t0, int T, bool vec,
+                                         float2 (&v)[kSelK]) {
+  if (row && vec && t0 + kSelK <= T) {
+    const float4 *q = reinterpret_cast<const float4 *>(row + t0);
+    const float4 a = __ldcs(q), b = __ldcs(q + 1);
+    v[0] = make_float2(a.x, a.y); v[1] = make_float2(a.z, a.w);
+    v[2] = make_float2(b.x, b.y); v[3] = make_float2(b.z, b.w);
+    return;
+  }
+#pragma unroll
+  for (int k = 0; k < kSelK; ++k) v[k] = (row && t0 + k < T) ? __ldcs(row + t0 + k) : cz();
+}
+__device__ __forceinline__ void sel_st_c(float2 *row, int t0, int T, bool vec,
+                                         const float2 (&v)[kSelK]) {
+  if (vec && t0 + kSelK <= T) {
+    float4 *q = reinterpret_cast<float4 *>(row + t0);
+    __stcs(q, make_float4(v[0].x, v[0].y, v[1].x, v[1].y));
+    __stcs(q + 1, make_float4(v[2].x, v[2].y, v[3].x, v[3].y));
+    return;
+  }
+#pragma unroll
+  for (int k = 0; k < kSelK; ++k)
+    if (t0 + k < T) __stcs(row + t0 + k, v[k]);
+}
+__device__ __forceinline__ void sel_st_f(float *row, int t0, int T, bool vec,
+                                         const float (&v)[kSelK]) {
+  if (vec && t0 + kSelK <= T) {
+    __stcs(reinterpret_cast<float4 *>(row + t0), make_float4(v[0], v[1], v[2], v[3]));
+    return;
+  }
+#pragma unroll
+  for (int k = 0; k < kSelK; ++k)
+    if (t0 + k < T) __stcs(row + t0 + k, v[k]);
+}
+// z[t0 - 1]: the previous thread's last sample, from memory for lane 0.
+__device__ __forceinline__ float2 sel_prev_z(const float2 *row, int t0, int T, float2 zlast,
+                                             int lane) {
+  float2 zp = shfl_up2(zlast, 1);
+  if (lane == 0) zp = (t0 > 0 && t0 - 1 < T) ? row[t0 - 1] : cz();
+  return zp;
 }
 
 // ------------------------------------------------------------ forward
@@ -195,6 +291,7 @@ __global__ void __launch_bounds__(NT) sel_fwd_kernel(const SelArgs a) {
   __shared__ float4 s_warp[2][NT / 32];  // double-buffered across consecutive tiles
   const int tid = threadIdx.x;
   const int T = a.T;
+  const bool vec = a.vec != 0;
   unsigned tcount = 0;
   for (int row = blockIdx.x; row < a.rows; row += gridDim.x) {
     const int f = row / a.batch, b = row - f * a.batch;
@@ -207,13 +304,12 @@ __global__ void __launch_bounds__(NT) sel_fwd_kernel(const SelArgs a) {
     for (int j = 0; j < a.ntiles; ++j, ++tcount) {
       const int t0 = j * L + tid * K;
       float2 z[K];
-#pragma unroll
-      for (int k = 0; k < K; ++k) z[k] = (t0 + k < T) ? __ldcs(zrow + t0 + k) : cz();
-      const float2 zp = (t0 > 0 && t0 - 1 < T) ? zrow[t0 - 1] : cz();
+      sel_ld_c(zrow, t0, T, vec, z);
+      const float2 zp = sel_prev_z(zrow, t0, T, z[K - 1], tid & 31);
       float gl[K], dl[K], wl[K];
-      sel_load_logits<K>(grow, t0, T, gl);
-      sel_load_logits<K>(drow, t0, T, dl);
-      sel_load_logits<K>(wrow, t0, T, wl);
+      sel_ld_f(grow, t0, T, vec, gl);
+      sel_ld_f(drow, t0, T, vec, dl);
+      sel_ld_f(wrow, t0, T, vec, wl);
       float2 A[K], u[K];
 #pragma unroll
       for (int k = 0; k < K; ++k) {
@@ -235,21 +331,22 @@ __global__ void __launch_bounds__(NT) sel_fwd_kernel(const SelArgs a) {
       cta_scan_pair_entry_fwd<NT>(g, y, carry, e, At, s_warp[tcount & 1]);
       if (tid == 0) a.carries[(size_t)row * a.ntiles + j] = carry;
       carry = At;
+      float2 ys[K], acts[K];
 #pragma unroll
       for (int k = 0; k < K; ++k) {
         e = c_fma(A[k], e, u[k]);
-        if (t0 + k < T) {
-          if (a.raw) __stcs(a.raw + (size_t)row * T + t0 + k, e);
-          if (a.act) __stcs(a.act + (size_t)row * T + t0 + k, c_relu(e));
-        }
+        ys[k] = e;
+        acts[k] = c_relu(e);
       }
+      if (a.raw) sel_st_c(a.raw + (size_t)row * T, t0, T, vec, ys);
+      if (a.act) sel_st_c(a.act + (size_t)row * T, t0, T, vec, acts);
     }
   }
 }
 
 // ------------------------------------------------------------ backward
 template <int NT, int K>
-__global__ void __launch_bounds__(NT) sel_bwd_kernel(const SelArgs a) {
+__global__ void __launch_bounds__(NT, 3) sel_bwd_kernel(const SelArgs a) {
   constexpr int NW = NT / 32, L = NT * K;
   __shared__ float4 s_warp_f[NW];
   __shared__ float4 s_warp_r[NW];
@@ -263,6 +360,7 @@ __global__ void __launch_bounds__(NT) sel_bwd_kernel(const SelArgs a) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int T = a.T;
   const bool prosp = a.o.prospective != 0;
+  const bool vec = a.vec != 0;
   for (int row = blockIdx.x; row < a.rows; row += gridDim.x) {
     const int f = row / a.batch, b = row - f * a.batch;
     const SelChan c = sel_chan(a, f);
@@ -277,13 +375,15 @@ __global__ void __launch_bounds__(NT) sel_bwd_kernel(const SelArgs a) {
       __syncthreads();  // shared slots of the previous tile are free
       const int t0 = jr * L + tid * K;
       float2 z[K], e[K];
-#pragma unroll
-      for (int k = 0; k < K; ++k) z[k] = (t0 + k < T) ? __ldcs(a.z + roff + t0 + k) : cz();
-      const float2 zp = (t0 > 0 && t0 - 1 < T) ? a.z[roff + t0 - 1] : cz();
+      sel_ld_c(a.z + roff, t0, T, vec, z);
+      const float2 zp = sel_prev_z(a.z + roff, t0, T, z[K - 1], lane);
       float gl[K], dl[K], wl[K];
-      sel_load_logits<K>(grow, t0, T, gl);
-      sel_load_logits<K>(drow, t0, T, dl);
-      sel_load_logits<K>(wrow, t0, T, wl);
+      sel_ld_f(grow, t0, T, vec, gl);
+      sel_ld_f(drow, t0, T, vec, dl);
+      sel_ld_f(wrow, t0, T, vec, wl);
+      float2 gyv[K], gxv[K];
+      sel_ld_c(a.gy ? a.gy + roff : nullptr, t0, T, vec, gyv);
+      sel_ld_c(a.gx ? a.gx + roff : nullptr, t0, T, vec, gxv);
       // forward replay of the tile from its stored entry state
       float2 A[K], nn[K], u[K];
 #pragma unroll
@@ -320,11 +420,8 @@ __global__ void __launch_bounds__(NT) sel_bwd_kernel(const SelArgs a) {
       for (int k = 0; k < K; ++k) {
         yprev[k] = ent;
         ent = c_fma(A[k], ent, u[k]);
-        float2 ek = cz();
-        if (t0 + k < T) {
-          if (a.gy) ek = __ldcs(a.gy + roff + t0 + k);
-          if (a.gx) ek = c_add(ek, c_relu_mask(__ldcs(a.gx + roff + t0 + k), ent));
-        }
+        float2 ek = gyv[k];  // zero past T
+        if (a.gx) ek = c_add(ek, c_relu_mask(gxv[k], ent));
         e[k] = ek;
       }
       // neighbours: (A, n) of the sample after each thread's last one
@@ -364,8 +461,19 @@ __global__ void __launch_bounds__(NT) sel_bwd_kernel(const SelArgs a) {
         cta_scan_pair_entry_rev<NT>(gr, h, dcarry, dn, Art, s_warp_r);
         dcarry_next = Art;
       }
-      // per-sample coefficient VJP, in reverse order
+      // per-sample coefficient VJP, in reverse order; results gathered per
+      // thread and stored as 16-byte groups after the loop
       float2 dnext = dn, A1 = An, N1 = Nn;
+      float2 o_dz[K], o_dzw[K];
+      float o_dG[K], o_dD[K], o_dW[K];
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        o_dz[k] = cz();
+        o_dzw[k] = cz();
+        o_dG[k] = 0.f;
+        o_dD[k] = 0.f;
+        o_dW[k] = 0.f;
+      }
 #pragma unroll
       for (int k = K - 1; k >= 0; --k) {
         const int t = t0 + k;
@@ -387,7 +495,7 @@ __global__ void __launch_bounds__(NT) sel_bwd_kernel(const SelArgs a) {
           co.n0 = cz();
           co.ratio = 0.f;
           if (prosp) {
-            co.ratio = a.o.gamma_horizon ? 1.f / ct.g : c.horizon;
+            co.ratio = a.o.gamma_horizon ? sel_rcp(ct.g) : c.horizon;
             const float rg = co.ratio * ct.g;
             co.p0 = make_float2(fmaf(rg, co.A.x, co.p0.x), fmaf(rg, co.A.y, co.p0.y));
             co.n0 = make_float2(-rg * co.A.x, -rg * co.A.y);
@@ -395,8 +503,8 @@ __global__ void __launch_bounds__(NT) sel_bwd_kernel(const SelArgs a) {
           const float2 p = make_float2(ct.gate * co.p0.x, ct.gate * co.p0.y);
           const float2 dzs = c_cfma(p, d, cz());
           const float2 dzwv = prosp ? c_cfma(N1, dnext, dzs) : dzs;
-          __stcs(a.dz + roff + t, a.truncated ? dzs : dzwv);
-          if (a.truncated) __stcs(a.dzw + roff + t, dzwv);
+          o_dz[k] = a.truncated ? dzs : dzwv;
+          o_dzw[k] = dzwv;
           const float2 zk = z[k], zpk = k > 0 ? z[k - 1] : zp;
           const float2 dp = c_cfma(zk, d, cz());
           const float2 dnv = c_cfma(zpk, d, cz());
@@ -422,10 +530,10 @@ __global__ void __launch_bounds__(NT) sel_bwd_kernel(const SelArgs a) {
           if (a.o.has_gamma) {
             if (a.o.log_shift) {
               dbias_e = dgam * ct.g;
-              a.dG[roff + t] = dbias_e * a.o.gamma_scale * (1.f - ct.sig * ct.sig);
+              o_dG[k] = dbias_e * a.o.gamma_scale * (1.f - ct.sig * ct.sig);
             } else {
               dbias_e = dgam * c.span * ct.sig * (1.f - ct.sig);
-              a.dG[roff + t] = dbias_e;
+              o_dG[k] = dbias_e;
             }
           }
           float dtheta_e = dth;
@@ -434,11 +542,11 @@ __global__ void __launch_bounds__(NT) sel_bwd_kernel(const SelArgs a) {
               const float un = c.theta * ct.scale;
               dth = (un >= c.th_lo && un <= c.th_hi) ? dth : 0.f;
             }
-            a.dD[roff + t] = dth * ct.th * a.o.warp_scale * (1.f - ct.warp * ct.warp);
+            o_dD[k] = dth * ct.th * a.o.warp_scale * (1.f - ct.warp * ct.warp);
             dtheta_e = dth * ct.scale;
           }
           if (a.o.has_write)
-            a.dW[roff + t] =
+            o_dW[k] =
                 a.o.write_sigmoid ? dgate * ct.gate * (1.f - ct.gate / a.o.write_max) : dgate;
           acc_bias += dbias_e;
           acc_theta += dtheta_e;
@@ -447,6 +555,11 @@ __global__ void __launch_bounds__(NT) sel_bwd_kernel(const SelArgs a) {
         A1 = A[k];
         N1 = nn[k];
       }
+      sel_st_c(a.dz + roff, t0, T, vec, o_dz);
+      if (a.truncated) sel_st_c(a.dzw + roff, t0, T, vec, o_dzw);
+      if (a.o.has_gamma) sel_st_f(a.dG + roff, t0, T, vec, o_dG);
+      if (a.o.has_warp) sel_st_f(a.dD + roff, t0, T, vec, o_dD);
+      if (a.o.has_write) sel_st_f(a.dW + roff, t0, T, vec, o_dW);
       dcarry = dcarry_next;
       {
         const float4 q = s_first[0];
@@ -475,24 +588,62 @@ __global__ void __launch_bounds__(NT) sel_bwd_kernel(const SelArgs a) {
   }
 }
 
-// dd_group[g, b, t] = sum over channels f of group g of dD[f, b, t], summed in
-// increasing f (deterministic); one thread per (b, t), up to 32 groups.
+// Channels ordered by warp group (stable in f) for the group reduction:
+// order[bounds[g] .. bounds[g+1]) are the channels of group g in increasing f.
+// One warp per group; channels with an out-of-range group (latched as an
+// argument error by the backward kernel) are left out.  One block.
+__global__ void __launch_bounds__(1024)
+    sel_group_order_kernel(const long long *__restrict__ groups, int F, int ngroups,
+                           int *__restrict__ order, int *__restrict__ bounds) {
+  __shared__ int s_count[32];
+  const int g = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int count = 0;
+  if (g < ngroups)
+    for (int f0 = 0; f0 < F; f0 += 32) {
+      const int f = f0 + lane;
+      count += __popc(__ballot_sync(0xffffffffu, f < F && groups[f] == g));
+    }
+  if (lane == 0 && g < 32) s_count[g] = count;
+  __syncthreads();
+  int base = 0;
+  for (int q = 0; q < g && q < ngroups; ++q) base += s_count[q];
+  if (g < ngroups) {
+    if (lane == 0) {
+      bounds[g] = base;
+      if (g == ngroups - 1) bounds[ngroups] = base + count;
+    }
+    for (int f0 = 0; f0 < F; f0 += 32) {
+      const int f = f0 + lane;
+      const bool in = f < F && groups[f] == g;
+      const unsigned m = __ballot_sync(0xffffffffu, in);
+      if (in) order[base + __popc(m & ((1u << lane) - 1u))] = f;
+      base += __popc(m);
+    }
+  }
+}
+
+// dd_group[g, b, t] = sum of dD[f, b, t] over the channels f of group g, in
+// increasing f (deterministic); one thread per (b, t), eight loads in flight.
 __global__ void __launch_bounds__(256)
-    sel_group_reduce_kernel(const float *__restrict__ dD, const long long *__restrict__ groups,
-                            float *__restrict__ out, int F, int ngroups, int64_t BT) {
+    sel_group_reduce_kernel(const float *__restrict__ dD, const int *__restrict__ order,
+                            const int *__restrict__ bounds, float *__restrict__ out, int ngroups,
+                            int64_t BT) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= BT) return;
-  float acc[32];
+  for (int g = 0; g < ngroups; ++g) {
+    const int b0 = bounds[g], b1 = bounds[g + 1];
+    float acc = 0.f;
+    int q = b0;
+    for (; q + 8 <= b1; q += 8) {
+      float v[8];
 #pragma unroll
-  for (int g = 0; g < 32; ++g) acc[g] = 0.f;
-  for (int f = 0; f < F; ++f) {
-    const int g = (int)groups[f];
-    const float v = dD[(int64_t)f * BT + i];
+      for (int u = 0; u < 8; ++u) v[u] = __ldcs(dD + (int64_t)order[q + u] * BT + i);
 #pragma unroll
-    for (int q = 0; q < 32; ++q)
-      if (q == g) acc[q] += v;
+      for (int u = 0; u < 8; ++u) acc += v[u];
+    }
+    for (; q < b1; ++q) acc += __ldcs(dD + (int64_t)order[q] * BT + i);
+    out[(int64_t)g * BT + i] = acc;
   }
-  for (int g = 0; g < ngroups; ++g) out[(int64_t)g * BT + i] = acc[g];
 }
 
 // dbias / dtheta from the per-row sums, summed in double over the batch.
