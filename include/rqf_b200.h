@@ -76,7 +76,10 @@ int rqf_read_device_error(int *out_code, int clear, rqf_stream_t stream);
 int rqf_selftest_lookback_timeout(void *scratch, rqf_stream_t stream);
 
 /* ---- sizes of saved context and scratch ------------------------------ */
-/* BTF kernels: tiles along time, rows = batch * filters. */
+/* BTF kernels: rows = batch * filters; a tile is 1..8 sub-tiles of 128 time
+ * steps, the count chosen from batch * ceil(filters / 32).
+ * rqf_btf_num_tiles gives the 128-step sub-tiles along time (an upper bound
+ * on the tiles); size buffers with rqf_btf_carry_count / _scratch_bytes. */
 int64_t rqf_btf_num_tiles(int64_t time);
 int64_t rqf_btf_carry_count(int64_t batch, int64_t time, int64_t filters);
 size_t rqf_btf_scratch_bytes(int64_t batch, int64_t time, int64_t filters);

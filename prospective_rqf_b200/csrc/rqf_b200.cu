@@ -29,8 +29,9 @@ constexpr int64_t kMaxTickets = 0x7fffffffLL;
 // 16 warps x 8 steps; both tile 128 time steps so they share the carries.
 constexpr int kBtfFwdWarps = 8, kBtfFwdK = 16;
 constexpr int kBtfBwdWarps = 16, kBtfBwdK = 8;
-static_assert(kBtfFwdWarps * kBtfFwdK == kBtfTile, "BTF forward tile");
-static_assert(kBtfBwdWarps * kBtfBwdK == kBtfTile, "BTF backward tile");
+static_assert(kBtfFwdWarps * kBtfFwdK == kBtfSub, "BTF forward sub-tile");
+static_assert(kBtfBwdWarps * kBtfBwdK == kBtfSub, "BTF backward sub-tile");
+
 
 inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 inline size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -50,6 +51,19 @@ inline Scratch scratch_layout(int64_t rows, int64_t ntiles) {
 }
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Sub-tiles per (B,T,F) tile.  A chain (batch x 32-channel block) advances by
+// one look-back hop (~1 us) per tile, so the tiles of all chains together must
+// cover enough data per hop: ngroups * S >= 80 (~5 MB per hop), S = 1..8.
+inline int btf_subtiles(int64_t B, int64_t F) {
+  const int64_t groups = B * ceil_div(F, 32);
+  int s = 1;
+  while (s < kBtfMaxS && groups * s < 80) s *= 2;
+  return s;
+}
+inline int64_t btf_tiles(int64_t B, int64_t T, int64_t F) {
+  return T <= 0 ? 0 : ceil_div(T, (int64_t)kBtfSub * btf_subtiles(B, F));
+}
 
 inline int launch_status() {
   const cudaError_t e = cudaGetLastError();
@@ -143,9 +157,37 @@ FbtArgs fbt_args(const float *c1, const float *tap0, const float *tap1, const fl
 // ------------------------------------------------------------- BTF
 int btf_dims_ok(int64_t B, int64_t T, int64_t F) {
   if (B < 0 || T < 0 || F < 0) return RQF_ERR_SHAPE;
-  if (B > 0 && F > 0 && ceil_div(T, kBtfTile) * B * ceil_div(F, 32) > kMaxTickets)
+  if (B > 0 && F > 0 && btf_tiles(B, T, F) * B * ceil_div(F, 32) > kMaxTickets)
     return RQF_ERR_SHAPE;
   return RQF_OK;
+}
+
+template <int DRIVE>
+void btf_launch_fwd(int S, unsigned grid, int nt, cudaStream_t st, const BtfArgs &a) {
+  switch (S) {
+    case 1: btf_fwd_kernel<kBtfFwdWarps, kBtfFwdK, 1, DRIVE><<<grid, nt, 0, st>>>(a); break;
+    case 2: btf_fwd_kernel<kBtfFwdWarps, kBtfFwdK, 2, DRIVE><<<grid, nt, 0, st>>>(a); break;
+    case 4: btf_fwd_kernel<kBtfFwdWarps, kBtfFwdK, 4, DRIVE><<<grid, nt, 0, st>>>(a); break;
+    default: btf_fwd_kernel<kBtfFwdWarps, kBtfFwdK, 8, DRIVE><<<grid, nt, 0, st>>>(a); break;
+  }
+}
+template <int DRIVE>
+void btf_launch_bwd(int S, unsigned grid, int nt, cudaStream_t st, const BtfArgs &a) {
+  switch (S) {
+    case 1: btf_bwd_kernel<kBtfBwdWarps, kBtfBwdK, 1, DRIVE><<<grid, nt, 0, st>>>(a); break;
+    case 2: btf_bwd_kernel<kBtfBwdWarps, kBtfBwdK, 2, DRIVE><<<grid, nt, 0, st>>>(a); break;
+    case 4: btf_bwd_kernel<kBtfBwdWarps, kBtfBwdK, 4, DRIVE><<<grid, nt, 0, st>>>(a); break;
+    default: btf_bwd_kernel<kBtfBwdWarps, kBtfBwdK, 8, DRIVE><<<grid, nt, 0, st>>>(a); break;
+  }
+}
+template <bool FUSE>
+void btf_launch_tbptt(int S, unsigned grid, int nt, cudaStream_t st, const BtfArgs &a) {
+  switch (S) {
+    case 1: btf_tbptt_bwd_kernel<kBtfBwdWarps, kBtfBwdK, 1, FUSE><<<grid, nt, 0, st>>>(a); break;
+    case 2: btf_tbptt_bwd_kernel<kBtfBwdWarps, kBtfBwdK, 2, FUSE><<<grid, nt, 0, st>>>(a); break;
+    case 4: btf_tbptt_bwd_kernel<kBtfBwdWarps, kBtfBwdK, 4, FUSE><<<grid, nt, 0, st>>>(a); break;
+    default: btf_tbptt_bwd_kernel<kBtfBwdWarps, kBtfBwdK, 8, FUSE><<<grid, nt, 0, st>>>(a); break;
+  }
 }
 
 BtfArgs btf_args(const float *c1, const float *c2, const float *tap1, const void *x,
@@ -164,8 +206,10 @@ BtfArgs btf_args(const float *c1, const float *c2, const float *tap1, const void
   a.T = T;
   a.F = F;
   a.nfb = (int)ceil_div(F, 32);
-  a.ntiles = (int)ceil_div(T, kBtfTile);
-  a.log2L = kBtfLog2Tile;
+  a.ngroups = (int)(B * a.nfb);
+  a.ntiles = (int)btf_tiles(B, T, F);
+  const int S = btf_subtiles(B, F);
+  a.log2L = kBtfLog2Sub + (S == 1 ? 0 : S == 2 ? 1 : S == 4 ? 2 : 3);
   const Scratch lay = scratch_layout(B * F, a.ntiles);
   a.ticket = at<unsigned>(scratch, 0);
   a.flags = at<u64>(scratch, lay.flags_off);
@@ -190,12 +234,13 @@ int btf_forward(int drive, const float *c1, const float *c2, const float *tap1, 
   if ((st = clear_lookback(scratch, lay, stream)) != RQF_OK) return st;
   const unsigned grid = (unsigned)(B * a.nfb * a.ntiles);
   const int nt = kBtfFwdWarps * 32;
+  const int S = btf_subtiles(B, F);
   if (drive == kReal)
-    btf_fwd_kernel<kBtfFwdWarps, kBtfFwdK, kReal><<<grid, nt, 0, stream>>>(a);
+    btf_launch_fwd<kReal>(S, grid, nt, stream, a);
   else if (drive == kPlain)
-    btf_fwd_kernel<kBtfFwdWarps, kBtfFwdK, kPlain><<<grid, nt, 0, stream>>>(a);
+    btf_launch_fwd<kPlain>(S, grid, nt, stream, a);
   else
-    btf_fwd_kernel<kBtfFwdWarps, kBtfFwdK, kTwoTap><<<grid, nt, 0, stream>>>(a);
+    btf_launch_fwd<kTwoTap>(S, grid, nt, stream, a);
   return launch_status();
 }
 
@@ -223,12 +268,13 @@ int btf_backward(int drive, const float *c1, const float *c2, const float *tap1,
   if ((st = clear_lookback(scratch, lay, stream)) != RQF_OK) return st;
   const unsigned grid = (unsigned)(B * a.nfb * a.ntiles);
   const int nt = kBtfBwdWarps * 32;
+  const int S = btf_subtiles(B, F);
   if (drive == kReal)
-    btf_bwd_kernel<kBtfBwdWarps, kBtfBwdK, kReal><<<grid, nt, 0, stream>>>(a);
+    btf_launch_bwd<kReal>(S, grid, nt, stream, a);
   else if (drive == kPlain)
-    btf_bwd_kernel<kBtfBwdWarps, kBtfBwdK, kPlain><<<grid, nt, 0, stream>>>(a);
+    btf_launch_bwd<kPlain>(S, grid, nt, stream, a);
   else
-    btf_bwd_kernel<kBtfBwdWarps, kBtfBwdK, kTwoTap><<<grid, nt, 0, stream>>>(a);
+    btf_launch_bwd<kTwoTap>(S, grid, nt, stream, a);
   if ((st = launch_status()) != RQF_OK) return st;
   reduce_partials_kernel<<<(unsigned)F, 256, 0, stream>>>(
       a.partials, reinterpret_cast<float2 *>(o0), reinterpret_cast<float2 *>(o1),
@@ -294,13 +340,13 @@ int rqf_selftest_lookback_timeout(void *scratch, rqf_stream_t stream) {
 }
 
 // ---------------------------------------------------------------- sizes
-int64_t rqf_btf_num_tiles(int64_t time) { return time <= 0 ? 0 : ceil_div(time, kBtfTile); }
+int64_t rqf_btf_num_tiles(int64_t time) { return time <= 0 ? 0 : ceil_div(time, kBtfSub); }
 int64_t rqf_btf_carry_count(int64_t batch, int64_t time, int64_t filters) {
-  return batch * filters * rqf_btf_num_tiles(time);
+  return batch * filters * btf_tiles(batch, time, filters);
 }
 size_t rqf_btf_scratch_bytes(int64_t batch, int64_t time, int64_t filters) {
   if (batch <= 0 || time <= 0 || filters <= 0) return 256;
-  return scratch_layout(batch * filters, rqf_btf_num_tiles(time)).total;
+  return scratch_layout(batch * filters, btf_tiles(batch, time, filters)).total;
 }
 int64_t rqf_fbt_num_tiles(int64_t time) { return time <= 0 ? 0 : ceil_div(time, kFbtTile); }
 int64_t rqf_fbt_carry_count(int64_t filters, int64_t batch, int64_t time) {
@@ -494,9 +540,9 @@ int rqf_tbptt1_two_tap_backward(int layout, const float *c1, const float *tap0,
     const unsigned grid = (unsigned)(B * a.nfb * a.ntiles);
     const int nt = kBtfBwdWarps * 32;
     if (fuse_act)
-      btf_tbptt_bwd_kernel<kBtfBwdWarps, kBtfBwdK, true><<<grid, nt, 0, stream>>>(a);
+      btf_launch_tbptt<true>(btf_subtiles(B, F), grid, nt, stream, a);
     else
-      btf_tbptt_bwd_kernel<kBtfBwdWarps, kBtfBwdK, false><<<grid, nt, 0, stream>>>(a);
+      btf_launch_tbptt<false>(btf_subtiles(B, F), grid, nt, stream, a);
     if ((st = launch_status()) != RQF_OK) return st;
     reduce_partials_kernel<<<(unsigned)F, 256, 0, stream>>>(
         a.partials, reinterpret_cast<float2 *>(grad_c1), reinterpret_cast<float2 *>(grad_tap0),

@@ -249,8 +249,13 @@ def test_fbt_matches_btf_layout():
 
 
 # ------------------------------------------- (B,T,F) sweeps vs oracle
+# A (B,T,F) tile is S sub-tiles of 128 steps, S from the chain count
+# B * ceil(F / 32): S = 8 below 20 chains, 4 below 40, 2 below 80, else 1.
 BTF_SHAPES = [(1, 1, 1), (2, 63, 5), (2, 128, 32), (3, 129, 33), (2, 1023, 8), (1, 777, 16),
-              (2, 4096, 96), (2, 16000, 32)]
+              (2, 4096, 96), (2, 16000, 32),
+              (10, 2000, 96), (16, 3001, 33),   # 30 / 32 chains: S = 4
+              (45, 700, 32),                    # 45 chains: S = 2
+              (80, 300, 32), (40, 257, 70)]     # 80 / 120 chains: S = 1
 
 
 @pytest.mark.parametrize("B,T,F", BTF_SHAPES)
@@ -326,10 +331,10 @@ def test_config1_exact_shapes():
 
 # ------------------------------------------------------- TBPTT(1)
 @pytest.mark.parametrize("layout", ["btf", "fbt"])
-@pytest.mark.parametrize("T", [1, 5, 2049, 3000])
-def test_tbptt_vs_oracle(layout, T):
-    rng = np.random.default_rng(T + (0 if layout == "btf" else 1))
-    F, B = 6, 3
+@pytest.mark.parametrize("T,B", [(1, 3), (5, 3), (2049, 3), (3000, 3), (1500, 30), (700, 90)])
+def test_tbptt_vs_oracle(layout, T, B):
+    rng = np.random.default_rng(T + B + (0 if layout == "btf" else 1))
+    F = 6
     shape = (B, T, F) if layout == "btf" else (F, B, T)
     c1 = coeffs(rng, F)
     t0, t1 = c64(crandn(rng, F, 0.5)), c64(crandn(rng, F, 0.5))
