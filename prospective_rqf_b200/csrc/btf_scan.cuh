@@ -54,28 +54,27 @@ constexpr int kBtfSub = 128;     // time steps of a sub-tile
 constexpr int kBtfLog2Sub = 7;
 constexpr int kBtfMaxS = 8;      // sub-tiles per tile, at most
 
-template <int DRIVE>
-__device__ __forceinline__ float2 btf_load_x(const void *x, int64_t idx) {
-  if constexpr (DRIVE == kReal) {
-    return make_float2(__ldcs(static_cast<const float *>(x) + idx), 0.f);
-  } else {
-    return __ldcs(static_cast<const float2 *>(x) + idx);
-  }
+// Load policies.  A tile read twice (S > 1) is read in pass 1 with the default
+// policy so that it stays in L2, and in pass 2 (its last use) as streaming
+// (evict-first); a tile read once streams.
+template <typename V>
+__device__ __forceinline__ V btf_ld(const V *p, bool last_use) {
+  return last_use ? __ldcs(p) : __ldcg(p);
 }
-// Second read of a tile in pass 2: the data is in L2, keep the default policy.
 template <int DRIVE>
-__device__ __forceinline__ float2 btf_reload_x(const void *x, int64_t idx) {
+__device__ __forceinline__ float2 btf_load_x(const void *x, int64_t idx, bool last_use) {
   if constexpr (DRIVE == kReal) {
-    return make_float2(static_cast<const float *>(x)[idx], 0.f);
+    return make_float2(btf_ld(static_cast<const float *>(x) + idx, last_use), 0.f);
   } else {
-    return static_cast<const float2 *>(x)[idx];
+    return btf_ld(static_cast<const float2 *>(x) + idx, last_use);
   }
 }
 
 __host__ __device__ constexpr int ilog2(int v) { return v <= 1 ? 0 : 1 + ilog2(v / 2); }
 
-// Drive b[k] = c2 x[k] (+ tap1 x[k-1]) of a warp's K steps starting at tw.
-template <int K, int DRIVE, bool RELOAD>
+// Drive b[k] = c2 x[k] (+ tap1 x[k-1]) of a warp's K steps starting at tw;
+// LAST: this is the tile's last read (see the load policies above).
+template <int K, int DRIVE, bool LAST>
 __device__ __forceinline__ void btf_drive(const BtfArgs &a, int64_t base, int64_t tw, bool fv,
                                           float2 c2, float2 t1, float2 (&x)[K], float2 &xp,
                                           float2 (&b)[K]) {
@@ -83,13 +82,12 @@ __device__ __forceinline__ void btf_drive(const BtfArgs &a, int64_t base, int64_
   for (int k = 0; k < K; ++k) {
     const int64_t t = tw + k;
     const bool in = fv && t < a.T;
-    x[k] = in ? (RELOAD ? btf_reload_x<DRIVE>(a.x, base + t * a.F)
-                        : btf_load_x<DRIVE>(a.x, base + t * a.F))
-              : cz();
+    x[k] = in ? btf_load_x<DRIVE>(a.x, base + t * a.F, LAST) : cz();
   }
   xp = cz();
   if constexpr (DRIVE == kTwoTap) {
-    xp = (fv && tw > 0 && tw - 1 < a.T) ? btf_reload_x<DRIVE>(a.x, base + (tw - 1) * a.F) : cz();
+    xp = (fv && tw > 0 && tw - 1 < a.T) ? btf_load_x<DRIVE>(a.x, base + (tw - 1) * a.F, false)
+                                        : cz();
     b[0] = c_fma(t1, xp, c_mul(c2, x[0]));
 #pragma unroll
     for (int k = 1; k < K; ++k) b[k] = c_fma(t1, x[k - 1], c_mul(c2, x[k]));
@@ -134,7 +132,7 @@ __global__ void __launch_bounds__(NW * 32) btf_fwd_kernel(const BtfArgs a) {
 #pragma unroll 1
   for (int s = 0; s < S; ++s) {
     const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
-    btf_drive<K, DRIVE, false>(a, base, tw, fv, c2, t1, x, xp, b);
+    btf_drive<K, DRIVE, S == 1>(a, base, tw, fv, c2, t1, x, xp, b);
     float2 y = cz();
 #pragma unroll
     for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
@@ -234,11 +232,11 @@ __global__ void __launch_bounds__(NW * 32) btf_bwd_kernel(const BtfArgs a) {
 #pragma unroll 1
   for (int s = 0; s < S; ++s) {
     const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
-    btf_drive<K, DRIVE, false>(a, base, tw, fv, c2, t1, x, xp, b);
+    btf_drive<K, DRIVE, S == 1>(a, base, tw, fv, c2, t1, x, xp, b);
 #pragma unroll
     for (int k = 0; k < K; ++k) {
       const int64_t t = tw + k;
-      go[k] = (fv && t < a.T) ? __ldcs(a.gout + base + t * a.F) : cz();
+      go[k] = (fv && t < a.T) ? btf_ld(a.gout + base + t * a.F, S == 1) : cz();
     }
     float2 y = cz(), h = cz();
 #pragma unroll
@@ -301,7 +299,7 @@ __global__ void __launch_bounds__(NW * 32) btf_bwd_kernel(const BtfArgs a) {
 #pragma unroll
       for (int k = 0; k < K; ++k) {
         const int64_t t = tw + k;
-        go[k] = (fv && t < a.T) ? a.gout[base + t * a.F] : cz();
+        go[k] = (fv && t < a.T) ? __ldcs(a.gout + base + t * a.F) : cz();
       }
       float2 y = cz(), h = cz();
 #pragma unroll
@@ -421,7 +419,7 @@ __global__ void __launch_bounds__(NW * 32) btf_tbptt_bwd_kernel(const BtfArgs a)
   for (int s = 0; s < S; ++s) {
     const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
     float2 x[K], xp, b[K], go[K];
-    btf_drive<K, kTwoTap, S != 1>(a, base, tw, fv, t0, t1, x, xp, b);
+    btf_drive<K, kTwoTap, true>(a, base, tw, fv, t0, t1, x, xp, b);
 #pragma unroll
     for (int k = 0; k < K; ++k) {
       const int64_t t = tw + k;
