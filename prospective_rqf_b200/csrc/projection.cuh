@@ -555,14 +555,23 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 // projection).  B = [h' ; h~'] must be MN-major for a 32-bit operand, so the
 // transform warps transpose the TMA-loaded h' tile into the 32-byte-atom
 // layout while splitting it, writing both halves as hi and lo parts.
+//
+// Two rings.  The TMA lands raw (gz', h') tiles in an 8-deep raw ring; the
+// transform warps turn each into MMA operands in a 2-deep compute ring and
+// release the raw stage at once.  At full size the tile CTAs of one k-split
+// drift apart and their shared rows fall out of L2, so the loads see HBM
+// latency; the raw ring keeps 7 tiles (112 KB) in flight per SM to cover it.
 constexpr int kWgRows = 128;                     // j per tile (A rows) and i per tile
-constexpr int kWgStages = 4;
-constexpr int kWgABytes = kWgRows * kBK * 4;     // 8 KB: gz' raw -> hi (in place); + lo
-constexpr int kWgSrcBytes = kWgRows * kBK * 4;   // 8 KB: h' raw
+constexpr int kWgRawStages = 8;
+constexpr int kWgCompStages = 2;
+constexpr int kWgABytes = kWgRows * kBK * 4;     // 8 KB: gz' tile (raw / hi / lo)
+constexpr int kWgSrcBytes = kWgRows * kBK * 4;   // 8 KB: h' raw tile
 constexpr int kWgBBytes = kBK * kBN * 4;         // 16 KB: one of B_hi / B_lo
-constexpr int kWgStageBytes = 2 * kWgABytes + kWgSrcBytes + 2 * kWgBBytes;  // 56 KB
-constexpr int kWgTxBytes = kWgABytes + kWgSrcBytes;
-constexpr int kWgSmemBytes = kWgStages * kWgStageBytes + kBarBytes + 1024;
+constexpr int kWgRawBytes = kWgABytes + kWgSrcBytes;             // 16 KB
+constexpr int kWgCompBytes = 2 * kWgABytes + 2 * kWgBBytes;      // 48 KB: A_hi A_lo B_hi B_lo
+constexpr int kWgTxBytes = kWgRawBytes;
+constexpr int kWgSmemBytes =
+    kWgRawStages * kWgRawBytes + kWgCompStages * kWgCompBytes + kBarBytes + 1024;
 // TMEM: columns [0, 256) the CTA's running total, [256, 512) the chunk
 // accumulator.  The tensor core's fp32 accumulate rounds with a bias that
 // grows with the number of accumulations into one accumulator (about 2e-4
@@ -587,35 +596,49 @@ __device__ __forceinline__ uint32_t mn32_offset(int c, int k) {
                     ((c & 7) << 2));
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+// 14 warps: 0 TMA, 1 MMA, 2..5 epilogue, 6..13 transform (two per h' row).
+constexpr int kWgThreads = 448;
+constexpr int kWgTransformWarps = 8;
+
+__global__ void __launch_bounds__(kWgThreads, 1)
 proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmH,
                   const WgParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kWgStages * kWgStageBytes);
-  uint64_t *full = bars;
-  uint64_t *ready = bars + kWgStages;
-  uint64_t *empty = bars + 2 * kWgStages;
-  uint64_t *accf = bars + 3 * kWgStages;  // chunk accumulated   (tcgen05.commit)
+  uint8_t *raw = smem;                                    // kWgRawStages x 16 KB
+  uint8_t *comp = smem + kWgRawStages * kWgRawBytes;      // kWgCompStages x 48 KB
+  uint64_t *bars = reinterpret_cast<uint64_t *>(comp + kWgCompStages * kWgCompBytes);
+  uint64_t *rfull = bars;                         // raw tile landed       (1 + tx)
+  uint64_t *rempty = rfull + kWgRawStages;        // raw tile consumed     (8 transform warps)
+  uint64_t *cready = rempty + kWgRawStages;       // operands written      (8 transform warps)
+  uint64_t *cempty = cready + kWgCompStages;      // operands consumed     (tcgen05.commit)
+  uint64_t *accf = cempty + kWgCompStages;  // chunk accumulated   (tcgen05.commit)
   uint64_t *acce = accf + 1;              // chunk folded/drained (4 epilogue warps)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acce + 1);
   volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tile = blockIdx.x / p.splits;
-  const int split = blockIdx.x - tile * p.splits;
+  // tile fastest: the CTAs that share a gz' or h' block over the same k range
+  // are neighbours in launch order and progress together, so the block is
+  // read from HBM once and from L2 by its second user
+  const int ntiles = p.m_tiles * p.i_tiles;
+  const int split = blockIdx.x / ntiles;
+  const int tile = blockIdx.x - split * ntiles;
   const int mt = tile % p.m_tiles;
   const int it = tile / p.m_tiles;
   const long long kb0 = (long long)split * p.kblocks / p.splits;
   const long long kb1 = (long long)(split + 1) * p.kblocks / p.splits;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kWgStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&ready[s], 4);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < kWgRawStages; ++s) {
+      mbar_init(&rfull[s], 1);
+      mbar_init(&rempty[s], kWgTransformWarps);
+    }
+    for (int s = 0; s < kWgCompStages; ++s) {
+      mbar_init(&cready[s], kWgTransformWarps);
+      mbar_init(&cempty[s], 1);
     }
     mbar_init(accf, 1);
     mbar_init(acce, 4);
@@ -642,23 +665,23 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
       int stage = 0, issued = 0;
       uint32_t phase = 0;
       for (long long kb = kb0; kb < kb1; ++kb) {
-        if (!mbar_wait(&empty[stage], phase ^ 1u, abort, 1)) break;
-        uint8_t *st = smem + stage * kWgStageBytes;
-        mbar_expect_tx(&full[stage], kWgTxBytes);
-        tma_load_2d(st, &tmG, &full[stage], (int)(kb * kBK), mt * kWgRows);
-        tma_load_2d(st + 2 * kWgABytes, &tmH, &full[stage], (int)(kb * kBK), it * kWgRows);
+        if (!mbar_wait(&rempty[stage], phase ^ 1u, abort, 1)) break;
+        uint8_t *st = raw + stage * kWgRawBytes;
+        mbar_expect_tx(&rfull[stage], kWgTxBytes);
+        tma_load_2d(st, &tmG, &rfull[stage], (int)(kb * kBK), mt * kWgRows);
+        tma_load_2d(st + kWgABytes, &tmH, &rfull[stage], (int)(kb * kBK), it * kWgRows);
         ++issued;
-        if (++stage == kWgStages) {
+        if (++stage == kWgRawStages) {
           stage = 0;
           phase ^= 1u;
         }
       }
-      for (int i = 0; i < kWgStages && i < issued; ++i) {
+      for (int i = 0; i < kWgRawStages && i < issued; ++i) {
         if (--stage < 0) {
-          stage = kWgStages - 1;
+          stage = kWgRawStages - 1;
           phase ^= 1u;
         }
-        mbar_drain(&full[stage], phase);
+        mbar_drain(&rfull[stage], phase);
       }
     }
   } else if (warp == 1) {
@@ -675,15 +698,15 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
         if (!mbar_wait(acce, cphase ^ 1u, abort, 3)) break;  // previous chunk read out
         tc_fence_after();
         for (long long kb = c0; kb < c1; ++kb) {
-          if (!mbar_wait(&ready[stage], phase, abort, 4)) {
+          if (!mbar_wait(&cready[stage], phase, abort, 4)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t st = smem_u32(smem + stage * kWgStageBytes);
+          const uint32_t st = smem_u32(comp + stage * kWgCompBytes);
           const uint64_t a_hi = smem_desc(st, 16, 512, kSwizzle64B);
           const uint64_t a_lo = smem_desc(st + kWgABytes, 16, 512, kSwizzle64B);
-          const uint32_t bb = st + 2 * kWgABytes + kWgSrcBytes;
+          const uint32_t bb = st + 2 * kWgABytes;
           const uint64_t b_hi = smem_desc(bb, kBK * 128, 512, kSwizzle128BBase32);
           const uint64_t b_lo = smem_desc(bb + kWgBBytes, kBK * 128, 512, kSwizzle128BBase32);
 #pragma unroll
@@ -695,10 +718,10 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
             tc_mma_tf32(d_tmem, a_hi + da, b_lo + db, kIdesc, 1u);
             tc_mma_tf32(d_tmem, a_lo + da, b_hi + db, kIdesc, 1u);
           }
-          tc_commit(&empty[stage]);
-          last = &empty[stage];
+          tc_commit(&cempty[stage]);
+          last = &cempty[stage];
           last_parity = phase;
-          if (++stage == kWgStages) {
+          if (++stage == kWgCompStages) {
             stage = 0;
             phase ^= 1u;
           }
@@ -770,35 +793,48 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
     }
   } else {
     // ---------------------------------------------------------- transform
-    const int t = threadIdx.x - 6 * 32;  // 0..127: also the h' row this thread transposes
-    int stage = 0;
-    uint32_t phase = 0;
+    const int t = threadIdx.x - 6 * 32;  // 0..255
+    const int hr = t & (kWgRows - 1);    // the h' row this thread transposes ...
+    const int kh = (t >> 7) * (kBK / 2); // ... over the steps [kh, kh + 8) of the tile
+    int rs = 0, cs = 0;
+    uint32_t rph = 0, cph = 0;
     for (long long kb = kb0; kb < kb1; ++kb) {
-      if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, abort, 2))) break;
-      uint8_t *st = smem + stage * kWgStageBytes;
-      float4 *ab = reinterpret_cast<float4 *>(st);
-      float4 *al = reinterpret_cast<float4 *>(st + kWgABytes);
+      if (!__all_sync(0xffffffffu, mbar_wait(&rfull[rs], rph, abort, 2))) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&cempty[cs], cph ^ 1u, abort, 2))) break;
+      const uint8_t *rst = raw + rs * kWgRawBytes;
+      uint8_t *cst = comp + cs * kWgCompBytes;
+      // gz': the raw tile is the hi part (copied, keeping its 64-byte swizzle
+      // on a 1024-byte-aligned buffer), plus the lo part
+      const float4 *ar = reinterpret_cast<const float4 *>(rst);
+      float4 *ah = reinterpret_cast<float4 *>(cst);
+      float4 *al = reinterpret_cast<float4 *>(cst + kWgABytes);
 #pragma unroll
-      for (int i = t; i < kWgABytes / 16; i += 128) {
-        const float4 v = ab[i];  // stays in place as the hi part
+      for (int i = t; i < kWgABytes / 16; i += 32 * kWgTransformWarps) {
+        const float4 v = ar[i];
+        ah[i] = v;
         al[i] = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
       }
-      // h' row t: 16 floats in four 16-byte chunks, 64-byte swizzle
-      // (chunk q of row r at q ^ ((r >> 1) & 3)).
-      const uint8_t *src = st + 2 * kWgABytes + t * 64;
-      float x[kBK];
+      // h' row hr, steps [kh, kh + 8): two of the four 16-byte chunks of the
+      // row, 64-byte swizzle (chunk q of row r at q ^ ((r >> 1) & 3))
+      const uint8_t *src = rst + kWgABytes + hr * 64;
+      float x[kBK / 2];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float4 v = *reinterpret_cast<const float4 *>(src + ((q ^ ((t >> 1) & 3)) << 4));
-        x[4 * q] = v.x; x[4 * q + 1] = v.y; x[4 * q + 2] = v.z; x[4 * q + 3] = v.w;
+      for (int q2 = 0; q2 < 2; ++q2) {
+        const int q = (kh >> 2) + q2;
+        const float4 v = *reinterpret_cast<const float4 *>(src + ((q ^ ((hr >> 1) & 3)) << 4));
+        x[4 * q2] = v.x; x[4 * q2 + 1] = v.y; x[4 * q2 + 2] = v.z; x[4 * q2 + 3] = v.w;
       }
-      uint8_t *bh = st + 2 * kWgABytes + kWgSrcBytes;
+      // the raw stage is no longer needed: hand it back to the producer
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rempty[rs]);
+      uint8_t *bh = cst + 2 * kWgABytes;
       uint8_t *bl = bh + kWgBBytes;
 #pragma unroll
-      for (int k = 0; k < kBK; ++k) {
-        const float v = x[k];
-        const float sw = (k & 1) ? x[k - 1] : -x[k + 1];  // h~'
-        const uint32_t o1 = mn32_offset(t, k), o2 = mn32_offset(t + kWgRows, k);
+      for (int kk = 0; kk < kBK / 2; ++kk) {
+        const int k = kh + kk;
+        const float v = x[kk];
+        const float sw = (kk & 1) ? x[kk - 1] : -x[kk + 1];  // h~' (pairs stay in one half)
+        const uint32_t o1 = mn32_offset(hr, k), o2 = mn32_offset(hr + kWgRows, k);
         *reinterpret_cast<float *>(bh + o1) = v;
         *reinterpret_cast<float *>(bl + o1) = tf32_lo(v);
         *reinterpret_cast<float *>(bh + o2) = sw;
@@ -806,10 +842,14 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ready[stage]);
-      if (++stage == kWgStages) {
-        stage = 0;
-        phase ^= 1u;
+      if (lane == 0) mbar_arrive(&cready[cs]);
+      if (++rs == kWgRawStages) {
+        rs = 0;
+        rph ^= 1u;
+      }
+      if (++cs == kWgCompStages) {
+        cs = 0;
+        cph ^= 1u;
       }
     }
   }

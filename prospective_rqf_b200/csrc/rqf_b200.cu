@@ -912,8 +912,15 @@ inline WgGeometry wgrad_geometry(int64_t m, int64_t k, int64_t n, int sms) {
   g.i_tiles = (int)ceil_div(k, proj::kWgRows);
   g.kblocks = ceil_div(2 * n, proj::kBK);
   const int64_t tiles = (int64_t)g.m_tiles * g.i_tiles;
-  int64_t splits = sms > 0 ? sms / tiles : 1;
-  if (splits < 1) splits = 1;
+  // whole waves of CTAs (one per SM), enough of them that no CTA runs more
+  // than ~256 k-blocks: CTAs sharing an operand block then stay close enough
+  // in progress for the block's second read to hit L2
+  int64_t per_wave = sms > 0 ? sms / tiles : 1;
+  if (per_wave < 1) per_wave = 1;
+  int64_t waves = ceil_div(g.kblocks, per_wave * 256);
+  if (waves > 16) waves = 16;
+  if (waves < 1) waves = 1;
+  int64_t splits = per_wave * waves;
   if (splits > g.kblocks) splits = g.kblocks;
   g.splits = (int)splits;
   return g;
@@ -984,7 +991,8 @@ int rqf_projection_weight_grad(const float *gz, const float *x, float *gw, int64
   p.kblocks = g.kblocks;
   p.ld = g.i_tiles * proj::kWgRows;
   const int64_t grid = (int64_t)g.m_tiles * g.i_tiles * g.splits;
-  proj::proj_wgrad_kernel<<<(unsigned)grid, proj::kThreads, proj::kWgSmemBytes, st>>>(tmG, tmH, p);
+  proj::proj_wgrad_kernel<<<(unsigned)grid, proj::kWgThreads, proj::kWgSmemBytes, st>>>(tmG, tmH,
+                                                                                    p);
   if (cudaGetLastError() != cudaSuccess) return RQF_ERR_LAUNCH;
   const int64_t total = m * k;
   const int64_t blocks = ceil_div(total, 256);
