@@ -1,6 +1,12 @@
-"""Informational timing of the reference's own GPU path (its Triton kernels and
-its Pure RQF encoder) beside this backend on the same B200, same shapes, same
-CUDA-event method.  The reference comes from its offline install:
+"""Informational timing of the reference's own paths beside this backend on the
+same machine:
+- its GPU path (its Triton kernels and its Pure RQF encoder) on the same B200,
+  same shapes, same CUDA-event method;
+- its CPU PyTorch path on the box's host cores (config 1: sequential_scan
+  forward + backward on the exact BASELINE tensors; config-2 scale:
+  parallel_scan on one batch row), beside this backend's GPU op.
+
+The reference comes from its offline install:
 
     python -m pip install --no-index --no-build-isolation --no-deps \\
         --find-links /opt/wheelhouse --target baseline/_ref <copy of the reference tree>
@@ -152,11 +158,57 @@ def encoder(out):
         "reference_triton": timed(step(ref), 2, 3), "b200": timed(step(mine), 2, 3)}
 
 
+def cpu_reference(out):
+    """The reference's CPU PyTorch scans, timed on this host (all cores)."""
+    import time
+
+    import prospective_rqf_b200 as ours
+    from rqf_models.ops.scan import parallel_scan, sequential_scan
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    out["host_threads"] = torch.get_num_threads()
+
+    def wall(fn, reps):
+        fn()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        return round((time.perf_counter() - t0) / reps * 1e3, 3)
+
+    # config 1: u real N(0,1) [32,161,128]; lambda = r e^{i theta}, r ~ U(0.90, 0.999),
+    # theta ~ U(0, pi); b ~ CN(0,1); loss sum |y|^2
+    g = torch.Generator().manual_seed(0)
+    B, T, H = 32, 161, 128
+    u = torch.randn(B, T, H, generator=g)
+    r = 0.90 + 0.099 * torch.rand(H, generator=g)
+    lam = torch.polar(r, torch.pi * torch.rand(H, generator=g)).to(torch.complex64)
+    b = (torch.randn(H, generator=g) + 1j * torch.randn(H, generator=g)).to(torch.complex64) / 2 ** 0.5
+
+    def step(op, c1, c2, x):
+        def run():
+            xx = x.detach().requires_grad_(True)
+            c1g, c2g = c1.detach().requires_grad_(True), c2.detach().requires_grad_(True)
+            y = op(c1g, c2g, xx)
+            (y.abs() ** 2).sum().backward()
+        return run
+    cpu_ms = wall(step(sequential_scan, lam, b, u), 3)
+    gpu_ms = timed(step(ours.sequential_scan, lam.to(DEV), b.to(DEV), u.to(DEV)), 3, 10)
+    out["config 1 sequential_scan B32 T161 H128 real u, fwd+bwd"] = {
+        "reference_cpu": cpu_ms, "b200": gpu_ms}
+    # config-2 scale, one batch row: complex u [1,16000,128], parallel_scan (Blelloch)
+    u2 = (torch.randn(1, 16000, 128, generator=g) + 1j * torch.randn(1, 16000, 128, generator=g)).to(torch.complex64)
+    lam2 = torch.polar(0.9 + 0.099 * torch.rand(128, generator=g), torch.pi * torch.rand(128, generator=g)).to(torch.complex64)
+    cpu_ms = wall(step(parallel_scan, lam2, b, u2), 1)
+    gpu_ms = timed(step(ours.parallel_scan, lam2.to(DEV), b.to(DEV), u2.to(DEV)), 3, 10)
+    out["parallel_scan B1 T16000 H128 complex u, fwd+bwd"] = {"reference_cpu": cpu_ms, "b200": gpu_ms}
+
+
 def main():
     out = {"unit": "ms", "device": torch.cuda.get_device_name()}
     scans(out)
     selective(out)
     encoder(out)
+    cpu_reference(out)
     print(json.dumps(out), flush=True)
 
 
