@@ -56,29 +56,47 @@ __device__ __forceinline__ void stage_table(float2 (*s_pw)[kPowTable], int s, bo
   }
 }
 
+// The striped slot v*32 + lane of a warp region swizzles to v*32 + swz(lane)
+// when K <= 8 (the swizzle only mixes bits 3-4 of the slot into bits 0-1), so
+// each lane addresses its slots and samples from one base plus constants.
+// A warp region lying wholly inside the row (every tile but a row's last)
+// takes the copies without per-copy bounds tests.
 template <int K>
 __device__ __forceinline__ void fbt_issue_tile(float4 *wbuf, const float2 *row, int wstart, int T,
                                                int lane) {
+  static_assert(K <= 8, "slot swizzle decomposition needs K <= 8");
+  float4 *dst = wbuf + swz<K>(lane);
+  const float2 *src = row + wstart + 2 * lane;
+  if (wstart + 32 * K <= T) {
 #pragma unroll
-  for (int v = 0; v < K / 2; ++v) {
-    const int t = wstart + 2 * (v * 32 + lane);
-    const bool in = t < T;
-    cp_async16(&wbuf[swz<K>(v * 32 + lane)], row + (in ? t : 0), in);
+    for (int v = 0; v < K / 2; ++v) cp_async16_full(dst + 32 * v, src + 64 * v);
+  } else {
+#pragma unroll
+    for (int v = 0; v < K / 2; ++v) {
+      const bool in = wstart + 2 * lane + 64 * v < T;
+      cp_async16(dst + 32 * v, in ? src + 64 * v : row, in);
+    }
   }
 }
 
 template <int K>
 __device__ __forceinline__ void fbt_store_tile(float4 *wbuf, const float2 (&o)[K], float2 *row,
                                                int wstart, int T, int lane) {
+  static_assert(K <= 8, "slot swizzle decomposition needs K <= 8");
 #pragma unroll
   for (int m = 0; m < K / 2; ++m)
     wbuf[swz<K>(lane * (K / 2) + m)] =
         make_float4(o[2 * m].x, o[2 * m].y, o[2 * m + 1].x, o[2 * m + 1].y);
   __syncwarp();
+  const float4 *sp = wbuf + swz<K>(lane);
+  float2 *dp = row + wstart + 2 * lane;
+  if (wstart + 32 * K <= T) {
 #pragma unroll
-  for (int v = 0; v < K / 2; ++v) {
-    const int t = wstart + 2 * (v * 32 + lane);
-    if (t < T) st_stream4(row + t, wbuf[swz<K>(v * 32 + lane)]);
+    for (int v = 0; v < K / 2; ++v) st_stream4(dp + 64 * v, sp[32 * v]);
+  } else {
+#pragma unroll
+    for (int v = 0; v < K / 2; ++v)
+      if (wstart + 2 * lane + 64 * v < T) st_stream4(dp + 64 * v, sp[32 * v]);
   }
 }
 

@@ -353,6 +353,36 @@ __device__ __forceinline__ void cta_scan_const_rev(float2 a, const float2 *pw, f
   At = Xall;
 }
 
+// Cross-warp step of the constant-gate CTA scans: from the per-warp totals
+// s_warp[0..NW) (each warp spanning 32K samples, gate pw[g0] = lambda^(32K)),
+// Xw = the composition of the warps before this one (after it when REV, gate
+// conj(lambda)) and Xall = the CTA total.  Lanes 0..NW-1 of every warp run a
+// log2(NW)-step shuffle scan (gate pw[g0+d] for distance 2^d) instead of each
+// thread composing all NW totals serially; lanes >= NW hold zero, so the
+// neighbour of the first (last when REV) warp reads zero.
+template <int NW, bool REV>
+__device__ __forceinline__ void warp_totals(const float2 *s_warp, const float2 *pw, int g0,
+                                            float2 &Xw, float2 &Xall) {
+  static_assert(NW >= 1 && NW < 32 && (NW & (NW - 1)) == 0, "NW must be a power of two < 32");
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float2 v = lane < NW ? s_warp[lane] : cz();
+#pragma unroll
+  for (int d = 0; (1 << d) < NW; ++d) {
+    const int o = 1 << d;
+    if constexpr (REV) {
+      const float2 u = shfl_down2(v, o);
+      if (lane + o < NW) v = c_fma(c_conj(pw[g0 + d]), u, v);
+    } else {
+      const float2 u = shfl_up2(v, o);
+      if (lane >= o) v = c_fma(pw[g0 + d], u, v);
+    }
+  }
+  const int src = REV ? warp + 1 : (warp - 1) & 31;
+  Xw = make_float2(__shfl_sync(0xffffffffu, v.x, src), __shfl_sync(0xffffffffu, v.y, src));
+  const int tot = REV ? 0 : NW - 1;
+  Xall = make_float2(__shfl_sync(0xffffffffu, v.x, tot), __shfl_sync(0xffffffffu, v.y, tot));
+}
+
 // Scans for the row-sequential kernels, where the state entering the tile is
 // known before the scan: it is folded into the first thread's aggregate, so
 // the scan directly yields each thread's entry state E and the state after the
@@ -376,13 +406,8 @@ __device__ __forceinline__ void cta_scan_entry_fwd(float2 a, float2 entry, const
   if (lane == 0) ae = cz();
   if (lane == 31) s_warp[warp] = a;
   __syncthreads();
-  const float2 gw = pw[LK + 5];
-  float2 Xw = cz(), Xall = cz();
-#pragma unroll
-  for (int w = 0; w < NW; ++w) {
-    if (w == warp) Xw = Xall;
-    Xall = c_fma(gw, Xall, s_warp[w]);
-  }
+  float2 Xw, Xall;
+  warp_totals<NW, false>(s_warp, pw, LK + 5, Xw, Xall);
   E = threadIdx.x == 0 ? entry : c_fma(lanepow, Xw, ae);
   At = Xall;
 }
@@ -404,15 +429,39 @@ __device__ __forceinline__ void cta_scan_entry_rev(float2 a, float2 entry, const
   if (lane == 31) ae = cz();
   if (lane == 0) s_warp[warp] = a;
   __syncthreads();
-  const float2 gw = c_conj(pw[LK + 5]);
-  float2 Xw = cz(), Xall = cz();
-#pragma unroll
-  for (int w = NW - 1; w >= 0; --w) {
-    if (w == warp) Xw = Xall;
-    Xall = c_fma(gw, Xall, s_warp[w]);
-  }
+  float2 Xw, Xall;
+  warp_totals<NW, true>(s_warp, pw, LK + 5, Xw, Xall);
   E = threadIdx.x == NT - 1 ? entry : c_fma(lanepow, Xw, ae);
   At = Xall;
+}
+
+// Cross-warp step of the time-varying-gate CTA scans: s_warp[w] = (gate, value)
+// of warp w's samples as a float4.  Lanes 0..NW-1 of every warp compose them
+// with a log2(NW)-step shuffle scan; lanes >= NW hold the identity (1, 0).
+// Xw = the value entering this warp, Xall = the CTA total, as warp_totals.
+template <int NW, bool REV>
+__device__ __forceinline__ void warp_pair_totals(const float4 *s_warp, float2 &Xw, float2 &Xall) {
+  static_assert(NW >= 1 && NW < 32 && (NW & (NW - 1)) == 0, "NW must be a power of two < 32");
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float2 g = cone(), v = cz();
+  if (lane < NW) {
+    const float4 q = s_warp[lane];
+    g = make_float2(q.x, q.y);
+    v = make_float2(q.z, q.w);
+  }
+#pragma unroll
+  for (int o = 1; o < NW; o <<= 1) {
+    const float2 gp = REV ? shfl_down2(g, o) : shfl_up2(g, o);
+    const float2 vp = REV ? shfl_down2(v, o) : shfl_up2(v, o);
+    if (REV ? lane + o < NW : lane >= o) {
+      v = c_fma(g, vp, v);
+      g = c_mul(g, gp);
+    }
+  }
+  const int src = REV ? warp + 1 : (warp - 1) & 31;
+  Xw = make_float2(__shfl_sync(0xffffffffu, v.x, src), __shfl_sync(0xffffffffu, v.y, src));
+  const int tot = REV ? 0 : NW - 1;
+  Xall = make_float2(__shfl_sync(0xffffffffu, v.x, tot), __shfl_sync(0xffffffffu, v.y, tot));
 }
 
 // Generic (time-varying gate) counterparts of cta_scan_entry_*: each thread
@@ -440,13 +489,8 @@ __device__ __forceinline__ void cta_scan_pair_entry_fwd(float2 g, float2 a, floa
   }
   if (lane == 31) s_warp[warp] = make_float4(g.x, g.y, a.x, a.y);
   __syncthreads();
-  float2 Xw = cz(), Xall = cz();
-#pragma unroll
-  for (int w = 0; w < NW; ++w) {
-    const float4 q = s_warp[w];
-    if (w == warp) Xw = Xall;
-    Xall = c_fma(make_float2(q.x, q.y), Xall, make_float2(q.z, q.w));
-  }
+  float2 Xw, Xall;
+  warp_pair_totals<NW, false>(s_warp, Xw, Xall);
   E = threadIdx.x == 0 ? entry : c_fma(ge, Xw, ae);
   At = Xall;
 }
@@ -472,13 +516,8 @@ __device__ __forceinline__ void cta_scan_pair_entry_rev(float2 g, float2 a, floa
   }
   if (lane == 0) s_warp[warp] = make_float4(g.x, g.y, a.x, a.y);
   __syncthreads();
-  float2 Xw = cz(), Xall = cz();
-#pragma unroll
-  for (int w = NW - 1; w >= 0; --w) {
-    const float4 q = s_warp[w];
-    if (w == warp) Xw = Xall;
-    Xall = c_fma(make_float2(q.x, q.y), Xall, make_float2(q.z, q.w));
-  }
+  float2 Xw, Xall;
+  warp_pair_totals<NW, true>(s_warp, Xw, Xall);
   E = threadIdx.x == NT - 1 ? entry : c_fma(ge, Xw, ae);
   At = Xall;
 }
@@ -549,6 +588,11 @@ __device__ __forceinline__ void cp_async16(void *smem, const void *gmem, bool pr
   const int n = pred ? 16 : 0;
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(n)
                : "memory");
+}
+// Unpredicated form: the whole 16 bytes are in range.
+__device__ __forceinline__ void cp_async16_full(void *smem, const void *gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
 }
 __device__ __forceinline__ void cp_async8(void *smem, const void *gmem, bool pred) {
   const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
