@@ -76,10 +76,18 @@ int rqf_read_device_error(int *out_code, int clear, rqf_stream_t stream);
 int rqf_selftest_lookback_timeout(void *scratch, rqf_stream_t stream);
 
 /* ---- sizes of saved context and scratch ------------------------------ */
-/* BTF kernels: rows = batch * filters; a tile is 1..8 sub-tiles of 128 time
- * steps, the count chosen from batch * ceil(filters / 32).
- * rqf_btf_num_tiles gives the 128-step sub-tiles along time (an upper bound
- * on the tiles); size buffers with rqf_btf_carry_count / _scratch_bytes. */
+/* BTF kernels: rows = batch * filters.  Two kernel families share the
+ * buffers: a streaming one (tiles of 1..8 x 128 steps, re-read from L2 in a
+ * second pass) for few chains of batch x 32 channels, and a tile-resident one
+ * (tiles of 1..4 x 64 steps held in shared memory, entry states saved per
+ * 64-step sub-tile) for many.  rqf_btf_num_tiles gives the 64-step sub-tiles
+ * along time (an upper bound on the tiles of either family); size buffers
+ * with rqf_btf_carry_count / _scratch_bytes.
+ * rqf_btf_select_path: 0 = automatic (streaming below 48 chains), 1 =
+ * streaming, 2 = tile-resident.  Returns the previous selection, or -1 for an
+ * invalid one.  Process-wide; a forward and its backward must run under the
+ * same selection, since the saved entry states of the two families differ. */
+int rqf_btf_select_path(int path);
 int64_t rqf_btf_num_tiles(int64_t time);
 int64_t rqf_btf_carry_count(int64_t batch, int64_t time, int64_t filters);
 size_t rqf_btf_scratch_bytes(int64_t batch, int64_t time, int64_t filters);
@@ -173,7 +181,9 @@ int rqf_fbt_prospective_backward(const float *c1, const float *tap0,
  * rqf_fbt_prospective_forward (layout 1, FBT).  This replaces the pointwise
  * autograd of the one-step rebuild  C1*h[t-1].detach() + tap0*z[t] +
  * tap1*zw[t-1]  (block.py:946-954) with one kernel, no temporal scan:
- *   g        = grad_out (masked by split-ReLU'(y) when fuse_act)
+ *   g        = grad_out (masked by split-ReLU'(y) when fuse_act; layout 1
+ *              only: the BTF forward has no fused activation, so layout 0
+ *              with fuse_act returns RQF_ERR_ARGUMENT)
  *   grad_z   = conj(tap0) g[t]
  *   grad_zw  = conj(tap1) g[t+1]  (cotangent of the lag source zw = z values)
  *   grad_c1  = sum conj(y[t-1]) g[t], grad_tap0 = sum conj(z[t]) g[t],

@@ -48,6 +48,7 @@ SIGNATURES: dict[str, tuple] = {
     "rqf_status_string": (ctypes.c_char_p, [_int]),
     "rqf_read_device_error": (_int, [ctypes.POINTER(_int), _int, _p]),
     "rqf_selftest_lookback_timeout": (_int, [_p, _p]),
+    "rqf_btf_select_path": (_int, [_int]),
     "rqf_btf_num_tiles": (_i64, [_i64]),
     "rqf_btf_carry_count": (_i64, [_i64, _i64, _i64]),
     "rqf_btf_scratch_bytes": (_sz, [_i64, _i64, _i64]),

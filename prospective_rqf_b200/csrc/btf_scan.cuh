@@ -8,21 +8,35 @@
 //   TWO_TAP  y[t] = c1*y[t-1] + tap0*x[t] + tap1*x[t-1]
 //
 // Work decomposition.  A "chain" is one batch index and a block of 32 adjacent
-// channels (lanes, so every load and store of a time step is one coalesced
-// 256-byte row segment).  A sub-tile is NW warps x K consecutive time steps
-// (128 steps): each lane runs its channel's recurrence serially over its K
-// steps and the warps are composed in shared memory.  A CTA owns a tile of S
-// consecutive sub-tiles: pass 1 streams them to form the tile's aggregate, a
-// per-channel decoupled look-back chains the tiles of a chain, and pass 2
-// re-streams the sub-tiles (from L2: the tile was just read) with their
-// entry states to produce the outputs.  S (1..8) is chosen per call from the
-// number of chains, so that few long chains (config 4: 16 chains of 16,384
-// steps) still keep the look-back hops rare relative to the data they cover.
-// Tickets run tile-major across chains, so resident CTAs work on different
-// chains instead of queueing behind one.
-// Backward recomputes y from the per-tile carries and fuses the adjoint with
-// grad_u / grad_x and the coefficient-gradient partial sums (one partial per
-// tile, reduced in fixed order afterwards).
+// channels: lane = channel, so each time step of a chain is one coalesced
+// 256-byte row.  A sub-tile is 64 time steps of a chain; each of the 8 warps
+// runs its lanes' recurrences serially over 8 consecutive steps and the warps
+// are composed through shared memory.  A tile is S consecutive sub-tiles (the
+// forward S <= 4, the backward S <= 2); the per-tile entry states saved by the
+// forward are kept per sub-tile, so the two directions may tile differently.
+//
+// One CTA per tile, in atomic-ticket order (tile-major across chains, so the
+// resident CTAs spread over the chains and every tile a look-back waits on
+// belongs to a CTA that is already running).  The whole tile is staged in
+// shared memory by cp.async at the start (one commit group per sub-tile, all
+// in flight together), so each sample crosses HBM once and no pass re-reads
+// global memory:
+//   pass 1  per sub-tile, the drive (stored over the input in shared memory
+//           for complex inputs), the warps' aggregates with zero entry, each
+//           thread's prefix over the earlier warps, the sub-tile total;
+//   link    the tile total, a decoupled look-back (several predecessors per
+//           round trip) for the tile's entry, the inclusive prefix, the
+//           sub-tile entry states (saved for the backward);
+//   pass 2  the outputs from the entry states, reading the stored drive.
+// A header of per-channel constants (c1 and its powers from a
+// double-precision table, the drive coefficients, the saved entry states)
+// rides in the first copy group.
+//
+// The backward (tiles in reverse time order) recomputes y from the saved
+// entry states and fuses the adjoint with grad_u / grad_x and the
+// coefficient-gradient partial sums (one partial per tile, reduced in fixed
+// order afterwards).  The TBPTT(1) backward has no adjoint: its sub-tiles are
+// independent, each starting from its saved entry state.
 #pragma once
 
 #include "rqf_common.cuh"
@@ -39,318 +53,460 @@ struct BtfArgs {
   const float2 *gout;  // (B,T,F) cotangent (backward)
   void *out;           // forward: y; backward: grad_x (float for REAL)
   float2 *out2;        // TBPTT backward: grad_zw
-  float2 *carries;     // (B*F, ntiles), row = b*F + f
+  float2 *carries;     // (B*F, nsub): entry state of every sub-tile, row = b*F + f
   float2 *partials;    // (B*F, ntiles, 3)
   u64 *flags;          // (B*F, ntiles, 2)
   unsigned *ticket;
+  const float2 *pw;    // (kBtfPowLevels, F): c1^(2^i)
   int64_t B, T, F;
   int nfb;      // channel blocks of 32
   int ngroups;  // chains: B * nfb
-  int ntiles;   // tiles along time
-  int log2L;    // log2 of the tile length (S sub-tiles)
+  int nsub;     // sub-tiles along time
+  int ntiles;   // tiles of this launch along time: ceil(nsub / S)
+  int S;        // sub-tiles per tile of this launch
+  int log2S;
 };
 
-constexpr int kBtfSub = 128;     // time steps of a sub-tile
-constexpr int kBtfLog2Sub = 7;
-constexpr int kBtfMaxS = 8;      // sub-tiles per tile, at most
+constexpr int kBtfSub = 64;  // time steps of a sub-tile
+constexpr int kBtfLog2Sub = 6;
+constexpr int kBtfWarps = 8;
+constexpr int kBtfK = kBtfSub / kBtfWarps;  // steps per thread
+constexpr int kBtfThreads = kBtfWarps * 32;
+constexpr int kBtfMaxFwdS = 4, kBtfMaxBwdS = 2, kBtfTbpttS = 4;
+constexpr int kBtfPowLevels = kBtfLog2Sub + 3;  // c1^(2^i), i <= log2(64 * 4)
+static_assert(kBtfK == 8, "lambda^(8*warp) is assembled from the 8/16/32 power rows");
 
-// Load policies.  A tile read twice (S > 1) is read in pass 1 with the default
-// policy so that it stays in L2, and in pass 2 (its last use) as streaming
-// (evict-first); a tile read once streams.
-template <typename V>
-__device__ __forceinline__ V btf_ld(const V *p, bool last_use) {
-  return last_use ? __ldcs(p) : __ldcg(p);
-}
+// Header rows (one float2 per lane = channel); kHCarry + s holds the saved
+// entry state of the tile's sub-tile s (backward kinds).
+enum BtfHdr { kHLam = 0, kHC2, kHT1, kHPow8, kHPow16, kHPow32, kHPow64, kHGate, kHCarry };
+
 template <int DRIVE>
-__device__ __forceinline__ float2 btf_load_x(const void *x, int64_t idx, bool last_use) {
-  if constexpr (DRIVE == kReal) {
-    return make_float2(btf_ld(static_cast<const float *>(x) + idx, last_use), 0.f);
+struct BtfElem {
+  using T = float2;
+};
+template <>
+struct BtfElem<kReal> {
+  using T = float;
+};
+
+// One tile: chain (b, 32-channel block) and time tile j.
+struct BtfTile {
+  int64_t b, f0;
+  int j;    // time tile
+  int pos;  // processing position along the chain (look-back order)
+};
+
+__device__ __forceinline__ BtfTile btf_decode(const BtfArgs &a, unsigned tk, bool reverse) {
+  BtfTile t;
+  const int p = (int)(tk / (unsigned)a.ngroups);
+  const int64_t grp = tk - (unsigned)p * (unsigned)a.ngroups;
+  t.b = grp / a.nfb;
+  t.f0 = (grp - t.b * a.nfb) * 32;
+  t.pos = p;
+  t.j = reverse ? a.ntiles - 1 - p : p;
+  return t;
+}
+
+// Tile of this CTA: one atomic ticket, taken by thread 0.
+__device__ __forceinline__ unsigned btf_ticket(const BtfArgs &a, unsigned *s_tk) {
+  if (threadIdx.x == 0) *s_tk = atomicAdd(a.ticket, 1u);
+  __syncthreads();
+  return *s_tk;
+}
+
+// Copy rows [r0, r1) of a (B,T,F) tensor into a shared region of 32-element
+// rows: region row r holds time step t0 + r (zero outside [0, T) and for
+// channels >= F).  VEC: 16-byte copies (F a multiple of the elements per 16
+// bytes and a 16-byte aligned tensor), else one element per copy.
+template <typename E, bool VEC>
+__device__ __forceinline__ void btf_copy_rows(E *dst, const E *src, const BtfArgs &a,
+                                              const BtfTile &tl, int64_t t0, int r0, int r1) {
+  const int tid = threadIdx.x;
+  if constexpr (VEC) {
+    constexpr int PER = 16 / (int)sizeof(E);  // elements per chunk
+    constexpr int CPR = 32 / PER;             // chunks per row
+    constexpr int RSTEP = kBtfThreads / CPR;  // rows per pass of the CTA
+    const int q = tid % CPR;
+    const int64_t f = tl.f0 + (int64_t)q * PER;
+    const bool fv = f < a.F;
+    int r = r0 + tid / CPR;
+    int64_t t = t0 + r;
+    int64_t off = (tl.b * a.T + t) * a.F + f;
+    for (; r < r1; r += RSTEP, t += RSTEP, off += (int64_t)RSTEP * a.F) {
+      const bool ok = fv && t >= 0 && t < a.T;
+      cp_async16(dst + r * 32 + q * PER, ok ? src + off : src, ok);
+    }
   } else {
-    return btf_ld(static_cast<const float2 *>(x) + idx, last_use);
+    const int lane = tid & 31, warp = tid >> 5;
+    const int64_t f = tl.f0 + lane;
+    const bool fv = f < a.F;
+    int r = r0 + warp;
+    int64_t t = t0 + r;
+    int64_t off = (tl.b * a.T + t) * a.F + f;
+    for (; r < r1; r += kBtfWarps, t += kBtfWarps, off += (int64_t)kBtfWarps * a.F) {
+      const bool ok = fv && t >= 0 && t < a.T;
+      if constexpr (sizeof(E) == 8)
+        cp_async8(dst + r * 32 + lane, ok ? src + off : src, ok);
+      else
+        cp_async4(dst + r * 32 + lane, ok ? src + off : src, ok);
+    }
   }
 }
 
-__host__ __device__ constexpr int ilog2(int v) { return v <= 1 ? 0 : 1 + ilog2(v / 2); }
-
-// Drive b[k] = c2 x[k] (+ tap1 x[k-1]) of a warp's K steps starting at tw;
-// LAST: this is the tile's last read (see the load policies above).
-template <int K, int DRIVE, bool LAST>
-__device__ __forceinline__ void btf_drive(const BtfArgs &a, int64_t base, int64_t tw, bool fv,
-                                          float2 c2, float2 t1, float2 (&x)[K], float2 &xp,
-                                          float2 (&b)[K]) {
-#pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const int64_t t = tw + k;
-    const bool in = fv && t < a.T;
-    x[k] = in ? btf_load_x<DRIVE>(a.x, base + t * a.F, LAST) : cz();
+// Header copies: rows kHLam..kHGate (one per warp) and, for NCARRY > 0, the
+// saved entry states of sub-tiles first_sub .. first_sub+NCARRY-1 (warp 0).
+template <int DRIVE, int NCARRY>
+__device__ __forceinline__ void btf_copy_header(float2 *hdr, const BtfArgs &a, const BtfTile &tl,
+                                                int log2_tile, int first_sub) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t f = tl.f0 + lane;
+  const bool fv = f < a.F;
+  const int64_t fc = fv ? f : 0;
+  const float2 *src;
+  bool ok = fv;
+  switch (warp) {
+    case kHLam: src = a.pw + fc; break;
+    case kHC2: src = a.c2 + fc; break;
+    case kHT1:
+      src = DRIVE == kTwoTap ? a.tap1 + fc : a.c2;
+      ok = fv && DRIVE == kTwoTap;
+      break;
+    case kHPow8: src = a.pw + 3 * a.F + fc; break;
+    case kHPow16: src = a.pw + 4 * a.F + fc; break;
+    case kHPow32: src = a.pw + 5 * a.F + fc; break;
+    case kHPow64: src = a.pw + 6 * a.F + fc; break;
+    default: src = a.pw + (int64_t)log2_tile * a.F + fc; break;  // kHGate: lambda^(tile)
   }
-  xp = cz();
-  if constexpr (DRIVE == kTwoTap) {
-    xp = (fv && tw > 0 && tw - 1 < a.T) ? btf_load_x<DRIVE>(a.x, base + (tw - 1) * a.F, false)
-                                        : cz();
-    b[0] = c_fma(t1, xp, c_mul(c2, x[0]));
+  cp_async8(hdr + warp * 32 + lane, src, ok);
+  if (NCARRY > 0 && warp == 0) {
 #pragma unroll
-    for (int k = 1; k < K; ++k) b[k] = c_fma(t1, x[k - 1], c_mul(c2, x[k]));
-  } else {
-#pragma unroll
-    for (int k = 0; k < K; ++k) b[k] = c_mul(c2, x[k]);
+    for (int q = 0; q < NCARRY; ++q) {
+      const bool okc = fv && first_sub + q < a.nsub;
+      cp_async8(hdr + (kHCarry + q) * 32 + lane,
+                okc ? a.carries + (tl.b * a.F + fc) * a.nsub + first_sub + q : a.carries, okc);
+    }
   }
 }
+
+// Per-tile constants of this lane's channel, from the header.
+struct BtfConst {
+  float2 lam, c2, t1, gK, gL, M;
+  float2 Gw;   // lambda^(8*warp): from the sub-tile start to this warp's first step
+  float2 Grw;  // conj(lambda)^(8*(7-warp)): from the sub-tile end back to this warp's end
+};
+__device__ __forceinline__ float2 btf_pow8n(const float2 *hdr, int lane, int n) {
+  float2 g = cone();  // lambda^(8n), n < 8, from the lambda^8/16/32 rows
+  if (n & 1) g = hdr[kHPow8 * 32 + lane];
+  if (n & 2) g = c_mul(g, hdr[kHPow16 * 32 + lane]);
+  if (n & 4) g = c_mul(g, hdr[kHPow32 * 32 + lane]);
+  return g;
+}
+__device__ __forceinline__ BtfConst btf_consts(const float2 *hdr, int lane, int warp) {
+  BtfConst c;
+  c.lam = hdr[kHLam * 32 + lane];
+  c.c2 = hdr[kHC2 * 32 + lane];
+  c.t1 = hdr[kHT1 * 32 + lane];
+  c.gK = hdr[kHPow8 * 32 + lane];
+  c.gL = hdr[kHPow64 * 32 + lane];
+  c.M = hdr[kHGate * 32 + lane];
+  c.Gw = btf_pow8n(hdr, lane, warp);
+  c.Grw = c_conj(btf_pow8n(hdr, lane, kBtfWarps - 1 - warp));
+  return c;
+}
+
+// K + 1 consecutive rows (from row r) of this lane's channel: v[0] is the step
+// before the thread's first.
+template <typename E>
+__device__ __forceinline__ void btf_rows9(const E *rows, int r, int lane, float2 (&v)[kBtfK + 1]) {
+#pragma unroll
+  for (int k = 0; k <= kBtfK; ++k) {
+    if constexpr (sizeof(E) == 4)
+      v[k] = make_float2(rows[(r + k) * 32 + lane], 0.f);
+    else
+      v[k] = rows[(r + k) * 32 + lane];
+  }
+}
+
+template <int DRIVE>
+__device__ __forceinline__ float2 btf_drive1(const BtfConst &c, float2 x, float2 xprev) {
+  return DRIVE == kTwoTap ? c_fma(c.t1, xprev, c_mul(c.c2, x)) : c_mul(c.c2, x);
+}
+
+// Composition of the 8 warps' values v[w] with gate g per warp: sum g^(7-w) v[w].
+__device__ __forceinline__ float2 btf_total8(const float2 (*v)[32], float2 g, int lane) {
+  float2 X = cz();
+#pragma unroll
+  for (int w = 0; w < kBtfWarps; ++w) X = c_fma(g, X, v[w][lane]);
+  return X;
+}
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait_rt(int n) {  // n < N pending groups
+  if constexpr (N > 1) {
+    if (n >= N - 1) {
+      cp_async_wait<N - 1>();
+      return;
+    }
+    cp_async_wait_rt<N - 1>(n);
+  } else {
+    cp_async_wait<0>();
+  }
+}
+
+// Dynamic shared memory of the kernels below (bytes).
+template <int DRIVE, int S>
+__host__ __device__ constexpr size_t btf_fwd_smem() {
+  return (size_t)kHCarry * 32 * sizeof(float2) +
+         (size_t)(kBtfSub * S + 1) * 32 * sizeof(typename BtfElem<DRIVE>::T);
+}
+template <int DRIVE, int S>
+__host__ __device__ constexpr size_t btf_bwd_smem() {
+  return (size_t)(kHCarry + S) * 32 * sizeof(float2) +
+         (size_t)(kBtfSub * S + 1) * 32 * sizeof(typename BtfElem<DRIVE>::T) +
+         (size_t)kBtfSub * S * 32 * sizeof(float2);
+}
+constexpr size_t kBtfTbpttStage = (size_t)(kHCarry + 1) * 32 * sizeof(float2) +
+                                  2 * (size_t)(kBtfSub + 1) * 32 * sizeof(float2);
+constexpr size_t btf_tbptt_smem() { return 2 * kBtfTbpttStage; }
 
 // ------------------------------------------------------------ forward
-template <int NW, int K, int S, int DRIVE>
-__global__ void __launch_bounds__(NW * 32) btf_fwd_kernel(const BtfArgs a) {
-  constexpr int L = NW * K;  // sub-tile
-  static_assert(L == kBtfSub, "sub-tile length");
-  __shared__ float2 s_y[2][NW][32];
-  __shared__ float2 s_sub[S][32];
-  __shared__ float2 s_C[32];
-  __shared__ unsigned s_ticket;
+template <int DRIVE, bool VECX, int S>
+__global__ void __launch_bounds__(kBtfThreads, 3) btf_fwd_kernel(const BtfArgs a) {
+  using E = typename BtfElem<DRIVE>::T;
+  extern __shared__ __align__(16) unsigned char btf_dsm[];
+  __shared__ float2 s_y[2][kBtfWarps][32];
+  __shared__ float2 s_X[S][32];
+  __shared__ float2 s_C[S][32];
+  __shared__ float2 s_xl[32];  // TWO_TAP: x of the last step of the previous sub-tile
+  __shared__ unsigned s_tk;
+  constexpr bool STORE_B = DRIVE != kReal;  // the drive replaces x in shared memory
+  float2 *hdr = reinterpret_cast<float2 *>(btf_dsm);
+  E *xs = reinterpret_cast<E *>(btf_dsm + (size_t)kHCarry * 32 * sizeof(float2));
+  float2 *bs = reinterpret_cast<float2 *>(xs);  // the drive, when STORE_B
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) s_ticket = atomicAdd(a.ticket, 1u);
-  __syncthreads();
-  const unsigned tk = s_ticket;
-  const int j = (int)(tk / (unsigned)a.ngroups);
-  const int64_t grp = tk - (unsigned)j * (unsigned)a.ngroups;
-  const int64_t bi = grp / a.nfb;
-  const int64_t f = (grp - bi * a.nfb) * 32 + lane;
-  const bool fv = f < a.F;
-  const float2 lam = fv ? a.c1[f] : cz();
-  const float2 c2 = fv ? a.c2[f] : cz();
-  const float2 t1 = (DRIVE == kTwoTap && fv) ? a.tap1[f] : cz();
-  const int64_t base = bi * a.T * a.F + f;  // element (bi, t, f) = base + t*F
-  const int64_t tile0 = (int64_t)j * S * L;
-  const float2 gK = c_pow2k(lam, ilog2(K));
-  const float2 gL = c_pow2k(lam, kBtfLog2Sub);
-  float2 Gw = cone();  // lam^(K*warp): gain from this warp's start back to the sub-tile start
-  for (int w = 0; w < warp; ++w) Gw = c_mul(gK, Gw);
+  const BtfTile tl = btf_decode(a, btf_ticket(a, &s_tk), false);
+  const int64_t ts0 = (int64_t)tl.j * S * kBtfSub;  // first step of the tile; row r = step ts0-1+r
 
-  // pass 1: sub-tile aggregates (zero entry), composed into the tile's.  With
-  // one sub-tile (S == 1) the drive stays in registers for pass 2.
-  float2 Xtile = cz();
-  float2 x[K], xp, b[K];
-#pragma unroll 1
+#pragma unroll
   for (int s = 0; s < S; ++s) {
-    const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
-    btf_drive<K, DRIVE, S == 1>(a, base, tw, fv, c2, t1, x, xp, b);
+    if (s == 0) btf_copy_header<DRIVE, 0>(hdr, a, tl, kBtfLog2Sub + a.log2S, 0);
+    btf_copy_rows<E, VECX>(xs, static_cast<const E *>(a.x), a, tl, ts0 - 1,
+                           s > 0 ? kBtfSub * s + 1 : (DRIVE == kTwoTap ? 0 : 1),
+                           kBtfSub * (s + 1) + 1);
+    cp_async_commit();
+  }
+
+  BtfConst c{};
+  float2 Xw[S];
+  const int rw = warp * kBtfK;  // row of the step before this thread's first (in a sub-tile)
+#pragma unroll
+  for (int s = 0; s < S; ++s) {
+    cp_async_wait_rt<S>(S - 1 - s);
+    __syncthreads();
+    if (s == 0) c = btf_consts(hdr, lane, warp);
+    float2 v[kBtfK + 1];
+    btf_rows9(xs, kBtfSub * s + rw, lane, v);
+    if (DRIVE == kTwoTap && s > 0 && warp == 0) v[0] = s_xl[lane];
+    float2 b[kBtfK];
+#pragma unroll
+    for (int k = 0; k < kBtfK; ++k) b[k] = btf_drive1<DRIVE>(c, v[k + 1], v[k]);
     float2 y = cz();
 #pragma unroll
-    for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
+    for (int k = 0; k < kBtfK; ++k) y = c_fma(c.lam, y, b[k]);
     s_y[s & 1][warp][lane] = y;
-    __syncthreads();
-    float2 X = cz();
+    __syncthreads();  // aggregates complete; every x of this sub-tile has been read
+    if constexpr (STORE_B) {
 #pragma unroll
-    for (int w = 0; w < NW; ++w) X = c_fma(gK, X, s_y[s & 1][w][lane]);
-    if (warp == 0) s_sub[s][lane] = X;
-    Xtile = c_fma(gL, Xtile, X);
-  }
-  if (warp == 0) {
-    float2 C = cz();
-    if (fv) {
-      const int64_t row = bi * a.F + f;
-      u64 *fl = a.flags + row * (int64_t)a.ntiles * 2;
-      const bool has_next = j + 1 < a.ntiles;
-      if (j == 0) {
-        if (has_next) flag_publish2(fl, Xtile, kInclusive);
-      } else {
-        if (has_next) flag_publish2(fl + 2 * j, Xtile, kAggregate);
-        const float2 M = c_pow2k(lam, a.log2L);
-        C = lookback_const(fl, j, M);
-        if (has_next) flag_publish2(fl + 2 * j, c_fma(M, C, Xtile), kInclusive);
-      }
-      a.carries[row * a.ntiles + j] = C;
+      for (int k = 0; k < kBtfK; ++k) bs[(kBtfSub * s + rw + 1 + k) * 32 + lane] = b[k];
+      if (DRIVE == kTwoTap && warp == kBtfWarps - 1) s_xl[lane] = v[kBtfK];
     }
-    s_C[lane] = C;
+    float2 X = cz();
+    for (int w = 0; w < warp; ++w) X = c_fma(c.gK, X, s_y[s & 1][w][lane]);
+    Xw[s] = X;
+    if (warp == (s & 7)) s_X[s][lane] = btf_total8(s_y[s & 1], c.gK, lane);
   }
   __syncthreads();
-
-  // pass 2: outputs, sub-tile by sub-tile from their entry states
-  float2 es = s_C[lane];
-  float2 *yout = static_cast<float2 *>(a.out);
+  const int64_t f = tl.f0 + lane;
+  if (warp == 0) {  // link: tile total, look-back, entry states of the sub-tiles
+    float2 XT = cz();
+#pragma unroll
+    for (int s = 0; s < S; ++s) XT = c_fma(c.gL, XT, s_X[s][lane]);
+    float2 C = cz();
+    if (f < a.F) {
+      const int64_t row = tl.b * a.F + f;
+      u64 *fl = a.flags + row * (int64_t)a.ntiles * 2;
+      const bool has_next = tl.j + 1 < a.ntiles;
+      if (tl.j == 0) {
+        if (has_next) flag_publish2(fl, XT, kInclusive);
+      } else {
+        if (has_next) flag_publish2(fl + 2 * tl.j, XT, kAggregate);
+        C = lookback_const_win(fl, tl.j, c.M);
+        if (has_next) flag_publish2(fl + 2 * tl.j, c_fma(c.M, C, XT), kInclusive);
+      }
+    }
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+      s_C[s][lane] = C;
+      const int sub = tl.j * S + s;
+      if (f < a.F && sub < a.nsub) a.carries[(tl.b * a.F + f) * a.nsub + sub] = C;
+      C = c_fma(c.gL, C, s_X[s][lane]);
+    }
+  }
+  __syncthreads();
+  // pass 2: outputs
+  if (f < a.F) {
+    float2 *yo = static_cast<float2 *>(a.out) + (tl.b * a.T + ts0 + rw) * a.F + f;
 #pragma unroll 1
-  for (int s = 0; s < S; ++s) {
-    const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
-    if constexpr (S > 1) {
-      btf_drive<K, DRIVE, true>(a, base, tw, fv, c2, t1, x, xp, b);
-      float2 y = cz();
+    for (int s = 0; s < S; ++s, yo += (int64_t)kBtfSub * a.F) {
+      float2 e = c_fma(c.Gw, s_C[s][lane], Xw[s]);
+      const int64_t left = a.T - (ts0 + kBtfSub * s + rw);
+      const int kmax = left < kBtfK ? (int)left : kBtfK;
+      float2 b[kBtfK];
+      if constexpr (STORE_B) {
 #pragma unroll
-      for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
-      s_y[s & 1][warp][lane] = y;
-      __syncthreads();
-    }
-    float2 Xw = cz();
-    for (int w = 0; w < warp; ++w) Xw = c_fma(gK, Xw, s_y[s & 1][w][lane]);
-    float2 e = c_fma(Gw, es, Xw);
+        for (int k = 0; k < kBtfK; ++k) b[k] = bs[(kBtfSub * s + rw + 1 + k) * 32 + lane];
+      } else {
+        float2 v[kBtfK + 1];
+        btf_rows9(xs, kBtfSub * s + rw, lane, v);
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-      e = c_fma(lam, e, b[k]);
-      const int64_t t = tw + k;
-      if (fv && t < a.T) __stcs(yout + base + t * a.F, e);
+        for (int k = 0; k < kBtfK; ++k) b[k] = btf_drive1<DRIVE>(c, v[k + 1], v[k]);
+      }
+      float2 *p = yo;
+#pragma unroll
+      for (int k = 0; k < kBtfK; ++k, p += a.F) {
+        e = c_fma(c.lam, e, b[k]);
+        if (k < kmax) __stcs(p, e);
+      }
     }
-    es = c_fma(gL, es, s_sub[s][lane]);
   }
 }
 
 // ------------------------------------------------------------ backward
-template <int NW, int K, int S, int DRIVE>
-__global__ void __launch_bounds__(NW * 32) btf_bwd_kernel(const BtfArgs a) {
-  constexpr int L = NW * K;
-  static_assert(L == kBtfSub, "sub-tile length");
-  __shared__ float4 s_yh[2][NW][32];   // (forward local y, reverse local h) per warp
-  __shared__ float4 s_sub[S][32];      // (forward, reverse) sub-tile aggregates
-  __shared__ float2 s_red[3][NW][32];
+// Tiles run in reverse time order (processing position p = tile ntiles-1-p).
+template <int DRIVE, bool VECX, bool VECG, int S>
+__global__ void __launch_bounds__(kBtfThreads, 2) btf_bwd_kernel(const BtfArgs a) {
+  using E = typename BtfElem<DRIVE>::T;
+  extern __shared__ __align__(16) unsigned char btf_dsm[];
+  __shared__ float4 s_yh[S][kBtfWarps][32];  // (forward y, reverse h) per warp
+  __shared__ float2 s_H[S][32];               // reverse sub-tile totals
   __shared__ float2 s_D[32];
-  __shared__ unsigned s_ticket;
+  __shared__ float2 s_red[3][kBtfWarps][32];
+  __shared__ unsigned s_tk;
+  float2 *hdr = reinterpret_cast<float2 *>(btf_dsm);
+  E *xs = reinterpret_cast<E *>(btf_dsm + (size_t)(kHCarry + S) * 32 * sizeof(float2));
+  float2 *gs = reinterpret_cast<float2 *>(reinterpret_cast<unsigned char *>(xs) +
+                                          (size_t)(kBtfSub * S + 1) * 32 * sizeof(E));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) s_ticket = atomicAdd(a.ticket, 1u);
-  __syncthreads();
-  const unsigned tk = s_ticket;
-  const int p = (int)(tk / (unsigned)a.ngroups);
-  const int64_t grp = tk - (unsigned)p * (unsigned)a.ngroups;
-  const int j = a.ntiles - 1 - p;
-  const int64_t bi = grp / a.nfb;
-  const int64_t f = (grp - bi * a.nfb) * 32 + lane;
-  const bool fv = f < a.F;
-  const int64_t row = bi * a.F + f;
-  const float2 lam = fv ? a.c1[f] : cz();
-  const float2 c2 = fv ? a.c2[f] : cz();
-  const float2 t1 = (DRIVE == kTwoTap && fv) ? a.tap1[f] : cz();
-  const float2 C = fv ? a.carries[row * a.ntiles + j] : cz();
-  const int64_t base = bi * a.T * a.F + f;
-  const int64_t tile0 = (int64_t)j * S * L;
-  const float2 mu = c_conj(lam);
-  const float2 gK = c_pow2k(lam, ilog2(K)), muK = c_conj(gK);
-  const float2 gL = c_pow2k(lam, kBtfLog2Sub), muL = c_conj(gL);
-  float2 Gw = cone(), Grw = cone();  // lam^(K*warp), conj(lam)^(K*(NW-1-warp))
-  for (int w = 0; w < warp; ++w) Gw = c_mul(gK, Gw);
-  for (int w = NW - 1; w > warp; --w) Grw = c_mul(muK, Grw);
+  const BtfTile tl = btf_decode(a, btf_ticket(a, &s_tk), true);
+  const int64_t ts0 = (int64_t)tl.j * S * kBtfSub;
 
-  // pass 1: forward and reverse sub-tile aggregates.  With one sub-tile
-  // (S == 1) the loaded values and the warp exchange stay for pass 2.
-  float2 Xrtile = cz(), pw = cone();
-  float2 x[K], xp, b[K], go[K];
-#pragma unroll 1
-  for (int s = 0; s < S; ++s) {
-    const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
-    btf_drive<K, DRIVE, S == 1>(a, base, tw, fv, c2, t1, x, xp, b);
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-      const int64_t t = tw + k;
-      go[k] = (fv && t < a.T) ? btf_ld(a.gout + base + t * a.F, S == 1) : cz();
-    }
+  for (int s = 0; s < S; ++s) {
+    if (s == 0) btf_copy_header<DRIVE, S>(hdr, a, tl, kBtfLog2Sub + a.log2S, tl.j * S);
+    btf_copy_rows<E, VECX>(xs, static_cast<const E *>(a.x), a, tl, ts0 - 1,
+                           s > 0 ? kBtfSub * s + 1 : (DRIVE == kTwoTap ? 0 : 1),
+                           kBtfSub * (s + 1) + 1);
+    btf_copy_rows<float2, VECG>(gs, a.gout, a, tl, ts0, kBtfSub * s, kBtfSub * (s + 1));
+    cp_async_commit();
+  }
+
+  BtfConst c{};
+  const int rw = warp * kBtfK;
+#pragma unroll
+  for (int s = 0; s < S; ++s) {
+    cp_async_wait_rt<S>(S - 1 - s);
+    __syncthreads();
+    if (s == 0) c = btf_consts(hdr, lane, warp);
+    float2 v[kBtfK + 1];
+    btf_rows9(xs, kBtfSub * s + rw, lane, v);
     float2 y = cz(), h = cz();
 #pragma unroll
-    for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
+    for (int k = 0; k < kBtfK; ++k) y = c_fma(c.lam, y, btf_drive1<DRIVE>(c, v[k + 1], v[k]));
+    const float2 mu = c_conj(c.lam);
 #pragma unroll
-    for (int k = K - 1; k >= 0; --k) h = c_fma(mu, h, go[k]);
-    s_yh[s & 1][warp][lane] = make_float4(y.x, y.y, h.x, h.y);
-    __syncthreads();
-    float2 X = cz(), Xr = cz();
-#pragma unroll
-    for (int w = 0; w < NW; ++w) {
-      const float4 q = s_yh[s & 1][w][lane];
-      X = c_fma(gK, X, make_float2(q.x, q.y));
-    }
-#pragma unroll
-    for (int w = NW - 1; w >= 0; --w) {
-      const float4 q = s_yh[s & 1][w][lane];
-      Xr = c_fma(muK, Xr, make_float2(q.z, q.w));
-    }
-    if (warp == 0) s_sub[s][lane] = make_float4(X.x, X.y, Xr.x, Xr.y);
-    Xrtile = c_fma(pw, Xr, Xrtile);  // sub-tile s starts L*s steps into the tile
-    pw = c_mul(muL, pw);
+    for (int k = kBtfK - 1; k >= 0; --k) h = c_fma(mu, h, gs[(kBtfSub * s + rw + k) * 32 + lane]);
+    s_yh[s][warp][lane] = make_float4(y.x, y.y, h.x, h.y);
   }
-  if (warp == 0) {
+  __syncthreads();
+  const float2 mu = c_conj(c.lam), muK = c_conj(c.gK), muL = c_conj(c.gL);
+  if (warp < S) {  // reverse sub-tile totals
+    float2 H = cz();
+#pragma unroll
+    for (int w = kBtfWarps - 1; w >= 0; --w)
+      H = c_fma(muK, H, make_float2(s_yh[warp][w][lane].z, s_yh[warp][w][lane].w));
+    s_H[warp][lane] = H;
+  }
+  __syncthreads();
+  const int64_t f = tl.f0 + lane;
+  const bool fv = f < a.F;
+  if (warp == 0) {  // link: reverse tile total (sub-tile q sits 64q steps in), look-back
+    float2 HT = s_H[S - 1][lane];
+#pragma unroll
+    for (int q = S - 2; q >= 0; --q) HT = c_fma(muL, HT, s_H[q][lane]);
     float2 D = cz();
     if (fv) {
+      const int64_t row = tl.b * a.F + f;
       u64 *fl = a.flags + row * (int64_t)a.ntiles * 2;
-      const bool has_next = p + 1 < a.ntiles;
-      if (p == 0) {
-        if (has_next) flag_publish2(fl, Xrtile, kInclusive);
+      const bool has_next = tl.pos + 1 < a.ntiles;
+      const float2 Mr = c_conj(c.M);
+      if (tl.pos == 0) {
+        if (has_next) flag_publish2(fl, HT, kInclusive);
       } else {
-        if (has_next) flag_publish2(fl + 2 * p, Xrtile, kAggregate);
-        const float2 M = c_pow2k(mu, a.log2L);
-        D = lookback_const(fl, p, M);
-        if (has_next) flag_publish2(fl + 2 * p, c_fma(M, D, Xrtile), kInclusive);
+        if (has_next) flag_publish2(fl + 2 * tl.pos, HT, kAggregate);
+        D = lookback_const_win(fl, tl.pos, Mr);
+        if (has_next) flag_publish2(fl + 2 * tl.pos, c_fma(Mr, D, HT), kInclusive);
       }
     }
     s_D[lane] = D;
   }
   __syncthreads();
-
-  // sub-tile entry states: forward C_s from the tile carry, reverse D_s (the
-  // adjoint entering sub-tile s from its right) from the look-back
-  float2 Cs[S];
-  Cs[0] = C;
-#pragma unroll
-  for (int s = 1; s < S; ++s) {
-    const float4 q = s_sub[s - 1][lane];
-    Cs[s] = c_fma(gL, Cs[s - 1], make_float2(q.x, q.y));
-  }
-  float2 Ds = s_D[lane];
-
-  // pass 2: sub-tiles from last to first
+  float2 Ds = s_D[lane];  // adjoint entering the last sub-tile from its right
   float2 acc_c1 = cz(), acc_1 = cz(), acc_2 = cz();
 #pragma unroll 1
   for (int s = S - 1; s >= 0; --s) {
-    const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
-    if constexpr (S > 1) {
-      btf_drive<K, DRIVE, true>(a, base, tw, fv, c2, t1, x, xp, b);
-#pragma unroll
-      for (int k = 0; k < K; ++k) {
-        const int64_t t = tw + k;
-        go[k] = (fv && t < a.T) ? __ldcs(a.gout + base + t * a.F) : cz();
-      }
-      float2 y = cz(), h = cz();
-#pragma unroll
-      for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
-#pragma unroll
-      for (int k = K - 1; k >= 0; --k) h = c_fma(mu, h, go[k]);
-      s_yh[s & 1][warp][lane] = make_float4(y.x, y.y, h.x, h.y);
-      __syncthreads();
-    }
     float2 Xw = cz(), Xrw = cz();
-    for (int w = 0; w < warp; ++w) {
-      const float4 q = s_yh[s & 1][w][lane];
-      Xw = c_fma(gK, Xw, make_float2(q.x, q.y));
-    }
-    for (int w = NW - 1; w > warp; --w) {
-      const float4 q = s_yh[s & 1][w][lane];
-      Xrw = c_fma(muK, Xrw, make_float2(q.z, q.w));
-    }
-    float2 e = c_fma(Gw, Cs[s], Xw);
-    float2 yprev[K];
+    for (int w = 0; w < warp; ++w)
+      Xw = c_fma(c.gK, Xw, make_float2(s_yh[s][w][lane].x, s_yh[s][w][lane].y));
+    for (int w = kBtfWarps - 1; w > warp; --w)
+      Xrw = c_fma(muK, Xrw, make_float2(s_yh[s][w][lane].z, s_yh[s][w][lane].w));
+    float2 e = c_fma(c.Gw, hdr[(kHCarry + s) * 32 + lane], Xw);
+    float2 gnext = c_fma(c.Grw, Ds, Xrw);
+    float2 v[kBtfK + 1];
+    btf_rows9(xs, kBtfSub * s + rw, lane, v);
+    float2 yprev[kBtfK];
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
+    for (int k = 0; k < kBtfK; ++k) {
       yprev[k] = e;
-      e = c_fma(lam, e, b[k]);
+      e = c_fma(c.lam, e, btf_drive1<DRIVE>(c, v[k + 1], v[k]));
     }
-    float2 gnext = c_fma(Grw, Ds, Xrw);
+    const int64_t t0 = ts0 + kBtfSub * s + rw;
+    const int64_t left = a.T - t0;
+    const int kmax = !fv ? 0 : (left < kBtfK ? (int)left : kBtfK);
+    const int64_t obase = (tl.b * a.T + t0) * a.F + f;
 #pragma unroll
-    for (int k = K - 1; k >= 0; --k) {
-      const float2 g = c_fma(mu, gnext, go[k]);
-      const int64_t t = tw + k;
-      const bool in = fv && t < a.T;
+    for (int k = kBtfK - 1; k >= 0; --k) {
+      const float2 g = c_fma(mu, gnext, gs[(kBtfSub * s + rw + k) * 32 + lane]);
       if constexpr (DRIVE == kReal) {
         // grad of the real input: Re(conj(c2) g)
-        if (in) __stcs(static_cast<float *>(a.out) + base + t * a.F, c2.x * g.x + c2.y * g.y);
-        acc_1 = make_float2(fmaf(x[k].x, g.x, acc_1.x), fmaf(x[k].x, g.y, acc_1.y));
+        if (k < kmax)
+          __stcs(static_cast<float *>(a.out) + obase + k * a.F, c.c2.x * g.x + c.c2.y * g.y);
+        acc_1 = make_float2(fmaf(v[k + 1].x, g.x, acc_1.x), fmaf(v[k + 1].x, g.y, acc_1.y));
       } else if constexpr (DRIVE == kPlain) {
-        if (in) __stcs(static_cast<float2 *>(a.out) + base + t * a.F, c_cfma(c2, g, cz()));
-        acc_1 = c_cfma(x[k], g, acc_1);
+        if (k < kmax) __stcs(static_cast<float2 *>(a.out) + obase + k * a.F, c_cfma(c.c2, g, cz()));
+        acc_1 = c_cfma(v[k + 1], g, acc_1);
       } else {
-        if (in)
-          __stcs(static_cast<float2 *>(a.out) + base + t * a.F,
-                 c_cfma(t1, gnext, c_cfma(c2, g, cz())));
-        acc_1 = c_cfma(x[k], g, acc_1);
-        acc_2 = c_cfma(k > 0 ? x[k - 1] : xp, g, acc_2);
+        if (k < kmax)
+          __stcs(static_cast<float2 *>(a.out) + obase + k * a.F,
+                 c_cfma(c.t1, gnext, c_cfma(c.c2, g, cz())));
+        acc_1 = c_cfma(v[k + 1], g, acc_1);
+        acc_2 = c_cfma(v[k], g, acc_2);
       }
       acc_c1 = c_cfma(yprev[k], g, acc_c1);
       gnext = g;
     }
-    const float4 q = s_sub[s][lane];
-    Ds = c_fma(muL, Ds, make_float2(q.z, q.w));  // adjoint entering sub-tile s-1
+    if (s > 0) Ds = c_fma(muL, Ds, s_H[s][lane]);  // adjoint entering sub-tile s-1 from its right
   }
+  // per-tile partial sums, fixed order over the warps
   s_red[0][warp][lane] = acc_c1;
   s_red[1][warp][lane] = acc_1;
   s_red[2][warp][lane] = acc_2;
@@ -358,120 +514,95 @@ __global__ void __launch_bounds__(NW * 32) btf_bwd_kernel(const BtfArgs a) {
   if (warp < 3 && fv) {
     float2 sum = cz();
 #pragma unroll
-    for (int w = 0; w < NW; ++w) sum = c_add(sum, s_red[warp][w][lane]);
-    a.partials[(row * a.ntiles + j) * 3 + warp] = sum;
+    for (int w = 0; w < kBtfWarps; ++w) sum = c_add(sum, s_red[warp][w][lane]);
+    a.partials[((tl.b * a.F + f) * a.ntiles + tl.j) * 3 + warp] = sum;
   }
 }
 
-// TBPTT(1) surrogate backward in (B,T,F) layout (no temporal adjoint).  One
-// CTA per (tile, chain) in blockIdx order; pass 1 forms the forward sub-tile
-// aggregates so that pass 2 can start every sub-tile from its entry state.
-template <int NW, int K, int S, bool FUSE_ACT>
-__global__ void __launch_bounds__(NW * 32) btf_tbptt_bwd_kernel(const BtfArgs a) {
-  constexpr int L = NW * K;
-  static_assert(L == kBtfSub, "sub-tile length");
-  __shared__ float2 s_y[2][NW][32];
-  __shared__ float2 s_sub[S][32];
-  __shared__ float2 s_first[2][NW + 1][32];
-  __shared__ float2 s_red[3][NW][32];
+// TBPTT(1) surrogate backward in (B,T,F) layout: no temporal adjoint, so the
+// sub-tiles are independent, each starting from its saved entry state.  A CTA
+// takes kBtfTbpttS consecutive sub-tiles of a chain through a two-stage ring;
+// grad_zw[t] = conj(tap1) g[t+1] reads the cotangent row after each thread's
+// steps from the stage (the row after the sub-tile is copied with it).
+template <bool VECX>
+__global__ void __launch_bounds__(kBtfThreads, 2) btf_tbptt_bwd_kernel(const BtfArgs a) {
+  extern __shared__ __align__(16) unsigned char btf_dsm[];
+  __shared__ float2 s_y[2][kBtfWarps][32];
+  __shared__ float2 s_red[3][kBtfWarps][32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int j = (int)(blockIdx.x / (unsigned)a.ngroups);
-  const int64_t grp = blockIdx.x - (unsigned)j * (unsigned)a.ngroups;
-  const int64_t bi = grp / a.nfb;
-  const int64_t f = (grp - bi * a.nfb) * 32 + lane;
-  const bool fv = f < a.F;
-  const int64_t row = bi * a.F + f;
-  const float2 lam = fv ? a.c1[f] : cz();
-  const float2 t0 = fv ? a.c2[f] : cz();
-  const float2 t1 = fv ? a.tap1[f] : cz();
-  const float2 C = fv ? a.carries[row * a.ntiles + j] : cz();
-  const int64_t base = bi * a.T * a.F + f;
-  const int64_t tile0 = (int64_t)j * S * L;
-  const float2 *xs = static_cast<const float2 *>(a.x);
-  const float2 gK = c_pow2k(lam, ilog2(K));
-  const float2 gL = c_pow2k(lam, kBtfLog2Sub);
-  float2 Gw = cone();
-  for (int w = 0; w < warp; ++w) Gw = c_mul(gK, Gw);
-
-  // pass 1: forward sub-tile aggregates (S > 1 only)
-  if constexpr (S > 1) {
-#pragma unroll 1
-    for (int s = 0; s < S - 1; ++s) {
-      const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
-      float2 x[K], xp, b[K];
-      btf_drive<K, kTwoTap, false>(a, base, tw, fv, t0, t1, x, xp, b);
-      float2 y = cz();
-#pragma unroll
-      for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
-      s_y[s & 1][warp][lane] = y;
-      __syncthreads();
-      float2 X = cz();
-#pragma unroll
-      for (int w = 0; w < NW; ++w) X = c_fma(gK, X, s_y[s & 1][w][lane]);
-      if (warp == 0) s_sub[s][lane] = X;
+  const BtfTile tl = btf_decode(a, blockIdx.x, false);  // independent tiles: no ticket
+  constexpr int S = kBtfTbpttS;
+  constexpr size_t kHdr = (size_t)(kHCarry + 1) * 32 * sizeof(float2);
+  constexpr size_t kRows = (size_t)(kBtfSub + 1) * 32 * sizeof(float2);
+  auto issue = [&](int s) {
+    if (s < S) {
+      unsigned char *st = btf_dsm + (s & 1) * kBtfTbpttStage;
+      float2 *hdr = reinterpret_cast<float2 *>(st);
+      const int sub = tl.j * S + s;
+      if (s == 0) {
+        btf_copy_header<kTwoTap, 1>(hdr, a, tl, kBtfLog2Sub, sub);
+      } else if (warp == 0) {  // the entry state of this sub-tile
+        const int64_t ff = tl.f0 + lane;
+        const bool ok = ff < a.F && sub < a.nsub;
+        cp_async8(hdr + kHCarry * 32 + lane,
+                  ok ? a.carries + (tl.b * a.F + ff) * a.nsub + sub : a.carries, ok);
+      }
+      const int64_t t0 = (int64_t)sub * kBtfSub;
+      btf_copy_rows<float2, VECX>(reinterpret_cast<float2 *>(st + kHdr),
+                                  static_cast<const float2 *>(a.x), a, tl, t0 - 1, 0, kBtfSub + 1);
+      btf_copy_rows<float2, VECX>(reinterpret_cast<float2 *>(st + kHdr + kRows), a.gout, a, tl, t0,
+                                  0, kBtfSub + 1);
     }
-    __syncthreads();
-  }
+    cp_async_commit();
+  };
+  issue(0);
 
-  float2 es = C;
+  BtfConst c{};
   float2 acc_c1 = cz(), acc_t0 = cz(), acc_t1 = cz();
+  const int64_t f = tl.f0 + lane;
+  const bool fv = f < a.F;
+  const int rw = warp * kBtfK;
 #pragma unroll 1
   for (int s = 0; s < S; ++s) {
-    const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
-    float2 x[K], xp, b[K], go[K];
-    btf_drive<K, kTwoTap, true>(a, base, tw, fv, t0, t1, x, xp, b);
+    cp_async_wait<0>();
+    __syncthreads();
+    issue(s + 1);
+    const unsigned char *st = btf_dsm + (s & 1) * kBtfTbpttStage;
+    const float2 *hdr = reinterpret_cast<const float2 *>(st);
+    const float2 *xs = reinterpret_cast<const float2 *>(st + kHdr);
+    const float2 *gs = reinterpret_cast<const float2 *>(st + kHdr + kRows);
+    if (s == 0) c = btf_consts(hdr, lane, warp);
+    const float2 C = hdr[kHCarry * 32 + lane];
+    float2 v[kBtfK + 1];
+    btf_rows9(xs, rw, lane, v);
+    float2 b[kBtfK];
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-      const int64_t t = tw + k;
-      go[k] = (fv && t < a.T) ? __ldcs(a.gout + base + t * a.F) : cz();
-    }
+    for (int k = 0; k < kBtfK; ++k) b[k] = btf_drive1<kTwoTap>(c, v[k + 1], v[k]);
     float2 y = cz();
 #pragma unroll
-    for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
+    for (int k = 0; k < kBtfK; ++k) y = c_fma(c.lam, y, b[k]);
     s_y[s & 1][warp][lane] = y;
     __syncthreads();
     float2 Xw = cz();
-    for (int w = 0; w < warp; ++w) Xw = c_fma(gK, Xw, s_y[s & 1][w][lane]);
-    float2 e = c_fma(Gw, es, Xw);
-    float2 yprev[K];
+    for (int w = 0; w < warp; ++w) Xw = c_fma(c.gK, Xw, s_y[s & 1][w][lane]);
+    float2 e = c_fma(c.Gw, C, Xw);
+    const int64_t t0 = (int64_t)(tl.j * S + s) * kBtfSub + rw;
+    const int64_t left = a.T - t0;
+    const int kmax = !fv ? 0 : (left < kBtfK ? (int)left : kBtfK);
+    const int64_t obase = (tl.b * a.T + t0) * a.F + f;
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-      yprev[k] = e;
-      e = c_fma(lam, e, b[k]);
-      if (FUSE_ACT) go[k] = c_relu_mask(go[k], e);
-    }
-    s_first[s & 1][warp][lane] = go[0];
-    if (warp == NW - 1) {
-      // cotangent of the first sample after this sub-tile (its lag tap)
-      const int64_t tn = tw + K;
-      float2 g_next = cz();
-      if (fv && tn < a.T) {
-        g_next = a.gout[base + tn * a.F];
-        if (FUSE_ACT) {
-          const float2 yn = c_fma(lam, e, c_fma(t1, x[K - 1], c_mul(t0, xs[base + tn * a.F])));
-          g_next = c_relu_mask(g_next, yn);
-        }
+    for (int k = 0; k < kBtfK; ++k) {
+      const float2 yp = e;
+      e = c_fma(c.lam, e, b[k]);
+      const float2 g = gs[(rw + k) * 32 + lane];
+      const float2 g1 = gs[(rw + k + 1) * 32 + lane];  // zero after the sequence
+      if (k < kmax) {
+        __stcs(static_cast<float2 *>(a.out) + obase + k * a.F, c_cfma(c.c2, g, cz()));
+        __stcs(a.out2 + obase + k * a.F, c_cfma(c.t1, g1, cz()));
       }
-      s_first[s & 1][NW][lane] = g_next;
-    }
-    __syncthreads();
-    const float2 gn = s_first[s & 1][warp + 1][lane];
-#pragma unroll
-    for (int k = 0; k < K; ++k) {
-      const float2 g = go[k];
-      const float2 g1 = (k + 1 < K) ? go[k + 1] : gn;
-      const int64_t t = tw + k;
-      if (fv && t < a.T) {
-        __stcs(static_cast<float2 *>(a.out) + base + t * a.F, c_cfma(t0, g, cz()));
-        __stcs(a.out2 + base + t * a.F, c_cfma(t1, g1, cz()));
-      }
-      acc_c1 = c_cfma(yprev[k], g, acc_c1);
-      acc_t0 = c_cfma(x[k], g, acc_t0);
-      acc_t1 = c_cfma(k > 0 ? x[k - 1] : xp, g, acc_t1);
-    }
-    if (s + 1 < S) {
-      // entry of the next sub-tile: the state after this one
-      if constexpr (S > 1) es = c_fma(gL, es, s_sub[s][lane]);
+      acc_c1 = c_cfma(yp, g, acc_c1);
+      acc_t0 = c_cfma(v[k + 1], g, acc_t0);
+      acc_t1 = c_cfma(v[k], g, acc_t1);
     }
   }
   s_red[0][warp][lane] = acc_c1;
@@ -481,8 +612,24 @@ __global__ void __launch_bounds__(NW * 32) btf_tbptt_bwd_kernel(const BtfArgs a)
   if (warp < 3 && fv) {
     float2 sum = cz();
 #pragma unroll
-    for (int w = 0; w < NW; ++w) sum = c_add(sum, s_red[warp][w][lane]);
-    a.partials[(row * a.ntiles + j) * 3 + warp] = sum;
+    for (int w = 0; w < kBtfWarps; ++w) sum = c_add(sum, s_red[warp][w][lane]);
+    a.partials[((tl.b * a.F + f) * a.ntiles + tl.j) * 3 + warp] = sum;
+  }
+}
+
+// c1^(2^i) for i < kBtfPowLevels in double precision, one thread per channel:
+// pw[i*F + f].
+__global__ void btf_pow_table_kernel(const float2 *__restrict__ c1, float2 *__restrict__ pw,
+                                     int64_t F) {
+  const int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (f >= F) return;
+  double re = c1[f].x, im = c1[f].y;
+  for (int i = 0; i < kBtfPowLevels; ++i) {
+    pw[i * F + f] = make_float2((float)re, (float)im);
+    const double nr = re * re - im * im;
+    const double ni = 2.0 * re * im;
+    re = nr;
+    im = ni;
   }
 }
 

@@ -1,0 +1,505 @@
+// Diagonal scans in (batch, time, filters) layout — filters innermost.
+//
+// Serves rqf_models/ops/chunked_scan_kernel.py:_triton_chunked_scan (:340)
+// and _triton_chunked_scan_prospective (:506) without their (B,T,F) <-> (B,F,T)
+// permutes (chunked_scan_kernel.py:212-214, :249, :272-275, :302):
+//   PLAIN    y[t] = c1*y[t-1] + c2*u[t]                 (u complex)
+//   REAL     same with u real (scan.py:366 promotes; the values are identical)
+//   TWO_TAP  y[t] = c1*y[t-1] + tap0*x[t] + tap1*x[t-1]
+//
+// Streaming variant (namespace rqf::btfs), used when there are few chains
+// (batch x 32-channel blocks): long tiles keep the look-back hops per step
+// low, and the second pass re-reads a tile from L2 instead of holding it in
+// shared memory (rqf::btf_*_kernel in btf_scan.cuh hold it).
+//
+// Work decomposition.  A "chain" is one batch index and a block of 32 adjacent
+// channels (lanes, so every load and store of a time step is one coalesced
+// 256-byte row segment).  A sub-tile is NW warps x K consecutive time steps
+// (128 steps): each lane runs its channel's recurrence serially over its K
+// steps and the warps are composed in shared memory.  A CTA owns a tile of S
+// consecutive sub-tiles: pass 1 streams them to form the tile's aggregate, a
+// per-channel decoupled look-back chains the tiles of a chain, and pass 2
+// re-streams the sub-tiles (from L2: the tile was just read) with their
+// entry states to produce the outputs.  S (1..8) is chosen per call from the
+// number of chains.  Tickets run tile-major across chains, so resident CTAs
+// work on different chains instead of queueing behind one.
+// Backward recomputes y from the per-tile carries and fuses the adjoint with
+// grad_u / grad_x and the coefficient-gradient partial sums (one partial per
+// tile, reduced in fixed order afterwards).
+#pragma once
+
+#include "rqf_common.cuh"
+
+namespace rqf {
+namespace btfs {
+
+
+struct BtfArgs {
+  const float2 *c1;
+  const float2 *c2;    // c2 (PLAIN/REAL) or tap0 (TWO_TAP)
+  const float2 *tap1;  // TWO_TAP only
+  const void *x;       // (B,T,F) complex, or float for REAL
+  const float2 *gout;  // (B,T,F) cotangent (backward)
+  void *out;           // forward: y; backward: grad_x (float for REAL)
+  float2 *out2;        // TBPTT backward: grad_zw
+  float2 *carries;     // (B*F, ntiles), row = b*F + f
+  float2 *partials;    // (B*F, ntiles, 3)
+  u64 *flags;          // (B*F, ntiles, 2)
+  unsigned *ticket;
+  int64_t B, T, F;
+  int nfb;      // channel blocks of 32
+  int ngroups;  // chains: B * nfb
+  int ntiles;   // tiles along time
+  int log2L;    // log2 of the tile length (S sub-tiles)
+};
+
+constexpr int kBtfSub = 128;     // time steps of a sub-tile
+constexpr int kBtfLog2Sub = 7;
+constexpr int kBtfMaxS = 8;      // sub-tiles per tile, at most
+
+// Load policies.  A tile read twice (S > 1) is read in pass 1 with the default
+// policy so that it stays in L2, and in pass 2 (its last use) as streaming
+// (evict-first); a tile read once streams.
+template <typename V>
+__device__ __forceinline__ V btf_ld(const V *p, bool last_use) {
+  return last_use ? __ldcs(p) : __ldcg(p);
+}
+template <int DRIVE>
+__device__ __forceinline__ float2 btf_load_x(const void *x, int64_t idx, bool last_use) {
+  if constexpr (DRIVE == kReal) {
+    return make_float2(btf_ld(static_cast<const float *>(x) + idx, last_use), 0.f);
+  } else {
+    return btf_ld(static_cast<const float2 *>(x) + idx, last_use);
+  }
+}
+
+__host__ __device__ constexpr int ilog2(int v) { return v <= 1 ? 0 : 1 + ilog2(v / 2); }
+
+// Drive b[k] = c2 x[k] (+ tap1 x[k-1]) of a warp's K steps starting at tw;
+// LAST: this is the tile's last read (see the load policies above).
+template <int K, int DRIVE, bool LAST>
+__device__ __forceinline__ void btf_drive(const BtfArgs &a, int64_t base, int64_t tw, bool fv,
+                                          float2 c2, float2 t1, float2 (&x)[K], float2 &xp,
+                                          float2 (&b)[K]) {
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int64_t t = tw + k;
+    const bool in = fv && t < a.T;
+    x[k] = in ? btf_load_x<DRIVE>(a.x, base + t * a.F, LAST) : cz();
+  }
+  xp = cz();
+  if constexpr (DRIVE == kTwoTap) {
+    xp = (fv && tw > 0 && tw - 1 < a.T) ? btf_load_x<DRIVE>(a.x, base + (tw - 1) * a.F, false)
+                                        : cz();
+    b[0] = c_fma(t1, xp, c_mul(c2, x[0]));
+#pragma unroll
+    for (int k = 1; k < K; ++k) b[k] = c_fma(t1, x[k - 1], c_mul(c2, x[k]));
+  } else {
+#pragma unroll
+    for (int k = 0; k < K; ++k) b[k] = c_mul(c2, x[k]);
+  }
+}
+
+// ------------------------------------------------------------ forward
+template <int NW, int K, int S, int DRIVE>
+__global__ void __launch_bounds__(NW * 32) btf_fwd_kernel(const BtfArgs a) {
+  constexpr int L = NW * K;  // sub-tile
+  static_assert(L == kBtfSub, "sub-tile length");
+  __shared__ float2 s_y[2][NW][32];
+  __shared__ float2 s_sub[S][32];
+  __shared__ float2 s_C[32];
+  __shared__ unsigned s_ticket;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) s_ticket = atomicAdd(a.ticket, 1u);
+  __syncthreads();
+  const unsigned tk = s_ticket;
+  const int j = (int)(tk / (unsigned)a.ngroups);
+  const int64_t grp = tk - (unsigned)j * (unsigned)a.ngroups;
+  const int64_t bi = grp / a.nfb;
+  const int64_t f = (grp - bi * a.nfb) * 32 + lane;
+  const bool fv = f < a.F;
+  const float2 lam = fv ? a.c1[f] : cz();
+  const float2 c2 = fv ? a.c2[f] : cz();
+  const float2 t1 = (DRIVE == kTwoTap && fv) ? a.tap1[f] : cz();
+  const int64_t base = bi * a.T * a.F + f;  // element (bi, t, f) = base + t*F
+  const int64_t tile0 = (int64_t)j * S * L;
+  const float2 gK = c_pow2k(lam, ilog2(K));
+  const float2 gL = c_pow2k(lam, kBtfLog2Sub);
+  float2 Gw = cone();  // lam^(K*warp): gain from this warp's start back to the sub-tile start
+  for (int w = 0; w < warp; ++w) Gw = c_mul(gK, Gw);
+
+  // pass 1: sub-tile aggregates (zero entry), composed into the tile's.  With
+  // one sub-tile (S == 1) the drive stays in registers for pass 2.
+  float2 Xtile = cz();
+  float2 x[K], xp, b[K];
+#pragma unroll 1
+  for (int s = 0; s < S; ++s) {
+    const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
+    btf_drive<K, DRIVE, S == 1>(a, base, tw, fv, c2, t1, x, xp, b);
+    float2 y = cz();
+#pragma unroll
+    for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
+    s_y[s & 1][warp][lane] = y;
+    __syncthreads();
+    if (warp == 0) {  // only warp 0 needs the sub-tile and tile totals
+      float2 X = cz();
+#pragma unroll
+      for (int w = 0; w < NW; ++w) X = c_fma(gK, X, s_y[s & 1][w][lane]);
+      s_sub[s][lane] = X;
+      Xtile = c_fma(gL, Xtile, X);
+    }
+  }
+  if (warp == 0) {
+    float2 C = cz();
+    if (fv) {
+      const int64_t row = bi * a.F + f;
+      u64 *fl = a.flags + row * (int64_t)a.ntiles * 2;
+      const bool has_next = j + 1 < a.ntiles;
+      if (j == 0) {
+        if (has_next) flag_publish2(fl, Xtile, kInclusive);
+      } else {
+        if (has_next) flag_publish2(fl + 2 * j, Xtile, kAggregate);
+        const float2 M = c_pow2k(lam, a.log2L);
+        C = lookback_const_win(fl, j, M);
+        if (has_next) flag_publish2(fl + 2 * j, c_fma(M, C, Xtile), kInclusive);
+      }
+      a.carries[row * a.ntiles + j] = C;
+    }
+    s_C[lane] = C;
+  }
+  __syncthreads();
+
+  // pass 2: outputs, sub-tile by sub-tile from their entry states
+  float2 es = s_C[lane];
+  float2 *yout = static_cast<float2 *>(a.out);
+#pragma unroll 1
+  for (int s = 0; s < S; ++s) {
+    const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
+    if constexpr (S > 1) {
+      btf_drive<K, DRIVE, true>(a, base, tw, fv, c2, t1, x, xp, b);
+      float2 y = cz();
+#pragma unroll
+      for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
+      s_y[s & 1][warp][lane] = y;
+      __syncthreads();
+    }
+    float2 Xw = cz();
+    for (int w = 0; w < warp; ++w) Xw = c_fma(gK, Xw, s_y[s & 1][w][lane]);
+    float2 e = c_fma(Gw, es, Xw);
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      e = c_fma(lam, e, b[k]);
+      const int64_t t = tw + k;
+      if (fv && t < a.T) __stcs(yout + base + t * a.F, e);
+    }
+    es = c_fma(gL, es, s_sub[s][lane]);
+  }
+}
+
+// ------------------------------------------------------------ backward
+template <int NW, int K, int S, int DRIVE>
+__global__ void __launch_bounds__(NW * 32) btf_bwd_kernel(const BtfArgs a) {
+  constexpr int L = NW * K;
+  static_assert(L == kBtfSub, "sub-tile length");
+  __shared__ float4 s_yh[2][NW][32];   // (forward local y, reverse local h) per warp
+  __shared__ float2 s_subf[S][32];     // forward sub-tile aggregates
+  __shared__ float2 s_subr[S][32];     // reverse sub-tile aggregates
+  __shared__ float2 s_red[3][NW][32];
+  __shared__ float2 s_D[32];
+  __shared__ unsigned s_ticket;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) s_ticket = atomicAdd(a.ticket, 1u);
+  __syncthreads();
+  const unsigned tk = s_ticket;
+  const int p = (int)(tk / (unsigned)a.ngroups);
+  const int64_t grp = tk - (unsigned)p * (unsigned)a.ngroups;
+  const int j = a.ntiles - 1 - p;
+  const int64_t bi = grp / a.nfb;
+  const int64_t f = (grp - bi * a.nfb) * 32 + lane;
+  const bool fv = f < a.F;
+  const int64_t row = bi * a.F + f;
+  const float2 lam = fv ? a.c1[f] : cz();
+  const float2 c2 = fv ? a.c2[f] : cz();
+  const float2 t1 = (DRIVE == kTwoTap && fv) ? a.tap1[f] : cz();
+  const float2 C = fv ? a.carries[row * a.ntiles + j] : cz();
+  const int64_t base = bi * a.T * a.F + f;
+  const int64_t tile0 = (int64_t)j * S * L;
+  const float2 mu = c_conj(lam);
+  const float2 gK = c_pow2k(lam, ilog2(K)), muK = c_conj(gK);
+  const float2 gL = c_pow2k(lam, kBtfLog2Sub), muL = c_conj(gL);
+  float2 Gw = cone(), Grw = cone();  // lam^(K*warp), conj(lam)^(K*(NW-1-warp))
+  for (int w = 0; w < warp; ++w) Gw = c_mul(gK, Gw);
+  for (int w = NW - 1; w > warp; --w) Grw = c_mul(muK, Grw);
+
+  // pass 1: forward and reverse sub-tile aggregates.  With one sub-tile
+  // (S == 1) the loaded values and the warp exchange stay for pass 2.
+  float2 Xrtile = cz(), pw = cone();
+  float2 x[K], xp, b[K], go[K];
+#pragma unroll 1
+  for (int s = 0; s < S; ++s) {
+    const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
+    btf_drive<K, DRIVE, S == 1>(a, base, tw, fv, c2, t1, x, xp, b);
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int64_t t = tw + k;
+      go[k] = (fv && t < a.T) ? btf_ld(a.gout + base + t * a.F, S == 1) : cz();
+    }
+    float2 y = cz(), h = cz();
+#pragma unroll
+    for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
+#pragma unroll
+    for (int k = K - 1; k >= 0; --k) h = c_fma(mu, h, go[k]);
+    s_yh[s & 1][warp][lane] = make_float4(y.x, y.y, h.x, h.y);
+    __syncthreads();
+    // sub-tile totals: forward by warp 0, reverse by warp 1 (tile total kept
+    // by warp 1 and handed to warp 0 through s_D below)
+    if (warp == 0) {
+      float2 X = cz();
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        const float4 q = s_yh[s & 1][w][lane];
+        X = c_fma(gK, X, make_float2(q.x, q.y));
+      }
+      s_subf[s][lane] = X;
+    } else if (warp == 1) {
+      float2 Xr = cz();
+#pragma unroll
+      for (int w = NW - 1; w >= 0; --w) {
+        const float4 q = s_yh[s & 1][w][lane];
+        Xr = c_fma(muK, Xr, make_float2(q.z, q.w));
+      }
+      s_subr[s][lane] = Xr;
+      Xrtile = c_fma(pw, Xr, Xrtile);  // sub-tile s starts L*s steps into the tile
+      pw = c_mul(muL, pw);
+    }
+  }
+  if (warp == 1) s_D[lane] = Xrtile;
+  __syncthreads();
+  if (warp == 0) {
+    float2 D = cz();
+    const float2 Xrtile0 = s_D[lane];
+    if (fv) {
+      u64 *fl = a.flags + row * (int64_t)a.ntiles * 2;
+      const bool has_next = p + 1 < a.ntiles;
+      if (p == 0) {
+        if (has_next) flag_publish2(fl, Xrtile0, kInclusive);
+      } else {
+        if (has_next) flag_publish2(fl + 2 * p, Xrtile0, kAggregate);
+        const float2 M = c_pow2k(mu, a.log2L);
+        D = lookback_const_win(fl, p, M);
+        if (has_next) flag_publish2(fl + 2 * p, c_fma(M, D, Xrtile0), kInclusive);
+      }
+    }
+    __syncwarp();
+    s_D[lane] = D;
+  }
+  __syncthreads();
+
+  // sub-tile entry states: forward C_s from the tile carry, reverse D_s (the
+  // adjoint entering sub-tile s from its right) from the look-back
+  float2 Cs[S];
+  Cs[0] = C;
+#pragma unroll
+  for (int s = 1; s < S; ++s) Cs[s] = c_fma(gL, Cs[s - 1], s_subf[s - 1][lane]);
+  float2 Ds = s_D[lane];
+
+  // pass 2: sub-tiles from last to first
+  float2 acc_c1 = cz(), acc_1 = cz(), acc_2 = cz();
+#pragma unroll 1
+  for (int s = S - 1; s >= 0; --s) {
+    const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
+    if constexpr (S > 1) {
+      btf_drive<K, DRIVE, true>(a, base, tw, fv, c2, t1, x, xp, b);
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const int64_t t = tw + k;
+        go[k] = (fv && t < a.T) ? __ldcs(a.gout + base + t * a.F) : cz();
+      }
+      float2 y = cz(), h = cz();
+#pragma unroll
+      for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
+#pragma unroll
+      for (int k = K - 1; k >= 0; --k) h = c_fma(mu, h, go[k]);
+      s_yh[s & 1][warp][lane] = make_float4(y.x, y.y, h.x, h.y);
+      __syncthreads();
+    }
+    float2 Xw = cz(), Xrw = cz();
+    for (int w = 0; w < warp; ++w) {
+      const float4 q = s_yh[s & 1][w][lane];
+      Xw = c_fma(gK, Xw, make_float2(q.x, q.y));
+    }
+    for (int w = NW - 1; w > warp; --w) {
+      const float4 q = s_yh[s & 1][w][lane];
+      Xrw = c_fma(muK, Xrw, make_float2(q.z, q.w));
+    }
+    float2 e = c_fma(Gw, Cs[s], Xw);
+    float2 yprev[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      yprev[k] = e;
+      e = c_fma(lam, e, b[k]);
+    }
+    float2 gnext = c_fma(Grw, Ds, Xrw);
+#pragma unroll
+    for (int k = K - 1; k >= 0; --k) {
+      const float2 g = c_fma(mu, gnext, go[k]);
+      const int64_t t = tw + k;
+      const bool in = fv && t < a.T;
+      if constexpr (DRIVE == kReal) {
+        // grad of the real input: Re(conj(c2) g)
+        if (in) __stcs(static_cast<float *>(a.out) + base + t * a.F, c2.x * g.x + c2.y * g.y);
+        acc_1 = make_float2(fmaf(x[k].x, g.x, acc_1.x), fmaf(x[k].x, g.y, acc_1.y));
+      } else if constexpr (DRIVE == kPlain) {
+        if (in) __stcs(static_cast<float2 *>(a.out) + base + t * a.F, c_cfma(c2, g, cz()));
+        acc_1 = c_cfma(x[k], g, acc_1);
+      } else {
+        if (in)
+          __stcs(static_cast<float2 *>(a.out) + base + t * a.F,
+                 c_cfma(t1, gnext, c_cfma(c2, g, cz())));
+        acc_1 = c_cfma(x[k], g, acc_1);
+        acc_2 = c_cfma(k > 0 ? x[k - 1] : xp, g, acc_2);
+      }
+      acc_c1 = c_cfma(yprev[k], g, acc_c1);
+      gnext = g;
+    }
+    Ds = c_fma(muL, Ds, s_subr[s][lane]);  // adjoint entering sub-tile s-1
+  }
+  s_red[0][warp][lane] = acc_c1;
+  s_red[1][warp][lane] = acc_1;
+  s_red[2][warp][lane] = acc_2;
+  __syncthreads();
+  if (warp < 3 && fv) {
+    float2 sum = cz();
+#pragma unroll
+    for (int w = 0; w < NW; ++w) sum = c_add(sum, s_red[warp][w][lane]);
+    a.partials[(row * a.ntiles + j) * 3 + warp] = sum;
+  }
+}
+
+// TBPTT(1) surrogate backward in (B,T,F) layout (no temporal adjoint).  One
+// CTA per (tile, chain) in blockIdx order; pass 1 forms the forward sub-tile
+// aggregates so that pass 2 can start every sub-tile from its entry state.
+template <int NW, int K, int S, bool FUSE_ACT>
+__global__ void __launch_bounds__(NW * 32) btf_tbptt_bwd_kernel(const BtfArgs a) {
+  constexpr int L = NW * K;
+  static_assert(L == kBtfSub, "sub-tile length");
+  __shared__ float2 s_y[2][NW][32];
+  __shared__ float2 s_sub[S][32];
+  __shared__ float2 s_first[2][NW + 1][32];
+  __shared__ float2 s_red[3][NW][32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int j = (int)(blockIdx.x / (unsigned)a.ngroups);
+  const int64_t grp = blockIdx.x - (unsigned)j * (unsigned)a.ngroups;
+  const int64_t bi = grp / a.nfb;
+  const int64_t f = (grp - bi * a.nfb) * 32 + lane;
+  const bool fv = f < a.F;
+  const int64_t row = bi * a.F + f;
+  const float2 lam = fv ? a.c1[f] : cz();
+  const float2 t0 = fv ? a.c2[f] : cz();
+  const float2 t1 = fv ? a.tap1[f] : cz();
+  const float2 C = fv ? a.carries[row * a.ntiles + j] : cz();
+  const int64_t base = bi * a.T * a.F + f;
+  const int64_t tile0 = (int64_t)j * S * L;
+  const float2 *xs = static_cast<const float2 *>(a.x);
+  const float2 gK = c_pow2k(lam, ilog2(K));
+  const float2 gL = c_pow2k(lam, kBtfLog2Sub);
+  float2 Gw = cone();
+  for (int w = 0; w < warp; ++w) Gw = c_mul(gK, Gw);
+
+  // pass 1: forward sub-tile aggregates (S > 1 only)
+  if constexpr (S > 1) {
+#pragma unroll 1
+    for (int s = 0; s < S - 1; ++s) {
+      const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
+      float2 x[K], xp, b[K];
+      btf_drive<K, kTwoTap, false>(a, base, tw, fv, t0, t1, x, xp, b);
+      float2 y = cz();
+#pragma unroll
+      for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
+      s_y[s & 1][warp][lane] = y;
+      __syncthreads();
+      if (warp == 0) {
+        float2 X = cz();
+#pragma unroll
+        for (int w = 0; w < NW; ++w) X = c_fma(gK, X, s_y[s & 1][w][lane]);
+        s_sub[s][lane] = X;
+      }
+    }
+    __syncthreads();
+  }
+
+  float2 es = C;
+  float2 acc_c1 = cz(), acc_t0 = cz(), acc_t1 = cz();
+#pragma unroll 1
+  for (int s = 0; s < S; ++s) {
+    const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
+    float2 x[K], xp, b[K], go[K];
+    btf_drive<K, kTwoTap, true>(a, base, tw, fv, t0, t1, x, xp, b);
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int64_t t = tw + k;
+      go[k] = (fv && t < a.T) ? __ldcs(a.gout + base + t * a.F) : cz();
+    }
+    float2 y = cz();
+#pragma unroll
+    for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
+    s_y[s & 1][warp][lane] = y;
+    __syncthreads();
+    float2 Xw = cz();
+    for (int w = 0; w < warp; ++w) Xw = c_fma(gK, Xw, s_y[s & 1][w][lane]);
+    float2 e = c_fma(Gw, es, Xw);
+    float2 yprev[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      yprev[k] = e;
+      e = c_fma(lam, e, b[k]);
+      if (FUSE_ACT) go[k] = c_relu_mask(go[k], e);
+    }
+    s_first[s & 1][warp][lane] = go[0];
+    if (warp == NW - 1) {
+      // cotangent of the first sample after this sub-tile (its lag tap)
+      const int64_t tn = tw + K;
+      float2 g_next = cz();
+      if (fv && tn < a.T) {
+        g_next = a.gout[base + tn * a.F];
+        if (FUSE_ACT) {
+          const float2 yn = c_fma(lam, e, c_fma(t1, x[K - 1], c_mul(t0, xs[base + tn * a.F])));
+          g_next = c_relu_mask(g_next, yn);
+        }
+      }
+      s_first[s & 1][NW][lane] = g_next;
+    }
+    __syncthreads();
+    const float2 gn = s_first[s & 1][warp + 1][lane];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const float2 g = go[k];
+      const float2 g1 = (k + 1 < K) ? go[k + 1] : gn;
+      const int64_t t = tw + k;
+      if (fv && t < a.T) {
+        __stcs(static_cast<float2 *>(a.out) + base + t * a.F, c_cfma(t0, g, cz()));
+        __stcs(a.out2 + base + t * a.F, c_cfma(t1, g1, cz()));
+      }
+      acc_c1 = c_cfma(yprev[k], g, acc_c1);
+      acc_t0 = c_cfma(x[k], g, acc_t0);
+      acc_t1 = c_cfma(k > 0 ? x[k - 1] : xp, g, acc_t1);
+    }
+    if (s + 1 < S) {
+      // entry of the next sub-tile: the state after this one
+      if constexpr (S > 1) es = c_fma(gL, es, s_sub[s][lane]);
+    }
+  }
+  s_red[0][warp][lane] = acc_c1;
+  s_red[1][warp][lane] = acc_t0;
+  s_red[2][warp][lane] = acc_t1;
+  __syncthreads();
+  if (warp < 3 && fv) {
+    float2 sum = cz();
+#pragma unroll
+    for (int w = 0; w < NW; ++w) sum = c_add(sum, s_red[warp][w][lane]);
+    a.partials[(row * a.ntiles + j) * 3 + warp] = sum;
+  }
+}
+
+}  // namespace btfs
+}  // namespace rqf

@@ -12,6 +12,7 @@
 
 #include "../../include/rqf_b200.h"
 #include "btf_scan.cuh"
+#include "btf_stream.cuh"
 #include "fbt_rows.cuh"
 #include "fbt_scan.cuh"
 #include "reduce.cuh"
@@ -24,14 +25,6 @@ namespace {
 
 constexpr int kAbiVersion = 1;
 constexpr int64_t kMaxTickets = 0x7fffffffLL;
-
-// BTF launch shapes: the forward uses 8 warps x 16 steps, the backward
-// 16 warps x 8 steps; both tile 128 time steps so they share the carries.
-constexpr int kBtfFwdWarps = 8, kBtfFwdK = 16;
-constexpr int kBtfBwdWarps = 16, kBtfBwdK = 8;
-static_assert(kBtfFwdWarps * kBtfFwdK == kBtfSub, "BTF forward sub-tile");
-static_assert(kBtfBwdWarps * kBtfBwdK == kBtfSub, "BTF backward sub-tile");
-
 
 inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 inline size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -52,17 +45,30 @@ inline Scratch scratch_layout(int64_t rows, int64_t ntiles) {
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
-// Sub-tiles per (B,T,F) tile.  A chain (batch x 32-channel block) advances by
-// one look-back hop (~1 us) per tile, so the tiles of all chains together must
-// cover enough data per hop: ngroups * S >= 80 (~5 MB per hop), S = 1..8.
-inline int btf_subtiles(int64_t B, int64_t F) {
-  const int64_t groups = B * ceil_div(F, 32);
-  int s = 1;
-  while (s < kBtfMaxS && groups * s < 80) s *= 2;
-  return s;
+// (B,T,F) tiling.  Sub-tiles of 64 steps; the saved entry states are per
+// sub-tile, so each launch picks its own tile length: long tiles amortise a
+// tile's fixed costs (ticket, header, look-back round trip), but there should
+// still be a tile for every SM.
+inline int64_t btf_nsub(int64_t T) { return T <= 0 ? 0 : ceil_div(T, (int64_t)kBtfSub); }
+inline int btf_log2_tile(int64_t B, int64_t T, int64_t F, int max_log2) {
+  const int64_t groups = B * ceil_div(F, 32), nsub = btf_nsub(T);
+  int l = max_log2;
+  while (l > 0 && ((1LL << (l - 1)) >= nsub || groups * ceil_div(nsub, 1LL << l) < 148)) --l;
+  return l;
 }
-inline int64_t btf_tiles(int64_t B, int64_t T, int64_t F) {
-  return T <= 0 ? 0 : ceil_div(T, (int64_t)kBtfSub * btf_subtiles(B, F));
+// Scratch of the (B,T,F) kernels: ticket, look-back flags and partials sized
+// for one tile per sub-tile (the most tiles any launch uses), then the c1
+// power table (kBtfPowLevels x F).
+struct BtfScratch {
+  Scratch base;
+  size_t pw_off, total;
+};
+inline BtfScratch btf_scratch_layout(int64_t B, int64_t T, int64_t F) {
+  BtfScratch s;
+  s.base = scratch_layout(B * F, btf_nsub(T));
+  s.pw_off = s.base.total;
+  s.total = s.pw_off + round256((size_t)kBtfPowLevels * (size_t)F * sizeof(float2));
+  return s;
 }
 
 inline int launch_status() {
@@ -157,42 +163,14 @@ FbtArgs fbt_args(const float *c1, const float *tap0, const float *tap1, const fl
 // ------------------------------------------------------------- BTF
 int btf_dims_ok(int64_t B, int64_t T, int64_t F) {
   if (B < 0 || T < 0 || F < 0) return RQF_ERR_SHAPE;
-  if (B > 0 && F > 0 && btf_tiles(B, T, F) * B * ceil_div(F, 32) > kMaxTickets)
-    return RQF_ERR_SHAPE;
+  if (B > 0 && F > 0 && btf_nsub(T) * B * ceil_div(F, 32) > kMaxTickets) return RQF_ERR_SHAPE;
   return RQF_OK;
 }
 
-template <int DRIVE>
-void btf_launch_fwd(int S, unsigned grid, int nt, cudaStream_t st, const BtfArgs &a) {
-  switch (S) {
-    case 1: btf_fwd_kernel<kBtfFwdWarps, kBtfFwdK, 1, DRIVE><<<grid, nt, 0, st>>>(a); break;
-    case 2: btf_fwd_kernel<kBtfFwdWarps, kBtfFwdK, 2, DRIVE><<<grid, nt, 0, st>>>(a); break;
-    case 4: btf_fwd_kernel<kBtfFwdWarps, kBtfFwdK, 4, DRIVE><<<grid, nt, 0, st>>>(a); break;
-    default: btf_fwd_kernel<kBtfFwdWarps, kBtfFwdK, 8, DRIVE><<<grid, nt, 0, st>>>(a); break;
-  }
-}
-template <int DRIVE>
-void btf_launch_bwd(int S, unsigned grid, int nt, cudaStream_t st, const BtfArgs &a) {
-  switch (S) {
-    case 1: btf_bwd_kernel<kBtfBwdWarps, kBtfBwdK, 1, DRIVE><<<grid, nt, 0, st>>>(a); break;
-    case 2: btf_bwd_kernel<kBtfBwdWarps, kBtfBwdK, 2, DRIVE><<<grid, nt, 0, st>>>(a); break;
-    case 4: btf_bwd_kernel<kBtfBwdWarps, kBtfBwdK, 4, DRIVE><<<grid, nt, 0, st>>>(a); break;
-    default: btf_bwd_kernel<kBtfBwdWarps, kBtfBwdK, 8, DRIVE><<<grid, nt, 0, st>>>(a); break;
-  }
-}
-template <bool FUSE>
-void btf_launch_tbptt(int S, unsigned grid, int nt, cudaStream_t st, const BtfArgs &a) {
-  switch (S) {
-    case 1: btf_tbptt_bwd_kernel<kBtfBwdWarps, kBtfBwdK, 1, FUSE><<<grid, nt, 0, st>>>(a); break;
-    case 2: btf_tbptt_bwd_kernel<kBtfBwdWarps, kBtfBwdK, 2, FUSE><<<grid, nt, 0, st>>>(a); break;
-    case 4: btf_tbptt_bwd_kernel<kBtfBwdWarps, kBtfBwdK, 4, FUSE><<<grid, nt, 0, st>>>(a); break;
-    default: btf_tbptt_bwd_kernel<kBtfBwdWarps, kBtfBwdK, 8, FUSE><<<grid, nt, 0, st>>>(a); break;
-  }
-}
-
+// Arguments of one launch whose tiles are 2^log2S sub-tiles.
 BtfArgs btf_args(const float *c1, const float *c2, const float *tap1, const void *x,
                  const float *gout, void *out, float *out2, float *carries, void *scratch,
-                 int64_t B, int64_t T, int64_t F) {
+                 int64_t B, int64_t T, int64_t F, int log2S) {
   BtfArgs a;
   a.c1 = reinterpret_cast<const float2 *>(c1);
   a.c2 = reinterpret_cast<const float2 *>(c2);
@@ -207,14 +185,137 @@ BtfArgs btf_args(const float *c1, const float *c2, const float *tap1, const void
   a.F = F;
   a.nfb = (int)ceil_div(F, 32);
   a.ngroups = (int)(B * a.nfb);
-  a.ntiles = (int)btf_tiles(B, T, F);
-  const int S = btf_subtiles(B, F);
-  a.log2L = kBtfLog2Sub + (S == 1 ? 0 : S == 2 ? 1 : S == 4 ? 2 : 3);
+  a.nsub = (int)btf_nsub(T);
+  a.log2S = log2S;
+  a.S = 1 << log2S;
+  a.ntiles = (int)ceil_div(a.nsub, a.S);
+  const BtfScratch lay = btf_scratch_layout(B, T, F);
+  a.ticket = at<unsigned>(scratch, 0);
+  a.flags = at<u64>(scratch, lay.base.flags_off);
+  a.partials = at<float2>(scratch, lay.base.partials_off);
+  a.pw = at<float2>(scratch, lay.pw_off);
+  return a;
+}
+
+// Clears the ticket and flags, fills the power table, and launches a (B,T,F)
+// kernel with one CTA per tile.
+template <typename Kern>
+int btf_launch(Kern kernel, size_t smem, const BtfArgs &a, void *scratch, cudaStream_t stream) {
+  const BtfScratch lay = btf_scratch_layout(a.B, a.T, a.F);
+  int st = clear_lookback(scratch, lay.base, stream);
+  if (st != RQF_OK) return st;
+  btf_pow_table_kernel<<<(unsigned)ceil_div(a.F, 128), 128, 0, stream>>>(
+      a.c1, const_cast<float2 *>(a.pw), a.F);
+  if ((st = launch_status()) != RQF_OK) return st;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return RQF_ERR_LAUNCH;
+  const int64_t tiles = (int64_t)a.ngroups * a.ntiles;
+  kernel<<<(unsigned)tiles, kBtfThreads, smem, stream>>>(a);
+  return launch_status();
+}
+
+template <int DRIVE, bool VEC>
+int btf_launch_fwd(const BtfArgs &a, void *scratch, cudaStream_t stream) {
+  switch (a.S) {
+    case 1: return btf_launch(btf_fwd_kernel<DRIVE, VEC, 1>, btf_fwd_smem<DRIVE, 1>(), a, scratch, stream);
+    case 2: return btf_launch(btf_fwd_kernel<DRIVE, VEC, 2>, btf_fwd_smem<DRIVE, 2>(), a, scratch, stream);
+    default: return btf_launch(btf_fwd_kernel<DRIVE, VEC, 4>, btf_fwd_smem<DRIVE, 4>(), a, scratch, stream);
+  }
+}
+
+template <int DRIVE, bool VECX, bool VECG>
+int btf_launch_bwd(const BtfArgs &a, void *scratch, cudaStream_t stream) {
+  if (a.S == 1)
+    return btf_launch(btf_bwd_kernel<DRIVE, VECX, VECG, 1>, btf_bwd_smem<DRIVE, 1>(), a, scratch,
+                      stream);
+  return btf_launch(btf_bwd_kernel<DRIVE, VECX, VECG, 2>, btf_bwd_smem<DRIVE, 2>(), a, scratch,
+                    stream);
+}
+
+// 16-byte staging copies: the row of a chain starts on a 16-byte boundary.
+inline bool btf_vec(const void *p, int64_t F, size_t elem) {
+  return p && aligned(p, 16) && (F * (int64_t)elem) % 16 == 0;
+}
+
+// ---- streaming path (rqf::btfs): few long chains.  Tiles of S x 128 steps
+// re-read from L2 in their second pass, so a chain advances up to 1024 steps
+// per look-back; the tile-resident kernels above hold a tile in shared memory
+// and win when there are enough chains to keep the look-backs short.
+namespace bs = rqf::btfs;
+constexpr int kBtfsFwdWarps = 8, kBtfsFwdK = 16;
+constexpr int kBtfsBwdWarps = 16, kBtfsBwdK = 8;
+static_assert(kBtfsFwdWarps * kBtfsFwdK == bs::kBtfSub, "streaming forward sub-tile");
+static_assert(kBtfsBwdWarps * kBtfsBwdK == bs::kBtfSub, "streaming backward sub-tile");
+constexpr int64_t kBtfStreamChains = 48;  // chains below which the streaming path is used
+
+int g_btf_path = 0;  // 0 automatic, 1 streaming, 2 tile-resident (rqf_btf_select_path)
+
+inline bool btf_streaming(int64_t B, int64_t F) {
+  if (g_btf_path != 0) return g_btf_path == 1;
+  return B * ceil_div(F, 32) < kBtfStreamChains;
+}
+
+// Sub-tiles (128 steps) per streaming tile: ngroups * S >= 80, S = 1..8.
+inline int btfs_subtiles(int64_t B, int64_t F) {
+  const int64_t groups = B * ceil_div(F, 32);
+  int s = 1;
+  while (s < bs::kBtfMaxS && groups * s < 80) s *= 2;
+  return s;
+}
+
+bs::BtfArgs btfs_args(const float *c1, const float *c2, const float *tap1, const void *x,
+                      const float *gout, void *out, float *out2, float *carries, void *scratch,
+                      int64_t B, int64_t T, int64_t F) {
+  bs::BtfArgs a;
+  a.c1 = reinterpret_cast<const float2 *>(c1);
+  a.c2 = reinterpret_cast<const float2 *>(c2);
+  a.tap1 = reinterpret_cast<const float2 *>(tap1);
+  a.x = x;
+  a.gout = reinterpret_cast<const float2 *>(gout);
+  a.out = out;
+  a.out2 = reinterpret_cast<float2 *>(out2);
+  a.carries = reinterpret_cast<float2 *>(carries);
+  a.B = B;
+  a.T = T;
+  a.F = F;
+  a.nfb = (int)ceil_div(F, 32);
+  a.ngroups = (int)(B * a.nfb);
+  const int S = btfs_subtiles(B, F);
+  a.ntiles = (int)ceil_div(T, (int64_t)bs::kBtfSub * S);
+  a.log2L = bs::kBtfLog2Sub + (S == 1 ? 0 : S == 2 ? 1 : S == 4 ? 2 : 3);
   const Scratch lay = scratch_layout(B * F, a.ntiles);
   a.ticket = at<unsigned>(scratch, 0);
   a.flags = at<u64>(scratch, lay.flags_off);
   a.partials = at<float2>(scratch, lay.partials_off);
   return a;
+}
+
+// One streaming kernel: KIND 0 forward, 1 backward, 2 TBPTT(1) backward.
+template <int KIND, int DRIVE, int S>
+void btfs_kernel(const bs::BtfArgs &a, unsigned grid, cudaStream_t st) {
+  if constexpr (KIND == 0)
+    bs::btf_fwd_kernel<kBtfsFwdWarps, kBtfsFwdK, S, DRIVE><<<grid, kBtfsFwdWarps * 32, 0, st>>>(a);
+  else if constexpr (KIND == 1)
+    bs::btf_bwd_kernel<kBtfsBwdWarps, kBtfsBwdK, S, DRIVE><<<grid, kBtfsBwdWarps * 32, 0, st>>>(a);
+  else
+    bs::btf_tbptt_bwd_kernel<kBtfsBwdWarps, kBtfsBwdK, S, false>
+        <<<grid, kBtfsBwdWarps * 32, 0, st>>>(a);
+}
+
+// Launches a streaming kernel over all tiles after clearing the ticket and flags.
+template <int KIND, int DRIVE>
+int btfs_launch(const bs::BtfArgs &a, void *scratch, cudaStream_t st) {
+  const int rc = clear_lookback(scratch, scratch_layout(a.B * a.F, a.ntiles), st);
+  if (rc != RQF_OK) return rc;
+  const unsigned grid = (unsigned)((int64_t)a.ngroups * a.ntiles);
+  switch (btfs_subtiles(a.B, a.F)) {
+    case 1: btfs_kernel<KIND, DRIVE, 1>(a, grid, st); break;
+    case 2: btfs_kernel<KIND, DRIVE, 2>(a, grid, st); break;
+    case 4: btfs_kernel<KIND, DRIVE, 4>(a, grid, st); break;
+    default: btfs_kernel<KIND, DRIVE, 8>(a, grid, st); break;
+  }
+  return launch_status();
 }
 
 int btf_forward(int drive, const float *c1, const float *c2, const float *tap1, const void *x,
@@ -229,19 +330,30 @@ int btf_forward(int drive, const float *c1, const float *c2, const float *tap1, 
       !aligned(scratch, 16) || !aligned(x, drive == kReal ? 4 : 8) ||
       (tap1 && !aligned(tap1, 8)))
     return RQF_ERR_ALIGN;
-  BtfArgs a = btf_args(c1, c2, tap1, x, nullptr, y, nullptr, carries, scratch, B, T, F);
-  const Scratch lay = scratch_layout(B * F, a.ntiles);
-  if ((st = clear_lookback(scratch, lay, stream)) != RQF_OK) return st;
-  const unsigned grid = (unsigned)(B * a.nfb * a.ntiles);
-  const int nt = kBtfFwdWarps * 32;
-  const int S = btf_subtiles(B, F);
+  if (btf_streaming(B, F)) {
+    const bs::BtfArgs sa = btfs_args(c1, c2, tap1, x, nullptr, y, nullptr, carries, scratch, B, T, F);
+    if (drive == kReal) return btfs_launch<0, kReal>(sa, scratch, stream);
+    if (drive == kPlain) return btfs_launch<0, kPlain>(sa, scratch, stream);
+    return btfs_launch<0, kTwoTap>(sa, scratch, stream);
+  }
+  const BtfArgs a = btf_args(c1, c2, tap1, x, nullptr, y, nullptr, carries, scratch, B, T, F,
+                             btf_log2_tile(B, T, F, 2));
   if (drive == kReal)
-    btf_launch_fwd<kReal>(S, grid, nt, stream, a);
-  else if (drive == kPlain)
-    btf_launch_fwd<kPlain>(S, grid, nt, stream, a);
-  else
-    btf_launch_fwd<kTwoTap>(S, grid, nt, stream, a);
-  return launch_status();
+    return btf_vec(x, F, 4) ? btf_launch_fwd<kReal, true>(a, scratch, stream)
+                            : btf_launch_fwd<kReal, false>(a, scratch, stream);
+  if (drive == kPlain)
+    return btf_vec(x, F, 8) ? btf_launch_fwd<kPlain, true>(a, scratch, stream)
+                            : btf_launch_fwd<kPlain, false>(a, scratch, stream);
+  return btf_vec(x, F, 8) ? btf_launch_fwd<kTwoTap, true>(a, scratch, stream)
+                          : btf_launch_fwd<kTwoTap, false>(a, scratch, stream);
+}
+
+template <int DRIVE>
+int btf_backward_drive(const BtfArgs &a, bool vecx, bool vecg, void *scratch,
+                       cudaStream_t stream) {
+  if (vecx && vecg) return btf_launch_bwd<DRIVE, true, true>(a, scratch, stream);
+  if (vecg) return btf_launch_bwd<DRIVE, false, true>(a, scratch, stream);
+  return btf_launch_bwd<DRIVE, false, false>(a, scratch, stream);
 }
 
 int btf_backward(int drive, const float *c1, const float *c2, const float *tap1, const void *x,
@@ -262,20 +374,28 @@ int btf_backward(int drive, const float *c1, const float *c2, const float *tap1,
       !aligned(scratch, 16) || !aligned(x, drive == kReal ? 4 : 8) ||
       !aligned(gx, drive == kReal ? 4 : 8) || (tap1 && !aligned(tap1, 8)))
     return RQF_ERR_ALIGN;
-  BtfArgs a = btf_args(c1, c2, tap1, x, gy, gx, nullptr, const_cast<float *>(carries), scratch,
-                       B, T, F);
-  const Scratch lay = scratch_layout(B * F, a.ntiles);
-  if ((st = clear_lookback(scratch, lay, stream)) != RQF_OK) return st;
-  const unsigned grid = (unsigned)(B * a.nfb * a.ntiles);
-  const int nt = kBtfBwdWarps * 32;
-  const int S = btf_subtiles(B, F);
+  if (btf_streaming(B, F)) {
+    const bs::BtfArgs sa = btfs_args(c1, c2, tap1, x, gy, gx, nullptr,
+                                     const_cast<float *>(carries), scratch, B, T, F);
+    st = drive == kReal    ? btfs_launch<1, kReal>(sa, scratch, stream)
+         : drive == kPlain ? btfs_launch<1, kPlain>(sa, scratch, stream)
+                           : btfs_launch<1, kTwoTap>(sa, scratch, stream);
+    if (st != RQF_OK) return st;
+    reduce_partials_kernel<<<(unsigned)F, 256, 0, stream>>>(
+        sa.partials, reinterpret_cast<float2 *>(o0), reinterpret_cast<float2 *>(o1),
+        reinterpret_cast<float2 *>(o2), B, 1, F, sa.ntiles);
+    return launch_status();
+  }
+  const BtfArgs a = btf_args(c1, c2, tap1, x, gy, gx, nullptr, const_cast<float *>(carries),
+                             scratch, B, T, F, btf_log2_tile(B, T, F, 1));
+  const bool vecg = btf_vec(gy, F, 8);
   if (drive == kReal)
-    btf_launch_bwd<kReal>(S, grid, nt, stream, a);
+    st = btf_backward_drive<kReal>(a, btf_vec(x, F, 4), vecg, scratch, stream);
   else if (drive == kPlain)
-    btf_launch_bwd<kPlain>(S, grid, nt, stream, a);
+    st = btf_backward_drive<kPlain>(a, btf_vec(x, F, 8), vecg, scratch, stream);
   else
-    btf_launch_bwd<kTwoTap>(S, grid, nt, stream, a);
-  if ((st = launch_status()) != RQF_OK) return st;
+    st = btf_backward_drive<kTwoTap>(a, btf_vec(x, F, 8), vecg, scratch, stream);
+  if (st != RQF_OK) return st;
   reduce_partials_kernel<<<(unsigned)F, 256, 0, stream>>>(
       a.partials, reinterpret_cast<float2 *>(o0), reinterpret_cast<float2 *>(o1),
       reinterpret_cast<float2 *>(o2), B, 1, F, a.ntiles);
@@ -340,13 +460,20 @@ int rqf_selftest_lookback_timeout(void *scratch, rqf_stream_t stream) {
 }
 
 // ---------------------------------------------------------------- sizes
-int64_t rqf_btf_num_tiles(int64_t time) { return time <= 0 ? 0 : ceil_div(time, kBtfSub); }
+int rqf_btf_select_path(int path) {
+  if (path < 0 || path > 2) return -1;
+  const int prev = g_btf_path;
+  g_btf_path = path;
+  return prev;
+}
+
+int64_t rqf_btf_num_tiles(int64_t time) { return btf_nsub(time); }
 int64_t rqf_btf_carry_count(int64_t batch, int64_t time, int64_t filters) {
-  return batch * filters * btf_tiles(batch, time, filters);
+  return batch * filters * btf_nsub(time);
 }
 size_t rqf_btf_scratch_bytes(int64_t batch, int64_t time, int64_t filters) {
   if (batch <= 0 || time <= 0 || filters <= 0) return 256;
-  return scratch_layout(batch * filters, btf_tiles(batch, time, filters)).total;
+  return btf_scratch_layout(batch, time, filters).total;
 }
 int64_t rqf_fbt_num_tiles(int64_t time) { return time <= 0 ? 0 : ceil_div(time, kFbtTile); }
 int64_t rqf_fbt_carry_count(int64_t filters, int64_t batch, int64_t time) {
@@ -535,15 +662,24 @@ int rqf_tbptt1_two_tap_backward(int layout, const float *c1, const float *tap0,
       !aligned(carries, 8) || !aligned(scratch, 16))
     return RQF_ERR_ALIGN;
   if (layout == 0) {
-    BtfArgs a = btf_args(c1, tap0, tap1, z, grad_out, grad_z, grad_zw,
-                         const_cast<float *>(carries), scratch, B, T, F);
-    const unsigned grid = (unsigned)(B * a.nfb * a.ntiles);
-    const int nt = kBtfBwdWarps * 32;
-    if (fuse_act)
-      btf_launch_tbptt<true>(btf_subtiles(B, F), grid, nt, stream, a);
-    else
-      btf_launch_tbptt<false>(btf_subtiles(B, F), grid, nt, stream, a);
-    if ((st = launch_status()) != RQF_OK) return st;
+    // the (B,T,F) forward has no fused activation, so neither has its TBPTT(1) backward
+    if (fuse_act) return RQF_ERR_ARGUMENT;
+    if (btf_streaming(B, F)) {
+      const bs::BtfArgs sa = btfs_args(c1, tap0, tap1, z, grad_out, grad_z, grad_zw,
+                                       const_cast<float *>(carries), scratch, B, T, F);
+      if ((st = btfs_launch<2, kTwoTap>(sa, scratch, stream)) != RQF_OK) return st;
+      reduce_partials_kernel<<<(unsigned)F, 256, 0, stream>>>(
+          sa.partials, reinterpret_cast<float2 *>(grad_c1), reinterpret_cast<float2 *>(grad_tap0),
+          reinterpret_cast<float2 *>(grad_tap1), B, 1, F, sa.ntiles);
+      return launch_status();
+    }
+    static_assert(kBtfTbpttS == 4, "TBPTT(1) tiles of 4 sub-tiles");
+    const BtfArgs a = btf_args(c1, tap0, tap1, z, grad_out, grad_z, grad_zw,
+                               const_cast<float *>(carries), scratch, B, T, F, 2);
+    const bool vec = btf_vec(z, F, 8) && btf_vec(grad_out, F, 8);
+    st = vec ? btf_launch(btf_tbptt_bwd_kernel<true>, btf_tbptt_smem(), a, scratch, stream)
+             : btf_launch(btf_tbptt_bwd_kernel<false>, btf_tbptt_smem(), a, scratch, stream);
+    if (st != RQF_OK) return st;
     reduce_partials_kernel<<<(unsigned)F, 256, 0, stream>>>(
         a.partials, reinterpret_cast<float2 *>(grad_c1), reinterpret_cast<float2 *>(grad_tap0),
         reinterpret_cast<float2 *>(grad_tap1), B, 1, F, a.ntiles);

@@ -146,6 +146,60 @@ __device__ __forceinline__ float2 lookback_const(const u64 *flags, int pos, floa
   return acc;
 }
 
+// lookback_const reading kLookbackWin predecessors per round trip: when many
+// tiles of a row are in flight (few long rows split into many tiles), the
+// aggregates to combine before the first inclusive prefix arrive together.
+// Words after the first one not yet published are read again next round.
+constexpr int kLookbackWin = 4;
+__device__ __forceinline__ float2 lookback_const_win(const u64 *flags, int pos, float2 M) {
+  float2 acc = cz(), mult = cone();
+  int i = pos - 1;
+  unsigned spins = 0, ns = 32;
+  while (i >= 0) {
+    u64 w[2 * kLookbackWin];
+#pragma unroll
+    for (int q = 0; q < kLookbackWin; ++q) {
+      const int k = i - q >= 0 ? i - q : 0;
+      w[2 * q] = ld_relaxed_u64(flags + 2 * k);
+      w[2 * q + 1] = ld_relaxed_u64(flags + 2 * k + 1);
+    }
+    int used = 0;
+    bool done = false, stalled = false;
+#pragma unroll
+    for (int q = 0; q < kLookbackWin; ++q) {
+      if (done || stalled || i - q < 0) continue;
+      const unsigned s0 = (unsigned)(w[2 * q] >> 32), s1 = (unsigned)(w[2 * q + 1] >> 32);
+      if (s0 == 0u || s0 != s1) {
+        stalled = true;
+        continue;
+      }
+      const float2 v =
+          make_float2(__uint_as_float((unsigned)w[2 * q]), __uint_as_float((unsigned)w[2 * q + 1]));
+      acc = c_fma(mult, v, acc);
+      ++used;
+      if (s0 == kInclusive) {
+        done = true;
+        continue;
+      }
+      mult = c_mul(mult, M);
+    }
+    if (done) break;
+    i -= used;
+    if (used == 0) {  // the nearest unread predecessor has published nothing yet
+      if (++spins > kSpinLimit) {
+        latch_error(kErrLookbackTimeout);
+        break;
+      }
+      __nanosleep(ns);
+      ns = ns < 256u ? ns * 2u : 256u;
+    } else {
+      spins = 0;
+      ns = 32;
+    }
+  }
+  return acc;
+}
+
 // Same for tiles with their own gate aggregates (time-varying recurrences).
 __device__ __forceinline__ float2 lookback_pair(const u64 *flags, int pos) {
   float2 acc = cz(), mult = cone();
@@ -598,6 +652,12 @@ __device__ __forceinline__ void cp_async8(void *smem, const void *gmem, bool pre
   const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
   const int n = pred ? 8 : 0;
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(s), "l"(gmem), "r"(n)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *smem, const void *gmem, bool pred) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  const int n = pred ? 4 : 0;
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem), "r"(n)
                : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() {

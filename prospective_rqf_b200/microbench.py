@@ -22,6 +22,8 @@ Ops:
              complex); reports TFLOP/s (8 F^2 B T real flops per GEMM)
   projection_torch  the same two GEMMs through torch.matmul (cuBLAS fp32)
 
+--btf-path forces one (B,T,F) kernel family (1 streaming, 2 tile-resident).
+
 Every tensor is at least --T x --B x --F complex64; the shapes used for the
 committed figures exceed the 126 MB L2, so the timings read HBM.
 """
@@ -183,9 +185,16 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--groups", type=int, default=8)
     ap.add_argument("--truncated", action="store_true")
+    ap.add_argument("--btf-path", type=int, choices=(0, 1, 2), default=0,
+                    help="(B,T,F) kernel family: 0 automatic, 1 streaming, 2 tile-resident")
     a = ap.parse_args(argv)
-    print(json.dumps(measure(a.op, a.F, a.B, a.T, a.iters, a.warmup, a.groups, a.truncated)),
-          flush=True)
+    if a.btf_path:
+        from . import _abi
+
+        _abi.load().rqf_btf_select_path(a.btf_path)
+    out = measure(a.op, a.F, a.B, a.T, a.iters, a.warmup, a.groups, a.truncated)
+    out["btf_path"] = a.btf_path
+    print(json.dumps(out), flush=True)
 
 
 if __name__ == "__main__":

@@ -77,11 +77,23 @@ def test_size_queries(lib):
     assert lib.rqf_fbt_num_tiles(2049) == 2
     assert lib.rqf_fbt_num_tiles(0) == 0
     assert lib.rqf_fbt_carry_count(128, 16, 16000) == 128 * 16 * 8
-    assert lib.rqf_btf_num_tiles(161) == 2
-    assert lib.rqf_btf_carry_count(32, 161, 128) == 32 * 128 * 2
+    assert lib.rqf_btf_num_tiles(161) == 3  # 64-step sub-tiles
+    assert lib.rqf_btf_carry_count(32, 161, 128) == 32 * 128 * 3
     s = lib.rqf_fbt_scratch_bytes(128, 16, 16000)
     assert s % 256 == 0 and s >= 256 + 128 * 16 * 8 * 40
     assert lib.rqf_btf_scratch_bytes(0, 10, 10) == 256
+
+
+def test_btf_path_selector(lib):
+    prev = lib.rqf_btf_select_path(2)
+    try:
+        assert prev == 0
+        assert lib.rqf_btf_select_path(1) == 2
+        assert lib.rqf_btf_select_path(3) == -1
+        assert lib.rqf_btf_select_path(-1) == -1
+        assert lib.rqf_btf_select_path(0) == 1
+    finally:
+        lib.rqf_btf_select_path(prev)
 
 
 def test_host_side_validation_needs_no_gpu(lib):

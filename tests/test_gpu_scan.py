@@ -31,6 +31,19 @@ def rqf():
     return prospective_rqf_b200
 
 
+@pytest.fixture(params=[1, 2], ids=["streaming", "resident"])
+def btf_path(request):
+    """Runs a (B,T,F) test under each kernel family (rqf_btf_select_path):
+    1 = streaming (few chains), 2 = tile-resident (many chains)."""
+    from prospective_rqf_b200 import _abi
+
+    lib = _abi.load()
+    prev = lib.rqf_btf_select_path(request.param)
+    assert prev >= 0
+    yield request.param
+    lib.rqf_btf_select_path(prev)
+
+
 def dev(a, dtype=torch.complex64, grad=False):
     t = torch.from_numpy(np.ascontiguousarray(a)).to("cuda").to(dtype)
     return t.requires_grad_(grad)
@@ -79,7 +92,7 @@ def check_fbt(ins, y, gy, c1, t0, t1, z, fuse, layout="fbt"):
 
 
 # ----------------------------------------------------------- goldens
-def test_golden_scan_complex():
+def test_golden_scan_complex(btf_path):
     g = golden("scan_complex")
     c1, c2, u = dev(g["c1"], grad=True), dev(g["c2"], grad=True), dev(g["u"], grad=True)
     y = rqf()._triton_chunked_scan(c1, c2, u)
@@ -89,7 +102,7 @@ def test_golden_scan_complex():
         assert_close(host(t.grad), g[k], GRAD_TOL, k)
 
 
-def test_golden_real_input_cfg1_style():
+def test_golden_real_input_cfg1_style(btf_path):
     g = golden("scan_real_cfg1")
     c1, c2 = dev(g["c1"], grad=True), dev(g["c2"], grad=True)
     u = dev(g["u"], dtype=torch.float32, grad=True)
@@ -103,7 +116,7 @@ def test_golden_real_input_cfg1_style():
     assert_close(u.grad.cpu().numpy(), g["gu"], GRAD_TOL, "gu")
 
 
-def test_golden_prospective_btf():
+def test_golden_prospective_btf(btf_path):
     g = golden("prospective_btf")
     ins = [dev(g[k], grad=True) for k in ("c1", "tap0", "tap1", "x")]
     y = rqf()._triton_chunked_scan_prospective(*ins)
@@ -249,17 +262,20 @@ def test_fbt_matches_btf_layout():
 
 
 # ------------------------------------------- (B,T,F) sweeps vs oracle
-# A (B,T,F) tile is S sub-tiles of 128 steps, S from the chain count
-# B * ceil(F / 32): S = 8 below 20 chains, 4 below 40, 2 below 80, else 1.
+# Every shape runs under both (B,T,F) kernel families.  Chains = B * ceil(F / 32).
+# Streaming tiles: S x 128 steps, S = 8 below 20 chains, 4 below 40, 2 below 80,
+# else 1.  Tile-resident tiles: 1..4 (forward) or 1..2 (backward) x 64 steps,
+# the longest leaving a tile per SM, no longer than T needs.
 BTF_SHAPES = [(1, 1, 1), (2, 63, 5), (2, 128, 32), (3, 129, 33), (2, 1023, 8), (1, 777, 16),
-              (2, 4096, 96), (2, 16000, 32),
-              (10, 2000, 96), (16, 3001, 33),   # 30 / 32 chains: S = 4
-              (45, 700, 32),                    # 45 chains: S = 2
-              (80, 300, 32), (40, 257, 70)]     # 80 / 120 chains: S = 1
+              (2, 4096, 96), (2, 16000, 32),    # resident: 125 / 250 tiles per chain
+              (10, 2000, 96), (16, 3001, 33),   # 30 / 32 chains
+              (45, 700, 32),                    # 45 chains
+              (80, 300, 32), (40, 257, 70),     # 80 / 120 chains
+              (160, 1100, 32)]                  # 160 chains: resident tiles of 4 x 64
 
 
 @pytest.mark.parametrize("B,T,F", BTF_SHAPES)
-def test_btf_plain_vs_oracle(B, T, F):
+def test_btf_plain_vs_oracle(B, T, F, btf_path):
     rng = np.random.default_rng(B * 100000 + T * 10 + F)
     c1 = coeffs(rng, F)
     c2 = c64(crandn(rng, F, 0.1))
@@ -275,7 +291,7 @@ def test_btf_plain_vs_oracle(B, T, F):
 
 
 @pytest.mark.parametrize("B,T,F", BTF_SHAPES)
-def test_btf_prospective_vs_oracle(B, T, F):
+def test_btf_prospective_vs_oracle(B, T, F, btf_path):
     rng = np.random.default_rng(7 + B * 100000 + T * 10 + F)
     c1 = coeffs(rng, F)
     t0, t1 = c64(crandn(rng, F, 0.5)), c64(crandn(rng, F, 0.5))
@@ -290,7 +306,7 @@ def test_btf_prospective_vs_oracle(B, T, F):
         assert_close(host(t.grad), r, GRAD_TOL, k)
 
 
-def test_btf_real_input_matches_promoted():
+def test_btf_real_input_matches_promoted(btf_path):
     rng = np.random.default_rng(5)
     B, T, F = 3, 500, 20
     c1, c2 = coeffs(rng, F), c64(crandn(rng, F))
@@ -306,7 +322,7 @@ def test_btf_real_input_matches_promoted():
     torch.testing.assert_close(ur.grad, uc.grad.real, rtol=1e-5, atol=1e-5)
 
 
-def test_config1_exact_shapes():
+def test_config1_exact_shapes(btf_path):
     """u real [32,161,128] ~ N(0,1), lambda = r e^{i theta},
     r ~ U(0.90, 0.999), theta ~ U(0, pi), b ~ CN(0,1)/sqrt(2), y0 = 0; grads of
     sum |y|^2 w.r.t. u, lambda and b."""
@@ -332,7 +348,7 @@ def test_config1_exact_shapes():
 # ------------------------------------------------------- TBPTT(1)
 @pytest.mark.parametrize("layout", ["btf", "fbt"])
 @pytest.mark.parametrize("T,B", [(1, 3), (5, 3), (2049, 3), (3000, 3), (1500, 30), (700, 90)])
-def test_tbptt_vs_oracle(layout, T, B):
+def test_tbptt_vs_oracle(layout, T, B, btf_path):
     rng = np.random.default_rng(T + B + (0 if layout == "btf" else 1))
     F = 6
     shape = (B, T, F) if layout == "btf" else (F, B, T)
