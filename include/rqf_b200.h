@@ -107,6 +107,17 @@ int rqf_chunked_scan_forward(const float *c1, const float *c2, const void *u,
                              void *scratch, int64_t batch, int64_t time,
                              int64_t filters, rqf_stream_t stream);
 
+/* Magnitude |y[t]| of the same scan, for no-grad consumers: replaces
+ * rqf_models/ops/triton_scan_kernel.py:_sequential_scan_forward_abs_raw_block_f
+ * (:507) and _sequential_scan_real_forward_abs_raw_block_f (:1531), reached
+ * from rqf_models/ops/scan.py:sequential_scan_abs (:381-432).  y_abs is
+ * float32 (B,T,F); no carries are saved (there is no backward); scratch as
+ * rqf_btf_scratch_bytes. */
+int rqf_chunked_scan_abs_forward(const float *c1, const float *c2, const void *u,
+                                 int u_is_real, float *y_abs, void *scratch,
+                                 int64_t batch, int64_t time, int64_t filters,
+                                 rqf_stream_t stream);
+
 /* Replaces chunked_scan_kernel.py:_chunked_scan_backward_raw (:252) /
  * _chunked_scan_backward_kernel (:122): g[t] = gy[t] + conj(c1) g[t+1];
  * grad_u = conj(c2) g (real part only when u_is_real);

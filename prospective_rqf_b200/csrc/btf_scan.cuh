@@ -232,6 +232,16 @@ __device__ __forceinline__ float2 btf_drive1(const BtfConst &c, float2 x, float2
   return DRIVE == kTwoTap ? c_fma(c.t1, xprev, c_mul(c.c2, x)) : c_mul(c.c2, x);
 }
 
+// Forward output: the complex state, or (ABS) its magnitude |y| as float, the
+// inference epilogue of rqf_models/ops/scan.py:sequential_scan_abs (:381-432).
+template <bool ABS>
+__device__ __forceinline__ void btf_store_y(void *out, int64_t idx, float2 e) {
+  if constexpr (ABS)
+    __stcs(static_cast<float *>(out) + idx, sqrtf(fmaf(e.x, e.x, e.y * e.y)));
+  else
+    __stcs(static_cast<float2 *>(out) + idx, e);
+}
+
 // Composition of the 8 warps' values v[w] with gate g per warp: sum g^(7-w) v[w].
 __device__ __forceinline__ float2 btf_total8(const float2 (*v)[32], float2 g, int lane) {
   float2 X = cz();
@@ -270,7 +280,9 @@ constexpr size_t kBtfTbpttStage = (size_t)(kHCarry + 1) * 32 * sizeof(float2) +
 constexpr size_t btf_tbptt_smem() { return 2 * kBtfTbpttStage; }
 
 // ------------------------------------------------------------ forward
-template <int DRIVE, bool VECX, int S>
+// ABS: write |y| (float) instead of y; a null carries pointer skips the saved
+// entry states (no backward follows).
+template <int DRIVE, bool VECX, int S, bool ABS = false>
 __global__ void __launch_bounds__(kBtfThreads, 3) btf_fwd_kernel(const BtfArgs a) {
   using E = typename BtfElem<DRIVE>::T;
   extern __shared__ __align__(16) unsigned char btf_dsm[];
@@ -348,14 +360,14 @@ __global__ void __launch_bounds__(kBtfThreads, 3) btf_fwd_kernel(const BtfArgs a
     for (int s = 0; s < S; ++s) {
       s_C[s][lane] = C;
       const int sub = tl.j * S + s;
-      if (f < a.F && sub < a.nsub) a.carries[(tl.b * a.F + f) * a.nsub + sub] = C;
+      if (a.carries && f < a.F && sub < a.nsub) a.carries[(tl.b * a.F + f) * a.nsub + sub] = C;
       C = c_fma(c.gL, C, s_X[s][lane]);
     }
   }
   __syncthreads();
   // pass 2: outputs
   if (f < a.F) {
-    float2 *yo = static_cast<float2 *>(a.out) + (tl.b * a.T + ts0 + rw) * a.F + f;
+    int64_t yo = (tl.b * a.T + ts0 + rw) * a.F + f;
 #pragma unroll 1
     for (int s = 0; s < S; ++s, yo += (int64_t)kBtfSub * a.F) {
       float2 e = c_fma(c.Gw, s_C[s][lane], Xw[s]);
@@ -371,11 +383,11 @@ __global__ void __launch_bounds__(kBtfThreads, 3) btf_fwd_kernel(const BtfArgs a
 #pragma unroll
         for (int k = 0; k < kBtfK; ++k) b[k] = btf_drive1<DRIVE>(c, v[k + 1], v[k]);
       }
-      float2 *p = yo;
+      int64_t p = yo;
 #pragma unroll
       for (int k = 0; k < kBtfK; ++k, p += a.F) {
         e = c_fma(c.lam, e, b[k]);
-        if (k < kmax) __stcs(p, e);
+        if (k < kmax) btf_store_y<ABS>(a.out, p, e);
       }
     }
   }

@@ -101,7 +101,9 @@ __device__ __forceinline__ void btf_drive(const BtfArgs &a, int64_t base, int64_
 }
 
 // ------------------------------------------------------------ forward
-template <int NW, int K, int S, int DRIVE>
+// ABS: write |y| (float) instead of y (rqf::btf_store_y); a null carries
+// pointer skips the saved entry states.
+template <int NW, int K, int S, int DRIVE, bool ABS = false>
 __global__ void __launch_bounds__(NW * 32) btf_fwd_kernel(const BtfArgs a) {
   constexpr int L = NW * K;  // sub-tile
   static_assert(L == kBtfSub, "sub-tile length");
@@ -163,7 +165,7 @@ __global__ void __launch_bounds__(NW * 32) btf_fwd_kernel(const BtfArgs a) {
         C = lookback_const_win(fl, j, M);
         if (has_next) flag_publish2(fl + 2 * j, c_fma(M, C, Xtile), kInclusive);
       }
-      a.carries[row * a.ntiles + j] = C;
+      if (a.carries) a.carries[row * a.ntiles + j] = C;
     }
     s_C[lane] = C;
   }
@@ -171,7 +173,6 @@ __global__ void __launch_bounds__(NW * 32) btf_fwd_kernel(const BtfArgs a) {
 
   // pass 2: outputs, sub-tile by sub-tile from their entry states
   float2 es = s_C[lane];
-  float2 *yout = static_cast<float2 *>(a.out);
 #pragma unroll 1
   for (int s = 0; s < S; ++s) {
     const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
@@ -190,7 +191,7 @@ __global__ void __launch_bounds__(NW * 32) btf_fwd_kernel(const BtfArgs a) {
     for (int k = 0; k < K; ++k) {
       e = c_fma(lam, e, b[k]);
       const int64_t t = tw + k;
-      if (fv && t < a.T) __stcs(yout + base + t * a.F, e);
+      if (fv && t < a.T) btf_store_y<ABS>(a.out, base + t * a.F, e);
     }
     es = c_fma(gL, es, s_sub[s][lane]);
   }

@@ -215,12 +215,18 @@ int btf_launch(Kern kernel, size_t smem, const BtfArgs &a, void *scratch, cudaSt
   return launch_status();
 }
 
-template <int DRIVE, bool VEC>
+template <int DRIVE, bool VEC, bool ABS = false>
 int btf_launch_fwd(const BtfArgs &a, void *scratch, cudaStream_t stream) {
   switch (a.S) {
-    case 1: return btf_launch(btf_fwd_kernel<DRIVE, VEC, 1>, btf_fwd_smem<DRIVE, 1>(), a, scratch, stream);
-    case 2: return btf_launch(btf_fwd_kernel<DRIVE, VEC, 2>, btf_fwd_smem<DRIVE, 2>(), a, scratch, stream);
-    default: return btf_launch(btf_fwd_kernel<DRIVE, VEC, 4>, btf_fwd_smem<DRIVE, 4>(), a, scratch, stream);
+    case 1:
+      return btf_launch(btf_fwd_kernel<DRIVE, VEC, 1, ABS>, btf_fwd_smem<DRIVE, 1>(), a, scratch,
+                        stream);
+    case 2:
+      return btf_launch(btf_fwd_kernel<DRIVE, VEC, 2, ABS>, btf_fwd_smem<DRIVE, 2>(), a, scratch,
+                        stream);
+    default:
+      return btf_launch(btf_fwd_kernel<DRIVE, VEC, 4, ABS>, btf_fwd_smem<DRIVE, 4>(), a, scratch,
+                        stream);
   }
 }
 
@@ -292,10 +298,11 @@ bs::BtfArgs btfs_args(const float *c1, const float *c2, const float *tap1, const
 }
 
 // One streaming kernel: KIND 0 forward, 1 backward, 2 TBPTT(1) backward.
-template <int KIND, int DRIVE, int S>
+template <int KIND, int DRIVE, int S, bool ABS>
 void btfs_kernel(const bs::BtfArgs &a, unsigned grid, cudaStream_t st) {
   if constexpr (KIND == 0)
-    bs::btf_fwd_kernel<kBtfsFwdWarps, kBtfsFwdK, S, DRIVE><<<grid, kBtfsFwdWarps * 32, 0, st>>>(a);
+    bs::btf_fwd_kernel<kBtfsFwdWarps, kBtfsFwdK, S, DRIVE, ABS>
+        <<<grid, kBtfsFwdWarps * 32, 0, st>>>(a);
   else if constexpr (KIND == 1)
     bs::btf_bwd_kernel<kBtfsBwdWarps, kBtfsBwdK, S, DRIVE><<<grid, kBtfsBwdWarps * 32, 0, st>>>(a);
   else
@@ -304,48 +311,59 @@ void btfs_kernel(const bs::BtfArgs &a, unsigned grid, cudaStream_t st) {
 }
 
 // Launches a streaming kernel over all tiles after clearing the ticket and flags.
-template <int KIND, int DRIVE>
+template <int KIND, int DRIVE, bool ABS = false>
 int btfs_launch(const bs::BtfArgs &a, void *scratch, cudaStream_t st) {
   const int rc = clear_lookback(scratch, scratch_layout(a.B * a.F, a.ntiles), st);
   if (rc != RQF_OK) return rc;
   const unsigned grid = (unsigned)((int64_t)a.ngroups * a.ntiles);
   switch (btfs_subtiles(a.B, a.F)) {
-    case 1: btfs_kernel<KIND, DRIVE, 1>(a, grid, st); break;
-    case 2: btfs_kernel<KIND, DRIVE, 2>(a, grid, st); break;
-    case 4: btfs_kernel<KIND, DRIVE, 4>(a, grid, st); break;
-    default: btfs_kernel<KIND, DRIVE, 8>(a, grid, st); break;
+    case 1: btfs_kernel<KIND, DRIVE, 1, ABS>(a, grid, st); break;
+    case 2: btfs_kernel<KIND, DRIVE, 2, ABS>(a, grid, st); break;
+    case 4: btfs_kernel<KIND, DRIVE, 4, ABS>(a, grid, st); break;
+    default: btfs_kernel<KIND, DRIVE, 8, ABS>(a, grid, st); break;
   }
   return launch_status();
 }
 
-int btf_forward(int drive, const float *c1, const float *c2, const float *tap1, const void *x,
-                float *y, float *carries, void *scratch, int64_t B, int64_t T, int64_t F,
-                cudaStream_t stream) {
-  int st = btf_dims_ok(B, T, F);
-  if (st != RQF_OK) return st;
-  if (B == 0 || T == 0 || F == 0) return RQF_OK;
-  if (!c1 || !c2 || !x || !y || !carries || !scratch || (drive == kTwoTap && !tap1))
-    return RQF_ERR_ARGUMENT;
-  if (!aligned(c1, 8) || !aligned(c2, 8) || !aligned(y, 8) || !aligned(carries, 8) ||
-      !aligned(scratch, 16) || !aligned(x, drive == kReal ? 4 : 8) ||
-      (tap1 && !aligned(tap1, 8)))
-    return RQF_ERR_ALIGN;
+// Forward of one drive in one family; ABS writes |y| (float) and saves no carries.
+template <int DRIVE, bool ABS>
+int btf_forward_drive(const float *c1, const float *c2, const float *tap1, const void *x, void *y,
+                      float *carries, void *scratch, int64_t B, int64_t T, int64_t F,
+                      cudaStream_t stream) {
   if (btf_streaming(B, F)) {
     const bs::BtfArgs sa = btfs_args(c1, c2, tap1, x, nullptr, y, nullptr, carries, scratch, B, T, F);
-    if (drive == kReal) return btfs_launch<0, kReal>(sa, scratch, stream);
-    if (drive == kPlain) return btfs_launch<0, kPlain>(sa, scratch, stream);
-    return btfs_launch<0, kTwoTap>(sa, scratch, stream);
+    return btfs_launch<0, DRIVE, ABS>(sa, scratch, stream);
   }
   const BtfArgs a = btf_args(c1, c2, tap1, x, nullptr, y, nullptr, carries, scratch, B, T, F,
                              btf_log2_tile(B, T, F, 2));
+  const bool vec = btf_vec(x, F, DRIVE == kReal ? 4 : 8);
+  return vec ? btf_launch_fwd<DRIVE, true, ABS>(a, scratch, stream)
+             : btf_launch_fwd<DRIVE, false, ABS>(a, scratch, stream);
+}
+
+int btf_forward(int drive, const float *c1, const float *c2, const float *tap1, const void *x,
+                void *y, float *carries, void *scratch, int64_t B, int64_t T, int64_t F,
+                cudaStream_t stream, bool abs_out = false) {
+  int st = btf_dims_ok(B, T, F);
+  if (st != RQF_OK) return st;
+  if (B == 0 || T == 0 || F == 0) return RQF_OK;
+  if (!c1 || !c2 || !x || !y || (!carries && !abs_out) || !scratch ||
+      (drive == kTwoTap && !tap1) || (abs_out && drive == kTwoTap))
+    return RQF_ERR_ARGUMENT;
+  if (!aligned(c1, 8) || !aligned(c2, 8) || !aligned(y, abs_out ? 4 : 8) ||
+      (carries && !aligned(carries, 8)) || !aligned(scratch, 16) ||
+      !aligned(x, drive == kReal ? 4 : 8) || (tap1 && !aligned(tap1, 8)))
+    return RQF_ERR_ALIGN;
+  if (abs_out)
+    return drive == kReal
+               ? btf_forward_drive<kReal, true>(c1, c2, tap1, x, y, nullptr, scratch, B, T, F, stream)
+               : btf_forward_drive<kPlain, true>(c1, c2, tap1, x, y, nullptr, scratch, B, T, F,
+                                                 stream);
   if (drive == kReal)
-    return btf_vec(x, F, 4) ? btf_launch_fwd<kReal, true>(a, scratch, stream)
-                            : btf_launch_fwd<kReal, false>(a, scratch, stream);
+    return btf_forward_drive<kReal, false>(c1, c2, tap1, x, y, carries, scratch, B, T, F, stream);
   if (drive == kPlain)
-    return btf_vec(x, F, 8) ? btf_launch_fwd<kPlain, true>(a, scratch, stream)
-                            : btf_launch_fwd<kPlain, false>(a, scratch, stream);
-  return btf_vec(x, F, 8) ? btf_launch_fwd<kTwoTap, true>(a, scratch, stream)
-                          : btf_launch_fwd<kTwoTap, false>(a, scratch, stream);
+    return btf_forward_drive<kPlain, false>(c1, c2, tap1, x, y, carries, scratch, B, T, F, stream);
+  return btf_forward_drive<kTwoTap, false>(c1, c2, tap1, x, y, carries, scratch, B, T, F, stream);
 }
 
 template <int DRIVE>
@@ -490,6 +508,13 @@ int rqf_chunked_scan_forward(const float *c1, const float *c2, const void *u, in
                              int64_t time, int64_t filters, rqf_stream_t stream) {
   return btf_forward(u_is_real ? kReal : kPlain, c1, c2, nullptr, u, y, carries, scratch, batch,
                      time, filters, stream);
+}
+
+int rqf_chunked_scan_abs_forward(const float *c1, const float *c2, const void *u, int u_is_real,
+                                 float *y_abs, void *scratch, int64_t batch, int64_t time,
+                                 int64_t filters, rqf_stream_t stream) {
+  return btf_forward(u_is_real ? kReal : kPlain, c1, c2, nullptr, u, y_abs, nullptr, scratch,
+                     batch, time, filters, stream, true);
 }
 
 int rqf_chunked_scan_backward(const float *c1, const float *c2, const void *u, int u_is_real,

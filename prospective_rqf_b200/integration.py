@@ -9,6 +9,7 @@ behind it change.  ``uninstall()`` restores the originals.
 
 Call sites served (reference paths):
   rqf_models/ops/scan.py:367, :509            -> _triton_chunked_scan
+  rqf_models/ops/scan.py:430-432               -> |scan| epilogue (sequential_scan_abs)
   rqf_models/backbones/rqf/block.py:926-934   -> _triton_chunked_scan_prospective
   rqf_models/backbones/rqf/pure.py:234-238    -> fbt_prospective_scan / fbt_recompute_scan
   rqf_models/backbones/rqf/block.py:882, :904 -> TBPTT(1) fused surrogate on CUDA
@@ -28,6 +29,10 @@ _BINDINGS = [
     ("rqf_models.ops.chunked_scan_kernel", "_triton_chunked_scan_prospective",
      ops._triton_chunked_scan_prospective),
     ("rqf_models.ops.scan", "_triton_chunked_scan", ops._triton_chunked_scan),
+    ("rqf_models.ops.scan", "_sequential_scan_forward_abs_raw_block_f",
+     ops._sequential_scan_forward_abs_raw_block_f),
+    ("rqf_models.ops.scan", "_sequential_scan_real_forward_abs_raw_block_f",
+     ops._sequential_scan_real_forward_abs_raw_block_f),
     ("rqf_models.ops.fbt_scan_kernel", "fbt_prospective_scan", ops.fbt_prospective_scan),
     ("rqf_models.ops.fbt_scan_kernel", "fbt_recompute_scan", ops.fbt_recompute_scan),
     ("rqf_models.backbones.rqf.block", "_triton_chunked_scan_prospective",

@@ -13,6 +13,8 @@ Reference callables (paths inside the reference project):
   fbt_recompute_scan                rqf_models/ops/fbt_scan_kernel.py:667
   sequential_scan / parallel_scan   rqf_models/ops/scan.py:290 / :435 (CUDA branch)
   sequential_scan_abs               rqf_models/ops/scan.py:381
+  _sequential_scan_forward_abs_raw_block_f        triton_scan_kernel.py:507
+  _sequential_scan_real_forward_abs_raw_block_f   triton_scan_kernel.py:1531
 New (no single reference callable; replaces the autograd surrogate of
 rqf_models/backbones/rqf/block.py:_scan_two_tap_with_grad_mode :904-954 and
 _scan_with_grad_mode :882-902):
@@ -432,9 +434,53 @@ def parallel_scan(C1, C2, u, B=None):
     return sequential_scan(C1, C2, u, B)
 
 
+def _scan_abs(C1, C2, u) -> torch.Tensor:
+    """|y| of y[t] = C1*y[t-1] + C2*u[t] on (B,T,F), written by the scan's own
+    epilogue (no complex output, no saved context); float32 (B,T,F)."""
+    dev = _require_cuda(C1, C2, u)
+    real = not u.is_complex()
+    uu = u.to(torch.float32).contiguous() if real else _c64(u)
+    B, T, F = _shape3(uu, "u")
+    c1, c2 = _coef(C1, F, "C1"), _coef(C2, F, "C2")
+    lib = _abi.load()
+    y = torch.empty((B, T, F), dtype=torch.float32, device=dev)
+    scratch = _scratch(lib.rqf_btf_scratch_bytes(B, T, F), dev)
+    with _timing.launch("rqf_chunked_scan_abs_forward", B * T * F, _nbytes(uu, y)):
+        _abi.check(lib.rqf_chunked_scan_abs_forward(
+            _abi.ptr(c1), _abi.ptr(c2), _abi.ptr(uu), int(real), _abi.ptr(y), _abi.ptr(scratch),
+            B, T, F, _abi.stream_of(uu)), "rqf_chunked_scan_abs_forward")
+    _done(dev)
+    return y
+
+
+def _sequential_scan_forward_abs_raw_block_f(C1, C2, u):
+    """Drop-in for rqf_models/ops/triton_scan_kernel.py:
+    _sequential_scan_forward_abs_raw_block_f (:507): |scan| of complex u."""
+    if not u.is_complex():
+        raise ValueError("_sequential_scan_forward_abs_raw_block_f expects complex input")
+    return _scan_abs(C1, C2, u)
+
+
+def _sequential_scan_real_forward_abs_raw_block_f(C1, C2, u):
+    """Drop-in for triton_scan_kernel.py:_sequential_scan_real_forward_abs_raw_block_f
+    (:1531): |scan| of real u (float32)."""
+    if u.is_complex():
+        raise ValueError("_sequential_scan_real_forward_abs_raw_block_f expects real input")
+    return _scan_abs(C1, C2, u)
+
+
 def sequential_scan_abs(C1, C2, u, B=None):
-    """|sequential_scan(...)| (rqf_models/ops/scan.py:381-432)."""
-    return sequential_scan(C1, C2, u, B).abs()
+    """|sequential_scan(...)| (rqf_models/ops/scan.py:381-432).  Without a B
+    matrix and with no gradient required, the magnitude is written by the scan
+    kernel's epilogue (half the output bytes, no separate abs pass), as the
+    reference's fast path; otherwise the complex scan runs and .abs() follows."""
+    needs_grad = torch.is_grad_enabled() and (
+        u.requires_grad or getattr(C1, "requires_grad", False)
+        or getattr(C2, "requires_grad", False) or (B is not None and B.requires_grad))
+    if B is not None or needs_grad or not u.is_cuda:
+        return sequential_scan(C1, C2, u, B).abs()
+    C1, C2, u = _prepare(C1, C2, u, None)
+    return _scan_abs(C1, C2, u)
 
 
 # ------------------------------------------------------ selective scan

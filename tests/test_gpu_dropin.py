@@ -15,7 +15,8 @@ Modules covered:
 - the S4-RQF block (prospective (B,T,F) scan, block.py:926-934, s4_rqf.py:176-208);
 - the S5 layer (sequential_scan, scan.py:367; s5/layer.py:245-257);
 - TBPTT(1) (block.py:904-954);
-- the selective Pure RQF encoder (selective_scan.py:119, :133).
+- the selective Pure RQF encoder (selective_scan.py:119, :133);
+- sequential_scan_abs under no_grad, the fused-|y| path (scan.py:381-432).
 
 Smooth activations are used where gradients are compared: a split-ReLU
 derivative can flip between two fp32 implementations at a state within
@@ -152,3 +153,33 @@ def test_selective_pure_encoder_forward():
     x = torch.randn(2, 1024, 1, device="cuda", generator=torch.Generator("cuda").manual_seed(6))
     launched = _compare(enc, x, fwd_only=True)
     assert "rqf_selective_forward" in launched
+
+
+def test_sequential_scan_abs_epilogue():
+    """rqf_models.ops.scan.sequential_scan_abs under no_grad: the reference's
+    fused-|y| Triton path against this backend's epilogue (complex and real u)."""
+    import prospective_rqf_b200 as rqf
+    from prospective_rqf_b200 import _timing
+    from rqf_models.ops.scan import sequential_scan_abs
+
+    g = torch.Generator("cuda").manual_seed(7)
+    F = 48
+    c1 = torch.polar(0.9 + 0.09 * torch.rand(F, device="cuda", generator=g),
+                     3.0 * torch.rand(F, device="cuda", generator=g))
+    c2 = torch.randn(F, dtype=torch.complex64, device="cuda", generator=g)
+    for u in (torch.randn(3, 700, F, dtype=torch.complex64, device="cuda", generator=g),
+              torch.randn(3, 700, F, device="cuda", generator=g)):
+        rqf.uninstall()
+        with torch.no_grad():
+            y0 = sequential_scan_abs(c1, c2, u)
+        rqf.install()
+        try:
+            with _timing.KernelTimer() as timer, torch.no_grad():
+                y1 = sequential_scan_abs(c1, c2, u)
+            launched = timer.summary()
+        finally:
+            rqf.uninstall()
+        assert "rqf_chunked_scan_abs_forward" in launched
+        e = rel_err(_np(y1), _np(y0))
+        assert e <= FWD_TOL, f"|y| differs by {e:.2e}"
+

@@ -322,6 +322,26 @@ def test_btf_real_input_matches_promoted(btf_path):
     torch.testing.assert_close(ur.grad, uc.grad.real, rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("B,T,F,real", [(1, 1, 1, False), (2, 1023, 8, False), (3, 500, 20, True),
+                                         (80, 300, 32, False), (160, 1100, 32, True)])
+def test_scan_abs_epilogue_vs_oracle(B, T, F, real, btf_path):
+    """sequential_scan_abs without gradients: |y| written by the scan's epilogue
+    (float32 output), against |oracle scan|."""
+    rng = np.random.default_rng(11 + B * 1000 + T + F)
+    c1, c2 = coeffs(rng, F), c64(crandn(rng, F, 0.5))
+    if real:
+        u = rng.standard_normal((B, T, F)).astype(np.float32).astype(np.float64)
+        ud = dev(u, dtype=torch.float32)
+    else:
+        u = c64(crandn(rng, (B, T, F)))
+        ud = dev(u)
+    with torch.no_grad():
+        y = rqf().sequential_scan_abs(dev(c1), dev(c2), ud)
+    assert y.dtype == torch.float32 and tuple(y.shape) == (B, T, F)
+    ref = np.abs(oracle.chunked_scan(c1, c2, u))
+    assert_close(y.cpu().numpy().astype(np.float64), ref, FWD_TOL, "|y|")
+
+
 def test_config1_exact_shapes(btf_path):
     """u real [32,161,128] ~ N(0,1), lambda = r e^{i theta},
     r ~ U(0.90, 0.999), theta ~ U(0, pi), b ~ CN(0,1)/sqrt(2), y0 = 0; grads of

@@ -122,6 +122,8 @@ def test_install_against_the_reference_tree(monkeypatch):
         import rqf_models.ops.selective_scan_kernel as sk
 
         assert sk.selective_forward is ops.selective_forward
-        assert len(patched) == 12
+        assert scan._sequential_scan_forward_abs_raw_block_f is \
+            ops._sequential_scan_forward_abs_raw_block_f
+        assert len(patched) == 14
     finally:
         integration.uninstall()
