@@ -225,9 +225,48 @@ class PureRQFEncoderB200(nn.Module):
             r.clamp_parameters()
 
 
+class _ReadoutHidden(torch.autograd.Function):
+    """hid = relu(W1 @ [Re h; Im h] + b1) over the (F, B*T) view of h, on the
+    split-TF32 tensor-core projections.
+
+    With V = W1[:, :F] - i W1[:, F:] (complex H x F), W1 @ [Re h; Im h] is
+    Re(V h), so the forward is one complex projection whose real part is kept;
+    the input cotangent is V^H g and the weight cotangent P = g h^H gives
+    [Re P, -Im P].  No [Re; Im] copy of h is made."""
+
+    @staticmethod
+    def forward(ctx, h, W1, b1):
+        F = h.shape[0]
+        V = torch.complex(W1[:, :F], -W1[:, F:]).contiguous()
+        pre = _project(V, h).real + b1[:, None, None]
+        mask = pre > 0
+        ctx.save_for_backward(h, V, mask)
+        return pre.mul_(mask)
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, ghid):
+        h, V, mask = ctx.saved_tensors
+        need = ctx.needs_input_grad
+        g = ghid * mask
+        gc = torch.complex(g, torch.zeros_like(g))
+        gh = _project(V, gc, conj_transpose=True) if need[0] else None
+        gW1 = None
+        if need[1]:
+            P = _weight_grad(gc, h)
+            gW1 = torch.cat([P.real, -P.imag], dim=1)
+        gb1 = g.sum(dim=(1, 2)) if need[2] else None
+        return gh, gW1, gb1
+
+
 class ComplexReadout(nn.Module):
     """Per-timestep MLP on [Re h; Im h] with mean-pooled logits
-    (train.py:ComplexReadoutClassifier, hidden_dims set)."""
+    (train.py:ComplexReadoutClassifier, hidden_dims set).
+
+    On CUDA with the tensor-core projections (the default), the hidden layer
+    runs as _ReadoutHidden, and with mean pooling the output layer is applied
+    to the time-mean of the hidden activations: mean_t(W2 hid_t + b2) =
+    W2 mean_t(hid_t) + b2, the same logits without the per-step output GEMM."""
 
     def __init__(self, features: int, num_classes: int, hidden_dims: int = 256, seed: int = 1):
         super().__init__()
@@ -243,6 +282,13 @@ class ComplexReadout(nn.Module):
 
     def forward(self, h: torch.Tensor, per_step: bool = False) -> torch.Tensor:
         F, B, T = h.shape
+        if PROJECTION == "tc" and h.is_cuda:
+            hid = _ReadoutHidden.apply(h, self.fc1.weight, self.fc1.bias)  # (H, B, T)
+            if per_step:
+                logits = torch.addmm(self.fc2.bias[:, None], self.fc2.weight,
+                                     hid.reshape(hid.shape[0], B * T))
+                return logits.reshape(-1, B, T).permute(1, 2, 0)  # (B, T, C)
+            return torch.addmm(self.fc2.bias[:, None], self.fc2.weight, hid.mean(dim=2)).t()
         feats = torch.cat([h.real, h.imag], dim=0).reshape(2 * F, B * T)
         hid = torch.relu(torch.addmm(self.fc1.bias[:, None], self.fc1.weight, feats))
         logits = torch.addmm(self.fc2.bias[:, None], self.fc2.weight, hid)  # (C, B*T)

@@ -245,3 +245,33 @@ def test_pure_block_tc_projection_matches_torch(F, B, T, fuse, monkeypatch):
     if not fuse:
         for a, b, k in zip(res["tc"][1], res["torch"][1], ("h", "W", "c1", "tap0", "tap1")):
             assert_close(_np(a.cpu()), _np(b.cpu()), 1e-4, f"grad {k}")
+
+
+# -------------------------------- readout on the tensor-core projections
+@pytest.mark.parametrize("per_step", [False, True])
+def test_readout_tc_matches_torch(per_step, monkeypatch):
+    """ComplexReadout with its hidden layer as Re(V h) on the split-TF32
+    projections (and, when mean-pooled, the output layer after pooling)
+    against the plain torch composition on [Re h; Im h]."""
+    from prospective_rqf_b200 import encoder
+
+    g = torch.Generator().manual_seed(13)
+    F, H, C, B, T = 64, 96, 7, 3, 2048
+    ro = encoder.ComplexReadout(F, C, H, seed=2).cuda()
+    with torch.no_grad():  # an output layer large enough to matter in the gradients
+        ro.fc2.weight.normal_(0.0, 0.1, generator=torch.Generator("cuda").manual_seed(3))
+    h = _crandn(g, F, B, T).cuda()
+    gout = torch.randn((B, T, C) if per_step else (B, C), generator=g).cuda()
+    res = {}
+    for mode in ("tc", "torch"):
+        monkeypatch.setattr(encoder, "PROJECTION", mode)
+        ro.zero_grad(set_to_none=True)
+        hh = h.clone().requires_grad_(True)
+        out = ro(hh, per_step=per_step)
+        out.backward(gout)
+        res[mode] = (out.detach(), hh.grad, {n: p.grad for n, p in ro.named_parameters()})
+    assert_close(_np(res["tc"][0].cpu()), _np(res["torch"][0].cpu()), FWD_TOL, "logits")
+    assert_close(_np(res["tc"][1].cpu()), _np(res["torch"][1].cpu()), GRAD_TOL, "grad h")
+    for n in res["torch"][2]:
+        assert_close(_np(res["tc"][2][n].cpu()), _np(res["torch"][2][n].cpu()), GRAD_TOL,
+                     f"grad {n}")
