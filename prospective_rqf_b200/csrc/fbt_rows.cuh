@@ -158,9 +158,16 @@ __global__ void __launch_bounds__(NT) fbt_fwd_rows_kernel(const FbtArgs a) {
         zp = (pc.j > 0) ? s_zlast : cz();
     }
     float2 b[K];
-    b[0] = c_fma(t1, zp, c_mul(t0, z[0]));
+    {
+      const CPair T0 = cpair(t0), T1 = cpair(t1);
+      float2 sp = c_swap(zp);
 #pragma unroll
-    for (int k = 1; k < K; ++k) b[k] = c_fma(t1, z[k - 1], c_mul(t0, z[k]));
+      for (int k = 0; k < K; ++k) {
+        const float2 sk = c_swap(z[k]);
+        b[k] = cp_fma(T0, z[k], sk, cp_mul(T1, k > 0 ? z[k - 1] : zp, sp));
+        sp = sk;
+      }
+    }
     float2 y = cz();
 #pragma unroll
     for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
@@ -256,9 +263,16 @@ __global__ void __launch_bounds__(NT, 3) fbt_bwd_rows_kernel(const FbtArgs a) {
     if (lane == 0) zp = warp > 0 ? read_sample<K>(zbuf - WSZ, 32 * K - 1) : s_meta[s][1];
 
     float2 b[K];
-    b[0] = c_fma(t1, zp, c_mul(t0, z[0]));
+    {
+      const CPair T0 = cpair(t0), T1 = cpair(t1);
+      float2 sp = c_swap(zp);
 #pragma unroll
-    for (int k = 1; k < K; ++k) b[k] = c_fma(t1, z[k - 1], c_mul(t0, z[k]));
+      for (int k = 0; k < K; ++k) {
+        const float2 sk = c_swap(z[k]);
+        b[k] = cp_fma(T0, z[k], sk, cp_mul(T1, k > 0 ? z[k - 1] : zp, sp));
+        sp = sk;
+      }
+    }
     float2 y = cz();
 #pragma unroll
     for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
@@ -279,15 +293,33 @@ __global__ void __launch_bounds__(NT, 3) fbt_bwd_rows_kernel(const FbtArgs a) {
     cta_scan_entry_rev<NT, LK>(h, dcarry, pw, lpow_r, gnext, Art, s_warp_r);
     dcarry = Art;  // g at this tile's first sample: right entry of the tile before it
     float2 gz[K];
+    // Element-wise products on paired fp32 FMAs: conj(t) g = (t.x, t.x) * g +
+    // (t.y, -t.y) * (g.y, g.x); the sums conj(v) g accumulate v * (g.x, g.x) and
+    // v * (g.y, g.y) in two pairs, combined once per tile.
+    const float2 T0X = make_float2(t0.x, t0.x), T0Y = make_float2(t0.y, -t0.y);
+    const float2 T1X = make_float2(t1.x, t1.x), T1Y = make_float2(t1.y, -t1.y);
+    float2 pc1 = cz(), qc1 = cz(), pt0 = cz(), qt0 = cz(), pt1 = cz(), qt1 = cz();
+    float2 gsw = make_float2(gnext.y, gnext.x);
 #pragma unroll
     for (int k = K - 1; k >= 0; --k) {
       const float2 g = c_fma(mu, gnext, b[k]);
-      gz[k] = c_cfma(t1, gnext, c_cfma(t0, g, cz()));
-      acc_c1 = c_cfma(yprev[k], g, acc_c1);
-      acc_t0 = c_cfma(z[k], g, acc_t0);
-      acc_t1 = c_cfma(k > 0 ? z[k - 1] : zp, g, acc_t1);
+      const float2 gs = make_float2(g.y, g.x);
+      gz[k] = __ffma2_rn(T0X, g, __ffma2_rn(T0Y, gs, __ffma2_rn(T1X, gnext, __fmul2_rn(T1Y, gsw))));
+      const float2 gx = make_float2(g.x, g.x), gy = make_float2(g.y, g.y);
+      pc1 = __ffma2_rn(yprev[k], gx, pc1);
+      qc1 = __ffma2_rn(yprev[k], gy, qc1);
+      pt0 = __ffma2_rn(z[k], gx, pt0);
+      qt0 = __ffma2_rn(z[k], gy, qt0);
+      const float2 zk1 = k > 0 ? z[k - 1] : zp;
+      pt1 = __ffma2_rn(zk1, gx, pt1);
+      qt1 = __ffma2_rn(zk1, gy, qt1);
       gnext = g;
+      gsw = gs;
     }
+    // conj(v) g = (v.x g.x + v.y g.y, v.x g.y - v.y g.x)
+    acc_c1 = c_add(acc_c1, make_float2(pc1.x + qc1.y, qc1.x - pc1.y));
+    acc_t0 = c_add(acc_t0, make_float2(pt0.x + qt0.y, qt0.x - pt0.y));
+    acc_t1 = c_add(acc_t1, make_float2(pt1.x + qt1.y, qt1.x - pt1.y));
     fbt_store_tile<K>(gbuf, gz, a.out + (size_t)pc.row * T, jt * L + wofs, T, lane);
     if (jt == 0) {  // row finished: deterministic CTA reduction of the row's sums
 #pragma unroll

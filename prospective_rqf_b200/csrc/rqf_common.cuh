@@ -41,6 +41,25 @@ __device__ __forceinline__ float2 c_cfma(float2 a, float2 b, float2 c) {
   return make_float2(fmaf(a.x, b.x, fmaf(a.y, b.y, c.x)),
                      fmaf(a.x, b.y, fmaf(-a.y, b.x, c.y)));
 }
+// Complex products on paired fp32 FMAs (__ffma2_rn, two lanes per
+// instruction): for a fixed complex a, a * v = (a.x, a.x) * v + (-a.y, a.y) *
+// (v.y, v.x).  cpair(a) holds the two constant pairs; the swapped operand
+// (v.y, v.x) is passed in so a caller can reuse it.
+struct CPair {
+  float2 re, im;
+};
+__device__ __forceinline__ CPair cpair(float2 a) {
+  return {make_float2(a.x, a.x), make_float2(-a.y, a.y)};
+}
+__device__ __forceinline__ float2 c_swap(float2 v) { return make_float2(v.y, v.x); }
+// a * v + c
+__device__ __forceinline__ float2 cp_fma(const CPair &a, float2 v, float2 vs, float2 c) {
+  return __ffma2_rn(a.re, v, __ffma2_rn(a.im, vs, c));
+}
+// a * v
+__device__ __forceinline__ float2 cp_mul(const CPair &a, float2 v, float2 vs) {
+  return __ffma2_rn(a.re, v, __fmul2_rn(a.im, vs));
+}
 // split-ReLU: relu(Re) + i relu(Im)   (rqf_models/backbones/rqf/utils/activations.py:14-18)
 __device__ __forceinline__ float2 c_relu(float2 a) {
   return make_float2(a.x > 0.f ? a.x : 0.f, a.y > 0.f ? a.y : 0.f);
