@@ -130,6 +130,43 @@ int rqf_chunked_scan_backward(const float *c1, const float *c2, const void *u,
                               int64_t time, int64_t filters,
                               rqf_stream_t stream);
 
+/* ---- multi-oscillator scan with C-weight reduction, (B,T,F) layout --- *
+ * Replaces rqf_models/ops/triton_scan_kernel.py:_triton_sequential_scan_multi_osc
+ * (:2499; forward _sequential_scan_multi_osc_forward_raw :1935, backward
+ * _sequential_scan_multi_osc_backward_raw :2280), its real-input and
+ * parallel variants (:3071, :4106) and magnitude epilogues (:2019, :2688),
+ * reached from rqf_models/backbones/rqf/block.py:_scan_standard_multi_osc
+ * (:737):
+ *   x_s[t] = c1_s x_s[t-1] + c2_s u[t, s / n],   s < filters * n,
+ *   out[t, f] = sum_{k<n} cw_{f n + k} x_{f n + k}[t],
+ * n = num_osc (a power of two <= 32, else RQF_ERR_SHAPE).  c1, c2, cw are
+ * complex (filters * n); u is complex, or float32 with u_is_real,
+ * (B,T,filters); out is complex (B,T,filters), or float32 |out| with out_abs
+ * (then carries may be null: nothing is saved).  Size carries and scratch
+ * with rqf_multi_osc_carry_count / _scratch_bytes. */
+int rqf_multi_osc_forward(const float *c1, const float *c2, const float *cw,
+                          const void *u, int u_is_real, void *out, int out_abs,
+                          float *carries, void *scratch, int64_t batch,
+                          int64_t time, int64_t filters, int64_t num_osc,
+                          rqf_stream_t stream);
+
+/* g_s[t] = conj(c1_s) g_s[t+1] + conj(cw_s) grad_out[t, f];
+ * grad_u[t, f] = sum_k conj(c2_s) g_s[t] (its real part when u_is_real);
+ * grad_c1_s = sum conj(x_s[t-1]) g_s[t], grad_c2_s = sum conj(u[t, f]) g_s[t],
+ * grad_cw_s = sum conj(x_s[t]) grad_out[t, f] (complex: the reference's real
+ * (filters*n, 2) C-weight gradient is its real view).  The three coefficient
+ * gradients are overwritten. */
+int rqf_multi_osc_backward(const float *c1, const float *c2, const float *cw,
+                           const void *u, int u_is_real, const float *carries,
+                           const float *grad_out, void *grad_u, float *grad_c1,
+                           float *grad_c2, float *grad_cw, void *scratch,
+                           int64_t batch, int64_t time, int64_t filters,
+                           int64_t num_osc, rqf_stream_t stream);
+int64_t rqf_multi_osc_carry_count(int64_t batch, int64_t time, int64_t filters,
+                                  int64_t num_osc);
+size_t rqf_multi_osc_scratch_bytes(int64_t batch, int64_t time, int64_t filters,
+                                   int64_t num_osc);
+
 /* ---- two-tap prospective scan, (B,T,F) layout ------------------------ *
  * Replaces chunked_scan_kernel.py:_chunked_prospective_forward_raw (:442) /
  * _chunked_prospective_kernel (:374):

@@ -57,6 +57,12 @@ SIGNATURES: dict[str, tuple] = {
     "rqf_fbt_scratch_bytes": (_sz, [_i64, _i64, _i64]),
     "rqf_chunked_scan_forward": (_int, [_p, _p, _p, _int, _p, _p, _p, _i64, _i64, _i64, _p]),
     "rqf_chunked_scan_abs_forward": (_int, [_p, _p, _p, _int, _p, _p, _i64, _i64, _i64, _p]),
+    "rqf_multi_osc_forward": (_int, [_p, _p, _p, _p, _int, _p, _int, _p, _p, _i64, _i64, _i64,
+                                     _i64, _p]),
+    "rqf_multi_osc_backward": (_int, [_p, _p, _p, _p, _int, _p, _p, _p, _p, _p, _p, _p, _i64,
+                                      _i64, _i64, _i64, _p]),
+    "rqf_multi_osc_carry_count": (_i64, [_i64, _i64, _i64, _i64]),
+    "rqf_multi_osc_scratch_bytes": (_sz, [_i64, _i64, _i64, _i64]),
     "rqf_chunked_scan_backward": (
         _int, [_p, _p, _p, _int, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p]),
     "rqf_chunked_prospective_forward": (_int, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p]),

@@ -58,6 +58,13 @@ struct BtfArgs {
   u64 *flags;          // (B*F, ntiles, 2)
   unsigned *ticket;
   const float2 *pw;    // (kBtfPowLevels, F): c1^(2^i)
+  // multi-oscillator scans: F = Fin << log2n oscillator channels, the
+  // C-weights cw (F,), inputs / outputs (B,T,Fin), the C-weight gradient's
+  // partials (B*F, ntiles, 3; slot 0).  Otherwise cw = null, Fin = F, log2n = 0.
+  const float2 *cw;
+  float2 *partials2;
+  int64_t Fin;
+  int log2n;
   int64_t B, T, F;
   int nfb;      // channel blocks of 32
   int ngroups;  // chains: B * nfb
@@ -153,6 +160,27 @@ __device__ __forceinline__ void btf_copy_rows(E *dst, const E *src, const BtfArg
   }
 }
 
+// Multi-oscillator inputs: rows of a (B,T,Fin) tensor holding the 32 >> log2n
+// input channels whose oscillators the chain's lanes carry, channel
+// (f0 >> log2n) + q in column q of a 32-element row.
+template <typename E>
+__device__ __forceinline__ void btf_copy_narrow(E *dst, const E *src, const BtfArgs &a,
+                                                const BtfTile &tl, int64_t t0, int r0, int r1) {
+  const int q = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t fi = (tl.f0 >> a.log2n) + q;
+  const bool fv = q < (32 >> a.log2n) && fi < a.Fin;
+  int r = r0 + warp;
+  int64_t t = t0 + r;
+  int64_t off = (tl.b * a.T + t) * a.Fin + fi;
+  for (; r < r1; r += kBtfWarps, t += kBtfWarps, off += (int64_t)kBtfWarps * a.Fin) {
+    const bool ok = fv && t >= 0 && t < a.T;
+    if constexpr (sizeof(E) == 8)
+      cp_async8(dst + r * 32 + q, ok ? src + off : src, ok);
+    else
+      cp_async4(dst + r * 32 + q, ok ? src + off : src, ok);
+  }
+}
+
 // Header copies: rows kHLam..kHGate (one per warp) and, for NCARRY > 0, the
 // saved entry states of sub-tiles first_sub .. first_sub+NCARRY-1 (warp 0).
 template <int DRIVE, int NCARRY>
@@ -167,9 +195,9 @@ __device__ __forceinline__ void btf_copy_header(float2 *hdr, const BtfArgs &a, c
   switch (warp) {
     case kHLam: src = a.pw + fc; break;
     case kHC2: src = a.c2 + fc; break;
-    case kHT1:
-      src = DRIVE == kTwoTap ? a.tap1 + fc : a.c2;
-      ok = fv && DRIVE == kTwoTap;
+    case kHT1:  // tap1, or the C-weight of a multi-oscillator scan
+      src = DRIVE == kTwoTap ? a.tap1 + fc : (a.cw ? a.cw + fc : a.c2);
+      ok = fv && (DRIVE == kTwoTap || a.cw != nullptr);
       break;
     case kHPow8: src = a.pw + 3 * a.F + fc; break;
     case kHPow16: src = a.pw + 4 * a.F + fc; break;
@@ -217,13 +245,13 @@ __device__ __forceinline__ BtfConst btf_consts(const float2 *hdr, int lane, int 
 // K + 1 consecutive rows (from row r) of this lane's channel: v[0] is the step
 // before the thread's first.
 template <typename E>
-__device__ __forceinline__ void btf_rows9(const E *rows, int r, int lane, float2 (&v)[kBtfK + 1]) {
+__device__ __forceinline__ void btf_rows9(const E *rows, int r, int col, float2 (&v)[kBtfK + 1]) {
 #pragma unroll
   for (int k = 0; k <= kBtfK; ++k) {
     if constexpr (sizeof(E) == 4)
-      v[k] = make_float2(rows[(r + k) * 32 + lane], 0.f);
+      v[k] = make_float2(rows[(r + k) * 32 + col], 0.f);
     else
-      v[k] = rows[(r + k) * 32 + lane];
+      v[k] = rows[(r + k) * 32 + col];
   }
 }
 
@@ -240,6 +268,12 @@ __device__ __forceinline__ void btf_store_y(void *out, int64_t idx, float2 e) {
     __stcs(static_cast<float *>(out) + idx, sqrtf(fmaf(e.x, e.x, e.y * e.y)));
   else
     __stcs(static_cast<float2 *>(out) + idx, e);
+}
+
+// Sum over the 1 << log2n adjacent lanes holding one filter's oscillators.
+__device__ __forceinline__ float2 btf_group_sum(float2 v, int log2n) {
+  for (int o = 1; o < (1 << log2n); o <<= 1) v = c_add(v, shfl_xor2(v, o));
+  return v;
 }
 
 // Composition of the 8 warps' values v[w] with gate g per warp: sum g^(7-w) v[w].
@@ -281,8 +315,10 @@ constexpr size_t btf_tbptt_smem() { return 2 * kBtfTbpttStage; }
 
 // ------------------------------------------------------------ forward
 // ABS: write |y| (float) instead of y; a null carries pointer skips the saved
-// entry states (no backward follows).
-template <int DRIVE, bool VECX, int S, bool ABS = false>
+// entry states (no backward follows).  MOSC (PLAIN / REAL drives): the lanes
+// are oscillators, 1 << log2n per input channel, and the output is their
+// C-weighted sum per channel.
+template <int DRIVE, bool VECX, int S, bool ABS = false, bool MOSC = false>
 __global__ void __launch_bounds__(kBtfThreads, 3) btf_fwd_kernel(const BtfArgs a) {
   using E = typename BtfElem<DRIVE>::T;
   extern __shared__ __align__(16) unsigned char btf_dsm[];
@@ -291,7 +327,8 @@ __global__ void __launch_bounds__(kBtfThreads, 3) btf_fwd_kernel(const BtfArgs a
   __shared__ float2 s_C[S][32];
   __shared__ float2 s_xl[32];  // TWO_TAP: x of the last step of the previous sub-tile
   __shared__ unsigned s_tk;
-  constexpr bool STORE_B = DRIVE != kReal;  // the drive replaces x in shared memory
+  static_assert(!MOSC || DRIVE != kTwoTap, "multi-oscillator scans have a one-tap drive");
+  constexpr bool STORE_B = DRIVE != kReal && !MOSC;  // the drive replaces x in shared memory
   float2 *hdr = reinterpret_cast<float2 *>(btf_dsm);
   E *xs = reinterpret_cast<E *>(btf_dsm + (size_t)kHCarry * 32 * sizeof(float2));
   float2 *bs = reinterpret_cast<float2 *>(xs);  // the drive, when STORE_B
@@ -302,14 +339,19 @@ __global__ void __launch_bounds__(kBtfThreads, 3) btf_fwd_kernel(const BtfArgs a
 #pragma unroll
   for (int s = 0; s < S; ++s) {
     if (s == 0) btf_copy_header<DRIVE, 0>(hdr, a, tl, kBtfLog2Sub + a.log2S, 0);
-    btf_copy_rows<E, VECX>(xs, static_cast<const E *>(a.x), a, tl, ts0 - 1,
-                           s > 0 ? kBtfSub * s + 1 : (DRIVE == kTwoTap ? 0 : 1),
-                           kBtfSub * (s + 1) + 1);
+    if constexpr (MOSC)
+      btf_copy_narrow<E>(xs, static_cast<const E *>(a.x), a, tl, ts0 - 1, kBtfSub * s + 1,
+                         kBtfSub * (s + 1) + 1);
+    else
+      btf_copy_rows<E, VECX>(xs, static_cast<const E *>(a.x), a, tl, ts0 - 1,
+                             s > 0 ? kBtfSub * s + 1 : (DRIVE == kTwoTap ? 0 : 1),
+                             kBtfSub * (s + 1) + 1);
     cp_async_commit();
   }
 
   BtfConst c{};
   float2 Xw[S];
+  const int col = MOSC ? (lane >> a.log2n) : lane;  // x column of this lane
   const int rw = warp * kBtfK;  // row of the step before this thread's first (in a sub-tile)
 #pragma unroll
   for (int s = 0; s < S; ++s) {
@@ -317,7 +359,7 @@ __global__ void __launch_bounds__(kBtfThreads, 3) btf_fwd_kernel(const BtfArgs a
     __syncthreads();
     if (s == 0) c = btf_consts(hdr, lane, warp);
     float2 v[kBtfK + 1];
-    btf_rows9(xs, kBtfSub * s + rw, lane, v);
+    btf_rows9(xs, kBtfSub * s + rw, col, v);
     if (DRIVE == kTwoTap && s > 0 && warp == 0) v[0] = s_xl[lane];
     float2 b[kBtfK];
 #pragma unroll
@@ -366,7 +408,25 @@ __global__ void __launch_bounds__(kBtfThreads, 3) btf_fwd_kernel(const BtfArgs a
   }
   __syncthreads();
   // pass 2: outputs
-  if (f < a.F) {
+  if constexpr (MOSC) {  // C-weighted sum over each filter's oscillators
+    const bool lead = (lane & ((1 << a.log2n) - 1)) == 0 && f < a.F;
+    int64_t yo = (tl.b * a.T + ts0 + rw) * a.Fin + (f >> a.log2n);
+#pragma unroll 1
+    for (int s = 0; s < S; ++s, yo += (int64_t)kBtfSub * a.Fin) {
+      float2 e = c_fma(c.Gw, s_C[s][lane], Xw[s]);
+      const int64_t left = a.T - (ts0 + kBtfSub * s + rw);
+      const int kmax = left < kBtfK ? (int)left : kBtfK;
+      float2 v[kBtfK + 1];
+      btf_rows9(xs, kBtfSub * s + rw, col, v);
+      int64_t p = yo;
+#pragma unroll
+      for (int k = 0; k < kBtfK; ++k, p += a.Fin) {
+        e = c_fma(c.lam, e, btf_drive1<DRIVE>(c, v[k + 1], v[k]));
+        const float2 o = btf_group_sum(c_mul(c.t1, e), a.log2n);
+        if (lead && k < kmax) btf_store_y<ABS>(a.out, p, o);
+      }
+    }
+  } else if (f < a.F) {
     int64_t yo = (tl.b * a.T + ts0 + rw) * a.F + f;
 #pragma unroll 1
     for (int s = 0; s < S; ++s, yo += (int64_t)kBtfSub * a.F) {
@@ -395,14 +455,18 @@ __global__ void __launch_bounds__(kBtfThreads, 3) btf_fwd_kernel(const BtfArgs a
 
 // ------------------------------------------------------------ backward
 // Tiles run in reverse time order (processing position p = tile ntiles-1-p).
-template <int DRIVE, bool VECX, bool VECG, int S>
+// MOSC: multi-oscillator scan (see the forward); the cotangent of oscillator s
+// is conj(cw_s) gy[f], grad_u[f] sums conj(c2_s) g_s over f's oscillators, and
+// grad_cw_s = sum conj(y_s[t]) gy[t, f] goes to the second partials array.
+template <int DRIVE, bool VECX, bool VECG, int S, bool MOSC = false>
 __global__ void __launch_bounds__(kBtfThreads, 2) btf_bwd_kernel(const BtfArgs a) {
+  static_assert(!MOSC || DRIVE != kTwoTap, "multi-oscillator scans have a one-tap drive");
   using E = typename BtfElem<DRIVE>::T;
   extern __shared__ __align__(16) unsigned char btf_dsm[];
   __shared__ float4 s_yh[S][kBtfWarps][32];  // (forward y, reverse h) per warp
   __shared__ float2 s_H[S][32];               // reverse sub-tile totals
   __shared__ float2 s_D[32];
-  __shared__ float2 s_red[3][kBtfWarps][32];
+  __shared__ float2 s_red[MOSC ? 4 : 3][kBtfWarps][32];
   __shared__ unsigned s_tk;
   float2 *hdr = reinterpret_cast<float2 *>(btf_dsm);
   E *xs = reinterpret_cast<E *>(btf_dsm + (size_t)(kHCarry + S) * 32 * sizeof(float2));
@@ -415,28 +479,40 @@ __global__ void __launch_bounds__(kBtfThreads, 2) btf_bwd_kernel(const BtfArgs a
 #pragma unroll
   for (int s = 0; s < S; ++s) {
     if (s == 0) btf_copy_header<DRIVE, S>(hdr, a, tl, kBtfLog2Sub + a.log2S, tl.j * S);
-    btf_copy_rows<E, VECX>(xs, static_cast<const E *>(a.x), a, tl, ts0 - 1,
-                           s > 0 ? kBtfSub * s + 1 : (DRIVE == kTwoTap ? 0 : 1),
-                           kBtfSub * (s + 1) + 1);
-    btf_copy_rows<float2, VECG>(gs, a.gout, a, tl, ts0, kBtfSub * s, kBtfSub * (s + 1));
+    if constexpr (MOSC) {
+      btf_copy_narrow<E>(xs, static_cast<const E *>(a.x), a, tl, ts0 - 1, kBtfSub * s + 1,
+                         kBtfSub * (s + 1) + 1);
+      btf_copy_narrow<float2>(gs, a.gout, a, tl, ts0, kBtfSub * s, kBtfSub * (s + 1));
+    } else {
+      btf_copy_rows<E, VECX>(xs, static_cast<const E *>(a.x), a, tl, ts0 - 1,
+                             s > 0 ? kBtfSub * s + 1 : (DRIVE == kTwoTap ? 0 : 1),
+                             kBtfSub * (s + 1) + 1);
+      btf_copy_rows<float2, VECG>(gs, a.gout, a, tl, ts0, kBtfSub * s, kBtfSub * (s + 1));
+    }
     cp_async_commit();
   }
 
   BtfConst c{};
   const int rw = warp * kBtfK;
+  const int col = MOSC ? (lane >> a.log2n) : lane;  // x / cotangent column of this lane
+  // cotangent of this lane's state at stage row r
+  auto gcot = [&](int r) {
+    const float2 g = gs[r * 32 + col];
+    return MOSC ? c_cfma(c.t1, g, cz()) : g;
+  };
 #pragma unroll
   for (int s = 0; s < S; ++s) {
     cp_async_wait_rt<S>(S - 1 - s);
     __syncthreads();
     if (s == 0) c = btf_consts(hdr, lane, warp);
     float2 v[kBtfK + 1];
-    btf_rows9(xs, kBtfSub * s + rw, lane, v);
+    btf_rows9(xs, kBtfSub * s + rw, col, v);
     float2 y = cz(), h = cz();
 #pragma unroll
     for (int k = 0; k < kBtfK; ++k) y = c_fma(c.lam, y, btf_drive1<DRIVE>(c, v[k + 1], v[k]));
     const float2 mu = c_conj(c.lam);
 #pragma unroll
-    for (int k = kBtfK - 1; k >= 0; --k) h = c_fma(mu, h, gs[(kBtfSub * s + rw + k) * 32 + lane]);
+    for (int k = kBtfK - 1; k >= 0; --k) h = c_fma(mu, h, gcot(kBtfSub * s + rw + k));
     s_yh[s][warp][lane] = make_float4(y.x, y.y, h.x, h.y);
   }
   __syncthreads();
@@ -473,7 +549,7 @@ __global__ void __launch_bounds__(kBtfThreads, 2) btf_bwd_kernel(const BtfArgs a
   }
   __syncthreads();
   float2 Ds = s_D[lane];  // adjoint entering the last sub-tile from its right
-  float2 acc_c1 = cz(), acc_1 = cz(), acc_2 = cz();
+  float2 acc_c1 = cz(), acc_1 = cz(), acc_2 = cz(), acc_w = cz();
 #pragma unroll 1
   for (int s = S - 1; s >= 0; --s) {
     float2 Xw = cz(), Xrw = cz();
@@ -484,12 +560,13 @@ __global__ void __launch_bounds__(kBtfThreads, 2) btf_bwd_kernel(const BtfArgs a
     float2 e = c_fma(c.Gw, hdr[(kHCarry + s) * 32 + lane], Xw);
     float2 gnext = c_fma(c.Grw, Ds, Xrw);
     float2 v[kBtfK + 1];
-    btf_rows9(xs, kBtfSub * s + rw, lane, v);
+    btf_rows9(xs, kBtfSub * s + rw, col, v);
     float2 yprev[kBtfK];
 #pragma unroll
     for (int k = 0; k < kBtfK; ++k) {
       yprev[k] = e;
       e = c_fma(c.lam, e, btf_drive1<DRIVE>(c, v[k + 1], v[k]));
+      if constexpr (MOSC) acc_w = c_cfma(e, gs[(kBtfSub * s + rw + k) * 32 + col], acc_w);
     }
     const int64_t t0 = ts0 + kBtfSub * s + rw;
     const int64_t left = a.T - t0;
@@ -497,8 +574,19 @@ __global__ void __launch_bounds__(kBtfThreads, 2) btf_bwd_kernel(const BtfArgs a
     const int64_t obase = (tl.b * a.T + t0) * a.F + f;
 #pragma unroll
     for (int k = kBtfK - 1; k >= 0; --k) {
-      const float2 g = c_fma(mu, gnext, gs[(kBtfSub * s + rw + k) * 32 + lane]);
-      if constexpr (DRIVE == kReal) {
+      const float2 g = c_fma(mu, gnext, gcot(kBtfSub * s + rw + k));
+      if constexpr (MOSC) {  // grad_u[f]: the filter's oscillators summed
+        const float2 gu = btf_group_sum(c_cfma(c.c2, g, cz()), a.log2n);
+        const bool lead = (lane & ((1 << a.log2n) - 1)) == 0 && k < kmax;
+        const int64_t ui = (tl.b * a.T + t0 + k) * a.Fin + (f >> a.log2n);
+        if (DRIVE == kReal) {
+          if (lead) __stcs(static_cast<float *>(a.out) + ui, gu.x);
+          acc_1 = make_float2(fmaf(v[k + 1].x, g.x, acc_1.x), fmaf(v[k + 1].x, g.y, acc_1.y));
+        } else {
+          if (lead) __stcs(static_cast<float2 *>(a.out) + ui, gu);
+          acc_1 = c_cfma(v[k + 1], g, acc_1);
+        }
+      } else if constexpr (DRIVE == kReal) {
         // grad of the real input: Re(conj(c2) g)
         if (k < kmax)
           __stcs(static_cast<float *>(a.out) + obase + k * a.F, c.c2.x * g.x + c.c2.y * g.y);
@@ -522,12 +610,17 @@ __global__ void __launch_bounds__(kBtfThreads, 2) btf_bwd_kernel(const BtfArgs a
   s_red[0][warp][lane] = acc_c1;
   s_red[1][warp][lane] = acc_1;
   s_red[2][warp][lane] = acc_2;
+  if constexpr (MOSC) s_red[3][warp][lane] = acc_w;
   __syncthreads();
-  if (warp < 3 && fv) {
+  if (warp < (MOSC ? 4 : 3) && fv) {
     float2 sum = cz();
 #pragma unroll
     for (int w = 0; w < kBtfWarps; ++w) sum = c_add(sum, s_red[warp][w][lane]);
-    a.partials[((tl.b * a.F + f) * a.ntiles + tl.j) * 3 + warp] = sum;
+    const int64_t slot = ((tl.b * a.F + f) * a.ntiles + tl.j) * 3;
+    if (warp < 3)
+      a.partials[slot + warp] = sum;
+    else
+      a.partials2[slot] = sum;
   }
 }
 

@@ -194,6 +194,10 @@ BtfArgs btf_args(const float *c1, const float *c2, const float *tap1, const void
   a.flags = at<u64>(scratch, lay.base.flags_off);
   a.partials = at<float2>(scratch, lay.base.partials_off);
   a.pw = at<float2>(scratch, lay.pw_off);
+  a.cw = nullptr;
+  a.partials2 = nullptr;
+  a.Fin = F;
+  a.log2n = 0;
   return a;
 }
 
@@ -215,28 +219,60 @@ int btf_launch(Kern kernel, size_t smem, const BtfArgs &a, void *scratch, cudaSt
   return launch_status();
 }
 
-template <int DRIVE, bool VEC, bool ABS = false>
+template <int DRIVE, bool VEC, bool ABS = false, bool MOSC = false>
 int btf_launch_fwd(const BtfArgs &a, void *scratch, cudaStream_t stream) {
   switch (a.S) {
     case 1:
-      return btf_launch(btf_fwd_kernel<DRIVE, VEC, 1, ABS>, btf_fwd_smem<DRIVE, 1>(), a, scratch,
-                        stream);
+      return btf_launch(btf_fwd_kernel<DRIVE, VEC, 1, ABS, MOSC>, btf_fwd_smem<DRIVE, 1>(), a,
+                        scratch, stream);
     case 2:
-      return btf_launch(btf_fwd_kernel<DRIVE, VEC, 2, ABS>, btf_fwd_smem<DRIVE, 2>(), a, scratch,
-                        stream);
+      return btf_launch(btf_fwd_kernel<DRIVE, VEC, 2, ABS, MOSC>, btf_fwd_smem<DRIVE, 2>(), a,
+                        scratch, stream);
     default:
-      return btf_launch(btf_fwd_kernel<DRIVE, VEC, 4, ABS>, btf_fwd_smem<DRIVE, 4>(), a, scratch,
-                        stream);
+      return btf_launch(btf_fwd_kernel<DRIVE, VEC, 4, ABS, MOSC>, btf_fwd_smem<DRIVE, 4>(), a,
+                        scratch, stream);
   }
 }
 
-template <int DRIVE, bool VECX, bool VECG>
+template <int DRIVE, bool VECX, bool VECG, bool MOSC = false>
 int btf_launch_bwd(const BtfArgs &a, void *scratch, cudaStream_t stream) {
   if (a.S == 1)
-    return btf_launch(btf_bwd_kernel<DRIVE, VECX, VECG, 1>, btf_bwd_smem<DRIVE, 1>(), a, scratch,
-                      stream);
-  return btf_launch(btf_bwd_kernel<DRIVE, VECX, VECG, 2>, btf_bwd_smem<DRIVE, 2>(), a, scratch,
-                    stream);
+    return btf_launch(btf_bwd_kernel<DRIVE, VECX, VECG, 1, MOSC>, btf_bwd_smem<DRIVE, 1>(), a,
+                      scratch, stream);
+  return btf_launch(btf_bwd_kernel<DRIVE, VECX, VECG, 2, MOSC>, btf_bwd_smem<DRIVE, 2>(), a,
+                    scratch, stream);
+}
+
+// ---- multi-oscillator scans (tile-resident family only): Fin filters of
+// num_osc oscillators each, lanes = oscillators.  Scratch: the BTF layout of
+// the Fin * num_osc oscillator channels, then the C-weight partials.
+inline int mosc_log2(int64_t n) {
+  for (int l = 0; l <= 5; ++l)
+    if ((int64_t)1 << l == n) return l;
+  return -1;
+}
+struct MoscScratch {
+  BtfScratch base;
+  size_t p2_off, total;
+};
+inline MoscScratch mosc_scratch_layout(int64_t B, int64_t T, int64_t Fs) {
+  MoscScratch m;
+  m.base = btf_scratch_layout(B, T, Fs);
+  m.p2_off = m.base.total;
+  m.total = m.p2_off + round256((size_t)(B * Fs) * (size_t)btf_nsub(T) * 3 * sizeof(float2));
+  return m;
+}
+BtfArgs mosc_args(const float *c1, const float *c2, const float *cw, const void *u,
+                  const float *gout, void *out, float *carries, void *scratch, int64_t B,
+                  int64_t T, int64_t Fin, int log2n, int max_log2_tile) {
+  const int64_t Fs = Fin << log2n;
+  BtfArgs a = btf_args(c1, c2, nullptr, u, gout, out, nullptr, carries, scratch, B, T, Fs,
+                       btf_log2_tile(B, T, Fs, max_log2_tile));
+  a.cw = reinterpret_cast<const float2 *>(cw);
+  a.partials2 = at<float2>(scratch, mosc_scratch_layout(B, T, Fs).p2_off);
+  a.Fin = Fin;
+  a.log2n = log2n;
+  return a;
 }
 
 // 16-byte staging copies: the row of a chain starts on a 16-byte boundary.
@@ -515,6 +551,81 @@ int rqf_chunked_scan_abs_forward(const float *c1, const float *c2, const void *u
                                  int64_t filters, rqf_stream_t stream) {
   return btf_forward(u_is_real ? kReal : kPlain, c1, c2, nullptr, u, y_abs, nullptr, scratch,
                      batch, time, filters, stream, true);
+}
+
+int rqf_multi_osc_forward(const float *c1, const float *c2, const float *cw, const void *u,
+                          int u_is_real, void *out, int out_abs, float *carries, void *scratch,
+                          int64_t batch, int64_t time, int64_t filters, int64_t num_osc,
+                          rqf_stream_t stream) {
+  const int l = mosc_log2(num_osc);
+  if (batch < 0 || time < 0 || filters < 0 || l < 0) return RQF_ERR_SHAPE;
+  int st = btf_dims_ok(batch, time, filters << l);
+  if (st != RQF_OK) return st;
+  if (batch == 0 || time == 0 || filters == 0) return RQF_OK;
+  if (!c1 || !c2 || !cw || !u || !out || (!carries && !out_abs) || !scratch)
+    return RQF_ERR_ARGUMENT;
+  if (!aligned(c1, 8) || !aligned(c2, 8) || !aligned(cw, 8) || !aligned(u, u_is_real ? 4 : 8) ||
+      !aligned(out, out_abs ? 4 : 8) || (carries && !aligned(carries, 8)) ||
+      !aligned(scratch, 16))
+    return RQF_ERR_ALIGN;
+  const BtfArgs a = mosc_args(c1, c2, cw, u, nullptr, out, out_abs ? nullptr : carries, scratch,
+                              batch, time, filters, l, 2);
+  if (u_is_real)
+    return out_abs ? btf_launch_fwd<kReal, false, true, true>(a, scratch, stream)
+                   : btf_launch_fwd<kReal, false, false, true>(a, scratch, stream);
+  return out_abs ? btf_launch_fwd<kPlain, false, true, true>(a, scratch, stream)
+                 : btf_launch_fwd<kPlain, false, false, true>(a, scratch, stream);
+}
+
+int rqf_multi_osc_backward(const float *c1, const float *c2, const float *cw, const void *u,
+                           int u_is_real, const float *carries, const float *grad_out,
+                           void *grad_u, float *grad_c1, float *grad_c2, float *grad_cw,
+                           void *scratch, int64_t batch, int64_t time, int64_t filters,
+                           int64_t num_osc, rqf_stream_t stream) {
+  const int l = mosc_log2(num_osc);
+  if (batch < 0 || time < 0 || filters < 0 || l < 0) return RQF_ERR_SHAPE;
+  const int64_t Fs = filters << l;
+  int st = btf_dims_ok(batch, time, Fs);
+  if (st != RQF_OK) return st;
+  if (filters == 0) return RQF_OK;
+  if (batch == 0 || time == 0) {
+    if ((st = zero_complex(grad_c1, Fs, stream)) != RQF_OK) return st;
+    if ((st = zero_complex(grad_c2, Fs, stream)) != RQF_OK) return st;
+    return zero_complex(grad_cw, Fs, stream);
+  }
+  if (!c1 || !c2 || !cw || !u || !carries || !grad_out || !grad_u || !scratch)
+    return RQF_ERR_ARGUMENT;
+  if (!aligned(c1, 8) || !aligned(c2, 8) || !aligned(cw, 8) || !aligned(u, u_is_real ? 4 : 8) ||
+      !aligned(grad_out, 8) || !aligned(grad_u, u_is_real ? 4 : 8) || !aligned(carries, 8) ||
+      !aligned(scratch, 16))
+    return RQF_ERR_ALIGN;
+  const BtfArgs a = mosc_args(c1, c2, cw, u, grad_out, grad_u, const_cast<float *>(carries),
+                              scratch, batch, time, filters, l, 1);
+  st = u_is_real ? btf_launch_bwd<kReal, false, false, true>(a, scratch, stream)
+                 : btf_launch_bwd<kPlain, false, false, true>(a, scratch, stream);
+  if (st != RQF_OK) return st;
+  reduce_partials_kernel<<<(unsigned)Fs, 256, 0, stream>>>(
+      a.partials, reinterpret_cast<float2 *>(grad_c1), reinterpret_cast<float2 *>(grad_c2),
+      nullptr, batch, 1, Fs, a.ntiles);
+  if ((st = launch_status()) != RQF_OK) return st;
+  reduce_partials_kernel<<<(unsigned)Fs, 256, 0, stream>>>(
+      a.partials2, reinterpret_cast<float2 *>(grad_cw), nullptr, nullptr, batch, 1, Fs,
+      a.ntiles);
+  return launch_status();
+}
+
+int64_t rqf_multi_osc_carry_count(int64_t batch, int64_t time, int64_t filters,
+                                  int64_t num_osc) {
+  const int l = mosc_log2(num_osc);
+  if (l < 0 || batch < 0 || time < 0 || filters < 0) return 0;
+  return batch * (filters << l) * btf_nsub(time);
+}
+
+size_t rqf_multi_osc_scratch_bytes(int64_t batch, int64_t time, int64_t filters,
+                                   int64_t num_osc) {
+  const int l = mosc_log2(num_osc);
+  if (l < 0 || batch <= 0 || time <= 0 || filters <= 0) return 256;
+  return mosc_scratch_layout(batch, time, filters << l).total;
 }
 
 int rqf_chunked_scan_backward(const float *c1, const float *c2, const void *u, int u_is_real,

@@ -11,6 +11,7 @@ Call sites served (reference paths):
   rqf_models/ops/scan.py:367, :509            -> _triton_chunked_scan
   rqf_models/ops/scan.py:430-432               -> |scan| epilogue (sequential_scan_abs)
   rqf_models/backbones/rqf/block.py:926-934   -> _triton_chunked_scan_prospective
+  rqf_models/backbones/rqf/block.py:737-764   -> fused multi-oscillator scans
   rqf_models/backbones/rqf/pure.py:234-238    -> fbt_prospective_scan / fbt_recompute_scan
   rqf_models/backbones/rqf/block.py:882, :904 -> TBPTT(1) fused surrogate on CUDA
   rqf_models/ops/selective_scan.py:119, :133   -> selective_forward / selective_backward
@@ -39,6 +40,16 @@ _BINDINGS = [
      ops._triton_chunked_scan_prospective),
     ("rqf_models.backbones.rqf.pure", "fbt_prospective_scan", ops.fbt_prospective_scan),
     ("rqf_models.backbones.rqf.pure", "fbt_recompute_scan", ops.fbt_recompute_scan),
+    ("rqf_models.backbones.rqf.block", "_triton_sequential_scan_multi_osc",
+     ops._triton_sequential_scan_multi_osc),
+    ("rqf_models.backbones.rqf.block", "_triton_sequential_scan_multi_osc_real",
+     ops._triton_sequential_scan_multi_osc_real),
+    ("rqf_models.backbones.rqf.block", "_triton_parallel_scan_multi_osc",
+     ops._triton_parallel_scan_multi_osc),
+    ("rqf_models.backbones.rqf.block", "_sequential_scan_multi_osc_forward_abs_raw",
+     ops._sequential_scan_multi_osc_forward_abs_raw),
+    ("rqf_models.backbones.rqf.block", "_sequential_scan_multi_osc_real_forward_abs_raw",
+     ops._sequential_scan_multi_osc_real_forward_abs_raw),
     ("rqf_models.ops.selective_scan_kernel", "selective_forward", ops.selective_forward),
     ("rqf_models.ops.selective_scan_kernel", "selective_backward", ops.selective_backward),
 ]

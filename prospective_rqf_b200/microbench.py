@@ -21,6 +21,8 @@ Ops:
              its weight cotangent gz h^H (split-TF32 tcgen05 GEMMs, W of F x F
              complex); reports TFLOP/s (8 F^2 B T real flops per GEMM)
   projection_torch  the same two GEMMs through torch.matmul (cuBLAS fp32)
+  mosc       the fused multi-oscillator scan (B,T,F) -> (B,T,F), --groups
+             oscillators per filter
 
 --btf-path forces one (B,T,F) kernel family (1 streaming, 2 tile-resident).
 
@@ -119,6 +121,18 @@ def make_case(op: str, F: int, B: int, T: int, groups: int = 8, truncated: bool 
             ops._fbt_backward(saved, gy, True)
         return run
 
+    if op == "mosc":  # groups = oscillators per filter; F filters in and out
+        n = groups
+        c1m, c2m, _ = _coeffs(F * n, dev, g)
+        cw = torch.randn(F * n, 2, generator=g).to(dev)
+        u = crandn(B, T, F).requires_grad_(True)
+        gy = crandn(B, T, F)
+
+        def run():
+            y = ops._triton_sequential_scan_multi_osc(c1m, c2m, u, cw, n)
+            torch.autograd.grad(y, (u,), gy)
+        return run
+
     fbt = op in ("fbt", "fbt_raw", "tbptt_fbt")
     shape = (F, B, T) if fbt else (B, T, F)
     if op == "btf_real":
@@ -144,7 +158,7 @@ def make_case(op: str, F: int, B: int, T: int, groups: int = 8, truncated: bool 
 
 
 OPS = ("fbt", "fbt_raw", "fbt_skip", "tbptt_fbt", "tbptt_btf", "btf", "btf_real", "btf_pro",
-       "selective", "projection", "projection_torch")
+       "selective", "projection", "projection_torch", "mosc")
 
 
 def measure(op, F, B, T, iters=10, warmup=3, groups=8, truncated=False) -> dict:

@@ -15,6 +15,8 @@ Reference callables (paths inside the reference project):
   sequential_scan_abs               rqf_models/ops/scan.py:381
   _sequential_scan_forward_abs_raw_block_f        triton_scan_kernel.py:507
   _sequential_scan_real_forward_abs_raw_block_f   triton_scan_kernel.py:1531
+  _triton_sequential_scan_multi_osc (+ _real, parallel, abs forms)
+                                    triton_scan_kernel.py:2499, :3071, :4106, :2019, :2688
 New (no single reference callable; replaces the autograd surrogate of
 rqf_models/backbones/rqf/block.py:_scan_two_tap_with_grad_mode :904-954 and
 _scan_with_grad_mode :882-902):
@@ -481,6 +483,137 @@ def sequential_scan_abs(C1, C2, u, B=None):
         return sequential_scan(C1, C2, u, B).abs()
     C1, C2, u = _prepare(C1, C2, u, None)
     return _scan_abs(C1, C2, u)
+
+
+# ------------------------------------------- multi-oscillator scans
+def _mosc_pow2(n: int) -> bool:
+    return 1 <= n <= 32 and (n & (n - 1)) == 0
+
+
+def _cw_complex(c_weights: torch.Tensor) -> torch.Tensor:
+    """The reference's real (scan_filters, 2) C-weights as complex64 (scan_filters,)."""
+    return torch.view_as_complex(c_weights.detach().to(torch.float32).contiguous())
+
+
+class _MultiOscScan(torch.autograd.Function):
+    """out[t, f] = sum_k cw_{f n + k} x_{f n + k}[t] with x_s[t] = C1_s x_s[t-1] +
+    C2_s u[t, s / n]: the fused multi-oscillator scan of
+    triton_scan_kernel.py:_SequentialScanMultiOscFunction (:2413-2496), one
+    lane per oscillator and the C-weight sum in the epilogue, so neither the
+    repeated input nor the (B,T,F*n) states are materialised.  Saves C1, C2,
+    the C-weights, u and one carry per 64-step sub-tile per oscillator."""
+
+    @staticmethod
+    def forward(ctx, C1, C2, u, c_weights, num_osc):
+        dev = _require_cuda(C1, C2, u, c_weights)
+        real = not u.is_complex()
+        uu = u.to(torch.float32).contiguous() if real else _c64(u)
+        B, T, F = _shape3(uu, "u")
+        n = int(num_osc)
+        c1, c2 = _coef(C1, F * n, "C1"), _coef(C2, F * n, "C2")
+        cw = _coef(_cw_complex(c_weights), F * n, "c_weights")
+        lib = _abi.load()
+        out = torch.empty((B, T, F), dtype=torch.complex64, device=dev)
+        carries = _carries(lib.rqf_multi_osc_carry_count(B, T, F, n), dev)
+        scratch = _scratch(lib.rqf_multi_osc_scratch_bytes(B, T, F, n), dev)
+        with _timing.launch("rqf_multi_osc_forward", B * T * F * n, _nbytes(uu, out)):
+            _abi.check(lib.rqf_multi_osc_forward(
+                _abi.ptr(c1), _abi.ptr(c2), _abi.ptr(cw), _abi.ptr(uu), int(real), _abi.ptr(out),
+                0, _abi.ptr(carries), _abi.ptr(scratch), B, T, F, n, _abi.stream_of(uu)),
+                "rqf_multi_osc_forward")
+        _done(dev)
+        ctx.save_for_backward(c1, c2, cw, uu, carries)
+        ctx.real, ctx.n = real, n
+        return out
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_output):
+        c1, c2, cw, uu, carries = ctx.saved_tensors
+        B, T, F = uu.shape
+        n = ctx.n
+        dev = uu.device
+        gy = _c64(grad_output)
+        lib = _abi.load()
+        gu = torch.empty_like(uu)
+        gc1, gc2, gcw = torch.empty_like(c1), torch.empty_like(c2), torch.empty_like(cw)
+        scratch = _scratch(lib.rqf_multi_osc_scratch_bytes(B, T, F, n), dev)
+        with _timing.launch("rqf_multi_osc_backward", B * T * F * n, _nbytes(uu, gy, gu)):
+            _abi.check(lib.rqf_multi_osc_backward(
+                _abi.ptr(c1), _abi.ptr(c2), _abi.ptr(cw), _abi.ptr(uu), int(ctx.real),
+                _abi.ptr(carries), _abi.ptr(gy), _abi.ptr(gu), _abi.ptr(gc1), _abi.ptr(gc2),
+                _abi.ptr(gcw), _abi.ptr(scratch), B, T, F, n, _abi.stream_of(gy)),
+                "rqf_multi_osc_backward")
+        _done(dev)
+        need = ctx.needs_input_grad
+        return (gc1 if need[0] else None, gc2 if need[1] else None, gu if need[2] else None,
+                torch.view_as_real(gcw) if need[3] else None, None)
+
+
+def _multi_osc_composed(C1, C2, u, c_weights, num_osc):
+    """Any oscillator count: the scan over the repeated input, then the
+    C-weighted sum (the reference's unfused path, block.py:_c_weighted_sum)."""
+    B, T, F = u.shape
+    y = sequential_scan(C1, C2, u.repeat_interleave(num_osc, dim=-1))
+    cw = torch.view_as_complex(c_weights.to(torch.float32).contiguous())
+    return (y.view(B, T, F, num_osc) * cw.view(F, num_osc)).sum(dim=-1)
+
+
+def _triton_sequential_scan_multi_osc(C1, C2, u, c_weights, num_osc):
+    """Drop-in for triton_scan_kernel.py:_triton_sequential_scan_multi_osc (:2499)."""
+    if _mosc_pow2(int(num_osc)):
+        return _MultiOscScan.apply(C1, C2, u, c_weights, int(num_osc))
+    return _multi_osc_composed(C1, C2, u, c_weights, int(num_osc))
+
+
+def _triton_sequential_scan_multi_osc_real(C1, C2, u, c_weights, num_osc):
+    """Drop-in for triton_scan_kernel.py:_triton_sequential_scan_multi_osc_real
+    (:3071): real u, scanned without materialising its imaginary part."""
+    if u.is_complex():
+        raise ValueError("_triton_sequential_scan_multi_osc_real expects real input")
+    return _triton_sequential_scan_multi_osc(C1, C2, u, c_weights, num_osc)
+
+
+def _triton_parallel_scan_multi_osc(C1, C2, u, c_weights, num_osc):
+    """Drop-in for triton_scan_kernel.py:_triton_parallel_scan_multi_osc
+    (:4106); the same values as the sequential form."""
+    return _triton_sequential_scan_multi_osc(C1, C2, u, c_weights, num_osc)
+
+
+def _multi_osc_abs(C1, C2, u, cw_complex, num_osc):
+    n = int(num_osc)
+    dev = _require_cuda(C1, C2, u)
+    if not _mosc_pow2(n):
+        return _multi_osc_composed(C1, C2, u, torch.view_as_real(cw_complex), n).abs()
+    real = not u.is_complex()
+    uu = u.to(torch.float32).contiguous() if real else _c64(u)
+    B, T, F = _shape3(uu, "u")
+    c1, c2 = _coef(C1, F * n, "C1"), _coef(C2, F * n, "C2")
+    cw = _coef(cw_complex, F * n, "c_weights")
+    lib = _abi.load()
+    out = torch.empty((B, T, F), dtype=torch.float32, device=dev)
+    scratch = _scratch(lib.rqf_multi_osc_scratch_bytes(B, T, F, n), dev)
+    with _timing.launch("rqf_multi_osc_forward", B * T * F * n, _nbytes(uu, out)):
+        _abi.check(lib.rqf_multi_osc_forward(
+            _abi.ptr(c1), _abi.ptr(c2), _abi.ptr(cw), _abi.ptr(uu), int(real), _abi.ptr(out), 1,
+            None, _abi.ptr(scratch), B, T, F, n, _abi.stream_of(uu)), "rqf_multi_osc_forward")
+    _done(dev)
+    return out
+
+
+def _sequential_scan_multi_osc_forward_abs_raw(C1, C2, u, cw_real, cw_imag, num_osc):
+    """Drop-in for triton_scan_kernel.py:_sequential_scan_multi_osc_forward_abs_raw
+    (:2019): |C-weighted multi-oscillator scan|, no autograd."""
+    cw = torch.complex(cw_real.to(torch.float32), cw_imag.to(torch.float32)).contiguous()
+    return _multi_osc_abs(C1, C2, u, cw, num_osc)
+
+
+def _sequential_scan_multi_osc_real_forward_abs_raw(C1, C2, u, c_weights, num_osc):
+    """Drop-in for triton_scan_kernel.py:_sequential_scan_multi_osc_real_forward_abs_raw
+    (:2688): real u, |output|, no autograd."""
+    if u.is_complex():
+        raise ValueError("_sequential_scan_multi_osc_real_forward_abs_raw expects real input")
+    return _multi_osc_abs(C1, C2, u, _cw_complex(c_weights), num_osc)
 
 
 # ------------------------------------------------------ selective scan

@@ -183,3 +183,14 @@ def test_sequential_scan_abs_epilogue():
         e = rel_err(_np(y1), _np(y0))
         assert e <= FWD_TOL, f"|y| differs by {e:.2e}"
 
+
+
+@pytest.mark.parametrize("parallel", [False, True])
+def test_s4_rqf_block_multi_oscillator(parallel):
+    """S4-RQF block with 4 oscillators per filter on the standard (one-tap)
+    path: the reference's fused multi-oscillator Triton kernels against this
+    backend's (block.py:737-764), outputs and every gradient."""
+    x = torch.randn(2, 1500, 16, device="cuda", generator=torch.Generator("cuda").manual_seed(8))
+    launched = _compare(_s4(prospective_input=False, num_oscillators=4,
+                            use_parallel_scan=parallel), x)
+    assert "rqf_multi_osc_forward" in launched and "rqf_multi_osc_backward" in launched

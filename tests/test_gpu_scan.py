@@ -475,3 +475,71 @@ def test_repeated_calls_are_deterministic():
         assert torch.equal(y, outs[0][0])
         assert torch.equal(gz, outs[0][1])
         assert torch.equal(gc, outs[0][2])
+
+
+# ------------------------------------------- multi-oscillator scans
+def _mosc_ref(c1, c2, u, cw, n):
+    """fp64 torch restatement: the scan over the repeated input, then the
+    C-weighted sum per filter (rqf_models/backbones/rqf/block.py:_c_weighted_sum)."""
+    B, T, F = u.shape
+    ur = u.repeat_interleave(n, dim=-1)
+    x = torch.zeros(B, F * n, dtype=torch.complex128)
+    outs = []
+    for t in range(T):
+        x = c1 * x + c2 * ur[:, t]
+        outs.append((x.view(B, F, n) * cw.view(F, n)).sum(-1))
+    return torch.stack(outs, 1)
+
+
+@pytest.mark.parametrize("B,T,F,n,real", [(2, 300, 3, 4, False), (3, 700, 16, 2, True),
+                                          (2, 1100, 10, 8, False), (40, 257, 4, 32, False),
+                                          (2, 200, 5, 3, False), (1, 1, 2, 16, True)])
+def test_multi_osc_vs_fp64(B, T, F, n, real):
+    """The fused multi-oscillator scan (lanes = oscillators, C-weighted sum in
+    the epilogue; n = 3 takes the composed path) against fp64, with the
+    gradients of C1, C2, u and the real (F*n, 2) C-weights."""
+    rng = np.random.default_rng(B * 7 + T + F * 11 + n)
+    Fs = F * n
+    c1, c2 = coeffs(rng, Fs), c64(crandn(rng, Fs, 0.5))
+    cw = (0.5 * rng.standard_normal((Fs, 2))).astype(np.float32).astype(np.float64)
+    u = (rng.standard_normal((B, T, F)).astype(np.float32).astype(np.float64) if real
+         else c64(crandn(rng, (B, T, F))))
+    gy = c64(crandn(rng, (B, T, F)))
+    ins = [dev(c1, grad=True), dev(c2, grad=True),
+           dev(u, dtype=torch.float32 if real else torch.complex64, grad=True),
+           dev(cw, dtype=torch.float32, grad=True)]
+    y = rqf().ops._triton_sequential_scan_multi_osc(*ins, n)
+    refs = [torch.from_numpy(np.asarray(a)).requires_grad_(True) for a in (c1, c2, u, cw)]
+    y_ref = _mosc_ref(refs[0], refs[1], refs[2], torch.view_as_complex(refs[3]), n)
+    assert_close(host(y), y_ref.detach().numpy(), FWD_TOL, "y")
+    y.backward(dev(gy))
+    y_ref.backward(torch.from_numpy(gy))
+    for t, r, k in zip(ins, refs, ("gc1", "gc2", "gu", "gcw")):
+        assert_close(t.grad.detach().cpu().numpy().astype(np.complex128),
+                     r.grad.numpy().astype(np.complex128), GRAD_TOL, k)
+
+
+@pytest.mark.parametrize("n,real", [(4, False), (8, True), (3, False)])
+def test_multi_osc_abs_epilogue(n, real):
+    rng = np.random.default_rng(n + 100)
+    B, T, F = 3, 500, 6
+    Fs = F * n
+    c1, c2 = coeffs(rng, Fs), c64(crandn(rng, Fs, 0.5))
+    cw = (0.5 * rng.standard_normal((Fs, 2))).astype(np.float32).astype(np.float64)
+    u = (rng.standard_normal((B, T, F)).astype(np.float32).astype(np.float64) if real
+         else c64(crandn(rng, (B, T, F))))
+    ops = rqf().ops
+    ud = dev(u, dtype=torch.float32 if real else torch.complex64)
+    with torch.no_grad():
+        if real:
+            y = ops._sequential_scan_multi_osc_real_forward_abs_raw(
+                dev(c1), dev(c2), ud, dev(cw, dtype=torch.float32), n)
+        else:
+            cwd = dev(cw, dtype=torch.float32)
+            y = ops._sequential_scan_multi_osc_forward_abs_raw(
+                dev(c1), dev(c2), ud, cwd[:, 0].contiguous(), cwd[:, 1].contiguous(), n)
+    assert y.dtype == torch.float32
+    ref = _mosc_ref(torch.from_numpy(np.asarray(c1)), torch.from_numpy(np.asarray(c2)),
+                    torch.from_numpy(np.asarray(u)), torch.view_as_complex(torch.from_numpy(cw)),
+                    n).abs()
+    assert_close(y.cpu().numpy().astype(np.float64), ref.numpy(), FWD_TOL, "|y|")
