@@ -9,6 +9,8 @@ behind it change.  ``uninstall()`` restores the originals.
 
 Call sites served (reference paths):
   rqf_models/ops/scan.py:367, :509            -> _triton_chunked_scan
+  rqf_models/ops/scan.py:361                   -> B-matrix scan (library GEMM drive + scan)
+  rqf_models/backbones/s5/layer.py:254        -> parallel_scan with a B matrix on CUDA
   rqf_models/ops/scan.py:430-432               -> |scan| epilogue (sequential_scan_abs)
   rqf_models/backbones/rqf/block.py:926-934   -> _triton_chunked_scan_prospective
   rqf_models/backbones/rqf/block.py:737-764   -> fused multi-oscillator scans
@@ -30,6 +32,8 @@ _BINDINGS = [
     ("rqf_models.ops.chunked_scan_kernel", "_triton_chunked_scan_prospective",
      ops._triton_chunked_scan_prospective),
     ("rqf_models.ops.scan", "_triton_chunked_scan", ops._triton_chunked_scan),
+    ("rqf_models.ops.scan", "_triton_sequential_scan_b_matrix",
+     ops._triton_sequential_scan_b_matrix),
     ("rqf_models.ops.scan", "_sequential_scan_forward_abs_raw_block_f",
      ops._sequential_scan_forward_abs_raw_block_f),
     ("rqf_models.ops.scan", "_sequential_scan_real_forward_abs_raw_block_f",
@@ -76,6 +80,26 @@ def _tbptt_single_tap(orig):
     return _scan_with_grad_mode
 
 
+def _cuda_parallel_scan(orig):
+    """parallel_scan as bound in a caller module: CUDA inputs take this
+    backend (with or without a B matrix; the reference's CUDA branch sends a
+    B matrix to its PyTorch Blelloch scan, scan.py:503-529), others keep the
+    reference's own path."""
+    def parallel_scan(C1, C2, u, B=None):
+        if u.is_cuda:
+            return ops.parallel_scan(C1, C2, u, B)
+        return orig(C1, C2, u, B)
+
+    parallel_scan.__wrapped__ = orig
+    return parallel_scan
+
+
+# (module, attribute, wrapper of the original)
+_WRAPPED = [
+    ("rqf_models.backbones.s5.layer", "parallel_scan", _cuda_parallel_scan),
+]
+
+
 def install() -> list[str]:
     """Rebind the reference callables; returns the names that were patched."""
     if _SAVED:
@@ -86,6 +110,16 @@ def install() -> list[str]:
         if hasattr(mod, attr):
             _SAVED.append((mod, attr, getattr(mod, attr)))
             setattr(mod, attr, fn)
+            patched.append(f"{mod_name}.{attr}")
+    for mod_name, attr, wrap in _WRAPPED:
+        try:
+            mod = importlib.import_module(mod_name)
+        except ImportError:
+            continue
+        if hasattr(mod, attr):
+            orig = getattr(mod, attr)
+            _SAVED.append((mod, attr, orig))
+            setattr(mod, attr, wrap(orig))
             patched.append(f"{mod_name}.{attr}")
     block = importlib.import_module("rqf_models.backbones.rqf.block")
     base = block.BaseRQFBlock

@@ -471,6 +471,16 @@ def _sequential_scan_real_forward_abs_raw_block_f(C1, C2, u):
     return _scan_abs(C1, C2, u)
 
 
+def _triton_sequential_scan_b_matrix(C1, C2, u, B):
+    """Drop-in for triton_scan_kernel.py:_triton_sequential_scan_b_matrix (:3375):
+    x[n] = C1 x[n-1] + (C2 ⊙ B) @ u[n], B real (F, I), u (batch, time, I).  The
+    input projection B @ u runs as one library GEMM over all (batch, time) rows
+    and the recurrence on this backend's (B,T,F) scan with gain C2; autograd
+    gives the reference's gradients (grad_B real: the real part of the
+    complex one, as its backward takes)."""
+    return sequential_scan(C1, C2, u, B)
+
+
 def sequential_scan_abs(C1, C2, u, B=None):
     """|sequential_scan(...)| (rqf_models/ops/scan.py:381-432).  Without a B
     matrix and with no gradient required, the magnitude is written by the scan

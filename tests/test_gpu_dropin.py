@@ -194,3 +194,52 @@ def test_s4_rqf_block_multi_oscillator(parallel):
     launched = _compare(_s4(prospective_input=False, num_oscillators=4,
                             use_parallel_scan=parallel), x)
     assert "rqf_multi_osc_forward" in launched and "rqf_multi_osc_backward" in launched
+
+
+def test_s5_layer_parallel_scan():
+    """S5 layer with use_parallel_scan (s5/layer.py:253-254): parallel_scan as
+    bound in the layer's module runs on this backend."""
+    from rqf_models.backbones.s5.layer import S5Layer
+
+    torch.manual_seed(0)
+    layer = S5Layer(d_model=16, d_state=32, blocks=2, dropout=0.0, use_parallel_scan=True).cuda()
+    x = torch.randn(2, 1200, 16, device="cuda", generator=torch.Generator("cuda").manual_seed(9))
+    launched = _compare(layer, x)
+    assert "rqf_chunked_scan_forward" in launched
+
+
+def test_sequential_scan_b_matrix():
+    """rqf_models.ops.scan.sequential_scan with a B matrix (scan.py:338-361):
+    the reference's B-matrix Triton kernel against this backend (library GEMM
+    drive + scan), output and the gradients of C1, C2, u and B."""
+    import prospective_rqf_b200 as rqf
+    from prospective_rqf_b200 import _timing
+    from rqf_models.ops.scan import sequential_scan
+
+    g = torch.Generator("cuda").manual_seed(10)
+    F, I = 24, 12
+    C1 = torch.polar(0.9 + 0.09 * torch.rand(F, device="cuda", generator=g),
+                     3.0 * torch.rand(F, device="cuda", generator=g))
+    C2 = torch.randn(F, dtype=torch.complex64, device="cuda", generator=g)
+    Bm = torch.randn(F, I, device="cuda", generator=g) / 4
+    u = torch.randn(3, 900, I, dtype=torch.complex64, device="cuda", generator=g)
+    gy = torch.randn(3, 900, F, dtype=torch.complex64, device="cuda", generator=g)
+    res = []
+    for installed in (False, True):
+        rqf.uninstall()
+        if installed:
+            rqf.install()
+        try:
+            leaves = [t.clone().requires_grad_(True) for t in (C1, C2, u, Bm)]
+            with _timing.KernelTimer() as timer:
+                y = sequential_scan(leaves[0], leaves[1], leaves[2], B=leaves[3])
+                y.backward(gy)
+            res.append((y.detach(), [l.grad for l in leaves], timer.summary()))
+        finally:
+            rqf.uninstall()
+    assert "rqf_chunked_scan_forward" in res[1][2]
+    e = rel_err(_np(res[1][0]), _np(res[0][0]))
+    assert e <= FWD_TOL, f"forward differs by {e:.2e}"
+    for a, b, k in zip(res[1][1], res[0][1], ("C1", "C2", "u", "B")):
+        e = rel_err(_np(a), _np(b))
+        assert e <= GRAD_TOL, f"gradient of {k} differs by {e:.2e}"
