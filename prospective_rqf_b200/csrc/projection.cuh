@@ -51,19 +51,21 @@
 namespace rqf {
 namespace proj {
 
-constexpr int kBM = 128;              // A' rows per tile
-constexpr int kBN = 256;              // X' columns per tile
+constexpr int kBM = 128;              // A' rows per CTA (TMEM lanes)
+constexpr int kPairM = 2 * kBM;       // A' rows per CTA-pair tile: M of the two-SM MMA
+constexpr int kBN = 256;              // X' columns per pair tile: N of the MMA
+constexpr int kBNh = kBN / 2;         // X' columns each CTA of the pair stages
 constexpr int kBK = 16;               // K per stage: one 64-byte swizzle row of fp32
 constexpr int kUmmaK = 8;             // K of one tcgen05.mma kind::tf32
-constexpr int kStages = 4;
+constexpr int kStages = 6;
 constexpr int kAccBufs = 2;
 constexpr int kTmemCols = kBN * kAccBufs;  // 512: the whole TMEM of the SM
 constexpr int kThreads = 320;
-constexpr int kNBlocks = kBN / 32;    // 32-column (128-byte) blocks of an X' stage
+constexpr int kNBlocks = kBNh / 32;   // 32-column (128-byte) blocks of a CTA's X' stage
 
 constexpr int kABytes = kBM * kBK * 4;            // 8 KB, one of A_hi / A_lo
-constexpr int kBBytes = kBK * kBN * 4;            // 16 KB, one of X_hi / X_lo
-constexpr int kStageBytes = 2 * kABytes + 2 * kBBytes;
+constexpr int kBBytes = kBK * kBNh * 4;           // 8 KB, one of X_hi / X_lo
+constexpr int kStageBytes = 2 * kABytes + 2 * kBBytes;  // 32 KB
 constexpr int kTxBytes = 2 * kABytes + kBBytes;   // bytes the TMA lands per stage
 constexpr int kBarBytes = 256;
 constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;  // + alignment slack
@@ -83,9 +85,9 @@ struct Params {
   long long M;         // complex output rows
   long long N;         // complex samples
   int K;               // complex reduction length
-  int m_tiles, n_tiles, k_blocks;
+  int m_pairs, n_tiles, k_blocks;  // pair tiles: kPairM A' rows x kBN X' columns
   long long num_tiles;
-  int a_rows_pad;      // rows of the hi half of the split A' buffer
+  int a_rows_pad;      // rows of the hi half of the split A' buffer (a multiple of kPairM)
 };
 
 // ------------------------------------------------------------ PTX wrappers
@@ -173,21 +175,71 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-__device__ __forceinline__ void tc_commit(uint64_t *bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          smem_u32(bar))
-      : "memory");
+// ------------------------------------------------------------ CTA pair
+// The two CTAs of a cluster (ranks 0 and 1) run on the two SMs of one TPC and
+// share each tcgen05.mma.cta_group::2: rank 0 (the leader) issues it, each
+// CTA holds its half of A (128 rows) and of B (N/2 columns) at the same
+// shared-memory offsets, and each CTA's TMEM receives its 128 rows of D.
+// The peer reaches the leader's barriers through the cluster window; the
+// leader's commits arrive on both CTAs' barriers, one commit per barrier.
+__device__ __forceinline__ uint32_t pair_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
 }
-__device__ __forceinline__ void tc_mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                            uint32_t idesc, uint32_t accumulate) {
+__device__ __forceinline__ uint32_t pair_index() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t pair_count() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// Address of `local`'s counterpart in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void *local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(caddr)
+               : "memory");
+}
+// Every thread of both CTAs.
+__device__ __forceinline__ void pair_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit_pair(uint32_t caddr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   caddr)
+               : "memory");
+}
+__device__ __forceinline__ void tc_mma_pair_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                 uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// TMEM of the pair: one warp of each CTA (the same warp index) allocates and
+// frees together.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *slot, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(slot)),
+               "r"(cols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_free_pair(uint32_t base, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(cols)
+               : "memory");
+}
+
 // 32 lanes x 32 consecutive fp32 columns: thread i of the warp receives
 // columns [col, col+32) of TMEM lane (lane base + i).
 __device__ __forceinline__ void tc_ld_32x32b_x32(uint32_t taddr, float (&v)[32]) {
@@ -253,9 +305,13 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
          ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (swizzle << 61);
 }
 
-// Instruction descriptor: D fp32, A and B TF32, A K-major, B MN-major, M = 128, N = 256.
+// Instruction descriptors (kind::tf32, D fp32): M = 256 (the CTA pair), N = 256.
+// kIdesc: A K-major, B MN-major (the projection's X').  kIdescKK: both
+// K-major (the weight gradient's h' rows).
 constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | (0u << 15) | (1u << 16) |
-                            ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+                            ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kPairM >> 4) << 24);
+constexpr uint32_t kIdescKK = (1u << 4) | (2u << 7) | (2u << 10) | (0u << 15) | (0u << 16) |
+                              ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kPairM >> 4) << 24);
 
 // ------------------------------------------------------------ weight split
 // A' rows alternate Re and Im of op(W)[j,:]; hi in rows [0, rows_pad), lo in
@@ -285,38 +341,43 @@ __global__ void proj_prep_kernel(const float2 *__restrict__ W, float *__restrict
 }
 
 // ------------------------------------------------------------ main kernel
-__device__ __forceinline__ void tile_coords(long long tile, const Params &p, int &mt, int &nt) {
-  mt = (int)(tile % p.m_tiles);  // consecutive CTAs share an X' tile through L2
-  nt = (int)(tile / p.m_tiles);
+// Pair tile t covers A' rows [mp*256, mp*256+256) and X' columns
+// [nt*256, nt*256+256); the pair tiles of one X' column block are neighbours
+// (mp fastest), so the block is read from HBM once and from L2 after.
+__device__ __forceinline__ void tile_coords(long long tile, const Params &p, int &mp, int &nt) {
+  mp = (int)(tile % p.m_pairs);
+  nt = (int)(tile / p.m_pairs);
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmX,
             const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
-  uint64_t *full = bars;                 // TMA landed            (1 arrival + tx)
-  uint64_t *ready = bars + kStages;      // X' split done         (4 transform warps)
-  uint64_t *empty = bars + 2 * kStages;  // MMAs done with stage  (tcgen05.commit)
-  uint64_t *accf = bars + 3 * kStages;   // accumulator complete  (tcgen05.commit)
-  uint64_t *acce = accf + kAccBufs;      // accumulator drained   (4 epilogue warps)
+  uint64_t *full = bars;                 // this CTA's TMA landed  (1 arrival + tx)
+  uint64_t *ready = bars + kStages;      // X' split done, both CTAs (leader's; 8 warps)
+  uint64_t *empty = bars + 2 * kStages;  // MMAs done with stage  (leader's commit)
+  uint64_t *accf = bars + 3 * kStages;   // accumulator complete  (leader's commit)
+  uint64_t *acce = accf + kAccBufs;      // accumulator drained, both CTAs (leader's; 8 warps)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acce + kAccBufs);
   volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = pair_rank();
+  const long long pair0 = pair_index(), npairs = pair_count();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&ready[s], 4);
+      mbar_init(&ready[s], 8);
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < kAccBufs; ++a) {
       mbar_init(&accf[a], 1);
-      mbar_init(&acce[a], 4);
+      mbar_init(&acce[a], 8);
     }
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -324,14 +385,11 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     prefetch_tmap(&tmX);
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_slot)),
-                 "r"(kTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    tmem_alloc_pair(tmem_slot, kTmemCols);
     tc_fence_before();
   }
   __syncthreads();
+  pair_sync();  // both CTAs' barriers initialised before any remote arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -342,9 +400,11 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (long long tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-        int mt, nt;
-        tile_coords(tile, p, mt, nt);
+      for (long long tile = pair0; ok && tile < p.num_tiles; tile += npairs) {
+        int mp, nt;
+        tile_coords(tile, p, mp, nt);
+        const int arow = mp * kPairM + (int)rank * kBM;
+        const int xcol = nt * kBN + (int)rank * kBNh;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort, 1)) {
             ok = false;
@@ -352,12 +412,12 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           }
           uint8_t *st = smem + stage * kStageBytes;
           mbar_expect_tx(&full[stage], kTxBytes);
-          tma_load_2d(st, &tmA, &full[stage], kb * kBK, mt * kBM);
-          tma_load_2d(st + kABytes, &tmA, &full[stage], kb * kBK, p.a_rows_pad + mt * kBM);
+          tma_load_2d(st, &tmA, &full[stage], kb * kBK, arow);
+          tma_load_2d(st + kABytes, &tmA, &full[stage], kb * kBK, p.a_rows_pad + arow);
 #pragma unroll
           for (int i = 0; i < kNBlocks; ++i)
-            tma_load_2d(st + 2 * kABytes + i * (kBK * 128), &tmX, &full[stage],
-                        nt * kBN + i * 32, kb * kBK);
+            tma_load_2d(st + 2 * kABytes + i * (kBK * 128), &tmX, &full[stage], xcol + i * 32,
+                        kb * kBK);
           ++issued;
           if (++stage == kStages) {
             stage = 0;
@@ -375,14 +435,14 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       }
     }
   } else if (warp == 1) {
-    // ---------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // ---------------------------------------------------------- MMA issuer (leader)
+    if (rank == 0 && lane == 0) {
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
       uint64_t *last = nullptr;
       uint32_t last_parity = 0;
-      for (long long tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+      for (long long tile = pair0; ok && tile < p.num_tiles; tile += npairs) {
         if (!mbar_wait(&acce[acc], acc_phase ^ 1u, abort, 3)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kBN);
@@ -395,7 +455,7 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           const uint32_t st = smem_u32(smem + stage * kStageBytes);
           // A': K-major 64-byte rows, 8-row groups 512 B apart.  X': MN-major,
           // 32-column (128-byte) blocks kBK*128 B apart (LBO), 4-row groups
-          // 512 B apart (SBO).
+          // 512 B apart (SBO).  Both CTAs hold their halves at these offsets.
           const uint64_t a_hi = smem_desc(st, 16, 512, kSwizzle64B);
           const uint64_t a_lo = smem_desc(st + kABytes, 16, 512, kSwizzle64B);
           const uint64_t b_hi = smem_desc(st + 2 * kABytes, kBK * 128, 512, kSwizzle128BBase32);
@@ -408,11 +468,12 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             const uint64_t da = (uint64_t)(ks * (kUmmaK * 4) >> 4);
             const uint64_t db = (uint64_t)(ks * (kUmmaK * 128) >> 4);
             const uint32_t accum = (kb > 0 || ks > 0) ? 1u : 0u;
-            tc_mma_tf32(d_tmem, a_hi + da, b_hi + db, kIdesc, accum);
-            tc_mma_tf32(d_tmem, a_hi + da, b_lo + db, kIdesc, 1u);
-            tc_mma_tf32(d_tmem, a_lo + da, b_hi + db, kIdesc, 1u);
+            tc_mma_pair_tf32(d_tmem, a_hi + da, b_hi + db, kIdesc, accum);
+            tc_mma_pair_tf32(d_tmem, a_hi + da, b_lo + db, kIdesc, 1u);
+            tc_mma_pair_tf32(d_tmem, a_lo + da, b_hi + db, kIdesc, 1u);
           }
-          tc_commit(&empty[stage]);
+          tc_commit_pair(cluster_addr(&empty[stage], 0));
+          tc_commit_pair(cluster_addr(&empty[stage], 1));
           last = &empty[stage];
           last_parity = phase;
           if (++stage == kStages) {
@@ -421,32 +482,35 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           }
         }
         if (!ok) break;
-        tc_commit(&accf[acc]);
+        tc_commit_pair(cluster_addr(&accf[acc], 0));
+        tc_commit_pair(cluster_addr(&accf[acc], 1));
         if (++acc == kAccBufs) {
           acc = 0;
           acc_phase ^= 1u;
         }
       }
-      // The MMAs read shared memory and write TMEM asynchronously: the last
-      // commit must land before the CTA frees either.
+      // The MMAs read both CTAs' shared memory and write both TMEMs
+      // asynchronously: the last commit must land before either CTA frees them.
       if (last != nullptr) mbar_drain(last, last_parity);
     }
   } else if (warp < 6) {
     // ---------------------------------------------------------- epilogue
     const int quarter = warp & 3;          // TMEM lanes this warp may read
-    const int row = quarter * 32 + lane;   // A' row within the tile
+    const int row = quarter * 32 + lane;   // A' row within this CTA's half of the tile
     const bool odd = (row & 1) != 0;
+    const uint32_t acce0 = cluster_addr(&acce[0], 0);
+    const uint32_t acce1 = cluster_addr(&acce[1], 0);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (long long tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+    for (long long tile = pair0; tile < p.num_tiles; tile += npairs) {
       // every lane waits; the decision is made warp-uniform before the
       // .sync.aligned TMEM loads
       const bool ok = mbar_wait(&accf[acc], acc_phase, abort, 5);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      int mt, nt;
-      tile_coords(tile, p, mt, nt);
-      const long long j = (long long)mt * (kBM / 2) + (row >> 1);
+      int mp, nt;
+      tile_coords(tile, p, mp, nt);
+      const long long j = ((long long)mp * kPairM + (long long)rank * kBM + row) >> 1;
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kBN);
 #pragma unroll 1
       for (int c = 0; c < kBN / 32; ++c) {
@@ -495,7 +559,7 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acce[acc]);
+      if (lane == 0) mbar_arrive_cluster(acc ? acce1 : acce0);
       if (++acc == kAccBufs) {
         acc = 0;
         acc_phase ^= 1u;
@@ -507,13 +571,13 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (long long tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+    for (long long tile = pair0; ok && tile < p.num_tiles; tile += npairs) {
       for (int kb = 0; kb < p.k_blocks; ++kb) {
         ok = __all_sync(0xffffffffu, mbar_wait(&full[stage], phase, abort, 2));
         if (!ok) break;
         float4 *xb = reinterpret_cast<float4 *>(smem + stage * kStageBytes + 2 * kABytes);
         float4 *xl = reinterpret_cast<float4 *>(smem + stage * kStageBytes + 2 * kABytes + kBBytes);
-#pragma unroll 4
+#pragma unroll
         for (int i = t; i < kBBytes / 16; i += 128) {
           const float4 v = xb[i];  // stays in place as the hi part
           xl[i] = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
@@ -521,7 +585,7 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         // generic-proxy smem writes -> visible to the tensor core (async proxy)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
-        if (lane == 0) mbar_arrive(&ready[stage]);
+        if (lane == 0) mbar_arrive_cluster(cluster_addr(&ready[stage], 0));
         if (++stage == kStages) {
           stage = 0;
           phase ^= 1u;
@@ -533,11 +597,10 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   __syncwarp();  // lanes of warps 0 and 1 wait for their elected lane's loop
   tc_fence_before();
   __syncthreads();
+  pair_sync();  // no MMA, commit or remote arrival of either CTA is still pending
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(kTmemCols)
-                 : "memory");
+    tmem_free_pair(tmem_base, kTmemCols);
   }
 }
 
@@ -546,32 +609,30 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 // gW[j, i] = sum_n gz[j, n] conj(h[i, n]): the weight cotangent of z = W h.
 // Over the interleaved samples k' = 2n + {0: Re, 1: Im},
 //   Re gW[j,i] = sum_k' gz'[j,k'] h'[i,k'],    Im gW[j,i] = sum_k' gz'[j,k'] h~'[i,k'],
-// with h~'[i,2n] = -Im h[i,n] and h~'[i,2n+1] = Re h[i,n].  A work tile of
-// 128 j x 128 i accumulates D[j][c] in TMEM: column c < 128 holds Re and
-// c >= 128 holds Im of gW[j, i0 + c mod 128].  The k' range is split over
-// CTAs (split-K); each CTA stores its fp32 partial tile and
-// proj_wgrad_reduce_kernel sums the partials in a fixed order (deterministic).
-// A = gz' is K-major as loaded (64-byte swizzle, split in place like X' of the
-// projection).  B = [h' ; h~'] must be MN-major for a 32-bit operand, so the
-// transform warps transpose the TMA-loaded h' tile into the 32-byte-atom
-// layout while splitting it, writing both halves as hi and lo parts.
+// with h~'[i,2n] = -Im h[i,n] and h~'[i,2n+1] = Re h[i,n].  A CTA pair owns a
+// work tile of 256 j x 128 i: A = gz' (each CTA 128 j rows), B = 256 columns,
+// CTA r's half being [h' ; h~'] of the 64 rows i0 + 64r + [0, 64).  Both
+// operands are K-major, as TMA lands them (64-byte swizzle): h' is its own hi
+// part, and h~' is a swap-and-negate of each (Re, Im) pair inside a 16-byte
+// chunk, so the transform warps only rewrite chunks in place order (lo parts
+// and h~'), with no transpose.  Each CTA's TMEM holds D[j][c] for its 128 j:
+// column c = 128h + 64q + e holds (q = 0: Re, 1: Im) gW[j, i0 + 64h + e].  The
+// k' range is split over CTA pairs (split-K); each CTA stores its fp32
+// partial tile and proj_wgrad_reduce_kernel sums the partials in a fixed
+// order (deterministic).
 //
-// Two rings.  The TMA lands raw (gz', h') tiles in an 8-deep raw ring; the
-// transform warps turn each into MMA operands in a 2-deep compute ring and
-// release the raw stage at once.  At full size the tile CTAs of one k-split
-// drift apart and their shared rows fall out of L2, so the loads see HBM
-// latency; the raw ring keeps 7 tiles (112 KB) in flight per SM to cover it.
-constexpr int kWgRows = 128;                     // j per tile (A rows) and i per tile
-constexpr int kWgRawStages = 8;
-constexpr int kWgCompStages = 2;
-constexpr int kWgABytes = kWgRows * kBK * 4;     // 8 KB: gz' tile (raw / hi / lo)
-constexpr int kWgSrcBytes = kWgRows * kBK * 4;   // 8 KB: h' raw tile
-constexpr int kWgBBytes = kBK * kBN * 4;         // 16 KB: one of B_hi / B_lo
-constexpr int kWgRawBytes = kWgABytes + kWgSrcBytes;             // 16 KB
-constexpr int kWgCompBytes = 2 * kWgABytes + 2 * kWgBBytes;      // 48 KB: A_hi A_lo B_hi B_lo
-constexpr int kWgTxBytes = kWgRawBytes;
-constexpr int kWgSmemBytes =
-    kWgRawStages * kWgRawBytes + kWgCompStages * kWgCompBytes + kBarBytes + 1024;
+// Stage (32 KB per CTA): A_hi = gz' (TMA, 8 KB) | B_hi = h' (TMA, 4 KB), h~'
+// (4 KB) | A_lo (8 KB) | B_lo = h'_lo, h~'_lo (8 KB).
+constexpr int kWgRows = 128;                     // j rows per CTA
+constexpr int kWgPairRows = 2 * kWgRows;         // j rows per pair tile
+constexpr int kWgCols = 128;                     // i per pair tile
+constexpr int kWgHRows = kWgCols / 2;            // h' rows each CTA stages
+constexpr int kWgStages = 6;
+constexpr int kWgABytes = kWgRows * kBK * 4;     // 8 KB: gz' tile (hi or lo)
+constexpr int kWgHBytes = kWgHRows * kBK * 4;    // 4 KB: h' rows (one of h', h~')
+constexpr int kWgStageBytes = 2 * kWgABytes + 4 * kWgHBytes;  // 32 KB
+constexpr int kWgTxBytes = kWgABytes + kWgHBytes;             // 12 KB landed by TMA
+constexpr int kWgSmemBytes = kWgStages * kWgStageBytes + kBarBytes + 1024;
 // TMEM: columns [0, 256) the CTA's running total, [256, 512) the chunk
 // accumulator.  The tensor core's fp32 accumulate rounds with a bias that
 // grows with the number of accumulations into one accumulator (about 2e-4
@@ -582,111 +643,103 @@ constexpr int kWgTmemCols = 2 * kBN;
 constexpr int kWgChunk = 16;
 
 struct WgParams {
-  float2 *partials;          // [splits][m_tiles*128][ld] complex
+  float2 *partials;          // [splits][m_pairs*256][ld] complex
   long long M, K;            // gW is M x K (F_out x F_in)
-  int m_tiles, i_tiles, splits;
+  int m_pairs, i_tiles, splits;
   long long kblocks;         // ceil(2N / kBK)
   int ld;                    // i_tiles * 128
 };
 
-// Byte offset of element (column c, row k) of an MN-major 32-byte-atom tile
-// whose 32-column blocks are kBK rows of 128 bytes.
-__device__ __forceinline__ uint32_t mn32_offset(int c, int k) {
-  return (uint32_t)((c >> 5) * (kBK * 128) + k * 128 + ((((c & 31) >> 3) ^ (k & 3)) << 5) +
-                    ((c & 7) << 2));
+// 10 warps: 0 TMA, 1 MMA (leader) / TMEM, 2..5 epilogue, 6..9 transform.
+constexpr int kWgThreads = 320;
+
+__device__ __forceinline__ float4 swap_neg(float4 v) { return make_float4(-v.y, v.x, -v.w, v.z); }
+__device__ __forceinline__ float4 tf32_lo4(float4 v) {
+  return make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
 }
 
-// 14 warps: 0 TMA, 1 MMA, 2..5 epilogue, 6..13 transform (two per h' row).
-constexpr int kWgThreads = 448;
-constexpr int kWgTransformWarps = 8;
-
-__global__ void __launch_bounds__(kWgThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWgThreads, 1)
 proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmH,
                   const WgParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *raw = smem;                                    // kWgRawStages x 16 KB
-  uint8_t *comp = smem + kWgRawStages * kWgRawBytes;      // kWgCompStages x 48 KB
-  uint64_t *bars = reinterpret_cast<uint64_t *>(comp + kWgCompStages * kWgCompBytes);
-  uint64_t *rfull = bars;                         // raw tile landed       (1 + tx)
-  uint64_t *rempty = rfull + kWgRawStages;        // raw tile consumed     (8 transform warps)
-  uint64_t *cready = rempty + kWgRawStages;       // operands written      (8 transform warps)
-  uint64_t *cempty = cready + kWgCompStages;      // operands consumed     (tcgen05.commit)
-  uint64_t *accf = cempty + kWgCompStages;  // chunk accumulated   (tcgen05.commit)
-  uint64_t *acce = accf + 1;              // chunk folded/drained (4 epilogue warps)
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kWgStages * kWgStageBytes);
+  uint64_t *full = bars;                   // this CTA's TMA landed   (1 + tx)
+  uint64_t *ready = full + kWgStages;      // operands written, both CTAs (leader's; 8 warps)
+  uint64_t *empty = ready + kWgStages;     // MMAs done with stage   (leader's commit)
+  uint64_t *accf = empty + kWgStages;      // chunk accumulated      (leader's commit)
+  uint64_t *acce = accf + 1;               // chunk folded, both CTAs (leader's; 8 warps)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acce + 1);
   volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // tile fastest: the CTAs that share a gz' or h' block over the same k range
-  // are neighbours in launch order and progress together, so the block is
-  // read from HBM once and from L2 by its second user
-  const int ntiles = p.m_tiles * p.i_tiles;
-  const int split = blockIdx.x / ntiles;
-  const int tile = blockIdx.x - split * ntiles;
-  const int mt = tile % p.m_tiles;
-  const int it = tile / p.m_tiles;
+  const uint32_t rank = pair_rank();
+  // tile fastest: the pairs that share a gz' or h' block over the same k
+  // range are neighbours in launch order and progress together, so the block
+  // is read from HBM once and from L2 by its second user
+  const int ntiles = p.m_pairs * p.i_tiles;
+  const int pid = (int)pair_index();
+  const int split = pid / ntiles;
+  const int tile = pid - split * ntiles;
+  const int mp = tile % p.m_pairs;
+  const int it = tile / p.m_pairs;
   const long long kb0 = (long long)split * p.kblocks / p.splits;
   const long long kb1 = (long long)(split + 1) * p.kblocks / p.splits;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kWgRawStages; ++s) {
-      mbar_init(&rfull[s], 1);
-      mbar_init(&rempty[s], kWgTransformWarps);
-    }
-    for (int s = 0; s < kWgCompStages; ++s) {
-      mbar_init(&cready[s], kWgTransformWarps);
-      mbar_init(&cempty[s], 1);
+    for (int s = 0; s < kWgStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&ready[s], 8);
+      mbar_init(&empty[s], 1);
     }
     mbar_init(accf, 1);
-    mbar_init(acce, 4);
+    mbar_init(acce, 8);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_tmap(&tmG);
     prefetch_tmap(&tmH);
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_slot)),
-                 "r"(kWgTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    tmem_alloc_pair(tmem_slot, kWgTmemCols);
     tc_fence_before();
   }
   __syncthreads();
+  pair_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
     // ---------------------------------------------------------- producer
     if (lane == 0) {
+      const int jrow = mp * kWgPairRows + (int)rank * kWgRows;
+      const int irow = it * kWgCols + (int)rank * kWgHRows;
       int stage = 0, issued = 0;
       uint32_t phase = 0;
       for (long long kb = kb0; kb < kb1; ++kb) {
-        if (!mbar_wait(&rempty[stage], phase ^ 1u, abort, 1)) break;
-        uint8_t *st = raw + stage * kWgRawBytes;
-        mbar_expect_tx(&rfull[stage], kWgTxBytes);
-        tma_load_2d(st, &tmG, &rfull[stage], (int)(kb * kBK), mt * kWgRows);
-        tma_load_2d(st + kWgABytes, &tmH, &rfull[stage], (int)(kb * kBK), it * kWgRows);
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort, 1)) break;
+        uint8_t *st = smem + stage * kWgStageBytes;
+        mbar_expect_tx(&full[stage], kWgTxBytes);
+        tma_load_2d(st, &tmG, &full[stage], (int)(kb * kBK), jrow);
+        tma_load_2d(st + kWgABytes, &tmH, &full[stage], (int)(kb * kBK), irow);
         ++issued;
-        if (++stage == kWgRawStages) {
+        if (++stage == kWgStages) {
           stage = 0;
           phase ^= 1u;
         }
       }
-      for (int i = 0; i < kWgRawStages && i < issued; ++i) {
+      for (int i = 0; i < kWgStages && i < issued; ++i) {
         if (--stage < 0) {
-          stage = kWgRawStages - 1;
+          stage = kWgStages - 1;
           phase ^= 1u;
         }
-        mbar_drain(&rfull[stage], phase);
+        mbar_drain(&full[stage], phase);
       }
     }
   } else if (warp == 1) {
-    // ---------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // ---------------------------------------------------------- MMA issuer (leader)
+    if (rank == 0 && lane == 0) {
       int stage = 0;
       uint32_t phase = 0, cphase = 0;
       bool ok = true;
@@ -698,36 +751,37 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
         if (!mbar_wait(acce, cphase ^ 1u, abort, 3)) break;  // previous chunk read out
         tc_fence_after();
         for (long long kb = c0; kb < c1; ++kb) {
-          if (!mbar_wait(&cready[stage], phase, abort, 4)) {
+          if (!mbar_wait(&ready[stage], phase, abort, 4)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t st = smem_u32(comp + stage * kWgCompBytes);
+          const uint32_t st = smem_u32(smem + stage * kWgStageBytes);
           const uint64_t a_hi = smem_desc(st, 16, 512, kSwizzle64B);
-          const uint64_t a_lo = smem_desc(st + kWgABytes, 16, 512, kSwizzle64B);
-          const uint32_t bb = st + 2 * kWgABytes;
-          const uint64_t b_hi = smem_desc(bb, kBK * 128, 512, kSwizzle128BBase32);
-          const uint64_t b_lo = smem_desc(bb + kWgBBytes, kBK * 128, 512, kSwizzle128BBase32);
+          const uint64_t b_hi = smem_desc(st + kWgABytes, 16, 512, kSwizzle64B);
+          const uint64_t a_lo = smem_desc(st + kWgABytes + 2 * kWgHBytes, 16, 512, kSwizzle64B);
+          const uint64_t b_lo =
+              smem_desc(st + 2 * kWgABytes + 2 * kWgHBytes, 16, 512, kSwizzle64B);
 #pragma unroll
           for (int ks = 0; ks < kBK / kUmmaK; ++ks) {
-            const uint64_t da = (uint64_t)(ks * (kUmmaK * 4) >> 4);
-            const uint64_t db = (uint64_t)(ks * (kUmmaK * 128) >> 4);
+            const uint64_t dk = (uint64_t)(ks * (kUmmaK * 4) >> 4);  // 32 B along K
             const uint32_t accum = (kb > c0 || ks > 0) ? 1u : 0u;
-            tc_mma_tf32(d_tmem, a_hi + da, b_hi + db, kIdesc, accum);
-            tc_mma_tf32(d_tmem, a_hi + da, b_lo + db, kIdesc, 1u);
-            tc_mma_tf32(d_tmem, a_lo + da, b_hi + db, kIdesc, 1u);
+            tc_mma_pair_tf32(d_tmem, a_hi + dk, b_hi + dk, kIdescKK, accum);
+            tc_mma_pair_tf32(d_tmem, a_hi + dk, b_lo + dk, kIdescKK, 1u);
+            tc_mma_pair_tf32(d_tmem, a_lo + dk, b_hi + dk, kIdescKK, 1u);
           }
-          tc_commit(&cempty[stage]);
-          last = &cempty[stage];
+          tc_commit_pair(cluster_addr(&empty[stage], 0));
+          tc_commit_pair(cluster_addr(&empty[stage], 1));
+          last = &empty[stage];
           last_parity = phase;
-          if (++stage == kWgCompStages) {
+          if (++stage == kWgStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        tc_commit(accf);
+        tc_commit_pair(cluster_addr(accf, 0));
+        tc_commit_pair(cluster_addr(accf, 1));
         last = accf;
         last_parity = cphase;
         cphase ^= 1u;
@@ -739,6 +793,7 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16);
+    const uint32_t acce_leader = cluster_addr(acce, 0);
     const long long nchunks = (kb1 - kb0 + kWgChunk - 1) / kWgChunk;
     uint32_t cphase = 0;
     bool ok = true;
@@ -762,21 +817,23 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
         }
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       } else {
-        // last chunk: partial = total + chunk, Re in columns [0,128), Im in [128,256)
-        const long long j = (long long)mt * kWgRows + row;
-        float2 *dst = p.partials + ((long long)split * p.m_tiles * kWgRows + j) * p.ld +
-                      (long long)it * kWgRows;
+        // last chunk: partial = total + chunk; columns 128h + 64q + e hold
+        // (q = 0: Re, 1: Im) of i = i0 + 64h + e
+        const long long j = (long long)mp * kWgPairRows + (long long)rank * kWgRows + row;
+        float2 *dst = p.partials + ((long long)split * p.m_pairs * kWgPairRows + j) * p.ld +
+                      (long long)it * kWgCols;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
+          const int col = (c >> 1) * 128 + (c & 1) * 32;  // Re columns; Im at col + 64
           float re[32], im[32];
-          tc_ld_32x32b_x32(tbase + (uint32_t)(kBN + c * 32), re);
-          tc_ld_32x32b_x32(tbase + (uint32_t)(kBN + 128 + c * 32), im);
+          tc_ld_32x32b_x32(tbase + (uint32_t)(kBN + col), re);
+          tc_ld_32x32b_x32(tbase + (uint32_t)(kBN + col + 64), im);
           if (q > 0) {
             float t[32];
-            tc_ld_32x32b_x32(tbase + (uint32_t)(c * 32), t);
+            tc_ld_32x32b_x32(tbase + (uint32_t)col, t);
 #pragma unroll
             for (int i = 0; i < 32; ++i) re[i] += t[i];
-            tc_ld_32x32b_x32(tbase + (uint32_t)(128 + c * 32), t);
+            tc_ld_32x32b_x32(tbase + (uint32_t)(col + 64), t);
 #pragma unroll
             for (int i = 0; i < 32; ++i) im[i] += t[i];
           }
@@ -788,68 +845,41 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(acce);
+      if (lane == 0) mbar_arrive_cluster(acce_leader);
       cphase ^= 1u;
     }
   } else {
     // ---------------------------------------------------------- transform
-    const int t = threadIdx.x - 6 * 32;  // 0..255
-    const int hr = t & (kWgRows - 1);    // the h' row this thread transposes ...
-    const int kh = (t >> 7) * (kBK / 2); // ... over the steps [kh, kh + 8) of the tile
-    int rs = 0, cs = 0;
-    uint32_t rph = 0, cph = 0;
+    // Chunk-wise (16 bytes = two (Re, Im) pairs): every derived operand sits
+    // at the same offset within its region as the TMA chunk it comes from, so
+    // the 64-byte swizzle carries over unchanged.
+    const int t = threadIdx.x - 6 * 32;  // 0..127
+    int stage = 0;
+    uint32_t phase = 0;
     for (long long kb = kb0; kb < kb1; ++kb) {
-      if (!__all_sync(0xffffffffu, mbar_wait(&rfull[rs], rph, abort, 2))) break;
-      if (!__all_sync(0xffffffffu, mbar_wait(&cempty[cs], cph ^ 1u, abort, 2))) break;
-      const uint8_t *rst = raw + rs * kWgRawBytes;
-      uint8_t *cst = comp + cs * kWgCompBytes;
-      // gz': the raw tile is the hi part (copied, keeping its 64-byte swizzle
-      // on a 1024-byte-aligned buffer), plus the lo part
-      const float4 *ar = reinterpret_cast<const float4 *>(rst);
-      float4 *ah = reinterpret_cast<float4 *>(cst);
-      float4 *al = reinterpret_cast<float4 *>(cst + kWgABytes);
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, abort, 2))) break;
+      uint8_t *st = smem + stage * kWgStageBytes;
+      const float4 *ah = reinterpret_cast<const float4 *>(st);
+      float4 *bh = reinterpret_cast<float4 *>(st + kWgABytes);
+      float4 *al = reinterpret_cast<float4 *>(st + kWgABytes + 2 * kWgHBytes);
+      float4 *bl = reinterpret_cast<float4 *>(st + 2 * kWgABytes + 2 * kWgHBytes);
+      constexpr int kAChunks = kWgABytes / 16, kHChunks = kWgHBytes / 16;
 #pragma unroll
-      for (int i = t; i < kWgABytes / 16; i += 32 * kWgTransformWarps) {
-        const float4 v = ar[i];
-        ah[i] = v;
-        al[i] = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
-      }
-      // h' row hr, steps [kh, kh + 8): two of the four 16-byte chunks of the
-      // row, 64-byte swizzle (chunk q of row r at q ^ ((r >> 1) & 3))
-      const uint8_t *src = rst + kWgABytes + hr * 64;
-      float x[kBK / 2];
+      for (int i = t; i < kAChunks; i += 128) al[i] = tf32_lo4(ah[i]);
 #pragma unroll
-      for (int q2 = 0; q2 < 2; ++q2) {
-        const int q = (kh >> 2) + q2;
-        const float4 v = *reinterpret_cast<const float4 *>(src + ((q ^ ((hr >> 1) & 3)) << 4));
-        x[4 * q2] = v.x; x[4 * q2 + 1] = v.y; x[4 * q2 + 2] = v.z; x[4 * q2 + 3] = v.w;
-      }
-      // the raw stage is no longer needed: hand it back to the producer
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&rempty[rs]);
-      uint8_t *bh = cst + 2 * kWgABytes;
-      uint8_t *bl = bh + kWgBBytes;
-#pragma unroll
-      for (int kk = 0; kk < kBK / 2; ++kk) {
-        const int k = kh + kk;
-        const float v = x[kk];
-        const float sw = (kk & 1) ? x[kk - 1] : -x[kk + 1];  // h~' (pairs stay in one half)
-        const uint32_t o1 = mn32_offset(hr, k), o2 = mn32_offset(hr + kWgRows, k);
-        *reinterpret_cast<float *>(bh + o1) = v;
-        *reinterpret_cast<float *>(bl + o1) = tf32_lo(v);
-        *reinterpret_cast<float *>(bh + o2) = sw;
-        *reinterpret_cast<float *>(bl + o2) = tf32_lo(sw);
+      for (int i = t; i < kHChunks; i += 128) {
+        const float4 v = bh[i];
+        const float4 lo = tf32_lo4(v);
+        bh[kHChunks + i] = swap_neg(v);
+        bl[i] = lo;
+        bl[kHChunks + i] = swap_neg(lo);
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
-      if (lane == 0) mbar_arrive(&cready[cs]);
-      if (++rs == kWgRawStages) {
-        rs = 0;
-        rph ^= 1u;
-      }
-      if (++cs == kWgCompStages) {
-        cs = 0;
-        cph ^= 1u;
+      if (lane == 0) mbar_arrive_cluster(cluster_addr(&ready[stage], 0));
+      if (++stage == kWgStages) {
+        stage = 0;
+        phase ^= 1u;
       }
     }
   }
@@ -857,11 +887,10 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
   __syncwarp();
   tc_fence_before();
   __syncthreads();
+  pair_sync();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(kWgTmemCols)
-                 : "memory");
+    tmem_free_pair(tmem_base, kWgTmemCols);
   }
 }
 

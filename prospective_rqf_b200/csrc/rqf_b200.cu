@@ -1067,25 +1067,44 @@ struct ProjGeometry {
 
 inline ProjGeometry proj_geometry(int64_t m, int64_t k) {
   ProjGeometry g;
-  g.rows_pad = ceil_div(2 * m, proj::kBM) * proj::kBM;
+  g.rows_pad = ceil_div(2 * m, proj::kPairM) * proj::kPairM;
   g.k_pad = ceil_div(k, proj::kBK) * proj::kBK;
   return g;
 }
 
-int proj_ctas_per_device() {
-  int dev = 0, sms = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+// How many CTA pairs (clusters of 2) of `kernel` the device holds at once,
+// after raising its dynamic shared-memory limit; 0 on failure.  Cached per
+// device and kernel.
+template <int kSlot>
+int pair_capacity(const void *kernel, int threads, int smem) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
   static std::mutex mu;
-  static bool configured[64] = {};
+  static int cached[64] = {};
   std::lock_guard<std::mutex> lock(mu);
-  if (dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(proj::proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             proj::kSmemBytes) != cudaSuccess)
+  if (cached[dev] == 0) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
       return 0;
-    configured[dev] = true;
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(sms & ~1), 1, 1);
+    cfg.blockDim = dim3((unsigned)threads, 1, 1);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sms / 2;  // one CTA per SM, SMs paired per TPC
+    }
+    cached[dev] = n;
   }
-  return sms;
+  return cached[dev];
+}
+
+int proj_pairs_per_device() {
+  return pair_capacity<0>(reinterpret_cast<const void *>(proj::proj_kernel), proj::kThreads,
+                          proj::kSmemBytes);
 }
 
 }  // namespace
@@ -1132,8 +1151,8 @@ int rqf_projection(const float *w, const float *x, const float *acc, float *out,
     return RQF_ERR_ALIGN;
   const ProjGeometry g = proj_geometry(m, k);
   if (g.rows_pad > 0x3fffffffLL || g.k_pad > 0x7fffffffLL) return RQF_ERR_SHAPE;
-  const int sms = proj_ctas_per_device();
-  if (sms <= 0) return RQF_ERR_LAUNCH;
+  const int pairs = proj_pairs_per_device();
+  if (pairs <= 0) return RQF_ERR_LAUNCH;
 
   float *a_split = static_cast<float *>(workspace);
   {
@@ -1158,12 +1177,12 @@ int rqf_projection(const float *w, const float *x, const float *acc, float *out,
   p.M = m;
   p.N = n;
   p.K = (int)k;
-  p.m_tiles = (int)(g.rows_pad / proj::kBM);
+  p.m_pairs = (int)(g.rows_pad / proj::kPairM);
   p.n_tiles = (int)ceil_div(2 * n, proj::kBN);
   p.k_blocks = (int)(g.k_pad / proj::kBK);
-  p.num_tiles = (long long)p.m_tiles * p.n_tiles;
+  p.num_tiles = (long long)p.m_pairs * p.n_tiles;
   p.a_rows_pad = (int)g.rows_pad;
-  const long long grid = p.num_tiles < sms ? p.num_tiles : sms;
+  const long long grid = 2 * (p.num_tiles < pairs ? p.num_tiles : pairs);  // whole CTA pairs
   proj::proj_kernel<<<(unsigned)grid, proj::kThreads, proj::kSmemBytes, st>>>(tmA, tmX, p);
   return launch_status();
 }
@@ -1174,20 +1193,20 @@ int rqf_projection(const float *w, const float *x, const float *acc, float *out,
 namespace {
 
 struct WgGeometry {
-  int m_tiles, i_tiles, splits;
+  int m_pairs, i_tiles, splits;
   int64_t kblocks;
 };
 
-inline WgGeometry wgrad_geometry(int64_t m, int64_t k, int64_t n, int sms) {
+inline WgGeometry wgrad_geometry(int64_t m, int64_t k, int64_t n, int pairs) {
   WgGeometry g;
-  g.m_tiles = (int)ceil_div(m, proj::kWgRows);
-  g.i_tiles = (int)ceil_div(k, proj::kWgRows);
+  g.m_pairs = (int)ceil_div(m, proj::kWgPairRows);
+  g.i_tiles = (int)ceil_div(k, proj::kWgCols);
   g.kblocks = ceil_div(2 * n, proj::kBK);
-  const int64_t tiles = (int64_t)g.m_tiles * g.i_tiles;
-  // whole waves of CTAs (one per SM), enough of them that no CTA runs more
-  // than ~256 k-blocks: CTAs sharing an operand block then stay close enough
-  // in progress for the block's second read to hit L2
-  int64_t per_wave = sms > 0 ? sms / tiles : 1;
+  const int64_t tiles = (int64_t)g.m_pairs * g.i_tiles;
+  // whole waves of CTA pairs (one CTA per SM), enough of them that no pair
+  // runs more than ~256 k-blocks: pairs sharing an operand block then stay
+  // close enough in progress for the block's second read to hit L2
+  int64_t per_wave = pairs > 0 ? pairs / tiles : 1;
   if (per_wave < 1) per_wave = 1;
   int64_t waves = ceil_div(g.kblocks, per_wave * 256);
   if (waves > 16) waves = 16;
@@ -1198,11 +1217,9 @@ inline WgGeometry wgrad_geometry(int64_t m, int64_t k, int64_t n, int sms) {
   return g;
 }
 
-int device_sms() {
-  int dev = 0, sms = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
-  return sms;
+int wgrad_pairs_per_device() {
+  return pair_capacity<1>(reinterpret_cast<const void *>(proj::proj_wgrad_kernel),
+                          proj::kWgThreads, proj::kWgSmemBytes);
 }
 
 }  // namespace
@@ -1211,9 +1228,9 @@ extern "C" {
 
 size_t rqf_projection_weight_grad_workspace_bytes(int64_t m, int64_t k, int64_t n) {
   if (m <= 0 || k <= 0 || n <= 0) return 0;
-  const WgGeometry g = wgrad_geometry(m, k, n, device_sms());
-  return (size_t)g.splits * (size_t)g.m_tiles * proj::kWgRows * (size_t)g.i_tiles *
-         proj::kWgRows * sizeof(float2);
+  const WgGeometry g = wgrad_geometry(m, k, n, wgrad_pairs_per_device());
+  return (size_t)g.splits * (size_t)g.m_pairs * proj::kWgPairRows * (size_t)g.i_tiles *
+         proj::kWgCols * sizeof(float2);
 }
 
 int rqf_projection_weight_grad(const float *gz, const float *x, float *gw, int64_t m, int64_t k,
@@ -1231,38 +1248,25 @@ int rqf_projection_weight_grad(const float *gz, const float *x, float *gw, int64
   if ((n & 1) != 0 || n >= (int64_t(1) << 30) || m > 0x7fffffffLL || k > 0x7fffffffLL)
     return RQF_ERR_SHAPE;
   if (!aligned(gz, 16) || !aligned(x, 16) || !aligned(workspace, 16)) return RQF_ERR_ALIGN;
-  const int sms = device_sms();
-  if (sms <= 0) return RQF_ERR_LAUNCH;
-  const WgGeometry g = wgrad_geometry(m, k, n, sms);
-  {
-    static std::mutex mu;
-    static bool configured[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    std::lock_guard<std::mutex> lock(mu);
-    if (dev < 64 && !configured[dev]) {
-      if (cudaFuncSetAttribute(proj::proj_wgrad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               proj::kWgSmemBytes) != cudaSuccess)
-        return RQF_ERR_LAUNCH;
-      configured[dev] = true;
-    }
-  }
+  const int pairs = wgrad_pairs_per_device();
+  if (pairs <= 0) return RQF_ERR_LAUNCH;
+  const WgGeometry g = wgrad_geometry(m, k, n, pairs);
   CUtensorMap tmG, tmH;
   if (!encode_map_2d(&tmG, gz, (uint64_t)(2 * n), (uint64_t)m, (uint64_t)(2 * n) * sizeof(float),
                      proj::kBK, proj::kWgRows, CU_TENSOR_MAP_SWIZZLE_64B) ||
       !encode_map_2d(&tmH, x, (uint64_t)(2 * n), (uint64_t)k, (uint64_t)(2 * n) * sizeof(float),
-                     proj::kBK, proj::kWgRows, CU_TENSOR_MAP_SWIZZLE_64B))
+                     proj::kBK, proj::kWgHRows, CU_TENSOR_MAP_SWIZZLE_64B))
     return RQF_ERR_LAUNCH;
   proj::WgParams p;
   p.partials = static_cast<float2 *>(workspace);
   p.M = m;
   p.K = k;
-  p.m_tiles = g.m_tiles;
+  p.m_pairs = g.m_pairs;
   p.i_tiles = g.i_tiles;
   p.splits = g.splits;
   p.kblocks = g.kblocks;
-  p.ld = g.i_tiles * proj::kWgRows;
-  const int64_t grid = (int64_t)g.m_tiles * g.i_tiles * g.splits;
+  p.ld = g.i_tiles * proj::kWgCols;
+  const int64_t grid = 2 * (int64_t)g.m_pairs * g.i_tiles * g.splits;  // whole CTA pairs
   proj::proj_wgrad_kernel<<<(unsigned)grid, proj::kWgThreads, proj::kWgSmemBytes, st>>>(tmG, tmH,
                                                                                     p);
   if (cudaGetLastError() != cudaSuccess) return RQF_ERR_LAUNCH;
@@ -1270,7 +1274,7 @@ int rqf_projection_weight_grad(const float *gz, const float *x, float *gw, int64
   const int64_t blocks = ceil_div(total, 256);
   proj::proj_wgrad_reduce_kernel<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, st>>>(
       p.partials, reinterpret_cast<float2 *>(gw), m, k, g.splits,
-      (long long)g.m_tiles * proj::kWgRows, p.ld);
+      (long long)g.m_pairs * proj::kWgPairRows, p.ld);
   return launch_status();
 }
 
