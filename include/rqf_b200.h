@@ -359,6 +359,35 @@ size_t rqf_projection_weight_grad_workspace_bytes(int64_t m, int64_t k, int64_t 
 int rqf_projection_weight_grad(const float *gz, const float *x, float *gw, int64_t m, int64_t k,
                                int64_t n, void *workspace, rqf_stream_t stream);
 
+/* First block over a low-rank input projection (pure.py:_forward_fbt_stack
+ * :522-534: proj = w_in @ x_cf (+ b_in), h = proj.to(complex64), then the
+ * first block's z = W @ h).  With I = input_dims <= 4:
+ *
+ *   z[f, n] = sum_i u[f, i] x[i, n] + beta[f]        complex64, (F, N)
+ *   h[f, n] = sum_i w_in[f, i] x[i, n] + b_in[f]     complex64, imaginary 0
+ *
+ * u = W w_in (F x I complex), beta = W b_in (F complex); x (I x N) real with
+ * N contiguous and even.  beta, b_in and h may be null (h null: z only).
+ * One HBM-bound pass replaces the F x F projection GEMM of the first block.
+ * z and h 16-byte aligned, x 8-byte aligned. */
+int rqf_lowrank_drive(const float *u, const float *beta, const float *w_in, const float *b_in,
+                      const float *x, float *z, float *h, int64_t f, int64_t n, int i,
+                      rqf_stream_t stream);
+
+/* Row dots of a complex (F x N) matrix against I <= 4 real rows, for the
+ * first block's cotangents (gW = (gz x^T) w_in^T, grad w_in = Re(W^H (gz x^T)
+ * + g x^T), and the bias terms from the row sums):
+ *
+ *   out[f, j] = sum_n a[f, n] x[j, n]   (j < I);   out[f, I] = sum_n a[f, n]  (with_sum)
+ *
+ * out complex (F x (I + with_sum)).  Fixed-order reduction (per-chunk partials
+ * in double, summed in chunk order): deterministic.  `workspace` needs
+ * rqf_rowdot_workspace_bytes(f, n, i, with_sum) bytes.  a 16-byte aligned, x
+ * 8-byte aligned, N even, F <= 65535. */
+size_t rqf_rowdot_workspace_bytes(int64_t f, int64_t n, int i, int with_sum);
+int rqf_rowdot(const float *a, const float *x, float *out, void *workspace, int64_t f, int64_t n,
+               int i, int with_sum, rqf_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -15,6 +15,7 @@
 #include "btf_stream.cuh"
 #include "fbt_rows.cuh"
 #include "fbt_scan.cuh"
+#include "lowrank.cuh"
 #include "reduce.cuh"
 #include "projection.cuh"
 #include "selective.cuh"
@@ -1275,6 +1276,65 @@ int rqf_projection_weight_grad(const float *gz, const float *x, float *gw, int64
   proj::proj_wgrad_reduce_kernel<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, st>>>(
       p.partials, reinterpret_cast<float2 *>(gw), m, k, g.splits,
       (long long)g.m_pairs * proj::kWgPairRows, p.ld);
+  return launch_status();
+}
+
+}  // extern "C"
+
+// ------------------------------------------------ low-rank first block
+extern "C" {
+
+int rqf_lowrank_drive(const float *u, const float *beta, const float *w_in, const float *b_in,
+                      const float *x, float *z, float *h, int64_t f, int64_t n, int i,
+                      rqf_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (f < 0 || n < 0 || i < 0 || i > lowrank::kMaxRank) return RQF_ERR_SHAPE;
+  if (f == 0 || n == 0) return RQF_OK;
+  if ((n & 1) != 0) return RQF_ERR_SHAPE;
+  if (z == nullptr || (i > 0 && (u == nullptr || x == nullptr)) ||
+      (h != nullptr && i > 0 && w_in == nullptr))
+    return RQF_ERR_ARGUMENT;
+  if (!aligned(z, 16) || (h != nullptr && !aligned(h, 16)) || (x != nullptr && !aligned(x, 8)))
+    return RQF_ERR_ALIGN;
+  const int64_t total = f * (n / 2);
+  const int64_t blocks = ceil_div(total, 256);
+  lowrank::lowrank_drive_kernel<<<(unsigned)(blocks < 8192 ? blocks : 8192), 256, 0, st>>>(
+      reinterpret_cast<const float2 *>(u), reinterpret_cast<const float2 *>(beta), w_in, b_in, x,
+      reinterpret_cast<float2 *>(z), reinterpret_cast<float2 *>(h), f, n, i);
+  return launch_status();
+}
+
+size_t rqf_rowdot_workspace_bytes(int64_t f, int64_t n, int i, int with_sum) {
+  if (f <= 0 || n <= 0 || i < 0) return 0;
+  const int64_t chunks = ceil_div(n, lowrank::kRowdotChunk);
+  return (size_t)(f * chunks * (i + (with_sum ? 1 : 0))) * sizeof(double2);
+}
+
+int rqf_rowdot(const float *a, const float *x, float *out, void *workspace, int64_t f, int64_t n,
+               int i, int with_sum, rqf_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int J = i + (with_sum ? 1 : 0);
+  if (f < 0 || n < 0 || i < 0 || i > lowrank::kMaxRank || f > 65535) return RQF_ERR_SHAPE;
+  if (f == 0 || J == 0) return RQF_OK;
+  if (out == nullptr) return RQF_ERR_ARGUMENT;
+  if (n == 0)
+    return cudaMemsetAsync(out, 0, (size_t)(f * J) * sizeof(float2), st) == cudaSuccess
+               ? RQF_OK
+               : RQF_ERR_LAUNCH;
+  if ((n & 1) != 0) return RQF_ERR_SHAPE;
+  if (a == nullptr || workspace == nullptr || (i > 0 && x == nullptr)) return RQF_ERR_ARGUMENT;
+  if (!aligned(a, 16) || !aligned(workspace, 16) || (x != nullptr && !aligned(x, 8)))
+    return RQF_ERR_ALIGN;
+  const int64_t chunks = ceil_div(n, lowrank::kRowdotChunk);
+  if (chunks > 0x7fffffffLL) return RQF_ERR_SHAPE;
+  double2 *partials = static_cast<double2 *>(workspace);
+  lowrank::rowdot_partial_kernel<<<dim3((unsigned)chunks, (unsigned)f), lowrank::kRowdotThreads, 0,
+                                   st>>>(reinterpret_cast<const float2 *>(a), x, partials, n, i,
+                                         with_sum ? 1 : 0, (int)chunks);
+  if (cudaGetLastError() != cudaSuccess) return RQF_ERR_LAUNCH;
+  const int64_t outs = f * J;
+  lowrank::rowdot_finish_kernel<<<(unsigned)ceil_div(outs, 256), 256, 0, st>>>(
+      partials, reinterpret_cast<float2 *>(out), f, J, (int)chunks);
   return launch_status();
 }
 

@@ -58,6 +58,8 @@ def _project(W, h, conj_transpose=False, acc=None):
     if acc is None:
         return (opw @ h.reshape(d, B * T)).reshape(-1, B, T)
     return torch.addmm(acc.reshape(-1, B * T), opw, h.reshape(d, B * T)).reshape(-1, B, T)
+# Inputs of at most this many channels take the low-rank first block (_InputBlock).
+LOWRANK_MAX_INPUTS = 4
 NOMINAL_FILTER_GAIN = 0.5  # utils/init.py NOMINAL_FILTER_GAIN
 
 
@@ -169,6 +171,53 @@ class _PureBlock(torch.autograd.Function):
         return gh, gW, gc1, gt0, gt1, None, None
 
 
+class _InputBlock(torch.autograd.Function):
+    """The input projection and the first full-BPTT block together
+    (pure.py:_forward_fbt_stack :522-534 and the block's _forward_fbt
+    :212-243).  h0 = w_in x (+ b_in) has rank <= I = input_dims, so the
+    block's projection z0 = W h0 = (W w_in) x (+ W b_in) needs no F x F GEMM
+    (rqf_lowrank_drive writes z0 and h0 in one pass), and neither do its
+    cotangents, with G = gz0 [x; 1]^T (rqf_rowdot, one pass over gz0):
+      gW = gz0 h0^H = G [w_in, b_in]^T                      (h0 is real)
+      grad [w_in, b_in] = Re(g_h0 [x; 1]^T),  g_h0 = W^H gz0 + g (skip),
+    i.e. Re(W^H G + g [x; 1]^T), the second term one pass over g.  x itself
+    gets no gradient (the encoder routes inputs that need one through the
+    general blocks)."""
+
+    @staticmethod
+    def forward(ctx, x_cf, w_in, b_in, W, C1, tap0, tap1, fuse_act, skip, B, T):
+        F = W.shape[0]
+        beta = W @ b_in.to(torch.complex64) if b_in is not None else None
+        z, h0 = ops.lowrank_drive(W @ w_in.to(torch.complex64), x_cf, beta,
+                                  w_in if skip else None, b_in)
+        z = z.view(F, B, T)
+        out, saved = ops._fbt_forward(C1, tap0, tap1, z, bool(fuse_act),
+                                      h0.view(F, B, T) if skip else None)
+        ctx.save_for_backward(x_cf, w_in, b_in, W, *saved)
+        ctx.fuse_act, ctx.skip = bool(fuse_act), bool(skip)
+        return out
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, g):
+        x_cf, w_in, b_in, W, *saved = ctx.saved_tensors
+        gc1, gt0, gt1, gz = ops._fbt_backward(saved, g, ctx.fuse_act)
+        need = ctx.needs_input_grad
+        I, has_b = w_in.shape[1], b_in is not None
+        G = ops.rowdot(gz, x_cf, with_sum=has_b)  # (F, I + has_b)
+        gW = gw_in = gb_in = None
+        if need[3]:
+            rows = torch.cat([w_in, b_in[:, None]], dim=1) if has_b else w_in
+            gW = G @ rows.t().to(torch.complex64)
+        if need[1] or need[2]:
+            gh = W.mH @ G
+            if ctx.skip:
+                gh = gh + ops.rowdot(g, x_cf, with_sum=has_b)
+            gw_in = gh[:, :I].real.contiguous() if need[1] else None
+            gb_in = gh[:, I].real.contiguous() if (has_b and need[2]) else None
+        return None, gw_in, gb_in, gW, gc1, gt0, gt1, None, None, None, None
+
+
 class PureRQFEncoderB200(nn.Module):
     """Pure RQF encoder in (F,B,T) layout on the B200 scan kernels.
 
@@ -204,10 +253,20 @@ class PureRQFEncoderB200(nn.Module):
         B, T, I = x.shape
         x_cf = x.permute(2, 0, 1).reshape(I, B * T)
         w_in, b_in = self.input_proj.weight, self.input_proj.bias
-        proj = w_in @ x_cf if b_in is None else torch.addmm(b_in[:, None], w_in, x_cf)
-        h = proj.reshape(-1, B, T).to(torch.complex64)
         n = len(self.W)
-        for i in range(n):
+        first = 0
+        if (PROJECTION == "tc" and x.is_cuda and self.scan_grad_mode == "full" and n > 0
+                and I <= LOWRANK_MAX_INPUTS and (B * T) % 2 == 0 and not x.requires_grad):
+            c1, t0, t1 = self.rqf[0].two_tap()
+            W = self.W[0]
+            h = _InputBlock.apply(x_cf, w_in, b_in, W, c1, t0, t1,
+                                  self.final_activation or n > 1,
+                                  self.skip and W.shape[0] == W.shape[1], B, T)
+            first = 1
+        else:
+            proj = w_in @ x_cf if b_in is None else torch.addmm(b_in[:, None], w_in, x_cf)
+            h = proj.reshape(-1, B, T).to(torch.complex64)
+        for i in range(first, n):
             act = self.final_activation or i + 1 < n
             c1, t0, t1 = self.rqf[i].two_tap()
             W = self.W[i]

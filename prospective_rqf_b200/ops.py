@@ -856,3 +856,56 @@ def projection_weight_grad(gz: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
             _abi.stream_of(g)), "rqf_projection_weight_grad")
     _done(dev)
     return gw
+
+
+# ------------------------------------------------ low-rank first block
+def lowrank_drive(u: torch.Tensor, x: torch.Tensor, beta: torch.Tensor | None = None,
+                  w_in: torch.Tensor | None = None, b_in: torch.Tensor | None = None):
+    """The first block's drive over a low-rank input projection
+    (pure.py:_forward_fbt_stack :522-534): z = u @ x (+ beta[:, None]) as
+    complex64 (F, N), and, when w_in is given, h = (w_in @ x (+ b_in)) as
+    complex64 with zero imaginary part, in one pass (rqf_lowrank_drive).
+    u (F, I) complex, x (I, N) real with I <= 4 and N even."""
+    dev = _require_cuda(u, x)
+    uu = _c64(u)
+    xx = x.detach().to(torch.float32).contiguous()
+    F, I = int(uu.shape[0]), int(uu.shape[1])
+    N = int(xx.shape[1])
+    if xx.shape[0] != I:
+        raise ValueError(f"u {tuple(uu.shape)} and x {tuple(xx.shape)} disagree on the rank")
+    bb = _c64(beta) if beta is not None else None
+    ww = w_in.detach().to(torch.float32).contiguous() if w_in is not None else None
+    bi = b_in.detach().to(torch.float32).contiguous() if (w_in is not None and b_in is not None) else None
+    z = torch.empty((F, N), dtype=torch.complex64, device=dev)
+    h = torch.empty((F, N), dtype=torch.complex64, device=dev) if ww is not None else None
+    lib = _abi.load()
+    with _timing.launch("rqf_lowrank_drive", F * N, _nbytes(xx, z) + (h.numel() * 8 if h is not None else 0)):
+        _abi.check(lib.rqf_lowrank_drive(
+            _abi.ptr(uu), _abi.ptr(bb), _abi.ptr(ww), _abi.ptr(bi), _abi.ptr(xx), _abi.ptr(z),
+            _abi.ptr(h), F, N, I, _abi.stream_of(z)), "rqf_lowrank_drive")
+    _done(dev)
+    return z, h
+
+
+def rowdot(a: torch.Tensor, x: torch.Tensor | None, with_sum: bool = False) -> torch.Tensor:
+    """out[:, j] = a @ x[j] for the real rows of x (I <= 4), then the row sums
+    of a when with_sum: complex64 (F, I + with_sum), over the flattened
+    trailing dims of a complex (F, ...).  Fixed-order reduction (rqf_rowdot)."""
+    dev = _require_cuda(a)
+    aa = _c64(a)
+    F = int(aa.shape[0])
+    N = aa.numel() // F if F else 0
+    xx = x.detach().to(torch.float32).contiguous() if x is not None else None
+    I = int(xx.shape[0]) if xx is not None else 0
+    if xx is not None and xx.numel() != I * N:
+        raise ValueError(f"x {tuple(xx.shape)} does not match {N} samples")
+    J = I + int(bool(with_sum))
+    out = torch.empty((F, J), dtype=torch.complex64, device=dev)
+    lib = _abi.load()
+    ws = _scratch(lib.rqf_rowdot_workspace_bytes(F, N, I, int(bool(with_sum))), dev)
+    with _timing.launch("rqf_rowdot", F * N, _nbytes(aa) + (_nbytes(xx) if xx is not None else 0)):
+        _abi.check(lib.rqf_rowdot(
+            _abi.ptr(aa), _abi.ptr(xx), _abi.ptr(out), _abi.ptr(ws), F, N, I, int(bool(with_sum)),
+            _abi.stream_of(aa)), "rqf_rowdot")
+    _done(dev)
+    return out

@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 import torch
 
-from _util import FWD_TOL, GRAD_TOL, assert_close
+from _util import FWD_TOL, GRAD_TOL, assert_close, rel_err
 from oracle import oracle
 
 pytestmark = pytest.mark.gpu
@@ -86,8 +86,10 @@ def _two_tap(log_theta, log_gamma, dt, tau):
 def reference_forward(model, x, params):
     enc = model.encoder
     B, T, I = x.shape
-    h = (params["input_proj.weight"] @ x.permute(2, 0, 1).reshape(I, B * T)).reshape(-1, B, T)
-    h = h.to(torch.complex128)
+    h = params["input_proj.weight"] @ x.permute(2, 0, 1).reshape(I, B * T)
+    if "input_proj.bias" in params:
+        h = h + params["input_proj.bias"][:, None]
+    h = h.reshape(-1, B, T).to(torch.complex128)
     n = len(enc.W)
     for i in range(n):
         r = enc.rqf[i]
@@ -149,6 +151,92 @@ def test_encoder_matches_fp64_restatement(mode, T):
         assert ref is not None, k
         assert_close(p.grad.cpu().numpy().astype(np.complex128 if p.is_complex() else np.float64),
                      ref.numpy(), GRAD_TOL, f"grad {k}")
+
+
+def _lowrank_case(I, bias, skip, T, lowrank):
+    """Logits and every parameter gradient of a small encoder + readout, and
+    the fp64 restatement's, with the first block on the low-rank path or on
+    the general F x F GEMM path."""
+    from prospective_rqf_b200 import encoder as E
+
+    E.LOWRANK_MAX_INPUTS = 4 if lowrank else 0
+    torch.manual_seed(0)
+    enc = E.PureRQFEncoderB200(input_dims=I, hidden_dims=16, num_layers=3, skip_connection=skip,
+                               input_proj_bias=bias, seed=4)
+    model = E.RQFClassifier(enc, 5, 32).cuda()
+    with torch.no_grad():
+        for r in model.encoder.rqf:
+            r.log_gamma.copy_(torch.linspace(math.log(1e-3), math.log(0.9), 16))
+    g = torch.Generator().manual_seed(6)
+    B = 4
+    x = (0.5 * torch.randn(B, T, I, generator=g)).clamp(-1, 1)
+    y = torch.randint(0, 5, (B,), generator=g)
+    logits = model(x.cuda())
+    torch.nn.functional.cross_entropy(logits, y.cuda()).backward()
+    names = {n.replace("encoder.", "").replace("readout.", ""): p
+             for n, p in model.named_parameters()}
+    params = {k: (p.detach().cpu().to(torch.complex128 if p.is_complex() else torch.float64)
+                  .requires_grad_(True)) for k, p in names.items()}
+    logits_ref = reference_forward(model, x.double(), params)
+    torch.nn.functional.cross_entropy(logits_ref, y).backward()
+    got = {"logits": logits.detach().cpu().double().numpy()}
+    ref = {"logits": logits_ref.detach().numpy()}
+    for k, p in names.items():
+        got[k] = p.grad.cpu().numpy().astype(np.complex128 if p.is_complex() else np.float64)
+        ref[k] = params[k].grad.numpy()
+    return got, ref
+
+
+@pytest.mark.parametrize("I,bias,skip,T", [(1, False, True, 3000), (1, True, True, 1000),
+                                          (3, True, False, 1000), (2, False, True, 2001)])
+def test_encoder_lowrank_first_block_matches_fp64(I, bias, skip, T, monkeypatch):
+    """The first block over the low-rank input projection (_InputBlock:
+    rqf_lowrank_drive forward, rqf_rowdot cotangents) against the fp64
+    restatement, which runs the F x F projection on h0 = w_in x + b_in.
+    Each quantity is within tolerance of fp64 or no worse than the general
+    path (F x F GEMMs) on the same inputs: some of these small configurations
+    put a late layer's log_theta gradient near 1e-3 from fp64 in fp32 on
+    either path."""
+    from prospective_rqf_b200 import encoder as E
+    from prospective_rqf_b200 import ops
+
+    calls = []
+    real_drive = ops.lowrank_drive
+    monkeypatch.setattr(ops, "lowrank_drive", lambda *a, **k: calls.append(1) or real_drive(*a, **k))
+    monkeypatch.setattr(E, "LOWRANK_MAX_INPUTS", E.LOWRANK_MAX_INPUTS)
+    gen, ref = _lowrank_case(I, bias, skip, T, lowrank=False)
+    assert not calls
+    low, ref2 = _lowrank_case(I, bias, skip, T, lowrank=True)
+    assert calls, "the low-rank first block did not run"
+    for k in ref:
+        e_low, e_gen = rel_err(low[k], ref2[k]), rel_err(gen[k], ref[k])
+        tol = FWD_TOL if k == "logits" else GRAD_TOL
+        assert e_low <= max(tol, 1.05 * e_gen), f"{k}: {e_low:.3e} vs fp64 (general path {e_gen:.3e})"
+
+
+def test_rowdot_and_lowrank_drive_vs_fp64():
+    from prospective_rqf_b200 import ops
+
+    g = torch.Generator().manual_seed(2)
+    F, N, I = 37, 2 * 20011, 3
+    a = _crandn(g, F, N)
+    x = torch.randn(I, N, generator=g)
+    out = ops.rowdot(a.cuda(), x.cuda(), with_sum=True).cpu().numpy()
+    a64, x64 = a.numpy().astype(np.complex128), x.numpy().astype(np.float64)
+    ref = np.concatenate([a64 @ x64.T, a64.sum(1, keepdims=True)], axis=1)
+    assert_close(out.astype(np.complex128), ref, 1e-5, "rowdot")
+    assert torch.equal(ops.rowdot(a.cuda(), x.cuda(), True).cpu(), torch.from_numpy(out))
+    u, beta = _crandn(g, F, I), _crandn(g, F)
+    w, b = torch.randn(F, I, generator=g), torch.randn(F, generator=g)
+    z, h = ops.lowrank_drive(u.cuda(), x.cuda(), beta.cuda(), w.cuda(), b.cuda())
+    zr = u.numpy().astype(np.complex128) @ x64 + beta.numpy()[:, None]
+    hr = w.numpy().astype(np.float64) @ x64 + b.numpy()[:, None]
+    assert_close(z.cpu().numpy().astype(np.complex128), zr, 1e-6, "drive z")
+    assert_close(h.cpu().numpy().astype(np.complex128), hr.astype(np.complex128), 1e-6, "drive h")
+    z2, h2 = ops.lowrank_drive(u.cuda(), x.cuda())
+    assert h2 is None
+    assert_close(z2.cpu().numpy().astype(np.complex128), u.numpy().astype(np.complex128) @ x64,
+                 1e-6, "drive z, no bias")
 
 
 # ------------------------------------------- fused skip (rqf_fbt_block_forward)
