@@ -388,6 +388,23 @@ size_t rqf_rowdot_workspace_bytes(int64_t f, int64_t n, int i, int with_sum);
 int rqf_rowdot(const float *a, const float *x, float *out, void *workspace, int64_t f, int64_t n,
                int i, int with_sum, rqf_stream_t stream);
 
+/* Hidden layer of the mean-pooled readout (train.py:ComplexReadoutClassifier
+ * :74-136, Linear -> ReLU per step, logits mean-pooled over time), given the
+ * complex projection z (H x B x T, T contiguous) of the encoder state:
+ *
+ *   pooled[h, b] = (1/T) sum_t relu(Re z[h, b, t] + bias[h])      float32 (H x B)
+ *   mask[(h B + b) W + t/32] bit t%32 = (Re z + bias > 0),  W = ceil(T/32)
+ *
+ * bias may be null.  One pass over z; fixed-order reduction. */
+int rqf_readout_relu_pool(const float *z, const float *bias, uint32_t *mask, float *pooled,
+                          int64_t h, int64_t batch, int64_t time, rqf_stream_t stream);
+/* Its backward: gc[h, b, t] = (mask ? scale[h, b] : 0) + 0i (complex64, the
+ * input of the projection GEMMs' cotangents; scale = gpool / T) and
+ * counts[h, b] = number of set mask bits (float32; may be null). */
+int rqf_readout_relu_pool_backward(const uint32_t *mask, const float *scale, float *gc,
+                                   float *counts, int64_t h, int64_t batch, int64_t time,
+                                   rqf_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -894,21 +894,37 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
   }
 }
 
-// gW[j, i] = sum over splits of the partial tiles, in split order.
-__global__ void proj_wgrad_reduce_kernel(const float2 *__restrict__ partials,
-                                         float2 *__restrict__ gw, long long M, long long K,
-                                         int splits, long long rows_pad, int ld) {
-  const long long total = M * K;
-  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
-       e += (long long)gridDim.x * blockDim.x) {
-    const long long j = e / K, i = e - j * K;
-    double re = 0.0, im = 0.0;
-    for (int s = 0; s < splits; ++s) {
+// gW[j, i] = sum over splits of the partial tiles, in a fixed order: a CTA
+// owns 32 consecutive outputs; warp g sums the splits s = g, g + 8, ... in
+// ascending order (lane = output, so each load is one coalesced 256-byte
+// row piece), then the 8 group sums are added in group order, in double.
+constexpr int kWgReduceGroups = 8;
+__global__ void __launch_bounds__(32 * kWgReduceGroups)
+proj_wgrad_reduce_kernel(const float2 *__restrict__ partials, float2 *__restrict__ gw, long long M,
+                         long long K, int splits, long long rows_pad, int ld) {
+  const int lane = threadIdx.x & 31, grp = threadIdx.x >> 5;
+  const long long e = blockIdx.x * 32LL + lane;
+  const bool valid = e < M * K;
+  const long long j = valid ? e / K : 0, i = valid ? e - j * K : 0;
+  double re = 0.0, im = 0.0;
+  if (valid) {
+    for (int s = grp; s < splits; s += kWgReduceGroups) {
       const float2 v = partials[((long long)s * rows_pad + j) * ld + i];
       re += v.x;
       im += v.y;
     }
-    gw[e] = make_float2((float)re, (float)im);
+  }
+  __shared__ double2 part[kWgReduceGroups][32];
+  part[grp][lane] = make_double2(re, im);
+  __syncthreads();
+  if (grp == 0 && valid) {
+    double sr = 0.0, si = 0.0;
+#pragma unroll
+    for (int g = 0; g < kWgReduceGroups; ++g) {
+      sr += part[g][lane].x;
+      si += part[g][lane].y;
+    }
+    gw[e] = make_float2((float)sr, (float)si);
   }
 }
 

@@ -1,0 +1,86 @@
+// Hidden layer of the mean-pooled per-timestep readout
+// (train.py:ComplexReadoutClassifier :74-136: Linear(2F, H) -> ReLU ->
+// Linear(H, C) per step, logits mean-pooled over time).  With the output
+// layer applied after pooling, the hidden layer only has to deliver
+//
+//   pooled[h, b] = (1/T) sum_t relu(Re z[h, b, t] + bias[h])
+//
+// where z = V h_enc is the complex projection of the encoder state, and its
+// backward only needs the ReLU mask:
+//
+//   g[h, b, t] = mask[h, b, t] * gpool[h, b] / T
+//
+// Both kernels work one (h, b) row of T samples per CTA, one 32-sample word of
+// the bit mask per warp iteration (bit t % 32 of word t / 32), and reduce in a
+// fixed order (deterministic).  Both are HBM-bound: the forward reads z once
+// (8 bytes per sample) and writes 1 bit; the backward reads the bit and writes
+// the complex cotangent (8 bytes) that the projection GEMMs take as input.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rqf {
+namespace readout {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+
+__global__ void __launch_bounds__(kThreads)
+relu_pool_kernel(const float2 *__restrict__ z, const float *__restrict__ bias,
+                 uint32_t *__restrict__ mask, float *__restrict__ pooled, int batch,
+                 long long T, long long words) {
+  const long long row = blockIdx.x;  // h * batch + b
+  const float bh = bias ? bias[row / batch] : 0.f;
+  const float2 *zr = z + row * T;
+  uint32_t *mr = mask + row * words;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float acc = 0.f;
+  for (long long w = warp; w < words; w += kWarps) {
+    const long long t = w * 32 + lane;
+    float v = 0.f;
+    if (t < T) v = zr[t].x + bh;
+    const bool on = v > 0.f;
+    const uint32_t bits = __ballot_sync(0xffffffffu, on);
+    if (lane == 0) mr[w] = bits;
+    if (on) acc += v;
+  }
+  __shared__ double red[kThreads];
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  for (int s = kThreads / 2; s > 0; s >>= 1) {
+    if (threadIdx.x < s) red[threadIdx.x] += red[threadIdx.x + s];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) pooled[row] = (float)(red[0] / (double)T);
+}
+
+// gc[row, t] = (mask ? scale[row] : 0, 0); counts[row] = number of set bits.
+__global__ void __launch_bounds__(kThreads)
+relu_pool_backward_kernel(const uint32_t *__restrict__ mask, const float *__restrict__ scale,
+                          float2 *__restrict__ gc, float *__restrict__ counts, long long T,
+                          long long words) {
+  const long long row = blockIdx.x;
+  const float s = scale[row];
+  const uint32_t *mr = mask + row * words;
+  float2 *gr = gc + row * T;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int cnt = 0;
+  for (long long w = warp; w < words; w += kWarps) {
+    const uint32_t bits = mr[w];
+    const long long t = w * 32 + lane;
+    if (t < T) gr[t] = make_float2(((bits >> lane) & 1u) ? s : 0.f, 0.f);
+    if (lane == 0) cnt += __popc(bits);
+  }
+  __shared__ int red[kThreads];
+  red[threadIdx.x] = cnt;
+  __syncthreads();
+  for (int k = kThreads / 2; k > 0; k >>= 1) {
+    if (threadIdx.x < k) red[threadIdx.x] += red[threadIdx.x + k];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0 && counts) counts[row] = (float)red[0];
+}
+
+}  // namespace readout
+}  // namespace rqf

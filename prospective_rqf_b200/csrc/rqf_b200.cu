@@ -16,6 +16,7 @@
 #include "fbt_rows.cuh"
 #include "fbt_scan.cuh"
 #include "lowrank.cuh"
+#include "readout.cuh"
 #include "reduce.cuh"
 #include "projection.cuh"
 #include "selective.cuh"
@@ -1272,8 +1273,9 @@ int rqf_projection_weight_grad(const float *gz, const float *x, float *gw, int64
                                                                                     p);
   if (cudaGetLastError() != cudaSuccess) return RQF_ERR_LAUNCH;
   const int64_t total = m * k;
-  const int64_t blocks = ceil_div(total, 256);
-  proj::proj_wgrad_reduce_kernel<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, st>>>(
+  const int64_t blocks = ceil_div(total, 32);
+  if (blocks > 0x7fffffffLL) return RQF_ERR_SHAPE;
+  proj::proj_wgrad_reduce_kernel<<<(unsigned)blocks, 32 * proj::kWgReduceGroups, 0, st>>>(
       p.partials, reinterpret_cast<float2 *>(gw), m, k, g.splits,
       (long long)g.m_pairs * proj::kWgPairRows, p.ld);
   return launch_status();
@@ -1335,6 +1337,42 @@ int rqf_rowdot(const float *a, const float *x, float *out, void *workspace, int6
   const int64_t outs = f * J;
   lowrank::rowdot_finish_kernel<<<(unsigned)ceil_div(outs, 256), 256, 0, st>>>(
       partials, reinterpret_cast<float2 *>(out), f, J, (int)chunks);
+  return launch_status();
+}
+
+}  // extern "C"
+
+// ------------------------------------------------ mean-pooled readout hidden layer
+extern "C" {
+
+int rqf_readout_relu_pool(const float *z, const float *bias, uint32_t *mask, float *pooled,
+                          int64_t h, int64_t batch, int64_t time, rqf_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (h < 0 || batch < 0 || time < 0) return RQF_ERR_SHAPE;
+  const int64_t rows = h * batch;
+  if (rows == 0) return RQF_OK;
+  if (rows > 0x7fffffffLL || batch > 0x7fffffffLL) return RQF_ERR_SHAPE;
+  if (time == 0) return RQF_ERR_SHAPE;  // the mean over no samples is undefined
+  if (z == nullptr || mask == nullptr || pooled == nullptr) return RQF_ERR_ARGUMENT;
+  if (!aligned(z, 8)) return RQF_ERR_ALIGN;
+  readout::relu_pool_kernel<<<(unsigned)rows, readout::kThreads, 0, st>>>(
+      reinterpret_cast<const float2 *>(z), bias, mask, pooled, (int)batch, time,
+      ceil_div(time, 32));
+  return launch_status();
+}
+
+int rqf_readout_relu_pool_backward(const uint32_t *mask, const float *scale, float *gc,
+                                   float *counts, int64_t h, int64_t batch, int64_t time,
+                                   rqf_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (h < 0 || batch < 0 || time < 0) return RQF_ERR_SHAPE;
+  const int64_t rows = h * batch;
+  if (rows == 0 || time == 0) return RQF_OK;
+  if (rows > 0x7fffffffLL) return RQF_ERR_SHAPE;
+  if (mask == nullptr || scale == nullptr || gc == nullptr) return RQF_ERR_ARGUMENT;
+  if (!aligned(gc, 8)) return RQF_ERR_ALIGN;
+  readout::relu_pool_backward_kernel<<<(unsigned)rows, readout::kThreads, 0, st>>>(
+      mask, scale, reinterpret_cast<float2 *>(gc), counts, time, ceil_div(time, 32));
   return launch_status();
 }
 

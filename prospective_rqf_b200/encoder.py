@@ -318,14 +318,50 @@ class _ReadoutHidden(torch.autograd.Function):
         return gh, gW1, gb1
 
 
+class _ReadoutPooled(torch.autograd.Function):
+    """pooled = mean_t relu(W1 [Re h; Im h] + b1), (H, B), for the mean-pooled
+    readout (train.py:ComplexReadoutClassifier :126-136): the projection
+    Re(V h) of _ReadoutHidden, then one pass (rqf_readout_relu_pool) that
+    keeps only the ReLU mask bits and the time-means.  Backward: the mask
+    turns gpool into g = mask * gpool / T (rqf_readout_relu_pool_backward),
+    which feeds the same two projection cotangents; gb1 = sum_b gpool / T *
+    (set bits of the (h, b) row)."""
+
+    @staticmethod
+    def forward(ctx, h, W1, b1):
+        F = h.shape[0]
+        V = torch.complex(W1[:, :F], -W1[:, F:]).contiguous()
+        pooled, mask = ops.readout_relu_pool(_project(V, h), b1)
+        ctx.save_for_backward(h, V, mask)
+        ctx.time = h.shape[2]
+        return pooled
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, gpool):
+        h, V, mask = ctx.saved_tensors
+        need = ctx.needs_input_grad
+        scale = gpool / ctx.time
+        gc, counts = ops.readout_relu_pool_backward(mask, scale, ctx.time)
+        gh = _project(V, gc, conj_transpose=True) if need[0] else None
+        gW1 = None
+        if need[1]:
+            P = _weight_grad(gc, h)
+            gW1 = torch.cat([P.real, -P.imag], dim=1)
+        gb1 = (scale * counts).sum(dim=1) if need[2] else None
+        return gh, gW1, gb1
+
+
 class ComplexReadout(nn.Module):
     """Per-timestep MLP on [Re h; Im h] with mean-pooled logits
     (train.py:ComplexReadoutClassifier, hidden_dims set).
 
-    On CUDA with the tensor-core projections (the default), the hidden layer
-    runs as _ReadoutHidden, and with mean pooling the output layer is applied
-    to the time-mean of the hidden activations: mean_t(W2 hid_t + b2) =
-    W2 mean_t(hid_t) + b2, the same logits without the per-step output GEMM."""
+    On CUDA with the tensor-core projections (the default), the output layer
+    is applied to the time-mean of the hidden activations with mean pooling:
+    mean_t(W2 hid_t + b2) = W2 mean_t(hid_t) + b2, the same logits without
+    the per-step output GEMM; the hidden layer then runs as _ReadoutPooled
+    (no per-step activations are kept, only the ReLU mask bits).  Per-step
+    logits run _ReadoutHidden."""
 
     def __init__(self, features: int, num_classes: int, hidden_dims: int = 256, seed: int = 1):
         super().__init__()
@@ -342,12 +378,13 @@ class ComplexReadout(nn.Module):
     def forward(self, h: torch.Tensor, per_step: bool = False) -> torch.Tensor:
         F, B, T = h.shape
         if PROJECTION == "tc" and h.is_cuda:
+            if not per_step:
+                pooled = _ReadoutPooled.apply(h, self.fc1.weight, self.fc1.bias)  # (H, B)
+                return torch.addmm(self.fc2.bias[:, None], self.fc2.weight, pooled).t()
             hid = _ReadoutHidden.apply(h, self.fc1.weight, self.fc1.bias)  # (H, B, T)
-            if per_step:
-                logits = torch.addmm(self.fc2.bias[:, None], self.fc2.weight,
-                                     hid.reshape(hid.shape[0], B * T))
-                return logits.reshape(-1, B, T).permute(1, 2, 0)  # (B, T, C)
-            return torch.addmm(self.fc2.bias[:, None], self.fc2.weight, hid.mean(dim=2)).t()
+            logits = torch.addmm(self.fc2.bias[:, None], self.fc2.weight,
+                                 hid.reshape(hid.shape[0], B * T))
+            return logits.reshape(-1, B, T).permute(1, 2, 0)  # (B, T, C)
         feats = torch.cat([h.real, h.imag], dim=0).reshape(2 * F, B * T)
         hid = torch.relu(torch.addmm(self.fc1.bias[:, None], self.fc1.weight, feats))
         logits = torch.addmm(self.fc2.bias[:, None], self.fc2.weight, hid)  # (C, B*T)

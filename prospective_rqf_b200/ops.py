@@ -909,3 +909,45 @@ def rowdot(a: torch.Tensor, x: torch.Tensor | None, with_sum: bool = False) -> t
             _abi.stream_of(aa)), "rqf_rowdot")
     _done(dev)
     return out
+
+
+# ------------------------------------------------ mean-pooled readout hidden layer
+def readout_relu_pool(z: torch.Tensor, bias: torch.Tensor | None):
+    """pooled = mean_t relu(Re z + bias[:, None, None]) as float32 (H, B), and
+    the ReLU mask as int32 words (H, B, ceil(T/32)), bit t % 32 of word t / 32,
+    from the complex (H, B, T) projection z in one pass (rqf_readout_relu_pool;
+    train.py:ComplexReadoutClassifier :74-136 with mean pooling)."""
+    dev = _require_cuda(z)
+    zz = _c64(z)
+    H, B, T = (int(d) for d in zz.shape)
+    words = (T + 31) // 32
+    mask = torch.empty((H, B, words), dtype=torch.int32, device=dev)
+    pooled = torch.empty((H, B), dtype=torch.float32, device=dev)
+    bb = bias.detach().to(torch.float32).contiguous() if bias is not None else None
+    lib = _abi.load()
+    with _timing.launch("rqf_readout_relu_pool", H * B * T, _nbytes(zz, mask)):
+        _abi.check(lib.rqf_readout_relu_pool(_abi.ptr(zz), _abi.ptr(bb), _abi.ptr(mask),
+                                             _abi.ptr(pooled), H, B, T, _abi.stream_of(zz)),
+                   "rqf_readout_relu_pool")
+    _done(dev)
+    return pooled, mask
+
+
+def readout_relu_pool_backward(mask: torch.Tensor, scale: torch.Tensor, time: int):
+    """gc = mask * scale[:, :, None] as complex64 (H, B, T) (zero imaginary
+    part) and the set-bit count per (h, b) row (rqf_readout_relu_pool_backward)."""
+    dev = _require_cuda(mask, scale)
+    mask = mask.contiguous()
+    H, B, words = (int(d) for d in mask.shape)
+    if words != (time + 31) // 32:
+        raise ValueError(f"mask of {words} words does not cover {time} steps")
+    ss = scale.detach().to(torch.float32).contiguous()
+    gc = torch.empty((H, B, time), dtype=torch.complex64, device=dev)
+    counts = torch.empty((H, B), dtype=torch.float32, device=dev)
+    lib = _abi.load()
+    with _timing.launch("rqf_readout_relu_pool_backward", H * B * time, _nbytes(mask, gc)):
+        _abi.check(lib.rqf_readout_relu_pool_backward(
+            _abi.ptr(mask), _abi.ptr(ss), _abi.ptr(gc), _abi.ptr(counts), H, B, time,
+            _abi.stream_of(gc)), "rqf_readout_relu_pool_backward")
+    _done(dev)
+    return gc, counts

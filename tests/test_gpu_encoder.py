@@ -214,6 +214,32 @@ def test_encoder_lowrank_first_block_matches_fp64(I, bias, skip, T, monkeypatch)
         assert e_low <= max(tol, 1.05 * e_gen), f"{k}: {e_low:.3e} vs fp64 (general path {e_gen:.3e})"
 
 
+@pytest.mark.parametrize("H,B,T", [(7, 3, 1000), (5, 2, 33), (4, 3, 1), (16, 4, 4096)])
+def test_readout_relu_pool_vs_torch(H, B, T):
+    """rqf_readout_relu_pool / _backward against torch fp64 on the same z:
+    the pooled ReLU means, the mask bits, the cotangent and the counts."""
+    from prospective_rqf_b200 import ops
+
+    g = torch.Generator().manual_seed(H * 100 + T)
+    z = _crandn(g, H, B, T)
+    bias = 0.3 * torch.randn(H, generator=g)
+    pooled, mask = ops.readout_relu_pool(z.cuda(), bias.cuda())
+    pre = z.real.double() + bias.double()[:, None, None]
+    ref = torch.relu(pre).mean(dim=2)
+    assert_close(pooled.cpu().double().numpy(), ref.numpy(), 1e-6, "pooled")
+    on = pre > 0
+    words = (T + 31) // 32
+    bits = torch.zeros(H, B, words * 32, dtype=torch.bool)
+    bits[:, :, :T] = on
+    want = (bits.reshape(H, B, words, 32).long() << torch.arange(32)).sum(-1)
+    got = mask.cpu().long() & 0xFFFFFFFF
+    assert torch.equal(got, want), "mask bits"
+    scale = torch.randn(H, B, generator=g)
+    gc, counts = ops.readout_relu_pool_backward(mask, scale.cuda(), T)
+    assert torch.equal(gc.cpu(), torch.complex(on.float() * scale[:, :, None], torch.zeros(H, B, T)))
+    assert torch.equal(counts.cpu(), on.sum(dim=2).float())
+
+
 def test_rowdot_and_lowrank_drive_vs_fp64():
     from prospective_rqf_b200 import ops
 
