@@ -180,7 +180,10 @@ class _InputBlock(torch.autograd.Function):
     cotangents, with G = gz0 [x; 1]^T (rqf_rowdot, one pass over gz0):
       gW = gz0 h0^H = G [w_in, b_in]^T                      (h0 is real)
       grad [w_in, b_in] = Re(g_h0 [x; 1]^T),  g_h0 = W^H gz0 + g (skip),
-    i.e. Re(W^H G + g [x; 1]^T), the second term one pass over g.  x itself
+    i.e. Re(W^H G + g [x; 1]^T), the second term one pass over g.  The
+    reference's _Layer0RealScan (fbt_scan_kernel.py:899-1032) takes the same
+    block's real input as a stacked real GEMM; the rank of h0 removes the
+    F x F GEMM altogether.  x itself
     gets no gradient (the encoder routes inputs that need one through the
     general blocks)."""
 
@@ -209,6 +212,48 @@ class _InputBlock(torch.autograd.Function):
         if need[3]:
             rows = torch.cat([w_in, b_in[:, None]], dim=1) if has_b else w_in
             gW = G @ rows.t().to(torch.complex64)
+        if need[1] or need[2]:
+            gh = W.mH @ G
+            if ctx.skip:
+                gh = gh + ops.rowdot(g, x_cf, with_sum=has_b)
+            gw_in = gh[:, :I].real.contiguous() if need[1] else None
+            gb_in = gh[:, I].real.contiguous() if (has_b and need[2]) else None
+        return None, gw_in, gb_in, gW, gc1, gt0, gt1, None, None, None, None
+
+
+class _InputTBPTT(torch.autograd.Function):
+    """The input projection and the first TBPTT(1) layer together, with the
+    skip add (the TBPTT counterpart of _InputBlock; pure.py:184-187 for the
+    lag tap).  z0 = (W w_in) x (+ W b_in) from rqf_lowrank_drive, the TBPTT(1)
+    scan, then out = y + h0.  With G = gz0 [x; 1]^T and Gw = gzw [x; 1]^T:
+      gW = (gz0 + gzw) h0^H = (G + Gw) [w_in, b_in]^T
+      grad [w_in, b_in] = Re(W^H G + g [x; 1]^T)   (the lag cotangent updates W only)."""
+
+    @staticmethod
+    def forward(ctx, x_cf, w_in, b_in, W, C1, tap0, tap1, fuse_act, skip, B, T):
+        F = W.shape[0]
+        beta = W @ b_in.to(torch.complex64) if b_in is not None else None
+        z, h0 = ops.lowrank_drive(W @ w_in.to(torch.complex64), x_cf, beta,
+                                  w_in if skip else None, b_in)
+        y, saved = ops._fbt_forward(C1, tap0, tap1, z.view(F, B, T), bool(fuse_act))
+        ctx.save_for_backward(x_cf, w_in, b_in, W, *saved)
+        ctx.fuse_act, ctx.skip = bool(fuse_act), bool(skip)
+        return y + h0.view(F, B, T) if skip else y
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, g):
+        x_cf, w_in, b_in, W, *saved = ctx.saved_tensors
+        z = saved[3]
+        gc1, gt0, gt1, gz, gzw = ops._tbptt_backward(saved, "fbt", tuple(z.shape), g,
+                                                     ctx.fuse_act)
+        need = ctx.needs_input_grad
+        I, has_b = w_in.shape[1], b_in is not None
+        G = ops.rowdot(gz, x_cf, with_sum=has_b)
+        gW = gw_in = gb_in = None
+        if need[3]:
+            rows = torch.cat([w_in, b_in[:, None]], dim=1) if has_b else w_in
+            gW = (G + ops.rowdot(gzw, x_cf, with_sum=has_b)) @ rows.t().to(torch.complex64)
         if need[1] or need[2]:
             gh = W.mH @ G
             if ctx.skip:
@@ -255,13 +300,13 @@ class PureRQFEncoderB200(nn.Module):
         w_in, b_in = self.input_proj.weight, self.input_proj.bias
         n = len(self.W)
         first = 0
-        if (PROJECTION == "tc" and x.is_cuda and self.scan_grad_mode == "full" and n > 0
-                and I <= LOWRANK_MAX_INPUTS and (B * T) % 2 == 0 and not x.requires_grad):
+        if (PROJECTION == "tc" and x.is_cuda and n > 0 and I <= LOWRANK_MAX_INPUTS
+                and (B * T) % 2 == 0 and not x.requires_grad):
             c1, t0, t1 = self.rqf[0].two_tap()
             W = self.W[0]
-            h = _InputBlock.apply(x_cf, w_in, b_in, W, c1, t0, t1,
-                                  self.final_activation or n > 1,
-                                  self.skip and W.shape[0] == W.shape[1], B, T)
+            block = _InputTBPTT if self.scan_grad_mode == "tbptt1" else _InputBlock
+            h = block.apply(x_cf, w_in, b_in, W, c1, t0, t1, self.final_activation or n > 1,
+                            self.skip and W.shape[0] == W.shape[1], B, T)
             first = 1
         else:
             proj = w_in @ x_cf if b_in is None else torch.addmm(b_in[:, None], w_in, x_cf)

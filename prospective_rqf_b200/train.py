@@ -55,17 +55,30 @@ WORKLOADS = {
 
 def waveform_batch(batch: int, time: int, fs: float, num_classes: int,
                    generator: torch.Generator, device="cpu"):
-    """(x (B,T,1) float32 in [-1, 1], y (B,) int64) — BASELINE config 2/5 generator."""
+    """(x (B,T,1) float32 in [-1, 1], y (B,) int64) — BASELINE config 2/5 generator.
+
+    Drawn on the generator's device: a CUDA generator makes the whole batch on
+    the GPU (no host work or copy per step); a CPU generator draws on the host
+    and the batch is then moved to `device`."""
     g = generator
-    freq = 50.0 + (4000.0 - 50.0) * torch.rand(batch, 3, 1, generator=g)
-    amp = 0.1 + 0.4 * torch.rand(batch, 3, 1, generator=g)
-    phase = 2 * math.pi * torch.rand(batch, 3, 1, generator=g)
-    t = torch.arange(time, dtype=torch.float64) / fs
+    gd = g.device
+    freq = 50.0 + (4000.0 - 50.0) * torch.rand(batch, 3, 1, generator=g, device=gd)
+    amp = 0.1 + 0.4 * torch.rand(batch, 3, 1, generator=g, device=gd)
+    phase = 2 * math.pi * torch.rand(batch, 3, 1, generator=g, device=gd)
+    t = torch.arange(time, dtype=torch.float64, device=gd) / fs
     x = (amp.double() * torch.sin(2 * math.pi * freq.double() * t + phase.double())).sum(1)
-    x = x + 0.05 * torch.randn(batch, time, generator=g, dtype=torch.float64)
+    x = x + 0.05 * torch.randn(batch, time, generator=g, dtype=torch.float64, device=gd)
     x = x.clamp(-1.0, 1.0).float().unsqueeze(-1)
-    y = torch.randint(0, num_classes, (batch,), generator=g)
+    y = torch.randint(0, num_classes, (batch,), generator=g, device=gd)
     return x.to(device), y.to(device)
+
+
+def synthetic_batches(cfg: "StepConfig", device, seed: int = 0):
+    """Endless fresh batches of the workload's synthetic waveforms, drawn on
+    `device` (a CUDA device keeps data generation on the GPU)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    while True:
+        yield waveform_batch(cfg.batch, cfg.time, cfg.samp_frequency, cfg.num_classes, g, device)
 
 
 def build_model(cfg: StepConfig, device, seed: int = 0) -> RQFClassifier:

@@ -153,7 +153,7 @@ def test_encoder_matches_fp64_restatement(mode, T):
                      ref.numpy(), GRAD_TOL, f"grad {k}")
 
 
-def _lowrank_case(I, bias, skip, T, lowrank):
+def _lowrank_case(I, bias, skip, T, lowrank, mode="full"):
     """Logits and every parameter gradient of a small encoder + readout, and
     the fp64 restatement's, with the first block on the low-rank path or on
     the general F x F GEMM path."""
@@ -162,7 +162,7 @@ def _lowrank_case(I, bias, skip, T, lowrank):
     E.LOWRANK_MAX_INPUTS = 4 if lowrank else 0
     torch.manual_seed(0)
     enc = E.PureRQFEncoderB200(input_dims=I, hidden_dims=16, num_layers=3, skip_connection=skip,
-                               input_proj_bias=bias, seed=4)
+                               input_proj_bias=bias, scan_grad_mode=mode, seed=4)
     model = E.RQFClassifier(enc, 5, 32).cuda()
     with torch.no_grad():
         for r in model.encoder.rqf:
@@ -187,11 +187,14 @@ def _lowrank_case(I, bias, skip, T, lowrank):
     return got, ref
 
 
-@pytest.mark.parametrize("I,bias,skip,T", [(1, False, True, 3000), (1, True, True, 1000),
-                                          (3, True, False, 1000), (2, False, True, 2001)])
-def test_encoder_lowrank_first_block_matches_fp64(I, bias, skip, T, monkeypatch):
-    """The first block over the low-rank input projection (_InputBlock:
-    rqf_lowrank_drive forward, rqf_rowdot cotangents) against the fp64
+@pytest.mark.parametrize("I,bias,skip,T,mode", [
+    (1, False, True, 3000, "full"), (1, True, True, 1000, "full"), (3, True, False, 1000, "full"),
+    (2, False, True, 2001, "full"), (1, False, True, 2500, "tbptt1"), (2, True, True, 1000, "tbptt1"),
+    (1, True, False, 1000, "tbptt1")])
+def test_encoder_lowrank_first_block_matches_fp64(I, bias, skip, T, mode, monkeypatch):
+    """The first block over the low-rank input projection (_InputBlock, and
+    _InputTBPTT for TBPTT(1): rqf_lowrank_drive forward, rqf_rowdot
+    cotangents) against the fp64
     restatement, which runs the F x F projection on h0 = w_in x + b_in.
     Each quantity is within tolerance of fp64 or no worse than the general
     path (F x F GEMMs) on the same inputs: some of these small configurations
@@ -204,9 +207,9 @@ def test_encoder_lowrank_first_block_matches_fp64(I, bias, skip, T, monkeypatch)
     real_drive = ops.lowrank_drive
     monkeypatch.setattr(ops, "lowrank_drive", lambda *a, **k: calls.append(1) or real_drive(*a, **k))
     monkeypatch.setattr(E, "LOWRANK_MAX_INPUTS", E.LOWRANK_MAX_INPUTS)
-    gen, ref = _lowrank_case(I, bias, skip, T, lowrank=False)
+    gen, ref = _lowrank_case(I, bias, skip, T, lowrank=False, mode=mode)
     assert not calls
-    low, ref2 = _lowrank_case(I, bias, skip, T, lowrank=True)
+    low, ref2 = _lowrank_case(I, bias, skip, T, lowrank=True, mode=mode)
     assert calls, "the low-rank first block did not run"
     for k in ref:
         e_low, e_gen = rel_err(low[k], ref2[k]), rel_err(gen[k], ref[k])
@@ -238,6 +241,16 @@ def test_readout_relu_pool_vs_torch(H, B, T):
     gc, counts = ops.readout_relu_pool_backward(mask, scale.cuda(), T)
     assert torch.equal(gc.cpu(), torch.complex(on.float() * scale[:, :, None], torch.zeros(H, B, T)))
     assert torch.equal(counts.cpu(), on.sum(dim=2).float())
+
+
+def test_synthetic_waveforms_drawn_on_the_gpu():
+    from prospective_rqf_b200.train import StepConfig, synthetic_batches
+
+    cfg = StepConfig(batch=4, time=16000, num_classes=35)
+    x, y = next(synthetic_batches(cfg, "cuda", seed=1))
+    assert x.is_cuda and y.is_cuda and x.shape == (4, 16000, 1)
+    assert float(x.abs().max()) <= 1.0 and 0.05 < float(x.std()) < 1.0
+    assert int(y.min()) >= 0 and int(y.max()) < 35
 
 
 def test_rowdot_and_lowrank_drive_vs_fp64():

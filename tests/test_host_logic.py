@@ -127,3 +127,21 @@ def test_install_against_the_reference_tree(monkeypatch):
         assert len(patched) == 21
     finally:
         integration.uninstall()
+
+
+def test_synthetic_waveforms_shape_range_and_fresh_batches():
+    """Config 2/5 synthetic batches: (B, T, 1) in [-1, 1], labels in range, a
+    new draw per step, and the same seed gives the same stream."""
+    import torch
+
+    from prospective_rqf_b200.train import StepConfig, synthetic_batches
+
+    cfg = StepConfig(batch=3, time=800, num_classes=35)
+    a = synthetic_batches(cfg, "cpu", seed=7)
+    x0, y0 = next(a)
+    x1, _ = next(a)
+    assert x0.shape == (3, 800, 1) and x0.dtype == torch.float32
+    assert y0.shape == (3,) and int(y0.min()) >= 0 and int(y0.max()) < 35
+    assert float(x0.abs().max()) <= 1.0 and float(x0.std()) > 0.05
+    assert not torch.equal(x0, x1)
+    assert torch.equal(next(synthetic_batches(cfg, "cpu", seed=7))[0], x0)
