@@ -359,6 +359,28 @@ size_t rqf_projection_weight_grad_workspace_bytes(int64_t m, int64_t k, int64_t 
 int rqf_projection_weight_grad(const float *gz, const float *x, float *gw, int64_t m, int64_t k,
                                int64_t n, void *workspace, rqf_stream_t stream);
 
+/* The same two GEMMs with a real left operand, for the readout's hidden layer
+ * (train.py:ComplexReadoutClassifier :74-136: Linear(2F, H) on [Re h; Im h],
+ * whose cotangent g is real): x (k x n) real in rqf_projection_real,
+ *
+ *   out[j, n] = sum_k op(W)[j, k] * x[k, n] (+ acc[j, n])          complex64
+ *
+ * and gz (m x n) real in rqf_projection_weight_grad_real,
+ *
+ *   gw[j, i] = sum_n gz[j, n] * conj(x[i, n])                      complex64.
+ *
+ * Half the tensor-core work of the complex forms, which would multiply the
+ * zero imaginary parts.  n must be a multiple of 4 (the real rows' TMA
+ * pitch); the rest as rqf_projection / rqf_projection_weight_grad, with
+ * workspace sizes from rqf_projection_workspace_bytes and
+ * rqf_projection_weight_grad_real_workspace_bytes. */
+int rqf_projection_real(const float *w, const float *x, const float *acc, float *out, int64_t m,
+                        int64_t k, int64_t n, int conj_transpose, void *workspace,
+                        rqf_stream_t stream);
+size_t rqf_projection_weight_grad_real_workspace_bytes(int64_t m, int64_t k, int64_t n);
+int rqf_projection_weight_grad_real(const float *gz, const float *x, float *gw, int64_t m,
+                                    int64_t k, int64_t n, void *workspace, rqf_stream_t stream);
+
 /* First block over a low-rank input projection (pure.py:_forward_fbt_stack
  * :522-534: proj = w_in @ x_cf (+ b_in), h = proj.to(complex64), then the
  * first block's z = W @ h).  With I = input_dims <= 4:
@@ -398,9 +420,10 @@ int rqf_rowdot(const float *a, const float *x, float *out, void *workspace, int6
  * bias may be null.  One pass over z; fixed-order reduction. */
 int rqf_readout_relu_pool(const float *z, const float *bias, uint32_t *mask, float *pooled,
                           int64_t h, int64_t batch, int64_t time, rqf_stream_t stream);
-/* Its backward: gc[h, b, t] = (mask ? scale[h, b] : 0) + 0i (complex64, the
- * input of the projection GEMMs' cotangents; scale = gpool / T) and
- * counts[h, b] = number of set mask bits (float32; may be null). */
+/* Its backward: g[h, b, t] = mask ? scale[h, b] : 0 (float32, the real
+ * input of rqf_projection_real and rqf_projection_weight_grad_real; scale =
+ * gpool / T) and counts[h, b] = number of set mask bits (float32; may be
+ * null). */
 int rqf_readout_relu_pool_backward(const uint32_t *mask, const float *scale, float *gc,
                                    float *counts, int64_t h, int64_t batch, int64_t time,
                                    rqf_stream_t stream);

@@ -76,7 +76,29 @@ rowdot_partial_kernel(const float2 *__restrict__ A, const float *__restrict__ x,
 #pragma unroll
   for (int j = 0; j < kMaxCols; ++j) acc[j] = make_float2(0.f, 0.f);
   const float2 *row = A + f * N;
-  for (long long n = n0 + 2 * threadIdx.x; n < n1; n += 2 * kRowdotThreads) {
+  // kUnroll pairs per thread per iteration, loaded before any is used, so
+  // that each thread keeps kUnroll 16-byte loads in flight
+  constexpr int kUnroll = 4;
+  constexpr long long kStep = 2LL * kRowdotThreads;
+  long long n = n0 + 2 * threadIdx.x;
+  for (; n + (kUnroll - 1) * kStep < n1; n += kUnroll * kStep) {
+    float4 a[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) a[u] = *reinterpret_cast<const float4 *>(row + n + u * kStep);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const long long m = n + u * kStep;
+#pragma unroll
+      for (int j = 0; j < kMaxCols; ++j) {
+        if (j >= J) break;
+        float2 xv = make_float2(1.f, 1.f);
+        if (j < I) xv = *reinterpret_cast<const float2 *>(x + (long long)j * N + m);
+        acc[j].x = fmaf(a[u].x, xv.x, fmaf(a[u].z, xv.y, acc[j].x));
+        acc[j].y = fmaf(a[u].y, xv.x, fmaf(a[u].w, xv.y, acc[j].y));
+      }
+    }
+  }
+  for (; n < n1; n += kStep) {
     const float4 a = *reinterpret_cast<const float4 *>(row + n);  // samples n, n + 1
 #pragma unroll
     for (int j = 0; j < kMaxCols; ++j) {

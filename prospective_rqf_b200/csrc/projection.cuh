@@ -88,6 +88,7 @@ struct Params {
   int m_pairs, n_tiles, k_blocks;  // pair tiles: kPairM A' rows x kBN X' columns
   long long num_tiles;
   int a_rows_pad;      // rows of the hi half of the split A' buffer (a multiple of kPairM)
+  int real_x;          // X real (K x N): columns are samples, not (Re, Im) pairs
 };
 
 // ------------------------------------------------------------ PTX wrappers
@@ -512,6 +513,42 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       tile_coords(tile, p, mp, nt);
       const long long j = ((long long)mp * kPairM + (long long)rank * kBM + row) >> 1;
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kBN);
+      if (p.real_x) {
+        // Real X: TMEM lane 2j holds Re and lane 2j+1 Im of out[j, n0 + 0..31];
+        // the even lane writes samples n0 + 0..15, the odd lane n0 + 16..31.
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          float v[32];
+          tc_ld_32x32b_x32(tbase + (uint32_t)(c * 32), v);
+          float r[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            r[i] = __shfl_xor_sync(0xffffffffu, odd ? v[i] : v[16 + i], 1);
+          const long long n0 = (long long)nt * kBN + c * 32 + (odd ? 16 : 0);
+          if (j < p.M && n0 < p.N) {
+            float2 *dst = p.out + j * p.N + n0;
+            const float2 *src = p.acc ? p.acc + j * p.N + n0 : nullptr;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              float2 z0 = odd ? make_float2(r[2 * q], v[16 + 2 * q]) : make_float2(v[2 * q], r[2 * q]);
+              float2 z1 = odd ? make_float2(r[2 * q + 1], v[16 + 2 * q + 1])
+                              : make_float2(v[2 * q + 1], r[2 * q + 1]);
+              const long long n = n0 + 2 * q;
+              if (n + 2 <= p.N) {
+                if (src) {
+                  const float4 a = reinterpret_cast<const float4 *>(src)[q];
+                  z0 = make_float2(z0.x + a.x, z0.y + a.y);
+                  z1 = make_float2(z1.x + a.z, z1.y + a.w);
+                }
+                reinterpret_cast<float4 *>(dst)[q] = make_float4(z0.x, z0.y, z1.x, z1.y);
+              } else if (n < p.N) {
+                if (src) z0 = make_float2(z0.x + src[2 * q].x, z0.y + src[2 * q].y);
+                dst[2 * q] = z0;
+              }
+            }
+          }
+        }
+      } else {
 #pragma unroll 1
       for (int c = 0; c < kBN / 32; ++c) {
         float v[32];
@@ -557,6 +594,7 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           }
         }
       }
+      }  // complex X
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? acce1 : acce0);
@@ -627,12 +665,19 @@ constexpr int kWgRows = 128;                     // j rows per CTA
 constexpr int kWgPairRows = 2 * kWgRows;         // j rows per pair tile
 constexpr int kWgCols = 128;                     // i per pair tile
 constexpr int kWgHRows = kWgCols / 2;            // h' rows each CTA stages
-constexpr int kWgStages = 6;
 constexpr int kWgABytes = kWgRows * kBK * 4;     // 8 KB: gz' tile (hi or lo)
 constexpr int kWgHBytes = kWgHRows * kBK * 4;    // 4 KB: h' rows (one of h', h~')
-constexpr int kWgStageBytes = 2 * kWgABytes + 4 * kWgHBytes;  // 32 KB
-constexpr int kWgTxBytes = kWgABytes + kWgHBytes;             // 12 KB landed by TMA
-constexpr int kWgSmemBytes = kWgStages * kWgStageBytes + kBarBytes + 1024;
+constexpr int kWgRawOff = 2 * kWgABytes + 4 * kWgHBytes;      // 32 KB: the operand regions
+// Real gz (the readout's cotangent): a stage also holds the raw h' tile, 64
+// rows x 16 samples x (Re, Im) = 128-byte rows (128-byte swizzle), which the
+// transform de-interleaves into the Re and -Im planes of B.
+template <bool kRealGz>
+struct WgLayout {
+  static constexpr int kStages = kRealGz ? 5 : 6;
+  static constexpr int kStageBytes = kRealGz ? kWgRawOff + 8192 : kWgRawOff;  // 40 / 32 KB
+  static constexpr int kTxBytes = kRealGz ? kWgABytes + 8192 : kWgABytes + kWgHBytes;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;
+};
 // TMEM: columns [0, 256) the CTA's running total, [256, 512) the chunk
 // accumulator.  The tensor core's fp32 accumulate rounds with a bias that
 // grows with the number of accumulations into one accumulator (about 2e-4
@@ -658,9 +703,18 @@ __device__ __forceinline__ float4 tf32_lo4(float4 v) {
   return make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
 }
 
+// kRealGz: gz is real (M x N) and the reduction runs over the N samples:
+// Re gW = sum_n gz h_re, Im gW = sum_n gz (-h_im); A = gz as TMA lands it,
+// B = the de-interleaved [h_re ; -h_im] rows.  Half the k-blocks of the
+// complex form, whose A would be gz interleaved with zeros.
+template <bool kRealGz>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kWgThreads, 1)
 proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmH,
                   const WgParams p) {
+  using L = WgLayout<kRealGz>;
+  constexpr int kWgStages = L::kStages;
+  constexpr int kWgStageBytes = L::kStageBytes;
+  constexpr int kWgTxBytes = L::kTxBytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -722,7 +776,10 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
         uint8_t *st = smem + stage * kWgStageBytes;
         mbar_expect_tx(&full[stage], kWgTxBytes);
         tma_load_2d(st, &tmG, &full[stage], (int)(kb * kBK), jrow);
-        tma_load_2d(st + kWgABytes, &tmH, &full[stage], (int)(kb * kBK), irow);
+        if (kRealGz)  // h' floats [32 kb, 32 kb + 32): samples [16 kb, 16 kb + 16)
+          tma_load_2d(st + kWgRawOff, &tmH, &full[stage], (int)(kb * 2 * kBK), irow);
+        else
+          tma_load_2d(st + kWgABytes, &tmH, &full[stage], (int)(kb * kBK), irow);
         ++issued;
         if (++stage == kWgStages) {
           stage = 0;
@@ -866,13 +923,34 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
       constexpr int kAChunks = kWgABytes / 16, kHChunks = kWgHBytes / 16;
 #pragma unroll
       for (int i = t; i < kAChunks; i += 128) al[i] = tf32_lo4(ah[i]);
+      if (kRealGz) {
+        // raw row r (128 bytes): chunk q holds samples 2q, 2q+1 as (Re, Im,
+        // Re, Im), stored at chunk q ^ (r & 7).  Output chunk c of a 64-byte
+        // plane row holds samples 4c..4c+3, stored at c ^ ((r >> 1) & 3).
+        const uint8_t *raw = st + kWgRawOff;
 #pragma unroll
-      for (int i = t; i < kHChunks; i += 128) {
-        const float4 v = bh[i];
-        const float4 lo = tf32_lo4(v);
-        bh[kHChunks + i] = swap_neg(v);
-        bl[i] = lo;
-        bl[kHChunks + i] = swap_neg(lo);
+        for (int e = t; e < kWgHRows * 4; e += 128) {
+          const int r = e >> 2, c = e & 3;
+          const float4 v0 = *reinterpret_cast<const float4 *>(raw + r * 128 + (((2 * c) ^ (r & 7)) << 4));
+          const float4 v1 =
+              *reinterpret_cast<const float4 *>(raw + r * 128 + (((2 * c + 1) ^ (r & 7)) << 4));
+          const float4 re = make_float4(v0.x, v0.z, v1.x, v1.z);
+          const float4 im = make_float4(-v0.y, -v0.w, -v1.y, -v1.w);
+          const int o = r * 4 + (c ^ ((r >> 1) & 3));  // float4 index in a 4 KB plane
+          bh[o] = re;
+          bh[kHChunks + o] = im;
+          bl[o] = tf32_lo4(re);
+          bl[kHChunks + o] = tf32_lo4(im);
+        }
+      } else {
+#pragma unroll
+        for (int i = t; i < kHChunks; i += 128) {
+          const float4 v = bh[i];
+          const float4 lo = tf32_lo4(v);
+          bh[kHChunks + i] = swap_neg(v);
+          bl[i] = lo;
+          bl[kHChunks + i] = swap_neg(lo);
+        }
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();

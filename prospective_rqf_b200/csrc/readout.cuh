@@ -14,7 +14,7 @@
 // the bit mask per warp iteration (bit t % 32 of word t / 32), and reduce in a
 // fixed order (deterministic).  Both are HBM-bound: the forward reads z once
 // (8 bytes per sample) and writes 1 bit; the backward reads the bit and writes
-// the complex cotangent (8 bytes) that the projection GEMMs take as input.
+// the real cotangent (4 bytes) that the real-operand projection GEMMs take.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -55,21 +55,21 @@ relu_pool_kernel(const float2 *__restrict__ z, const float *__restrict__ bias,
   if (threadIdx.x == 0) pooled[row] = (float)(red[0] / (double)T);
 }
 
-// gc[row, t] = (mask ? scale[row] : 0, 0); counts[row] = number of set bits.
+// g[row, t] = mask ? scale[row] : 0; counts[row] = number of set bits.
 __global__ void __launch_bounds__(kThreads)
 relu_pool_backward_kernel(const uint32_t *__restrict__ mask, const float *__restrict__ scale,
-                          float2 *__restrict__ gc, float *__restrict__ counts, long long T,
+                          float *__restrict__ gc, float *__restrict__ counts, long long T,
                           long long words) {
   const long long row = blockIdx.x;
   const float s = scale[row];
   const uint32_t *mr = mask + row * words;
-  float2 *gr = gc + row * T;
+  float *gr = gc + row * T;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int cnt = 0;
   for (long long w = warp; w < words; w += kWarps) {
     const uint32_t bits = mr[w];
     const long long t = w * 32 + lane;
-    if (t < T) gr[t] = make_float2(((bits >> lane) & 1u) ? s : 0.f, 0.f);
+    if (t < T) gr[t] = ((bits >> lane) & 1u) ? s : 0.f;
     if (lane == 0) cnt += __popc(bits);
   }
   __shared__ int red[kThreads];

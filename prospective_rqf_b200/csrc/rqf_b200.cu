@@ -1129,9 +1129,14 @@ size_t rqf_projection_workspace_bytes(int64_t m, int64_t k) {
   return (size_t)(2 * g.rows_pad * g.k_pad) * sizeof(float);
 }
 
-int rqf_projection(const float *w, const float *x, const float *acc, float *out, int64_t m,
-                   int64_t k, int64_t n, int conj_transpose, void *workspace,
-                   rqf_stream_t stream) {
+}  // extern "C"
+
+namespace {
+
+// x complex (k x n) when real_x = 0, real (k x n) when real_x = 1.
+int projection_impl(const float *w, const float *x, const float *acc, float *out, int64_t m,
+                    int64_t k, int64_t n, int conj_transpose, void *workspace,
+                    rqf_stream_t stream, int real_x) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (m < 0 || k < 0 || n < 0) return RQF_ERR_SHAPE;
   if (m == 0 || n == 0) return RQF_OK;
@@ -1145,8 +1150,10 @@ int rqf_projection(const float *w, const float *x, const float *acc, float *out,
                               : cudaMemsetAsync(out, 0, out_bytes, st);
     return e == cudaSuccess ? RQF_OK : RQF_ERR_LAUNCH;
   }
-  // TMA: the X' row pitch (8n bytes) must be a multiple of 16, coordinates are int32.
-  if ((n & 1) != 0 || n >= (int64_t(1) << 30) || k > 0x7fffffffLL || m > (int64_t(1) << 40))
+  // TMA: the X' row pitch (8n bytes complex, 4n real) must be a multiple of
+  // 16, coordinates are int32.
+  if ((n & (real_x ? 3 : 1)) != 0 || n >= (int64_t(1) << 30) || k > 0x7fffffffLL ||
+      m > (int64_t(1) << 40))
     return RQF_ERR_SHAPE;
   if (!aligned(x, 16) || !aligned(out, 16) || !aligned(workspace, 16) ||
       (acc != nullptr && !aligned(acc, 16)))
@@ -1169,8 +1176,9 @@ int rqf_projection(const float *w, const float *x, const float *acc, float *out,
   if (!encode_map_2d(&tmA, a_split, (uint64_t)g.k_pad, (uint64_t)(2 * g.rows_pad),
                      (uint64_t)g.k_pad * sizeof(float), proj::kBK, proj::kBM,
                      CU_TENSOR_MAP_SWIZZLE_64B) ||
-      !encode_map_2d(&tmX, x, (uint64_t)(2 * n), (uint64_t)k, (uint64_t)(2 * n) * sizeof(float),
-                     32, proj::kBK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
+      !encode_map_2d(&tmX, x, (uint64_t)(real_x ? n : 2 * n), (uint64_t)k,
+                     (uint64_t)(real_x ? n : 2 * n) * sizeof(float), 32, proj::kBK,
+                     CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
     return RQF_ERR_LAUNCH;
 
   proj::Params p;
@@ -1180,13 +1188,30 @@ int rqf_projection(const float *w, const float *x, const float *acc, float *out,
   p.N = n;
   p.K = (int)k;
   p.m_pairs = (int)(g.rows_pad / proj::kPairM);
-  p.n_tiles = (int)ceil_div(2 * n, proj::kBN);
+  p.n_tiles = (int)ceil_div(real_x ? n : 2 * n, proj::kBN);
   p.k_blocks = (int)(g.k_pad / proj::kBK);
   p.num_tiles = (long long)p.m_pairs * p.n_tiles;
   p.a_rows_pad = (int)g.rows_pad;
+  p.real_x = real_x;
   const long long grid = 2 * (p.num_tiles < pairs ? p.num_tiles : pairs);  // whole CTA pairs
   proj::proj_kernel<<<(unsigned)grid, proj::kThreads, proj::kSmemBytes, st>>>(tmA, tmX, p);
   return launch_status();
+}
+
+}  // namespace
+
+extern "C" {
+
+int rqf_projection(const float *w, const float *x, const float *acc, float *out, int64_t m,
+                   int64_t k, int64_t n, int conj_transpose, void *workspace,
+                   rqf_stream_t stream) {
+  return projection_impl(w, x, acc, out, m, k, n, conj_transpose, workspace, stream, 0);
+}
+
+int rqf_projection_real(const float *w, const float *x, const float *acc, float *out, int64_t m,
+                        int64_t k, int64_t n, int conj_transpose, void *workspace,
+                        rqf_stream_t stream) {
+  return projection_impl(w, x, acc, out, m, k, n, conj_transpose, workspace, stream, 1);
 }
 
 }  // extern "C"
@@ -1199,11 +1224,13 @@ struct WgGeometry {
   int64_t kblocks;
 };
 
-inline WgGeometry wgrad_geometry(int64_t m, int64_t k, int64_t n, int pairs) {
+// kblocks: k-blocks of the reduction, ceil(2n / 16) for complex gz and
+// ceil(n / 16) for real gz.
+inline WgGeometry wgrad_geometry(int64_t m, int64_t k, int64_t kblocks, int pairs) {
   WgGeometry g;
   g.m_pairs = (int)ceil_div(m, proj::kWgPairRows);
   g.i_tiles = (int)ceil_div(k, proj::kWgCols);
-  g.kblocks = ceil_div(2 * n, proj::kBK);
+  g.kblocks = kblocks;
   const int64_t tiles = (int64_t)g.m_pairs * g.i_tiles;
   // whole waves of CTA pairs (one CTA per SM), enough of them that no pair
   // runs more than ~256 k-blocks: pairs sharing an operand block then stay
@@ -1219,24 +1246,30 @@ inline WgGeometry wgrad_geometry(int64_t m, int64_t k, int64_t n, int pairs) {
   return g;
 }
 
+template <bool kRealGz>
 int wgrad_pairs_per_device() {
-  return pair_capacity<1>(reinterpret_cast<const void *>(proj::proj_wgrad_kernel),
-                          proj::kWgThreads, proj::kWgSmemBytes);
+  return pair_capacity<kRealGz ? 2 : 1>(
+      reinterpret_cast<const void *>(proj::proj_wgrad_kernel<kRealGz>), proj::kWgThreads,
+      proj::WgLayout<kRealGz>::kSmemBytes);
 }
 
-}  // namespace
+inline int64_t wgrad_kblocks(int64_t n, bool real_gz) {
+  return ceil_div(real_gz ? n : 2 * n, proj::kBK);
+}
 
-extern "C" {
-
-size_t rqf_projection_weight_grad_workspace_bytes(int64_t m, int64_t k, int64_t n) {
+template <bool kRealGz>
+size_t wgrad_workspace_bytes(int64_t m, int64_t k, int64_t n) {
   if (m <= 0 || k <= 0 || n <= 0) return 0;
-  const WgGeometry g = wgrad_geometry(m, k, n, wgrad_pairs_per_device());
+  const WgGeometry g =
+      wgrad_geometry(m, k, wgrad_kblocks(n, kRealGz), wgrad_pairs_per_device<kRealGz>());
   return (size_t)g.splits * (size_t)g.m_pairs * proj::kWgPairRows * (size_t)g.i_tiles *
          proj::kWgCols * sizeof(float2);
 }
 
-int rqf_projection_weight_grad(const float *gz, const float *x, float *gw, int64_t m, int64_t k,
-                               int64_t n, void *workspace, rqf_stream_t stream) {
+// gz complex (m x n) or, with kRealGz, real (m x n); x complex (k x n).
+template <bool kRealGz>
+int wgrad_impl(const float *gz, const float *x, float *gw, int64_t m, int64_t k, int64_t n,
+               void *workspace, rqf_stream_t stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (m < 0 || k < 0 || n < 0) return RQF_ERR_SHAPE;
   if (m == 0 || k == 0) return RQF_OK;
@@ -1247,18 +1280,28 @@ int rqf_projection_weight_grad(const float *gz, const float *x, float *gw, int64
                : RQF_ERR_LAUNCH;
   }
   if (gz == nullptr || x == nullptr || workspace == nullptr) return RQF_ERR_ARGUMENT;
-  if ((n & 1) != 0 || n >= (int64_t(1) << 30) || m > 0x7fffffffLL || k > 0x7fffffffLL)
+  // TMA row pitches (8n bytes complex, 4n real) must be multiples of 16.
+  if ((n & (kRealGz ? 3 : 1)) != 0 || n >= (int64_t(1) << 30) || m > 0x7fffffffLL ||
+      k > 0x7fffffffLL)
     return RQF_ERR_SHAPE;
   if (!aligned(gz, 16) || !aligned(x, 16) || !aligned(workspace, 16)) return RQF_ERR_ALIGN;
-  const int pairs = wgrad_pairs_per_device();
+  const int pairs = wgrad_pairs_per_device<kRealGz>();
   if (pairs <= 0) return RQF_ERR_LAUNCH;
-  const WgGeometry g = wgrad_geometry(m, k, n, pairs);
+  const WgGeometry g = wgrad_geometry(m, k, wgrad_kblocks(n, kRealGz), pairs);
+  const uint64_t gz_cols = kRealGz ? (uint64_t)n : (uint64_t)(2 * n);
   CUtensorMap tmG, tmH;
-  if (!encode_map_2d(&tmG, gz, (uint64_t)(2 * n), (uint64_t)m, (uint64_t)(2 * n) * sizeof(float),
-                     proj::kBK, proj::kWgRows, CU_TENSOR_MAP_SWIZZLE_64B) ||
-      !encode_map_2d(&tmH, x, (uint64_t)(2 * n), (uint64_t)k, (uint64_t)(2 * n) * sizeof(float),
-                     proj::kBK, proj::kWgHRows, CU_TENSOR_MAP_SWIZZLE_64B))
-    return RQF_ERR_LAUNCH;
+  const bool ok_g = encode_map_2d(&tmG, gz, gz_cols, (uint64_t)m, gz_cols * sizeof(float),
+                                  proj::kBK, proj::kWgRows, CU_TENSOR_MAP_SWIZZLE_64B);
+  // complex gz: h' boxes of 16 floats x 64 rows (64-byte swizzle); real gz:
+  // 32 floats (16 samples) x 64 rows, de-interleaved in shared memory
+  const bool ok_h =
+      kRealGz ? encode_map_2d(&tmH, x, (uint64_t)(2 * n), (uint64_t)k,
+                              (uint64_t)(2 * n) * sizeof(float), 2 * proj::kBK, proj::kWgHRows,
+                              CU_TENSOR_MAP_SWIZZLE_128B)
+              : encode_map_2d(&tmH, x, (uint64_t)(2 * n), (uint64_t)k,
+                              (uint64_t)(2 * n) * sizeof(float), proj::kBK, proj::kWgHRows,
+                              CU_TENSOR_MAP_SWIZZLE_64B);
+  if (!ok_g || !ok_h) return RQF_ERR_LAUNCH;
   proj::WgParams p;
   p.partials = static_cast<float2 *>(workspace);
   p.M = m;
@@ -1269,8 +1312,8 @@ int rqf_projection_weight_grad(const float *gz, const float *x, float *gw, int64
   p.kblocks = g.kblocks;
   p.ld = g.i_tiles * proj::kWgCols;
   const int64_t grid = 2 * (int64_t)g.m_pairs * g.i_tiles * g.splits;  // whole CTA pairs
-  proj::proj_wgrad_kernel<<<(unsigned)grid, proj::kWgThreads, proj::kWgSmemBytes, st>>>(tmG, tmH,
-                                                                                    p);
+  proj::proj_wgrad_kernel<kRealGz>
+      <<<(unsigned)grid, proj::kWgThreads, proj::WgLayout<kRealGz>::kSmemBytes, st>>>(tmG, tmH, p);
   if (cudaGetLastError() != cudaSuccess) return RQF_ERR_LAUNCH;
   const int64_t total = m * k;
   const int64_t blocks = ceil_div(total, 32);
@@ -1279,6 +1322,28 @@ int rqf_projection_weight_grad(const float *gz, const float *x, float *gw, int64
       p.partials, reinterpret_cast<float2 *>(gw), m, k, g.splits,
       (long long)g.m_pairs * proj::kWgPairRows, p.ld);
   return launch_status();
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t rqf_projection_weight_grad_workspace_bytes(int64_t m, int64_t k, int64_t n) {
+  return wgrad_workspace_bytes<false>(m, k, n);
+}
+
+int rqf_projection_weight_grad(const float *gz, const float *x, float *gw, int64_t m, int64_t k,
+                               int64_t n, void *workspace, rqf_stream_t stream) {
+  return wgrad_impl<false>(gz, x, gw, m, k, n, workspace, stream);
+}
+
+size_t rqf_projection_weight_grad_real_workspace_bytes(int64_t m, int64_t k, int64_t n) {
+  return wgrad_workspace_bytes<true>(m, k, n);
+}
+
+int rqf_projection_weight_grad_real(const float *gz, const float *x, float *gw, int64_t m,
+                                    int64_t k, int64_t n, void *workspace, rqf_stream_t stream) {
+  return wgrad_impl<true>(gz, x, gw, m, k, n, workspace, stream);
 }
 
 }  // extern "C"
@@ -1370,9 +1435,8 @@ int rqf_readout_relu_pool_backward(const uint32_t *mask, const float *scale, flo
   if (rows == 0 || time == 0) return RQF_OK;
   if (rows > 0x7fffffffLL) return RQF_ERR_SHAPE;
   if (mask == nullptr || scale == nullptr || gc == nullptr) return RQF_ERR_ARGUMENT;
-  if (!aligned(gc, 8)) return RQF_ERR_ALIGN;
   readout::relu_pool_backward_kernel<<<(unsigned)rows, readout::kThreads, 0, st>>>(
-      mask, scale, reinterpret_cast<float2 *>(gc), counts, time, ceil_div(time, 32));
+      mask, scale, gc, counts, time, ceil_div(time, 32));
   return launch_status();
 }
 

@@ -368,9 +368,11 @@ class _ReadoutPooled(torch.autograd.Function):
     readout (train.py:ComplexReadoutClassifier :126-136): the projection
     Re(V h) of _ReadoutHidden, then one pass (rqf_readout_relu_pool) that
     keeps only the ReLU mask bits and the time-means.  Backward: the mask
-    turns gpool into g = mask * gpool / T (rqf_readout_relu_pool_backward),
-    which feeds the same two projection cotangents; gb1 = sum_b gpool / T *
-    (set bits of the (h, b) row)."""
+    turns gpool into the real g = mask * gpool / T
+    (rqf_readout_relu_pool_backward), which feeds the real-operand forms of
+    the two projection cotangents (rqf_projection_real,
+    rqf_projection_weight_grad_real); gb1 = sum_b gpool / T * (set bits of
+    the (h, b) row)."""
 
     @staticmethod
     def forward(ctx, h, W1, b1):
@@ -387,11 +389,11 @@ class _ReadoutPooled(torch.autograd.Function):
         h, V, mask = ctx.saved_tensors
         need = ctx.needs_input_grad
         scale = gpool / ctx.time
-        gc, counts = ops.readout_relu_pool_backward(mask, scale, ctx.time)
-        gh = _project(V, gc, conj_transpose=True) if need[0] else None
+        g, counts = ops.readout_relu_pool_backward(mask, scale, ctx.time)
+        gh = ops.projection_real(V, g, conj_transpose=True) if need[0] else None
         gW1 = None
         if need[1]:
-            P = _weight_grad(gc, h)
+            P = ops.projection_weight_grad_real(g, h)
             gW1 = torch.cat([P.real, -P.imag], dim=1)
         gb1 = (scale * counts).sum(dim=1) if need[2] else None
         return gh, gW1, gb1

@@ -934,15 +934,16 @@ def readout_relu_pool(z: torch.Tensor, bias: torch.Tensor | None):
 
 
 def readout_relu_pool_backward(mask: torch.Tensor, scale: torch.Tensor, time: int):
-    """gc = mask * scale[:, :, None] as complex64 (H, B, T) (zero imaginary
-    part) and the set-bit count per (h, b) row (rqf_readout_relu_pool_backward)."""
+    """g = mask * scale[:, :, None] as float32 (H, B, T) (the real cotangent
+    of the readout's hidden layer) and the set-bit count per (h, b) row
+    (rqf_readout_relu_pool_backward)."""
     dev = _require_cuda(mask, scale)
     mask = mask.contiguous()
     H, B, words = (int(d) for d in mask.shape)
     if words != (time + 31) // 32:
         raise ValueError(f"mask of {words} words does not cover {time} steps")
     ss = scale.detach().to(torch.float32).contiguous()
-    gc = torch.empty((H, B, time), dtype=torch.complex64, device=dev)
+    gc = torch.empty((H, B, time), dtype=torch.float32, device=dev)
     counts = torch.empty((H, B), dtype=torch.float32, device=dev)
     lib = _abi.load()
     with _timing.launch("rqf_readout_relu_pool_backward", H * B * time, _nbytes(mask, gc)):
@@ -951,3 +952,64 @@ def readout_relu_pool_backward(mask: torch.Tensor, scale: torch.Tensor, time: in
             _abi.stream_of(gc)), "rqf_readout_relu_pool_backward")
     _done(dev)
     return gc, counts
+
+
+# ------------------------------------------------ real-operand projections
+def projection_real(W: torch.Tensor, x: torch.Tensor, conj_transpose: bool = False,
+                    acc: torch.Tensor | None = None) -> torch.Tensor:
+    """out = op(W) @ x (+ acc) for a real float32 x (K, ...), complex64 out
+    (M, ...): the readout's input cotangent V^H g with g real
+    (rqf_projection_real, half the tensor-core work of projection on a
+    complex x).  N not a multiple of 4 runs torch.matmul on the GPU."""
+    dev = _require_cuda(W, x, acc)
+    w = _c64(W)
+    xx = x.detach().to(torch.float32).contiguous()
+    K = int(xx.shape[0])
+    M = int(w.shape[1] if conj_transpose else w.shape[0])
+    if int(w.shape[0] if conj_transpose else w.shape[1]) != K:
+        raise ValueError(f"W {tuple(w.shape)} does not match x {tuple(xx.shape)}")
+    tail = tuple(xx.shape[1:])
+    N = xx.numel() // K if K else 0
+    out_shape = (M,) + tail
+    a = _c64(acc) if acc is not None else None
+    if a is not None and tuple(a.shape) != out_shape:
+        raise ValueError(f"acc must have shape {out_shape}, got {tuple(a.shape)}")
+    if N % 4 != 0:
+        opw = w.mH if conj_transpose else w
+        out = (opw @ xx.reshape(K, N).to(torch.complex64)).reshape(out_shape)
+        return out if a is None else out.add_(a)
+    lib = _abi.load()
+    out = torch.empty(out_shape, dtype=torch.complex64, device=dev)
+    ws = _scratch(lib.rqf_projection_workspace_bytes(M, K), dev)
+    with _timing.launch("rqf_projection_real", M * N, _nbytes(xx, out, a)):
+        _abi.check(lib.rqf_projection_real(
+            _abi.ptr(w), _abi.ptr(xx), _abi.ptr(a), _abi.ptr(out), M, K, N, int(bool(conj_transpose)),
+            _abi.ptr(ws), _abi.stream_of(out)), "rqf_projection_real")
+    _done(dev)
+    return out
+
+
+def projection_weight_grad_real(gz: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """gW = gz @ x^H for a real float32 gz (M, ...) and complex x (K, ...):
+    the readout's weight cotangent with its real cotangent g
+    (rqf_projection_weight_grad_real: the reduction runs over the samples,
+    half the k-blocks of the complex form).  N not a multiple of 4 runs
+    torch.matmul on the GPU."""
+    dev = _require_cuda(gz, x)
+    g = gz.detach().to(torch.float32).contiguous()
+    xx = _c64(x)
+    M, K = int(g.shape[0]), int(xx.shape[0])
+    if tuple(g.shape[1:]) != tuple(xx.shape[1:]):
+        raise ValueError(f"gz {tuple(g.shape)} and x {tuple(xx.shape)} differ in trailing dims")
+    N = g.numel() // M if M else 0
+    if N % 4 != 0:
+        return g.reshape(M, N).to(torch.complex64) @ xx.reshape(K, N).mH
+    lib = _abi.load()
+    gw = torch.empty((M, K), dtype=torch.complex64, device=dev)
+    ws = _scratch(lib.rqf_projection_weight_grad_real_workspace_bytes(M, K, N), dev)
+    with _timing.launch("rqf_projection_weight_grad_real", M * N, _nbytes(g, xx, gw)):
+        _abi.check(lib.rqf_projection_weight_grad_real(
+            _abi.ptr(g), _abi.ptr(xx), _abi.ptr(gw), M, K, N, _abi.ptr(ws),
+            _abi.stream_of(g)), "rqf_projection_weight_grad_real")
+    _done(dev)
+    return gw

@@ -153,3 +153,55 @@ def test_weight_grad_odd_n_uses_torch():
     gz, x = _crandn(g, 6, 3, 5), _crandn(g, 4, 3, 5)
     gw = ops.projection_weight_grad(gz.cuda(), x.cuda())
     assert_close(gw.cpu().numpy().astype(np.complex128), _ref_wgrad(gz, x), 1e-6, "odd N")
+
+
+# ------------------------------------------------ real left operands (readout)
+@pytest.mark.parametrize("M,K,N", [(64, 32, 256), (37, 50, 1000), (256, 256, 2 * 1112), (5, 3, 4),
+                                   (200, 130, 64)])
+@pytest.mark.parametrize("conj", [False, True])
+def test_projection_real_x_vs_fp64(M, K, N, conj):
+    """rqf_projection_real (x real) against fp64, with and without acc."""
+    from prospective_rqf_b200 import ops
+
+    g = torch.Generator().manual_seed(M * 31 + K + N + int(conj))
+    W = _crandn(g, *((K, M) if conj else (M, K)), scale=1 / np.sqrt(2 * K))
+    x = torch.randn(K, N, generator=g)
+    acc = _crandn(g, M, N)
+    out = ops.projection_real(W.cuda(), x.cuda(), conj_transpose=conj)
+    assert out.shape == (M, N)
+    ref = _ref(W, x.to(torch.complex64), conj)
+    assert_close(out.cpu().numpy().astype(np.complex128), ref, PROJ_TOL, "op(W) x, x real")
+    out2 = ops.projection_real(W.cuda(), x.cuda(), conj, acc.cuda())
+    assert_close(out2.cpu().numpy().astype(np.complex128),
+                 _ref(W, x.to(torch.complex64), conj, acc), PROJ_TOL, "op(W) x + acc, x real")
+
+
+@pytest.mark.parametrize("M,K,N", [(64, 32, 256), (37, 50, 1000), (256, 256, 2 * 1112), (5, 3, 4),
+                                   (200, 130, 64)])
+def test_weight_grad_real_gz_vs_fp64(M, K, N):
+    """rqf_projection_weight_grad_real (gz real) against fp64."""
+    from prospective_rqf_b200 import ops
+
+    g = torch.Generator().manual_seed(M * 17 + K * 3 + N)
+    gz, x = torch.randn(M, N, generator=g), _crandn(g, K, N)
+    gw = ops.projection_weight_grad_real(gz.cuda(), x.cuda())
+    assert gw.shape == (M, K)
+    ref = _ref_wgrad(gz.to(torch.complex64), x)
+    e32 = rel_err((gz.cuda().to(torch.complex64) @ x.cuda().mH).cpu().numpy(), ref)
+    assert_close(gw.cpu().numpy().astype(np.complex128), ref, max(PROJ_TOL, 3 * e32), "gz x^H, gz real")
+
+
+def test_weight_grad_real_gz_full_layer_and_deterministic():
+    """The readout shape: H = F = 256, N = 32 x 16000 samples."""
+    from prospective_rqf_b200 import ops
+
+    g = torch.Generator().manual_seed(12)
+    F, B, T = 256, 32, 16000
+    gz = torch.randn(F, B, T, generator=g).cuda()
+    h = torch.randn(F, B, T, dtype=torch.complex64, generator=g).cuda()
+    gw = ops.projection_weight_grad_real(gz, h)
+    ref = (gz.reshape(F, -1).double().to(torch.complex128) @ h.reshape(F, -1).to(torch.complex128).mH)
+    ref = ref.cpu().numpy()
+    e32 = rel_err((gz.reshape(F, -1).to(torch.complex64) @ h.reshape(F, -1).mH).cpu().numpy(), ref)
+    assert_close(gw.cpu().numpy().astype(np.complex128), ref, max(2e-5, 3 * e32), "full layer, gz real")
+    assert torch.equal(gw, ops.projection_weight_grad_real(gz, h))
