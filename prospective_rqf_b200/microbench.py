@@ -92,6 +92,19 @@ def make_case(op: str, F: int, B: int, T: int, groups: int = 8, truncated: bool 
             rqf.selective_backward(z, inputs, ent, gy, gx, True, truncated, None)
         return run
 
+    if op == "projection_real":  # the readout's real-cotangent GEMMs, beside the complex forms
+        W = (crandn(F, F) / math.sqrt(2 * F))
+        h = crandn(F, B, T)
+        g_real = torch.randn(F, B, T, generator=g).to(dev)
+        g_c = g_real.to(torch.complex64)
+
+        def run():
+            ops.projection_real(W, g_real, True)
+            ops.projection_weight_grad_real(g_real, h)
+            ops.projection(W, g_c, True)
+            ops.projection_weight_grad(g_c, h)
+        return run
+
     if op in ("projection", "projection_torch"):
         W = (crandn(F, F) / math.sqrt(2 * F))
         h, gz, gh = crandn(F, B, T), crandn(F, B, T), crandn(F, B, T)
@@ -158,7 +171,7 @@ def make_case(op: str, F: int, B: int, T: int, groups: int = 8, truncated: bool 
 
 
 OPS = ("fbt", "fbt_raw", "fbt_skip", "tbptt_fbt", "tbptt_btf", "btf", "btf_real", "btf_pro",
-       "selective", "projection", "projection_torch", "mosc")
+       "selective", "projection", "projection_torch", "projection_real", "mosc")
 
 
 def measure(op, F, B, T, iters=10, warmup=3, groups=8, truncated=False) -> dict:
