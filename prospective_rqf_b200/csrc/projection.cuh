@@ -68,7 +68,11 @@ constexpr int kBBytes = kBK * kBNh * 4;           // 8 KB, one of X_hi / X_lo
 constexpr int kStageBytes = 2 * kABytes + 2 * kBBytes;  // 32 KB
 constexpr int kTxBytes = 2 * kABytes + kBBytes;   // bytes the TMA lands per stage
 constexpr int kBarBytes = 256;
-constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;  // + alignment slack
+// Epilogue staging: each epilogue warp turns its 16 output rows x 32 samples
+// into full-line row stores through 4 KB of shared memory.
+constexpr int kStagingBytes = 4 * 4096;
+constexpr int kSmemBytes =
+    kStages * kStageBytes + kBarBytes + kStagingBytes + 1024;  // + alignment slack
 
 constexpr int kErrPipelineTimeout = 7;            // RQF_ERR_PIPELINE_TIMEOUT
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
@@ -501,6 +505,8 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     const bool odd = (row & 1) != 0;
     const uint32_t acce0 = cluster_addr(&acce[0], 0);
     const uint32_t acce1 = cluster_addr(&acce[1], 0);
+    float4 *stage = reinterpret_cast<float4 *>(smem + kStages * kStageBytes + kBarBytes +
+                                               quarter * (kStagingBytes / 4));
     int acc = 0;
     uint32_t acc_phase = 0;
     for (long long tile = pair0; tile < p.num_tiles; tile += npairs) {
@@ -511,90 +517,87 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       tc_fence_after();
       int mp, nt;
       tile_coords(tile, p, mp, nt);
-      const long long j = ((long long)mp * kPairM + (long long)rank * kBM + row) >> 1;
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kBN);
-      if (p.real_x) {
-        // Real X: TMEM lane 2j holds Re and lane 2j+1 Im of out[j, n0 + 0..31];
-        // the even lane writes samples n0 + 0..15, the odd lane n0 + 16..31.
-#pragma unroll 1
-        for (int c = 0; c < kBN / 32; ++c) {
-          float v[32];
-          tc_ld_32x32b_x32(tbase + (uint32_t)(c * 32), v);
-          float r[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            r[i] = __shfl_xor_sync(0xffffffffu, odd ? v[i] : v[16 + i], 1);
-          const long long n0 = (long long)nt * kBN + c * 32 + (odd ? 16 : 0);
-          if (j < p.M && n0 < p.N) {
-            float2 *dst = p.out + j * p.N + n0;
-            const float2 *src = p.acc ? p.acc + j * p.N + n0 : nullptr;
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              float2 z0 = odd ? make_float2(r[2 * q], v[16 + 2 * q]) : make_float2(v[2 * q], r[2 * q]);
-              float2 z1 = odd ? make_float2(r[2 * q + 1], v[16 + 2 * q + 1])
-                              : make_float2(v[2 * q + 1], r[2 * q + 1]);
-              const long long n = n0 + 2 * q;
-              if (n + 2 <= p.N) {
-                if (src) {
-                  const float4 a = reinterpret_cast<const float4 *>(src)[q];
-                  z0 = make_float2(z0.x + a.x, z0.y + a.y);
-                  z1 = make_float2(z1.x + a.z, z1.y + a.w);
-                }
-                reinterpret_cast<float4 *>(dst)[q] = make_float4(z0.x, z0.y, z1.x, z1.y);
-              } else if (n < p.N) {
-                if (src) z0 = make_float2(z0.x + src[2 * q].x, z0.y + src[2 * q].y);
-                dst[2 * q] = z0;
-              }
-            }
-          }
-        }
-      } else {
+      // Each chunk of 32 TMEM columns gives this warp 16 output rows x W
+      // samples (W = 16 complex X, 32 real X).  The lanes combine their
+      // products into complex outputs, stage them in shared memory (16-byte
+      // chunk k of row r at k ^ (r & 7): conflict-free both ways), and write
+      // them back as whole rows, 8 or 16 lanes per row, so every store
+      // instruction covers full 128-byte lines (and so does the acc load).
+      const int W = p.real_x ? 32 : 16;            // samples per row per chunk
+      const int kpr = W / 2;                       // 16-byte chunks per row
+      const long long jw0 = ((long long)mp * kPairM + (long long)rank * kBM + quarter * 32) >> 1;
+      const int r_own = lane >> 1;
+      const int iters = 16 * kpr / 32;             // 16-byte pieces per lane per chunk
 #pragma unroll 1
       for (int c = 0; c < kBN / 32; ++c) {
+        const long long nbase = p.real_x ? (long long)nt * kBN + c * 32
+                                         : (long long)nt * (kBN / 2) + c * 16;
+        // this lane's acc pieces, loaded first so that their latency hides
+        // behind the TMEM load and the staging
+        float4 av[8];
+        if (p.acc) {
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            av[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+            const int e = it * 32 + lane;
+            const int rr = e / kpr, k = e - rr * kpr;
+            const long long jj = jw0 + rr, n = nbase + 2 * k;
+            if (it < iters && jj < p.M && n < p.N)
+              av[it] = *reinterpret_cast<const float4 *>(p.acc + jj * p.N + n);
+          }
+        }
         float v[32];
         tc_ld_32x32b_x32(tbase + (uint32_t)(c * 32), v);
         float r[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) r[i] = __shfl_xor_sync(0xffffffffu, odd ? v[i] : v[16 + i], 1);
-        float2 z[8];
+        if (p.real_x) {
+          // lane 2j holds Re, lane 2j+1 Im of samples 0..31: the even lane
+          // keeps samples 0..15, the odd lane 16..31
 #pragma unroll
-        for (int s = 0; s < 8; ++s) {
-          const float pr_re = odd ? r[2 * s] : v[2 * s];
-          const float pr_im = odd ? r[2 * s + 1] : v[2 * s + 1];
-          const float pi_re = odd ? v[16 + 2 * s] : r[2 * s];
-          const float pi_im = odd ? v[16 + 2 * s + 1] : r[2 * s + 1];
-          z[s] = make_float2(pr_re - pi_im, pr_im + pi_re);
+          for (int q = 0; q < 8; ++q) {
+            const float4 o = odd ? make_float4(r[2 * q], v[16 + 2 * q], r[2 * q + 1], v[17 + 2 * q])
+                                 : make_float4(v[2 * q], r[2 * q], v[2 * q + 1], r[2 * q + 1]);
+            const int k = (odd ? 8 : 0) + q;
+            stage[r_own * kpr + (k ^ (r_own & 7))] = o;
+          }
+        } else {
+          // complex X: P[2j, 2n], P[2j+1, 2n+1] etc. give out[j, n]; the even
+          // lane keeps samples 0..7, the odd lane 8..15
+          float2 z[8];
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            const float pr_re = odd ? r[2 * t] : v[2 * t];
+            const float pr_im = odd ? r[2 * t + 1] : v[2 * t + 1];
+            const float pi_re = odd ? v[16 + 2 * t] : r[2 * t];
+            const float pi_im = odd ? v[16 + 2 * t + 1] : r[2 * t + 1];
+            z[t] = make_float2(pr_re - pi_im, pr_im + pi_re);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int k = (odd ? 4 : 0) + q;
+            stage[r_own * kpr + (k ^ (r_own & 7))] =
+                make_float4(z[2 * q].x, z[2 * q].y, z[2 * q + 1].x, z[2 * q + 1].y);
+          }
         }
-        const long long n0 = (long long)nt * (kBN / 2) + c * 16 + (odd ? 8 : 0);
-        if (j < p.M && n0 < p.N) {
-          float2 *dst = p.out + j * p.N + n0;
-          const float2 *src = p.acc ? p.acc + j * p.N + n0 : nullptr;
-          if (n0 + 8 <= p.N) {
-            if (src) {
+        __syncwarp();
 #pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const float4 a = reinterpret_cast<const float4 *>(src)[q];
-                z[2 * q] = make_float2(z[2 * q].x + a.x, z[2 * q].y + a.y);
-                z[2 * q + 1] = make_float2(z[2 * q + 1].x + a.z, z[2 * q + 1].y + a.w);
-              }
-            }
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-              reinterpret_cast<float4 *>(dst)[q] =
-                  make_float4(z[2 * q].x, z[2 * q].y, z[2 * q + 1].x, z[2 * q + 1].y);
-          } else {
-#pragma unroll
-            for (int s = 0; s < 8; ++s) {
-              if (n0 + s < p.N) {
-                float2 o = z[s];
-                if (src) o = make_float2(o.x + src[s].x, o.y + src[s].y);
-                dst[s] = o;
-              }
+        for (int it = 0; it < 8; ++it) {
+          if (it < iters) {
+            const int e = it * 32 + lane;
+            const int rr = e / kpr, k = e - rr * kpr;
+            float4 o = stage[rr * kpr + (k ^ (rr & 7))];
+            const long long jj = jw0 + rr;
+            const long long n = nbase + 2 * k;  // even; N is even, so n < N covers n + 1
+            if (jj < p.M && n < p.N) {
+              if (p.acc) o = make_float4(o.x + av[it].x, o.y + av[it].y, o.z + av[it].z, o.w + av[it].w);
+              *reinterpret_cast<float4 *>(p.out + jj * p.N + n) = o;
             }
           }
         }
+        __syncwarp();
       }
-      }  // complex X
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? acce1 : acce0);
@@ -676,7 +679,7 @@ struct WgLayout {
   static constexpr int kStages = kRealGz ? 5 : 6;
   static constexpr int kStageBytes = kRealGz ? kWgRawOff + 8192 : kWgRawOff;  // 40 / 32 KB
   static constexpr int kTxBytes = kRealGz ? kWgABytes + 8192 : kWgABytes + kWgHBytes;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + kStagingBytes + 1024;
 };
 // TMEM: columns [0, 256) the CTA's running total, [256, 512) the chunk
 // accumulator.  The tensor core's fp32 accumulate rounds with a bias that
@@ -848,9 +851,10 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
   } else if (warp < 6) {
     // ---------------------------------------------------------- epilogue
     const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
     const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16);
     const uint32_t acce_leader = cluster_addr(acce, 0);
+    float4 *stage = reinterpret_cast<float4 *>(smem + kWgStages * kWgStageBytes + kBarBytes +
+                                               quarter * (kStagingBytes / 4));
     const long long nchunks = (kb1 - kb0 + kWgChunk - 1) / kWgChunk;
     uint32_t cphase = 0;
     bool ok = true;
@@ -875,10 +879,13 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       } else {
         // last chunk: partial = total + chunk; columns 128h + 64q + e hold
-        // (q = 0: Re, 1: Im) of i = i0 + 64h + e
-        const long long j = (long long)mp * kWgPairRows + (long long)rank * kWgRows + row;
-        float2 *dst = p.partials + ((long long)split * p.m_pairs * kWgPairRows + j) * p.ld +
-                      (long long)it * kWgCols;
+        // (q = 0: Re, 1: Im) of i = i0 + 64h + e.  16 outputs of each of the
+        // warp's 32 rows at a time go through shared memory (chunk k of row
+        // r at k ^ (r & 7)) and out as whole 128-byte row pieces.
+        const long long jrow0 =
+            (long long)mp * kWgPairRows + (long long)rank * kWgRows + quarter * 32;
+        float2 *dst0 = p.partials + ((long long)split * p.m_pairs * kWgPairRows + jrow0) * p.ld +
+                       (long long)it * kWgCols;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           const int col = (c >> 1) * 128 + (c & 1) * 32;  // Re columns; Im at col + 64
@@ -895,9 +902,22 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
             for (int i = 0; i < 32; ++i) im[i] += t[i];
           }
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            reinterpret_cast<float4 *>(dst + c * 32)[i] =
-                make_float4(re[2 * i], im[2 * i], re[2 * i + 1], im[2 * i + 1]);
+          for (int half = 0; half < 2; ++half) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const int i = half * 16 + 2 * k;
+              stage[lane * 8 + (k ^ (lane & 7))] = make_float4(re[i], im[i], re[i + 1], im[i + 1]);
+            }
+            __syncwarp();
+#pragma unroll
+            for (int itr = 0; itr < 8; ++itr) {
+              const int e = itr * 32 + lane;
+              const int rr = e >> 3, k = e & 7;
+              *reinterpret_cast<float4 *>(dst0 + (long long)rr * p.ld + c * 32 + half * 16 + 2 * k) =
+                  stage[rr * 8 + (k ^ (rr & 7))];
+            }
+            __syncwarp();
+          }
         }
       }
       tc_fence_before();
