@@ -76,6 +76,40 @@ def _expm1_div_x(x: torch.Tensor, threshold: float = 1e-4) -> torch.Tensor:
     return torch.where(small, taylor, direct)
 
 
+def two_tap_coefficients(log_theta: torch.Tensor, log_gamma: torch.Tensor, dt: float,
+                         tau: float) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """ZOH prospective two-tap coefficients (tau mode, rho = 1) of log-space
+    leaves of any shape (filter.py:510-664): a = (-gamma + i theta (1 - gamma))
+    dt / tau, C1 = e^a, tap0 = gamma (dt/tau) (e^a - 1)/a + gamma C1,
+    tap1 = -gamma C1."""
+    gamma = log_gamma.exp()
+    theta = log_theta.exp()
+    a = torch.complex(-gamma / tau, (theta / tau) * (1.0 - gamma)) * dt
+    c1 = torch.exp(a)
+    b_bar = (dt / tau) * _expm1_div_x(a)
+    extra = gamma * c1  # gamma * rho * C1 with rho = 1
+    tap0 = gamma * b_bar + extra
+    tap1 = -extra
+    return c1.to(torch.complex64), tap0.to(torch.complex64), tap1.to(torch.complex64)
+
+
+def stacked_two_tap(layers) -> list[tuple[torch.Tensor, torch.Tensor, torch.Tensor]]:
+    """two_tap() of every layer, computed once on the stacked (L, F) leaves
+    when the layers share dt, tau and width: the same arithmetic, with one
+    launch per op for the whole stack instead of one per layer (and likewise
+    in the backward)."""
+    layers = list(layers)
+    same = len(layers) > 1 and all(
+        r.dt == layers[0].dt and r.tau == layers[0].tau and
+        r.log_theta.shape == layers[0].log_theta.shape for r in layers)
+    if not same:
+        return [r.two_tap() for r in layers]
+    c1, t0, t1 = two_tap_coefficients(torch.stack([r.log_theta for r in layers]),
+                                      torch.stack([r.log_gamma for r in layers]),
+                                      layers[0].dt, layers[0].tau)
+    return [(c1[i], t0[i], t1[i]) for i in range(len(layers))]
+
+
 class RQFCoefficients(nn.Module):
     """Log-space RQF leaves (resonant recipe, seq_duration set) and their ZOH
     prospective two-tap coefficients (tau mode, rho = 1)."""
@@ -99,15 +133,7 @@ class RQFCoefficients(nn.Module):
         self._gamma_bounds = (math.log(1e-6), math.log(1.0 - 1e-6))
 
     def two_tap(self) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-        gamma = self.log_gamma.exp()
-        theta = self.log_theta.exp()
-        a = torch.complex(-gamma / self.tau, (theta / self.tau) * (1.0 - gamma)) * self.dt
-        c1 = torch.exp(a)
-        b_bar = (self.dt / self.tau) * _expm1_div_x(a)
-        extra = gamma * c1  # gamma * rho * C1 with rho = 1
-        tap0 = gamma * b_bar + extra
-        tap1 = -extra
-        return c1.to(torch.complex64), tap0.to(torch.complex64), tap1.to(torch.complex64)
+        return two_tap_coefficients(self.log_theta, self.log_gamma, self.dt, self.tau)
 
     @torch.no_grad()
     def clamp_parameters(self) -> None:
@@ -299,10 +325,11 @@ class PureRQFEncoderB200(nn.Module):
         x_cf = x.permute(2, 0, 1).reshape(I, B * T)
         w_in, b_in = self.input_proj.weight, self.input_proj.bias
         n = len(self.W)
+        coeffs = stacked_two_tap(self.rqf)
         first = 0
         if (PROJECTION == "tc" and x.is_cuda and n > 0 and I <= LOWRANK_MAX_INPUTS
                 and (B * T) % 2 == 0 and not x.requires_grad):
-            c1, t0, t1 = self.rqf[0].two_tap()
+            c1, t0, t1 = coeffs[0]
             W = self.W[0]
             block = _InputTBPTT if self.scan_grad_mode == "tbptt1" else _InputBlock
             h = block.apply(x_cf, w_in, b_in, W, c1, t0, t1, self.final_activation or n > 1,
@@ -313,7 +340,7 @@ class PureRQFEncoderB200(nn.Module):
             h = proj.reshape(-1, B, T).to(torch.complex64)
         for i in range(first, n):
             act = self.final_activation or i + 1 < n
-            c1, t0, t1 = self.rqf[i].two_tap()
+            c1, t0, t1 = coeffs[i]
             W = self.W[i]
             skip = self.skip and W.shape[0] == W.shape[1]
             if self.scan_grad_mode == "tbptt1":
