@@ -133,6 +133,25 @@ class GradAllReduce:
             off += v.numel()
 
 
+@torch.no_grad()
+def clip_grad_norm_(params, max_norm: float) -> torch.Tensor:
+    """torch.nn.utils.clip_grad_norm_ (train.py:clip_model_grad_norm_
+    :777-789): total = ||(||g_p||)_p||, g *= min(1, max_norm / (total + 1e-6)).
+    Complex gradients enter through their real views, as the reference's own
+    MPS branch does, so all norms are one foreach launch instead of one
+    complex reduction per parameter."""
+    grads = [p.grad for p in params if p.grad is not None]
+    if not grads:
+        return torch.zeros(())
+    if any(g.is_complex() and g.is_conj() for g in grads):
+        return torch.nn.utils.clip_grad_norm_(params, max_norm)
+    views = [torch.view_as_real(g) if g.is_complex() else g for g in grads]
+    total = torch.linalg.vector_norm(torch.stack(torch._foreach_norm(views)))
+    scale = (max_norm / (total + 1e-6)).clamp(max=1.0)
+    torch._foreach_mul_(views, scale)
+    return total
+
+
 class TrainStep:
     """One optimisation step: returns the (detached) loss tensor on device."""
 
@@ -158,7 +177,7 @@ class TrainStep:
         self.opt.zero_grad(set_to_none=True)
         loss.backward()
         self.allreduce()
-        torch.nn.utils.clip_grad_norm_(self.model.parameters(), cfg.clip)
+        clip_grad_norm_(list(self.model.parameters()), cfg.clip)
         self.opt.step()
         self.model.encoder.clamp_parameters()
         return loss.detach()

@@ -145,3 +145,27 @@ def test_synthetic_waveforms_shape_range_and_fresh_batches():
     assert float(x0.abs().max()) <= 1.0 and float(x0.std()) > 0.05
     assert not torch.equal(x0, x1)
     assert torch.equal(next(synthetic_batches(cfg, "cpu", seed=7))[0], x0)
+
+
+def test_clip_grad_norm_matches_torch():
+    """train.clip_grad_norm_ (foreach over real views) equals
+    torch.nn.utils.clip_grad_norm_ on mixed real/complex gradients, clipping
+    and not clipping."""
+    import torch
+
+    from prospective_rqf_b200.train import clip_grad_norm_
+
+    g = torch.Generator().manual_seed(0)
+    for max_norm in (0.5, 1e6):
+        a = [torch.nn.Parameter(torch.randn(5, 4, dtype=torch.complex64, generator=g)),
+             torch.nn.Parameter(torch.randn(7, generator=g)),
+             torch.nn.Parameter(torch.randn(3, 3, dtype=torch.complex64, generator=g))]
+        b = [torch.nn.Parameter(p.detach().clone()) for p in a]
+        for p, q in zip(a, b):
+            p.grad = torch.randn(p.shape, dtype=p.dtype, generator=g)
+            q.grad = p.grad.clone()
+        ta = clip_grad_norm_(a, max_norm)
+        tb = torch.nn.utils.clip_grad_norm_(b, max_norm)
+        assert torch.allclose(ta, tb, rtol=1e-6)
+        for p, q in zip(a, b):
+            assert torch.allclose(p.grad, q.grad, rtol=1e-6, atol=1e-7)
