@@ -381,6 +381,20 @@ size_t rqf_projection_weight_grad_real_workspace_bytes(int64_t m, int64_t k, int
 int rqf_projection_weight_grad_real(const float *gz, const float *x, float *gw, int64_t m,
                                     int64_t k, int64_t n, void *workspace, rqf_stream_t stream);
 
+/* The readout hidden layer's forward GEMM, W1 [Re x; Im x] = Re(W x) with W
+ * = W1[:, :F] - i W1[:, F:] (train.py:ComplexReadoutClassifier :126-136):
+ *
+ *   out[j, n] = Re sum_k w[j, k] * x[k, n]                          float32 (m x n)
+ *
+ * w (m x k) and x (k x n) complex64.  x is split into its Re and Im planes in
+ * shared memory, so the tensor cores do the real product only (half the work
+ * of rqf_projection, whose imaginary part the readout discards).  n a
+ * multiple of 4; `workspace` needs rqf_projection_real_out_workspace_bytes(m,
+ * k) bytes. */
+size_t rqf_projection_real_out_workspace_bytes(int64_t m, int64_t k);
+int rqf_projection_real_out(const float *w, const float *x, float *out, int64_t m, int64_t k,
+                            int64_t n, void *workspace, rqf_stream_t stream);
+
 /* First block over a low-rank input projection (pure.py:_forward_fbt_stack
  * :522-534: proj = w_in @ x_cf (+ b_in), h = proj.to(complex64), then the
  * first block's z = W @ h).  With I = input_dims <= 4:
@@ -412,12 +426,13 @@ int rqf_rowdot(const float *a, const float *x, float *out, void *workspace, int6
 
 /* Hidden layer of the mean-pooled readout (train.py:ComplexReadoutClassifier
  * :74-136, Linear -> ReLU per step, logits mean-pooled over time), given the
- * complex projection z (H x B x T, T contiguous) of the encoder state:
+ * real part Re z (float32, H x B x T, T contiguous) of the projection of the
+ * encoder state (rqf_projection_real_out):
  *
  *   pooled[h, b] = (1/T) sum_t relu(Re z[h, b, t] + bias[h])      float32 (H x B)
  *   mask[(h B + b) W + t/32] bit t%32 = (Re z + bias > 0),  W = ceil(T/32)
  *
- * bias may be null.  One pass over z; fixed-order reduction. */
+ * bias may be null.  One pass over Re z; fixed-order reduction. */
 int rqf_readout_relu_pool(const float *z, const float *bias, uint32_t *mask, float *pooled,
                           int64_t h, int64_t batch, int64_t time, rqf_stream_t stream);
 /* Its backward: g[h, b, t] = mask ? scale[h, b] : 0 (float32, the real

@@ -96,6 +96,8 @@ SIGNATURES: dict[str, tuple] = {
     "rqf_projection_real": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _int, _p, _p]),
     "rqf_projection_weight_grad_real_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "rqf_projection_weight_grad_real": (_int, [_p, _p, _p, _i64, _i64, _i64, _p, _p]),
+    "rqf_projection_real_out_workspace_bytes": (_sz, [_i64, _i64]),
+    "rqf_projection_real_out": (_int, [_p, _p, _p, _i64, _i64, _i64, _p, _p]),
     "rqf_readout_relu_pool": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _p]),
     "rqf_readout_relu_pool_backward": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _p]),
 }

@@ -71,8 +71,21 @@ constexpr int kBarBytes = 256;
 // Epilogue staging: each epilogue warp turns its 16 output rows x 32 samples
 // into full-line row stores through 4 KB of shared memory.
 constexpr int kStagingBytes = 4 * 4096;
-constexpr int kSmemBytes =
-    kStages * kStageBytes + kBarBytes + kStagingBytes + 1024;  // + alignment slack
+// Real-output mode (Re(op(W) x) as float32, for the readout's hidden layer):
+// a stage also holds the raw x tile, 8 complex k rows x 128 samples (Re, Im
+// interleaved, no swizzle), which the transform splits into the Re and Im
+// planes of B; A = [Re op(W) | -Im op(W)] per k-block of 8 complex k.
+constexpr int kRawXBytes = 8 * kBNh * 2 * 4;     // 8 KB
+constexpr int kRawXOff = kStageBytes;            // after the four operand tiles
+template <bool kRealOut>
+struct ProjLayout {
+  static constexpr int kStages = kRealOut ? 5 : 6;
+  static constexpr int kStageBytes = kRealOut ? ::rqf::proj::kStageBytes + kRawXBytes
+                                              : ::rqf::proj::kStageBytes;  // 40 / 32 KB
+  static constexpr int kSmemBytes =
+      kStages * kStageBytes + kBarBytes + kStagingBytes + 1024;  // + alignment slack
+};
+constexpr int kSmemBytes = ProjLayout<false>::kSmemBytes;
 
 constexpr int kErrPipelineTimeout = 7;            // RQF_ERR_PIPELINE_TIMEOUT
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
@@ -93,6 +106,7 @@ struct Params {
   long long num_tiles;
   int a_rows_pad;      // rows of the hi half of the split A' buffer (a multiple of kPairM)
   int real_x;          // X real (K x N): columns are samples, not (Re, Im) pairs
+  float *out_real;     // real-output mode: Re(op(W) x), float32 (M x N)
 };
 
 // ------------------------------------------------------------ PTX wrappers
@@ -345,6 +359,26 @@ __global__ void proj_prep_kernel(const float2 *__restrict__ W, float *__restrict
   }
 }
 
+// Real-output A: row j, k-block b (16 columns) = [Re W[j, 8b..8b+8) |
+// -Im W[j, 8b..8b+8)], hi in rows [0, rows_pad), lo in [rows_pad, 2 rows_pad).
+__global__ void proj_prep_real_out_kernel(const float2 *__restrict__ W, float *__restrict__ a_split,
+                                          long long M, int K, int rows_pad, int k3_pad) {
+  const long long total = (long long)rows_pad * k3_pad;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / k3_pad;
+    const int c = (int)(i - r * k3_pad);
+    const int e = c & 15, k = (c >> 4) * 8 + (e & 7);
+    float v = 0.f;
+    if (r < M && k < K) {
+      const float2 w = W[r * K + k];
+      v = e < 8 ? w.x : -w.y;
+    }
+    a_split[i] = v;
+    a_split[total + i] = tf32_lo(v);
+  }
+}
+
 // ------------------------------------------------------------ main kernel
 // Pair tile t covers A' rows [mp*256, mp*256+256) and X' columns
 // [nt*256, nt*256+256); the pair tiles of one X' column block are neighbours
@@ -354,9 +388,21 @@ __device__ __forceinline__ void tile_coords(long long tile, const Params &p, int
   nt = (int)(tile / p.m_pairs);
 }
 
+// Byte offset of element (column c, row k) of an MN-major 32-bit operand tile
+// of kBK rows in the 128-byte swizzle of 32-byte atoms: 32-column blocks of
+// kBK rows x 128 bytes, 32-byte atom (c & 31) >> 3 of row k at that ^ (k & 3).
+__device__ __forceinline__ uint32_t mn32_offset(int c, int k) {
+  return (uint32_t)((c >> 5) * (kBK * 128) + k * 128 + ((((c & 31) >> 3) ^ (k & 3)) << 5) +
+                    ((c & 7) << 2));
+}
+
+template <bool kRealOut>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmX,
             const Params p) {
+  using L = ProjLayout<kRealOut>;
+  constexpr int kStages = L::kStages;
+  constexpr int kStageBytes = L::kStageBytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -419,10 +465,14 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           mbar_expect_tx(&full[stage], kTxBytes);
           tma_load_2d(st, &tmA, &full[stage], kb * kBK, arow);
           tma_load_2d(st + kABytes, &tmA, &full[stage], kb * kBK, p.a_rows_pad + arow);
+          if (kRealOut) {  // samples [xcol, xcol + 128) of complex rows [8 kb, 8 kb + 8)
+            tma_load_2d(st + kRawXOff, &tmX, &full[stage], 2 * xcol, kb * (kBK / 2));
+          } else {
 #pragma unroll
-          for (int i = 0; i < kNBlocks; ++i)
-            tma_load_2d(st + 2 * kABytes + i * (kBK * 128), &tmX, &full[stage], xcol + i * 32,
-                        kb * kBK);
+            for (int i = 0; i < kNBlocks; ++i)
+              tma_load_2d(st + 2 * kABytes + i * (kBK * 128), &tmX, &full[stage], xcol + i * 32,
+                          kb * kBK);
+          }
           ++issued;
           if (++stage == kStages) {
             stage = 0;
@@ -524,6 +574,32 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       // chunk k of row r at k ^ (r & 7): conflict-free both ways), and write
       // them back as whole rows, 8 or 16 lanes per row, so every store
       // instruction covers full 128-byte lines (and so does the acc load).
+      if (kRealOut) {
+        // lane = output row jr; each chunk is 32 consecutive samples of it,
+        // staged (chunk k of row r at k ^ (r & 7)) and written as whole
+        // 128-byte row pieces, 8 lanes per row
+        const long long jr0 = (long long)mp * kPairM + (long long)rank * kBM + quarter * 32;
+#pragma unroll 1
+        for (int c = 0; c < kBN / 32; ++c) {
+          float v[32];
+          tc_ld_32x32b_x32(tbase + (uint32_t)(c * 32), v);
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            stage[lane * 8 + (k ^ (lane & 7))] =
+                make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+          __syncwarp();
+          const long long nbase = (long long)nt * kBN + c * 32;
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int e = it * 32 + lane;
+            const int rr = e >> 3, k = e & 7;
+            const long long jj = jr0 + rr, n = nbase + 4 * k;  // N % 4 == 0
+            if (jj < p.M && n < p.N)
+              *reinterpret_cast<float4 *>(p.out_real + jj * p.N + n) = stage[rr * 8 + (k ^ (rr & 7))];
+          }
+          __syncwarp();
+        }
+      } else {
       const int W = p.real_x ? 32 : 16;            // samples per row per chunk
       const int kpr = W / 2;                       // 16-byte chunks per row
       const long long jw0 = ((long long)mp * kPairM + (long long)rank * kBM + quarter * 32) >> 1;
@@ -598,6 +674,7 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         }
         __syncwarp();
       }
+      }  // complex output
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? acce1 : acce0);
@@ -618,10 +695,30 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         if (!ok) break;
         float4 *xb = reinterpret_cast<float4 *>(smem + stage * kStageBytes + 2 * kABytes);
         float4 *xl = reinterpret_cast<float4 *>(smem + stage * kStageBytes + 2 * kABytes + kBBytes);
+        if (kRealOut) {
+          // raw row k (complex k index 8 kb + k): 128 samples as (Re, Im); B
+          // row k takes the Re plane, row 8 + k the Im plane, 4 samples per
+          // item (16 bytes inside one 32-byte atom of the MN-major layout)
+          const uint8_t *raw = smem + stage * kStageBytes + kRawXOff;
+          uint8_t *bh = reinterpret_cast<uint8_t *>(xb), *bl = reinterpret_cast<uint8_t *>(xl);
 #pragma unroll
-        for (int i = t; i < kBBytes / 16; i += 128) {
-          const float4 v = xb[i];  // stays in place as the hi part
-          xl[i] = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
+          for (int e = t; e < 8 * (kBNh / 4); e += 128) {
+            const int k = e / (kBNh / 4), g4 = e - k * (kBNh / 4);
+            const float4 a = *reinterpret_cast<const float4 *>(raw + k * (kBNh * 8) + g4 * 32);
+            const float4 b = *reinterpret_cast<const float4 *>(raw + k * (kBNh * 8) + g4 * 32 + 16);
+            const float4 re = make_float4(a.x, a.z, b.x, b.z), im = make_float4(a.y, a.w, b.y, b.w);
+            const uint32_t ore = mn32_offset(4 * g4, k), oim = mn32_offset(4 * g4, k + 8);
+            *reinterpret_cast<float4 *>(bh + ore) = re;
+            *reinterpret_cast<float4 *>(bh + oim) = im;
+            *reinterpret_cast<float4 *>(bl + ore) = make_float4(tf32_lo(re.x), tf32_lo(re.y), tf32_lo(re.z), tf32_lo(re.w));
+            *reinterpret_cast<float4 *>(bl + oim) = make_float4(tf32_lo(im.x), tf32_lo(im.y), tf32_lo(im.z), tf32_lo(im.w));
+          }
+        } else {
+#pragma unroll
+          for (int i = t; i < kBBytes / 16; i += 128) {
+            const float4 v = xb[i];  // stays in place as the hi part
+            xl[i] = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
+          }
         }
         // generic-proxy smem writes -> visible to the tensor core (async proxy)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

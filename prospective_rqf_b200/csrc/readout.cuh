@@ -5,15 +5,16 @@
 //
 //   pooled[h, b] = (1/T) sum_t relu(Re z[h, b, t] + bias[h])
 //
-// where z = V h_enc is the complex projection of the encoder state, and its
+// where Re z = Re(V h_enc) is the real part of the complex projection of the
+// encoder state (rqf_projection_real_out writes it as float32), and its
 // backward only needs the ReLU mask:
 //
 //   g[h, b, t] = mask[h, b, t] * gpool[h, b] / T
 //
 // Both kernels work one (h, b) row of T samples per CTA, one 32-sample word of
 // the bit mask per warp iteration (bit t % 32 of word t / 32), and reduce in a
-// fixed order (deterministic).  Both are HBM-bound: the forward reads z once
-// (8 bytes per sample) and writes 1 bit; the backward reads the bit and writes
+// fixed order (deterministic).  Both are HBM-bound: the forward reads Re z
+// once (4 bytes per sample) and writes 1 bit; the backward reads the bit and writes
 // the real cotangent (4 bytes) that the real-operand projection GEMMs take.
 #pragma once
 
@@ -27,19 +28,19 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 
 __global__ void __launch_bounds__(kThreads)
-relu_pool_kernel(const float2 *__restrict__ z, const float *__restrict__ bias,
+relu_pool_kernel(const float *__restrict__ z, const float *__restrict__ bias,
                  uint32_t *__restrict__ mask, float *__restrict__ pooled, int batch,
                  long long T, long long words) {
   const long long row = blockIdx.x;  // h * batch + b
   const float bh = bias ? bias[row / batch] : 0.f;
-  const float2 *zr = z + row * T;
+  const float *zr = z + row * T;
   uint32_t *mr = mask + row * words;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float acc = 0.f;
   for (long long w = warp; w < words; w += kWarps) {
     const long long t = w * 32 + lane;
     float v = 0.f;
-    if (t < T) v = zr[t].x + bh;
+    if (t < T) v = zr[t] + bh;
     const bool on = v > 0.f;
     const uint32_t bits = __ballot_sync(0xffffffffu, on);
     if (lane == 0) mr[w] = bits;

@@ -1105,8 +1105,8 @@ int pair_capacity(const void *kernel, int threads, int smem) {
 }
 
 int proj_pairs_per_device() {
-  return pair_capacity<0>(reinterpret_cast<const void *>(proj::proj_kernel), proj::kThreads,
-                          proj::kSmemBytes);
+  return pair_capacity<0>(reinterpret_cast<const void *>(proj::proj_kernel<false>),
+                          proj::kThreads, proj::kSmemBytes);
 }
 
 }  // namespace
@@ -1194,7 +1194,8 @@ int projection_impl(const float *w, const float *x, const float *acc, float *out
   p.a_rows_pad = (int)g.rows_pad;
   p.real_x = real_x;
   const long long grid = 2 * (p.num_tiles < pairs ? p.num_tiles : pairs);  // whole CTA pairs
-  proj::proj_kernel<<<(unsigned)grid, proj::kThreads, proj::kSmemBytes, st>>>(tmA, tmX, p);
+  p.out_real = nullptr;
+  proj::proj_kernel<false><<<(unsigned)grid, proj::kThreads, proj::kSmemBytes, st>>>(tmA, tmX, p);
   return launch_status();
 }
 
@@ -1212,6 +1213,69 @@ int rqf_projection_real(const float *w, const float *x, const float *acc, float 
                         int64_t k, int64_t n, int conj_transpose, void *workspace,
                         rqf_stream_t stream) {
   return projection_impl(w, x, acc, out, m, k, n, conj_transpose, workspace, stream, 1);
+}
+
+size_t rqf_projection_real_out_workspace_bytes(int64_t m, int64_t k) {
+  if (m <= 0 || k <= 0) return 0;
+  const int64_t rows_pad = ceil_div(m, proj::kPairM) * proj::kPairM;
+  const int64_t k3_pad = ceil_div(k, proj::kBK / 2) * proj::kBK;
+  return (size_t)(2 * rows_pad * k3_pad) * sizeof(float);
+}
+
+int rqf_projection_real_out(const float *w, const float *x, float *out, int64_t m, int64_t k,
+                            int64_t n, void *workspace, rqf_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (m < 0 || k < 0 || n < 0) return RQF_ERR_SHAPE;
+  if (m == 0 || n == 0) return RQF_OK;
+  if (out == nullptr || (k > 0 && (w == nullptr || x == nullptr || workspace == nullptr)))
+    return RQF_ERR_ARGUMENT;
+  if (k == 0)
+    return cudaMemsetAsync(out, 0, (size_t)m * (size_t)n * sizeof(float), st) == cudaSuccess
+               ? RQF_OK
+               : RQF_ERR_LAUNCH;
+  // float4 output stores and the x row pitch (8n bytes): n a multiple of 4
+  if ((n & 3) != 0 || n >= (int64_t(1) << 30) || k > 0x7fffffffLL || m > (int64_t(1) << 40))
+    return RQF_ERR_SHAPE;
+  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(workspace, 16)) return RQF_ERR_ALIGN;
+  const int64_t rows_pad = ceil_div(m, proj::kPairM) * proj::kPairM;
+  const int64_t kblocks = ceil_div(k, proj::kBK / 2);
+  const int64_t k3_pad = kblocks * proj::kBK;
+  if (rows_pad > 0x3fffffffLL || k3_pad > 0x7fffffffLL) return RQF_ERR_SHAPE;
+  const int pairs = pair_capacity<3>(reinterpret_cast<const void *>(proj::proj_kernel<true>),
+                                     proj::kThreads, proj::ProjLayout<true>::kSmemBytes);
+  if (pairs <= 0) return RQF_ERR_LAUNCH;
+  float *a_split = static_cast<float *>(workspace);
+  {
+    const int64_t total = rows_pad * k3_pad;
+    const int64_t blocks = ceil_div(total, 256);
+    proj::proj_prep_real_out_kernel<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, st>>>(
+        reinterpret_cast<const float2 *>(w), a_split, m, (int)k, (int)rows_pad, (int)k3_pad);
+    if (cudaGetLastError() != cudaSuccess) return RQF_ERR_LAUNCH;
+  }
+  CUtensorMap tmA, tmX;
+  if (!encode_map_2d(&tmA, a_split, (uint64_t)k3_pad, (uint64_t)(2 * rows_pad),
+                     (uint64_t)k3_pad * sizeof(float), proj::kBK, proj::kBM,
+                     CU_TENSOR_MAP_SWIZZLE_64B) ||
+      !encode_map_2d(&tmX, x, (uint64_t)(2 * n), (uint64_t)k, (uint64_t)(2 * n) * sizeof(float),
+                     2 * proj::kBNh, proj::kBK / 2, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return RQF_ERR_LAUNCH;
+  proj::Params p;
+  p.out = nullptr;
+  p.acc = nullptr;
+  p.out_real = out;
+  p.M = m;
+  p.N = n;
+  p.K = (int)k;
+  p.m_pairs = (int)(rows_pad / proj::kPairM);
+  p.n_tiles = (int)ceil_div(n, proj::kBN);
+  p.k_blocks = (int)kblocks;
+  p.num_tiles = (long long)p.m_pairs * p.n_tiles;
+  p.a_rows_pad = (int)rows_pad;
+  p.real_x = 0;
+  const long long grid = 2 * (p.num_tiles < pairs ? p.num_tiles : pairs);
+  proj::proj_kernel<true><<<(unsigned)grid, proj::kThreads, proj::ProjLayout<true>::kSmemBytes,
+                            st>>>(tmA, tmX, p);
+  return launch_status();
 }
 
 }  // extern "C"
@@ -1419,9 +1483,8 @@ int rqf_readout_relu_pool(const float *z, const float *bias, uint32_t *mask, flo
   if (rows > 0x7fffffffLL || batch > 0x7fffffffLL) return RQF_ERR_SHAPE;
   if (time == 0) return RQF_ERR_SHAPE;  // the mean over no samples is undefined
   if (z == nullptr || mask == nullptr || pooled == nullptr) return RQF_ERR_ARGUMENT;
-  if (!aligned(z, 8)) return RQF_ERR_ALIGN;
   readout::relu_pool_kernel<<<(unsigned)rows, readout::kThreads, 0, st>>>(
-      reinterpret_cast<const float2 *>(z), bias, mask, pooled, (int)batch, time,
+      z, bias, mask, pooled, (int)batch, time,
       ceil_div(time, 32));
   return launch_status();
 }

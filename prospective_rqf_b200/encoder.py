@@ -392,8 +392,9 @@ class _ReadoutHidden(torch.autograd.Function):
 
 class _ReadoutPooled(torch.autograd.Function):
     """pooled = mean_t relu(W1 [Re h; Im h] + b1), (H, B), for the mean-pooled
-    readout (train.py:ComplexReadoutClassifier :126-136): the projection
-    Re(V h) of _ReadoutHidden, then one pass (rqf_readout_relu_pool) that
+    readout (train.py:ComplexReadoutClassifier :126-136): the real part
+    Re(V h) of _ReadoutHidden's projection (rqf_projection_real_out, which
+    computes only that), then one pass (rqf_readout_relu_pool) that
     keeps only the ReLU mask bits and the time-means.  Backward: the mask
     turns gpool into the real g = mask * gpool / T
     (rqf_readout_relu_pool_backward), which feeds the real-operand forms of
@@ -405,7 +406,7 @@ class _ReadoutPooled(torch.autograd.Function):
     def forward(ctx, h, W1, b1):
         F = h.shape[0]
         V = torch.complex(W1[:, :F], -W1[:, F:]).contiguous()
-        pooled, mask = ops.readout_relu_pool(_project(V, h), b1)
+        pooled, mask = ops.readout_relu_pool(ops.projection_real_out(V, h), b1)
         ctx.save_for_backward(h, V, mask)
         ctx.time = h.shape[2]
         return pooled

@@ -913,12 +913,13 @@ def rowdot(a: torch.Tensor, x: torch.Tensor | None, with_sum: bool = False) -> t
 
 # ------------------------------------------------ mean-pooled readout hidden layer
 def readout_relu_pool(z: torch.Tensor, bias: torch.Tensor | None):
-    """pooled = mean_t relu(Re z + bias[:, None, None]) as float32 (H, B), and
+    """pooled = mean_t relu(z + bias[:, None, None]) as float32 (H, B), and
     the ReLU mask as int32 words (H, B, ceil(T/32)), bit t % 32 of word t / 32,
-    from the complex (H, B, T) projection z in one pass (rqf_readout_relu_pool;
-    train.py:ComplexReadoutClassifier :74-136 with mean pooling)."""
+    from the float32 (H, B, T) pre-activation z = Re(V h) in one pass
+    (rqf_readout_relu_pool; train.py:ComplexReadoutClassifier :74-136 with
+    mean pooling)."""
     dev = _require_cuda(z)
-    zz = _c64(z)
+    zz = z.detach().to(torch.float32).contiguous()
     H, B, T = (int(d) for d in zz.shape)
     words = (T + 31) // 32
     mask = torch.empty((H, B, words), dtype=torch.int32, device=dev)
@@ -1013,3 +1014,29 @@ def projection_weight_grad_real(gz: torch.Tensor, x: torch.Tensor) -> torch.Tens
             _abi.stream_of(g)), "rqf_projection_weight_grad_real")
     _done(dev)
     return gw
+
+
+def projection_real_out(W: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """Re(W @ x) as float32 (M, ...) for complex W (M, K) and x (K, ...): the
+    readout hidden layer's pre-activation W1 [Re h; Im h] with W = W1[:, :F] -
+    i W1[:, F:] (rqf_projection_real_out, half the tensor-core work of the
+    complex projection).  N not a multiple of 4 runs torch.matmul on the GPU."""
+    dev = _require_cuda(W, x)
+    w = _c64(W)
+    xx = _c64(x)
+    M, K = int(w.shape[0]), int(xx.shape[0])
+    if int(w.shape[1]) != K:
+        raise ValueError(f"W {tuple(w.shape)} does not match x {tuple(xx.shape)}")
+    tail = tuple(xx.shape[1:])
+    N = xx.numel() // K if K else 0
+    if N % 4 != 0:
+        return (w @ xx.reshape(K, N)).real.reshape((M,) + tail).contiguous()
+    lib = _abi.load()
+    out = torch.empty((M,) + tail, dtype=torch.float32, device=dev)
+    ws = _scratch(lib.rqf_projection_real_out_workspace_bytes(M, K), dev)
+    with _timing.launch("rqf_projection_real_out", M * N, _nbytes(xx, out)):
+        _abi.check(lib.rqf_projection_real_out(
+            _abi.ptr(w), _abi.ptr(xx), _abi.ptr(out), M, K, N, _abi.ptr(ws),
+            _abi.stream_of(out)), "rqf_projection_real_out")
+    _done(dev)
+    return out

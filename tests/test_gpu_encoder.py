@@ -224,10 +224,10 @@ def test_readout_relu_pool_vs_torch(H, B, T):
     from prospective_rqf_b200 import ops
 
     g = torch.Generator().manual_seed(H * 100 + T)
-    z = _crandn(g, H, B, T)
+    z = torch.randn(H, B, T, generator=g)
     bias = 0.3 * torch.randn(H, generator=g)
     pooled, mask = ops.readout_relu_pool(z.cuda(), bias.cuda())
-    pre = z.real.double() + bias.double()[:, None, None]
+    pre = z.double() + bias.double()[:, None, None]
     ref = torch.relu(pre).mean(dim=2)
     assert_close(pooled.cpu().double().numpy(), ref.numpy(), 1e-6, "pooled")
     on = pre > 0

@@ -205,3 +205,24 @@ def test_weight_grad_real_gz_full_layer_and_deterministic():
     e32 = rel_err((gz.reshape(F, -1).to(torch.complex64) @ h.reshape(F, -1).mH).cpu().numpy(), ref)
     assert_close(gw.cpu().numpy().astype(np.complex128), ref, max(2e-5, 3 * e32), "full layer, gz real")
     assert torch.equal(gw, ops.projection_weight_grad_real(gz, h))
+
+
+@pytest.mark.parametrize("M,K,N", [(64, 32, 256), (37, 50, 1000), (256, 256, 2 * 1112), (5, 3, 4),
+                                   (300, 20, 512)])
+def test_projection_real_out_vs_fp64(M, K, N):
+    """rqf_projection_real_out: Re(W x) as float32 against fp64, normwise
+    relative to the full complex product's scale."""
+    from prospective_rqf_b200 import ops
+
+    g = torch.Generator().manual_seed(M * 13 + K + N)
+    W = _crandn(g, M, K, scale=1 / np.sqrt(2 * K))
+    x = _crandn(g, K, N)
+    out = ops.projection_real_out(W.cuda(), x.cuda())
+    assert out.shape == (M, N) and out.dtype == torch.float32
+    ref = _ref(W, x, False)
+    # max |out - Re(W x)| / max |W x|: the same normalisation as the complex
+    # projection's test (the real part alone is ~1/sqrt(2) of that scale)
+    e = np.max(np.abs(out.cpu().numpy().astype(np.float64) - ref.real)) / np.max(np.abs(ref))
+    assert e <= PROJ_TOL, f"Re(W x): {e:.3e} of max |W x| > {PROJ_TOL:.1e}"
+    out3 = ops.projection_real_out(W.cuda(), x.reshape(K, N // 4, 4).cuda())
+    assert out3.shape == (M, N // 4, 4) and torch.equal(out3.reshape(M, N), out)
