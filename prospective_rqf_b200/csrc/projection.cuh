@@ -765,27 +765,37 @@ constexpr int kWgRows = 128;                     // j rows per CTA
 constexpr int kWgPairRows = 2 * kWgRows;         // j rows per pair tile
 constexpr int kWgCols = 128;                     // i per pair tile
 constexpr int kWgHRows = kWgCols / 2;            // h' rows each CTA stages
-constexpr int kWgABytes = kWgRows * kBK * 4;     // 8 KB: gz' tile (hi or lo)
-constexpr int kWgHBytes = kWgHRows * kBK * 4;    // 4 KB: h' rows (one of h', h~')
-constexpr int kWgRawOff = 2 * kWgABytes + 4 * kWgHBytes;      // 32 KB: the operand regions
 // Real gz (the readout's cotangent): a stage also holds the raw h' tile, 64
 // rows x 16 samples x (Re, Im) = 128-byte rows (128-byte swizzle), which the
 // transform de-interleaves into the Re and -Im planes of B.
+//
+// Complex gz stages 32 k' (128-byte rows, 128-byte swizzle): every row the
+// tile touches is a separate piece of gz or h (rows are N samples apart, 4 MB
+// at the config-5 layer), and a k-block touches 192 such rows per CTA; 128-
+// byte pieces halve the row accesses per byte against 64-byte ones (1.33 ->
+// 1.09 ms at the config-5 layer).  Real gz keeps 16 samples (64-byte rows)
+// beside its raw h tile.
 template <bool kRealGz>
 struct WgLayout {
-  static constexpr int kStages = kRealGz ? 5 : 6;
-  static constexpr int kStageBytes = kRealGz ? kWgRawOff + 8192 : kWgRawOff;  // 40 / 32 KB
-  static constexpr int kTxBytes = kRealGz ? kWgABytes + 8192 : kWgABytes + kWgHBytes;
+  static constexpr int kBKw = kRealGz ? kBK : 2 * kBK;       // k per stage
+  static constexpr int kABytes = kWgRows * kBKw * 4;         // 8 / 16 KB
+  static constexpr int kHBytes = kWgHRows * kBKw * 4;        // 4 / 8 KB
+  static constexpr int kRawOff = 2 * kABytes + 4 * kHBytes;  // 32 / 64 KB
+  static constexpr int kStages = kRealGz ? 5 : 3;
+  static constexpr int kStageBytes = kRealGz ? kRawOff + 8192 : kRawOff;  // 40 / 64 KB
+  static constexpr int kTxBytes = kRealGz ? kABytes + 8192 : kABytes + kHBytes;
+  static constexpr uint64_t kSwz = kRealGz ? kSwizzle64B : 2;   // 2: 128-byte swizzle
+  static constexpr uint32_t kSbo = kRealGz ? 512 : 1024;        // 8 rows
+  static constexpr int kChunk = kRealGz ? 16 : 8;               // k-blocks per fold: 96 MMAs
   static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + kStagingBytes + 1024;
 };
 // TMEM: columns [0, 256) the CTA's running total, [256, 512) the chunk
 // accumulator.  The tensor core's fp32 accumulate rounds with a bias that
 // grows with the number of accumulations into one accumulator (about 2e-4
 // relative after 10^4 of them, against ~5e-6 after 10^2), so the MMAs
-// accumulate kWgChunk k-blocks (6 per k-block) at a time and the epilogue
+// accumulate WgLayout::kChunk k-blocks (96 MMAs) at a time and the epilogue
 // warps fold each chunk into the total with ordinary fp32 adds.
 constexpr int kWgTmemCols = 2 * kBN;
-constexpr int kWgChunk = 16;
 
 struct WgParams {
   float2 *partials;          // [splits][m_pairs*256][ld] complex
@@ -815,6 +825,11 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
   constexpr int kWgStages = L::kStages;
   constexpr int kWgStageBytes = L::kStageBytes;
   constexpr int kWgTxBytes = L::kTxBytes;
+  constexpr int kWgABytes = L::kABytes;
+  constexpr int kWgHBytes = L::kHBytes;
+  constexpr int kWgRawOff = L::kRawOff;
+  constexpr int kWgChunk = L::kChunk;
+  constexpr int kBKw = L::kBKw;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -875,11 +890,11 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
         if (!mbar_wait(&empty[stage], phase ^ 1u, abort, 1)) break;
         uint8_t *st = smem + stage * kWgStageBytes;
         mbar_expect_tx(&full[stage], kWgTxBytes);
-        tma_load_2d(st, &tmG, &full[stage], (int)(kb * kBK), jrow);
+        tma_load_2d(st, &tmG, &full[stage], (int)(kb * kBKw), jrow);
         if (kRealGz)  // h' floats [32 kb, 32 kb + 32): samples [16 kb, 16 kb + 16)
-          tma_load_2d(st + kWgRawOff, &tmH, &full[stage], (int)(kb * 2 * kBK), irow);
+          tma_load_2d(st + kWgRawOff, &tmH, &full[stage], (int)(kb * 2 * kBKw), irow);
         else
-          tma_load_2d(st + kWgABytes, &tmH, &full[stage], (int)(kb * kBK), irow);
+          tma_load_2d(st + kWgABytes, &tmH, &full[stage], (int)(kb * kBKw), irow);
         ++issued;
         if (++stage == kWgStages) {
           stage = 0;
@@ -914,13 +929,13 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
           }
           tc_fence_after();
           const uint32_t st = smem_u32(smem + stage * kWgStageBytes);
-          const uint64_t a_hi = smem_desc(st, 16, 512, kSwizzle64B);
-          const uint64_t b_hi = smem_desc(st + kWgABytes, 16, 512, kSwizzle64B);
-          const uint64_t a_lo = smem_desc(st + kWgABytes + 2 * kWgHBytes, 16, 512, kSwizzle64B);
+          const uint64_t a_hi = smem_desc(st, 16, L::kSbo, L::kSwz);
+          const uint64_t b_hi = smem_desc(st + kWgABytes, 16, L::kSbo, L::kSwz);
+          const uint64_t a_lo = smem_desc(st + kWgABytes + 2 * kWgHBytes, 16, L::kSbo, L::kSwz);
           const uint64_t b_lo =
-              smem_desc(st + 2 * kWgABytes + 2 * kWgHBytes, 16, 512, kSwizzle64B);
+              smem_desc(st + 2 * kWgABytes + 2 * kWgHBytes, 16, L::kSbo, L::kSwz);
 #pragma unroll
-          for (int ks = 0; ks < kBK / kUmmaK; ++ks) {
+          for (int ks = 0; ks < kBKw / kUmmaK; ++ks) {
             const uint64_t dk = (uint64_t)(ks * (kUmmaK * 4) >> 4);  // 32 B along K
             const uint32_t accum = (kb > c0 || ks > 0) ? 1u : 0u;
             tc_mma_pair_tf32(d_tmem, a_hi + dk, b_hi + dk, kIdescKK, accum);

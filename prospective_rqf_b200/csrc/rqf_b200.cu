@@ -1318,7 +1318,8 @@ int wgrad_pairs_per_device() {
 }
 
 inline int64_t wgrad_kblocks(int64_t n, bool real_gz) {
-  return ceil_div(real_gz ? n : 2 * n, proj::kBK);
+  return real_gz ? ceil_div(n, proj::WgLayout<true>::kBKw)
+                 : ceil_div(2 * n, proj::WgLayout<false>::kBKw);
 }
 
 template <bool kRealGz>
@@ -1354,17 +1355,16 @@ int wgrad_impl(const float *gz, const float *x, float *gw, int64_t m, int64_t k,
   const WgGeometry g = wgrad_geometry(m, k, wgrad_kblocks(n, kRealGz), pairs);
   const uint64_t gz_cols = kRealGz ? (uint64_t)n : (uint64_t)(2 * n);
   CUtensorMap tmG, tmH;
-  const bool ok_g = encode_map_2d(&tmG, gz, gz_cols, (uint64_t)m, gz_cols * sizeof(float),
-                                  proj::kBK, proj::kWgRows, CU_TENSOR_MAP_SWIZZLE_64B);
-  // complex gz: h' boxes of 16 floats x 64 rows (64-byte swizzle); real gz:
-  // 32 floats (16 samples) x 64 rows, de-interleaved in shared memory
-  const bool ok_h =
-      kRealGz ? encode_map_2d(&tmH, x, (uint64_t)(2 * n), (uint64_t)k,
-                              (uint64_t)(2 * n) * sizeof(float), 2 * proj::kBK, proj::kWgHRows,
-                              CU_TENSOR_MAP_SWIZZLE_128B)
-              : encode_map_2d(&tmH, x, (uint64_t)(2 * n), (uint64_t)k,
-                              (uint64_t)(2 * n) * sizeof(float), proj::kBK, proj::kWgHRows,
-                              CU_TENSOR_MAP_SWIZZLE_64B);
+  // complex gz: gz' and h' boxes of 32 floats (128-byte swizzle); real gz:
+  // g boxes of 16 samples (64-byte swizzle) and h' boxes of 32 floats (16
+  // samples), de-interleaved in shared memory
+  constexpr int bk = proj::WgLayout<kRealGz>::kBKw;
+  const bool ok_g =
+      encode_map_2d(&tmG, gz, gz_cols, (uint64_t)m, gz_cols * sizeof(float), bk, proj::kWgRows,
+                    kRealGz ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+  const bool ok_h = encode_map_2d(&tmH, x, (uint64_t)(2 * n), (uint64_t)k,
+                                  (uint64_t)(2 * n) * sizeof(float), kRealGz ? 2 * bk : bk,
+                                  proj::kWgHRows, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!ok_g || !ok_h) return RQF_ERR_LAUNCH;
   proj::WgParams p;
   p.partials = static_cast<float2 *>(workspace);
