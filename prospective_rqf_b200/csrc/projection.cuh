@@ -28,18 +28,27 @@
 // right after its TMA load (writing only the lo part), so the activations
 // cross HBM once.
 //
-// CTA (one per SM, persistent over output tiles of 128 A' rows x 256 X'
-// columns = 64 complex outputs x 128 samples):
-//   warp 0      TMA producer: A_hi, A_lo (K-major, 64-byte swizzle) and X'
-//               (MN-major, 128-byte swizzle of 32-byte atoms) stages
-//   warp 1      TMEM owner and MMA issuer (tcgen05.mma.cta_group::1.kind::tf32)
-//   warps 2..5  epilogue: TMEM -> registers, complex combine, (+acc), store
+// CTA pairs (clusters of 2, one CTA per SM, persistent over pair tiles of
+// 256 A' rows x 256 X' columns): each tcgen05.mma.cta_group::2 (M = 256,
+// N = 256, K = 8) is issued by rank 0 and reads each CTA's half of A (its
+// 128 rows) and of B (its 128 columns) at the same shared-memory offsets;
+// each CTA's TMEM holds its 128 rows of D.  Per CTA:
+//   warp 0      TMA producer: A_hi, A_lo (K-major, 64-byte swizzle) and its
+//               X' columns (MN-major, 128-byte swizzle of 32-byte atoms)
+//   warp 1      TMEM allocation (both CTAs) and, in rank 0, the MMA issuer
+//   warps 2..5  epilogue: TMEM -> registers, complex combine, staged through
+//               shared memory into full-line row stores (+acc)
 //   warps 6..9  transform: X' stage -> lo part (the raw stage is the hi part)
-// Four smem stages of K = 16 and two TMEM accumulators (2 x 256 columns), so
-// the epilogue of one tile overlaps the MMAs of the next.  Every mbarrier wait
-// is bounded in time; on expiry the kernel latches RQF_ERR_PIPELINE_TIMEOUT,
-// every role stops, in-flight copies and MMAs are waited for (bounded) and
-// the TMEM is freed before exit.
+// Six shared-memory stages of K = 16 and two TMEM accumulators (2 x 256
+// columns), so the epilogue of one tile overlaps the MMAs of the next.  The
+// peer's transform and epilogue warps arrive on the leader's barriers through
+// the cluster window; the leader's commits arrive on both CTAs' barriers.
+// Variants: a real X (rqf_projection_real: samples, not (Re, Im) pairs) and a
+// real output (rqf_projection_real_out: Re(op(W) X) only, X split into its Re
+// and Im planes by the transform).  Every mbarrier wait is bounded in time;
+// on expiry the kernel latches RQF_ERR_PIPELINE_TIMEOUT, every role stops,
+// in-flight copies and MMAs are waited for (bounded) and the TMEM is freed
+// before exit.
 #pragma once
 
 #include <cuda.h>
