@@ -358,18 +358,20 @@ class PureRQFEncoderB200(nn.Module):
 
 class _ReadoutHidden(torch.autograd.Function):
     """hid = relu(W1 @ [Re h; Im h] + b1) over the (F, B*T) view of h, on the
-    split-TF32 tensor-core projections.
+    split-TF32 tensor-core projections (the real-output forward and the
+    real-operand cotangents; used for per-step logits).
 
     With V = W1[:, :F] - i W1[:, F:] (complex H x F), W1 @ [Re h; Im h] is
-    Re(V h), so the forward is one complex projection whose real part is kept;
-    the input cotangent is V^H g and the weight cotangent P = g h^H gives
+    Re(V h), computed directly (rqf_projection_real_out); with the real
+    cotangent g the input cotangent is V^H g (rqf_projection_real) and the
+    weight cotangent P = g h^H (rqf_projection_weight_grad_real) gives
     [Re P, -Im P].  No [Re; Im] copy of h is made."""
 
     @staticmethod
     def forward(ctx, h, W1, b1):
         F = h.shape[0]
         V = torch.complex(W1[:, :F], -W1[:, F:]).contiguous()
-        pre = _project(V, h).real + b1[:, None, None]
+        pre = ops.projection_real_out(V, h).add_(b1[:, None, None])
         mask = pre > 0
         ctx.save_for_backward(h, V, mask)
         return pre.mul_(mask)
@@ -379,12 +381,11 @@ class _ReadoutHidden(torch.autograd.Function):
     def backward(ctx, ghid):
         h, V, mask = ctx.saved_tensors
         need = ctx.needs_input_grad
-        g = ghid * mask
-        gc = torch.complex(g, torch.zeros_like(g))
-        gh = _project(V, gc, conj_transpose=True) if need[0] else None
+        g = ghid * mask  # real: the real-operand forms of both cotangent GEMMs
+        gh = ops.projection_real(V, g, conj_transpose=True) if need[0] else None
         gW1 = None
         if need[1]:
-            P = _weight_grad(gc, h)
+            P = ops.projection_weight_grad_real(g, h)
             gW1 = torch.cat([P.real, -P.imag], dim=1)
         gb1 = g.sum(dim=(1, 2)) if need[2] else None
         return gh, gW1, gb1
