@@ -260,6 +260,49 @@ def scan_roofline(timer_summary, hbm_peak, peak_kind, traffic):
     }
 
 
+def gemm_roofline(timer_summary):
+    """The projection GEMMs, which take most of the step: fp32-work FLOPs
+    (8 M K N for a complex product, 4 M K N for the real-operand forms) over
+    their summed launch times, against the split-TF32 ceiling: three TF32
+    passes per fp32 product, TF32 at half the measured bf16 rate."""
+    from prospective_rqf_b200.microbench import measured_peaks
+
+    flops = ms = 0.0
+    per = {}
+    for name, s in timer_summary.items():
+        if not s.get("flops"):
+            continue
+        flops += s["flops"]
+        ms += s["total_ms"]
+        per[name] = {"launches": s["launches"], "mean_ms": round(s["mean_ms"], 4),
+                     "tflops": round(s["flops"] / (s["total_ms"] * 1e-3) / 1e12, 1)
+                     if s["total_ms"] else None}
+    if not ms:
+        return None
+    pk = measured_peaks()
+    bf16 = pk.get("bf16_tflops") if pk else None
+    kind = "measured" if bf16 else "fallback"
+    bf16 = bf16 or 1590.0
+    ceiling = bf16 / 2 / 3
+    achieved = flops / (ms * 1e-3) / 1e12
+    out = {"bound": "tensor", "kernel": "projection GEMMs (" + ", ".join(sorted(per)) + ")",
+           "achieved": round(achieved, 1), "peak": round(ceiling, 1), "unit": "TFLOP/s",
+           "frac": round(achieved / ceiling, 4),
+           "peak_kind": f"{kind} bf16 burst {bf16:.0f} TFLOP/s / 2 (TF32) / 3 (split passes)",
+           "flops_unit": "fp32-work FLOPs", "per_kernel": per}
+    if pk and pk.get("bf16_tflops_sustained"):
+        out["frac_vs_sustained"] = round(achieved / (pk["bf16_tflops_sustained"] / 6), 4)
+    return out
+
+
+def safe_gemm_roofline(timer_summary):
+    """gemm_roofline, or {"error": ...}: an informational key never stops the line."""
+    try:
+        return gemm_roofline(timer_summary)
+    except Exception as exc:  # noqa: BLE001
+        return {"error": f"{type(exc).__name__}: {exc}"}
+
+
 def load_traffic(workload):
     """DRAM bytes (read + write) of one scan forward+backward launch pair from
     the committed ncu capture (profiles/traffic.json), or None."""
@@ -384,6 +427,7 @@ def main():
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config_dict(cfg, cfg.batch, world),
         "roofline": roof,
+        "roofline_gemm": safe_gemm_roofline(kt),
         "e2e": {"value": round(samples / (ms_e2e * 1e-3), 3), "unit": "samples/s",
                 "h2d_bytes_per_step": int(x_host.numel() * x_host.element_size()
                                           + y_host.numel() * y_host.element_size()),

@@ -24,6 +24,7 @@ class KernelTimer:
         self.events: dict[str, list[tuple[torch.cuda.Event, torch.cuda.Event]]] = defaultdict(list)
         self.meta: dict[str, list[int]] = defaultdict(list)
         self.nbytes: dict[str, list[int]] = defaultdict(list)
+        self.flops: dict[str, list[int]] = defaultdict(list)
 
     def __enter__(self):
         global _ACTIVE
@@ -45,14 +46,16 @@ class KernelTimer:
             out[name] = {"launches": len(ms), "total_ms": float(sum(ms)),
                          "mean_ms": float(sum(ms) / max(len(ms), 1)),
                          "elements": int(sum(self.meta[name])),
-                         "alg_bytes": int(sum(self.nbytes[name]))}
+                         "alg_bytes": int(sum(self.nbytes[name])),
+                         "flops": int(sum(self.flops[name]))}
         return out
 
 
 @contextmanager
-def launch(name: str, elements: int, nbytes: int = 0):
+def launch(name: str, elements: int, nbytes: int = 0, flops: int = 0):
     """Bracket one kernel launch (no-op unless a KernelTimer is active);
-    `nbytes` = the launch's algorithmic bytes."""
+    `nbytes` = the launch's algorithmic bytes, `flops` its fp32-work FLOPs
+    (GEMMs)."""
     t = _ACTIVE
     if t is None:
         yield
@@ -66,3 +69,4 @@ def launch(name: str, elements: int, nbytes: int = 0):
     t.events[name].append((a, b))
     t.meta[name].append(int(elements))
     t.nbytes[name].append(int(nbytes))
+    t.flops[name].append(int(flops))

@@ -54,6 +54,18 @@ def hbm_peak() -> tuple[float, str]:
     return FALLBACK_HBM_GBS, "fallback"
 
 
+def measured_peaks() -> dict | None:
+    """MEASURED_PEAKS.json beside the package (this pool's measured copy
+    bandwidth and bf16 GEMM rates), or None."""
+    p = Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except ValueError:
+            return None
+    return None
+
+
 def _coeffs(F, dev, g):
     mag = 0.9 + 0.0999 * torch.rand(F, generator=g)
     lam = torch.polar(mag, 2 * math.pi * torch.rand(F, generator=g)).to(torch.complex64)

@@ -824,7 +824,7 @@ def projection(W: torch.Tensor, x: torch.Tensor, conj_transpose: bool = False,
     lib = _abi.load()
     out = torch.empty(out_shape, dtype=torch.complex64, device=dev)
     ws = _scratch(lib.rqf_projection_workspace_bytes(M, K), dev)
-    with _timing.launch("rqf_projection", M * N, _nbytes(xx, out, a)):
+    with _timing.launch("rqf_projection", M * N, _nbytes(xx, out, a), 8 * M * K * N):
         _abi.check(lib.rqf_projection(
             _abi.ptr(w), _abi.ptr(xx), _abi.ptr(a), _abi.ptr(out), M, K, N,
             int(bool(conj_transpose)), _abi.ptr(ws), _abi.stream_of(xx)), "rqf_projection")
@@ -850,7 +850,7 @@ def projection_weight_grad(gz: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
     lib = _abi.load()
     gw = torch.empty((M, K), dtype=torch.complex64, device=dev)
     ws = _scratch(lib.rqf_projection_weight_grad_workspace_bytes(M, K, N), dev)
-    with _timing.launch("rqf_projection_weight_grad", M * N, _nbytes(g, xx, gw)):
+    with _timing.launch("rqf_projection_weight_grad", M * N, _nbytes(g, xx, gw), 8 * M * K * N):
         _abi.check(lib.rqf_projection_weight_grad(
             _abi.ptr(g), _abi.ptr(xx), _abi.ptr(gw), M, K, N, _abi.ptr(ws),
             _abi.stream_of(g)), "rqf_projection_weight_grad")
@@ -982,7 +982,7 @@ def projection_real(W: torch.Tensor, x: torch.Tensor, conj_transpose: bool = Fal
     lib = _abi.load()
     out = torch.empty(out_shape, dtype=torch.complex64, device=dev)
     ws = _scratch(lib.rqf_projection_workspace_bytes(M, K), dev)
-    with _timing.launch("rqf_projection_real", M * N, _nbytes(xx, out, a)):
+    with _timing.launch("rqf_projection_real", M * N, _nbytes(xx, out, a), 4 * M * K * N):
         _abi.check(lib.rqf_projection_real(
             _abi.ptr(w), _abi.ptr(xx), _abi.ptr(a), _abi.ptr(out), M, K, N, int(bool(conj_transpose)),
             _abi.ptr(ws), _abi.stream_of(out)), "rqf_projection_real")
@@ -1008,7 +1008,8 @@ def projection_weight_grad_real(gz: torch.Tensor, x: torch.Tensor) -> torch.Tens
     lib = _abi.load()
     gw = torch.empty((M, K), dtype=torch.complex64, device=dev)
     ws = _scratch(lib.rqf_projection_weight_grad_real_workspace_bytes(M, K, N), dev)
-    with _timing.launch("rqf_projection_weight_grad_real", M * N, _nbytes(g, xx, gw)):
+    with _timing.launch("rqf_projection_weight_grad_real", M * N, _nbytes(g, xx, gw),
+                        4 * M * K * N):
         _abi.check(lib.rqf_projection_weight_grad_real(
             _abi.ptr(g), _abi.ptr(xx), _abi.ptr(gw), M, K, N, _abi.ptr(ws),
             _abi.stream_of(g)), "rqf_projection_weight_grad_real")
@@ -1034,7 +1035,7 @@ def projection_real_out(W: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
     lib = _abi.load()
     out = torch.empty((M,) + tail, dtype=torch.float32, device=dev)
     ws = _scratch(lib.rqf_projection_real_out_workspace_bytes(M, K), dev)
-    with _timing.launch("rqf_projection_real_out", M * N, _nbytes(xx, out)):
+    with _timing.launch("rqf_projection_real_out", M * N, _nbytes(xx, out), 4 * M * K * N):
         _abi.check(lib.rqf_projection_real_out(
             _abi.ptr(w), _abi.ptr(xx), _abi.ptr(out), M, K, N, _abi.ptr(ws),
             _abi.stream_of(out)), "rqf_projection_real_out")

@@ -169,3 +169,23 @@ def test_clip_grad_norm_matches_torch():
         assert torch.allclose(ta, tb, rtol=1e-6)
         for p, q in zip(a, b):
             assert torch.allclose(p.grad, q.grad, rtol=1e-6, atol=1e-7)
+
+
+def test_bench_gemm_roofline_arithmetic():
+    """bench.gemm_roofline: fp32-work FLOPs over the GEMM launch times against
+    the split-TF32 ceiling (bf16 / 2 / 3); non-GEMM launches are ignored."""
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+    import bench
+
+    flops = 10 * 8 * 256 * 256 * 512000
+    r = bench.gemm_roofline({
+        "rqf_projection": {"launches": 10, "total_ms": 10.0, "mean_ms": 1.0, "flops": flops},
+        "rqf_fbt_block_forward": {"launches": 5, "total_ms": 2.5, "mean_ms": 0.5, "flops": 0}})
+    assert r["bound"] == "tensor" and r["unit"] == "TFLOP/s"
+    assert abs(r["achieved"] - flops / 10e-3 / 1e12) < 0.1
+    assert abs(r["frac"] - r["achieved"] / r["peak"]) < 1e-3
+    assert list(r["per_kernel"]) == ["rqf_projection"]
+    assert bench.gemm_roofline({"x": {"launches": 1, "total_ms": 1.0, "mean_ms": 1.0, "flops": 0}}) is None
