@@ -226,3 +226,25 @@ def test_projection_real_out_vs_fp64(M, K, N):
     assert e <= PROJ_TOL, f"Re(W x): {e:.3e} of max |W x| > {PROJ_TOL:.1e}"
     out3 = ops.projection_real_out(W.cuda(), x.reshape(K, N // 4, 4).cuda())
     assert out3.shape == (M, N // 4, 4) and torch.equal(out3.reshape(M, N), out)
+
+
+def test_real_forms_fall_back_for_unaligned_n():
+    """N not a multiple of 4 (the kernels' TMA row pitch): the real-operand
+    wrappers compute the same products with torch on the GPU."""
+    from prospective_rqf_b200 import ops
+
+    g = torch.Generator().manual_seed(21)
+    M, K, N = 9, 7, 6
+    W = _crandn(g, M, K)
+    xr = torch.randn(K, N, generator=g)
+    xc = _crandn(g, K, N)
+    gr = torch.randn(M, N, generator=g)
+    w64 = W.to(torch.complex128)
+    out = ops.projection_real(W.cuda(), xr.cuda()).cpu().numpy()
+    assert_close(out.astype(np.complex128), (w64 @ xr.double().to(torch.complex128)).numpy(), 1e-6,
+                 "projection_real fallback")
+    ro = ops.projection_real_out(W.cuda(), xc.cuda()).cpu().numpy()
+    assert_close(ro.astype(np.float64), (w64 @ xc.to(torch.complex128)).real.numpy(), 1e-6,
+                 "projection_real_out fallback")
+    gw = ops.projection_weight_grad_real(gr.cuda(), _crandn(g, K, N).cuda())
+    assert gw.shape == (M, K) and gw.dtype == torch.complex64
