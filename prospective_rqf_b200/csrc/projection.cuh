@@ -778,24 +778,25 @@ constexpr int kWgHRows = kWgCols / 2;            // h' rows each CTA stages
 // rows x 16 samples x (Re, Im) = 128-byte rows (128-byte swizzle), which the
 // transform de-interleaves into the Re and -Im planes of B.
 //
-// Complex gz stages 32 k' (128-byte rows, 128-byte swizzle): every row the
-// tile touches is a separate piece of gz or h (rows are N samples apart, 4 MB
-// at the config-5 layer), and a k-block touches 192 such rows per CTA; 128-
-// byte pieces halve the row accesses per byte against 64-byte ones (1.33 ->
-// 1.09 ms at the config-5 layer).  Real gz keeps 16 samples (64-byte rows)
-// beside its raw h tile.
+// Both forms stage 32 k per row (128-byte rows, 128-byte swizzle): every row
+// the tile touches is a separate piece of gz or h (rows are N samples apart,
+// 4 MB at the config-5 layer), and a k-block touches 192 such rows per CTA;
+// 128-byte pieces halve the row accesses per byte against 64-byte ones (1.33
+// -> 1.09 ms for the complex form at the config-5 layer).  Real gz lands its
+// raw h tile (64 rows x 32 samples x (Re, Im), two 128-byte boxes) in the
+// B_lo region, which the transform overwrites row by row after reading it.
 template <bool kRealGz>
 struct WgLayout {
-  static constexpr int kBKw = kRealGz ? kBK : 2 * kBK;       // k per stage
-  static constexpr int kABytes = kWgRows * kBKw * 4;         // 8 / 16 KB
-  static constexpr int kHBytes = kWgHRows * kBKw * 4;        // 4 / 8 KB
-  static constexpr int kRawOff = 2 * kABytes + 4 * kHBytes;  // 32 / 64 KB
-  static constexpr int kStages = kRealGz ? 5 : 3;
-  static constexpr int kStageBytes = kRealGz ? kRawOff + 8192 : kRawOff;  // 40 / 64 KB
-  static constexpr int kTxBytes = kRealGz ? kABytes + 8192 : kABytes + kHBytes;
-  static constexpr uint64_t kSwz = kRealGz ? kSwizzle64B : 2;   // 2: 128-byte swizzle
-  static constexpr uint32_t kSbo = kRealGz ? 512 : 1024;        // 8 rows
-  static constexpr int kChunk = kRealGz ? 16 : 8;               // k-blocks per fold: 96 MMAs
+  static constexpr int kBKw = 2 * kBK;                       // k (k' or samples) per stage
+  static constexpr int kABytes = kWgRows * kBKw * 4;         // 16 KB
+  static constexpr int kHBytes = kWgHRows * kBKw * 4;        // 8 KB
+  static constexpr int kRawOff = 2 * kABytes + 2 * kHBytes;  // 48 KB: the B_lo region
+  static constexpr int kStages = 3;
+  static constexpr int kStageBytes = 2 * kABytes + 4 * kHBytes;  // 64 KB
+  static constexpr int kTxBytes = kRealGz ? kABytes + 2 * kHBytes : kABytes + kHBytes;
+  static constexpr uint64_t kSwz = 2;                        // 128-byte swizzle
+  static constexpr uint32_t kSbo = 1024;                     // 8 rows of 128 bytes
+  static constexpr int kChunk = 8;                           // k-blocks per fold: 96 MMAs
   static constexpr int kSmemBytes = kStages * kStageBytes + kBarBytes + kStagingBytes + 1024;
 };
 // TMEM: columns [0, 256) the CTA's running total, [256, 512) the chunk
@@ -900,9 +901,11 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
         uint8_t *st = smem + stage * kWgStageBytes;
         mbar_expect_tx(&full[stage], kWgTxBytes);
         tma_load_2d(st, &tmG, &full[stage], (int)(kb * kBKw), jrow);
-        if (kRealGz)  // h' floats [32 kb, 32 kb + 32): samples [16 kb, 16 kb + 16)
+        if (kRealGz) {  // h' floats [64 kb, 64 kb + 64): samples [32 kb, 32 kb + 32)
           tma_load_2d(st + kWgRawOff, &tmH, &full[stage], (int)(kb * 2 * kBKw), irow);
-        else
+          tma_load_2d(st + kWgRawOff + kWgHBytes, &tmH, &full[stage], (int)(kb * 2 * kBKw + kBKw),
+                      irow);
+        } else
           tma_load_2d(st + kWgABytes, &tmH, &full[stage], (int)(kb * kBKw), irow);
         ++issued;
         if (++stage == kWgStages) {
@@ -1065,23 +1068,34 @@ proj_wgrad_kernel(const __grid_constant__ CUtensorMap tmG, const __grid_constant
 #pragma unroll
       for (int i = t; i < kAChunks; i += 128) al[i] = tf32_lo4(ah[i]);
       if (kRealGz) {
-        // raw row r (128 bytes): chunk q holds samples 2q, 2q+1 as (Re, Im,
-        // Re, Im), stored at chunk q ^ (r & 7).  Output chunk c of a 64-byte
-        // plane row holds samples 4c..4c+3, stored at c ^ ((r >> 1) & 3).
-        const uint8_t *raw = st + kWgRawOff;
+        // One thread per h' row r (t < 64): the raw row is two 128-byte rows
+        // (samples 0..15 and 16..31 as (Re, Im) pairs, 16-byte chunk q of row
+        // r at q ^ (r & 7)) in the B_lo region.  The thread reads all 16 of
+        // its raw chunks first, then writes the Re and -Im planes (chunk c =
+        // samples 4c..4c+3 at c ^ (r & 7)) to B_hi and their lo parts over
+        // its own raw row, so no thread overwrites bytes another still reads.
+        if (t < kWgHRows) {
+          const int r = t, sw = r & 7;
+          const uint8_t *raw = st + kWgRawOff + r * 128;
+          float4 v[16];
 #pragma unroll
-        for (int e = t; e < kWgHRows * 4; e += 128) {
-          const int r = e >> 2, c = e & 3;
-          const float4 v0 = *reinterpret_cast<const float4 *>(raw + r * 128 + (((2 * c) ^ (r & 7)) << 4));
-          const float4 v1 =
-              *reinterpret_cast<const float4 *>(raw + r * 128 + (((2 * c + 1) ^ (r & 7)) << 4));
-          const float4 re = make_float4(v0.x, v0.z, v1.x, v1.z);
-          const float4 im = make_float4(-v0.y, -v0.w, -v1.y, -v1.w);
-          const int o = r * 4 + (c ^ ((r >> 1) & 3));  // float4 index in a 4 KB plane
-          bh[o] = re;
-          bh[kHChunks + o] = im;
-          bl[o] = tf32_lo4(re);
-          bl[kHChunks + o] = tf32_lo4(im);
+          for (int q = 0; q < 8; ++q) {
+            v[q] = *reinterpret_cast<const float4 *>(raw + ((q ^ sw) << 4));
+            v[8 + q] = *reinterpret_cast<const float4 *>(raw + kWgHBytes + ((q ^ sw) << 4));
+          }
+          uint8_t *hre = st + kWgABytes + r * 128, *him = hre + kWgHBytes;
+          uint8_t *lre = st + kWgRawOff + r * 128, *lim = lre + kWgHBytes;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const float4 a0 = v[2 * c], a1 = v[2 * c + 1];
+            const float4 re = make_float4(a0.x, a0.z, a1.x, a1.z);
+            const float4 im = make_float4(-a0.y, -a0.w, -a1.y, -a1.w);
+            const int o = (c ^ sw) << 4;
+            *reinterpret_cast<float4 *>(hre + o) = re;
+            *reinterpret_cast<float4 *>(him + o) = im;
+            *reinterpret_cast<float4 *>(lre + o) = tf32_lo4(re);
+            *reinterpret_cast<float4 *>(lim + o) = tf32_lo4(im);
+          }
         }
       } else {
 #pragma unroll

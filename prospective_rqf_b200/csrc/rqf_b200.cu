@@ -1355,16 +1355,15 @@ int wgrad_impl(const float *gz, const float *x, float *gw, int64_t m, int64_t k,
   const WgGeometry g = wgrad_geometry(m, k, wgrad_kblocks(n, kRealGz), pairs);
   const uint64_t gz_cols = kRealGz ? (uint64_t)n : (uint64_t)(2 * n);
   CUtensorMap tmG, tmH;
-  // complex gz: gz' and h' boxes of 32 floats (128-byte swizzle); real gz:
-  // g boxes of 16 samples (64-byte swizzle) and h' boxes of 32 floats (16
-  // samples), de-interleaved in shared memory
+  // boxes of 32 floats x rows, 128-byte swizzle: gz' and h' (complex gz), or
+  // g (32 samples) and h' (two boxes per stage: 32 samples as (Re, Im) pairs,
+  // de-interleaved in shared memory) for real gz
   constexpr int bk = proj::WgLayout<kRealGz>::kBKw;
-  const bool ok_g =
-      encode_map_2d(&tmG, gz, gz_cols, (uint64_t)m, gz_cols * sizeof(float), bk, proj::kWgRows,
-                    kRealGz ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+  const bool ok_g = encode_map_2d(&tmG, gz, gz_cols, (uint64_t)m, gz_cols * sizeof(float), bk,
+                                  proj::kWgRows, CU_TENSOR_MAP_SWIZZLE_128B);
   const bool ok_h = encode_map_2d(&tmH, x, (uint64_t)(2 * n), (uint64_t)k,
-                                  (uint64_t)(2 * n) * sizeof(float), kRealGz ? 2 * bk : bk,
-                                  proj::kWgHRows, CU_TENSOR_MAP_SWIZZLE_128B);
+                                  (uint64_t)(2 * n) * sizeof(float), bk, proj::kWgHRows,
+                                  CU_TENSOR_MAP_SWIZZLE_128B);
   if (!ok_g || !ok_h) return RQF_ERR_LAUNCH;
   proj::WgParams p;
   p.partials = static_cast<float2 *>(workspace);
