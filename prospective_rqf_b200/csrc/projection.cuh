@@ -39,7 +39,8 @@
 //   warps 2..5  epilogue: TMEM -> registers, complex combine, staged through
 //               shared memory into full-line row stores (+acc)
 //   warps 6..9  transform: X' stage -> lo part (the raw stage is the hi part)
-// Six shared-memory stages of K = 16 and two TMEM accumulators (2 x 256
+// Six shared-memory stages of K = 16 (five of 40 KB in the real-output
+// form) and two TMEM accumulators (2 x 256
 // columns), so the epilogue of one tile overlaps the MMAs of the next.  The
 // peer's transform and epilogue warps arrive on the leader's barriers through
 // the cluster window; the leader's commits arrive on both CTAs' barriers.
@@ -759,7 +760,7 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 // with h~'[i,2n] = -Im h[i,n] and h~'[i,2n+1] = Re h[i,n].  A CTA pair owns a
 // work tile of 256 j x 128 i: A = gz' (each CTA 128 j rows), B = 256 columns,
 // CTA r's half being [h' ; h~'] of the 64 rows i0 + 64r + [0, 64).  Both
-// operands are K-major, as TMA lands them (64-byte swizzle): h' is its own hi
+// operands are K-major, as TMA lands them (128-byte swizzle): h' is its own hi
 // part, and h~' is a swap-and-negate of each (Re, Im) pair inside a 16-byte
 // chunk, so the transform warps only rewrite chunks in place order (lo parts
 // and h~'), with no transpose.  Each CTA's TMEM holds D[j][c] for its 128 j:
@@ -768,8 +769,8 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 // partial tile and proj_wgrad_reduce_kernel sums the partials in a fixed
 // order (deterministic).
 //
-// Stage (32 KB per CTA): A_hi = gz' (TMA, 8 KB) | B_hi = h' (TMA, 4 KB), h~'
-// (4 KB) | A_lo (8 KB) | B_lo = h'_lo, h~'_lo (8 KB).
+// Stage (64 KB per CTA, 32 k' per row): A_hi = gz' (TMA, 16 KB) | B_hi = h'
+// (TMA, 8 KB), h~' (8 KB) | A_lo (16 KB) | B_lo = h'_lo, h~'_lo (16 KB).
 constexpr int kWgRows = 128;                     // j rows per CTA
 constexpr int kWgPairRows = 2 * kWgRows;         // j rows per pair tile
 constexpr int kWgCols = 128;                     // i per pair tile
