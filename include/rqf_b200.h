@@ -443,6 +443,24 @@ int rqf_readout_relu_pool_backward(const uint32_t *mask, const float *scale, flo
                                    float *counts, int64_t h, int64_t batch, int64_t time,
                                    rqf_stream_t stream);
 
+/* ZOH prospective two-tap coefficients of n log-space leaves (tau mode, rho =
+ * 1; filter.py:510-664, the torch expressions of RQF.two_tap):
+ *
+ *   a = (dt/tau) (-gamma + i theta (1 - gamma)),  gamma = e^lg, theta = e^lt
+ *   c1 = e^a,  tap0 = gamma ((dt/tau) (e^a - 1)/a + c1),  tap1 = -gamma c1
+ *
+ * (e^a - 1)/a takes the reference's 4th-order Taylor form below |a| = 1e-4.
+ * Outputs complex64; computed in double.  The backward takes complex
+ * cotangents (each may be null) and writes the real gradients of the leaves:
+ * grad p = sum over outputs of Re(conj(d out / d p) * grad_out). */
+int rqf_two_tap_coefficients(const float *log_theta, const float *log_gamma, float *c1, float *tap0,
+                             float *tap1, int64_t n, double dt, double tau, rqf_stream_t stream);
+int rqf_two_tap_coefficients_backward(const float *log_theta, const float *log_gamma,
+                                      const float *grad_c1, const float *grad_tap0,
+                                      const float *grad_tap1, float *grad_log_theta,
+                                      float *grad_log_gamma, int64_t n, double dt, double tau,
+                                      rqf_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

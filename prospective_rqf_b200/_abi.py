@@ -19,6 +19,7 @@ _i64 = ctypes.c_int64
 _int = ctypes.c_int
 _sz = ctypes.c_size_t
 _f32 = ctypes.c_float
+_f64 = ctypes.c_double
 
 
 class SelectiveOptions(ctypes.Structure):
@@ -98,6 +99,9 @@ SIGNATURES: dict[str, tuple] = {
     "rqf_projection_weight_grad_real": (_int, [_p, _p, _p, _i64, _i64, _i64, _p, _p]),
     "rqf_projection_real_out_workspace_bytes": (_sz, [_i64, _i64]),
     "rqf_projection_real_out": (_int, [_p, _p, _p, _i64, _i64, _i64, _p, _p]),
+    "rqf_two_tap_coefficients": (_int, [_p, _p, _p, _p, _p, _i64, _f64, _f64, _p]),
+    "rqf_two_tap_coefficients_backward": (
+        _int, [_p, _p, _p, _p, _p, _p, _p, _i64, _f64, _f64, _p]),
     "rqf_readout_relu_pool": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _p]),
     "rqf_readout_relu_pool_backward": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _p]),
 }

@@ -15,6 +15,7 @@
 #include "btf_stream.cuh"
 #include "fbt_rows.cuh"
 #include "fbt_scan.cuh"
+#include "coeffs.cuh"
 #include "lowrank.cuh"
 #include "readout.cuh"
 #include "reduce.cuh"
@@ -1499,6 +1500,43 @@ int rqf_readout_relu_pool_backward(const uint32_t *mask, const float *scale, flo
   if (mask == nullptr || scale == nullptr || gc == nullptr) return RQF_ERR_ARGUMENT;
   readout::relu_pool_backward_kernel<<<(unsigned)rows, readout::kThreads, 0, st>>>(
       mask, scale, gc, counts, time, ceil_div(time, 32));
+  return launch_status();
+}
+
+}  // extern "C"
+
+// ------------------------------------------------ two-tap coefficient producer
+extern "C" {
+
+int rqf_two_tap_coefficients(const float *log_theta, const float *log_gamma, float *c1, float *tap0,
+                             float *tap1, int64_t n, double dt, double tau, rqf_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (n < 0 || !(tau > 0.0) || !(dt > 0.0)) return RQF_ERR_ARGUMENT;
+  if (n == 0) return RQF_OK;
+  if (!log_theta || !log_gamma || !c1 || !tap0 || !tap1) return RQF_ERR_ARGUMENT;
+  if (!aligned(c1, 8) || !aligned(tap0, 8) || !aligned(tap1, 8)) return RQF_ERR_ALIGN;
+  coef::two_tap_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(
+      log_theta, log_gamma, reinterpret_cast<float2 *>(c1), reinterpret_cast<float2 *>(tap0),
+      reinterpret_cast<float2 *>(tap1), n, dt / tau);
+  return launch_status();
+}
+
+int rqf_two_tap_coefficients_backward(const float *log_theta, const float *log_gamma,
+                                      const float *grad_c1, const float *grad_tap0,
+                                      const float *grad_tap1, float *grad_log_theta,
+                                      float *grad_log_gamma, int64_t n, double dt, double tau,
+                                      rqf_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (n < 0 || !(tau > 0.0) || !(dt > 0.0)) return RQF_ERR_ARGUMENT;
+  if (n == 0) return RQF_OK;
+  if (!log_theta || !log_gamma || !grad_log_theta || !grad_log_gamma) return RQF_ERR_ARGUMENT;
+  if ((grad_c1 && !aligned(grad_c1, 8)) || (grad_tap0 && !aligned(grad_tap0, 8)) ||
+      (grad_tap1 && !aligned(grad_tap1, 8)))
+    return RQF_ERR_ALIGN;
+  coef::two_tap_backward_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(
+      log_theta, log_gamma, reinterpret_cast<const float2 *>(grad_c1),
+      reinterpret_cast<const float2 *>(grad_tap0), reinterpret_cast<const float2 *>(grad_tap1),
+      grad_log_theta, grad_log_gamma, n, dt / tau);
   return launch_status();
 }
 

@@ -81,7 +81,11 @@ def two_tap_coefficients(log_theta: torch.Tensor, log_gamma: torch.Tensor, dt: f
     """ZOH prospective two-tap coefficients (tau mode, rho = 1) of log-space
     leaves of any shape (filter.py:510-664): a = (-gamma + i theta (1 - gamma))
     dt / tau, C1 = e^a, tap0 = gamma (dt/tau) (e^a - 1)/a + gamma C1,
-    tap1 = -gamma C1."""
+    tap1 = -gamma C1.  CUDA leaves take the fused kernel pair
+    (ops.TwoTapCoefficients); the torch expressions below are the same
+    formulas."""
+    if log_theta.is_cuda:
+        return ops.TwoTapCoefficients.apply(log_theta, log_gamma, dt, tau)
     gamma = log_gamma.exp()
     theta = log_theta.exp()
     a = torch.complex(-gamma / tau, (theta / tau) * (1.0 - gamma)) * dt

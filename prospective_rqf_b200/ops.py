@@ -1041,3 +1041,42 @@ def projection_real_out(W: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
             _abi.stream_of(out)), "rqf_projection_real_out")
     _done(dev)
     return out
+
+
+# ------------------------------------------------ two-tap coefficient producer
+class TwoTapCoefficients(torch.autograd.Function):
+    """(c1, tap0, tap1) complex64 of log-space leaves (log_theta, log_gamma)
+    of any shape (filter.py:510-664, ZOH, tau mode, rho = 1): one forward and
+    one backward launch (rqf_two_tap_coefficients[_backward], double inside)
+    instead of the ~90 small torch kernels of the same expressions."""
+
+    @staticmethod
+    def forward(ctx, log_theta, log_gamma, dt, tau):
+        dev = _require_cuda(log_theta, log_gamma)
+        lt = log_theta.detach().to(torch.float32).contiguous()
+        lg = log_gamma.detach().to(torch.float32).contiguous()
+        if lt.shape != lg.shape:
+            raise ValueError(f"log_theta {tuple(lt.shape)} and log_gamma {tuple(lg.shape)} differ")
+        outs = [torch.empty(lt.shape, dtype=torch.complex64, device=dev) for _ in range(3)]
+        lib = _abi.load()
+        with _timing.launch("rqf_two_tap_coefficients", lt.numel(), 0):
+            _abi.check(lib.rqf_two_tap_coefficients(
+                _abi.ptr(lt), _abi.ptr(lg), *(_abi.ptr(o) for o in outs), lt.numel(), float(dt),
+                float(tau), _abi.stream_of(lt)), "rqf_two_tap_coefficients")
+        _done(dev)
+        ctx.save_for_backward(lt, lg)
+        ctx.dt, ctx.tau = float(dt), float(tau)
+        return tuple(outs)
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, g1, g0, gm):
+        lt, lg = ctx.saved_tensors
+        gs = [None if g is None else _c64(g) for g in (g1, g0, gm)]
+        glt, glg = torch.empty_like(lt), torch.empty_like(lg)
+        lib = _abi.load()
+        _abi.check(lib.rqf_two_tap_coefficients_backward(
+            _abi.ptr(lt), _abi.ptr(lg), *(_abi.ptr(g) for g in gs), _abi.ptr(glt), _abi.ptr(glg),
+            lt.numel(), ctx.dt, ctx.tau, _abi.stream_of(lt)), "rqf_two_tap_coefficients_backward")
+        _done(lt.device)
+        return glt, glg, None, None

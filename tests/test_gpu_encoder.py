@@ -253,6 +253,42 @@ def test_synthetic_waveforms_drawn_on_the_gpu():
     assert int(y.min()) >= 0 and int(y.max()) < 35
 
 
+def test_two_tap_coefficient_kernels_vs_fp64_autograd():
+    """ops.TwoTapCoefficients (rqf_two_tap_coefficients[_backward]) against
+    the same expressions in torch fp64 with autograd: values and the leaves'
+    gradients, over the recipe band and leaves small enough that |a| takes
+    the 4th-order Taylor branch of (e^a - 1)/a."""
+    from prospective_rqf_b200 import ops
+
+    g = torch.Generator().manual_seed(8)
+    dt, tau = 1 / 16000, 5 / 16000
+    lt = torch.cat([torch.rand(200, generator=g) * 7 - 8, torch.full((8,), -12.0)])
+    lg = torch.cat([torch.rand(200, generator=g) * 13.5 - 13.8, torch.full((8,), -13.0)])
+    lt64 = lt.double().requires_grad_(True)
+    lg64 = lg.double().requires_grad_(True)
+    gam, th = lg64.exp(), lt64.exp()
+    a = torch.complex(-gam / tau, (th / tau) * (1.0 - gam)) * dt
+    small = a.abs() < 1e-4
+    safe = torch.where(small, torch.ones_like(a), a)
+    phi = torch.where(small, 1 + a / 2 + a ** 2 / 6 + a ** 3 / 24 + a ** 4 / 120,
+                      (torch.exp(a) - 1) / safe)
+    c1 = torch.exp(a)
+    ref = (c1, gam * (dt / tau) * phi + gam * c1, -gam * c1)
+    assert bool(small.any()) and bool((~small).any())
+    cot = [torch.randn(208, dtype=torch.complex128, generator=g) for _ in range(3)]
+    loss = sum((torch.conj(w) * y).real.sum() for w, y in zip(cot, ref))
+    glt_ref, glg_ref = torch.autograd.grad(loss, (lt64, lg64))
+    ltc, lgc = lt.cuda().requires_grad_(True), lg.cuda().requires_grad_(True)
+    out = ops.TwoTapCoefficients.apply(ltc, lgc, dt, tau)
+    for o, r in zip(out, ref):
+        assert_close(o.detach().cpu().numpy().astype(np.complex128), r.detach().numpy(), 1e-6,
+                     "two-tap coefficients")
+    l2 = sum((torch.conj(w.to(torch.complex64).cuda()) * y).real.sum() for w, y in zip(cot, out))
+    glt, glg = torch.autograd.grad(l2, (ltc, lgc))
+    assert_close(glt.cpu().double().numpy(), glt_ref.numpy(), 1e-5, "grad log_theta")
+    assert_close(glg.cpu().double().numpy(), glg_ref.numpy(), 1e-5, "grad log_gamma")
+
+
 def test_rowdot_and_lowrank_drive_vs_fp64():
     from prospective_rqf_b200 import ops
 
