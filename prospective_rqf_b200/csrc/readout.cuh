@@ -37,14 +37,24 @@ relu_pool_kernel(const float *__restrict__ z, const float *__restrict__ bias,
   uint32_t *mr = mask + row * words;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float acc = 0.f;
-  for (long long w = warp; w < words; w += kWarps) {
-    const long long t = w * 32 + lane;
-    float v = 0.f;
-    if (t < T) v = zr[t] + bh;
-    const bool on = v > 0.f;
-    const uint32_t bits = __ballot_sync(0xffffffffu, on);
-    if (lane == 0) mr[w] = bits;
-    if (on) acc += v;
+  // four words per warp iteration, their loads issued before any is used
+  constexpr int kU = 4;
+  for (long long w0 = warp; w0 < words; w0 += kU * kWarps) {
+    float v[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const long long t = (w0 + u * kWarps) * 32 + lane;
+      v[u] = t < T ? zr[t] : -INFINITY;
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const long long w = w0 + u * kWarps;
+      const float x = v[u] + bh;
+      const bool on = x > 0.f;  // false past T (and for whole words past the end)
+      const uint32_t bits = __ballot_sync(0xffffffffu, on);
+      if (lane == 0 && w < words) mr[w] = bits;
+      if (on) acc += x;
+    }
   }
   __shared__ double red[kThreads];
   red[threadIdx.x] = acc;
