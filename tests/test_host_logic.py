@@ -13,7 +13,9 @@ import torch
 import prospective_rqf_b200 as rqf
 from prospective_rqf_b200 import integration, ops
 
-REFERENCE = Path(os.environ.get("RQF_REFERENCE", "/root/reference"))
+# The reference's modules: its offline install under baseline/_ref (or RQF_REFERENCE).
+REFERENCE = Path(os.environ.get("RQF_REFERENCE",
+                                Path(__file__).resolve().parent.parent / "baseline" / "_ref"))
 
 
 def c(*shape):
