@@ -14,8 +14,13 @@ GPU (H=256, 32 samples/GPU, T=16000, full BPTT), weak scaling over N ranks.
 `e2e`    = the same with each step's inputs copied from pinned host memory and
            the loss read back to the host inside the timed region.
 `roofline` = the scan kernels (fwd + bwd, the backend's own kernels) timed
-           with CUDA events on their launching stream during the timed steps;
-           algorithmic bytes 16 B/element forward + 24 B/element backward.
+           with CUDA events on their launching stream in a separate pass of
+           steps after the timed ones (the events are not in `value`'s
+           region); algorithmic bytes 24 B/element forward (z, skip, out) +
+           24 B/element backward (g, z, gz).
+`triton_reference` = the reference's own model on its stock GPU path (Triton),
+           same B200, same batch shape (N = 1 only), for information;
+`reference_cpu_path` = its own CPU PyTorch path at reduced T, for information.
 """
 
 from __future__ import annotations
@@ -55,13 +60,33 @@ def parse():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", default="cfg5-full", choices=["cfg2", "cfg5-full", "cfg5-tbptt"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-info", action="store_true",
+                    help="skip the reference's own GPU (Triton) and CPU paths, for information")
     return ap.parse_args()
 
 
-def peaks():
-    from prospective_rqf_b200.microbench import hbm_peak
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
 
-    return hbm_peak()
+
+def measured_peaks() -> dict | None:
+    """MEASURED_PEAKS.json beside this file (this pool's measured copy
+    bandwidth and bf16 GEMM rates), or None."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except ValueError:
+            return None
+    return None
+
+
+def hbm_peak() -> tuple[float, str]:
+    """(GB/s, "measured" | "fallback"): the STREAM-style copy bandwidth."""
+    pk = measured_peaks()
+    if pk and pk.get("hbm_gbs"):
+        return float(pk["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
 
 
 # ------------------------------------------------------------------ clocks
@@ -236,7 +261,7 @@ def cpu_reference_steps(cfg, steps: int, warmup: int, batch: int):
 
 
 # ------------------------------------------------------------------- main
-def scan_roofline(timer_summary, hbm_peak, peak_kind, traffic):
+def scan_roofline(timer_summary, peak_gbs, peak_kind, traffic):
     tot_bytes = 0.0
     tot_ms = 0.0
     per = {}
@@ -252,8 +277,8 @@ def scan_roofline(timer_summary, hbm_peak, peak_kind, traffic):
     achieved = tot_bytes / (tot_ms * 1e-3) / 1e9 if tot_ms else 0.0
     return {
         "bound": "hbm", "kernel": "scan fwd+bwd (" + ", ".join(sorted(per)) + ")",
-        "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-        "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
+        "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
+        "frac": round(achieved / peak_gbs, 4), "peak_kind": peak_kind,
         "traffic": traffic, "traffic_unit": "bytes per fwd+bwd launch pair (ncu)",
         "alg_bytes_per_pair": int(sum(v["alg_bytes_per_launch"] for v in per.values())),
         "per_kernel": per,
@@ -263,10 +288,9 @@ def scan_roofline(timer_summary, hbm_peak, peak_kind, traffic):
 def gemm_roofline(timer_summary):
     """The projection GEMMs, which take most of the step: fp32-work FLOPs
     (8 M K N for a complex product, 4 M K N for the real-operand forms) over
-    their summed launch times, against the split-TF32 ceiling: three TF32
-    passes per fp32 product, TF32 at half the measured bf16 rate."""
-    from prospective_rqf_b200.microbench import measured_peaks
-
+    their summed launch times.  One ceiling: the split-TF32 rate derived from
+    the measured SUSTAINED bf16 rate (these GEMMs are timed inside a long
+    step): three TF32 passes per fp32 product, TF32 at half the bf16 rate."""
     flops = ms = 0.0
     per = {}
     for name, s in timer_summary.items():
@@ -279,28 +303,17 @@ def gemm_roofline(timer_summary):
                      if s["total_ms"] else None}
     if not ms:
         return None
-    pk = measured_peaks()
-    bf16 = pk.get("bf16_tflops") if pk else None
-    kind = "measured" if bf16 else "fallback"
-    bf16 = bf16 or 1590.0
+    pk = measured_peaks() or {}
+    bf16 = pk.get("bf16_tflops_sustained")
+    kind = "measured sustained" if bf16 else "fallback burst"
+    bf16 = bf16 or FALLBACK_BF16_TFLOPS
     ceiling = bf16 / 2 / 3
     achieved = flops / (ms * 1e-3) / 1e12
-    out = {"bound": "tensor", "kernel": "projection GEMMs (" + ", ".join(sorted(per)) + ")",
-           "achieved": round(achieved, 1), "peak": round(ceiling, 1), "unit": "TFLOP/s",
-           "frac": round(achieved / ceiling, 4),
-           "peak_kind": f"{kind} bf16 burst {bf16:.0f} TFLOP/s / 2 (TF32) / 3 (split passes)",
-           "flops_unit": "fp32-work FLOPs", "per_kernel": per}
-    if pk and pk.get("bf16_tflops_sustained"):
-        out["frac_vs_sustained"] = round(achieved / (pk["bf16_tflops_sustained"] / 6), 4)
-    return out
-
-
-def safe_gemm_roofline(timer_summary):
-    """gemm_roofline, or {"error": ...}: an informational key never stops the line."""
-    try:
-        return gemm_roofline(timer_summary)
-    except Exception as exc:  # noqa: BLE001
-        return {"error": f"{type(exc).__name__}: {exc}"}
+    return {"bound": "tensor", "kernel": "projection GEMMs (" + ", ".join(sorted(per)) + ")",
+            "achieved": round(achieved, 1), "peak": round(ceiling, 1), "unit": "TFLOP/s",
+            "frac": round(achieved / ceiling, 4),
+            "peak_kind": f"{kind} bf16 {bf16:.0f} TFLOP/s / 2 (TF32) / 3 (split-TF32 passes)",
+            "flops_unit": "fp32-work FLOPs", "per_kernel": per}
 
 
 def load_traffic(workload):
@@ -317,6 +330,9 @@ def load_traffic(workload):
 
 
 def run_reference_arm(args, world, rank):
+    """The reference arm: the CPU restatement of the step (oracle port), on
+    all host cores, rank 0 only; each step a bounded sample of 1 sample of
+    the workload whose config it reports (the same as this backend's arm)."""
     from prospective_rqf_b200.train import WORKLOADS
 
     if rank != 0:
@@ -329,7 +345,7 @@ def run_reference_arm(args, world, rank):
         "ms_per_step": round(dt / args.steps * 1e3, 1), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f64 scan / f32 GEMM", "data": "synthetic",
         "impl": "reference",
-        "config": config_dict(cfg, 1, world),
+        "config": config_dict(cfg, cfg.batch, world),
         "cpu_baseline": {"value": round(sps, 4), "unit": "samples/s", "cores": threads,
                          "kind": "port",
                          "sample": f"1 sample/step of {cfg.name} (T={cfg.time}, H={cfg.hidden}), "
@@ -338,6 +354,158 @@ def run_reference_arm(args, world, rank):
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+# ------------------------------------- the reference's own paths, for information
+REF_INSTALL = ROOT / "baseline" / "_ref"
+
+
+def _reference_modules():
+    """The reference's PureRQFEncoder from its offline install, or None."""
+    if not (REF_INSTALL / "rqf_models").exists():
+        return None
+    if str(REF_INSTALL) not in sys.path:
+        sys.path.insert(0, str(REF_INSTALL))
+    os.environ.setdefault("TRITON_CACHE_DIR", "/tmp/rqf_triton_cache")
+    from rqf_models.backbones.rqf.pure import PureRQFEncoder
+
+    return PureRQFEncoder
+
+
+def _reference_classifier(PureRQFEncoder, cfg, device):
+    """The reference's model for this workload: PureRQFEncoder (the paper
+    recipe, configs/model/pure_rqf_paper.yaml, at the workload's width, depth
+    and gradient mode) under the head that train.py:ComplexReadoutClassifier
+    (:74-136) builds: per-timestep Linear(2F, R) -> ReLU -> Dropout(0) ->
+    Linear(R, C) on [Re h; Im h], logits mean-pooled over time (or per step)."""
+    torch.manual_seed(0)
+    enc = PureRQFEncoder(
+        input_dims=1, output_dims=8, hidden_dims=cfg.hidden, num_layers=cfg.depth,
+        samp_frequency=cfg.samp_frequency, min_freq=1.0, max_freq=8000.0, tau=cfg.tau,
+        discretization="zoh", activation="split_relu", complex_weights=True,
+        param_space="log", seq_duration=1.0, w_init="forward", final_activation=False,
+        input_proj_bias=False, complex_output=True, prospective_input=True,
+        prospective_mode="tau", skip_connection=True, scan_grad_mode=cfg.scan_grad_mode)
+    head = torch.nn.Sequential(torch.nn.Linear(2 * cfg.hidden, cfg.readout_hidden),
+                               torch.nn.ReLU(), torch.nn.Dropout(0.0),
+                               torch.nn.Linear(cfg.readout_hidden, cfg.num_classes))
+    return torch.nn.ModuleDict({"encoder": enc, "head": head}).to(device)
+
+
+def reference_gpu_step(cfg, steps: int, warmup: int, device):
+    """The reference's own model on its stock GPU path (its Triton kernels),
+    one training step as train.py:run_epoch (:792-843) takes it: forward,
+    cross-entropy, backward, clip_grad_norm_, AdamW, clamp_parameters, on
+    the same synthetic batch shape as this backend's arm.  CUDA events."""
+    PureRQFEncoder = _reference_modules()
+    if PureRQFEncoder is None:
+        return {"unavailable": "reference install (baseline/_ref) absent"}
+    from prospective_rqf_b200.train import waveform_batch
+
+    model = _reference_classifier(PureRQFEncoder, cfg, device)
+    model.train()
+    leaves = [p for n, p in model.named_parameters() if "rqf_fwd" in n and p.requires_grad]
+    rest = [p for n, p in model.named_parameters() if "rqf_fwd" not in n and p.requires_grad]
+    opt = torch.optim.AdamW([{"params": rest, "lr": cfg.lr, "weight_decay": cfg.weight_decay},
+                             {"params": leaves, "lr": cfg.lr * cfg.rqf_lr_factor,
+                              "weight_decay": 0.0}], eps=1e-8)
+    g = torch.Generator().manual_seed(1000)
+    x, y = waveform_batch(cfg.batch, cfg.time, cfg.samp_frequency, cfg.num_classes, g)
+    x, y = x.to(device), y.to(device)
+    per_step = cfg.scan_grad_mode == "tbptt1"
+
+    def step():
+        feats = model["encoder"](x)  # (B, T, F) complex
+        B, T, F = feats.shape
+        logits = model["head"](torch.cat([feats.real, feats.imag], dim=-1).reshape(B * T, 2 * F))
+        logits = logits.reshape(B, T, -1)
+        if per_step:
+            loss = torch.nn.functional.cross_entropy(
+                logits.reshape(B * T, -1), y[:, None].expand(B, T).reshape(-1),
+                label_smoothing=cfg.label_smoothing)
+        else:
+            loss = torch.nn.functional.cross_entropy(logits.mean(dim=1), y,
+                                                     label_smoothing=cfg.label_smoothing)
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        torch.nn.utils.clip_grad_norm_(model.parameters(), cfg.clip)
+        opt.step()
+        model["encoder"].clamp_parameters()
+        return loss.detach()
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        loss = step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    del model, opt
+    return {"value": round(steps * cfg.batch / (ms * 1e-3), 3), "unit": "samples/s",
+            "ms_per_step": round(ms / steps, 3), "steps": steps, "warmup": warmup,
+            "loss": round(float(loss), 5), "same_config": True,
+            "what": "the reference's PureRQFEncoder (paper recipe) + the train.py "
+                    "ComplexReadoutClassifier head, full training step on its stock Triton "
+                    "path, same B200, same batch shape, from baseline/_ref"}
+
+
+def reference_cpu_paths(cfg, threads: int):
+    """The reference's own CPU PyTorch path, timed on the host cores:
+    PureRQFEncoder forward+backward (per sample, at reduced T: its CPU
+    backward does not finish a T=16000 sample in minutes) and config 1's
+    sequential_scan op (exact BASELINE shape)."""
+    PureRQFEncoder = _reference_modules()
+    if PureRQFEncoder is None:
+        return {"unavailable": "reference install (baseline/_ref) absent"}
+    from rqf_models.ops.scan import sequential_scan
+
+    torch.set_num_threads(threads)
+    out = {"cores": threads}
+    T = 2000
+    enc = PureRQFEncoder(
+        input_dims=1, output_dims=8, hidden_dims=cfg.hidden, num_layers=cfg.depth,
+        samp_frequency=cfg.samp_frequency, min_freq=1.0, max_freq=8000.0, tau=cfg.tau,
+        discretization="zoh", activation="split_relu", complex_weights=True,
+        param_space="log", seq_duration=1.0, w_init="forward", final_activation=False,
+        input_proj_bias=False, complex_output=True, prospective_input=True,
+        prospective_mode="tau", skip_connection=True, scan_grad_mode=cfg.scan_grad_mode)
+    x = torch.randn(1, T, 1, generator=torch.Generator().manual_seed(0))
+    enc(x).abs().mean().backward()
+    t0 = time.perf_counter()
+    enc(x).abs().mean().backward()
+    dt = time.perf_counter() - t0
+    out["encoder"] = {"value": round(1.0 / dt, 4), "unit": "samples/s",
+                      "shape": f"B=1, T={T}, H={cfg.hidden}, depth {cfg.depth}, "
+                               f"{cfg.scan_grad_mode} BPTT; encoder fwd+bwd only"}
+    g = torch.Generator().manual_seed(0)
+    u = torch.randn(32, 161, 128, generator=g)
+    lam = torch.polar(0.90 + 0.099 * torch.rand(128, generator=g),
+                      torch.pi * torch.rand(128, generator=g)).to(torch.complex64)
+    b = (torch.randn(128, generator=g) + 1j * torch.randn(128, generator=g)).to(
+        torch.complex64) / 2 ** 0.5
+
+    def op():
+        lg, bg, ug = (t.detach().requires_grad_(True) for t in (lam, b, u))
+        (sequential_scan(lg, bg, ug).abs() ** 2).sum().backward()
+    op()
+    t0 = time.perf_counter()
+    for _ in range(3):
+        op()
+    out["config1_sequential_scan"] = {
+        "ms": round((time.perf_counter() - t0) / 3 * 1e3, 3),
+        "shape": "B=32, T=161, H=128, real u, fwd+bwd of sum |y|^2"}
+    return out
+
+
+def safe_info(fn, *a):
+    """An informational key never stops the line."""
+    try:
+        return fn(*a)
+    except Exception as exc:  # noqa: BLE001
+        return {"error": f"{type(exc).__name__}: {exc}"[:300]}
 
 
 def metric_name(cfg):
@@ -383,12 +551,12 @@ def main():
         step(x_dev, y_dev)
     torch.cuda.synchronize()
 
-    # ---- value: inputs resident in HBM
+    # ---- value: inputs resident in HBM; nothing but the steps in the timed region
     stream = torch.cuda.current_stream(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
-    with ClockSampler(device.index) as clocks, _timing.KernelTimer() as timer:
+    with ClockSampler(device.index) as clocks:
         e0.record(stream)
         for _ in range(args.steps):
             loss = step(x_dev, y_dev)
@@ -396,7 +564,6 @@ def main():
         torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(e0.elapsed_time(e1), world)
-    kt = timer.summary()
 
     # ---- e2e: host buffers, H2D of inputs and D2H of the loss every step
     barrier(world)
@@ -411,37 +578,62 @@ def main():
     torch.cuda.synchronize()
     barrier(world)
     ms_e2e = max_over_ranks(f0.elapsed_time(f1), world)
+
+    # ---- kernel pass (not part of `value`): each C-ABI call bracketed by CUDA
+    # events on its launching stream, for the roofline keys and the launch count
+    kpass = max(1, min(args.steps, 5))
+    barrier(world)
+    with _timing.KernelTimer() as timer:
+        for _ in range(kpass):
+            step(x_dev, y_dev)
+        torch.cuda.synchronize()
+    barrier(world)
+    kt = timer.summary()
     rqf.check_device_errors(device)
     if not (loss_val == loss_val):
         raise FloatingPointError("non-finite loss")
 
-    hbm, peak_kind = peaks()
+    hbm, peak_kind = hbm_peak()
     roof = scan_roofline(kt, hbm, peak_kind, load_traffic(cfg.name))
-    launches = sum(s["launches"] * KERNELS_PER_CALL.get(n, 1) for n, s in kt.items())
+    launches_per_step = sum(s["launches"] * KERNELS_PER_CALL.get(n, 1)
+                            for n, s in kt.items()) / kpass
     samples = args.steps * cfg.batch * world
     line = {
         "metric": metric_name(cfg),
         "value": round(samples / (ms * 1e-3), 3), "unit": "samples/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "vs_baseline": None, "dtype": "f32 (split-TF32 GEMMs)", "data": "synthetic",
         "config": config_dict(cfg, cfg.batch, world),
         "roofline": roof,
-        "roofline_gemm": safe_gemm_roofline(kt),
+        "roofline_gemm": safe_info(gemm_roofline, kt),
+        "kernel_pass_steps": kpass,
         "e2e": {"value": round(samples / (ms_e2e * 1e-3), 3), "unit": "samples/s",
                 "h2d_bytes_per_step": int(x_host.numel() * x_host.element_size()
                                           + y_host.numel() * y_host.element_size()),
                 "d2h_bytes_per_step": 4},
-        "gpu_launches": int(launches),
+        "gpu_launches": int(round(launches_per_step * args.steps)),
         "clocks": clocks.summary(),
         "loss": round(loss_val, 5),
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sps, threads, dt = cpu_reference_steps(cfg, steps=2, warmup=1, batch=1)
-        line["cpu_baseline"] = {"value": round(sps, 4), "unit": "samples/s", "cores": threads,
-                                "kind": "port",
-                                "sample": f"1 sample/step x 2 steps of {cfg.name} (T={cfg.time}), "
-                                          "oracle fp64 scan + torch CPU fp32 GEMMs"}
+    if rank == 0 and world == 1:
+        del step
+        torch.cuda.empty_cache()
+        if not args.no_reference_info:
+            line["triton_reference"] = safe_info(reference_gpu_step, cfg, 3, 3, device)
+            tr = line["triton_reference"]
+            if isinstance(tr, dict) and tr.get("value"):
+                tr["value_over_reference"] = round(line["value"] / tr["value"], 3)
+        threads = os.cpu_count() or 1
+        if not args.no_cpu_baseline:
+            sps, threads, dt = cpu_reference_steps(cfg, steps=2, warmup=1, batch=1)
+            line["cpu_baseline"] = {"value": round(sps, 4), "unit": "samples/s",
+                                    "cores": threads, "kind": "port",
+                                    "sample": f"1 sample/step x 2 steps of {cfg.name} "
+                                              f"(T={cfg.time}), oracle fp64 scan + torch CPU "
+                                              "fp32 GEMMs"}
+        if not args.no_reference_info:
+            line["reference_cpu_path"] = safe_info(reference_cpu_paths, cfg, threads)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

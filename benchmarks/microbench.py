@@ -3,7 +3,7 @@ public op per iteration on seeded synthetic inputs, each C-ABI call timed with
 CUDA events on its launching stream, reported as milliseconds per launch and
 achieved algorithmic bandwidth against the measured HBM copy peak.
 
-    python -m prospective_rqf_b200.microbench --op fbt --F 256 --B 32 --T 16000
+    python benchmarks/microbench.py --op fbt --F 256 --B 32 --T 16000
 
 Ops:
   fbt        fbt_recompute_scan (split-ReLU fused), (F,B,T)
@@ -35,35 +35,16 @@ from __future__ import annotations
 import argparse
 import json
 import math
+import sys
 from pathlib import Path
 
 import torch
 
-FALLBACK_HBM_GBS = 6650.0
+ROOT = Path(__file__).resolve().parent.parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
 
-
-def hbm_peak() -> tuple[float, str]:
-    """(GB/s, "measured" | "fallback"): the STREAM-style copy bandwidth of this
-    pool's B200s if MEASURED_PEAKS.json sits beside the package."""
-    p = Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"
-    if p.exists():
-        try:
-            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
-        except (ValueError, KeyError):
-            pass
-    return FALLBACK_HBM_GBS, "fallback"
-
-
-def measured_peaks() -> dict | None:
-    """MEASURED_PEAKS.json beside the package (this pool's measured copy
-    bandwidth and bf16 GEMM rates), or None."""
-    p = Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"
-    if p.exists():
-        try:
-            return json.loads(p.read_text())
-        except ValueError:
-            return None
-    return None
+from bench import hbm_peak, measured_peaks  # noqa: E402
 
 
 def _coeffs(F, dev, g):
@@ -77,7 +58,7 @@ def _coeffs(F, dev, g):
 def make_case(op: str, F: int, B: int, T: int, groups: int = 8, truncated: bool = False):
     """Returns run() performing one forward + backward of `op`."""
     import prospective_rqf_b200 as rqf
-    from . import ops
+    from prospective_rqf_b200 import ops
 
     dev = torch.device("cuda")
     g = torch.Generator().manual_seed(0)
@@ -127,7 +108,7 @@ def make_case(op: str, F: int, B: int, T: int, groups: int = 8, truncated: bool 
                 ops.projection(W, gz, True, gh)
                 ops.projection_weight_grad(gz, h)
         else:
-            from . import _timing
+            from prospective_rqf_b200 import _timing
 
             def run():
                 with _timing.launch("torch_matmul", F * B * T, 16 * F * B * T):
@@ -188,7 +169,7 @@ OPS = ("fbt", "fbt_raw", "fbt_skip", "tbptt_fbt", "tbptt_btf", "btf", "btf_real"
 
 def measure(op, F, B, T, iters=10, warmup=3, groups=8, truncated=False) -> dict:
     import prospective_rqf_b200 as rqf
-    from . import _timing
+    from prospective_rqf_b200 import _timing
 
     run = make_case(op, F, B, T, groups, truncated)
     for _ in range(warmup):
@@ -227,11 +208,10 @@ def main(argv=None):
     ap.add_argument("--btf-path", type=int, choices=(0, 1, 2), default=0,
                     help="(B,T,F) kernel family: 0 automatic, 1 streaming, 2 tile-resident")
     a = ap.parse_args(argv)
-    if a.btf_path:
-        from . import _abi
+    from prospective_rqf_b200 import ops
 
-        _abi.load().rqf_btf_select_path(a.btf_path)
-    out = measure(a.op, a.F, a.B, a.T, a.iters, a.warmup, a.groups, a.truncated)
+    with ops.btf_kernel_family(a.btf_path):
+        out = measure(a.op, a.F, a.B, a.T, a.iters, a.warmup, a.groups, a.truncated)
     out["btf_path"] = a.btf_path
     print(json.dumps(out), flush=True)
 

@@ -83,15 +83,17 @@ int rqf_selftest_lookback_timeout(void *scratch, rqf_stream_t stream);
  * 64-step sub-tile) for many.  rqf_btf_num_tiles gives the 64-step sub-tiles
  * along time (an upper bound on the tiles of either family); size buffers
  * with rqf_btf_carry_count / _scratch_bytes.
- * rqf_btf_select_path: 0 = automatic (streaming below 48 chains), 1 =
- * streaming, 2 = tile-resident.  Returns the previous selection, or -1 for an
- * invalid one.  Process-wide; a forward and its backward must run under the
- * same selection, since the saved entry states of the two families differ. */
-int rqf_btf_select_path(int path);
+ * Every (B,T,F) scan entry point takes `path`, per call: 0 = automatic
+ * (streaming below 48 chains of batch x 32 channels), 1 = streaming, 2 =
+ * tile-resident; anything else is RQF_ERR_ARGUMENT.  A backward must be given
+ * the path its forward was given, since the saved entry states of the two
+ * families differ (the automatic choice depends only on batch and filters,
+ * so it agrees by itself). */
 int64_t rqf_btf_num_tiles(int64_t time);
 int64_t rqf_btf_carry_count(int64_t batch, int64_t time, int64_t filters);
 size_t rqf_btf_scratch_bytes(int64_t batch, int64_t time, int64_t filters);
-/* FBT kernels: rows = filters * batch, tiles along time. */
+/* FBT kernels: rows = filters * batch, tiles along time.  The scratch size is
+ * SIZE_MAX for shapes that the FBT entry points reject (RQF_ERR_SHAPE). */
 int64_t rqf_fbt_num_tiles(int64_t time);
 int64_t rqf_fbt_carry_count(int64_t filters, int64_t batch, int64_t time);
 size_t rqf_fbt_scratch_bytes(int64_t filters, int64_t batch, int64_t time);
@@ -105,7 +107,7 @@ size_t rqf_fbt_scratch_bytes(int64_t filters, int64_t batch, int64_t time);
 int rqf_chunked_scan_forward(const float *c1, const float *c2, const void *u,
                              int u_is_real, float *y, float *carries,
                              void *scratch, int64_t batch, int64_t time,
-                             int64_t filters, rqf_stream_t stream);
+                             int64_t filters, int path, rqf_stream_t stream);
 
 /* Magnitude |y[t]| of the same scan, for no-grad consumers: replaces
  * rqf_models/ops/triton_scan_kernel.py:_sequential_scan_forward_abs_raw_block_f
@@ -116,7 +118,7 @@ int rqf_chunked_scan_forward(const float *c1, const float *c2, const void *u,
 int rqf_chunked_scan_abs_forward(const float *c1, const float *c2, const void *u,
                                  int u_is_real, float *y_abs, void *scratch,
                                  int64_t batch, int64_t time, int64_t filters,
-                                 rqf_stream_t stream);
+                                 int path, rqf_stream_t stream);
 
 /* Replaces chunked_scan_kernel.py:_chunked_scan_backward_raw (:252) /
  * _chunked_scan_backward_kernel (:122): g[t] = gy[t] + conj(c1) g[t+1];
@@ -127,7 +129,7 @@ int rqf_chunked_scan_backward(const float *c1, const float *c2, const void *u,
                               int u_is_real, const float *carries,
                               const float *grad_y, void *grad_u, float *grad_c1,
                               float *grad_c2, void *scratch, int64_t batch,
-                              int64_t time, int64_t filters,
+                              int64_t time, int64_t filters, int path,
                               rqf_stream_t stream);
 
 /* ---- multi-oscillator scan with C-weight reduction, (B,T,F) layout --- *
@@ -175,7 +177,7 @@ int rqf_chunked_prospective_forward(const float *c1, const float *tap0,
                                     const float *tap1, const float *x, float *y,
                                     float *carries, void *scratch,
                                     int64_t batch, int64_t time,
-                                    int64_t filters, rqf_stream_t stream);
+                                    int64_t filters, int path, rqf_stream_t stream);
 
 /* Replaces _ChunkedProspectiveScanFunction.backward
  * (chunked_scan_kernel.py:489-503), fused into one kernel:
@@ -185,7 +187,7 @@ int rqf_chunked_prospective_backward(
     const float *c1, const float *tap0, const float *tap1, const float *x,
     const float *carries, const float *grad_y, float *grad_x, float *grad_c1,
     float *grad_tap0, float *grad_tap1, void *scratch, int64_t batch,
-    int64_t time, int64_t filters, rqf_stream_t stream);
+    int64_t time, int64_t filters, int path, rqf_stream_t stream);
 
 /* ---- two-tap prospective scan, (F,B,T) layout ------------------------ *
  * Replaces fbt_scan_kernel.py:_fbt_prospective_kernel (:34) and
@@ -236,14 +238,16 @@ int rqf_fbt_prospective_backward(const float *c1, const float *tap0,
  *   grad_zw  = conj(tap1) g[t+1]  (cotangent of the lag source zw = z values)
  *   grad_c1  = sum conj(y[t-1]) g[t], grad_tap0 = sum conj(z[t]) g[t],
  *   grad_tap1 = sum conj(z[t-1]) g[t].
- * dims = {batch, time, filters} for layout 0, {filters, batch, time} for 1. */
+ * dims = {batch, time, filters} for layout 0, {filters, batch, time} for 1;
+ * path as the (B,T,F) forward's (layout 0; ignored for layout 1). */
 int rqf_tbptt1_two_tap_backward(int layout, const float *c1, const float *tap0,
                                 const float *tap1, const float *z,
                                 const float *carries, const float *grad_out,
                                 float *grad_z, float *grad_zw, float *grad_c1,
                                 float *grad_tap0, float *grad_tap1,
                                 void *scratch, int64_t d0, int64_t d1,
-                                int64_t d2, int fuse_act, rqf_stream_t stream);
+                                int64_t d2, int fuse_act, int path,
+                                rqf_stream_t stream);
 
 /* ---- selective (input-dependent ZOH) scan, (F,B,T) layout ------------ *
  * Replaces rqf_models/ops/selective_scan_kernel.py:selective_forward (:491) /
@@ -302,10 +306,14 @@ int rqf_selective_backward(const float *z, const rqf_selective_inputs *inputs,
  * Same arguments and results as rqf_fbt_prospective_backward without
  * `scratch`: the scratch lives in a fixed 4 MiB __device__ array inside this
  * library (every GPU that loads the library holds it until process exit).
- * Shapes whose scratch (rqf_fbt_scratch_bytes) exceeds 4 MiB are rejected
- * with RQF_ERR_CAPACITY.  The first call on a device looks up the array's
+ * Shapes are validated first (RQF_ERR_SHAPE, as the regular entry point);
+ * valid shapes whose scratch (rqf_fbt_scratch_bytes) exceeds 4 MiB are
+ * rejected with RQF_ERR_CAPACITY.  The first call on a device looks up the array's
  * device address on that device (cudaGetSymbolAddress, once per device), so
- * make the first call on each device outside any stream capture.  All calls
+ * make the first call on each device outside any stream capture.  The cached
+ * address lives as long as the device's context: a process that calls
+ * cudaDeviceReset on a device after using this entry point there must not
+ * call it on that device again.  All calls
  * share the one array and it keeps the last call's contents (the part that
  * must start at zero is cleared on every call), so calls whose GPU work
  * overlaps — on different streams, or from different host threads without
@@ -443,16 +451,68 @@ int rqf_readout_relu_pool_backward(const uint32_t *mask, const float *scale, flo
                                    float *counts, int64_t h, int64_t batch, int64_t time,
                                    rqf_stream_t stream);
 
-/* ZOH prospective two-tap coefficients of n log-space leaves (tau mode, rho =
- * 1; filter.py:510-664, the torch expressions of RQF.two_tap):
+/* ---- RQF filter-bank coefficients (rqf_models/backbones/rqf/filter.py) -- *
+ * Replaces RQF.compute_two_tap_coefficients (filter.py:510-664) with the
+ * parameter reads it makes (the tau / gamma / freq properties, :402-449):
+ * every discretization that has a two-tap form (Euler and ZOH prospective,
+ * FOH prospective and not), tau mode (rho = 1), gamma mode (rho = 1/gamma),
+ * an explicit prospective_tau (rho = tau_p / tau), the dynamic gamma clamp
+ * (clamp_gamma, :594-598), and both leaf parametrizations:
+ *
+ *   log space     (param_space 0): theta_leaf = log_theta, gamma_leaf = log_gamma,
+ *                                  gamma = e^gamma_leaf, freq = e^theta_leaf / (2 pi tau)
+ *   sigmoid space (param_space 1): theta_leaf = freq_param, gamma_leaf = gamma_param,
+ *                                  gamma = min_gamma + (max_gamma - min_gamma) sig(gamma_leaf),
+ *                                  freq = min_freq + (max_freq - min_freq) sig(theta_leaf)
+ *
+ * tau = e^log_tau per filter (log_tau may be NULL: the scalar opts->tau).
+ * Outputs c1, tap0, tap1 complex64 (n,) — Euler's real taps with zero
+ * imaginary parts; computed in double from the fp32 leaves.  phi = (e^a-1)/a
+ * and psi = (e^a-1-a)/a^2 take the reference's 4th-order Taylor forms below
+ * |a| = 1e-4 and 1e-3.  bilinear has no two-tap form, and Euler / ZOH without
+ * prospective input are single-tap (RQF_ERR_ARGUMENT, as the reference raises).
+ *
+ * The backward takes complex cotangents (each may be NULL) and writes the
+ * real gradients of the leaves it is given outputs for (each may be NULL):
+ * grad p = sum over outputs of Re(conj(d out / d p) * grad_out), through every
+ * branch above (the clamp's derivative follows the selected operand, as
+ * torch.clamp's does). */
+enum { RQF_DISC_EULER = 0, RQF_DISC_ZOH = 1, RQF_DISC_FOH = 2 };
+
+typedef struct {
+  const float *theta_leaf;      /* log_theta or freq_param, (n,)           */
+  const float *gamma_leaf;      /* log_gamma or gamma_param, (n,)          */
+  const float *log_tau;         /* (n,) or NULL                            */
+  const float *min_gamma, *max_gamma, *min_freq, *max_freq; /* sigmoid (n,) */
+  const float *prospective_tau; /* (n,) seconds, or NULL (mode decides rho) */
+} rqf_coeff_leaves;
+
+typedef struct {
+  int discretization; /* RQF_DISC_*                                       */
+  int prospective;    /* 1: prospective taps; 0: FOH non-prospective taps */
+  int gamma_mode;     /* 0: tau mode; 1: gamma mode (ignored with tau_p)  */
+  int param_space;    /* 0: log leaves; 1: sigmoid leaves                 */
+  int clamp_gamma;
+  double dt;
+  double tau;         /* used when leaves->log_tau is NULL                */
+} rqf_coeff_options;
+
+int rqf_filter_two_tap_coefficients(const rqf_coeff_leaves *leaves, const rqf_coeff_options *opts,
+                                    float *c1, float *tap0, float *tap1, int64_t n,
+                                    rqf_stream_t stream);
+int rqf_filter_two_tap_coefficients_backward(const rqf_coeff_leaves *leaves,
+                                             const rqf_coeff_options *opts, const float *grad_c1,
+                                             const float *grad_tap0, const float *grad_tap1,
+                                             float *grad_theta_leaf, float *grad_gamma_leaf,
+                                             float *grad_log_tau, float *grad_prospective_tau,
+                                             int64_t n, rqf_stream_t stream);
+
+/* The log-space ZOH tau-mode case with one scalar tau (the Pure RQF paper
+ * recipe, and this backend's encoder): the general producer with
+ * {RQF_DISC_ZOH, prospective, tau mode, log space, no clamp}:
  *
  *   a = (dt/tau) (-gamma + i theta (1 - gamma)),  gamma = e^lg, theta = e^lt
- *   c1 = e^a,  tap0 = gamma ((dt/tau) (e^a - 1)/a + c1),  tap1 = -gamma c1
- *
- * (e^a - 1)/a takes the reference's 4th-order Taylor form below |a| = 1e-4.
- * Outputs complex64; computed in double.  The backward takes complex
- * cotangents (each may be null) and writes the real gradients of the leaves:
- * grad p = sum over outputs of Re(conj(d out / d p) * grad_out). */
+ *   c1 = e^a,  tap0 = gamma ((dt/tau) (e^a - 1)/a + c1),  tap1 = -gamma c1 */
 int rqf_two_tap_coefficients(const float *log_theta, const float *log_gamma, float *c1, float *tap0,
                              float *tap1, int64_t n, double dt, double tau, rqf_stream_t stream);
 int rqf_two_tap_coefficients_backward(const float *log_theta, const float *log_gamma,

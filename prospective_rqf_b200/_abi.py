@@ -40,8 +40,25 @@ class SelectiveInputs(ctypes.Structure):
                 ("num_groups", _i64)]
 
 
+class CoeffLeaves(ctypes.Structure):
+    """rqf_coeff_leaves (include/rqf_b200.h)."""
+
+    _fields_ = [("theta_leaf", _p), ("gamma_leaf", _p), ("log_tau", _p), ("min_gamma", _p),
+                ("max_gamma", _p), ("min_freq", _p), ("max_freq", _p),
+                ("prospective_tau", _p)]
+
+
+class CoeffOptions(ctypes.Structure):
+    """rqf_coeff_options (include/rqf_b200.h)."""
+
+    _fields_ = [("discretization", _int), ("prospective", _int), ("gamma_mode", _int),
+                ("param_space", _int), ("clamp_gamma", _int), ("dt", _f64), ("tau", _f64)]
+
+
 _pin = ctypes.POINTER(SelectiveInputs)
 _pop = ctypes.POINTER(SelectiveOptions)
+_pcl = ctypes.POINTER(CoeffLeaves)
+_pco = ctypes.POINTER(CoeffOptions)
 
 # name -> (restype, argtypes); mirrors include/rqf_b200.h exactly.
 SIGNATURES: dict[str, tuple] = {
@@ -49,15 +66,16 @@ SIGNATURES: dict[str, tuple] = {
     "rqf_status_string": (ctypes.c_char_p, [_int]),
     "rqf_read_device_error": (_int, [ctypes.POINTER(_int), _int, _p]),
     "rqf_selftest_lookback_timeout": (_int, [_p, _p]),
-    "rqf_btf_select_path": (_int, [_int]),
     "rqf_btf_num_tiles": (_i64, [_i64]),
     "rqf_btf_carry_count": (_i64, [_i64, _i64, _i64]),
     "rqf_btf_scratch_bytes": (_sz, [_i64, _i64, _i64]),
     "rqf_fbt_num_tiles": (_i64, [_i64]),
     "rqf_fbt_carry_count": (_i64, [_i64, _i64, _i64]),
     "rqf_fbt_scratch_bytes": (_sz, [_i64, _i64, _i64]),
-    "rqf_chunked_scan_forward": (_int, [_p, _p, _p, _int, _p, _p, _p, _i64, _i64, _i64, _p]),
-    "rqf_chunked_scan_abs_forward": (_int, [_p, _p, _p, _int, _p, _p, _i64, _i64, _i64, _p]),
+    "rqf_chunked_scan_forward": (_int, [_p, _p, _p, _int, _p, _p, _p, _i64, _i64, _i64, _int,
+                                        _p]),
+    "rqf_chunked_scan_abs_forward": (_int, [_p, _p, _p, _int, _p, _p, _i64, _i64, _i64, _int,
+                                            _p]),
     "rqf_multi_osc_forward": (_int, [_p, _p, _p, _p, _int, _p, _int, _p, _p, _i64, _i64, _i64,
                                      _i64, _p]),
     "rqf_multi_osc_backward": (_int, [_p, _p, _p, _p, _int, _p, _p, _p, _p, _p, _p, _p, _i64,
@@ -65,10 +83,11 @@ SIGNATURES: dict[str, tuple] = {
     "rqf_multi_osc_carry_count": (_i64, [_i64, _i64, _i64, _i64]),
     "rqf_multi_osc_scratch_bytes": (_sz, [_i64, _i64, _i64, _i64]),
     "rqf_chunked_scan_backward": (
-        _int, [_p, _p, _p, _int, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p]),
-    "rqf_chunked_prospective_forward": (_int, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p]),
+        _int, [_p, _p, _p, _int, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
+    "rqf_chunked_prospective_forward": (
+        _int, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "rqf_chunked_prospective_backward": (
-        _int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _p]),
+        _int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "rqf_fbt_prospective_forward": (
         _int, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "rqf_fbt_block_forward": (
@@ -85,7 +104,8 @@ SIGNATURES: dict[str, tuple] = {
         _int, [_p, _pin, _pop, _p, _p, _p, _int, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64,
                _i64, _p]),
     "rqf_tbptt1_two_tap_backward": (
-        _int, [_int, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
+        _int, [_int, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _int,
+               _p]),
     "rqf_projection_workspace_bytes": (_sz, [_i64, _i64]),
     "rqf_projection_timeout_site": (_int, [_int]),
     "rqf_projection": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _int, _p, _p]),
@@ -99,6 +119,9 @@ SIGNATURES: dict[str, tuple] = {
     "rqf_projection_weight_grad_real": (_int, [_p, _p, _p, _i64, _i64, _i64, _p, _p]),
     "rqf_projection_real_out_workspace_bytes": (_sz, [_i64, _i64]),
     "rqf_projection_real_out": (_int, [_p, _p, _p, _i64, _i64, _i64, _p, _p]),
+    "rqf_filter_two_tap_coefficients": (_int, [_pcl, _pco, _p, _p, _p, _i64, _p]),
+    "rqf_filter_two_tap_coefficients_backward": (
+        _int, [_pcl, _pco, _p, _p, _p, _p, _p, _p, _p, _i64, _p]),
     "rqf_two_tap_coefficients": (_int, [_p, _p, _p, _p, _p, _i64, _f64, _f64, _p]),
     "rqf_two_tap_coefficients_backward": (
         _int, [_p, _p, _p, _p, _p, _p, _p, _i64, _f64, _f64, _p]),

@@ -1,18 +1,35 @@
-// ZOH prospective two-tap coefficients of the log-space RQF leaves (tau mode,
-// rho = 1; rqf_models/backbones/rqf/filter.py:510-664) and their gradient,
-// one thread per leaf, in double precision:
+// Two-tap coefficients of the RQF filter bank and their gradient
+// (rqf_models/backbones/rqf/filter.py:RQF.compute_two_tap_coefficients
+// :510-664, with the parameter reads of :402-449 and the dynamic gamma clamp
+// of :594-598), one thread per filter, in double precision.
 //
-//   gamma = e^lg, theta = e^lt, s = dt / tau,
-//   a = s (-gamma + i theta (1 - gamma)),   C1 = e^a,
-//   phi(a) = (e^a - 1) / a  (4th-order Taylor below |a| = 1e-4, as the
-//   reference),   tap0 = gamma (s phi(a) + C1),   tap1 = -gamma C1.
+// Per filter, from its leaves (log space: log_theta, log_gamma; sigmoid space:
+// freq_param, gamma_param with per-filter bounds) and log_tau:
 //
-// Backward: for real leaves p and complex cotangents G (torch's convention),
-// grad p = sum over the outputs y of Re(conj(dy/dp) G_y), with
-// da/dlg = s (-gamma - i theta gamma), da/dlt = i s theta (1 - gamma) and
-// phi'(a) = (e^a (a - 1) + 1) / a^2 (Taylor 1/2 + a/3 + a^2/8 + a^3/30 below
-// the same threshold).  The torch restatement of the same formulas runs ~30
-// small kernels forward and ~60 backward for these few thousand leaves.
+//   tau = e^log_tau
+//   log space:     gamma = e^lg,  freq = e^lt / (2 pi tau)
+//   sigmoid space: gamma = gmin + (gmax - gmin) sig(gp),
+//                  freq  = fmin + (fmax - fmin) sig(fp)
+//   clamp_gamma:   gamma = clamp(gamma, 1 - 1/sqrt(1 + x^2), x / (1 + x)),
+//                  x = 2 pi freq tau
+//   rho = tau_p / tau (prospective_tau given), else 1 (tau mode) or
+//         1 / gamma (gamma mode)
+//   A = -gamma/tau + i 2 pi freq (1 - gamma),  a = A dt,  eta = dt / tau
+//   Euler: C1 = 1 + eta (-1 + (1 - gamma)(1 + i 2 pi tau freq)),
+//          tap0 = gamma eta + gamma rho,  tap1 = -gamma rho
+//   ZOH:   C1 = e^a, phi = (e^a - 1)/a, tap0 = gamma eta phi + gamma rho C1,
+//          tap1 = -gamma rho C1
+//   FOH:   psi = (e^a - 1 - a)/a^2;  prospective: tap0 = gamma eta psi +
+//          gamma rho phi, tap1 = gamma eta (phi - psi) - gamma rho phi;
+//          non-prospective: tap0 = gamma eta psi, tap1 = gamma eta (phi - psi)
+//
+// phi and psi take the reference's 4th-order Taylor forms below |a| = 1e-4 and
+// 1e-3.  The gradient carries forward-mode derivatives (Dual) through exactly
+// the expressions above, one leaf at a time, so every branch — including the
+// Taylor forms and the clamp, whose derivative follows the selected operand as
+// torch.clamp's does — is differentiated without a hand-derived formula:
+// grad p = sum over the outputs y of Re(conj(dy/dp) G_y) for complex
+// cotangents G (torch's convention).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -21,95 +38,219 @@
 namespace rqf {
 namespace coef {
 
-struct cd {
-  double x, y;
+constexpr double kTwoPi = 6.283185307179586476925286766559;
+
+// Value and derivative with respect to the seeded leaf.
+struct Dual {
+  double v, d;
 };
-__device__ __forceinline__ cd cadd(cd a, cd b) { return {a.x + b.x, a.y + b.y}; }
-__device__ __forceinline__ cd cmul(cd a, cd b) { return {a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x}; }
-__device__ __forceinline__ cd cscale(cd a, double s) { return {a.x * s, a.y * s}; }
-__device__ __forceinline__ cd cdiv(cd a, cd b) {
-  const double d = b.x * b.x + b.y * b.y;
-  return {(a.x * b.x + a.y * b.y) / d, (a.y * b.x - a.x * b.y) / d};
+__device__ __forceinline__ Dual operator+(Dual a, Dual b) { return {a.v + b.v, a.d + b.d}; }
+__device__ __forceinline__ Dual operator-(Dual a, Dual b) { return {a.v - b.v, a.d - b.d}; }
+__device__ __forceinline__ Dual operator-(Dual a) { return {-a.v, -a.d}; }
+__device__ __forceinline__ Dual operator*(Dual a, Dual b) { return {a.v * b.v, a.d * b.v + a.v * b.d}; }
+__device__ __forceinline__ Dual operator/(Dual a, Dual b) {
+  return {a.v / b.v, (a.d * b.v - a.v * b.d) / (b.v * b.v)};
 }
-__device__ __forceinline__ cd cexp(cd a) {
+__device__ __forceinline__ Dual operator+(Dual a, double b) { return {a.v + b, a.d}; }
+__device__ __forceinline__ Dual operator+(double a, Dual b) { return {a + b.v, b.d}; }
+__device__ __forceinline__ Dual operator-(Dual a, double b) { return {a.v - b, a.d}; }
+__device__ __forceinline__ Dual operator-(double a, Dual b) { return {a - b.v, -b.d}; }
+__device__ __forceinline__ Dual operator*(Dual a, double b) { return {a.v * b, a.d * b}; }
+__device__ __forceinline__ Dual operator*(double a, Dual b) { return {a * b.v, a * b.d}; }
+__device__ __forceinline__ Dual operator/(Dual a, double b) { return {a.v / b, a.d / b}; }
+__device__ __forceinline__ Dual operator/(double a, Dual b) { return {a / b.v, -a * b.d / (b.v * b.v)}; }
+
+__device__ __forceinline__ double val(double x) { return x; }
+__device__ __forceinline__ double val(Dual x) { return x.v; }
+__device__ __forceinline__ double fexp(double x) { return exp(x); }
+__device__ __forceinline__ Dual fexp(Dual x) {
+  const double e = exp(x.v);
+  return {e, e * x.d};
+}
+__device__ __forceinline__ double fsqrt(double x) { return sqrt(x); }
+__device__ __forceinline__ Dual fsqrt(Dual x) {
+  const double s = sqrt(x.v);
+  return {s, x.d / (2.0 * s)};
+}
+__device__ __forceinline__ void fsincos(double x, double *s, double *c) { sincos(x, s, c); }
+__device__ __forceinline__ void fsincos(Dual x, Dual *s, Dual *c) {
   double sn, cs;
-  sincos(a.y, &sn, &cs);
-  const double m = exp(a.x);
+  sincos(x.v, &sn, &cs);
+  *s = {sn, cs * x.d};
+  *c = {cs, -sn * x.d};
+}
+__device__ __forceinline__ double fsigmoid(double x) { return 1.0 / (1.0 + exp(-x)); }
+__device__ __forceinline__ Dual fsigmoid(Dual x) {
+  const double s = 1.0 / (1.0 + exp(-x.v));
+  return {s, s * (1.0 - s) * x.d};
+}
+// A leaf read as S: the seeded leaf carries derivative 1.
+template <class S>
+__device__ __forceinline__ S leaf(double x, bool seeded);
+template <>
+__device__ __forceinline__ double leaf<double>(double x, bool) { return x; }
+template <>
+__device__ __forceinline__ Dual leaf<Dual>(double x, bool seeded) { return {x, seeded ? 1.0 : 0.0}; }
+
+template <class S>
+struct Cx {
+  S re, im;
+};
+template <class S>
+__device__ __forceinline__ Cx<S> operator+(Cx<S> a, Cx<S> b) { return {a.re + b.re, a.im + b.im}; }
+template <class S>
+__device__ __forceinline__ Cx<S> operator-(Cx<S> a, Cx<S> b) { return {a.re - b.re, a.im - b.im}; }
+template <class S>
+__device__ __forceinline__ Cx<S> operator*(Cx<S> a, Cx<S> b) {
+  return {a.re * b.re - a.im * b.im, a.re * b.im + a.im * b.re};
+}
+template <class S>
+__device__ __forceinline__ Cx<S> operator/(Cx<S> a, Cx<S> b) {
+  const S d = b.re * b.re + b.im * b.im;
+  return {(a.re * b.re + a.im * b.im) / d, (a.im * b.re - a.re * b.im) / d};
+}
+template <class S>
+__device__ __forceinline__ Cx<S> scale(Cx<S> a, S s) { return {a.re * s, a.im * s}; }
+__device__ __forceinline__ Cx<Dual> scale(Cx<Dual> a, double s) { return {a.re * s, a.im * s}; }
+template <class S>
+__device__ __forceinline__ Cx<S> cexp(Cx<S> a) {
+  const S m = fexp(a.re);
+  S sn, cs;
+  fsincos(a.im, &sn, &cs);
   return {m * cs, m * sn};
 }
-// Re(conj(u) g)
-__device__ __forceinline__ double rdot(cd u, float2 g) { return u.x * g.x + u.y * g.y; }
+template <class S>
+__device__ __forceinline__ double cabs_v(Cx<S> a) {
+  const double x = val(a.re), y = val(a.im);
+  return sqrt(x * x + y * y);
+}
+template <class S>
+__device__ __forceinline__ Cx<S> cplus(Cx<S> a, double r) { return {a.re + r, a.im}; }
 
-constexpr double kSmall = 1e-4;
+enum : int { kEuler = 0, kZoh = 1, kFoh = 2 };
 
-struct Eval {
-  double gamma, theta;
-  cd a, ea, phi;
+// Host-filled, passed by value.  Null bound / tau_p / log_tau pointers fall
+// back to the scalars below (`tau`) or are unused.
+struct Leaves {
+  const float *theta;   // log_theta (log space) or freq_param (sigmoid space)
+  const float *gamma;   // log_gamma or gamma_param
+  const float *log_tau; // per filter; null: log(tau)
+  const float *min_gamma, *max_gamma, *min_freq, *max_freq;  // sigmoid space
+  const float *tau_p;   // prospective_tau (seconds) per filter, or null
+};
+struct Opts {
+  int disc, prospective, gamma_mode, sigmoid, clamp;
+  double dt, tau;
 };
 
-__device__ __forceinline__ Eval eval(float lt, float lg, double s) {
-  Eval e;
-  e.gamma = exp((double)lg);
-  e.theta = exp((double)lt);
-  e.a = {-s * e.gamma, s * e.theta * (1.0 - e.gamma)};
-  e.ea = cexp(e.a);
-  if (sqrt(e.a.x * e.a.x + e.a.y * e.a.y) < kSmall) {
-    const cd a = e.a, a2 = cmul(a, a), a3 = cmul(a2, a), a4 = cmul(a3, a);
-    e.phi = cadd(cadd({1.0 + a.x / 2, a.y / 2}, cscale(a2, 1.0 / 6)),
-                 cadd(cscale(a3, 1.0 / 24), cscale(a4, 1.0 / 120)));
+// seed: 0 theta leaf, 1 gamma leaf, 2 log_tau, 3 tau_p, -1 none.
+template <class S>
+__device__ __forceinline__ void eval(const Leaves &L, const Opts &o, long long i, int seed,
+                                     Cx<S> *c1, Cx<S> *t0, Cx<S> *t1) {
+  const S log_tau = leaf<S>(L.log_tau ? (double)L.log_tau[i] : log(o.tau), seed == 2);
+  const S tau = fexp(log_tau);
+  S gamma, freq;
+  if (!o.sigmoid) {
+    gamma = fexp(leaf<S>((double)L.gamma[i], seed == 1));
+    freq = fexp(leaf<S>((double)L.theta[i], seed == 0)) / (kTwoPi * tau);
   } else {
-    e.phi = cdiv({e.ea.x - 1.0, e.ea.y}, e.a);
+    const double g0 = L.min_gamma[i], g1 = L.max_gamma[i];
+    const double f0 = L.min_freq[i], f1 = L.max_freq[i];
+    gamma = g0 + (g1 - g0) * fsigmoid(leaf<S>((double)L.gamma[i], seed == 1));
+    freq = f0 + (f1 - f0) * fsigmoid(leaf<S>((double)L.theta[i], seed == 0));
   }
-  return e;
+  if (o.clamp) {  // torch.clamp(gamma, min=lo, max=hi) = min(max(gamma, lo), hi)
+    const S x = kTwoPi * freq * tau;
+    const S lo = 1.0 - 1.0 / fsqrt(1.0 + x * x);
+    const S hi = x / (1.0 + x);
+    S r = val(gamma) < val(lo) ? lo : gamma;
+    gamma = val(r) > val(hi) ? hi : r;
+  }
+  S rho;
+  if (L.tau_p)
+    rho = leaf<S>((double)L.tau_p[i], seed == 3) / tau;
+  else
+    rho = o.gamma_mode ? 1.0 / gamma : leaf<S>(1.0, false);
+  const S eta = o.dt / tau;
+  const S one_m_g = 1.0 - gamma;
+  if (o.disc == kEuler) {
+    const S extra = gamma * rho;
+    *c1 = {1.0 + eta * (one_m_g - 1.0), eta * one_m_g * (kTwoPi * tau * freq)};
+    *t0 = {gamma * eta + extra, leaf<S>(0.0, false)};
+    *t1 = {-extra, leaf<S>(0.0, false)};
+    return;
+  }
+  const Cx<S> a = {-(gamma / tau) * o.dt, kTwoPi * freq * one_m_g * o.dt};
+  const Cx<S> ea = cexp(a);
+  const double mag = cabs_v(a);
+  Cx<S> phi;
+  if (mag < 1e-4) {
+    const Cx<S> a2 = a * a, a3 = a2 * a, a4 = a3 * a;
+    phi = cplus(scale(a, 0.5), 1.0) + scale(a2, 1.0 / 6) + scale(a3, 1.0 / 24) +
+          scale(a4, 1.0 / 120);
+  } else {
+    phi = cplus(ea, -1.0) / a;
+  }
+  *c1 = ea;
+  if (o.disc == kZoh) {
+    const Cx<S> extra = scale(ea, gamma * rho);
+    *t0 = scale(phi, gamma * eta) + extra;
+    *t1 = {-extra.re, -extra.im};
+    return;
+  }
+  Cx<S> psi;
+  if (mag < 1e-3) {
+    const Cx<S> a2 = a * a, a3 = a2 * a, a4 = a3 * a;
+    psi = cplus(scale(a, 1.0 / 6), 0.5) + scale(a2, 1.0 / 24) + scale(a3, 1.0 / 120) +
+          scale(a4, 1.0 / 720);
+  } else {
+    psi = (cplus(ea, -1.0) - a) / (a * a);
+  }
+  const Cx<S> d0 = scale(psi, gamma * eta);           // gamma D_bar
+  const Cx<S> d1 = scale(phi - psi, gamma * eta);     // gamma (B_bar - D_bar)
+  if (o.prospective) {
+    const Cx<S> extra = scale(phi, gamma * rho);
+    *t0 = d0 + extra;
+    *t1 = d1 - extra;
+  } else {
+    *t0 = d0;
+    *t1 = d1;
+  }
 }
 
-__global__ void two_tap_kernel(const float *__restrict__ lt, const float *__restrict__ lg,
-                               float2 *__restrict__ c1, float2 *__restrict__ tap0,
-                               float2 *__restrict__ tap1, long long n, double s) {
+__global__ void two_tap_kernel(Leaves L, Opts o, float2 *__restrict__ c1, float2 *__restrict__ tap0,
+                               float2 *__restrict__ tap1, long long n) {
   const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   if (i >= n) return;
-  const Eval e = eval(lt[i], lg[i], s);
-  const cd t0 = cscale(cadd(cscale(e.phi, s), e.ea), e.gamma);
-  c1[i] = make_float2((float)e.ea.x, (float)e.ea.y);
-  tap0[i] = make_float2((float)t0.x, (float)t0.y);
-  tap1[i] = make_float2((float)(-e.gamma * e.ea.x), (float)(-e.gamma * e.ea.y));
+  Cx<double> c, t0, t1;
+  eval<double>(L, o, i, -1, &c, &t0, &t1);
+  c1[i] = make_float2((float)c.re, (float)c.im);
+  tap0[i] = make_float2((float)t0.re, (float)t0.im);
+  tap1[i] = make_float2((float)t1.re, (float)t1.im);
 }
 
-// Cotangents may be null (zero).
-__global__ void two_tap_backward_kernel(const float *__restrict__ lt, const float *__restrict__ lg,
-                                        const float2 *__restrict__ g1, const float2 *__restrict__ g0,
-                                        const float2 *__restrict__ gm, float *__restrict__ grad_lt,
-                                        float *__restrict__ grad_lg, long long n, double s) {
+// Re(conj(dy) g): the derivative parts of a dual complex against a cotangent.
+__device__ __forceinline__ double rdot(Cx<Dual> u, float2 g) { return u.re.d * g.x + u.im.d * g.y; }
+
+// Cotangents may be null (zero); so may any gradient output (not wanted).
+__global__ void two_tap_backward_kernel(Leaves L, Opts o, const float2 *__restrict__ g1,
+                                        const float2 *__restrict__ g0,
+                                        const float2 *__restrict__ gm, float *__restrict__ grad_theta,
+                                        float *__restrict__ grad_gamma,
+                                        float *__restrict__ grad_log_tau,
+                                        float *__restrict__ grad_tau_p, long long n) {
   const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   if (i >= n) return;
-  const Eval e = eval(lt[i], lg[i], s);
-  cd dphi;
-  if (sqrt(e.a.x * e.a.x + e.a.y * e.a.y) < kSmall) {
-    const cd a = e.a, a2 = cmul(a, a), a3 = cmul(a2, a);
-    dphi = cadd(cadd({0.5 + a.x / 3, a.y / 3}, cscale(a2, 1.0 / 8)), cscale(a3, 1.0 / 30));
-  } else {
-    const cd num = cadd(cmul(e.ea, {e.a.x - 1.0, e.a.y}), {1.0, 0.0});
-    dphi = cdiv(num, cmul(e.a, e.a));
-  }
   const float2 z = make_float2(0.f, 0.f);
   const float2 G1 = g1 ? g1[i] : z, G0 = g0 ? g0[i] : z, Gm = gm ? gm[i] : z;
-  const cd sphi_c1 = cadd(cscale(e.phi, s), e.ea);    // s phi + C1
-  const cd sdphi_c1 = cadd(cscale(dphi, s), e.ea);    // s phi' + C1
-  // p = lg: dgamma/dp = gamma; p = lt: 0
-  const cd da_lg = {-s * e.gamma, -s * e.theta * e.gamma};
-  const cd da_lt = {0.0, s * e.theta * (1.0 - e.gamma)};
-  double out[2];
-#pragma unroll
-  for (int p = 0; p < 2; ++p) {
-    const cd da = p == 0 ? da_lg : da_lt;
-    const double dg = p == 0 ? e.gamma : 0.0;
-    const cd dc1 = cmul(e.ea, da);
-    const cd dt0 = cadd(cscale(sphi_c1, dg), cscale(cmul(sdphi_c1, da), e.gamma));
-    const cd dt1 = cadd(cscale(e.ea, -dg), cscale(cmul(e.ea, da), -e.gamma));
-    out[p] = rdot(dc1, G1) + rdot(dt0, G0) + rdot(dt1, Gm);
+  float *outs[4] = {grad_theta, grad_gamma, grad_log_tau, grad_tau_p};
+#pragma unroll 1
+  for (int p = 0; p < 4; ++p) {
+    if (!outs[p]) continue;
+    Cx<Dual> c, t0, t1;
+    eval<Dual>(L, o, i, p, &c, &t0, &t1);
+    outs[p][i] = (float)(rdot(c, G1) + rdot(t0, G0) + rdot(t1, Gm));
   }
-  grad_lg[i] = (float)out[0];
-  grad_lt[i] = (float)out[1];
 }
 
 }  // namespace coef

@@ -19,7 +19,10 @@ void *g_noalloc_ptr[kNoAllocMaxDevices] = {};
 
 // Device address of g_noalloc_scratch on the current device, looked up once
 // per device.  Host code must not pass the symbol itself to a kernel: on the
-// host it only names a stand-in, not device memory.
+// host it only names a stand-in, not device memory.  The cached address stays
+// valid for the life of the device's primary context; after cudaDeviceReset
+// the module may be loaded again elsewhere, so this entry point does not
+// support a process that resets a device it has already been called on.
 int noalloc_scratch(void **out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return RQF_ERR_LAUNCH;
@@ -40,7 +43,8 @@ extern "C" int rqf_fbt_prospective_backward_noalloc(
     const float *c1, const float *tap0, const float *tap1, const float *z, const float *carries,
     const float *grad_out, float *grad_z, float *grad_c1, float *grad_tap0, float *grad_tap1,
     int64_t filters, int64_t batch, int64_t time, int fuse_act, rqf_stream_t stream) {
-  if (filters < 0 || batch < 0 || time < 0) return RQF_ERR_SHAPE;
+  const int dims = fbt_dims_ok(filters, batch, time);  // before any size product
+  if (dims != RQF_OK) return dims;
   if (rqf_fbt_scratch_bytes(filters, batch, time) > kNoAllocScratchBytes) return RQF_ERR_CAPACITY;
   void *scratch = nullptr;
   const int st = noalloc_scratch(&scratch);

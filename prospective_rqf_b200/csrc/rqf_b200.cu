@@ -131,10 +131,14 @@ __global__ void lookback_selftest_kernel(const u64 *flags, float2 *out) {
 }
 
 // ------------------------------------------------------------- FBT
+// Every product is bounded by dividing first, so absurd shapes cannot wrap
+// around int64 and pass: rows x tiles must fit the 31-bit ticket counter.
 int fbt_dims_ok(int64_t F, int64_t B, int64_t T) {
   if (F < 0 || B < 0 || T < 0) return RQF_ERR_SHAPE;
-  if (B > 0x7fffffffLL) return RQF_ERR_SHAPE;
-  if (F * B > 0 && ceil_div(T, kFbtTile) * F * B > kMaxTickets) return RQF_ERR_SHAPE;
+  if (B > 0x7fffffffLL || F > kMaxTickets || T > (1LL << 62)) return RQF_ERR_SHAPE;
+  if (F == 0 || B == 0 || T == 0) return RQF_OK;
+  if (F > kMaxTickets / B) return RQF_ERR_SHAPE;
+  if (ceil_div(T, kFbtTile) > kMaxTickets / (F * B)) return RQF_ERR_SHAPE;
   return RQF_OK;
 }
 
@@ -294,10 +298,13 @@ static_assert(kBtfsFwdWarps * kBtfsFwdK == bs::kBtfSub, "streaming forward sub-t
 static_assert(kBtfsBwdWarps * kBtfsBwdK == bs::kBtfSub, "streaming backward sub-tile");
 constexpr int64_t kBtfStreamChains = 48;  // chains below which the streaming path is used
 
-int g_btf_path = 0;  // 0 automatic, 1 streaming, 2 tile-resident (rqf_btf_select_path)
-
-inline bool btf_streaming(int64_t B, int64_t F) {
-  if (g_btf_path != 0) return g_btf_path == 1;
+// path: 0 automatic (by the number of chains), 1 streaming, 2 tile-resident.
+// Passed per call; a backward must get the path its forward got (the saved
+// entry states of the two families differ), which the automatic choice
+// guarantees by itself since it depends only on the batch and filter counts.
+inline bool btf_path_ok(int path) { return path >= 0 && path <= 2; }
+inline bool btf_streaming(int64_t B, int64_t F, int path) {
+  if (path != 0) return path == 1;
   return B * ceil_div(F, 32) < kBtfStreamChains;
 }
 
@@ -367,9 +374,9 @@ int btfs_launch(const bs::BtfArgs &a, void *scratch, cudaStream_t st) {
 // Forward of one drive in one family; ABS writes |y| (float) and saves no carries.
 template <int DRIVE, bool ABS>
 int btf_forward_drive(const float *c1, const float *c2, const float *tap1, const void *x, void *y,
-                      float *carries, void *scratch, int64_t B, int64_t T, int64_t F,
+                      float *carries, void *scratch, int64_t B, int64_t T, int64_t F, int path,
                       cudaStream_t stream) {
-  if (btf_streaming(B, F)) {
+  if (btf_streaming(B, F, path)) {
     const bs::BtfArgs sa = btfs_args(c1, c2, tap1, x, nullptr, y, nullptr, carries, scratch, B, T, F);
     return btfs_launch<0, DRIVE, ABS>(sa, scratch, stream);
   }
@@ -382,7 +389,8 @@ int btf_forward_drive(const float *c1, const float *c2, const float *tap1, const
 
 int btf_forward(int drive, const float *c1, const float *c2, const float *tap1, const void *x,
                 void *y, float *carries, void *scratch, int64_t B, int64_t T, int64_t F,
-                cudaStream_t stream, bool abs_out = false) {
+                int path, cudaStream_t stream, bool abs_out = false) {
+  if (!btf_path_ok(path)) return RQF_ERR_ARGUMENT;
   int st = btf_dims_ok(B, T, F);
   if (st != RQF_OK) return st;
   if (B == 0 || T == 0 || F == 0) return RQF_OK;
@@ -395,14 +403,18 @@ int btf_forward(int drive, const float *c1, const float *c2, const float *tap1, 
     return RQF_ERR_ALIGN;
   if (abs_out)
     return drive == kReal
-               ? btf_forward_drive<kReal, true>(c1, c2, tap1, x, y, nullptr, scratch, B, T, F, stream)
+               ? btf_forward_drive<kReal, true>(c1, c2, tap1, x, y, nullptr, scratch, B, T, F, path,
+                                                stream)
                : btf_forward_drive<kPlain, true>(c1, c2, tap1, x, y, nullptr, scratch, B, T, F,
-                                                 stream);
+                                                 path, stream);
   if (drive == kReal)
-    return btf_forward_drive<kReal, false>(c1, c2, tap1, x, y, carries, scratch, B, T, F, stream);
+    return btf_forward_drive<kReal, false>(c1, c2, tap1, x, y, carries, scratch, B, T, F, path,
+                                           stream);
   if (drive == kPlain)
-    return btf_forward_drive<kPlain, false>(c1, c2, tap1, x, y, carries, scratch, B, T, F, stream);
-  return btf_forward_drive<kTwoTap, false>(c1, c2, tap1, x, y, carries, scratch, B, T, F, stream);
+    return btf_forward_drive<kPlain, false>(c1, c2, tap1, x, y, carries, scratch, B, T, F, path,
+                                            stream);
+  return btf_forward_drive<kTwoTap, false>(c1, c2, tap1, x, y, carries, scratch, B, T, F, path,
+                                           stream);
 }
 
 template <int DRIVE>
@@ -415,8 +427,9 @@ int btf_backward_drive(const BtfArgs &a, bool vecx, bool vecg, void *scratch,
 
 int btf_backward(int drive, const float *c1, const float *c2, const float *tap1, const void *x,
                  const float *carries, const float *gy, void *gx, float *o0, float *o1,
-                 float *o2, void *scratch, int64_t B, int64_t T, int64_t F,
+                 float *o2, void *scratch, int64_t B, int64_t T, int64_t F, int path,
                  cudaStream_t stream) {
+  if (!btf_path_ok(path)) return RQF_ERR_ARGUMENT;
   int st = btf_dims_ok(B, T, F);
   if (st != RQF_OK) return st;
   if (F == 0) return RQF_OK;
@@ -431,7 +444,7 @@ int btf_backward(int drive, const float *c1, const float *c2, const float *tap1,
       !aligned(scratch, 16) || !aligned(x, drive == kReal ? 4 : 8) ||
       !aligned(gx, drive == kReal ? 4 : 8) || (tap1 && !aligned(tap1, 8)))
     return RQF_ERR_ALIGN;
-  if (btf_streaming(B, F)) {
+  if (btf_streaming(B, F, path)) {
     const bs::BtfArgs sa = btfs_args(c1, c2, tap1, x, gy, gx, nullptr,
                                      const_cast<float *>(carries), scratch, B, T, F);
     st = drive == kReal    ? btfs_launch<1, kReal>(sa, scratch, stream)
@@ -517,12 +530,6 @@ int rqf_selftest_lookback_timeout(void *scratch, rqf_stream_t stream) {
 }
 
 // ---------------------------------------------------------------- sizes
-int rqf_btf_select_path(int path) {
-  if (path < 0 || path > 2) return -1;
-  const int prev = g_btf_path;
-  g_btf_path = path;
-  return prev;
-}
 
 int64_t rqf_btf_num_tiles(int64_t time) { return btf_nsub(time); }
 int64_t rqf_btf_carry_count(int64_t batch, int64_t time, int64_t filters) {
@@ -537,6 +544,7 @@ int64_t rqf_fbt_carry_count(int64_t filters, int64_t batch, int64_t time) {
   return filters * batch * rqf_fbt_num_tiles(time);
 }
 size_t rqf_fbt_scratch_bytes(int64_t filters, int64_t batch, int64_t time) {
+  if (fbt_dims_ok(filters, batch, time) != RQF_OK) return SIZE_MAX;  // no such launch
   if (batch <= 0 || time <= 0 || filters <= 0) return 256;
   return scratch_layout(filters * batch, rqf_fbt_num_tiles(time)).total;
 }
@@ -544,16 +552,16 @@ size_t rqf_fbt_scratch_bytes(int64_t filters, int64_t batch, int64_t time) {
 // --------------------------------------------------------- BTF scans
 int rqf_chunked_scan_forward(const float *c1, const float *c2, const void *u, int u_is_real,
                              float *y, float *carries, void *scratch, int64_t batch,
-                             int64_t time, int64_t filters, rqf_stream_t stream) {
+                             int64_t time, int64_t filters, int path, rqf_stream_t stream) {
   return btf_forward(u_is_real ? kReal : kPlain, c1, c2, nullptr, u, y, carries, scratch, batch,
-                     time, filters, stream);
+                     time, filters, path, stream);
 }
 
 int rqf_chunked_scan_abs_forward(const float *c1, const float *c2, const void *u, int u_is_real,
                                  float *y_abs, void *scratch, int64_t batch, int64_t time,
-                                 int64_t filters, rqf_stream_t stream) {
+                                 int64_t filters, int path, rqf_stream_t stream) {
   return btf_forward(u_is_real ? kReal : kPlain, c1, c2, nullptr, u, y_abs, nullptr, scratch,
-                     batch, time, filters, stream, true);
+                     batch, time, filters, path, stream, true);
 }
 
 int rqf_multi_osc_forward(const float *c1, const float *c2, const float *cw, const void *u,
@@ -634,26 +642,27 @@ size_t rqf_multi_osc_scratch_bytes(int64_t batch, int64_t time, int64_t filters,
 int rqf_chunked_scan_backward(const float *c1, const float *c2, const void *u, int u_is_real,
                               const float *carries, const float *grad_y, void *grad_u,
                               float *grad_c1, float *grad_c2, void *scratch, int64_t batch,
-                              int64_t time, int64_t filters, rqf_stream_t stream) {
+                              int64_t time, int64_t filters, int path, rqf_stream_t stream) {
   return btf_backward(u_is_real ? kReal : kPlain, c1, c2, nullptr, u, carries, grad_y, grad_u,
-                      grad_c1, grad_c2, nullptr, scratch, batch, time, filters, stream);
+                      grad_c1, grad_c2, nullptr, scratch, batch, time, filters, path, stream);
 }
 
 int rqf_chunked_prospective_forward(const float *c1, const float *tap0, const float *tap1,
                                     const float *x, float *y, float *carries, void *scratch,
-                                    int64_t batch, int64_t time, int64_t filters,
+                                    int64_t batch, int64_t time, int64_t filters, int path,
                                     rqf_stream_t stream) {
   return btf_forward(kTwoTap, c1, tap0, tap1, x, y, carries, scratch, batch, time, filters,
-                     stream);
+                     path, stream);
 }
 
 int rqf_chunked_prospective_backward(const float *c1, const float *tap0, const float *tap1,
                                      const float *x, const float *carries, const float *grad_y,
                                      float *grad_x, float *grad_c1, float *grad_tap0,
                                      float *grad_tap1, void *scratch, int64_t batch,
-                                     int64_t time, int64_t filters, rqf_stream_t stream) {
+                                     int64_t time, int64_t filters, int path,
+                                     rqf_stream_t stream) {
   return btf_backward(kTwoTap, c1, tap0, tap1, x, carries, grad_y, grad_x, grad_c1, grad_tap0,
-                      grad_tap1, scratch, batch, time, filters, stream);
+                      grad_tap1, scratch, batch, time, filters, path, stream);
 }
 
 // --------------------------------------------------------- FBT scans
@@ -781,8 +790,9 @@ int rqf_tbptt1_two_tap_backward(int layout, const float *c1, const float *tap0,
                                 const float *grad_out, float *grad_z, float *grad_zw,
                                 float *grad_c1, float *grad_tap0, float *grad_tap1,
                                 void *scratch, int64_t d0, int64_t d1, int64_t d2, int fuse_act,
-                                rqf_stream_t stream) {
+                                int path, rqf_stream_t stream) {
   if (layout != 0 && layout != 1) return RQF_ERR_ARGUMENT;
+  if (!btf_path_ok(path)) return RQF_ERR_ARGUMENT;
   const int64_t F = layout == 0 ? d2 : d0;
   const int64_t B = layout == 0 ? d0 : d1;
   const int64_t T = layout == 0 ? d1 : d2;
@@ -803,7 +813,7 @@ int rqf_tbptt1_two_tap_backward(int layout, const float *c1, const float *tap0,
   if (layout == 0) {
     // the (B,T,F) forward has no fused activation, so neither has its TBPTT(1) backward
     if (fuse_act) return RQF_ERR_ARGUMENT;
-    if (btf_streaming(B, F)) {
+    if (btf_streaming(B, F, path)) {
       const bs::BtfArgs sa = btfs_args(c1, tap0, tap1, z, grad_out, grad_z, grad_zw,
                                        const_cast<float *>(carries), scratch, B, T, F);
       if ((st = btfs_launch<2, kTwoTap>(sa, scratch, stream)) != RQF_OK) return st;
@@ -1508,17 +1518,81 @@ int rqf_readout_relu_pool_backward(const uint32_t *mask, const float *scale, flo
 // ------------------------------------------------ two-tap coefficient producer
 extern "C" {
 
+namespace {
+int coeff_setup(const rqf_coeff_leaves *leaves, const rqf_coeff_options *opts, int64_t n,
+                coef::Leaves *L, coef::Opts *o) {
+  if (!leaves || !opts || n < 0) return RQF_ERR_ARGUMENT;
+  const int disc = opts->discretization;
+  if (disc != RQF_DISC_EULER && disc != RQF_DISC_ZOH && disc != RQF_DISC_FOH)
+    return RQF_ERR_ARGUMENT;
+  if (!opts->prospective && disc != RQF_DISC_FOH) return RQF_ERR_ARGUMENT;  // single-tap forms
+  if (opts->param_space != 0 && opts->param_space != 1) return RQF_ERR_ARGUMENT;
+  if (!(opts->dt > 0.0)) return RQF_ERR_ARGUMENT;
+  if (!leaves->log_tau && !(opts->tau > 0.0)) return RQF_ERR_ARGUMENT;
+  if (n > 0 && (!leaves->theta_leaf || !leaves->gamma_leaf)) return RQF_ERR_ARGUMENT;
+  if (n > 0 && opts->param_space == 1 &&
+      (!leaves->min_gamma || !leaves->max_gamma || !leaves->min_freq || !leaves->max_freq))
+    return RQF_ERR_ARGUMENT;
+  *L = {leaves->theta_leaf, leaves->gamma_leaf, leaves->log_tau, leaves->min_gamma,
+        leaves->max_gamma, leaves->min_freq, leaves->max_freq, leaves->prospective_tau};
+  *o = {disc, opts->prospective ? 1 : 0, opts->gamma_mode ? 1 : 0, opts->param_space,
+        opts->clamp_gamma ? 1 : 0, opts->dt, opts->tau};
+  return RQF_OK;
+}
+}  // namespace
+
+int rqf_filter_two_tap_coefficients(const rqf_coeff_leaves *leaves, const rqf_coeff_options *opts,
+                                    float *c1, float *tap0, float *tap1, int64_t n,
+                                    rqf_stream_t stream) {
+  coef::Leaves L;
+  coef::Opts o;
+  const int rc = coeff_setup(leaves, opts, n, &L, &o);
+  if (rc != RQF_OK) return rc;
+  if (n == 0) return RQF_OK;
+  if (!c1 || !tap0 || !tap1) return RQF_ERR_ARGUMENT;
+  if (!aligned(c1, 8) || !aligned(tap0, 8) || !aligned(tap1, 8)) return RQF_ERR_ALIGN;
+  coef::two_tap_kernel<<<(unsigned)ceil_div(n, 256), 256, 0,
+                         reinterpret_cast<cudaStream_t>(stream)>>>(
+      L, o, reinterpret_cast<float2 *>(c1), reinterpret_cast<float2 *>(tap0),
+      reinterpret_cast<float2 *>(tap1), n);
+  return launch_status();
+}
+
+int rqf_filter_two_tap_coefficients_backward(const rqf_coeff_leaves *leaves,
+                                             const rqf_coeff_options *opts, const float *grad_c1,
+                                             const float *grad_tap0, const float *grad_tap1,
+                                             float *grad_theta_leaf, float *grad_gamma_leaf,
+                                             float *grad_log_tau, float *grad_prospective_tau,
+                                             int64_t n, rqf_stream_t stream) {
+  coef::Leaves L;
+  coef::Opts o;
+  const int rc = coeff_setup(leaves, opts, n, &L, &o);
+  if (rc != RQF_OK) return rc;
+  if (n == 0) return RQF_OK;
+  if (grad_log_tau && !leaves->log_tau) return RQF_ERR_ARGUMENT;
+  if (grad_prospective_tau && !leaves->prospective_tau) return RQF_ERR_ARGUMENT;
+  if ((grad_c1 && !aligned(grad_c1, 8)) || (grad_tap0 && !aligned(grad_tap0, 8)) ||
+      (grad_tap1 && !aligned(grad_tap1, 8)))
+    return RQF_ERR_ALIGN;
+  if (!grad_theta_leaf && !grad_gamma_leaf && !grad_log_tau && !grad_prospective_tau)
+    return RQF_OK;
+  coef::two_tap_backward_kernel<<<(unsigned)ceil_div(n, 128), 128, 0,
+                                  reinterpret_cast<cudaStream_t>(stream)>>>(
+      L, o, reinterpret_cast<const float2 *>(grad_c1), reinterpret_cast<const float2 *>(grad_tap0),
+      reinterpret_cast<const float2 *>(grad_tap1), grad_theta_leaf, grad_gamma_leaf, grad_log_tau,
+      grad_prospective_tau, n);
+  return launch_status();
+}
+
+// The log-space ZOH tau-mode form with a scalar tau: the general producer
+// with those options.
 int rqf_two_tap_coefficients(const float *log_theta, const float *log_gamma, float *c1, float *tap0,
                              float *tap1, int64_t n, double dt, double tau, rqf_stream_t stream) {
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (n < 0 || !(tau > 0.0) || !(dt > 0.0)) return RQF_ERR_ARGUMENT;
-  if (n == 0) return RQF_OK;
-  if (!log_theta || !log_gamma || !c1 || !tap0 || !tap1) return RQF_ERR_ARGUMENT;
-  if (!aligned(c1, 8) || !aligned(tap0, 8) || !aligned(tap1, 8)) return RQF_ERR_ALIGN;
-  coef::two_tap_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(
-      log_theta, log_gamma, reinterpret_cast<float2 *>(c1), reinterpret_cast<float2 *>(tap0),
-      reinterpret_cast<float2 *>(tap1), n, dt / tau);
-  return launch_status();
+  const rqf_coeff_leaves L = {log_theta, log_gamma, nullptr, nullptr,
+                              nullptr,   nullptr,   nullptr, nullptr};
+  const rqf_coeff_options o = {RQF_DISC_ZOH, 1, 0, 0, 0, dt, tau};
+  return rqf_filter_two_tap_coefficients(&L, &o, c1, tap0, tap1, n, stream);
 }
 
 int rqf_two_tap_coefficients_backward(const float *log_theta, const float *log_gamma,
@@ -1526,18 +1600,14 @@ int rqf_two_tap_coefficients_backward(const float *log_theta, const float *log_g
                                       const float *grad_tap1, float *grad_log_theta,
                                       float *grad_log_gamma, int64_t n, double dt, double tau,
                                       rqf_stream_t stream) {
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (n < 0 || !(tau > 0.0) || !(dt > 0.0)) return RQF_ERR_ARGUMENT;
-  if (n == 0) return RQF_OK;
-  if (!log_theta || !log_gamma || !grad_log_theta || !grad_log_gamma) return RQF_ERR_ARGUMENT;
-  if ((grad_c1 && !aligned(grad_c1, 8)) || (grad_tap0 && !aligned(grad_tap0, 8)) ||
-      (grad_tap1 && !aligned(grad_tap1, 8)))
-    return RQF_ERR_ALIGN;
-  coef::two_tap_backward_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(
-      log_theta, log_gamma, reinterpret_cast<const float2 *>(grad_c1),
-      reinterpret_cast<const float2 *>(grad_tap0), reinterpret_cast<const float2 *>(grad_tap1),
-      grad_log_theta, grad_log_gamma, n, dt / tau);
-  return launch_status();
+  if (n > 0 && (!grad_log_theta || !grad_log_gamma)) return RQF_ERR_ARGUMENT;
+  const rqf_coeff_leaves L = {log_theta, log_gamma, nullptr, nullptr,
+                              nullptr,   nullptr,   nullptr, nullptr};
+  const rqf_coeff_options o = {RQF_DISC_ZOH, 1, 0, 0, 0, dt, tau};
+  return rqf_filter_two_tap_coefficients_backward(&L, &o, grad_c1, grad_tap0, grad_tap1,
+                                                  grad_log_theta, grad_log_gamma, nullptr,
+                                                  nullptr, n, stream);
 }
 
 }  // extern "C"

@@ -17,11 +17,16 @@ Call sites served (reference paths):
   rqf_models/backbones/rqf/pure.py:234-238    -> fbt_prospective_scan / fbt_recompute_scan
   rqf_models/backbones/rqf/block.py:882, :904 -> TBPTT(1) fused surrogate on CUDA
   rqf_models/ops/selective_scan.py:119, :133   -> selective_forward / selective_backward
+  rqf_models/backbones/rqf/filter.py:510       -> RQF.compute_two_tap_coefficients on fp32
+                                                  CUDA leaves (every caller: pure.py:225,
+                                                  block.py's prospective paths, selective.py)
 """
 
 from __future__ import annotations
 
 import importlib
+
+import torch
 
 from . import ops
 
@@ -94,6 +99,21 @@ def _cuda_parallel_scan(orig):
     return parallel_scan
 
 
+def _filter_coefficients(orig):
+    """RQF.compute_two_tap_coefficients: fp32 CUDA leaves take the fused
+    producer (ops.filter_two_tap_coefficients); other dtypes and devices keep
+    the reference's own torch expressions."""
+    def compute_two_tap_coefficients(self, prospective=True, mode="tau", prospective_tau=None):
+        leaves = [self.log_tau] + ([self.log_theta, self.log_gamma] if self.param_space == "log"
+                                   else [self.freq_param, self.gamma_param])
+        if all(t.is_cuda and t.dtype == torch.float32 for t in leaves):
+            return ops.filter_two_tap_coefficients(self, prospective, mode, prospective_tau)
+        return orig(self, prospective, mode, prospective_tau)
+
+    compute_two_tap_coefficients.__wrapped__ = orig
+    return compute_two_tap_coefficients
+
+
 # (module, attribute, wrapper of the original)
 _WRAPPED = [
     ("rqf_models.backbones.s5.layer", "parallel_scan", _cuda_parallel_scan),
@@ -121,6 +141,11 @@ def install() -> list[str]:
             _SAVED.append((mod, attr, orig))
             setattr(mod, attr, wrap(orig))
             patched.append(f"{mod_name}.{attr}")
+    rqf_cls = importlib.import_module("rqf_models.backbones.rqf.filter").RQF
+    orig = rqf_cls.compute_two_tap_coefficients
+    _SAVED.append((rqf_cls, "compute_two_tap_coefficients", orig))
+    rqf_cls.compute_two_tap_coefficients = _filter_coefficients(orig)
+    patched.append("rqf_models.backbones.rqf.filter.RQF.compute_two_tap_coefficients")
     block = importlib.import_module("rqf_models.backbones.rqf.block")
     base = block.BaseRQFBlock
     for attr, wrap in (("_scan_two_tap_with_grad_mode", _tbptt_two_tap),

@@ -25,6 +25,7 @@ _scan_with_grad_mode :882-902):
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 
@@ -99,6 +100,28 @@ def _nbytes(*tensors) -> int:
     return sum(t.numel() * t.element_size() for t in tensors if t is not None)
 
 
+# (B,T,F) kernel family for the next forwards: 0 automatic (by the number of
+# chains of batch x 32 channels), 1 streaming, 2 tile-resident.  Every forward
+# records the value it was given in its saved context and its backward passes
+# that same value, so the two always use the same family (their saved entry
+# states differ).
+_BTF_PATH = 0
+
+
+@contextlib.contextmanager
+def btf_kernel_family(path: int):
+    """Force one (B,T,F) kernel family for the forwards run inside (tests,
+    microbenchmarks); 0 restores the automatic choice."""
+    global _BTF_PATH
+    if path not in (0, 1, 2):
+        raise ValueError(f"path must be 0, 1 or 2, got {path!r}")
+    prev, _BTF_PATH = _BTF_PATH, int(path)
+    try:
+        yield
+    finally:
+        _BTF_PATH = prev
+
+
 def _shape3(x: torch.Tensor, what: str):
     if x.dim() != 3:
         raise ValueError(f"{what} must be 3-D, got shape {tuple(x.shape)}")
@@ -125,10 +148,11 @@ class _ChunkedScanFunction(torch.autograd.Function):
         with _timing.launch("rqf_chunked_scan_forward", B * T * F, _nbytes(uu, y)):
             _abi.check(lib.rqf_chunked_scan_forward(
                 _abi.ptr(c1), _abi.ptr(c2), _abi.ptr(uu), int(real), _abi.ptr(y), _abi.ptr(carries),
-                _abi.ptr(scratch), B, T, F, _abi.stream_of(uu)), "rqf_chunked_scan_forward")
+                _abi.ptr(scratch), B, T, F, _BTF_PATH, _abi.stream_of(uu)),
+                "rqf_chunked_scan_forward")
         _done(dev)
         ctx.save_for_backward(c1, c2, uu, carries)
-        ctx.real = real
+        ctx.real, ctx.path = real, _BTF_PATH
         return y
 
     @staticmethod
@@ -147,7 +171,7 @@ class _ChunkedScanFunction(torch.autograd.Function):
             _abi.check(lib.rqf_chunked_scan_backward(
                 _abi.ptr(c1), _abi.ptr(c2), _abi.ptr(uu), int(ctx.real), _abi.ptr(carries),
                 _abi.ptr(gy), _abi.ptr(gu), _abi.ptr(gc1), _abi.ptr(gc2), _abi.ptr(scratch),
-                B, T, F, _abi.stream_of(gy)), "rqf_chunked_scan_backward")
+                B, T, F, ctx.path, _abi.stream_of(gy)), "rqf_chunked_scan_backward")
         _done(dev)
         need = ctx.needs_input_grad
         return (gc1 if need[0] else None, gc2 if need[1] else None, gu if need[2] else None)
@@ -178,9 +202,11 @@ class _ChunkedProspectiveScanFunction(torch.autograd.Function):
         with _timing.launch("rqf_chunked_prospective_forward", B * T * F, _nbytes(xx, y)):
             _abi.check(lib.rqf_chunked_prospective_forward(
                 _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1), _abi.ptr(xx), _abi.ptr(y), _abi.ptr(carries),
-                _abi.ptr(scratch), B, T, F, _abi.stream_of(xx)), "rqf_chunked_prospective_forward")
+                _abi.ptr(scratch), B, T, F, _BTF_PATH, _abi.stream_of(xx)),
+                "rqf_chunked_prospective_forward")
         _done(dev)
         ctx.save_for_backward(c1, t0, t1, xx, carries)
+        ctx.path = _BTF_PATH
         return y
 
     @staticmethod
@@ -198,7 +224,8 @@ class _ChunkedProspectiveScanFunction(torch.autograd.Function):
             _abi.check(lib.rqf_chunked_prospective_backward(
                 _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1), _abi.ptr(xx), _abi.ptr(carries),
                 _abi.ptr(gy), _abi.ptr(gx), _abi.ptr(gc1), _abi.ptr(gt0), _abi.ptr(gt1),
-                _abi.ptr(scratch), B, T, F, _abi.stream_of(gy)), "rqf_chunked_prospective_backward")
+                _abi.ptr(scratch), B, T, F, ctx.path, _abi.stream_of(gy)),
+                "rqf_chunked_prospective_backward")
         _done(dev)
         need = ctx.needs_input_grad
         return (gc1 if need[0] else None, gt0 if need[1] else None, gt1 if need[2] else None,
@@ -342,20 +369,20 @@ class _TBPTT1TwoTap(torch.autograd.Function):
             with _timing.launch("rqf_chunked_prospective_forward", B * T * F, _nbytes(z, out)):
                 _abi.check(lib.rqf_chunked_prospective_forward(
                     _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1), _abi.ptr(z), _abi.ptr(out),
-                    _abi.ptr(carries), _abi.ptr(scratch), B, T, F, _abi.stream_of(z)),
+                    _abi.ptr(carries), _abi.ptr(scratch), B, T, F, _BTF_PATH, _abi.stream_of(z)),
                     "rqf_chunked_prospective_forward")
             _done(dev)
             dims = (B, T, F)
         ctx.save_for_backward(c1, t0, t1, z, carries)
         ctx.layout, ctx.fuse_act, ctx.dims = layout, bool(fuse_act), dims
-        ctx.has_lag = delayed_u is not None
+        ctx.has_lag, ctx.path = delayed_u is not None, _BTF_PATH
         return out
 
     @staticmethod
     @once_differentiable
     def backward(ctx, grad_output):
         gc1, gt0, gt1, gz, gzw = _tbptt_backward(ctx.saved_tensors, ctx.layout, ctx.dims,
-                                                 grad_output, ctx.fuse_act)
+                                                 grad_output, ctx.fuse_act, ctx.path)
         need = ctx.needs_input_grad
         if ctx.has_lag:
             gu, gd = gz, gzw
@@ -365,7 +392,7 @@ class _TBPTT1TwoTap(torch.autograd.Function):
                 gu if need[3] else None, gd if (need[4] and gd is not None) else None, None, None)
 
 
-def _tbptt_backward(saved, layout, dims, grad_output, fuse_act):
+def _tbptt_backward(saved, layout, dims, grad_output, fuse_act, path=0):
     """TBPTT(1) surrogate VJP kernel: returns (gc1, gtap0, gtap1, gz, gzw)."""
     c1, t0, t1, z, carries = saved
     dev = z.device
@@ -384,7 +411,7 @@ def _tbptt_backward(saved, layout, dims, grad_output, fuse_act):
             0 if layout == "btf" else 1, _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1),
             _abi.ptr(z), _abi.ptr(carries), _abi.ptr(gy), _abi.ptr(gz), _abi.ptr(gzw),
             _abi.ptr(gc1), _abi.ptr(gt0), _abi.ptr(gt1), _abi.ptr(scratch), d0, d1, d2,
-            int(bool(fuse_act)), _abi.stream_of(gy)), "rqf_tbptt1_two_tap_backward")
+            int(bool(fuse_act)), int(path), _abi.stream_of(gy)), "rqf_tbptt1_two_tap_backward")
     _done(dev)
     return gc1, gt0, gt1, gz, gzw
 
@@ -450,7 +477,7 @@ def _scan_abs(C1, C2, u) -> torch.Tensor:
     with _timing.launch("rqf_chunked_scan_abs_forward", B * T * F, _nbytes(uu, y)):
         _abi.check(lib.rqf_chunked_scan_abs_forward(
             _abi.ptr(c1), _abi.ptr(c2), _abi.ptr(uu), int(real), _abi.ptr(y), _abi.ptr(scratch),
-            B, T, F, _abi.stream_of(uu)), "rqf_chunked_scan_abs_forward")
+            B, T, F, _BTF_PATH, _abi.stream_of(uu)), "rqf_chunked_scan_abs_forward")
     _done(dev)
     return y
 
@@ -1080,3 +1107,109 @@ class TwoTapCoefficients(torch.autograd.Function):
             lt.numel(), ctx.dt, ctx.tau, _abi.stream_of(lt)), "rqf_two_tap_coefficients_backward")
         _done(lt.device)
         return glt, glg, None, None
+
+
+# ------------------------------------------- RQF filter-bank coefficients
+_DISCRETIZATIONS = {"euler": 0, "zoh": 1, "foh": 2}
+
+
+class FilterTwoTapCoefficients(torch.autograd.Function):
+    """(C1, tap0, tap1) complex64 of an RQF filter bank's leaves, every
+    two-tap branch of filter.py:510-664 (rqf_filter_two_tap_coefficients and
+    its backward: one launch each, double inside, derivatives carried through
+    every branch).  Gradients reach the theta / gamma leaves, log_tau and a
+    prospective_tau tensor when they need one; the sigmoid bounds are
+    constants (buffers in the reference)."""
+
+    @staticmethod
+    def forward(ctx, theta_leaf, gamma_leaf, log_tau, tau_p, min_g, max_g, min_f, max_f, disc,
+                prospective, gamma_mode, sigmoid, clamp, dt):
+        dev = _require_cuda(theta_leaf, gamma_leaf, log_tau, tau_p, min_g, max_g, min_f, max_f)
+        n = theta_leaf.numel()
+
+        def f32(t):
+            if t is None:
+                return None
+            t = t.detach().to(torch.float32).contiguous()
+            if t.numel() != n:
+                raise ValueError(f"filter-bank tensor of {t.numel()} elements, expected {n}")
+            return t
+
+        ts = [f32(t) for t in (theta_leaf, gamma_leaf, log_tau, min_g, max_g, min_f, max_f,
+                               tau_p)]
+        leaves = _abi.CoeffLeaves(*(_abi.ptr(t) for t in ts))
+        opts = _abi.CoeffOptions(int(disc), int(prospective), int(gamma_mode), int(sigmoid),
+                                 int(clamp), float(dt), 0.0)
+        outs = [torch.empty(theta_leaf.shape, dtype=torch.complex64, device=dev)
+                for _ in range(3)]
+        lib = _abi.load()
+        with _timing.launch("rqf_filter_two_tap_coefficients", n, 0):
+            _abi.check(lib.rqf_filter_two_tap_coefficients(
+                ctypes.byref(leaves), ctypes.byref(opts), *(_abi.ptr(o) for o in outs), n,
+                _abi.stream_of(outs[0])), "rqf_filter_two_tap_coefficients")
+        _done(dev)
+        ctx.save_for_backward(*[t for t in ts])
+        ctx.has = [t is not None for t in ts]
+        ctx.opts = (int(disc), int(prospective), int(gamma_mode), int(sigmoid), int(clamp),
+                    float(dt))
+        ctx.shapes = [None if t is None else t.shape for t in (theta_leaf, gamma_leaf, log_tau,
+                                                                tau_p)]
+        return tuple(outs)
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, g1, g0, gm):
+        ts = list(ctx.saved_tensors)
+        n = ts[0].numel()
+        leaves = _abi.CoeffLeaves(*(_abi.ptr(t) for t in ts))
+        opts = _abi.CoeffOptions(*ctx.opts[:5], ctx.opts[5], 0.0)
+        need = ctx.needs_input_grad
+        gs = [None if g is None else _c64(g) for g in (g1, g0, gm)]
+        # outputs: theta leaf, gamma leaf, log_tau, tau_p
+        want = [need[0], need[1], need[2] and ts[2] is not None, need[3] and ts[7] is not None]
+        grads = [torch.empty(n, dtype=torch.float32, device=ts[0].device) if w else None
+                 for w in want]
+        lib = _abi.load()
+        _abi.check(lib.rqf_filter_two_tap_coefficients_backward(
+            ctypes.byref(leaves), ctypes.byref(opts), *(_abi.ptr(g) for g in gs),
+            *(_abi.ptr(g) for g in grads), n, _abi.stream_of(ts[0])),
+            "rqf_filter_two_tap_coefficients_backward")
+        _done(ts[0].device)
+        out = [None if g is None else g.view(shape)
+               for g, shape in zip(grads, ctx.shapes)]
+        return (*out, None, None, None, None, None, None, None, None, None, None)
+
+
+def filter_two_tap_coefficients(rqf, prospective: bool = True, mode: str = "tau",
+                                prospective_tau=None):
+    """Drop-in for RQF.compute_two_tap_coefficients (filter.py:510-664) of an
+    RQF module whose leaves are fp32 CUDA tensors: the same (C1, tap0, tap1),
+    the same errors for the forms without a two-tap update, Euler's taps real
+    as the reference returns them."""
+    if mode not in ("tau", "gamma"):
+        raise ValueError(f"mode must be one of ('tau', 'gamma'), got {mode!r}")
+    disc = rqf.discretization
+    if disc == "bilinear":
+        raise NotImplementedError(
+            "Two-tap update is not defined for bilinear discretization. "
+            "Use 'euler', 'zoh', or 'foh'.")
+    if disc in ("euler", "zoh") and not prospective:
+        raise NotImplementedError(
+            f"Non-prospective {'Euler' if disc == 'euler' else 'ZOH'} uses the single-tap "
+            "recurrence; call compute_coefficients() instead.")
+    log_tau = rqf.log_tau
+    if rqf.param_space == "log":
+        theta_leaf, gamma_leaf, bounds, sigmoid = rqf.log_theta, rqf.log_gamma, (None,) * 4, 0
+    else:
+        theta_leaf, gamma_leaf, sigmoid = rqf.freq_param, rqf.gamma_param, 1
+        bounds = (rqf._min_gamma, rqf._max_gamma, rqf._min_freq, rqf._max_freq)
+    tau_p = None
+    if prospective_tau is not None:
+        tau_p = torch.as_tensor(prospective_tau, dtype=log_tau.dtype, device=log_tau.device)
+        tau_p = tau_p.expand(log_tau.shape)
+    c1, t0, t1 = FilterTwoTapCoefficients.apply(
+        theta_leaf, gamma_leaf, log_tau, tau_p, *bounds, _DISCRETIZATIONS[disc],
+        bool(prospective), mode == "gamma", sigmoid, bool(rqf.clamp_gamma), float(rqf.dt))
+    if disc == "euler":
+        return c1, t0.real, t1.real
+    return c1, t0, t1

@@ -84,16 +84,19 @@ def test_size_queries(lib):
     assert lib.rqf_btf_scratch_bytes(0, 10, 10) == 256
 
 
-def test_btf_path_selector(lib):
-    prev = lib.rqf_btf_select_path(2)
-    try:
-        assert prev == 0
-        assert lib.rqf_btf_select_path(1) == 2
-        assert lib.rqf_btf_select_path(3) == -1
-        assert lib.rqf_btf_select_path(-1) == -1
-        assert lib.rqf_btf_select_path(0) == 1
-    finally:
-        lib.rqf_btf_select_path(prev)
+def test_btf_path_is_a_per_call_argument(lib):
+    """The (B,T,F) kernel family is chosen per call (0 automatic, 1 streaming,
+    2 tile-resident); anything else is rejected before any CUDA call."""
+    assert not hasattr(lib, "rqf_btf_select_path")
+    for bad in (3, -1):
+        assert lib.rqf_chunked_scan_forward(None, None, None, 0, None, None, None,
+                                            2, 3, 4, bad, None) == 5
+        assert lib.rqf_chunked_prospective_backward(None, None, None, None, None, None, None,
+                                                    None, None, None, None, 2, 3, 4, bad,
+                                                    None) == 5
+        assert lib.rqf_tbptt1_two_tap_backward(0, None, None, None, None, None, None, None,
+                                               None, None, None, None, None, 1, 1, 1, 0, bad,
+                                               None) == 5
 
 
 def test_host_side_validation_needs_no_gpu(lib):
@@ -106,11 +109,11 @@ def test_host_side_validation_needs_no_gpu(lib):
     assert lib.rqf_fbt_prospective_forward(None, None, None, None, None, None, None,
                                            4, 0, 10, 1, None) == 0
     assert lib.rqf_chunked_scan_forward(None, None, None, 0, None, None, None,
-                                        2, 3, -4, None) == 1
+                                        2, 3, -4, 0, None) == 1
     assert lib.rqf_chunked_scan_forward(None, None, None, 0, None, None, None,
-                                        2, 3, 4, None) == 5
+                                        2, 3, 4, 0, None) == 5
     assert lib.rqf_tbptt1_two_tap_backward(7, None, None, None, None, None, None, None, None,
-                                           None, None, None, None, 1, 1, 1, 0, None) == 5
+                                           None, None, None, None, 1, 1, 1, 0, 0, None) == 5
     # misaligned pointers -> RQF_ERR_ALIGN
     buf = (ctypes.c_char * 64)()
     base = ctypes.addressof(buf)

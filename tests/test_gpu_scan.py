@@ -33,15 +33,12 @@ def rqf():
 
 @pytest.fixture(params=[1, 2], ids=["streaming", "resident"])
 def btf_path(request):
-    """Runs a (B,T,F) test under each kernel family (rqf_btf_select_path):
-    1 = streaming (few chains), 2 = tile-resident (many chains)."""
-    from prospective_rqf_b200 import _abi
+    """Runs a (B,T,F) test under each kernel family (the per-call path
+    argument): 1 = streaming (few chains), 2 = tile-resident (many chains)."""
+    from prospective_rqf_b200 import ops
 
-    lib = _abi.load()
-    prev = lib.rqf_btf_select_path(request.param)
-    assert prev >= 0
-    yield request.param
-    lib.rqf_btf_select_path(prev)
+    with ops.btf_kernel_family(request.param):
+        yield request.param
 
 
 def dev(a, dtype=torch.complex64, grad=False):

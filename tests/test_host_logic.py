@@ -81,6 +81,22 @@ def _fake_reference(monkeypatch):
             return "reference-single-tap"
 
     sys.modules["rqf_models.backbones.rqf.block"].BaseRQFBlock = BaseRQFBlock
+
+    class RQF:
+        param_space = "log"
+
+        def __init__(self):
+            self.log_tau = torch.zeros(3)
+            self.log_theta = torch.zeros(3)
+            self.log_gamma = torch.zeros(3)
+
+        def compute_two_tap_coefficients(self, prospective=True, mode="tau",
+                                         prospective_tau=None):
+            return "reference-coefficients"
+
+    filt = types.ModuleType("rqf_models.backbones.rqf.filter")
+    filt.RQF = RQF
+    monkeypatch.setitem(sys.modules, "rqf_models.backbones.rqf.filter", filt)
     return BaseRQFBlock
 
 
@@ -100,6 +116,11 @@ def test_install_rebinds_and_uninstall_restores(monkeypatch):
         assert blk._scan_two_tap_with_grad_mode(c(1, 2, 3), c(3), c(3), c(3)) == \
             "reference-two-tap"
         assert blk._scan_with_grad_mode(c(1, 2, 3), c(3), c(3)) == "reference-single-tap"
+        # Coefficient producer: CPU leaves keep the reference's own torch path.
+        filt = sys.modules["rqf_models.backbones.rqf.filter"]
+        assert "rqf_models.backbones.rqf.filter.RQF.compute_two_tap_coefficients" in patched
+        assert filt.RQF().compute_two_tap_coefficients() == "reference-coefficients"
+        assert filt.RQF.compute_two_tap_coefficients.__wrapped__ is not None
     finally:
         integration.uninstall()
     assert sys.modules["rqf_models.ops.scan"]._triton_chunked_scan == "orig"
@@ -126,7 +147,7 @@ def test_install_against_the_reference_tree(monkeypatch):
         assert sk.selective_forward is ops.selective_forward
         assert scan._sequential_scan_forward_abs_raw_block_f is \
             ops._sequential_scan_forward_abs_raw_block_f
-        assert len(patched) == 21
+        assert len(patched) == 22
     finally:
         integration.uninstall()
 
