@@ -412,10 +412,20 @@ __global__ void __launch_bounds__(NT, 3) fbt_tbptt_rows_kernel(const FbtArgs a) 
     read_blocked<K>(gbuf, go, lane);
     float2 zp = shfl_up2(z[K - 1], 1);
     if (lane == 0) zp = warp > 0 ? read_sample<K>(zbuf - WSZ, 32 * K - 1) : s_meta[s][1];
+    // The drive exactly as fbt_fwd_rows_kernel forms it (same paired FMAs), so
+    // the replayed states, and with them the split-ReLU decisions, are the
+    // forward's bit for bit.
     float2 b[K];
-    b[0] = c_fma(t1c, zp, c_mul(t0c, z[0]));
+    {
+      const CPair T0 = cpair(t0c), T1 = cpair(t1c);
+      float2 sp = c_swap(zp);
 #pragma unroll
-    for (int k = 1; k < K; ++k) b[k] = c_fma(t1c, z[k - 1], c_mul(t0c, z[k]));
+      for (int k = 0; k < K; ++k) {
+        const float2 sk = c_swap(z[k]);
+        b[k] = cp_fma(T0, z[k], sk, cp_mul(T1, k > 0 ? z[k - 1] : zp, sp));
+        sp = sk;
+      }
+    }
     float2 y = cz();
 #pragma unroll
     for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);

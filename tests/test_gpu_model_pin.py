@@ -14,7 +14,8 @@ results compared:
   first block on the low-rank path and on the general GEMM path;
 * with the reference's PureRQFEncoder on its stock GPU path (its Triton
   kernels, from the offline install in baseline/_ref): the complex features
-  and every parameter gradient of a fixed linear functional of them.
+  and every parameter gradient of mean |h|^2, width 64, depth 6, B = 4,
+  T = 4000, full BPTT and TBPTT(1).
 
 Forward: normwise max relative error <= 1e-4; gradients <= 1e-3 (two fp32
 implementations); the element-wise error (floor 1e-3 of the tensor's maximum)
@@ -144,21 +145,32 @@ def test_encoder_matches_reference_stock_gpu_path(mode, first_block):
 
     gen = torch.Generator(device="cuda").manual_seed(5)
     x = 0.5 * torch.randn(batch, time, 1, device="cuda", generator=gen)
-    cot = torch.randn(batch, time, hidden, dtype=torch.complex64, device="cuda", generator=gen)
 
+    # The loss of the other drop-in comparisons, mean |h|^2: its cotangent
+    # follows the features, as a trained model's does.  (A random cotangent
+    # makes every leaf gradient a sum of B*T terms of random sign that cancel
+    # to ~1/sqrt(B*T) of their size, which both fp32 implementations round
+    # at the 1e-3 level.)
     feats_ref = ref(x)  # (B, T, F) complex
-    (feats_ref * cot.conj()).real.sum().backward()
+    (feats_ref.abs() ** 2).mean().backward()
     xo = x.clone().requires_grad_(first_block == "gemm")
     feats = ours(xo)    # (F, B, T) complex
-    (feats * cot.permute(2, 0, 1).conj()).real.sum().backward()
+    (feats.abs() ** 2).mean().backward()
 
-    assert_close(feats.detach().permute(1, 2, 0).cpu().numpy(), feats_ref.detach().cpu().numpy(),
-                 FWD_TOL, "features", elem_tol=FWD_ELEM_TOL)
+    errs = {"features": assert_close(feats.detach().permute(1, 2, 0).cpu().numpy(),
+                                     feats_ref.detach().cpu().numpy(), FWD_TOL, "features",
+                                     elem_tol=FWD_ELEM_TOL)}
     mine = dict(ours.named_parameters())
     refp = dict(ref.named_parameters())
+    bad = []
     for ref_name, our_name in _load_encoder.items():
         a = mine[our_name[len("encoder."):]].grad
         b = refp[ref_name[len("encoder."):]].grad
         assert a is not None and b is not None, ref_name
-        assert_close(a.cpu().numpy(), b.cpu().numpy(), GRAD_TOL, ref_name,
-                     elem_tol=GRAD_ELEM_TOL)
+        try:
+            errs[ref_name] = assert_close(a.cpu().numpy(), b.cpu().numpy(), GRAD_TOL, ref_name,
+                                          elem_tol=GRAD_ELEM_TOL)
+        except AssertionError as exc:
+            bad.append(str(exc))
+    print({k: f"{v[0]:.2e} / {v[1]:.2e}" for k, v in errs.items()})
+    assert not bad, bad
