@@ -20,6 +20,8 @@ GPU (H=256, 32 samples/GPU, T=16000, full BPTT), weak scaling over N ranks.
            24 B/element backward (g, z, gz).
 `triton_reference` = the reference's own model on its stock GPU path (Triton),
            same B200, same batch shape (N = 1 only), for information;
+`triton_reference_scan` = the workload's layer scan alone, the reference's
+           Triton kernel beside this backend's (N = 1 only), for information;
 `reference_cpu_path` = its own CPU PyTorch path at reduced T, for information.
 """
 
@@ -452,6 +454,45 @@ def reference_gpu_step(cfg, steps: int, warmup: int, device):
                     "path, same B200, same batch shape, from baseline/_ref"}
 
 
+def reference_gpu_scan(cfg, device):
+    """The workload's dominant scan alone, the reference's Triton kernel
+    beside this backend's: fbt_recompute_scan (fbt_scan_kernel.py:667) at the
+    layer shape (F = hidden, B, T), forward + backward, CUDA events, warm."""
+    if _reference_modules() is None:
+        return {"unavailable": "reference install (baseline/_ref) absent"}
+    import prospective_rqf_b200 as rqf
+    from rqf_models.ops.fbt_scan_kernel import fbt_recompute_scan as ref_scan
+
+    F, B, T = cfg.hidden, cfg.batch, cfg.time
+    g = torch.Generator(device=device).manual_seed(3)
+    mag = 0.9 + 0.0999 * torch.rand(F, device=device, generator=g)
+    c1 = torch.polar(mag, 6.283 * torch.rand(F, device=device, generator=g))
+    t0 = 0.3 * torch.randn(F, dtype=torch.complex64, device=device, generator=g)
+    t1 = 0.3 * torch.randn(F, dtype=torch.complex64, device=device, generator=g)
+    z = torch.randn(F, B, T, dtype=torch.complex64, device=device, generator=g)
+    gy = torch.randn_like(z)
+    zz = z.requires_grad_(True)
+
+    def timed(op):
+        def run():
+            y = op(c1, t0, t1, zz)
+            torch.autograd.grad(y, (zz,), gy)
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 5
+
+    ref_ms, ours_ms = timed(ref_scan), timed(rqf.fbt_recompute_scan)
+    return {"op": f"fbt_recompute_scan F={F} B={B} T={T} fwd+bwd", "reference_ms": round(ref_ms, 4),
+            "b200_ms": round(ours_ms, 4), "speedup": round(ref_ms / ours_ms, 3)}
+
+
 def reference_cpu_paths(cfg, threads: int):
     """The reference's own CPU PyTorch path, timed on the host cores:
     PureRQFEncoder forward+backward (per sample, at reduced T: its CPU
@@ -624,6 +665,8 @@ def main():
             tr = line["triton_reference"]
             if isinstance(tr, dict) and tr.get("value"):
                 tr["value_over_reference"] = round(line["value"] / tr["value"], 3)
+            if cfg.scan_grad_mode == "full":
+                line["triton_reference_scan"] = safe_info(reference_gpu_scan, cfg, device)
         threads = os.cpu_count() or 1
         if not args.no_cpu_baseline:
             sps, threads, dt = cpu_reference_steps(cfg, steps=2, warmup=1, batch=1)

@@ -13,12 +13,13 @@ The reference comes from its offline install:
 
 Run from the repository root on a GPU box:
 
-    python baseline/time_reference_triton.py
+    python benchmarks/reference_paths.py
 
 Prints one JSON object: milliseconds per forward+backward (or per pass) for
 each workload, "reference_triton" beside "b200", and the largest relative
-difference of the selective scan's output between the two.  Nothing here is
-part of the backend, its tests or bench.py.
+difference of the selective scan's output between the two.  Op-level detail
+for every configuration; bench.py carries the headline comparison (the full
+training step and the workload's layer scan) in the line the driver records.
 """
 
 from __future__ import annotations
