@@ -16,6 +16,7 @@ from .ops import (
     _triton_chunked_scan,
     _triton_chunked_scan_prospective,
     fbt_prospective_scan,
+    fbt_layer0_real_scan,
     fbt_recompute_scan,
     parallel_scan,
     selective_backward,
@@ -36,6 +37,7 @@ __all__ = [
     "_triton_chunked_scan",
     "_triton_chunked_scan_prospective",
     "fbt_prospective_scan",
+    "fbt_layer0_real_scan",
     "fbt_recompute_scan",
     "parallel_scan",
     "selective_backward",

@@ -15,6 +15,7 @@ Call sites served (reference paths):
   rqf_models/backbones/rqf/block.py:926-934   -> _triton_chunked_scan_prospective
   rqf_models/backbones/rqf/block.py:737-764   -> fused multi-oscillator scans
   rqf_models/backbones/rqf/pure.py:234-238    -> fbt_prospective_scan / fbt_recompute_scan
+  rqf_models/ops/fbt_scan_kernel.py:1005       -> fbt_layer0_real_scan (no caller in the reference)
   rqf_models/backbones/rqf/block.py:882, :904 -> TBPTT(1) fused surrogate on CUDA
   rqf_models/ops/selective_scan.py:119, :133   -> selective_forward / selective_backward
   rqf_models/backbones/rqf/filter.py:510       -> RQF.compute_two_tap_coefficients on fp32
@@ -45,6 +46,7 @@ _BINDINGS = [
      ops._sequential_scan_real_forward_abs_raw_block_f),
     ("rqf_models.ops.fbt_scan_kernel", "fbt_prospective_scan", ops.fbt_prospective_scan),
     ("rqf_models.ops.fbt_scan_kernel", "fbt_recompute_scan", ops.fbt_recompute_scan),
+    ("rqf_models.ops.fbt_scan_kernel", "fbt_layer0_real_scan", ops.fbt_layer0_real_scan),
     ("rqf_models.backbones.rqf.block", "_triton_chunked_scan_prospective",
      ops._triton_chunked_scan_prospective),
     ("rqf_models.backbones.rqf.pure", "fbt_prospective_scan", ops.fbt_prospective_scan),

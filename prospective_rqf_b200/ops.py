@@ -11,6 +11,7 @@ Reference callables (paths inside the reference project):
   _triton_chunked_scan_prospective  rqf_models/ops/chunked_scan_kernel.py:506
   fbt_prospective_scan              rqf_models/ops/fbt_scan_kernel.py:332
   fbt_recompute_scan                rqf_models/ops/fbt_scan_kernel.py:667
+  fbt_layer0_real_scan              rqf_models/ops/fbt_scan_kernel.py:1005
   sequential_scan / parallel_scan   rqf_models/ops/scan.py:290 / :435 (CUDA branch)
   sequential_scan_abs               rqf_models/ops/scan.py:381
   _sequential_scan_forward_abs_raw_block_f        triton_scan_kernel.py:507
@@ -41,6 +42,7 @@ __all__ = [
     "_triton_chunked_scan_prospective",
     "fbt_prospective_scan",
     "fbt_recompute_scan",
+    "fbt_layer0_real_scan",
     "tbptt1_two_tap_scan",
     "tbptt1_scan",
     "sequential_scan",
@@ -334,6 +336,61 @@ def fbt_recompute_scan(C1, tap0, tap1, x_fbt):
     """Split-ReLU two-tap scan with recompute-in-backward — drop-in for
     rqf_models/ops/fbt_scan_kernel.py:fbt_recompute_scan (:667)."""
     return _FBTRecompute.apply(C1, tap0, tap1, x_fbt)
+
+
+# ------------------------------------- real-input first layer, (F,B,T)
+class _Layer0RealScan(torch.autograd.Function):
+    """z = (Wr + i Wi) h for a real h, then the split-ReLU recompute scan
+    (fbt_scan_kernel.py:_Layer0RealScan :899-996).  The projection is the
+    real-operand tensor-core GEMM (rqf_projection_real: a complex W against a
+    real h, half the work of the complex product) writing z interleaved, so
+    the scan reads it as any other layer; backward:
+      grad [Wr; Wi] = [Re P; Im P],  P = gz h^T = (h gz^H)^H   (rqf_projection_weight_grad_real)
+      grad h        = Re(W^H gz)                               (rqf_projection_real_out)."""
+
+    @staticmethod
+    def forward(ctx, w_stacked, h_real, C1, tap0, tap1, batch):
+        dev = _require_cuda(w_stacked, h_real, C1, tap0, tap1)
+        ws = w_stacked.detach().to(torch.float32)
+        if ws.dim() != 2 or ws.shape[0] % 2:
+            raise ValueError(f"w_stacked must be (2*filters, d_model), got {tuple(ws.shape)}")
+        F = ws.shape[0] // 2
+        h = h_real.detach().to(torch.float32).contiguous()
+        if h.dim() != 2 or h.shape[0] != ws.shape[1]:
+            raise ValueError(f"h_real must be ({ws.shape[1]}, batch*time), got {tuple(h.shape)}")
+        batch = int(batch)
+        cols = int(h.shape[1])
+        if batch <= 0 or cols % batch:
+            raise ValueError(f"{cols} columns do not split into batch {batch}")
+        W = torch.complex(ws[:F], ws[F:]).contiguous()
+        z = projection_real(W, h).view(F, batch, cols // batch)
+        out, saved = _fbt_forward(C1, tap0, tap1, z, True)
+        ctx.save_for_backward(W, h, *saved)
+        return out
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_act):
+        W, h, *saved = ctx.saved_tensors
+        gc1, gt0, gt1, gz = _fbt_backward(saved, grad_act, True)
+        need = ctx.needs_input_grad
+        F = W.shape[0]
+        g_ws = g_h = None
+        if need[0]:
+            Pt = projection_weight_grad_real(h, gz.reshape(F, -1))  # h gz^H = P^H, (d, F)
+            g_ws = torch.cat([Pt.real.t(), -Pt.imag.t()], dim=0).contiguous()
+        if need[1]:
+            g_h = projection_real_out(W.mH.contiguous(), gz.reshape(F, -1))
+        return (g_ws, g_h, gc1 if need[2] else None, gt0 if need[3] else None,
+                gt1 if need[4] else None, None)
+
+
+def fbt_layer0_real_scan(w_stacked, h_real, C1, tap0, tap1, batch):
+    """Real-input first-layer projection + split-ReLU prospective scan —
+    drop-in for rqf_models/ops/fbt_scan_kernel.py:fbt_layer0_real_scan
+    (:1005): w_stacked (2F, d) real [Wr; Wi], h_real (d, batch*time) real;
+    returns the complex (F, batch, time) split-ReLU output."""
+    return _Layer0RealScan.apply(w_stacked, h_real, C1, tap0, tap1, batch)
 
 
 # ------------------------------------------------------------- TBPTT(1)

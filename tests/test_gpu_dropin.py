@@ -262,3 +262,41 @@ def test_sequential_scan_b_matrix():
     for a, b, k in zip(res[1][1], res[0][1], ("C1", "C2", "u", "B")):
         e = rel_err(_np(a), _np(b))
         assert e <= GRAD_TOL, f"gradient of {k} differs by {e:.2e}"
+
+
+def test_layer0_real_scan_matches_reference_kernel():
+    """fbt_layer0_real_scan (fbt_scan_kernel.py:1005): the reference's stacked
+    real GEMM + planar Triton recompute scan against this backend's
+    real-operand GEMM + (F,B,T) scan, on the same inputs; output and the
+    gradients of the stacked weight, the input and the coefficients.  Smooth
+    loss on the split-ReLU output (its parameter-like sums absorb the rare
+    decision at a state within rounding of zero)."""
+    import prospective_rqf_b200 as rqf
+    from prospective_rqf_b200 import _timing
+    from rqf_models.ops import fbt_scan_kernel as fk
+
+    g = torch.Generator(device="cuda").manual_seed(8)
+    F, d, B, T = 48, 40, 6, 3000
+    ws = 0.2 * torch.randn(2 * F, d, device="cuda", generator=g)
+    h = torch.randn(d, B * T, device="cuda", generator=g)
+    c1 = torch.polar(0.9 + 0.099 * torch.rand(F, device="cuda", generator=g),
+                     3.0 * torch.rand(F, device="cuda", generator=g))
+    t0 = 0.5 * torch.randn(F, dtype=torch.complex64, device="cuda", generator=g)
+    t1 = 0.5 * torch.randn(F, dtype=torch.complex64, device="cuda", generator=g)
+
+    def run(fn):
+        ins = [t.detach().clone().requires_grad_(True) for t in (ws, h, c1, t0, t1)]
+        y = fn(*ins, B)
+        (y.abs() ** 2).mean().backward()
+        return y.detach(), [t.grad.detach() for t in ins]
+
+    rqf.uninstall()
+    y0, g0 = run(fk.fbt_layer0_real_scan)
+    with _timing.KernelTimer() as timer:
+        y1, g1 = run(rqf.fbt_layer0_real_scan)
+    assert "rqf_projection_real" in timer.summary()
+    e = rel_err(_np(y1), _np(y0))
+    assert e <= FWD_TOL, f"forward differs by {e:.2e}"
+    for name, a, b in zip(("w_stacked", "h_real", "C1", "tap0", "tap1"), g1, g0):
+        e = rel_err(_np(a), _np(b))
+        assert e <= GRAD_TOL, f"gradient of {name} differs by {e:.2e}"

@@ -147,7 +147,7 @@ def test_install_against_the_reference_tree(monkeypatch):
         assert sk.selective_forward is ops.selective_forward
         assert scan._sequential_scan_forward_abs_raw_block_f is \
             ops._sequential_scan_forward_abs_raw_block_f
-        assert len(patched) == 22
+        assert len(patched) == 23
     finally:
         integration.uninstall()
 
