@@ -16,6 +16,8 @@ Ops:
   btf_real   _triton_chunked_scan, real input, (B,T,F)
   btf_pro    _triton_chunked_scan_prospective, (B,T,F)
   selective  selective_forward + selective_backward with every controller on
+  selective_bf16  the same in the bf16 storage mode (bf16 logits, raw / act and
+             logit cotangents)
              (--groups warp groups, --truncated for the TBPTT(1) variant)
   projection the block projection z = W h, its input cotangent W^H gz + g and
              its weight cotangent gz h^H (split-TF32 tcgen05 GEMMs, W of F x F
@@ -67,7 +69,7 @@ def make_case(op: str, F: int, B: int, T: int, groups: int = 8, truncated: bool 
     def crandn(*shape):
         return torch.randn(*shape, dtype=torch.complex64, generator=g).to(dev)
 
-    if op == "selective":
+    if op in ("selective", "selective_bf16"):
         G = groups
         theta = (0.05 + 2 * torch.rand(F, generator=g)).to(dev)
         inputs = (torch.randn(F, B, T, generator=g).to(dev), torch.randn(G, B, T, generator=g).to(dev),
@@ -79,6 +81,15 @@ def make_case(op: str, F: int, B: int, T: int, groups: int = 8, truncated: bool 
                   (True, True, True, False, 0.223, 0.223, True, False, True, 2.0, 0.0, True))
         z = crandn(F, B, T)
         gy, gx = crandn(F, B, T), crandn(F, B, T)
+
+        if op == "selective_bf16":
+            inputs = tuple(t.to(torch.bfloat16) if i in (0, 1, 2) else t
+                           for i, t in enumerate(inputs[:12])) + (inputs[12],)
+
+            def run():
+                _, _, ent = ops.selective_forward_bf16(z, inputs, True, True)
+                ops.selective_backward_bf16(z, inputs, ent, gy, gx, True, truncated)
+            return run
 
         def run():
             _, _, ent = rqf.selective_forward(z, inputs, True, True, None)
@@ -164,7 +175,7 @@ def make_case(op: str, F: int, B: int, T: int, groups: int = 8, truncated: bool 
 
 
 OPS = ("fbt", "fbt_raw", "fbt_skip", "tbptt_fbt", "tbptt_btf", "btf", "btf_real", "btf_pro",
-       "selective", "projection", "projection_torch", "projection_real", "mosc")
+       "selective", "selective_bf16", "projection", "projection_torch", "projection_real", "mosc")
 
 
 def measure(op, F, B, T, iters=10, warmup=3, groups=8, truncated=False) -> dict:

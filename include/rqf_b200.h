@@ -296,6 +296,28 @@ int rqf_selective_backward(const float *z, const rqf_selective_inputs *inputs,
                            float *dbias, float *dtheta, void *scratch, int64_t filters,
                            int64_t batch, int64_t time, rqf_stream_t stream);
 
+/* ---- selective scan, bf16 storage mode -------------------------------- *
+ * No counterpart in the reference, whose selective kernel requires fp32
+ * logits and complex64 activations (rqf_models/ops/selective_scan.py:187-198):
+ * the storage mode of BASELINE config 3 ("bf16 activations, fp32 complex
+ * state").  Same arguments and arithmetic as rqf_selective_forward /
+ * _backward, except that the three logit pointers of `inputs` address bf16
+ * (2-byte) elements, raw / act are written as interleaved bf16 pairs
+ * (F,B,T,2), and the logit cotangents dgamma / dwarp / dwrite are written in
+ * bf16.  z, the carries, the output cotangents, dz / dzw and dbias / dtheta
+ * stay fp32, and so does every value inside the kernels (bf16 inputs are
+ * widened exactly; outputs are rounded to nearest-even once). */
+int rqf_selective_forward_bf16(const float *z, const rqf_selective_inputs *inputs,
+                               const rqf_selective_options *options, void *raw, void *act,
+                               float *carries, int64_t filters, int64_t batch, int64_t time,
+                               rqf_stream_t stream);
+int rqf_selective_backward_bf16(const float *z, const rqf_selective_inputs *inputs,
+                                const rqf_selective_options *options, const float *carries,
+                                const float *grad_raw, const float *grad_act, int truncated,
+                                float *dz, float *dzw, void *dgamma, void *dwarp, void *dwrite,
+                                float *dbias, float *dtheta, void *scratch, int64_t filters,
+                                int64_t batch, int64_t time, rqf_stream_t stream);
+
 /* ---- allocation-free variant of rqf_fbt_prospective_backward --------- *
  * No counterpart in the reference.  For callers that cannot allocate device
  * memory — e.g. code running inside a framework allocator's callback, a

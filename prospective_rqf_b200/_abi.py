@@ -103,6 +103,10 @@ SIGNATURES: dict[str, tuple] = {
     "rqf_selective_backward": (
         _int, [_p, _pin, _pop, _p, _p, _p, _int, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64,
                _i64, _p]),
+    "rqf_selective_forward_bf16": (_int, [_p, _pin, _pop, _p, _p, _p, _i64, _i64, _i64, _p]),
+    "rqf_selective_backward_bf16": (
+        _int, [_p, _pin, _pop, _p, _p, _p, _int, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64,
+               _i64, _p]),
     "rqf_tbptt1_two_tap_backward": (
         _int, [_int, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _int,
                _p]),

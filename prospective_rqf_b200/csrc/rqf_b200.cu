@@ -963,31 +963,38 @@ size_t rqf_selective_scratch_bytes(int64_t filters, int64_t batch, int64_t time,
   return dd + round256((size_t)filters * batch * 2 * sizeof(float)) + order;
 }
 
-int rqf_selective_forward(const float *z, const rqf_selective_inputs *inputs,
-                          const rqf_selective_options *options, float *raw, float *act,
-                          float *carries, int64_t filters, int64_t batch, int64_t time,
-                          rqf_stream_t stream) {
+}  // extern "C"
+
+namespace {
+
+template <bool BF>
+int sel_forward_impl(const float *z, const rqf_selective_inputs *inputs,
+                     const rqf_selective_options *options, void *raw, void *act, float *carries,
+                     int64_t filters, int64_t batch, int64_t time, rqf_stream_t stream) {
   int st = sel_check(z, inputs, options, filters, batch, time);
   if (st != RQF_OK || filters * batch * time == 0) return st;
   if ((!raw && !act) || !carries) return RQF_ERR_ARGUMENT;
-  if ((raw && !aligned(raw, 8)) || (act && !aligned(act, 8)) || !aligned(carries, 8))
+  const size_t out_align = BF ? 4 : 8;
+  if ((raw && !aligned(raw, out_align)) || (act && !aligned(act, out_align)) ||
+      !aligned(carries, 8))
     return RQF_ERR_ALIGN;
   SelArgs a = sel_args(z, inputs, options, filters, batch, time);
-  a.raw = reinterpret_cast<float2 *>(raw);
-  a.act = reinterpret_cast<float2 *>(act);
+  a.raw = raw;
+  a.act = act;
   a.carries = reinterpret_cast<float2 *>(carries);
   a.vec = sel_vec(a, time);
-  auto kern = sel_fwd_kernel<kSelThreads, kSelK>;
+  auto kern = sel_fwd_kernel<kSelThreads, kSelK, BF>;
   kern<<<sel_grid(kern, a.rows), kSelThreads, 0, stream>>>(a);
   return launch_status();
 }
 
-int rqf_selective_backward(const float *z, const rqf_selective_inputs *inputs,
-                           const rqf_selective_options *options, const float *carries,
-                           const float *grad_raw, const float *grad_act, int truncated,
-                           float *dz, float *dzw, float *dgamma, float *dwarp, float *dwrite,
-                           float *dbias, float *dtheta, void *scratch, int64_t filters,
-                           int64_t batch, int64_t time, rqf_stream_t stream) {
+template <bool BF>
+int sel_backward_impl(const float *z, const rqf_selective_inputs *inputs,
+                      const rqf_selective_options *options, const float *carries,
+                      const float *grad_raw, const float *grad_act, int truncated, float *dz,
+                      float *dzw, void *dgamma, void *dwarp, void *dwrite, float *dbias,
+                      float *dtheta, void *scratch, int64_t filters, int64_t batch, int64_t time,
+                      rqf_stream_t stream) {
   int st = sel_check(z, inputs, options, filters, batch, time);
   if (st != RQF_OK) return st;
   if (filters * batch * time == 0) {
@@ -1019,7 +1026,7 @@ int rqf_selective_backward(const float *z, const rqf_selective_inputs *inputs,
   a.dD = options->has_warp ? static_cast<float *>(scratch) : nullptr;
   a.partials = at<float>(scratch, dd_bytes);
   a.vec = sel_vec(a, time);
-  auto kern = sel_bwd_kernel<kSelThreads, kSelK>;
+  auto kern = sel_bwd_kernel<kSelThreads, kSelK, BF>;
   kern<<<sel_grid(kern, a.rows), kSelThreads, 0, stream>>>(a);
   if ((st = launch_status()) != RQF_OK) return st;
   if (options->has_warp) {
@@ -1029,13 +1036,55 @@ int rqf_selective_backward(const float *z, const rqf_selective_inputs *inputs,
     const int ng = (int)inputs->num_groups;
     sel_group_order_kernel<<<1, 32 * ng, 0, stream>>>(a.groups, (int)filters, ng, order, bounds);
     if ((st = launch_status()) != RQF_OK) return st;
-    sel_group_reduce_kernel<<<(unsigned)ceil_div(bt, 256), 256, 0, stream>>>(a.dD, order, bounds,
-                                                                              dwarp, ng, bt);
+    sel_group_reduce_kernel<BF><<<(unsigned)ceil_div(bt, 256), 256, 0, stream>>>(
+        a.dD, order, bounds, dwarp, ng, bt);
     if ((st = launch_status()) != RQF_OK) return st;
   }
   sel_param_reduce_kernel<<<(unsigned)ceil_div(filters, 128), 128, 0, stream>>>(
       a.partials, dbias, dtheta, (int)filters, (int)batch);
   return launch_status();
+}
+
+}  // namespace
+
+extern "C" {
+
+int rqf_selective_forward(const float *z, const rqf_selective_inputs *inputs,
+                          const rqf_selective_options *options, float *raw, float *act,
+                          float *carries, int64_t filters, int64_t batch, int64_t time,
+                          rqf_stream_t stream) {
+  return sel_forward_impl<false>(z, inputs, options, raw, act, carries, filters, batch, time,
+                                 stream);
+}
+
+int rqf_selective_backward(const float *z, const rqf_selective_inputs *inputs,
+                           const rqf_selective_options *options, const float *carries,
+                           const float *grad_raw, const float *grad_act, int truncated,
+                           float *dz, float *dzw, float *dgamma, float *dwarp, float *dwrite,
+                           float *dbias, float *dtheta, void *scratch, int64_t filters,
+                           int64_t batch, int64_t time, rqf_stream_t stream) {
+  return sel_backward_impl<false>(z, inputs, options, carries, grad_raw, grad_act, truncated, dz,
+                                  dzw, dgamma, dwarp, dwrite, dbias, dtheta, scratch, filters,
+                                  batch, time, stream);
+}
+
+int rqf_selective_forward_bf16(const float *z, const rqf_selective_inputs *inputs,
+                               const rqf_selective_options *options, void *raw, void *act,
+                               float *carries, int64_t filters, int64_t batch, int64_t time,
+                               rqf_stream_t stream) {
+  return sel_forward_impl<true>(z, inputs, options, raw, act, carries, filters, batch, time,
+                                stream);
+}
+
+int rqf_selective_backward_bf16(const float *z, const rqf_selective_inputs *inputs,
+                                const rqf_selective_options *options, const float *carries,
+                                const float *grad_raw, const float *grad_act, int truncated,
+                                float *dz, float *dzw, void *dgamma, void *dwarp, void *dwrite,
+                                float *dbias, float *dtheta, void *scratch, int64_t filters,
+                                int64_t batch, int64_t time, rqf_stream_t stream) {
+  return sel_backward_impl<true>(z, inputs, options, carries, grad_raw, grad_act, truncated, dz,
+                                 dzw, dgamma, dwarp, dwrite, dbias, dtheta, scratch, filters,
+                                 batch, time, stream);
 }
 
 }  // extern "C"

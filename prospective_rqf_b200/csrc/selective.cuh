@@ -26,6 +26,8 @@
 // (selective_scan_kernel.py:250-462) with one program per row.
 #pragma once
 
+#include <cuda_bf16.h>
+
 #include "rqf_common.cuh"
 
 namespace rqf {
@@ -38,16 +40,21 @@ struct SelOptions {  // layout of rqf_selective_options in include/rqf_b200.h
   int bound_warp;
 };
 
+// Storage of the logits, their cotangents and the raw / act outputs: fp32
+// (complex64 outputs), or bf16 in the bf16 storage mode (complex outputs as
+// interleaved bf16 pairs).  The drive z, the output cotangents, dz / dzw and
+// every value computed in the kernels stay fp32.
 struct SelArgs {
   const float2 *z;
-  const float *G, *D, *W;  // logits (F,B,T), (groups,B,T), (F,B,T); null when unused
+  const void *G, *D, *W;  // logits (F,B,T), (groups,B,T), (F,B,T); null when unused
   const float *bias, *theta, *lo, *span, *step, *horizon, *th_lo, *th_hi;  // (F,)
   const long long *groups;                                                  // (F,)
-  float2 *raw, *act;   // forward outputs (nullable)
+  void *raw, *act;     // forward outputs (nullable)
   float2 *carries;     // (rows, ntiles) entry states
   const float2 *gy, *gx;
   float2 *dz, *dzw;
-  float *dG, *dD, *dW;  // dD: per-channel (F,B,T) warp cotangent, group-reduced later
+  void *dG, *dW;        // logit cotangents (F,B,T), the logits' storage type
+  float *dD;            // per-channel (F,B,T) warp cotangent (fp32), group-reduced later
   float *partials;      // (rows, 2): bias and theta sums
   int rows, T, batch, ntiles, num_groups;
   SelOptions o;
@@ -276,6 +283,77 @@ __device__ __forceinline__ void sel_st_f(float *row, int t0, int T, bool vec,
   for (int k = 0; k < kSelK; ++k)
     if (t0 + k < T) __stcs(row + t0 + k, v[k]);
 }
+// The same accesses in the logits' storage type (fp32 or bf16) and for the
+// complex outputs (complex64 or bf16 pairs).  bf16 values are widened exactly
+// and written rounded to nearest-even.
+template <bool BF>
+__device__ __forceinline__ const void *sel_row(const void *base, size_t off) {
+  return base ? static_cast<const char *>(base) + off * (BF ? 2 : 4) : nullptr;
+}
+template <bool BF>
+__device__ __forceinline__ void *sel_row_out(void *base, size_t off, int per_sample) {
+  return static_cast<char *>(base) + off * (size_t)per_sample * (BF ? 2 : 4);
+}
+__device__ __forceinline__ float bf_to_f(unsigned short u) {
+  return __uint_as_float((unsigned)u << 16);
+}
+__device__ __forceinline__ unsigned short f_to_bf(float x) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+template <bool BF>
+__device__ __forceinline__ void sel_ld_l(const void *row, int t0, int T, bool vec,
+                                         float (&v)[kSelK]) {
+  if constexpr (!BF) {
+    sel_ld_f(static_cast<const float *>(row), t0, T, vec, v);
+  } else {
+    const unsigned short *r = static_cast<const unsigned short *>(row);
+    if (r && vec && t0 + kSelK <= T) {
+      const uint2 q = __ldg(reinterpret_cast<const uint2 *>(r + t0));
+      v[0] = __uint_as_float(q.x << 16); v[1] = __uint_as_float(q.x & 0xffff0000u);
+      v[2] = __uint_as_float(q.y << 16); v[3] = __uint_as_float(q.y & 0xffff0000u);
+      return;
+    }
+#pragma unroll
+    for (int k = 0; k < kSelK; ++k) v[k] = (r && t0 + k < T) ? bf_to_f(__ldg(r + t0 + k)) : 0.f;
+  }
+}
+template <bool BF>
+__device__ __forceinline__ void sel_st_l(void *row, int t0, int T, bool vec,
+                                         const float (&v)[kSelK]) {
+  if constexpr (!BF) {
+    sel_st_f(static_cast<float *>(row), t0, T, vec, v);
+  } else {
+    unsigned short *r = static_cast<unsigned short *>(row);
+    if (vec && t0 + kSelK <= T) {
+      const uint2 q = make_uint2((unsigned)f_to_bf(v[0]) | ((unsigned)f_to_bf(v[1]) << 16),
+                                 (unsigned)f_to_bf(v[2]) | ((unsigned)f_to_bf(v[3]) << 16));
+      __stcs(reinterpret_cast<uint2 *>(r + t0), q);
+      return;
+    }
+#pragma unroll
+    for (int k = 0; k < kSelK; ++k)
+      if (t0 + k < T) r[t0 + k] = f_to_bf(v[k]);
+  }
+}
+template <bool BF>
+__device__ __forceinline__ void sel_st_out(void *row, int t0, int T, bool vec,
+                                           const float2 (&v)[kSelK]) {
+  if constexpr (!BF) {
+    sel_st_c(static_cast<float2 *>(row), t0, T, vec, v);
+  } else {
+    unsigned *r = static_cast<unsigned *>(row);  // one bf16 pair per sample
+    auto pack = [](float2 c) { return (unsigned)f_to_bf(c.x) | ((unsigned)f_to_bf(c.y) << 16); };
+    if (vec && t0 + kSelK <= T) {
+      __stcs(reinterpret_cast<uint4 *>(r + t0),
+             make_uint4(pack(v[0]), pack(v[1]), pack(v[2]), pack(v[3])));
+      return;
+    }
+#pragma unroll
+    for (int k = 0; k < kSelK; ++k)
+      if (t0 + k < T) r[t0 + k] = pack(v[k]);
+  }
+}
+
 // z[t0 - 1]: the previous thread's last sample, from memory for lane 0.
 __device__ __forceinline__ float2 sel_prev_z(const float2 *row, int t0, int T, float2 zlast,
                                              int lane) {
@@ -285,7 +363,7 @@ __device__ __forceinline__ float2 sel_prev_z(const float2 *row, int t0, int T, f
 }
 
 // ------------------------------------------------------------ forward
-template <int NT, int K>
+template <int NT, int K, bool BF = false>
 __global__ void __launch_bounds__(NT) sel_fwd_kernel(const SelArgs a) {
   constexpr int L = NT * K;
   __shared__ float4 s_warp[2][NT / 32];  // double-buffered across consecutive tiles
@@ -297,9 +375,10 @@ __global__ void __launch_bounds__(NT) sel_fwd_kernel(const SelArgs a) {
     const int f = row / a.batch, b = row - f * a.batch;
     const SelChan c = sel_chan(a, f);
     const float2 *zrow = a.z + (size_t)row * T;
-    const float *grow = a.o.has_gamma ? a.G + (size_t)row * T : nullptr;
-    const float *wrow = a.o.has_write ? a.W + (size_t)row * T : nullptr;
-    const float *drow = a.o.has_warp ? a.D + ((size_t)c.group * a.batch + b) * T : nullptr;
+    const void *grow = a.o.has_gamma ? sel_row<BF>(a.G, (size_t)row * T) : nullptr;
+    const void *wrow = a.o.has_write ? sel_row<BF>(a.W, (size_t)row * T) : nullptr;
+    const void *drow =
+        a.o.has_warp ? sel_row<BF>(a.D, ((size_t)c.group * a.batch + b) * T) : nullptr;
     float2 carry = cz();
     for (int j = 0; j < a.ntiles; ++j, ++tcount) {
       const int t0 = j * L + tid * K;
@@ -307,9 +386,9 @@ __global__ void __launch_bounds__(NT) sel_fwd_kernel(const SelArgs a) {
       sel_ld_c(zrow, t0, T, vec, z);
       const float2 zp = sel_prev_z(zrow, t0, T, z[K - 1], tid & 31);
       float gl[K], dl[K], wl[K];
-      sel_ld_f(grow, t0, T, vec, gl);
-      sel_ld_f(drow, t0, T, vec, dl);
-      sel_ld_f(wrow, t0, T, vec, wl);
+      sel_ld_l<BF>(grow, t0, T, vec, gl);
+      sel_ld_l<BF>(drow, t0, T, vec, dl);
+      sel_ld_l<BF>(wrow, t0, T, vec, wl);
       float2 A[K], u[K];
 #pragma unroll
       for (int k = 0; k < K; ++k) {
@@ -338,14 +417,14 @@ __global__ void __launch_bounds__(NT) sel_fwd_kernel(const SelArgs a) {
         ys[k] = e;
         acts[k] = c_relu(e);
       }
-      if (a.raw) sel_st_c(a.raw + (size_t)row * T, t0, T, vec, ys);
-      if (a.act) sel_st_c(a.act + (size_t)row * T, t0, T, vec, acts);
+      if (a.raw) sel_st_out<BF>(sel_row_out<BF>(a.raw, (size_t)row * T, 2), t0, T, vec, ys);
+      if (a.act) sel_st_out<BF>(sel_row_out<BF>(a.act, (size_t)row * T, 2), t0, T, vec, acts);
     }
   }
 }
 
 // ------------------------------------------------------------ backward
-template <int NT, int K>
+template <int NT, int K, bool BF = false>
 __global__ void __launch_bounds__(NT, 3) sel_bwd_kernel(const SelArgs a) {
   constexpr int NW = NT / 32, L = NT * K;
   __shared__ float4 s_warp_f[NW];
@@ -365,9 +444,10 @@ __global__ void __launch_bounds__(NT, 3) sel_bwd_kernel(const SelArgs a) {
     const int f = row / a.batch, b = row - f * a.batch;
     const SelChan c = sel_chan(a, f);
     const size_t roff = (size_t)row * T;
-    const float *grow = a.o.has_gamma ? a.G + roff : nullptr;
-    const float *wrow = a.o.has_write ? a.W + roff : nullptr;
-    const float *drow = a.o.has_warp ? a.D + ((size_t)c.group * a.batch + b) * T : nullptr;
+    const void *grow = a.o.has_gamma ? sel_row<BF>(a.G, roff) : nullptr;
+    const void *wrow = a.o.has_write ? sel_row<BF>(a.W, roff) : nullptr;
+    const void *drow =
+        a.o.has_warp ? sel_row<BF>(a.D, ((size_t)c.group * a.batch + b) * T) : nullptr;
     float2 dcarry = cz();                   // d at the first sample of the next tile
     float2 A_next = cz(), n_next = cz();    // A, gated n at that sample (0 past T)
     float acc_bias = 0.f, acc_theta = 0.f;
@@ -378,9 +458,9 @@ __global__ void __launch_bounds__(NT, 3) sel_bwd_kernel(const SelArgs a) {
       sel_ld_c(a.z + roff, t0, T, vec, z);
       const float2 zp = sel_prev_z(a.z + roff, t0, T, z[K - 1], lane);
       float gl[K], dl[K], wl[K];
-      sel_ld_f(grow, t0, T, vec, gl);
-      sel_ld_f(drow, t0, T, vec, dl);
-      sel_ld_f(wrow, t0, T, vec, wl);
+      sel_ld_l<BF>(grow, t0, T, vec, gl);
+      sel_ld_l<BF>(drow, t0, T, vec, dl);
+      sel_ld_l<BF>(wrow, t0, T, vec, wl);
       float2 gyv[K], gxv[K];
       sel_ld_c(a.gy ? a.gy + roff : nullptr, t0, T, vec, gyv);
       sel_ld_c(a.gx ? a.gx + roff : nullptr, t0, T, vec, gxv);
@@ -557,9 +637,9 @@ __global__ void __launch_bounds__(NT, 3) sel_bwd_kernel(const SelArgs a) {
       }
       sel_st_c(a.dz + roff, t0, T, vec, o_dz);
       if (a.truncated) sel_st_c(a.dzw + roff, t0, T, vec, o_dzw);
-      if (a.o.has_gamma) sel_st_f(a.dG + roff, t0, T, vec, o_dG);
+      if (a.o.has_gamma) sel_st_l<BF>(sel_row_out<BF>(a.dG, roff, 1), t0, T, vec, o_dG);
       if (a.o.has_warp) sel_st_f(a.dD + roff, t0, T, vec, o_dD);
-      if (a.o.has_write) sel_st_f(a.dW + roff, t0, T, vec, o_dW);
+      if (a.o.has_write) sel_st_l<BF>(sel_row_out<BF>(a.dW, roff, 1), t0, T, vec, o_dW);
       dcarry = dcarry_next;
       {
         const float4 q = s_first[0];
@@ -624,9 +704,10 @@ __global__ void __launch_bounds__(1024)
 
 // dd_group[g, b, t] = sum of dD[f, b, t] over the channels f of group g, in
 // increasing f (deterministic); one thread per (b, t), eight loads in flight.
+template <bool BF = false>
 __global__ void __launch_bounds__(256)
     sel_group_reduce_kernel(const float *__restrict__ dD, const int *__restrict__ order,
-                            const int *__restrict__ bounds, float *__restrict__ out, int ngroups,
+                            const int *__restrict__ bounds, void *__restrict__ out, int ngroups,
                             int64_t BT) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= BT) return;
@@ -642,7 +723,10 @@ __global__ void __launch_bounds__(256)
       for (int u = 0; u < 8; ++u) acc += v[u];
     }
     for (; q < b1; ++q) acc += __ldcs(dD + (int64_t)order[q] * BT + i);
-    out[(int64_t)g * BT + i] = acc;
+    if constexpr (BF)
+      static_cast<unsigned short *>(out)[(int64_t)g * BT + i] = f_to_bf(acc);
+    else
+      static_cast<float *>(out)[(int64_t)g * BT + i] = acc;
   }
 }
 

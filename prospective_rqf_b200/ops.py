@@ -725,9 +725,10 @@ def _sel_options(opt) -> "_abi.SelectiveOptions":
     return o
 
 
-def _sel_tensors(inputs, device):
+def _sel_tensors(inputs, device, logit_dtype=torch.float32):
     """Contiguous fp32 / int64 device tensors of a SelectiveScanInputs-like
-    13-tuple (rqf_models/ops/selective_scan.py:10-23) and its C struct."""
+    13-tuple (rqf_models/ops/selective_scan.py:10-23) and its C struct; the
+    three logit tensors in `logit_dtype` (bf16 for the bf16 storage mode)."""
     opt = inputs[12]
     t = {}
     for i, name in enumerate(_SEL_FIELDS):
@@ -736,6 +737,8 @@ def _sel_tensors(inputs, device):
             t[name] = None
         elif name == "groups":
             t[name] = v.to(device=device, dtype=torch.int64).contiguous()
+        elif name.endswith("_logits"):
+            t[name] = v.to(device=device, dtype=logit_dtype).contiguous()
         else:
             t[name] = v.to(device=device, dtype=torch.float32).contiguous()
     if not opt[0]:
@@ -807,6 +810,67 @@ def selective_backward(z, inputs, entries, gy, gx, activate, truncated, chunk=No
             _abi.ptr(dzw if truncated else None), _abi.ptr(dg), _abi.ptr(dd), _abi.ptr(dw),
             _abi.ptr(dbias), _abi.ptr(dtheta), _abi.ptr(scratch), F, B, T, _abi.stream_of(zz)),
             "rqf_selective_backward")
+    _done(dev)
+    del keep
+    return dz, dzw, dg, dd, dw, dbias, dtheta
+
+
+def selective_forward_bf16(z, inputs, activate, write_raw):
+    """The bf16 storage mode of selective_forward (rqf_selective_forward_bf16;
+    no reference counterpart: BASELINE config 3's "bf16 activations, fp32
+    state").  The logits of `inputs` are read as bf16 (converted if given in
+    another dtype); raw and act are returned as bf16 (F, B, T, 2) [Re, Im]
+    pairs.  z, the carries and all arithmetic stay fp32."""
+    dev = _require_cuda(z)
+    if not activate and not write_raw:
+        raise ValueError("selective scan requires at least one output")
+    zz = _c64(z)
+    F, B, T = _shape3(zz, "z")
+    keep, sin, sopt = _sel_tensors(inputs, dev, torch.bfloat16)
+    lib = _abi.load()
+    raw = torch.empty((F, B, T, 2), dtype=torch.bfloat16, device=dev) if write_raw else None
+    act = torch.empty((F, B, T, 2), dtype=torch.bfloat16, device=dev) if activate else None
+    entries = torch.empty((F * B, max(int(lib.rqf_selective_num_tiles(T)), 1)),
+                          dtype=torch.complex64, device=dev)
+    nb = _nbytes(zz, keep["gamma_logits"], keep["warp_logits"], keep["write_logits"], raw, act)
+    with _timing.launch("rqf_selective_forward_bf16", F * B * T, nb):
+        _abi.check(lib.rqf_selective_forward_bf16(
+            _abi.ptr(zz), ctypes.byref(sin), ctypes.byref(sopt), _abi.ptr(raw), _abi.ptr(act),
+            _abi.ptr(entries), F, B, T, _abi.stream_of(zz)), "rqf_selective_forward_bf16")
+    _done(dev)
+    del keep
+    return raw, act, entries
+
+
+def selective_backward_bf16(z, inputs, entries, gy, gx, activate, truncated):
+    """The bf16 storage mode of selective_backward: the logit cotangents
+    (dg, dd_group, dw) come back in bf16; dz, dzw, dbias and dtheta in fp32 as
+    in selective_backward; gy / gx are complex64 cotangents."""
+    dev = _require_cuda(z)
+    zz = _c64(z)
+    F, B, T = _shape3(zz, "z")
+    keep, sin, sopt = _sel_tensors(inputs, dev, torch.bfloat16)
+    opt = inputs[12]
+    lib = _abi.load()
+    gyc = None if gy is None else _c64(gy)
+    gxc = None if gx is None else _c64(gx)
+    dz = torch.empty_like(zz)
+    dzw = torch.empty_like(zz) if truncated else dz
+    dg = torch.empty_like(keep["gamma_logits"]) if opt[0] else None
+    dd = torch.empty_like(keep["warp_logits"]) if opt[1] else None
+    dw = torch.empty_like(keep["write_logits"]) if opt[2] else None
+    dbias = torch.empty(F, dtype=torch.float32, device=dev)
+    dtheta = torch.empty(F, dtype=torch.float32, device=dev)
+    scratch = _scratch(lib.rqf_selective_scratch_bytes(F, B, T, int(bool(opt[1]))), dev)
+    nb = _nbytes(zz, keep["gamma_logits"], keep["warp_logits"], keep["write_logits"], gyc, gxc,
+                 dz, dzw if truncated else None, dg, dd, dw)
+    with _timing.launch("rqf_selective_backward_bf16", F * B * T, nb):
+        _abi.check(lib.rqf_selective_backward_bf16(
+            _abi.ptr(zz), ctypes.byref(sin), ctypes.byref(sopt), _abi.ptr(entries),
+            _abi.ptr(gyc), _abi.ptr(gxc), int(bool(truncated)), _abi.ptr(dz),
+            _abi.ptr(dzw if truncated else None), _abi.ptr(dg), _abi.ptr(dd), _abi.ptr(dw),
+            _abi.ptr(dbias), _abi.ptr(dtheta), _abi.ptr(scratch), F, B, T, _abi.stream_of(zz)),
+            "rqf_selective_backward_bf16")
     _done(dev)
     del keep
     return dz, dzw, dg, dd, dw, dbias, dtheta

@@ -193,3 +193,81 @@ def test_selective_config3_rows():
         return selective.backward(z, y, co, gy, gx, truncated=False, mask=mask, **ins)
 
     check(z, d, opt, gy, gx, False, (y, act), ref_bwd, use_kernel_mask=True)
+
+
+# ------------------------------------------------------ bf16 storage mode
+# Tolerances of the bf16 storage mode (no pinned parity: the reference has no
+# such mode).  Stored bf16 values carry half a bf16 ulp of rounding, 2^-9 of
+# their magnitude, so raw / act and the logit cotangents are held to 5e-3
+# normwise against the fp64 oracle; dz, dzw, dbias and dtheta stay fp32 and keep
+# the fp32 bounds.  Against the fp32 kernel on the same (bf16-valued) logits
+# the mode must agree to the bf16 rounding of the fp32 kernel's outputs.
+BF16_TOL = 5e-3
+
+
+def _bf16_values(d):
+    """The logits rounded to bf16 (both modes and the oracle see these values)."""
+    out = dict(d)
+    for k in ("gl", "dl", "wl"):
+        if d[k].size:
+            out[k] = torch.from_numpy(d[k]).to(torch.bfloat16).to(torch.float64).numpy()
+    return out
+
+
+@pytest.mark.parametrize("T", [1, 1023, 1025, 4096])
+@pytest.mark.parametrize("truncated", [False, True])
+def test_selective_bf16_storage_mode(T, truncated):
+    from prospective_rqf_b200 import ops
+
+    rng = np.random.default_rng(500 + T + int(truncated))
+    opt = (True, True, True, False, 0.223, 0.223, True, False, True, 2.0, 0.0, True)
+    F, B = 24, 4
+    z, d, gy, gx = random_case(rng, F, B, T, opt, ngroups=4)
+    d = _bf16_values(d)
+    inputs = as_inputs(d, opt, B, T)
+    zt = cuda(z, torch.complex64)
+    raw16, act16, ent16 = ops.selective_forward_bf16(zt, inputs, True, True)
+    out16 = ops.selective_backward_bf16(zt, inputs, ent16, cuda(gy, torch.complex64),
+                                        cuda(gx, torch.complex64), True, truncated)
+    raw32, act32, ent32 = ops.selective_forward(zt, inputs, True, True)
+    out32 = ops.selective_backward(zt, inputs, ent32, cuda(gy, torch.complex64),
+                                   cuda(gx, torch.complex64), True, truncated)
+
+    def c16(t):  # (F,B,T,2) bf16 -> complex128
+        a = t.float().cpu().numpy().astype(np.float64)
+        return a[..., 0] + 1j * a[..., 1]
+
+    def as_bf16_pairs(t):
+        return c16(torch.view_as_real(t).to(torch.bfloat16))
+
+    # same arithmetic: the bf16 outputs are the fp32 kernel's, rounded once
+    assert np.array_equal(c16(raw16), as_bf16_pairs(raw32))
+    assert np.array_equal(c16(act16), as_bf16_pairs(act32))
+    for i, name in ((0, "dz"), (1, "dzw"), (5, "dbias"), (6, "dtheta")):
+        assert torch.equal(out16[i], out32[i]), f"{name} differs from the fp32 mode"
+    for i, name in ((2, "dG"), (3, "dD"), (4, "dW")):
+        if out32[i] is not None:
+            assert torch.equal(out16[i], out32[i].to(torch.bfloat16)), f"{name} rounding differs"
+
+    # against the fp64 oracle, with the stated bf16-storage tolerance
+    ins = dict(gl=d["gl"], dl=d["dl"], wl=d["wl"], bias=d["bias"], theta=d["theta"],
+               groups=d["groups"], lo=d["lo"], span=d["span"], step=d["step"],
+               horizon=d["horizon"], th_lo=d["th_lo"], th_hi=d["th_hi"], opt=opt)
+    y, co = selective.forward(z, **ins)
+    act = np.maximum(y.real, 0) + 1j * np.maximum(y.imag, 0)
+    assert_close(c16(raw16), y, BF16_TOL, "raw (bf16)")
+    assert_close(c16(act16), act, BF16_TOL, "act (bf16)")
+    mask = core_oracle.relu_mask_from_output(c16(act16))
+    assert core_oracle.mask_disagreement(mask, y) < MASK_EDGE
+    rdz, rdzw, rdG, rdD, rdW, rdbias, rdtheta = selective.backward(
+        z, y, co, gy, gx, truncated=truncated, mask=mask, **ins)
+    dz, dzw, dG, dD, dW, dbias, dtheta = (None if t is None else t.float().cpu().numpy()
+                                          if t.dtype == torch.bfloat16 else host(t)
+                                          for t in out16)
+    assert_close(dz, rdz, GRAD_TOL, "dz")
+    assert_close(dzw, rdzw, GRAD_TOL, "dzw")
+    assert_close(dG, rdG, BF16_TOL, "dG (bf16)")
+    assert_close(dD, rdD, BF16_TOL, "dD (bf16)")
+    assert_close(dW, rdW, BF16_TOL, "dW (bf16)")
+    assert_close(dbias, rdbias, GRAD_TOL, "dbias")
+    assert_close(dtheta, rdtheta, GRAD_TOL, "dtheta")
