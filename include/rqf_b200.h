@@ -92,7 +92,11 @@ int rqf_selftest_lookback_timeout(void *scratch, rqf_stream_t stream);
 int64_t rqf_btf_num_tiles(int64_t time);
 int64_t rqf_btf_carry_count(int64_t batch, int64_t time, int64_t filters);
 size_t rqf_btf_scratch_bytes(int64_t batch, int64_t time, int64_t filters);
-/* FBT kernels: rows = filters * batch, tiles along time.  The scratch size is
+/* FBT kernels: rows = filters * batch, tiles of 2048 samples along time.  The
+ * saved context ("carries", complex64) holds one entry state per thread (256)
+ * of every tile plus one marker element: the forward fills it and the
+ * backward replays each thread's states from it (rqf_fbt_carry_count; 1/8 of
+ * the (F,B,T) tensor's size; 0 for rejected shapes).  The scratch size is
  * SIZE_MAX for shapes that the FBT entry points reject (RQF_ERR_SHAPE). */
 int64_t rqf_fbt_num_tiles(int64_t time);
 int64_t rqf_fbt_carry_count(int64_t filters, int64_t batch, int64_t time);

@@ -13,8 +13,10 @@
 // memory.  Work cursors are advanced incrementally (no integer division in the
 // loop).
 //
-// Same tile length and per-tile carries as fbt_scan.cuh, so the forward and
-// backward of either variant pair up.
+// Same tile length and saved-context layout as fbt_scan.cuh (kFbtSlots), so
+// the forward and backward of either variant pair up.  The forward saves every
+// thread's entry state, so the backward replays each thread's states from its
+// own entry without a forward scan of the tile.
 #pragma once
 
 #include "fbt_scan.cuh"
@@ -116,6 +118,9 @@ __global__ void __launch_bounds__(NT) fbt_fwd_rows_kernel(const FbtArgs a) {
   const int G = gridDim.x, rows = (int)a.rows, T = (int)a.T, ntiles = a.ntiles;
   const int wofs = warp * 32 * K;
 
+  static_assert(NT == kFbtSlots, "one saved entry state per thread");
+  if (blockIdx.x == 0 && tid == 0)
+    a.carries[fbt_marker(a.rows, ntiles)] = make_float2(1.f, 0.f);  // every slot written
   RowCursor ic{(int)blockIdx.x, 0, 0};  // next item to issue
   auto issue = [&]() {
     if (ic.row < rows) {
@@ -174,7 +179,8 @@ __global__ void __launch_bounds__(NT) fbt_fwd_rows_kernel(const FbtArgs a) {
     float2 e, At;
     cta_scan_entry_fwd<NT, LK>(y, carry, pw, lanepow, e, At, s_warp);
     if (tid == NT - 1) s_zlast = z[K - 1];
-    if (tid == 0) a.carries[(size_t)pc.row * ntiles + pc.j] = carry;
+    // every thread's entry state (slot 0: the tile's own entry, e == carry)
+    a.carries[fbt_slot(pc.row, ntiles, pc.j) + tid] = e;
     carry = At;  // entry of the next tile of this row
     float2 o[K];
 #pragma unroll
@@ -205,6 +211,7 @@ __global__ void __launch_bounds__(NT, 3) fbt_bwd_rows_kernel(const FbtArgs a) {
   extern __shared__ __align__(16) float4 dsm[];  // [S][2 inputs][NW][WSZ]
   __shared__ float2 s_pw[S][kPowTable];
   __shared__ float2 s_meta[S][2];  // {entry carry C, z sample before the tile}
+  __shared__ float2 s_ent[S][NT];  // this tile's per-thread entry states, when saved
   __shared__ float2 s_warp_f[NW];
   __shared__ float2 s_warp_r[NW];
   __shared__ float2 s_red[3][NW];
@@ -212,6 +219,10 @@ __global__ void __launch_bounds__(NT, 3) fbt_bwd_rows_kernel(const FbtArgs a) {
   const int G = gridDim.x, rows = (int)a.rows, T = (int)a.T, ntiles = a.ntiles;
   const int wofs = warp * 32 * K;
   constexpr size_t stage_sz = (size_t)2 * NW * WSZ;
+  static_assert(NT == kFbtSlots, "one saved entry state per thread");
+  // The forward saved every thread's entry state (row kernels) or only the
+  // tiles' (look-back kernels): one uniform branch per launch.
+  const bool per_thread = __ldg(a.carries + fbt_marker(a.rows, ntiles)).x == 1.f;
 
   // j counts processed tiles of the row; the tile index in time is ntiles-1-j.
   RowCursor ic{(int)blockIdx.x, 0, 0};
@@ -222,9 +233,11 @@ __global__ void __launch_bounds__(NT, 3) fbt_bwd_rows_kernel(const FbtArgs a) {
       const size_t roff = (size_t)ic.row * T;
       fbt_issue_tile<K>(base + warp * WSZ, a.z + roff, jt * L + wofs, T, lane);
       fbt_issue_tile<K>(base + (NW + warp) * WSZ, a.gout + roff, jt * L + wofs, T, lane);
+      if (per_thread) cp_async8(&s_ent[ic.stage][tid], a.carries + fbt_slot(ic.row, ntiles, jt) + tid,
+                                true);
       if (tid == 0) {
         const int t0 = jt * L;
-        cp_async8(&s_meta[ic.stage][0], a.carries + (size_t)ic.row * ntiles + jt, true);
+        cp_async8(&s_meta[ic.stage][0], a.carries + fbt_slot(ic.row, ntiles, jt), true);
         cp_async8(&s_meta[ic.stage][1], a.z + roff + (t0 > 0 ? t0 - 1 : 0), t0 > 0);
         stage_table<S>(s_pw, ic.stage, ic.j == 0, a.c1, ic.row / a.batch);
       }
@@ -273,11 +286,15 @@ __global__ void __launch_bounds__(NT, 3) fbt_bwd_rows_kernel(const FbtArgs a) {
         sp = sk;
       }
     }
-    float2 y = cz();
+    float2 e;
+    if (per_thread) {
+      e = s_ent[s][tid];
+    } else {
+      float2 y = cz(), At;
 #pragma unroll
-    for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
-    float2 e, At;
-    cta_scan_entry_fwd<NT, LK>(y, s_meta[s][0], pw, lpow_f, e, At, s_warp_f);
+      for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
+      cta_scan_entry_fwd<NT, LK>(y, s_meta[s][0], pw, lpow_f, e, At, s_warp_f);
+    }
     float2 yprev[K];
 #pragma unroll
     for (int k = 0; k < K; ++k) {
@@ -359,6 +376,7 @@ __global__ void __launch_bounds__(NT, 3) fbt_tbptt_rows_kernel(const FbtArgs a) 
   extern __shared__ __align__(16) float4 dsm[];  // [S][2 inputs][NW][WSZ]
   __shared__ float2 s_pw[S][kPowTable];
   __shared__ float2 s_meta[S][2];  // {entry carry C, z sample before the tile}
+  __shared__ float2 s_ent[S][NT];  // this tile's per-thread entry states, when saved
   __shared__ float2 s_warp_f[NW];
   __shared__ float2 s_gfirst[NW];
   __shared__ float2 s_red[3][NW];
@@ -366,6 +384,8 @@ __global__ void __launch_bounds__(NT, 3) fbt_tbptt_rows_kernel(const FbtArgs a) 
   const int G = gridDim.x, rows = (int)a.rows, T = (int)a.T, ntiles = a.ntiles;
   const int wofs = warp * 32 * K;
   constexpr size_t stage_sz = (size_t)2 * NW * WSZ;
+  static_assert(NT == kFbtSlots, "one saved entry state per thread");
+  const bool per_thread = __ldg(a.carries + fbt_marker(a.rows, ntiles)).x == 1.f;
 
   RowCursor ic{(int)blockIdx.x, 0, 0};
   auto issue = [&]() {
@@ -374,9 +394,11 @@ __global__ void __launch_bounds__(NT, 3) fbt_tbptt_rows_kernel(const FbtArgs a) 
       const size_t roff = (size_t)ic.row * T;
       fbt_issue_tile<K>(base + warp * WSZ, a.z + roff, ic.j * L + wofs, T, lane);
       fbt_issue_tile<K>(base + (NW + warp) * WSZ, a.gout + roff, ic.j * L + wofs, T, lane);
+      if (per_thread)
+        cp_async8(&s_ent[ic.stage][tid], a.carries + fbt_slot(ic.row, ntiles, ic.j) + tid, true);
       if (tid == 0) {
         const int t0 = ic.j * L;
-        cp_async8(&s_meta[ic.stage][0], a.carries + (size_t)ic.row * ntiles + ic.j, true);
+        cp_async8(&s_meta[ic.stage][0], a.carries + fbt_slot(ic.row, ntiles, ic.j), true);
         cp_async8(&s_meta[ic.stage][1], a.z + roff + (t0 > 0 ? t0 - 1 : 0), t0 > 0);
         stage_table<S>(s_pw, ic.stage, ic.j == 0, a.c1, ic.row / a.batch);
       }
@@ -426,11 +448,15 @@ __global__ void __launch_bounds__(NT, 3) fbt_tbptt_rows_kernel(const FbtArgs a) 
         sp = sk;
       }
     }
-    float2 y = cz();
+    float2 e;
+    if (per_thread) {
+      e = s_ent[s][tid];
+    } else {
+      float2 y = cz(), At;
 #pragma unroll
-    for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
-    float2 e, At;
-    cta_scan_entry_fwd<NT, LK>(y, s_meta[s][0], pw, lpow, e, At, s_warp_f);
+      for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
+      cta_scan_entry_fwd<NT, LK>(y, s_meta[s][0], pw, lpow, e, At, s_warp_f);
+    }
 #pragma unroll
     for (int k = 0; k < K; ++k) {
       const float2 yp = e;

@@ -32,7 +32,7 @@ struct FbtArgs {
   const float2 *skip;              // (rows, T) added to the forward output, or null
   float2 *out;                     // forward: act / raw; backward: grad_z
   float2 *out2;                    // TBPTT backward: grad_zw
-  float2 *carries;                 // (rows, ntiles)
+  float2 *carries;                 // entry states, see kFbtSlots
   float2 *partials;                // (rows, ntiles, 3)
   u64 *flags;                      // (rows, ntiles, 2)
   unsigned *ticket;
@@ -46,6 +46,20 @@ constexpr int kFbtThreads = 256;
 constexpr int kFbtK = 8;
 constexpr int kFbtTile = kFbtThreads * kFbtK;  // 2048 samples
 constexpr int kFbtLog2Tile = 11;
+// Saved context of the forward: one entry state per thread of every tile,
+// (rows, ntiles, kFbtSlots) complex, slot 0 being the tile's own entry, and
+// one marker element after them.  The persistent row kernels write every
+// slot and the marker (1, 0): their backward then starts each thread from its
+// own entry and needs no forward scan.  The look-back tile kernels write slot
+// 0 and the marker (0, 0), and their backward (or a row backward that finds
+// the marker unset) scans from the tile entry.
+constexpr int kFbtSlots = kFbtThreads;
+__host__ __device__ __forceinline__ int64_t fbt_slot(int64_t row, int ntiles, int j) {
+  return (row * ntiles + j) * kFbtSlots;
+}
+__host__ __device__ __forceinline__ int64_t fbt_marker(int64_t rows, int ntiles) {
+  return rows * ntiles * kFbtSlots;
+}
 constexpr int kPowTable = 12;  // lambda^(2^i), i <= log2(tile)
 
 // Load the K samples [tfirst, tfirst+K) of this thread (blocked order).
@@ -145,7 +159,8 @@ __global__ void __launch_bounds__(NT) fbt_fwd_kernel(const FbtArgs a) {
       C = lookback_const(fl, j, M);
       if (has_next) flag_publish2(fl + 2 * j, c_fma(M, C, At), kInclusive);
     }
-    a.carries[row * a.ntiles + j] = C;
+    a.carries[fbt_slot(row, a.ntiles, j)] = C;
+    if (tk == 0) a.carries[fbt_marker(a.rows, a.ntiles)] = cz();
     s_carry = C;
   }
   __syncthreads();
@@ -191,7 +206,7 @@ __global__ void __launch_bounds__(NT) fbt_bwd_kernel(const FbtArgs a) {
   const int j = a.ntiles - 1 - p;                         // tile index in time
   const int f = (int)(row / a.batch);
   const float2 lam = a.c1[f], t0 = a.tap0[f], t1 = a.tap1[f];
-  const float2 C = a.carries[row * a.ntiles + j];
+  const float2 C = a.carries[fbt_slot(row, a.ntiles, j)];
   const float2 *zrow = a.z + row * a.T;
   const float2 *grow = a.gout + row * a.T;
   const int64_t wstart = (int64_t)j * L + (int64_t)warp * 32 * K;
@@ -300,7 +315,7 @@ __global__ void __launch_bounds__(NT) fbt_tbptt_bwd_kernel(const FbtArgs a) {
   const int j = (int)(blockIdx.x - (unsigned)(row * a.ntiles));
   const int f = (int)(row / a.batch);
   const float2 lam = a.c1[f], t0 = a.tap0[f], t1 = a.tap1[f];
-  const float2 C = a.carries[row * a.ntiles + j];
+  const float2 C = a.carries[fbt_slot(row, a.ntiles, j)];
   const float2 *zrow = a.z + row * a.T;
   const float2 *grow = a.gout + row * a.T;
   const int64_t wstart = (int64_t)j * L + (int64_t)warp * 32 * K;

@@ -541,7 +541,9 @@ size_t rqf_btf_scratch_bytes(int64_t batch, int64_t time, int64_t filters) {
 }
 int64_t rqf_fbt_num_tiles(int64_t time) { return time <= 0 ? 0 : ceil_div(time, kFbtTile); }
 int64_t rqf_fbt_carry_count(int64_t filters, int64_t batch, int64_t time) {
-  return filters * batch * rqf_fbt_num_tiles(time);
+  if (fbt_dims_ok(filters, batch, time) != RQF_OK) return 0;
+  // per-thread entry states of every tile, plus the marker element
+  return fbt_marker(filters * batch, (int)rqf_fbt_num_tiles(time)) + 1;
 }
 size_t rqf_fbt_scratch_bytes(int64_t filters, int64_t batch, int64_t time) {
   if (fbt_dims_ok(filters, batch, time) != RQF_OK) return SIZE_MAX;  // no such launch

@@ -76,7 +76,8 @@ def test_size_queries(lib):
     assert lib.rqf_fbt_num_tiles(2048) == 1
     assert lib.rqf_fbt_num_tiles(2049) == 2
     assert lib.rqf_fbt_num_tiles(0) == 0
-    assert lib.rqf_fbt_carry_count(128, 16, 16000) == 128 * 16 * 8
+    # one entry state per thread (256) of every tile, plus the marker element
+    assert lib.rqf_fbt_carry_count(128, 16, 16000) == 128 * 16 * 8 * 256 + 1
     assert lib.rqf_btf_num_tiles(161) == 3  # 64-step sub-tiles
     assert lib.rqf_btf_carry_count(32, 161, 128) == 32 * 128 * 3
     s = lib.rqf_fbt_scratch_bytes(128, 16, 16000)
