@@ -379,6 +379,34 @@ int rqf_projection(const float *w, const float *x, const float *acc, float *out,
                    int64_t k, int64_t n, int conj_transpose, void *workspace,
                    rqf_stream_t stream);
 
+/* Pure RQF block forward in one launch: the projection of pure.py:223 with
+ * the block's scan, activation and skip connection (pure.py:529-535) run in
+ * the GEMM's epilogue, tile by tile, while the tensor cores work on the next
+ * tile.  Equal to rqf_projection (conj_transpose = 0, acc = NULL) into z
+ * followed by rqf_fbt_block_forward(c1, tap0, tap1, z, skip, out, carries):
+ *
+ *   z   = W x                       complex (filters, batch*time), written
+ *   out = act(y) + skip             y the two-tap scan of z along time
+ *   carries                         every 8-sample group's entry state, the
+ *                                   saved context of the (F,B,T) row kernels
+ *
+ * so rqf_fbt_prospective_backward and rqf_tbptt1_two_tap_backward (layout 1)
+ * take its z and carries unchanged.  W is (filters x k), x (k x batch*time)
+ * with time contiguous, skip (nullable) and out (filters, batch, time);
+ * carries holds rqf_fbt_carry_count(filters, batch, time) complex values.
+ * The scan's state crosses the GEMM's 128-sample tiles through link records
+ * in the workspace (rqf_projection_block_scan_workspace_bytes; 0 for shapes
+ * this entry rejects): every tile waits, bounded, for the tile before it.
+ * Requirements: time a multiple of 128, batch * time < 2^30, k > 0, x / z /
+ * out / skip / carries / workspace 16-byte aligned, out distinct from x, z
+ * and skip, z distinct from x and skip (RQF_ERR_ARGUMENT). */
+size_t rqf_projection_block_scan_workspace_bytes(int64_t filters, int64_t k, int64_t batch,
+                                                 int64_t time);
+int rqf_projection_block_scan(const float *w, const float *x, const float *c1, const float *tap0,
+                              const float *tap1, const float *skip, float *z, float *out,
+                              float *carries, void *workspace, int64_t filters, int64_t k,
+                              int64_t batch, int64_t time, int fuse_act, rqf_stream_t stream);
+
 /* Weight cotangent of the same projection (autograd of pure.py:223's matmul
  * with respect to W; cuBLAS fp32 in the reference):
  *

@@ -163,16 +163,7 @@ __global__ void __launch_bounds__(NT) fbt_fwd_rows_kernel(const FbtArgs a) {
         zp = (pc.j > 0) ? s_zlast : cz();
     }
     float2 b[K];
-    {
-      const CPair T0 = cpair(t0), T1 = cpair(t1);
-      float2 sp = c_swap(zp);
-#pragma unroll
-      for (int k = 0; k < K; ++k) {
-        const float2 sk = c_swap(z[k]);
-        b[k] = cp_fma(T0, z[k], sk, cp_mul(T1, k > 0 ? z[k - 1] : zp, sp));
-        sp = sk;
-      }
-    }
+    fbt_drive<K>(t0, t1, z, zp, b);
     float2 y = cz();
 #pragma unroll
     for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
@@ -276,16 +267,7 @@ __global__ void __launch_bounds__(NT, 3) fbt_bwd_rows_kernel(const FbtArgs a) {
     if (lane == 0) zp = warp > 0 ? read_sample<K>(zbuf - WSZ, 32 * K - 1) : s_meta[s][1];
 
     float2 b[K];
-    {
-      const CPair T0 = cpair(t0), T1 = cpair(t1);
-      float2 sp = c_swap(zp);
-#pragma unroll
-      for (int k = 0; k < K; ++k) {
-        const float2 sk = c_swap(z[k]);
-        b[k] = cp_fma(T0, z[k], sk, cp_mul(T1, k > 0 ? z[k - 1] : zp, sp));
-        sp = sk;
-      }
-    }
+    fbt_drive<K>(t0, t1, z, zp, b);
     float2 e;
     if (per_thread) {
       e = s_ent[s][tid];
@@ -434,20 +416,11 @@ __global__ void __launch_bounds__(NT, 3) fbt_tbptt_rows_kernel(const FbtArgs a) 
     read_blocked<K>(gbuf, go, lane);
     float2 zp = shfl_up2(z[K - 1], 1);
     if (lane == 0) zp = warp > 0 ? read_sample<K>(zbuf - WSZ, 32 * K - 1) : s_meta[s][1];
-    // The drive exactly as fbt_fwd_rows_kernel forms it (same paired FMAs), so
-    // the replayed states, and with them the split-ReLU decisions, are the
+    // The drive exactly as every forward forms it (fbt_drive), so the
+    // replayed states, and with them the split-ReLU decisions, are the
     // forward's bit for bit.
     float2 b[K];
-    {
-      const CPair T0 = cpair(t0c), T1 = cpair(t1c);
-      float2 sp = c_swap(zp);
-#pragma unroll
-      for (int k = 0; k < K; ++k) {
-        const float2 sk = c_swap(z[k]);
-        b[k] = cp_fma(T0, z[k], sk, cp_mul(T1, k > 0 ? z[k - 1] : zp, sp));
-        sp = sk;
-      }
-    }
+    fbt_drive<K>(t0c, t1c, z, zp, b);
     float2 e;
     if (per_thread) {
       e = s_ent[s][tid];

@@ -48,11 +48,14 @@ constexpr int kFbtTile = kFbtThreads * kFbtK;  // 2048 samples
 constexpr int kFbtLog2Tile = 11;
 // Saved context of the forward: one entry state per thread of every tile,
 // (rows, ntiles, kFbtSlots) complex, slot 0 being the tile's own entry, and
-// one marker element after them.  The persistent row kernels write every
-// slot and the marker (1, 0): their backward then starts each thread from its
-// own entry and needs no forward scan.  The look-back tile kernels write slot
-// 0 and the marker (0, 0), and their backward (or a row backward that finds
-// the marker unset) scans from the tile entry.
+// one marker element after them.  Every (F,B,T) forward — the persistent row
+// kernels, the look-back tile kernels and the projection's scan epilogue —
+// writes every slot and the marker (1, 0), and computes each output from its
+// thread's entry with the drive of fbt_drive and y = c1 y + b.  Every
+// backward starts each thread from that entry with the same operations, so
+// it replays the forward's states bit for bit (the split-ReLU decisions of a
+// state within rounding of zero included) whichever kernel family ran the
+// forward.  A backward that finds the marker unset scans from the tile entry.
 constexpr int kFbtSlots = kFbtThreads;
 __host__ __device__ __forceinline__ int64_t fbt_slot(int64_t row, int ntiles, int j) {
   return (row * ntiles + j) * kFbtSlots;
@@ -61,6 +64,21 @@ __host__ __device__ __forceinline__ int64_t fbt_marker(int64_t rows, int ntiles)
   return rows * ntiles * kFbtSlots;
 }
 constexpr int kPowTable = 12;  // lambda^(2^i), i <= log2(tile)
+
+// Two-tap drive of K consecutive samples, b[k] = tap0 z[k] + tap1 z[k-1]
+// (zp = the sample before z[0]), on paired FMAs.
+template <int K>
+__device__ __forceinline__ void fbt_drive(float2 t0, float2 t1, const float2 (&z)[K], float2 zp,
+                                          float2 (&b)[K]) {
+  const CPair T0 = cpair(t0), T1 = cpair(t1);
+  float2 sp = c_swap(zp);
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const float2 sk = c_swap(z[k]);
+    b[k] = cp_fma(T0, z[k], sk, cp_mul(T1, k > 0 ? z[k - 1] : zp, sp));
+    sp = sk;
+  }
+}
 
 // Load the K samples [tfirst, tfirst+K) of this thread (blocked order).
 template <int K, bool VEC>
@@ -137,9 +155,7 @@ __global__ void __launch_bounds__(NT) fbt_fwd_kernel(const FbtArgs a) {
   if (lane == 0) zp = (tfirst > 0 && tfirst - 1 < a.T) ? zrow[tfirst - 1] : cz();
 
   float2 b[K];
-  b[0] = c_fma(t1, zp, c_mul(t0, z[0]));
-#pragma unroll
-  for (int k = 1; k < K; ++k) b[k] = c_fma(t1, z[k - 1], c_mul(t0, z[k]));
+  fbt_drive<K>(t0, t1, z, zp, b);
   float2 y = cz();
 #pragma unroll
   for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
@@ -159,12 +175,13 @@ __global__ void __launch_bounds__(NT) fbt_fwd_kernel(const FbtArgs a) {
       C = lookback_const(fl, j, M);
       if (has_next) flag_publish2(fl + 2 * j, c_fma(M, C, At), kInclusive);
     }
-    a.carries[fbt_slot(row, a.ntiles, j)] = C;
-    if (tk == 0) a.carries[fbt_marker(a.rows, a.ntiles)] = cz();
+    if (tk == 0) a.carries[fbt_marker(a.rows, a.ntiles)] = make_float2(1.f, 0.f);
     s_carry = C;
   }
   __syncthreads();
-  float2 e = c_fma(G, s_carry, X);
+  // every thread's entry state (slot 0: the tile's own entry)
+  float2 e = tid == 0 ? s_carry : c_fma(G, s_carry, X);
+  a.carries[fbt_slot(row, a.ntiles, j) + tid] = e;
   float2 o[K];
 #pragma unroll
   for (int k = 0; k < K; ++k) {
@@ -207,6 +224,7 @@ __global__ void __launch_bounds__(NT) fbt_bwd_kernel(const FbtArgs a) {
   const int f = (int)(row / a.batch);
   const float2 lam = a.c1[f], t0 = a.tap0[f], t1 = a.tap1[f];
   const float2 C = a.carries[fbt_slot(row, a.ntiles, j)];
+  const bool per_thread = __ldg(a.carries + fbt_marker(a.rows, a.ntiles)).x == 1.f;
   const float2 *zrow = a.z + row * a.T;
   const float2 *grow = a.gout + row * a.T;
   const int64_t wstart = (int64_t)j * L + (int64_t)warp * 32 * K;
@@ -218,17 +236,21 @@ __global__ void __launch_bounds__(NT) fbt_bwd_kernel(const FbtArgs a) {
   float2 zp = shfl_up2(z[K - 1], 1);
   if (lane == 0) zp = (tfirst > 0 && tfirst - 1 < a.T) ? zrow[tfirst - 1] : cz();
 
-  // Recompute the forward states of this tile from its stored entry carry.
+  // Replay the forward states of this tile from the saved entries (or, with
+  // the marker unset, from a scan of the tile entry carry).
   float2 b[K];
-  b[0] = c_fma(t1, zp, c_mul(t0, z[0]));
+  fbt_drive<K>(t0, t1, z, zp, b);
+  float2 e;
+  if (per_thread) {
+    e = a.carries[fbt_slot(row, a.ntiles, j) + tid];
+  } else {
+    float2 y = cz();
 #pragma unroll
-  for (int k = 1; k < K; ++k) b[k] = c_fma(t1, z[k - 1], c_mul(t0, z[k]));
-  float2 y = cz();
-#pragma unroll
-  for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
-  float2 G, X, At;
-  cta_scan_const_fwd<NT, LK>(y, s_pw, G, X, At, s_warp_f);
-  float2 e = c_fma(G, C, X);
+    for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
+    float2 G, X, At;
+    cta_scan_const_fwd<NT, LK>(y, s_pw, G, X, At, s_warp_f);
+    e = c_fma(G, C, X);
+  }
   float2 yprev[K];  // y[t-1] per sample; reuse b[] storage for the masked cotangent
 #pragma unroll
   for (int k = 0; k < K; ++k) {
@@ -316,6 +338,7 @@ __global__ void __launch_bounds__(NT) fbt_tbptt_bwd_kernel(const FbtArgs a) {
   const int f = (int)(row / a.batch);
   const float2 lam = a.c1[f], t0 = a.tap0[f], t1 = a.tap1[f];
   const float2 C = a.carries[fbt_slot(row, a.ntiles, j)];
+  const bool per_thread = __ldg(a.carries + fbt_marker(a.rows, a.ntiles)).x == 1.f;
   const float2 *zrow = a.z + row * a.T;
   const float2 *grow = a.gout + row * a.T;
   const int64_t wstart = (int64_t)j * L + (int64_t)warp * 32 * K;
@@ -328,16 +351,19 @@ __global__ void __launch_bounds__(NT) fbt_tbptt_bwd_kernel(const FbtArgs a) {
   if (lane == 0) zp = (tfirst > 0 && tfirst - 1 < a.T) ? zrow[tfirst - 1] : cz();
 
   float2 b[K];
-  b[0] = c_fma(t1, zp, c_mul(t0, z[0]));
-#pragma unroll
-  for (int k = 1; k < K; ++k) b[k] = c_fma(t1, z[k - 1], c_mul(t0, z[k]));
-  float2 y = cz();
-#pragma unroll
-  for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
+  fbt_drive<K>(t0, t1, z, zp, b);
   __syncthreads();  // s_pw
-  float2 G, X, At;
-  cta_scan_const_fwd<NT, LK>(y, s_pw, G, X, At, s_warp_f);
-  float2 e = c_fma(G, C, X);
+  float2 e;
+  if (per_thread) {
+    e = a.carries[fbt_slot(row, a.ntiles, j) + tid];
+  } else {
+    float2 y = cz();
+#pragma unroll
+    for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
+    float2 G, X, At;
+    cta_scan_const_fwd<NT, LK>(y, s_pw, G, X, At, s_warp_f);
+    e = c_fma(G, C, X);
+  }
   float2 yprev[K];
 #pragma unroll
   for (int k = 0; k < K; ++k) {
@@ -354,8 +380,12 @@ __global__ void __launch_bounds__(NT) fbt_tbptt_bwd_kernel(const FbtArgs a) {
     if (tn < a.T) {
       g_next = grow[tn];
       if (FUSE_ACT) {
-        const float2 yn = c_fma(lam, e, c_fma(t1, z[K - 1], c_mul(t0, zrow[tn])));
-        g_next = c_relu_mask(g_next, yn);
+        // the next tile's first state, as that tile's thread 0 replays it
+        const float2 zn = zrow[tn];
+        const CPair T0 = cpair(t0), T1 = cpair(t1);
+        const float2 bn = cp_fma(T0, zn, c_swap(zn), cp_mul(T1, z[K - 1], c_swap(z[K - 1])));
+        const float2 en = per_thread ? a.carries[fbt_slot(row, a.ntiles, j + 1)] : e;
+        g_next = c_relu_mask(g_next, c_fma(lam, en, bn));
       }
     }
     s_first[NW] = g_next;

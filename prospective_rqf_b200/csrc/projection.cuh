@@ -56,6 +56,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "fbt_scan.cuh"
 #include "rqf_common.cuh"
 
 namespace rqf {
@@ -102,8 +103,8 @@ constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
 
 // Where the first expired wait of the projection pipeline gave up (0 = none):
 // 1 producer/empty, 2 transform/full, 3 MMA/accumulator-drained, 4 MMA/ready,
-// 5 epilogue/accumulator-full, 6 shutdown drain.  Read by
-// rqf_projection_timeout_site().
+// 5 epilogue/accumulator-full, 6 shutdown drain, 7 scan epilogue/link record
+// of the tile before along time.  Read by rqf_projection_timeout_site().
 __device__ int g_proj_timeout_site;
 
 struct Params {
@@ -117,6 +118,33 @@ struct Params {
   int a_rows_pad;      // rows of the hi half of the split A' buffer (a multiple of kPairM)
   int real_x;          // X real (K x N): columns are samples, not (Re, Im) pairs
   float *out_real;     // real-output mode: Re(op(W) x), float32 (M x N)
+  // Scan mode (proj_kernel<false, true>): the epilogue also runs the Pure RQF
+  // block's two-tap scan along each output row (see ScanParams).
+  int scan;
+};
+
+// The block scan fused into the projection's epilogue: out row j of the
+// (F,B,T) layout is filter j, N = B*T samples with T contiguous.  Per row,
+//   y[t] = c1 y[t-1] + tap0 z[t] + tap1 z[t-1],  act = split-ReLU(y) or y,
+//   out = act + skip,
+// computed exactly as fbt_fwd_rows_kernel computes it (same drive and
+// recurrence operations, 8 samples sequentially from their entry), so the
+// (F,B,T) backward replays the same states from the entries saved here.
+struct ScanParams {
+  const float2 *c1, *tap0, *tap1;  // (M,)
+  const float2 *skip;              // (M, N) or null
+  float2 *act;                     // (M, N) output
+  float2 *carries;                 // fbt_slot layout of the (F,B,T) kernels
+  float4 *link;                    // (num_tiles, 2 ranks, 64 rows): {y, z} at a tile's end
+  // (num_tiles, 2 ranks, 4 epilogue warps) link-published flags, then one
+  // abort word; all zeroed before the launch
+  unsigned *flags;
+  long long T;                     // samples per batch row (a multiple of 128)
+  int batch;                       // N / T
+  int tiles_per_row;               // T / 128: pair tiles of one (row block, batch) chain
+  int chains;                      // m_pairs * batch
+  int fbt_ntiles;                  // ceil(T / 2048): tiles of the (F,B,T) saved context
+  int fuse_act;
 };
 
 // ------------------------------------------------------------ PTX wrappers
@@ -393,7 +421,19 @@ __global__ void proj_prep_real_out_kernel(const float2 *__restrict__ W, float *_
 // Pair tile t covers A' rows [mp*256, mp*256+256) and X' columns
 // [nt*256, nt*256+256); the pair tiles of one X' column block are neighbours
 // (mp fastest), so the block is read from HBM once and from L2 after.
-__device__ __forceinline__ void tile_coords(long long tile, const Params &p, int &mp, int &nt) {
+// In scan mode the tiles run position-major over the (row block, batch)
+// chains instead: the pair tiles that run at the same time belong to different
+// chains, so a tile's predecessor along time (the tile `chains` earlier) has
+// normally finished before its epilogue needs the predecessor's end state.
+__device__ __forceinline__ void tile_coords(long long tile, const Params &p, int &mp, int &nt,
+                                            const ScanParams *sp = nullptr) {
+  if (sp != nullptr && p.scan) {
+    const long long pos = tile / sp->chains;
+    const int ch = (int)(tile - pos * sp->chains);
+    mp = ch % p.m_pairs;
+    nt = (int)((long long)(ch / p.m_pairs) * sp->tiles_per_row + pos);
+    return;
+  }
   mp = (int)(tile % p.m_pairs);
   nt = (int)(tile / p.m_pairs);
 }
@@ -406,10 +446,229 @@ __device__ __forceinline__ uint32_t mn32_offset(int c, int k) {
                     ((c & 7) << 2));
 }
 
-template <bool kRealOut>
+// ------------------------------------------------------------ scan epilogue
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_u32(unsigned *p, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_u32(unsigned *p, unsigned v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait of one epilogue warp for the link record of the tile before
+// its own along time.  False when the time limit passes (error latched) or
+// when this CTA or any other has aborted; either way the launch-wide abort
+// word is raised so that no other waiter runs into its own time limit.
+__device__ __forceinline__ bool scan_link_wait(const unsigned *flag, unsigned *abort_word,
+                                               volatile int *abort) {
+  const unsigned long long t0 = global_ns();
+  unsigned ns = 64;
+  for (;;) {
+    if (ld_acquire_u32(flag) != 0u) return true;
+    if (*abort || ld_relaxed_u32(abort_word) != 0u) break;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      latch_error(kErrPipelineTimeout);
+      atomicCAS(&g_proj_timeout_site, 0, 7);
+      break;
+    }
+    __nanosleep(ns);
+    ns = ns < 1024u ? 2u * ns : 1024u;
+  }
+  *abort = 1;
+  st_relaxed_u32(abort_word, 1u);
+  return false;
+}
+
+// One epilogue warp's share of a scan-mode pair tile: 16 filter rows (lane
+// pair 2r, 2r+1 holds row jw0 + r) x the tile's 128 samples, which lie in one
+// batch row because T is a multiple of 128.  Eight chunks of 16 samples,
+// the even lane's 8 then the odd lane's 8; per chunk:
+//   z        combined from the TMEM products as in the plain epilogue,
+//            staged and stored to p.out (the (F,B,T) backward reads it);
+//   drive    b[k] = tap0 z[k] + tap1 z[k-1] (fbt_drive, as every (F,B,T)
+//            kernel computes it);
+//   entry    the even lane enters with the row's running state E and folds
+//            its 8 drives; the odd lane enters with that result;
+//   outputs  both lanes run y = c1 y + b[k] from their own entry (the
+//            operations that the (F,B,T) backward replays from the saved
+//            entry, so its split-ReLU mask is this one), act = split-ReLU(y)
+//            or y, plus skip, staged and stored to sp.act.
+// Every lane's entry is the saved context slot of its 8 samples; the 16
+// slots of each row are staged and written as one 128-byte piece per tile.
+// The state entering the tile, {y, z} at the sample before it, is the link
+// record that the tile before it along time (tile - chains) published; at
+// the end of the tile this one publishes its own.  False on an abort.
+__device__ __forceinline__ bool scan_epilogue(uint32_t tbase, float4 *stage, const Params &p,
+                                              const ScanParams &sp, long long tile, int mp,
+                                              int nt, int rank, int quarter, int lane,
+                                              volatile int *abort) {
+  const bool odd = (lane & 1) != 0;
+  const int r_own = lane >> 1;
+  const long long jw0 = ((long long)mp * kPairM + (long long)rank * kBM + quarter * 32) >> 1;
+  const long long jrow = jw0 + r_own;
+  const bool row_ok = jrow < p.M;
+  const int bidx = nt / sp.tiles_per_row;
+  const int pos = nt - bidx * sp.tiles_per_row;
+  const long long tfirst = (long long)pos * (kBN / 2);  // first sample in the batch row
+  const long long n0 = (long long)nt * (kBN / 2);       // first sample in N
+  const float2 lam = row_ok ? __ldg(sp.c1 + jrow) : cz();
+  const float2 tap0 = row_ok ? __ldg(sp.tap0 + jrow) : cz();
+  const float2 tap1 = row_ok ? __ldg(sp.tap1 + jrow) : cz();
+  unsigned *abort_word = sp.flags + p.num_tiles * 8;
+
+  float2 E = cz(), zl = cz();  // y and z at the sample before the chunk
+  if (pos > 0) {
+    const long long pred = (tile - sp.chains) * 2 + rank;
+    const bool ok = scan_link_wait(sp.flags + pred * 4 + quarter, abort_word, abort);
+    if (!__all_sync(0xffffffffu, ok)) return false;
+    const float4 l = __ldcg(sp.link + pred * 64 + quarter * 16 + r_own);
+    E = make_float2(l.x, l.y);
+    zl = make_float2(l.z, l.w);
+  }
+  float2 *ent = reinterpret_cast<float2 *>(stage + 128);  // [16 rows][16 slots], swizzled
+
+#pragma unroll 1
+  for (int c = 0; c < kBN / 32; ++c) {
+    const long long nbase = n0 + c * 16;
+    // this lane's skip pieces (the store layout: row e >> 3, piece e & 7),
+    // loaded first so that their latency hides behind the TMEM load
+    float4 skp[4];
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int e = it * 32 + lane;
+      const long long jj = jw0 + (e >> 3);
+      skp[it] = (sp.skip != nullptr && jj < p.M)
+                    ? __ldg(reinterpret_cast<const float4 *>(sp.skip + jj * p.N + nbase +
+                                                             2 * (e & 7)))
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float v[32];
+    tc_ld_32x32b_x32(tbase + (uint32_t)(c * 32), v);
+    float r[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) r[i] = __shfl_xor_sync(0xffffffffu, odd ? v[i] : v[16 + i], 1);
+    float2 z[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      const float pr_re = odd ? r[2 * t] : v[2 * t];
+      const float pr_im = odd ? r[2 * t + 1] : v[2 * t + 1];
+      const float pi_re = odd ? v[16 + 2 * t] : r[2 * t];
+      const float pi_im = odd ? v[16 + 2 * t + 1] : r[2 * t + 1];
+      z[t] = make_float2(pr_re - pi_im, pr_im + pi_re);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      stage[r_own * 8 + (((odd ? 4 : 0) + q) ^ (r_own & 7))] =
+          make_float4(z[2 * q].x, z[2 * q].y, z[2 * q + 1].x, z[2 * q + 1].y);
+    __syncwarp();
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int e = it * 32 + lane;
+      const int rr = e >> 3, k = e & 7;
+      const long long jj = jw0 + rr;
+      if (jj < p.M)
+        *reinterpret_cast<float4 *>(p.out + jj * p.N + nbase + 2 * k) = stage[rr * 8 + (k ^ (rr & 7))];
+    }
+    __syncwarp();
+
+    // drives; the odd lane's z before its first sample is the even lane's last
+    const float2 zx = shfl_xor2(z[7], 1);
+    float2 bd[8];
+    fbt_drive<8>(tap0, tap1, z, odd ? zx : zl, bd);
+    zl = odd ? z[7] : zx;  // both lanes: z at the chunk's last sample
+    // entries: the even lane's is E, the odd lane's the even lane's fold of E
+    float2 y = E;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) y = c_fma(lam, y, bd[k]);
+    const float2 yx = shfl_xor2(y, 1);
+    float2 e = odd ? yx : E;
+    ent[r_own * 16 + ((c ^ (r_own & 7)) << 1) + (odd ? 1 : 0)] = e;
+    float2 o[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      e = c_fma(lam, e, bd[k]);
+      o[k] = sp.fuse_act ? c_relu(e) : e;
+    }
+    const float2 ex = shfl_xor2(e, 1);
+    E = odd ? e : ex;  // both lanes: y at the chunk's last sample
+
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      stage[r_own * 8 + (((odd ? 4 : 0) + q) ^ (r_own & 7))] =
+          make_float4(o[2 * q].x, o[2 * q].y, o[2 * q + 1].x, o[2 * q + 1].y);
+    __syncwarp();
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int e4 = it * 32 + lane;
+      const int rr = e4 >> 3, k = e4 & 7;
+      const long long jj = jw0 + rr;
+      if (jj < p.M) {
+        float4 a = stage[rr * 8 + (k ^ (rr & 7))];
+        a = make_float4(a.x + skp[it].x, a.y + skp[it].y, a.z + skp[it].z, a.w + skp[it].w);
+        *reinterpret_cast<float4 *>(sp.act + jj * p.N + nbase + 2 * k) = a;
+      }
+    }
+    __syncwarp();
+  }
+
+  // saved entries: 16 consecutive slots of each row of the (F,B,T) context
+  {
+    const long long jt = tfirst / kFbtTile;
+    const int s0 = (int)(tfirst - jt * kFbtTile) / kFbtK;
+    const float4 *ent4 = reinterpret_cast<const float4 *>(ent);
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int e4 = it * 32 + lane;
+      const int rr = e4 >> 3, k = e4 & 7;
+      const long long jj = jw0 + rr;
+      if (jj < p.M)
+        *reinterpret_cast<float4 *>(
+            sp.carries + fbt_slot(jj * sp.batch + bidx, sp.fbt_ntiles, (int)jt) + s0 + 2 * k) =
+            ent4[rr * 8 + (k ^ (rr & 7))];
+    }
+    // The slots past T of the row's last context tile: zero, so that the
+    // backward's replay of the padded samples stays finite.
+    if (pos == sp.tiles_per_row - 1) {
+      const long long jl = (sp.T - 1) / kFbtTile;
+      const int used = (int)(sp.T - jl * kFbtTile) / kFbtK;  // T % 128 == 0: even
+      const int pairs = (kFbtSlots - used) / 2;
+      for (int i = lane; i < 16 * pairs; i += 32) {
+        const int rr = i / pairs, k = i - rr * pairs;
+        const long long jj = jw0 + rr;
+        if (jj < p.M)
+          *reinterpret_cast<float4 *>(sp.carries +
+                                      fbt_slot(jj * sp.batch + bidx, sp.fbt_ntiles, (int)jl) +
+                                      used + 2 * k) = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    __syncwarp();  // staging reads done before the next tile writes
+  }
+
+  // publish {y, z} at the tile's last sample for the tile after it
+  if (pos + 1 < sp.tiles_per_row) {
+    const long long me = tile * 2 + rank;
+    if (odd) sp.link[me * 64 + quarter * 16 + r_own] = make_float4(E.x, E.y, zl.x, zl.y);
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) st_release_u32(sp.flags + me * 4 + quarter, 1u);
+  }
+  return true;
+}
+
+template <bool kRealOut, bool kScan = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmX,
-            const Params p) {
+            const Params p, const ScanParams sp) {
+  static_assert(!(kRealOut && kScan), "the scan epilogue runs on the complex output");
   using L = ProjLayout<kRealOut>;
   constexpr int kStages = L::kStages;
   constexpr int kStageBytes = L::kStageBytes;
@@ -463,7 +722,7 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       bool ok = true;
       for (long long tile = pair0; ok && tile < p.num_tiles; tile += npairs) {
         int mp, nt;
-        tile_coords(tile, p, mp, nt);
+        tile_coords(tile, p, mp, nt, kScan ? &sp : nullptr);
         const int arow = mp * kPairM + (int)rank * kBM;
         const int xcol = nt * kBN + (int)rank * kBNh;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
@@ -569,14 +828,21 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                                                quarter * (kStagingBytes / 4));
     int acc = 0;
     uint32_t acc_phase = 0;
+    if constexpr (kScan) {  // every thread's entry is saved (the row kernels' marker)
+      if (blockIdx.x == 0 && warp == 2 && lane == 0)
+        sp.carries[fbt_marker(p.M * sp.batch, sp.fbt_ntiles)] = make_float2(1.f, 0.f);
+    }
     for (long long tile = pair0; tile < p.num_tiles; tile += npairs) {
       // every lane waits; the decision is made warp-uniform before the
       // .sync.aligned TMEM loads
       const bool ok = mbar_wait(&accf[acc], acc_phase, abort, 5);
-      if (!__all_sync(0xffffffffu, ok)) break;
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (kScan && lane == 0) st_relaxed_u32(sp.flags + p.num_tiles * 8, 1u);
+        break;
+      }
       tc_fence_after();
       int mp, nt;
-      tile_coords(tile, p, mp, nt);
+      tile_coords(tile, p, mp, nt, kScan ? &sp : nullptr);
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kBN);
       // Each chunk of 32 TMEM columns gives this warp 16 output rows x W
       // samples (W = 16 complex X, 32 real X).  The lanes combine their
@@ -609,6 +875,8 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           }
           __syncwarp();
         }
+      } else if constexpr (kScan) {
+        if (!scan_epilogue(tbase, stage, p, sp, tile, mp, nt, rank, quarter, lane, abort)) break;
       } else {
       const int W = p.real_x ? 32 : 16;            // samples per row per chunk
       const int kpr = W / 2;                       // 16-byte chunks per row

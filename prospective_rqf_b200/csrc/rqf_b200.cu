@@ -1195,10 +1195,18 @@ size_t rqf_projection_workspace_bytes(int64_t m, int64_t k) {
 
 namespace {
 
-// x complex (k x n) when real_x = 0, real (k x n) when real_x = 1.
+int proj_scan_pairs_per_device() {
+  return pair_capacity<4>(reinterpret_cast<const void *>(proj::proj_kernel<false, true>),
+                          proj::kThreads, proj::kSmemBytes);
+}
+
+// x complex (k x n) when real_x = 0, real (k x n) when real_x = 1.  With
+// `scan` (complex x, no acc, n = batch * T): the block scan runs in the
+// epilogue (proj_kernel<false, true>); the caller has checked its shapes and
+// zeroed its flags, and chains is filled in here.
 int projection_impl(const float *w, const float *x, const float *acc, float *out, int64_t m,
                     int64_t k, int64_t n, int conj_transpose, void *workspace,
-                    rqf_stream_t stream, int real_x) {
+                    rqf_stream_t stream, int real_x, const proj::ScanParams *scan = nullptr) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (m < 0 || k < 0 || n < 0) return RQF_ERR_SHAPE;
   if (m == 0 || n == 0) return RQF_OK;
@@ -1222,7 +1230,7 @@ int projection_impl(const float *w, const float *x, const float *acc, float *out
     return RQF_ERR_ALIGN;
   const ProjGeometry g = proj_geometry(m, k);
   if (g.rows_pad > 0x3fffffffLL || g.k_pad > 0x7fffffffLL) return RQF_ERR_SHAPE;
-  const int pairs = proj_pairs_per_device();
+  const int pairs = scan ? proj_scan_pairs_per_device() : proj_pairs_per_device();
   if (pairs <= 0) return RQF_ERR_LAUNCH;
 
   float *a_split = static_cast<float *>(workspace);
@@ -1257,8 +1265,43 @@ int projection_impl(const float *w, const float *x, const float *acc, float *out
   p.real_x = real_x;
   const long long grid = 2 * (p.num_tiles < pairs ? p.num_tiles : pairs);  // whole CTA pairs
   p.out_real = nullptr;
-  proj::proj_kernel<false><<<(unsigned)grid, proj::kThreads, proj::kSmemBytes, st>>>(tmA, tmX, p);
+  p.scan = scan ? 1 : 0;
+  if (scan) {
+    // Every CTA pair must be resident at once: a tile's epilogue waits for
+    // the tile before it along time, which another pair may hold.  The
+    // persistent grid is the device's pair capacity at most.
+    proj::ScanParams sp = *scan;
+    sp.chains = p.m_pairs * sp.batch;
+    proj::proj_kernel<false, true><<<(unsigned)grid, proj::kThreads, proj::kSmemBytes, st>>>(
+        tmA, tmX, p, sp);
+  } else {
+    proj::proj_kernel<false><<<(unsigned)grid, proj::kThreads, proj::kSmemBytes, st>>>(
+        tmA, tmX, p, proj::ScanParams{});
+  }
   return launch_status();
+}
+
+// Workspace of rqf_projection_block_scan: the split op(W), then the link
+// records (num_tiles x 2 ranks x 64 rows of float4), then the flags
+// (num_tiles x 8 + 1 abort word).
+struct BlockScanLayout {
+  size_t link_off, flags_off, flags_bytes, total;
+  int64_t num_tiles;
+};
+
+bool block_scan_layout(int64_t filters, int64_t k, int64_t batch, int64_t time,
+                       BlockScanLayout &l) {
+  if (filters <= 0 || k <= 0 || batch <= 0 || time <= 0 || time % 128 != 0) return false;
+  if (fbt_dims_ok(filters, batch, time) != RQF_OK || k > 0x7fffffffLL) return false;
+  if (batch * time >= (int64_t(1) << 30)) return false;
+  const ProjGeometry g = proj_geometry(filters, k);
+  auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+  l.num_tiles = (g.rows_pad / proj::kPairM) * (batch * time / 128);
+  l.link_off = up((size_t)(2 * g.rows_pad * g.k_pad) * sizeof(float));
+  l.flags_off = l.link_off + up((size_t)l.num_tiles * 2 * 64 * sizeof(float4));
+  l.flags_bytes = (size_t)(l.num_tiles * 8 + 1) * sizeof(unsigned);
+  l.total = l.flags_off + up(l.flags_bytes);
+  return true;
 }
 
 }  // namespace
@@ -1275,6 +1318,52 @@ int rqf_projection_real(const float *w, const float *x, const float *acc, float 
                         int64_t k, int64_t n, int conj_transpose, void *workspace,
                         rqf_stream_t stream) {
   return projection_impl(w, x, acc, out, m, k, n, conj_transpose, workspace, stream, 1);
+}
+
+size_t rqf_projection_block_scan_workspace_bytes(int64_t filters, int64_t k, int64_t batch,
+                                                 int64_t time) {
+  BlockScanLayout l;
+  return block_scan_layout(filters, k, batch, time, l) ? l.total : 0;
+}
+
+int rqf_projection_block_scan(const float *w, const float *x, const float *c1, const float *tap0,
+                              const float *tap1, const float *skip, float *z, float *out,
+                              float *carries, void *workspace, int64_t filters, int64_t k,
+                              int64_t batch, int64_t time, int fuse_act, rqf_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (k < 0) return RQF_ERR_SHAPE;
+  int status = fbt_dims_ok(filters, batch, time);
+  if (status != RQF_OK) return status;
+  if (filters == 0 || batch == 0 || time == 0) return RQF_OK;
+  BlockScanLayout l;
+  if (!block_scan_layout(filters, k, batch, time, l)) return RQF_ERR_SHAPE;
+  if (!w || !x || !c1 || !tap0 || !tap1 || !z || !out || !carries || !workspace)
+    return RQF_ERR_ARGUMENT;
+  // out is written while other tiles still read x, z and skip
+  if (out == x || out == z || out == skip || z == x || (skip && z == skip))
+    return RQF_ERR_ARGUMENT;
+  if (!aligned(x, 16) || !aligned(z, 16) || !aligned(out, 16) || !aligned(carries, 16) ||
+      !aligned(workspace, 16) || (skip && !aligned(skip, 16)) || !aligned(c1, 8) ||
+      !aligned(tap0, 8) || !aligned(tap1, 8))
+    return RQF_ERR_ALIGN;
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  unsigned *flags = reinterpret_cast<unsigned *>(ws + l.flags_off);
+  if (cudaMemsetAsync(flags, 0, l.flags_bytes, st) != cudaSuccess) return RQF_ERR_LAUNCH;
+  proj::ScanParams sp{};
+  sp.c1 = reinterpret_cast<const float2 *>(c1);
+  sp.tap0 = reinterpret_cast<const float2 *>(tap0);
+  sp.tap1 = reinterpret_cast<const float2 *>(tap1);
+  sp.skip = reinterpret_cast<const float2 *>(skip);
+  sp.act = reinterpret_cast<float2 *>(out);
+  sp.carries = reinterpret_cast<float2 *>(carries);
+  sp.link = reinterpret_cast<float4 *>(ws + l.link_off);
+  sp.flags = flags;
+  sp.T = time;
+  sp.batch = (int)batch;
+  sp.tiles_per_row = (int)(time / 128);
+  sp.fbt_ntiles = (int)rqf_fbt_num_tiles(time);
+  sp.fuse_act = fuse_act ? 1 : 0;
+  return projection_impl(w, x, nullptr, z, filters, k, batch * time, 0, workspace, stream, 0, &sp);
 }
 
 size_t rqf_projection_real_out_workspace_bytes(int64_t m, int64_t k) {
@@ -1335,8 +1424,9 @@ int rqf_projection_real_out(const float *w, const float *x, float *out, int64_t 
   p.a_rows_pad = (int)rows_pad;
   p.real_x = 0;
   const long long grid = 2 * (p.num_tiles < pairs ? p.num_tiles : pairs);
+  p.scan = 0;
   proj::proj_kernel<true><<<(unsigned)grid, proj::kThreads, proj::ProjLayout<true>::kSmemBytes,
-                            st>>>(tmA, tmX, p);
+                            st>>>(tmA, tmX, p, proj::ScanParams{});
   return launch_status();
 }
 

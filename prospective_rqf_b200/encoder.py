@@ -40,6 +40,18 @@ SPLIT_RELU_GAIN = 0.5     # utils/init.py RQF_ACTIVATION_GAINS["split_relu"]
 # "tc": the block projections run on the split-TF32 tcgen05 GEMM
 # (ops.projection); "torch": torch.matmul (cuBLAS fp32), as the reference does.
 PROJECTION = os.environ.get("RQF_B200_PROJECTION", "tc")
+# "1": a block whose projection runs on the tcgen05 GEMM and whose T is a
+# multiple of 128 runs its scan in that GEMM's epilogue (ops.projection_block_scan);
+# "0": the projection, then the separate (F,B,T) scan kernel.
+BLOCK_SCAN = os.environ.get("RQF_B200_BLOCK_SCAN", "1") != "0"
+
+
+def _block_forward(W, h, C1, tap0, tap1, fuse_act, skip):
+    """z = W h, then the (F,B,T) scan (act(y) + skip when skip is given):
+    (out, saved) as ops._fbt_forward returns them."""
+    if PROJECTION == "tc" and BLOCK_SCAN and ops.block_scan_eligible(W, h):
+        return ops.projection_block_scan(W, h, C1, tap0, tap1, fuse_act, skip)
+    return ops._fbt_forward(C1, tap0, tap1, _project(W, h), fuse_act, skip)
 
 
 def _weight_grad(gz, h):
@@ -152,8 +164,7 @@ class _TBPTTLayer(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, h, W, C1, tap0, tap1, fuse_act):
-        z = _project(W, h)
-        y, saved = ops._fbt_forward(C1, tap0, tap1, z, bool(fuse_act))
+        y, saved = _block_forward(W, h, C1, tap0, tap1, bool(fuse_act), None)
         ctx.save_for_backward(h, W, *saved)
         ctx.fuse_act = bool(fuse_act)
         return y
@@ -182,8 +193,7 @@ class _PureBlock(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, h, W, C1, tap0, tap1, fuse_act, skip):
-        z = _project(W, h)
-        out, saved = ops._fbt_forward(C1, tap0, tap1, z, bool(fuse_act), h if skip else None)
+        out, saved = _block_forward(W, h, C1, tap0, tap1, bool(fuse_act), h if skip else None)
         ctx.save_for_backward(h, W, *saved)
         ctx.fuse_act, ctx.skip = bool(fuse_act), bool(skip)
         return out

@@ -266,6 +266,52 @@ def _fbt_forward(C1, tap0, tap1, x_fbt, fuse_act: bool, skip=None):
     return out, (c1, t0, t1, z, carries)
 
 
+def block_scan_eligible(W: torch.Tensor, h: torch.Tensor) -> bool:
+    """Whether projection_block_scan takes this block: complex W (F, K) on
+    the GPU against h (K, B, T) with T a multiple of 128 (the GEMM's sample
+    tile) and B*T below 2^30."""
+    return (W.is_cuda and h.is_cuda and W.dim() == 2 and h.dim() == 3
+            and int(W.shape[1]) == int(h.shape[0]) and int(h.shape[0]) > 0
+            and int(h.shape[2]) % 128 == 0 and int(h.shape[1]) * int(h.shape[2]) < (1 << 30))
+
+
+def projection_block_scan(W, h, C1, tap0, tap1, fuse_act: bool, skip=None):
+    """One Pure RQF block forward in one launch (rqf_projection_block_scan):
+    z = W h (pure.py:223) on the split-TF32 tensor-core GEMM, whose epilogue
+    runs the (F,B,T) two-tap scan of z along time, the split-ReLU and the
+    skip add (pure.py:529-535) tile by tile.  Returns (out, saved) exactly as
+    _fbt_forward(C1, tap0, tap1, W h, fuse_act, skip) does, so _fbt_backward
+    and _tbptt_backward take ``saved`` unchanged.  Requires
+    block_scan_eligible(W, h)."""
+    dev = _require_cuda(W, h, C1, tap0, tap1, skip)
+    w = _c64(W)
+    x = _c64(h)
+    if not block_scan_eligible(w, x):
+        raise ValueError(f"projection_block_scan: W {tuple(w.shape)} and h {tuple(x.shape)} "
+                         "need h (K, B, T) with T a multiple of 128")
+    F, K = int(w.shape[0]), int(w.shape[1])
+    _, B, T = (int(d) for d in x.shape)
+    c1, t0, t1 = _coef(C1, F, "C1"), _coef(tap0, F, "tap0"), _coef(tap1, F, "tap1")
+    sk = None
+    if skip is not None:
+        sk = _c64(skip)
+        if tuple(sk.shape) != (F, B, T):
+            raise ValueError(f"skip must have shape {(F, B, T)}, got {tuple(sk.shape)}")
+    lib = _abi.load()
+    z = torch.empty((F, B, T), dtype=torch.complex64, device=dev)
+    out = torch.empty((F, B, T), dtype=torch.complex64, device=dev)
+    carries = _carries(lib.rqf_fbt_carry_count(F, B, T), dev)
+    ws = _scratch(lib.rqf_projection_block_scan_workspace_bytes(F, K, B, T), dev)
+    with _timing.launch("rqf_projection_block_scan", F * B * T, _nbytes(x, z, sk, out),
+                        8 * F * K * B * T):
+        _abi.check(lib.rqf_projection_block_scan(
+            _abi.ptr(w), _abi.ptr(x), _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1), _abi.ptr(sk),
+            _abi.ptr(z), _abi.ptr(out), _abi.ptr(carries), _abi.ptr(ws), F, K, B, T,
+            int(bool(fuse_act)), _abi.stream_of(x)), "rqf_projection_block_scan")
+    _done(dev)
+    return out, (c1, t0, t1, z, carries)
+
+
 def _fbt_backward(saved, grad_output, fuse_act: bool):
     c1, t0, t1, z, carries = saved
     F, B, T = z.shape

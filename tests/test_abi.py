@@ -115,6 +115,16 @@ def test_host_side_validation_needs_no_gpu(lib):
                                         2, 3, 4, 0, None) == 5
     assert lib.rqf_tbptt1_two_tap_backward(7, None, None, None, None, None, None, None, None,
                                            None, None, None, None, 1, 1, 1, 0, 0, None) == 5
+    # fused block forward: T a multiple of 128, k > 0; empty problems are no-ops
+    nul = [None] * 10
+    assert lib.rqf_projection_block_scan(*nul, 64, 64, 2, 256, 1, None) == 5
+    assert lib.rqf_projection_block_scan(*nul, 64, 64, 2, 200, 1, None) == 1
+    assert lib.rqf_projection_block_scan(*nul, 64, 0, 2, 256, 1, None) == 1
+    assert lib.rqf_projection_block_scan(*nul, 64, -1, 2, 256, 1, None) == 1
+    assert lib.rqf_projection_block_scan(*nul, 0, 64, 2, 256, 1, None) == 0
+    assert lib.rqf_projection_block_scan_workspace_bytes(64, 64, 2, 200) == 0
+    assert lib.rqf_projection_block_scan_workspace_bytes(64, 64, 2, 256) > \
+        lib.rqf_projection_workspace_bytes(64, 64)
     # misaligned pointers -> RQF_ERR_ALIGN
     buf = (ctypes.c_char * 64)()
     base = ctypes.addressof(buf)
