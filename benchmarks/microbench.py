@@ -23,6 +23,9 @@ Ops:
              its weight cotangent gz h^H (split-TF32 tcgen05 GEMMs, W of F x F
              complex); reports TFLOP/s (8 F^2 B T real flops per GEMM)
   projection_torch  the same two GEMMs through torch.matmul (cuBLAS fp32)
+  block_scan the Pure RQF block forward fused into its projection
+             (rqf_projection_block_scan, skip = h, split-ReLU), beside the
+             unfused pair it replaces: rqf_projection, then rqf_fbt_block_forward
   mosc       the fused multi-oscillator scan (B,T,F) -> (B,T,F), --groups
              oscillators per filter
 
@@ -130,6 +133,16 @@ def make_case(op: str, F: int, B: int, T: int, groups: int = 8, truncated: bool 
                     gz.reshape(F, B * T) @ h.reshape(F, B * T).mH
         return run
 
+    if op == "block_scan":  # the fused block forward beside its two unfused launches
+        W = (crandn(F, F) / math.sqrt(2 * F))
+        h = crandn(F, B, T)
+
+        def run():
+            ops.projection_block_scan(W, h, c1, t0, t1, True, h)
+            z = ops.projection(W, h)
+            ops._fbt_forward(c1, t0, t1, z, True, h)
+        return run
+
     if op == "fbt_skip":
         z, h, gy = crandn(F, B, T), crandn(F, B, T), crandn(F, B, T)
 
@@ -175,7 +188,8 @@ def make_case(op: str, F: int, B: int, T: int, groups: int = 8, truncated: bool 
 
 
 OPS = ("fbt", "fbt_raw", "fbt_skip", "tbptt_fbt", "tbptt_btf", "btf", "btf_real", "btf_pro",
-       "selective", "selective_bf16", "projection", "projection_torch", "projection_real", "mosc")
+       "selective", "selective_bf16", "projection", "projection_torch", "projection_real", "mosc",
+       "block_scan")
 
 
 def measure(op, F, B, T, iters=10, warmup=3, groups=8, truncated=False) -> dict:
@@ -199,7 +213,8 @@ def measure(op, F, B, T, iters=10, warmup=3, groups=8, truncated=False) -> dict:
         kernels[name] = {"launches": v["launches"], "mean_ms": round(v["mean_ms"], 4),
                          "alg_bytes_per_launch": int(per), "gbs": round(gbs, 1),
                          "frac": round(gbs / peak, 4)}
-        if op.startswith("projection") and v["mean_ms"]:
+        if (op.startswith("projection") or op == "block_scan") and v["mean_ms"] \
+                and name != "rqf_fbt_block_forward":
             flops = 8.0 * F * F * B * T
             kernels[name]["tflops"] = round(flops / (v["mean_ms"] * 1e-3) / 1e12, 1)
     return {"op": op, "F": F, "B": B, "T": T, "iters": iters, "warmup": warmup,

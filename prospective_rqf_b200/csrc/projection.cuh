@@ -88,15 +88,26 @@ constexpr int kStagingBytes = 4 * 4096;
 // planes of B; A = [Re op(W) | -Im op(W)] per k-block of 8 complex k.
 constexpr int kRawXBytes = 8 * kBNh * 2 * 4;     // 8 KB
 constexpr int kRawXOff = kStageBytes;            // after the four operand tiles
-template <bool kRealOut>
+// Scan mode: each epilogue warp stages z, act (16 rows x 128 B each, in the
+// 128-byte swizzle of the TMA stores, so 1024-byte aligned: the staging
+// comes right after the stages) and the tile's entry slots.
+constexpr int kScanWarpStaging = 3 * 2048;
+template <bool kRealOut, bool kScan = false>
 struct ProjLayout {
   static constexpr int kStages = kRealOut ? 5 : 6;
   static constexpr int kStageBytes = kRealOut ? ::rqf::proj::kStageBytes + kRawXBytes
                                               : ::rqf::proj::kStageBytes;  // 40 / 32 KB
+  static constexpr int kWarpStaging = kScan ? kScanWarpStaging : kStagingBytes / 4;
+  // staging then barriers in scan mode; barriers then staging otherwise
+  static constexpr int kStagingOff =
+      kScan ? kStages * kStageBytes : kStages * kStageBytes + kBarBytes;
+  static constexpr int kBarOff = kScan ? kStages * kStageBytes + 4 * kWarpStaging
+                                       : kStages * kStageBytes;
   static constexpr int kSmemBytes =
-      kStages * kStageBytes + kBarBytes + kStagingBytes + 1024;  // + alignment slack
+      kStages * kStageBytes + kBarBytes + 4 * kWarpStaging + 1024;  // + alignment slack
 };
 constexpr int kSmemBytes = ProjLayout<false>::kSmemBytes;
+constexpr int kScanSmemBytes = ProjLayout<false, true>::kSmemBytes;
 
 constexpr int kErrPipelineTimeout = 7;            // RQF_ERR_PIPELINE_TIMEOUT
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
@@ -131,6 +142,7 @@ struct Params {
 // recurrence operations, 8 samples sequentially from their entry), so the
 // (F,B,T) backward replays the same states from the entries saved here.
 struct ScanParams {
+  CUtensorMap tmZ, tmAct;          // out (z) and act as (M rows, 2N floats), 16 x 32 boxes, 128-B swizzle
   const float2 *c1, *tap0, *tap1;  // (M,)
   const float2 *skip;              // (M, N) or null
   float2 *act;                     // (M, N) output
@@ -221,6 +233,31 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
+}
+// TMA tensor store of a shared-memory box, tracked by this thread's bulk
+// groups: commit after issuing, wait (.read: until the source may be
+// overwritten; plain: until the writes are complete).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int x,
+                                             int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+// generic-proxy shared-memory writes -> visible to the async proxy (TMA)
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -493,7 +530,8 @@ __device__ __forceinline__ bool scan_link_wait(const unsigned *flag, unsigned *a
 // batch row because T is a multiple of 128.  Eight chunks of 16 samples,
 // the even lane's 8 then the odd lane's 8; per chunk:
 //   z        combined from the TMEM products as in the plain epilogue,
-//            staged and stored to p.out (the (F,B,T) backward reads it);
+//            staged (128-byte swizzle) and written by a TMA tensor store to
+//            p.out (the (F,B,T) backward reads it);
 //   drive    b[k] = tap0 z[k] + tap1 z[k-1] (fbt_drive, as every (F,B,T)
 //            kernel computes it);
 //   entry    the even lane enters with the row's running state E and folds
@@ -501,12 +539,18 @@ __device__ __forceinline__ bool scan_link_wait(const unsigned *flag, unsigned *a
 //   outputs  both lanes run y = c1 y + b[k] from their own entry (the
 //            operations that the (F,B,T) backward replays from the saved
 //            entry, so its split-ReLU mask is this one), act = split-ReLU(y)
-//            or y, plus skip, staged and stored to sp.act.
-// Every lane's entry is the saved context slot of its 8 samples; the 16
-// slots of each row are staged and written as one 128-byte piece per tile.
-// The state entering the tile, {y, z} at the sample before it, is the link
-// record that the tile before it along time (tile - chains) published; at
-// the end of the tile this one publishes its own.  False on an abort.
+//            or y, plus skip, staged and written by a TMA tensor store to
+//            sp.act.
+// The skip lines of the tile are prefetched into L2 when it starts and each
+// lane loads its own 8 samples one chunk ahead, so no load waits on HBM.
+// The two staging buffers are reused once the bulk store that read them has
+// finished reading (bulk groups: z then act per chunk, waited with one group
+// left outstanding).  Every lane's entry is the saved context slot of its 8
+// samples; the 16 slots of each row are staged and written as one 128-byte
+// piece per tile.  The state entering the tile, {y, z} at the sample before
+// it, is the link record that the tile before it along time (tile - chains)
+// published; at the end of the tile this one publishes its own.  False on an
+// abort.
 __device__ __forceinline__ bool scan_epilogue(uint32_t tbase, float4 *stage, const Params &p,
                                               const ScanParams &sp, long long tile, int mp,
                                               int nt, int rank, int quarter, int lane,
@@ -516,6 +560,7 @@ __device__ __forceinline__ bool scan_epilogue(uint32_t tbase, float4 *stage, con
   const long long jw0 = ((long long)mp * kPairM + (long long)rank * kBM + quarter * 32) >> 1;
   const long long jrow = jw0 + r_own;
   const bool row_ok = jrow < p.M;
+  const bool warp_ok = jw0 < p.M;  // some row of the warp's 16 exists
   const int bidx = nt / sp.tiles_per_row;
   const int pos = nt - bidx * sp.tiles_per_row;
   const long long tfirst = (long long)pos * (kBN / 2);  // first sample in the batch row
@@ -524,6 +569,19 @@ __device__ __forceinline__ bool scan_epilogue(uint32_t tbase, float4 *stage, con
   const float2 tap0 = row_ok ? __ldg(sp.tap0 + jrow) : cz();
   const float2 tap1 = row_ok ? __ldg(sp.tap1 + jrow) : cz();
   unsigned *abort_word = sp.flags + p.num_tiles * 8;
+  const bool has_skip = sp.skip != nullptr;
+  const bool lane_skip = has_skip && row_ok;
+  // this lane's 8 skip samples of chunk c: the 64 bytes at skrow + 8 c
+  const float4 *skrow =
+      lane_skip ? reinterpret_cast<const float4 *>(sp.skip + jrow * p.N + n0 + (odd ? 8 : 0))
+                : nullptr;
+  if (has_skip && lane < 16 && jw0 + lane < p.M)  // the tile's 1 KB of each row, into L2
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], 1024;" ::"l"(sp.skip + (jw0 + lane) * p.N + n0)
+                 : "memory");
+  float4 skn[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    skn[i] = lane_skip ? __ldg(skrow + i) : make_float4(0.f, 0.f, 0.f, 0.f);
 
   float2 E = cz(), zl = cz();  // y and z at the sample before the chunk
   if (pos > 0) {
@@ -534,22 +592,19 @@ __device__ __forceinline__ bool scan_epilogue(uint32_t tbase, float4 *stage, con
     E = make_float2(l.x, l.y);
     zl = make_float2(l.z, l.w);
   }
-  float2 *ent = reinterpret_cast<float2 *>(stage + 128);  // [16 rows][16 slots], swizzled
+  float4 *zst = stage;                                    // z staging, 16 rows x 128 B
+  float4 *ast = stage + 128;                              // act staging
+  float2 *ent = reinterpret_cast<float2 *>(stage + 256);  // [16 rows][16 slots], swizzled
 
 #pragma unroll 1
   for (int c = 0; c < kBN / 32; ++c) {
     const long long nbase = n0 + c * 16;
-    // this lane's skip pieces (the store layout: row e >> 3, piece e & 7),
-    // loaded first so that their latency hides behind the TMEM load
-    float4 skp[4];
+    float4 sk[4];
 #pragma unroll
-    for (int it = 0; it < 4; ++it) {
-      const int e = it * 32 + lane;
-      const long long jj = jw0 + (e >> 3);
-      skp[it] = (sp.skip != nullptr && jj < p.M)
-                    ? __ldg(reinterpret_cast<const float4 *>(sp.skip + jj * p.N + nbase +
-                                                             2 * (e & 7)))
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = 0; i < 4; ++i) sk[i] = skn[i];
+    if (lane_skip && c + 1 < kBN / 32) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) skn[i] = __ldg(skrow + 8 * (c + 1) + i);
     }
     float v[32];
     tc_ld_32x32b_x32(tbase + (uint32_t)(c * 32), v);
@@ -565,20 +620,18 @@ __device__ __forceinline__ bool scan_epilogue(uint32_t tbase, float4 *stage, con
       const float pi_im = odd ? v[16 + 2 * t + 1] : r[2 * t + 1];
       z[t] = make_float2(pr_re - pi_im, pr_im + pi_re);
     }
+    if (lane == 0) bulk_wait_read<1>();  // the previous z store has read its staging
+    __syncwarp();
 #pragma unroll
     for (int q = 0; q < 4; ++q)
-      stage[r_own * 8 + (((odd ? 4 : 0) + q) ^ (r_own & 7))] =
+      zst[r_own * 8 + (((odd ? 4 : 0) + q) ^ (r_own & 7))] =
           make_float4(z[2 * q].x, z[2 * q].y, z[2 * q + 1].x, z[2 * q + 1].y);
+    fence_proxy_async_smem();
     __syncwarp();
-#pragma unroll
-    for (int it = 0; it < 4; ++it) {
-      const int e = it * 32 + lane;
-      const int rr = e >> 3, k = e & 7;
-      const long long jj = jw0 + rr;
-      if (jj < p.M)
-        *reinterpret_cast<float4 *>(p.out + jj * p.N + nbase + 2 * k) = stage[rr * 8 + (k ^ (rr & 7))];
+    if (lane == 0) {
+      if (warp_ok) tma_store_2d(&sp.tmZ, zst, (int)(2 * nbase), (int)jw0);
+      bulk_commit();
     }
-    __syncwarp();
 
     // drives; the odd lane's z before its first sample is the even lane's last
     const float2 zx = shfl_xor2(z[7], 1);
@@ -601,27 +654,24 @@ __device__ __forceinline__ bool scan_epilogue(uint32_t tbase, float4 *stage, con
     const float2 ex = shfl_xor2(e, 1);
     E = odd ? e : ex;  // both lanes: y at the chunk's last sample
 
+    if (lane == 0) bulk_wait_read<1>();  // the previous act store has read its staging
+    __syncwarp();
 #pragma unroll
     for (int q = 0; q < 4; ++q)
-      stage[r_own * 8 + (((odd ? 4 : 0) + q) ^ (r_own & 7))] =
-          make_float4(o[2 * q].x, o[2 * q].y, o[2 * q + 1].x, o[2 * q + 1].y);
+      ast[r_own * 8 + (((odd ? 4 : 0) + q) ^ (r_own & 7))] =
+          make_float4(o[2 * q].x + sk[q].x, o[2 * q].y + sk[q].y, o[2 * q + 1].x + sk[q].z,
+                      o[2 * q + 1].y + sk[q].w);
+    fence_proxy_async_smem();
     __syncwarp();
-#pragma unroll
-    for (int it = 0; it < 4; ++it) {
-      const int e4 = it * 32 + lane;
-      const int rr = e4 >> 3, k = e4 & 7;
-      const long long jj = jw0 + rr;
-      if (jj < p.M) {
-        float4 a = stage[rr * 8 + (k ^ (rr & 7))];
-        a = make_float4(a.x + skp[it].x, a.y + skp[it].y, a.z + skp[it].z, a.w + skp[it].w);
-        *reinterpret_cast<float4 *>(sp.act + jj * p.N + nbase + 2 * k) = a;
-      }
+    if (lane == 0) {
+      if (warp_ok) tma_store_2d(&sp.tmAct, ast, (int)(2 * nbase), (int)jw0);
+      bulk_commit();
     }
-    __syncwarp();
   }
 
   // saved entries: 16 consecutive slots of each row of the (F,B,T) context
   {
+    __syncwarp();
     const long long jt = tfirst / kFbtTile;
     const int s0 = (int)(tfirst - jt * kFbtTile) / kFbtK;
     const float4 *ent4 = reinterpret_cast<const float4 *>(ent);
@@ -667,15 +717,15 @@ __device__ __forceinline__ bool scan_epilogue(uint32_t tbase, float4 *stage, con
 template <bool kRealOut, bool kScan = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmX,
-            const Params p, const ScanParams sp) {
+            const Params p, const __grid_constant__ ScanParams sp) {
   static_assert(!(kRealOut && kScan), "the scan epilogue runs on the complex output");
-  using L = ProjLayout<kRealOut>;
+  using L = ProjLayout<kRealOut, kScan>;
   constexpr int kStages = L::kStages;
   constexpr int kStageBytes = L::kStageBytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::kBarOff);
   uint64_t *full = bars;                 // this CTA's TMA landed  (1 arrival + tx)
   uint64_t *ready = bars + kStages;      // X' split done, both CTAs (leader's; 8 warps)
   uint64_t *empty = bars + 2 * kStages;  // MMAs done with stage  (leader's commit)
@@ -824,8 +874,8 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     const bool odd = (row & 1) != 0;
     const uint32_t acce0 = cluster_addr(&acce[0], 0);
     const uint32_t acce1 = cluster_addr(&acce[1], 0);
-    float4 *stage = reinterpret_cast<float4 *>(smem + kStages * kStageBytes + kBarBytes +
-                                               quarter * (kStagingBytes / 4));
+    float4 *stage =
+        reinterpret_cast<float4 *>(smem + L::kStagingOff + quarter * L::kWarpStaging);
     int acc = 0;
     uint32_t acc_phase = 0;
     if constexpr (kScan) {  // every thread's entry is saved (the row kernels' marker)
@@ -960,6 +1010,10 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         acc = 0;
         acc_phase ^= 1u;
       }
+    }
+    if constexpr (kScan) {  // the TMA stores of this warp complete before the CTA exits
+      if (lane == 0) bulk_wait<0>();
+      __syncwarp();
     }
   } else {
     // ---------------------------------------------------------- transform

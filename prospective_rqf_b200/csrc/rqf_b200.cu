@@ -1197,7 +1197,7 @@ namespace {
 
 int proj_scan_pairs_per_device() {
   return pair_capacity<4>(reinterpret_cast<const void *>(proj::proj_kernel<false, true>),
-                          proj::kThreads, proj::kSmemBytes);
+                          proj::kThreads, proj::kScanSmemBytes);
 }
 
 // x complex (k x n) when real_x = 0, real (k x n) when real_x = 1.  With
@@ -1272,7 +1272,7 @@ int projection_impl(const float *w, const float *x, const float *acc, float *out
     // persistent grid is the device's pair capacity at most.
     proj::ScanParams sp = *scan;
     sp.chains = p.m_pairs * sp.batch;
-    proj::proj_kernel<false, true><<<(unsigned)grid, proj::kThreads, proj::kSmemBytes, st>>>(
+    proj::proj_kernel<false, true><<<(unsigned)grid, proj::kThreads, proj::kScanSmemBytes, st>>>(
         tmA, tmX, p, sp);
   } else {
     proj::proj_kernel<false><<<(unsigned)grid, proj::kThreads, proj::kSmemBytes, st>>>(
@@ -1350,6 +1350,14 @@ int rqf_projection_block_scan(const float *w, const float *x, const float *c1, c
   unsigned *flags = reinterpret_cast<unsigned *>(ws + l.flags_off);
   if (cudaMemsetAsync(flags, 0, l.flags_bytes, st) != cudaSuccess) return RQF_ERR_LAUNCH;
   proj::ScanParams sp{};
+  // z and out as (filters rows, 2 batch time floats): the epilogue's TMA
+  // stores write 16 rows x 16 complex samples per box
+  const uint64_t nf = 2 * (uint64_t)batch * (uint64_t)time;
+  if (!encode_map_2d(&sp.tmZ, z, nf, (uint64_t)filters, nf * sizeof(float), 32, 16,
+                     CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map_2d(&sp.tmAct, out, nf, (uint64_t)filters, nf * sizeof(float), 32, 16,
+                     CU_TENSOR_MAP_SWIZZLE_128B))
+    return RQF_ERR_LAUNCH;
   sp.c1 = reinterpret_cast<const float2 *>(c1);
   sp.tap0 = reinterpret_cast<const float2 *>(tap0);
   sp.tap1 = reinterpret_cast<const float2 *>(tap1);

@@ -40,16 +40,19 @@ SPLIT_RELU_GAIN = 0.5     # utils/init.py RQF_ACTIVATION_GAINS["split_relu"]
 # "tc": the block projections run on the split-TF32 tcgen05 GEMM
 # (ops.projection); "torch": torch.matmul (cuBLAS fp32), as the reference does.
 PROJECTION = os.environ.get("RQF_B200_PROJECTION", "tc")
-# "1": a block whose projection runs on the tcgen05 GEMM and whose T is a
-# multiple of 128 runs its scan in that GEMM's epilogue (ops.projection_block_scan);
-# "0": the projection, then the separate (F,B,T) scan kernel.
-BLOCK_SCAN = os.environ.get("RQF_B200_BLOCK_SCAN", "1") != "0"
+# "auto": a block whose projection runs on the tcgen05 GEMM runs its scan in
+# that GEMM's epilogue (ops.projection_block_scan) where that is expected to be
+# faster (ops.block_scan_preferred); "1": wherever it applies (T a multiple of
+# 128); "0": never — the projection, then the separate (F,B,T) scan kernel.
+BLOCK_SCAN = os.environ.get("RQF_B200_BLOCK_SCAN", "auto")
 
 
 def _block_forward(W, h, C1, tap0, tap1, fuse_act, skip):
     """z = W h, then the (F,B,T) scan (act(y) + skip when skip is given):
     (out, saved) as ops._fbt_forward returns them."""
-    if PROJECTION == "tc" and BLOCK_SCAN and ops.block_scan_eligible(W, h):
+    mode = str(BLOCK_SCAN)
+    if PROJECTION == "tc" and mode not in ("0", "False") and (
+            ops.block_scan_preferred(W, h) if mode == "auto" else ops.block_scan_eligible(W, h)):
         return ops.projection_block_scan(W, h, C1, tap0, tap1, fuse_act, skip)
     return ops._fbt_forward(C1, tap0, tap1, _project(W, h), fuse_act, skip)
 

@@ -203,7 +203,7 @@ def test_encoder_block_scan_matches_unfused():
                                      skip_connection=True, final_activation=False).cuda()
     x = 0.5 * torch.randn(4, 4096, 1, device="cuda")
     res = []
-    for fused in (True, False):
+    for fused in ("1", "0"):
         encoder.BLOCK_SCAN = fused
         try:
             enc.zero_grad()
@@ -212,7 +212,7 @@ def test_encoder_block_scan_matches_unfused():
             res.append((h.detach().clone(),
                         {n: p.grad.detach().clone() for n, p in enc.named_parameters()}))
         finally:
-            encoder.BLOCK_SCAN = True
+            encoder.BLOCK_SCAN = "auto"
     (h1, g1), (h2, g2) = res
     assert_close(_host(h1), _host(h2), 1e-5, "features")
     for n in g1:
