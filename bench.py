@@ -47,6 +47,8 @@ KERNELS_PER_CALL = {  # kernels each C-ABI call launches (the backward adds the 
     "rqf_projection": 2,
     "rqf_projection_weight_grad": 2,
     "rqf_fbt_block_forward": 1,
+    "rqf_projection_block_scan": 2,
+    "rqf_projection_block_scan_backward": 3,
     "rqf_fbt_prospective_backward": 2,
     "rqf_tbptt1_two_tap_backward": 2,
 }

@@ -26,6 +26,10 @@ Ops:
   block_scan the Pure RQF block forward fused into its projection
              (rqf_projection_block_scan, skip = h, split-ReLU), beside the
              unfused pair it replaces: rqf_projection, then rqf_fbt_block_forward
+  block_scan_bwd  the backward of two stacked blocks in one launch
+             (rqf_projection_block_scan_backward: W^H gz + acc with the lower
+             block's scan VJP in the epilogue), beside the unfused pair:
+             rqf_projection, then rqf_fbt_prospective_backward
   mosc       the fused multi-oscillator scan (B,T,F) -> (B,T,F), --groups
              oscillators per filter
 
@@ -143,6 +147,19 @@ def make_case(op: str, F: int, B: int, T: int, groups: int = 8, truncated: bool 
             ops._fbt_forward(c1, t0, t1, z, True, h)
         return run
 
+    if op == "block_scan_bwd":  # the fused backward pair beside its two unfused launches
+        W0 = (crandn(F, F) / math.sqrt(2 * F))
+        h = crandn(F, B, T)
+        _, saved = ops.projection_block_scan(W0, h, c1, t0, t1, True, h)
+        W = (crandn(F, F) / math.sqrt(2 * F))
+        gz_above, acc = crandn(F, B, T), crandn(F, B, T)
+
+        def run():
+            ops.projection_block_scan_backward(W, gz_above, acc, saved, True)
+            g = ops.projection(W, gz_above, conj_transpose=True, acc=acc)
+            ops._fbt_backward(saved, g, True)
+        return run
+
     if op == "fbt_skip":
         z, h, gy = crandn(F, B, T), crandn(F, B, T), crandn(F, B, T)
 
@@ -189,7 +206,7 @@ def make_case(op: str, F: int, B: int, T: int, groups: int = 8, truncated: bool 
 
 OPS = ("fbt", "fbt_raw", "fbt_skip", "tbptt_fbt", "tbptt_btf", "btf", "btf_real", "btf_pro",
        "selective", "selective_bf16", "projection", "projection_torch", "projection_real", "mosc",
-       "block_scan")
+       "block_scan", "block_scan_bwd")
 
 
 def measure(op, F, B, T, iters=10, warmup=3, groups=8, truncated=False) -> dict:
@@ -213,8 +230,8 @@ def measure(op, F, B, T, iters=10, warmup=3, groups=8, truncated=False) -> dict:
         kernels[name] = {"launches": v["launches"], "mean_ms": round(v["mean_ms"], 4),
                          "alg_bytes_per_launch": int(per), "gbs": round(gbs, 1),
                          "frac": round(gbs / peak, 4)}
-        if (op.startswith("projection") or op == "block_scan") and v["mean_ms"] \
-                and name != "rqf_fbt_block_forward":
+        if (op.startswith("projection") or op.startswith("block_scan")) and v["mean_ms"] \
+                and name not in ("rqf_fbt_block_forward", "rqf_fbt_prospective_backward"):
             flops = 8.0 * F * F * B * T
             kernels[name]["tflops"] = round(flops / (v["mean_ms"] * 1e-3) / 1e12, 1)
     return {"op": op, "F": F, "B": B, "T": T, "iters": iters, "warmup": warmup,

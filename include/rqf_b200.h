@@ -373,7 +373,8 @@ int rqf_fbt_prospective_backward_noalloc(const float *c1, const float *tap0, con
 size_t rqf_projection_workspace_bytes(int64_t m, int64_t k);
 /* Diagnostic: where the first expired wait of the projection pipeline gave
  * up since the last clear (0 none, 1 producer, 2 transform, 3/4 MMA issuer,
- * 5 epilogue, 6 shutdown drain); -1 on a CUDA error.  Synchronous. */
+ * 5 epilogue, 6 shutdown drain, 7 block-scan link record, 8 block-scan
+ * backward ring load); -1 on a CUDA error.  Synchronous. */
 int rqf_projection_timeout_site(int clear);
 int rqf_projection(const float *w, const float *x, const float *acc, float *out, int64_t m,
                    int64_t k, int64_t n, int conj_transpose, void *workspace,
@@ -406,6 +407,36 @@ int rqf_projection_block_scan(const float *w, const float *x, const float *c1, c
                               const float *tap1, const float *skip, float *z, float *out,
                               float *carries, void *workspace, int64_t filters, int64_t k,
                               int64_t batch, int64_t time, int fuse_act, rqf_stream_t stream);
+
+/* The backward of two stacked Pure RQF blocks meeting at one launch: the
+ * input cotangent of the upper block's projection (autograd of pure.py:223)
+ * with the lower block's scan VJP (fbt_scan_kernel.py:_FBTRecompute /
+ * _FBTProspectiveScan backward, :575-689 and :245-329) run in the GEMM's
+ * epilogue, tile by tile from the end of each batch row.  Equal to
+ * rqf_projection(w, gz_above, acc, grad_out, conj_transpose = 1) followed by
+ * rqf_fbt_prospective_backward(c1, tap0, tap1, z, carries, grad_out):
+ *
+ *   grad_out = W^H gz_above + acc        the lower block's output cotangent
+ *   grad_z, grad_c1, grad_tap0, grad_tap1   the lower block's scan VJP of it
+ *
+ * W is (k x filters), the upper block's weight; gz_above (k, batch, time)
+ * its z cotangent; acc (nullable) the skip's cotangent (filters, batch,
+ * time); c1 / tap0 / tap1, z and carries the lower block's coefficients and
+ * saved context from any (F,B,T) forward of this library (each saves every
+ * 8-sample group's entry state and the marker after them; a context without
+ * the marker latches RQF_ERR_ARGUMENT in the device error word).
+ * The coefficient gradients are summed per (row, tile) in the workspace and
+ * reduced in a fixed order in double.  Requirements as for
+ * rqf_projection_block_scan; the outputs distinct from every input. */
+size_t rqf_projection_block_scan_backward_workspace_bytes(int64_t filters, int64_t k,
+                                                          int64_t batch, int64_t time);
+int rqf_projection_block_scan_backward(const float *w, const float *gz_above, const float *acc,
+                                       const float *c1, const float *tap0, const float *tap1,
+                                       const float *z, const float *carries, float *grad_out,
+                                       float *grad_z, float *grad_c1, float *grad_tap0,
+                                       float *grad_tap1, void *workspace, int64_t filters,
+                                       int64_t k, int64_t batch, int64_t time, int fuse_act,
+                                       rqf_stream_t stream);
 
 /* Weight cotangent of the same projection (autograd of pure.py:223's matmul
  * with respect to W; cuBLAS fp32 in the reference):

@@ -116,6 +116,10 @@ SIGNATURES: dict[str, tuple] = {
     "rqf_projection_block_scan_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64]),
     "rqf_projection_block_scan": (
         _int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _p]),
+    "rqf_projection_block_scan_backward_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64]),
+    "rqf_projection_block_scan_backward": (
+        _int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
+               _int, _p]),
     "rqf_projection_weight_grad_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "rqf_projection_weight_grad": (_int, [_p, _p, _p, _i64, _i64, _i64, _p, _p]),
     "rqf_lowrank_drive": (_int, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _int, _p]),

@@ -88,26 +88,39 @@ constexpr int kStagingBytes = 4 * 4096;
 // planes of B; A = [Re op(W) | -Im op(W)] per k-block of 8 complex k.
 constexpr int kRawXBytes = 8 * kBNh * 2 * 4;     // 8 KB
 constexpr int kRawXOff = kStageBytes;            // after the four operand tiles
-// Scan mode: each epilogue warp stages z, act (16 rows x 128 B each, in the
-// 128-byte swizzle of the TMA stores, so 1024-byte aligned: the staging
-// comes right after the stages) and the tile's entry slots.
+// Scan modes (kScan: 1 the block forward, 2 its backward): each epilogue
+// warp stages its two outputs (16 rows x 128 B each, in the 128-byte swizzle
+// of the TMA stores, so 1024-byte aligned: the staging comes right after the
+// stages) and the tile's entry slots.
+constexpr int kScanFwd = 1, kScanBwd = 2;
 constexpr int kScanWarpStaging = 3 * 2048;
-template <bool kRealOut, bool kScan = false>
+// The backward scan mode also gives each epilogue warp a two-slot ring of
+// TMA-loaded chunks of its rows of z and acc (per slot 16 rows x 128 B of
+// each, in the 128-byte swizzle), and runs one operand stage fewer to make
+// room for it.
+constexpr int kRingSlotBytes = 4096;
+constexpr int kRingWarpBytes = 2 * kRingSlotBytes;
+template <bool kRealOut, int kScan = 0>
 struct ProjLayout {
-  static constexpr int kStages = kRealOut ? 5 : 6;
+  static constexpr int kStages = (kRealOut || kScan == kScanBwd) ? 5 : 6;
   static constexpr int kStageBytes = kRealOut ? ::rqf::proj::kStageBytes + kRawXBytes
                                               : ::rqf::proj::kStageBytes;  // 40 / 32 KB
   static constexpr int kWarpStaging = kScan ? kScanWarpStaging : kStagingBytes / 4;
-  // staging then barriers in scan mode; barriers then staging otherwise
+  static constexpr int kRingBytes = kScan == kScanBwd ? 4 * kRingWarpBytes : 0;
+  // scan modes: staging, ring, barriers; otherwise barriers then staging
   static constexpr int kStagingOff =
       kScan ? kStages * kStageBytes : kStages * kStageBytes + kBarBytes;
-  static constexpr int kBarOff = kScan ? kStages * kStageBytes + 4 * kWarpStaging
-                                       : kStages * kStageBytes;
+  static constexpr int kRingOff = kStages * kStageBytes + 4 * kWarpStaging;
+  static constexpr int kBarOff = kScan ? kRingOff + kRingBytes : kStages * kStageBytes;
   static constexpr int kSmemBytes =
-      kStages * kStageBytes + kBarBytes + 4 * kWarpStaging + 1024;  // + alignment slack
+      kStages * kStageBytes + kBarBytes + 4 * kWarpStaging + kRingBytes + 1024;  // + alignment slack
 };
 constexpr int kSmemBytes = ProjLayout<false>::kSmemBytes;
-constexpr int kScanSmemBytes = ProjLayout<false, true>::kSmemBytes;
+constexpr int kScanSmemBytes = ProjLayout<false, kScanFwd>::kSmemBytes;
+constexpr int kScanBwdSmemBytes = ProjLayout<false, kScanBwd>::kSmemBytes;
+static_assert(ProjLayout<false, kScanBwd>::kRingOff % 1024 == 0,
+              "the ring's swizzled slots need 1024-byte alignment");
+static_assert(kScanBwdSmemBytes <= 227 * 1024, "shared memory per CTA");
 
 constexpr int kErrPipelineTimeout = 7;            // RQF_ERR_PIPELINE_TIMEOUT
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
@@ -115,7 +128,8 @@ constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
 // Where the first expired wait of the projection pipeline gave up (0 = none):
 // 1 producer/empty, 2 transform/full, 3 MMA/accumulator-drained, 4 MMA/ready,
 // 5 epilogue/accumulator-full, 6 shutdown drain, 7 scan epilogue/link record
-// of the tile before along time.  Read by rqf_projection_timeout_site().
+// of the tile before along its chain, 8 backward scan epilogue/ring load.
+// Read by rqf_projection_timeout_site().
 __device__ int g_proj_timeout_site;
 
 struct Params {
@@ -141,12 +155,26 @@ struct Params {
 // computed exactly as fbt_fwd_rows_kernel computes it (same drive and
 // recurrence operations, 8 samples sequentially from their entry), so the
 // (F,B,T) backward replays the same states from the entries saved here.
+//
+// The backward mode (kScanBwd) runs the same block's scan VJP in the epilogue
+// of its input-cotangent GEMM: out = W'^H gz' + acc is the cotangent g of
+// the block below (W' and gz' those of the block above, acc the skip's
+// cotangent), and the epilogue turns g into that block's gz (see
+// scan_bwd_epilogue).  Fields in that mode: tmZ maps out (the GEMM output),
+// tmAct maps grad_z; c1, tap0, tap1, zin, carries and fuse_act belong to the
+// scanned block (its saved context); skip and act are unused.
 struct ScanParams {
   CUtensorMap tmZ, tmAct;          // out (z) and act as (M rows, 2N floats), 16 x 32 boxes, 128-B swizzle
   const float2 *c1, *tap0, *tap1;  // (M,)
   const float2 *skip;              // (M, N) or null
   float2 *act;                     // (M, N) output
   float2 *carries;                 // fbt_slot layout of the (F,B,T) kernels
+  const float2 *zin;               // backward: the scanned block's z (M, N)
+  CUtensorMap tmZin, tmAcc;        // backward: zin and p.acc, as tmZ (TMA loads into the ring)
+  // backward: (M * batch rows, tiles_per_row, 3) per-tile sums of
+  // conj(y[t-1]) d, conj(z) d, conj(z[t-1]) d, summed by reduce_partials_kernel
+  float2 *partials;
+  int reverse;                     // backward: each chain runs from the end of its batch row
   float4 *link;                    // (num_tiles, 2 ranks, 64 rows): {y, z} at a tile's end
   // (num_tiles, 2 ranks, 4 epilogue warps) link-published flags, then one
   // abort word; all zeroed before the launch
@@ -460,13 +488,15 @@ __global__ void proj_prep_real_out_kernel(const float2 *__restrict__ W, float *_
 // (mp fastest), so the block is read from HBM once and from L2 after.
 // In scan mode the tiles run position-major over the (row block, batch)
 // chains instead: the pair tiles that run at the same time belong to different
-// chains, so a tile's predecessor along time (the tile `chains` earlier) has
-// normally finished before its epilogue needs the predecessor's end state.
+// chains, so a tile's predecessor along its chain (the tile `chains` earlier:
+// the one before it in time, or after it in the backward) has normally
+// finished before its epilogue needs the predecessor's end state.
 __device__ __forceinline__ void tile_coords(long long tile, const Params &p, int &mp, int &nt,
                                             const ScanParams *sp = nullptr) {
   if (sp != nullptr && p.scan) {
-    const long long pos = tile / sp->chains;
-    const int ch = (int)(tile - pos * sp->chains);
+    const long long step = tile / sp->chains;  // position along the chain
+    const int ch = (int)(tile - step * sp->chains);
+    const long long pos = sp->reverse ? sp->tiles_per_row - 1 - step : step;
     mp = ch % p.m_pairs;
     nt = (int)((long long)(ch / p.m_pairs) * sp->tiles_per_row + pos);
     return;
@@ -714,7 +744,285 @@ __device__ __forceinline__ bool scan_epilogue(uint32_t tbase, float4 *stage, con
   return true;
 }
 
-template <bool kRealOut, bool kScan = false>
+// Ring of one epilogue warp in the backward scan mode.  The chunks the warp
+// consumes form one sequence over its tiles: chunk c of its j-th tile is
+// k = 8 j + 7 - c, lands in slot k & 1 and completes phase (k >> 1) & 1 of
+// that slot's barrier.  Lane 0 issues chunk k + 2 once every lane has used
+// chunk k, so each load has a chunk's work to land.
+struct ScanRing {
+  uint8_t *base;      // two slots of kRingSlotBytes: z rows (2 KB), then acc rows (2 KB)
+  uint64_t *bar;      // one barrier per slot
+  long long npairs;
+  uint32_t issued;    // lane 0: chunks whose loads were issued
+  uint32_t consumed;  // chunks used
+};
+
+// Lane 0: issue the TMA loads of chunk k, the 16 rows from y x 16 samples
+// from x / 2 of z and of acc, in the layout of the staging.
+__device__ __forceinline__ void ring_issue(ScanRing &r, uint32_t k, const Params &p,
+                                           const ScanParams &sp, int x, int y) {
+  uint8_t *slot = r.base + (k & 1) * kRingSlotBytes;
+  uint64_t *bar = r.bar + (k & 1);
+  const bool acc = p.acc != nullptr;
+  mbar_expect_tx(bar, acc ? 4096u : 2048u);
+  tma_load_2d(slot, &sp.tmZin, bar, x, y);
+  if (acc) tma_load_2d(slot + 2048, &sp.tmAcc, bar, x, y);
+  r.issued = k + 1;
+}
+// Where chunk c of tile t starts: x (floats along the rows) and y (the
+// warp's first row); false past the last tile.
+__device__ __forceinline__ bool ring_coords(long long t, int c, const Params &p,
+                                            const ScanParams &sp, int rank, int quarter, int &x,
+                                            int &y) {
+  if (t >= p.num_tiles) return false;
+  int mp, nt;
+  tile_coords(t, p, mp, nt, &sp);
+  y = (int)(((long long)mp * kPairM + (long long)rank * kBM + quarter * 32) >> 1);
+  x = (int)(2 * ((long long)nt * (kBN / 2) + 16 * c));  // 128-byte aligned
+  return true;
+}
+
+// One epilogue warp's share of a backward-mode pair tile: 16 rows (lane pair
+// 2r, 2r+1 holds row jw0 + r) x the tile's 128 samples of one batch row,
+// in chunks of 16 samples from the tile's end to its start (the even lane
+// holds the chunk's first 8 samples, the odd lane the last 8).  Per chunk:
+//   g        the GEMM output combined from the TMEM products, plus acc (the
+//            skip's cotangent), staged and written by a TMA tensor store to
+//            p.out: the block's output cotangent, and the acc of the next
+//            GEMM down;
+//   replay   the drive b[k] = tap0 z[k] + tap1 z[k-1] (fbt_drive) and
+//            y = c1 y + b[k] from the lane's saved entry state: the
+//            forward's own operations, so the states and the split-ReLU mask
+//            are the forward's bit for bit;
+//   adjoint  d[t] = mask(y[t]) g[t] + conj(c1) d[t+1]: the odd lane's fold of
+//            its 8 samples from D (d after the chunk) is the even lane's
+//            entry; then both lanes run their samples, giving
+//            grad_z[t] = conj(tap0) d[t] + conj(tap1) d[t+1] (staged, TMA
+//            tensor store through tmAct) and the sums conj(y[t-1]) d[t],
+//            conj(z[t]) d[t], conj(z[t-1]) d[t] of the coefficient
+//            gradients, on paired fp32 FMAs as in fbt_bwd_rows_kernel.
+// z and acc arrive through the warp's ring (TMA loads, two chunks ahead):
+// per-lane global loads of 16 rows each would queue behind the tensor core's
+// shared-memory traffic.  The z sample before the even lane's first one is
+// the odd lane's last of the next chunk in the ring (one load per tile before
+// the tile's first sample).  D entering the tile is d at the first sample
+// of the tile after it, published by that tile (the one `chains` earlier in
+// this launch) as its link record; zero at the end of a batch row.  The tile
+// publishes d at its own first sample at the end.  Its three sums per row go
+// to sp.partials[(row, tile)].  False on an abort.
+__device__ __forceinline__ bool scan_bwd_epilogue(uint32_t tbase, float4 *stage, const Params &p,
+                                                  const ScanParams &sp, long long tile, int mp,
+                                                  int nt, int rank, int quarter, int lane,
+                                                  ScanRing &ring, volatile int *abort) {
+  const bool odd = (lane & 1) != 0;
+  const int r_own = lane >> 1;
+  const long long jw0 = ((long long)mp * kPairM + (long long)rank * kBM + quarter * 32) >> 1;
+  const long long jrow = jw0 + r_own;
+  const bool row_ok = jrow < p.M;
+  const bool warp_ok = jw0 < p.M;  // some row of the warp's 16 exists
+  const int bidx = nt / sp.tiles_per_row;
+  const int pos = nt - bidx * sp.tiles_per_row;     // the tile's place in its batch row
+  const long long step = tile / sp.chains;           // its place along the chain (reversed)
+  const long long tfirst = (long long)pos * (kBN / 2);
+  const long long n0 = (long long)nt * (kBN / 2);
+  unsigned *abort_word = sp.flags + p.num_tiles * 8;
+  // The replay needs every thread's entry state in the saved context.
+  if (lane == 0 && __ldg(sp.carries + fbt_marker(p.M * sp.batch, sp.fbt_ntiles)).x != 1.f)
+    latch_error(5);  // RQF_ERR_ARGUMENT
+  const float2 lam = row_ok ? __ldg(sp.c1 + jrow) : cz();
+  const float2 tap0 = row_ok ? __ldg(sp.tap0 + jrow) : cz();
+  const float2 tap1 = row_ok ? __ldg(sp.tap1 + jrow) : cz();
+  const bool has_acc = p.acc != nullptr;
+  // z before the tile, for the even lane's first sample of chunk 0
+  const float2 zb = (row_ok && !odd && tfirst > 0) ? __ldg(sp.zin + jrow * p.N + n0 - 1) : cz();
+
+  // this tile's 16 saved entry slots of each row (one per 8 samples)
+  float4 *gst = stage;                                    // g staging, 16 rows x 128 B
+  float4 *dst = stage + 128;                              // grad_z staging
+  const float2 *ent = reinterpret_cast<const float2 *>(stage + 256);  // [16 rows][16 slots], swizzled
+  {
+    const long long jt = tfirst / kFbtTile;
+    const int s0 = (int)(tfirst - jt * kFbtTile) / kFbtK;
+    float4 *ent4 = stage + 256;
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int e4 = it * 32 + lane;
+      const int rr = e4 >> 3, k = e4 & 7;
+      const long long jj = jw0 + rr;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (jj < p.M)
+        v = __ldg(reinterpret_cast<const float4 *>(
+            sp.carries + fbt_slot(jj * sp.batch + bidx, sp.fbt_ntiles, (int)jt) + s0 + 2 * k));
+      ent4[rr * 8 + (k ^ (rr & 7))] = v;
+    }
+    __syncwarp();
+  }
+
+  float2 D = cz();  // d at the sample after the chunk
+  if (step > 0) {
+    const long long pred = (tile - sp.chains) * 2 + rank;
+    const bool ok = scan_link_wait(sp.flags + pred * 4 + quarter, abort_word, abort);
+    if (!__all_sync(0xffffffffu, ok)) return false;
+    const float4 l = __ldcg(sp.link + pred * 64 + quarter * 16 + r_own);
+    D = make_float2(l.x, l.y);
+  }
+  const float2 mu = c_conj(lam);
+  const float2 T0X = make_float2(tap0.x, tap0.x), T0Y = make_float2(tap0.y, -tap0.y);
+  const float2 T1X = make_float2(tap1.x, tap1.x), T1Y = make_float2(tap1.y, -tap1.y);
+  float2 pc1 = cz(), qc1 = cz(), pt0 = cz(), qt0 = cz(), pt1 = cz(), qt1 = cz();
+  const int own = r_own * 8, sw = r_own & 7, half = odd ? 4 : 0;
+  // the ring's loads two chunks ahead: chunks c - 2 of this tile, then the
+  // first two of the warp's next tile
+  int xn = 0, yn = 0;
+  const bool has_next =
+      lane == 0 && ring_coords(tile + ring.npairs, kBN / 32 - 1, p, sp, rank, quarter, xn, yn);
+
+#pragma unroll 1
+  for (int c = kBN / 32 - 1; c >= 0; --c) {
+    const long long nbase = n0 + c * 16;
+    const uint32_t kseq = ring.consumed;
+    bool ok = mbar_wait(ring.bar + (kseq & 1), (kseq >> 1) & 1u, abort, 8);
+    // chunk c - 1 (the next in the ring) holds the z before the even lane's
+    // first sample
+    if (c > 0) ok = ok && mbar_wait(ring.bar + ((kseq + 1) & 1), ((kseq + 1) >> 1) & 1u, abort, 8);
+    if (!__all_sync(0xffffffffu, ok)) return false;
+    const float4 *zs = reinterpret_cast<const float4 *>(ring.base + (kseq & 1) * kRingSlotBytes);
+    float2 z[8];
+    float4 ac[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 v = zs[own + ((half + q) ^ sw)];
+      z[2 * q] = make_float2(v.x, v.y);
+      z[2 * q + 1] = make_float2(v.z, v.w);
+      ac[q] = has_acc ? zs[128 + own + ((half + q) ^ sw)] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float2 zpe = zb;
+    if (c > 0) {
+      const float4 q = reinterpret_cast<const float4 *>(
+          ring.base + ((kseq + 1) & 1) * kRingSlotBytes)[own + (7 ^ sw)];
+      zpe = make_float2(q.z, q.w);
+    }
+
+    float v[32];
+    tc_ld_32x32b_x32(tbase + (uint32_t)(c * 32), v);
+    float r[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) r[i] = __shfl_xor_sync(0xffffffffu, odd ? v[i] : v[16 + i], 1);
+    float2 g[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      const float pr_re = odd ? r[2 * t] : v[2 * t];
+      const float pr_im = odd ? r[2 * t + 1] : v[2 * t + 1];
+      const float pi_re = odd ? v[16 + 2 * t] : r[2 * t];
+      const float pi_im = odd ? v[16 + 2 * t + 1] : r[2 * t + 1];
+      const float4 a = ac[t >> 1];
+      g[t] = make_float2(pr_re - pi_im + ((t & 1) ? a.z : a.x),
+                         pr_im + pi_re + ((t & 1) ? a.w : a.y));
+    }
+    if (lane == 0) bulk_wait_read<1>();  // the previous g store has read its staging
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      gst[own + ((half + q) ^ sw)] =
+          make_float4(g[2 * q].x, g[2 * q].y, g[2 * q + 1].x, g[2 * q + 1].y);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      if (warp_ok) tma_store_2d(&sp.tmZ, gst, (int)(2 * nbase), (int)jw0);
+      bulk_commit();
+    }
+
+    // z before each lane's first sample: the even lane's last (odd lane), or
+    // the one loaded a chunk ahead (even lane)
+    const float2 zx = shfl_xor2(z[7], 1);
+    const float2 zp = odd ? zx : zpe;
+    float2 bd[8];
+    fbt_drive<8>(tap0, tap1, z, zp, bd);
+    float2 e = ent[r_own * 16 + ((c ^ sw) << 1) + (odd ? 1 : 0)];
+    float2 yp[8], em[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      yp[k] = e;
+      e = c_fma(lam, e, bd[k]);
+      em[k] = sp.fuse_act ? c_relu_mask(g[k], e) : g[k];
+    }
+    // the odd lane's fold from D is d at its first sample: the even lane's D
+    float2 h = D;
+#pragma unroll
+    for (int k = 7; k >= 0; --k) h = c_fma(mu, h, em[k]);
+    const float2 hx = shfl_xor2(h, 1);
+    float2 dn = odd ? D : hx;
+    float2 dsw = make_float2(dn.y, dn.x);
+    float2 gz[8];
+#pragma unroll
+    for (int k = 7; k >= 0; --k) {
+      const float2 d = c_fma(mu, dn, em[k]);
+      const float2 ds = make_float2(d.y, d.x);
+      gz[k] = __ffma2_rn(T0X, d, __ffma2_rn(T0Y, ds, __ffma2_rn(T1X, dn, __fmul2_rn(T1Y, dsw))));
+      const float2 dx = make_float2(d.x, d.x), dy = make_float2(d.y, d.y);
+      pc1 = __ffma2_rn(yp[k], dx, pc1);
+      qc1 = __ffma2_rn(yp[k], dy, qc1);
+      pt0 = __ffma2_rn(z[k], dx, pt0);
+      qt0 = __ffma2_rn(z[k], dy, qt0);
+      const float2 zk1 = k > 0 ? z[k - 1] : zp;
+      pt1 = __ffma2_rn(zk1, dx, pt1);
+      qt1 = __ffma2_rn(zk1, dy, qt1);
+      dn = d;
+      dsw = ds;
+    }
+    // d at the chunk's first sample (the even lane's) enters the chunk before
+    const float2 dx2 = shfl_xor2(dn, 1);
+    D = odd ? dx2 : dn;
+
+    if (lane == 0) bulk_wait_read<1>();  // the previous grad_z store has read its staging
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      dst[own + ((half + q) ^ sw)] =
+          make_float4(gz[2 * q].x, gz[2 * q].y, gz[2 * q + 1].x, gz[2 * q + 1].y);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      if (warp_ok) tma_store_2d(&sp.tmAct, dst, (int)(2 * nbase), (int)jw0);
+      bulk_commit();
+      // every lane has used slot kseq: its next chunk
+      if (c >= 2)
+        ring_issue(ring, kseq + 2, p, sp, (int)(2 * (n0 + 16 * (c - 2))), (int)jw0);
+      else if (has_next)
+        ring_issue(ring, kseq + 2, p, sp, xn - 32 * (1 - c), yn);
+    }
+    ring.consumed = kseq + 1;
+  }
+
+  // the tile's sums per row: conj(v) d = (v.x d.x + v.y d.y, v.x d.y - v.y d.x)
+  {
+    float2 s1 = make_float2(pc1.x + qc1.y, qc1.x - pc1.y);
+    float2 s2 = make_float2(pt0.x + qt0.y, qt0.x - pt0.y);
+    float2 s3 = make_float2(pt1.x + qt1.y, qt1.x - pt1.y);
+    s1 = c_add(s1, shfl_xor2(s1, 1));
+    s2 = c_add(s2, shfl_xor2(s2, 1));
+    s3 = c_add(s3, shfl_xor2(s3, 1));
+    if (!odd && row_ok) {
+      float2 *pp = sp.partials + ((jrow * sp.batch + bidx) * sp.tiles_per_row + pos) * 3;
+      pp[0] = s1;
+      pp[1] = s2;
+      pp[2] = s3;
+    }
+  }
+  __syncwarp();  // entry-slot reads done before the next tile overwrites them
+
+  // publish d at the tile's first sample for the tile before it in time
+  if (pos > 0) {
+    const long long me = tile * 2 + rank;
+    if (odd) sp.link[me * 64 + quarter * 16 + r_own] = make_float4(D.x, D.y, 0.f, 0.f);
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) st_release_u32(sp.flags + me * 4 + quarter, 1u);
+  }
+  return true;
+}
+
+template <bool kRealOut, int kScan = 0>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmX,
             const Params p, const __grid_constant__ ScanParams sp) {
@@ -733,6 +1041,7 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   uint64_t *acce = accf + kAccBufs;      // accumulator drained, both CTAs (leader's; 8 warps)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acce + kAccBufs);
   volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  uint64_t *ringbar = reinterpret_cast<uint64_t *>(tmem_slot + 2);  // backward scan: 4 warps x 2
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -749,6 +1058,8 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       mbar_init(&accf[a], 1);
       mbar_init(&acce[a], 8);
     }
+    if constexpr (kScan == kScanBwd)
+      for (int i = 0; i < 8; ++i) mbar_init(&ringbar[i], 1);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_tmap(&tmA);
@@ -878,9 +1189,20 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         reinterpret_cast<float4 *>(smem + L::kStagingOff + quarter * L::kWarpStaging);
     int acc = 0;
     uint32_t acc_phase = 0;
-    if constexpr (kScan) {  // every thread's entry is saved (the row kernels' marker)
+    if constexpr (kScan == kScanFwd) {  // every thread's entry is saved (the row kernels' marker)
       if (blockIdx.x == 0 && warp == 2 && lane == 0)
         sp.carries[fbt_marker(p.M * sp.batch, sp.fbt_ntiles)] = make_float2(1.f, 0.f);
+    }
+    ScanRing ring{smem + L::kRingOff + quarter * kRingWarpBytes, ringbar + 2 * quarter, npairs,
+                  0u, 0u};
+    if constexpr (kScan == kScanBwd) {  // the first two chunks of this warp's sequence
+      int x0, y0;
+      if (lane == 0 && ring_coords(pair0, kBN / 32 - 1, p, sp, (int)rank, quarter, x0, y0)) {
+        prefetch_tmap(&sp.tmZin);
+        if (p.acc) prefetch_tmap(&sp.tmAcc);
+        ring_issue(ring, 0, p, sp, x0, y0);
+        ring_issue(ring, 1, p, sp, x0 - 32, y0);
+      }
     }
     for (long long tile = pair0; tile < p.num_tiles; tile += npairs) {
       // every lane waits; the decision is made warp-uniform before the
@@ -925,8 +1247,12 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           }
           __syncwarp();
         }
-      } else if constexpr (kScan) {
+      } else if constexpr (kScan == kScanFwd) {
         if (!scan_epilogue(tbase, stage, p, sp, tile, mp, nt, rank, quarter, lane, abort)) break;
+      } else if constexpr (kScan == kScanBwd) {
+        if (!scan_bwd_epilogue(tbase, stage, p, sp, tile, mp, nt, rank, quarter, lane, ring,
+                               abort))
+          break;
       } else {
       const int W = p.real_x ? 32 : 16;            // samples per row per chunk
       const int kpr = W / 2;                       // 16-byte chunks per row
@@ -1013,6 +1339,12 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     }
     if constexpr (kScan) {  // the TMA stores of this warp complete before the CTA exits
       if (lane == 0) bulk_wait<0>();
+      __syncwarp();
+    }
+    if constexpr (kScan == kScanBwd) {  // and so do its ring loads (after an abort: bounded)
+      if (lane == 0)
+        for (uint32_t k = ring.consumed; k < ring.issued; ++k)
+          mbar_drain(ring.bar + (k & 1), (k >> 1) & 1u);
       __syncwarp();
     }
   } else {

@@ -1195,18 +1195,22 @@ size_t rqf_projection_workspace_bytes(int64_t m, int64_t k) {
 
 namespace {
 
-int proj_scan_pairs_per_device() {
-  return pair_capacity<4>(reinterpret_cast<const void *>(proj::proj_kernel<false, true>),
+int proj_scan_pairs_per_device(int mode) {
+  if (mode == proj::kScanBwd)
+    return pair_capacity<5>(reinterpret_cast<const void *>(proj::proj_kernel<false, proj::kScanBwd>),
+                            proj::kThreads, proj::kScanBwdSmemBytes);
+  return pair_capacity<4>(reinterpret_cast<const void *>(proj::proj_kernel<false, proj::kScanFwd>),
                           proj::kThreads, proj::kScanSmemBytes);
 }
 
 // x complex (k x n) when real_x = 0, real (k x n) when real_x = 1.  With
-// `scan` (complex x, no acc, n = batch * T): the block scan runs in the
-// epilogue (proj_kernel<false, true>); the caller has checked its shapes and
-// zeroed its flags, and chains is filled in here.
+// `scan` (complex x, n = batch * T): the block scan (scan_mode kScanFwd, no
+// acc) or its VJP (kScanBwd) runs in the epilogue; the caller has checked its
+// shapes and zeroed its flags, and chains is filled in here.
 int projection_impl(const float *w, const float *x, const float *acc, float *out, int64_t m,
                     int64_t k, int64_t n, int conj_transpose, void *workspace,
-                    rqf_stream_t stream, int real_x, const proj::ScanParams *scan = nullptr) {
+                    rqf_stream_t stream, int real_x, const proj::ScanParams *scan = nullptr,
+                    int scan_mode = 0) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (m < 0 || k < 0 || n < 0) return RQF_ERR_SHAPE;
   if (m == 0 || n == 0) return RQF_OK;
@@ -1230,7 +1234,7 @@ int projection_impl(const float *w, const float *x, const float *acc, float *out
     return RQF_ERR_ALIGN;
   const ProjGeometry g = proj_geometry(m, k);
   if (g.rows_pad > 0x3fffffffLL || g.k_pad > 0x7fffffffLL) return RQF_ERR_SHAPE;
-  const int pairs = scan ? proj_scan_pairs_per_device() : proj_pairs_per_device();
+  const int pairs = scan ? proj_scan_pairs_per_device(scan_mode) : proj_pairs_per_device();
   if (pairs <= 0) return RQF_ERR_LAUNCH;
 
   float *a_split = static_cast<float *>(workspace);
@@ -1272,8 +1276,12 @@ int projection_impl(const float *w, const float *x, const float *acc, float *out
     // persistent grid is the device's pair capacity at most.
     proj::ScanParams sp = *scan;
     sp.chains = p.m_pairs * sp.batch;
-    proj::proj_kernel<false, true><<<(unsigned)grid, proj::kThreads, proj::kScanSmemBytes, st>>>(
-        tmA, tmX, p, sp);
+    if (scan_mode == proj::kScanBwd)
+      proj::proj_kernel<false, proj::kScanBwd>
+          <<<(unsigned)grid, proj::kThreads, proj::kScanBwdSmemBytes, st>>>(tmA, tmX, p, sp);
+    else
+      proj::proj_kernel<false, proj::kScanFwd>
+          <<<(unsigned)grid, proj::kThreads, proj::kScanSmemBytes, st>>>(tmA, tmX, p, sp);
   } else {
     proj::proj_kernel<false><<<(unsigned)grid, proj::kThreads, proj::kSmemBytes, st>>>(
         tmA, tmX, p, proj::ScanParams{});
@@ -1371,7 +1379,85 @@ int rqf_projection_block_scan(const float *w, const float *x, const float *c1, c
   sp.tiles_per_row = (int)(time / 128);
   sp.fbt_ntiles = (int)rqf_fbt_num_tiles(time);
   sp.fuse_act = fuse_act ? 1 : 0;
-  return projection_impl(w, x, nullptr, z, filters, k, batch * time, 0, workspace, stream, 0, &sp);
+  return projection_impl(w, x, nullptr, z, filters, k, batch * time, 0, workspace, stream, 0, &sp,
+                         proj::kScanFwd);
+}
+
+size_t rqf_projection_block_scan_backward_workspace_bytes(int64_t filters, int64_t k,
+                                                          int64_t batch, int64_t time) {
+  BlockScanLayout l;
+  if (!block_scan_layout(filters, k, batch, time, l)) return 0;
+  return l.total + (size_t)filters * (size_t)batch * (size_t)(time / 128) * 3 * sizeof(float2);
+}
+
+int rqf_projection_block_scan_backward(const float *w, const float *gz_above, const float *acc,
+                                       const float *c1, const float *tap0, const float *tap1,
+                                       const float *z, const float *carries, float *grad_out,
+                                       float *grad_z, float *grad_c1, float *grad_tap0,
+                                       float *grad_tap1, void *workspace, int64_t filters,
+                                       int64_t k, int64_t batch, int64_t time, int fuse_act,
+                                       rqf_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (k < 0) return RQF_ERR_SHAPE;
+  int status = fbt_dims_ok(filters, batch, time);
+  if (status != RQF_OK) return status;
+  if (filters == 0) return RQF_OK;
+  if (batch == 0 || time == 0) {  // empty sums
+    const size_t nb = (size_t)filters * sizeof(float2);
+    for (float *g : {grad_c1, grad_tap0, grad_tap1})
+      if (g && cudaMemsetAsync(g, 0, nb, st) != cudaSuccess) return RQF_ERR_LAUNCH;
+    return RQF_OK;
+  }
+  BlockScanLayout l;
+  if (!block_scan_layout(filters, k, batch, time, l)) return RQF_ERR_SHAPE;
+  if (!w || !gz_above || !c1 || !tap0 || !tap1 || !z || !carries || !grad_out || !grad_z ||
+      !grad_c1 || !grad_tap0 || !grad_tap1 || !workspace)
+    return RQF_ERR_ARGUMENT;
+  // the outputs are written while other tiles still read gz_above, acc and z
+  for (const float *in : {gz_above, acc, z, carries})
+    if (in && (in == grad_out || in == grad_z)) return RQF_ERR_ARGUMENT;
+  if (grad_out == grad_z) return RQF_ERR_ARGUMENT;
+  if (!aligned(gz_above, 16) || !aligned(z, 16) || !aligned(grad_out, 16) ||
+      !aligned(grad_z, 16) || !aligned(carries, 16) || !aligned(workspace, 16) ||
+      (acc && !aligned(acc, 16)) || !aligned(c1, 8) || !aligned(tap0, 8) || !aligned(tap1, 8) ||
+      !aligned(grad_c1, 8) || !aligned(grad_tap0, 8) || !aligned(grad_tap1, 8))
+    return RQF_ERR_ALIGN;
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  unsigned *flags = reinterpret_cast<unsigned *>(ws + l.flags_off);
+  float2 *partials = reinterpret_cast<float2 *>(ws + l.total);
+  if (cudaMemsetAsync(flags, 0, l.flags_bytes, st) != cudaSuccess) return RQF_ERR_LAUNCH;
+  proj::ScanParams sp{};
+  const uint64_t nf = 2 * (uint64_t)batch * (uint64_t)time;
+  if (!encode_map_2d(&sp.tmZ, grad_out, nf, (uint64_t)filters, nf * sizeof(float), 32, 16,
+                     CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map_2d(&sp.tmAct, grad_z, nf, (uint64_t)filters, nf * sizeof(float), 32, 16,
+                     CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_map_2d(&sp.tmZin, z, nf, (uint64_t)filters, nf * sizeof(float), 32, 16,
+                     CU_TENSOR_MAP_SWIZZLE_128B) ||
+      (acc && !encode_map_2d(&sp.tmAcc, acc, nf, (uint64_t)filters, nf * sizeof(float), 32, 16,
+                             CU_TENSOR_MAP_SWIZZLE_128B)))
+    return RQF_ERR_LAUNCH;
+  sp.c1 = reinterpret_cast<const float2 *>(c1);
+  sp.tap0 = reinterpret_cast<const float2 *>(tap0);
+  sp.tap1 = reinterpret_cast<const float2 *>(tap1);
+  sp.carries = const_cast<float2 *>(reinterpret_cast<const float2 *>(carries));  // read only
+  sp.zin = reinterpret_cast<const float2 *>(z);
+  sp.partials = partials;
+  sp.reverse = 1;
+  sp.link = reinterpret_cast<float4 *>(ws + l.link_off);
+  sp.flags = flags;
+  sp.T = time;
+  sp.batch = (int)batch;
+  sp.tiles_per_row = (int)(time / 128);
+  sp.fbt_ntiles = (int)rqf_fbt_num_tiles(time);
+  sp.fuse_act = fuse_act ? 1 : 0;
+  status = projection_impl(w, gz_above, acc, grad_out, filters, k, batch * time, 1, workspace,
+                           stream, 0, &sp, proj::kScanBwd);
+  if (status != RQF_OK) return status;
+  reduce_partials_kernel<<<(unsigned)filters, 256, 0, st>>>(
+      partials, reinterpret_cast<float2 *>(grad_c1), reinterpret_cast<float2 *>(grad_tap0),
+      reinterpret_cast<float2 *>(grad_tap1), batch, batch, 1, sp.tiles_per_row);
+  return launch_status();
 }
 
 size_t rqf_projection_real_out_workspace_bytes(int64_t m, int64_t k) {

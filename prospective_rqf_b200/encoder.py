@@ -45,14 +45,34 @@ PROJECTION = os.environ.get("RQF_B200_PROJECTION", "tc")
 # faster (ops.block_scan_preferred); "1": wherever it applies (T a multiple of
 # 128); "0": never — the projection, then the separate (F,B,T) scan kernel.
 BLOCK_SCAN = os.environ.get("RQF_B200_BLOCK_SCAN", "auto")
+# The same for the backward pairs of _PureStack (ops.projection_block_scan_backward):
+# "auto" where ops.block_scan_backward_preferred expects it to pay, "1"
+# wherever it applies, "0" never.
+BLOCK_SCAN_BWD = os.environ.get("RQF_B200_BLOCK_SCAN_BWD", "auto")
+
+
+def _block_scan_chosen(W, h) -> bool:
+    """Whether the block z = W h runs its scan in the GEMM's epilogue, by
+    BLOCK_SCAN (the same rule decides a backward pair: W the upper block's
+    weight conjugate-transposed, h its z cotangent)."""
+    mode = str(BLOCK_SCAN)
+    return PROJECTION == "tc" and mode not in ("0", "False") and (
+        ops.block_scan_preferred(W, h) if mode == "auto" else ops.block_scan_eligible(W, h))
+
+
+def _backward_pair_chosen(W, gz) -> bool:
+    """Whether the backward pair (W the upper block's weight, gz its z
+    cotangent) runs as one ops.projection_block_scan_backward launch."""
+    mode = str(BLOCK_SCAN_BWD)
+    return PROJECTION == "tc" and mode not in ("0", "False") and (
+        ops.block_scan_backward_preferred(W, gz) if mode == "auto"
+        else ops.block_scan_eligible(W.mH, gz))
 
 
 def _block_forward(W, h, C1, tap0, tap1, fuse_act, skip):
     """z = W h, then the (F,B,T) scan (act(y) + skip when skip is given):
     (out, saved) as ops._fbt_forward returns them."""
-    mode = str(BLOCK_SCAN)
-    if PROJECTION == "tc" and mode not in ("0", "False") and (
-            ops.block_scan_preferred(W, h) if mode == "auto" else ops.block_scan_eligible(W, h)):
+    if _block_scan_chosen(W, h):
         return ops.projection_block_scan(W, h, C1, tap0, tap1, fuse_act, skip)
     return ops._fbt_forward(C1, tap0, tap1, _project(W, h), fuse_act, skip)
 
@@ -214,6 +234,60 @@ class _PureBlock(torch.autograd.Function):
         return gh, gW, gc1, gt0, gt1, None, None
 
 
+class _PureStack(torch.autograd.Function):
+    """Consecutive full-BPTT Pure RQF blocks (pure.py:_forward_fbt_stack
+    :530-536, each block as in _PureBlock) as one autograd node, so that the
+    backward can hand each block's output cotangent straight to the scan VJP
+    of the block below inside one launch: for blocks i-1 < i,
+    ops.projection_block_scan_backward computes g_{i-1} = W_i^H gz_i + g_i
+    (g_i the skip's cotangent) and, in the same GEMM's epilogue, block i-1's
+    scan VJP of it from its saved context (every (F,B,T) forward saves the
+    entry states it replays), so g_{i-1} is not read back.  Where that launch
+    is not expected to pay (_backward_pair_chosen), the pair takes the
+    separate GEMM and (F,B,T) backward, as _PureBlock does.  Arguments: h, then per-block tuples of
+    flags (fuse_act, skip), then the blocks' W, C1, tap0 and tap1 in that
+    order."""
+
+    @staticmethod
+    def forward(ctx, h, acts, skips, *params):
+        m = len(acts)
+        Ws, c1s, t0s, t1s = (params[i * m:(i + 1) * m] for i in range(4))
+        inputs, saved = [], []
+        for i in range(m):
+            inputs.append(h)
+            h, sv = _block_forward(Ws[i], h, c1s[i], t0s[i], t1s[i], bool(acts[i]),
+                                   h if skips[i] else None)
+            saved.extend(sv)
+        ctx.save_for_backward(*inputs, *Ws, *saved)
+        ctx.acts, ctx.skips = tuple(map(bool, acts)), tuple(map(bool, skips))
+        return h
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, g):
+        m = len(ctx.acts)
+        st = ctx.saved_tensors
+        inputs, Ws = st[:m], st[m:2 * m]
+        saved = [st[2 * m + 5 * i:2 * m + 5 * i + 5] for i in range(m)]
+        need = ctx.needs_input_grad
+        gW, gc1, gt0, gt1 = ([None] * m for _ in range(4))
+        g = ops._c64(g)
+        vjp = ops._fbt_backward(saved[m - 1], g, ctx.acts[m - 1])
+        for i in range(m - 1, -1, -1):
+            gc1[i], gt0[i], gt1[i], gz = vjp
+            acc = g if ctx.skips[i] else None
+            if i > 0 and _backward_pair_chosen(Ws[i], gz):
+                g, vjp = ops.projection_block_scan_backward(Ws[i], gz, acc, saved[i - 1],
+                                                            ctx.acts[i - 1])
+            elif i > 0 or need[0]:
+                g = _project(Ws[i], gz, conj_transpose=True, acc=acc)
+                if i > 0:
+                    vjp = ops._fbt_backward(saved[i - 1], g, ctx.acts[i - 1])
+            if need[3 + i]:
+                gW[i] = _weight_grad(gz, inputs[i])
+        return (g if need[0] else None, None, None, *gW, *gc1, *gt0, *gt1)
+
+
 class _InputBlock(torch.autograd.Function):
     """The input projection and the first full-BPTT block together
     (pure.py:_forward_fbt_stack :522-534 and the block's _forward_fbt
@@ -355,16 +429,18 @@ class PureRQFEncoderB200(nn.Module):
         else:
             proj = w_in @ x_cf if b_in is None else torch.addmm(b_in[:, None], w_in, x_cf)
             h = proj.reshape(-1, B, T).to(torch.complex64)
-        for i in range(first, n):
-            act = self.final_activation or i + 1 < n
-            c1, t0, t1 = coeffs[i]
-            W = self.W[i]
-            skip = self.skip and W.shape[0] == W.shape[1]
-            if self.scan_grad_mode == "tbptt1":
-                out = _TBPTTLayer.apply(h, W, c1, t0, t1, act)
+        blocks = range(first, n)
+        acts = tuple(self.final_activation or i + 1 < n for i in blocks)
+        skips = tuple(self.skip and self.W[i].shape[0] == self.W[i].shape[1] for i in blocks)
+        if self.scan_grad_mode == "tbptt1":
+            for i, act, skip in zip(blocks, acts, skips):
+                c1, t0, t1 = coeffs[i]
+                out = _TBPTTLayer.apply(h, self.W[i], c1, t0, t1, act)
                 h = out + h if skip else out
-            else:
-                h = _PureBlock.apply(h, W, c1, t0, t1, act, skip)
+        elif len(blocks) > 0:
+            h = _PureStack.apply(h, acts, skips, *(self.W[i] for i in blocks),
+                                 *(coeffs[i][0] for i in blocks), *(coeffs[i][1] for i in blocks),
+                                 *(coeffs[i][2] for i in blocks))
         return h
 
     @torch.no_grad()

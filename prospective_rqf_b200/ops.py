@@ -329,6 +329,61 @@ def projection_block_scan(W, h, C1, tap0, tap1, fuse_act: bool, skip=None):
     return out, (c1, t0, t1, z, carries)
 
 
+def block_scan_backward_preferred(W: torch.Tensor, gz: torch.Tensor) -> bool:
+    """Whether projection_block_scan_backward is expected to beat the
+    input-cotangent GEMM followed by the separate (F,B,T) backward (W (k, F)
+    the upper block's weight, gz (k, B, T) its z cotangent): nowhere
+    measured so far.  At F = k = 256, T = 16000 the fused launch takes
+    2.25 ms at B = 32 against 1.30 + 0.55 ms for the two launches, and
+    2.29 ms against 0.65 + 0.28 ms at B = 16: its epilogue (the replay, the
+    reverse adjoint and the coefficient sums of 16 rows per warp, one warp
+    per TMEM lane quarter) needs ~12 us per tile, longer than the tile's
+    tensor-core work (~11 us), and the chains along time serialise it."""
+    return False
+
+
+def projection_block_scan_backward(W, gz_above, acc, saved, fuse_act: bool):
+    """The lower block's output cotangent and scan VJP in one launch
+    (rqf_projection_block_scan_backward): g = W^H gz_above + acc on the
+    split-TF32 tensor-core GEMM (the autograd of pure.py:223's matmul for
+    the upper block, acc the skip's cotangent), and in its epilogue the
+    lower block's (F,B,T) scan VJP of g from its saved context ``saved``
+    (c1, tap0, tap1, z, carries), which must come from projection_block_scan
+    or the row kernels (every 8-sample entry state saved).  Returns
+    (g, (gc1, gt0, gt1, gz)) with the second tuple as _fbt_backward(saved, g,
+    fuse_act) returns it."""
+    c1, t0, t1, z, carries = saved
+    dev = _require_cuda(W, gz_above, acc, z)
+    w = _c64(W)
+    x = _c64(gz_above)
+    F, B, T = (int(d) for d in z.shape)
+    k = int(w.shape[0])
+    if w.dim() != 2 or int(w.shape[1]) != F or tuple(x.shape) != (k, B, T):
+        raise ValueError(f"projection_block_scan_backward: W {tuple(w.shape)}, gz {tuple(x.shape)} "
+                         f"and z {tuple(z.shape)} do not chain")
+    if not block_scan_eligible(w.mH, x):
+        raise ValueError("projection_block_scan_backward needs T a multiple of 128")
+    a = None
+    if acc is not None:
+        a = _c64(acc)
+        if tuple(a.shape) != (F, B, T):
+            raise ValueError(f"acc must have shape {(F, B, T)}, got {tuple(a.shape)}")
+    lib = _abi.load()
+    g = torch.empty_like(z)
+    gz = torch.empty_like(z)
+    gc1, gt0, gt1 = torch.empty_like(c1), torch.empty_like(t0), torch.empty_like(t1)
+    ws = _scratch(lib.rqf_projection_block_scan_backward_workspace_bytes(F, k, B, T), dev)
+    with _timing.launch("rqf_projection_block_scan_backward", F * B * T,
+                        _nbytes(x, a, z, g, gz), 8 * F * k * B * T):
+        _abi.check(lib.rqf_projection_block_scan_backward(
+            _abi.ptr(w), _abi.ptr(x), _abi.ptr(a), _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1),
+            _abi.ptr(z), _abi.ptr(carries), _abi.ptr(g), _abi.ptr(gz), _abi.ptr(gc1),
+            _abi.ptr(gt0), _abi.ptr(gt1), _abi.ptr(ws), F, k, B, T, int(bool(fuse_act)),
+            _abi.stream_of(x)), "rqf_projection_block_scan_backward")
+    _done(dev)
+    return g, (gc1, gt0, gt1, gz)
+
+
 def _fbt_backward(saved, grad_output, fuse_act: bool):
     c1, t0, t1, z, carries = saved
     F, B, T = z.shape

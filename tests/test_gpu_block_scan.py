@@ -20,7 +20,7 @@ import numpy as np
 import pytest
 import torch
 
-from _util import FWD_TOL, GRAD_TOL, assert_close
+from _util import FWD_TOL, GRAD_ELEM_TOL, GRAD_TOL, assert_close
 from oracle import oracle
 
 pytestmark = pytest.mark.gpu
@@ -193,8 +193,8 @@ def test_block_scan_rejects():
 
 def test_encoder_block_scan_matches_unfused():
     """The encoder at T = 4096 (a multiple of 128) with its blocks on the
-    fused forward and on the separate projection + scan: features and every
-    parameter gradient agree to fp32 rounding."""
+    fused forward and backward launches and on the separate projection +
+    scan: features and every parameter gradient agree to fp32 rounding."""
     from prospective_rqf_b200 import encoder
 
     torch.manual_seed(0)
@@ -204,7 +204,7 @@ def test_encoder_block_scan_matches_unfused():
     x = 0.5 * torch.randn(4, 4096, 1, device="cuda")
     res = []
     for fused in ("1", "0"):
-        encoder.BLOCK_SCAN = fused
+        encoder.BLOCK_SCAN = encoder.BLOCK_SCAN_BWD = fused
         try:
             enc.zero_grad()
             h = enc(x)
@@ -212,9 +212,106 @@ def test_encoder_block_scan_matches_unfused():
             res.append((h.detach().clone(),
                         {n: p.grad.detach().clone() for n, p in enc.named_parameters()}))
         finally:
-            encoder.BLOCK_SCAN = "auto"
+            encoder.BLOCK_SCAN = encoder.BLOCK_SCAN_BWD = "auto"
     (h1, g1), (h2, g2) = res
     assert_close(_host(h1), _host(h2), 1e-5, "features")
     for n in g1:
         assert_close(g1[n].cpu().numpy().astype(np.complex128),
                      g2[n].cpu().numpy().astype(np.complex128), 1e-4, n)
+
+
+# ------------------------------------------------------------ fused backward
+# (F, K, k, B, T): the lower block's F filters over K inputs, the upper
+# block's k filters over those F
+BWD_SHAPES = [
+    (64, 64, 96, 2, 256),       # F below one pair tile's 128 rows
+    (128, 96, 128, 3, 2176),    # two context tiles, the second cut at 128 samples
+    (256, 256, 256, 4, 4096),   # whole context tiles
+    (96, 96, 64, 1, 128),       # one GEMM tile per row, one chain per row block
+    (200, 136, 160, 5, 1920),   # ragged F, K and k; T below one context tile
+    (128, 128, 128, 1, 8192),   # a single chain of 64 tiles, run from its end
+    (128, 128, 128, 96, 256),   # more chains than CTA pairs
+]
+
+
+def _upper(k, F, B, T, seed):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    W = (torch.randn(k, F, generator=g, dtype=torch.complex64) / np.sqrt(F)).cuda()
+    gz = torch.randn(k, B, T, generator=g, dtype=torch.complex64).cuda()
+    acc = torch.randn(F, B, T, generator=g, dtype=torch.complex64).cuda()
+    return W, gz, acc
+
+
+@pytest.mark.parametrize("F,K,k,B,T", BWD_SHAPES)
+@pytest.mark.parametrize("fuse", [True, False])
+@pytest.mark.parametrize("with_acc", [True, False])
+def test_block_scan_backward_vs_oracle(F, K, k, B, T, fuse, with_acc):
+    """rqf_projection_block_scan_backward: g = W^H gz_above (+ acc) against an
+    fp64 GEMM (the projection's bound) and bit-identical to rqf_projection's;
+    the lower block's scan VJP of that g against the fp64 oracle (gradient
+    tolerance, the kernel's own split-ReLU decisions) and against the
+    separate (F,B,T) backward on the same g."""
+    from prospective_rqf_b200 import ops
+
+    seed = F * 7 + K * 3 + k + B * 11 + T + 2 * fuse + with_acc
+    W0, h, c1, t0, t1 = _case(F, K, B, T, seed)
+    act, saved = ops.projection_block_scan(W0, h, c1, t0, t1, fuse, None)
+    W, gz_above, acc = _upper(k, F, B, T, seed + 1)
+    if not with_acc:
+        acc = None
+    g, (gc1, gt0, gt1, gz) = ops.projection_block_scan_backward(W, gz_above, acc, saved, fuse)
+
+    g2 = ops.projection(W, gz_above, conj_transpose=True, acc=acc)
+    assert torch.equal(g, g2), "g differs from rqf_projection's"
+    g_ref = W.cpu().to(torch.complex128).mH @ gz_above.cpu().to(torch.complex128).reshape(k, -1)
+    g_ref = g_ref.reshape(F, B, T).numpy()
+    if acc is not None:
+        g_ref = g_ref + _host(acc)
+    assert_close(_host(g), g_ref, PROJ_TOL, "g")
+
+    zc, c1h, t0h, t1h = _host(saved[3]), _host(c1), _host(t0), _host(t1)
+    mask = None
+    if fuse:
+        mask = oracle.relu_mask_from_output(_host(act))
+        raw = oracle.two_tap_forward(c1h, t0h, t1h, zc, "fbt", fuse_act=False)
+        assert oracle.mask_disagreement(mask, raw) < MASK_EDGE
+    rz, rc1, rt0, rt1 = oracle.two_tap_backward(c1h, t0h, t1h, zc, _host(g), "fbt",
+                                                fuse_act=fuse, mask=mask)
+    sep = ops._fbt_backward(saved, g, fuse)
+    for got, ref, other, name in ((gz, rz, sep[3], "gz"), (gc1, rc1, sep[0], "gc1"),
+                                  (gt0, rt0, sep[1], "gt0"), (gt1, rt1, sep[2], "gt1")):
+        assert_close(_host(got), ref, GRAD_TOL, name, elem_tol=GRAD_ELEM_TOL)
+        assert_close(_host(got), _host(other), 1e-5, name + " vs the separate backward")
+
+
+def test_block_scan_backward_after_row_kernel_forward():
+    """The lower block's context from the separate (F,B,T) forward (row
+    kernels at this size) serves the fused backward as well."""
+    from prospective_rqf_b200 import ops
+
+    F, B, T = 256, 8, 2048
+    W0, h, c1, t0, t1 = _case(F, F, B, T, 91)
+    z = ops.projection(W0, h)
+    _, saved = ops._fbt_forward(c1, t0, t1, z, True)
+    W, gz_above, acc = _upper(F, F, B, T, 92)
+    g, vjp = ops.projection_block_scan_backward(W, gz_above, acc, saved, True)
+    sep = ops._fbt_backward(saved, g, True)
+    for a, b, name in zip(vjp, sep, ("gc1", "gt0", "gt1", "gz")):
+        assert_close(_host(a), _host(b), 1e-5, name)
+
+
+def test_block_scan_backward_needs_entry_marker():
+    """A saved context without the every-thread marker latches
+    RQF_ERR_ARGUMENT (5) in the device error word; nothing faults."""
+    import prospective_rqf_b200 as rqf
+    from prospective_rqf_b200 import ops
+
+    F, B, T = 128, 2, 256
+    W0, h, c1, t0, t1 = _case(F, F, B, T, 93)
+    _, saved = ops.projection_block_scan(W0, h, c1, t0, t1, True, None)
+    carries = saved[4].clone()
+    carries[-1] = 0
+    W, gz_above, _ = _upper(F, F, B, T, 94)
+    rqf.read_device_error(clear=True)
+    ops.projection_block_scan_backward(W, gz_above, None, (*saved[:4], carries), True)
+    assert rqf.read_device_error(clear=True) == 5
