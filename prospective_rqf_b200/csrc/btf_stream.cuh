@@ -81,11 +81,17 @@ template <int K, int DRIVE, bool LAST>
 __device__ __forceinline__ void btf_drive(const BtfArgs &a, int64_t base, int64_t tw, bool fv,
                                           float2 c2, float2 t1, float2 (&x)[K], float2 &xp,
                                           float2 (&b)[K]) {
+  if (fv && tw + K <= a.T) {  // the whole segment in range: no per-step tests
+    int64_t idx = base + tw * a.F;
 #pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const int64_t t = tw + k;
-    const bool in = fv && t < a.T;
-    x[k] = in ? btf_load_x<DRIVE>(a.x, base + t * a.F, LAST) : cz();
+    for (int k = 0; k < K; ++k, idx += a.F) x[k] = btf_load_x<DRIVE>(a.x, idx, LAST);
+  } else {
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int64_t t = tw + k;
+      const bool in = fv && t < a.T;
+      x[k] = in ? btf_load_x<DRIVE>(a.x, base + t * a.F, LAST) : cz();
+    }
   }
   xp = cz();
   if constexpr (DRIVE == kTwoTap) {
@@ -97,6 +103,23 @@ __device__ __forceinline__ void btf_drive(const BtfArgs &a, int64_t base, int64_
   } else {
 #pragma unroll
     for (int k = 0; k < K; ++k) b[k] = c_mul(c2, x[k]);
+  }
+}
+
+// The cotangent of a warp's K steps starting at tw (zero past T).
+template <int K>
+__device__ __forceinline__ void btf_load_go(const BtfArgs &a, int64_t base, int64_t tw, bool fv,
+                                            bool last_use, float2 (&go)[K]) {
+  if (fv && tw + K <= a.T) {
+    int64_t idx = base + tw * a.F;
+#pragma unroll
+    for (int k = 0; k < K; ++k, idx += a.F) go[k] = btf_ld(a.gout + idx, last_use);
+  } else {
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int64_t t = tw + k;
+      go[k] = (fv && t < a.T) ? btf_ld(a.gout + base + t * a.F, last_use) : cz();
+    }
   }
 }
 
@@ -187,11 +210,20 @@ __global__ void __launch_bounds__(NW * 32) btf_fwd_kernel(const BtfArgs a) {
     float2 Xw = cz();
     for (int w = 0; w < warp; ++w) Xw = c_fma(gK, Xw, s_y[s & 1][w][lane]);
     float2 e = c_fma(Gw, es, Xw);
+    if (fv && tw + K <= a.T) {
+      int64_t idx = base + tw * a.F;
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-      e = c_fma(lam, e, b[k]);
-      const int64_t t = tw + k;
-      if (fv && t < a.T) btf_store_y<ABS>(a.out, base + t * a.F, e);
+      for (int k = 0; k < K; ++k, idx += a.F) {
+        e = c_fma(lam, e, b[k]);
+        btf_store_y<ABS>(a.out, idx, e);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        e = c_fma(lam, e, b[k]);
+        const int64_t t = tw + k;
+        if (fv && t < a.T) btf_store_y<ABS>(a.out, base + t * a.F, e);
+      }
     }
     es = c_fma(gL, es, s_sub[s][lane]);
   }
@@ -240,11 +272,7 @@ __global__ void __launch_bounds__(NW * 32) btf_bwd_kernel(const BtfArgs a) {
   for (int s = 0; s < S; ++s) {
     const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
     btf_drive<K, DRIVE, S == 1>(a, base, tw, fv, c2, t1, x, xp, b);
-#pragma unroll
-    for (int k = 0; k < K; ++k) {
-      const int64_t t = tw + k;
-      go[k] = (fv && t < a.T) ? btf_ld(a.gout + base + t * a.F, S == 1) : cz();
-    }
+    btf_load_go<K>(a, base, tw, fv, S == 1, go);
     float2 y = cz(), h = cz();
 #pragma unroll
     for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
@@ -304,18 +332,19 @@ __global__ void __launch_bounds__(NW * 32) btf_bwd_kernel(const BtfArgs a) {
   for (int s = 1; s < S; ++s) Cs[s] = c_fma(gL, Cs[s - 1], s_subf[s - 1][lane]);
   float2 Ds = s_D[lane];
 
-  // pass 2: sub-tiles from last to first
-  float2 acc_c1 = cz(), acc_1 = cz(), acc_2 = cz();
+  // pass 2: sub-tiles from last to first.  The element-wise products run on
+  // paired fp32 FMAs: conj(c) g = (c.x, c.x) g + (c.y, -c.y) (g.y, g.x), and
+  // each sum conj(v) g accumulates v (g.x, g.x) and v (g.y, g.y) separately,
+  // combined once at the end.
+  const float2 C2X = make_float2(c2.x, c2.x), C2Y = make_float2(c2.y, -c2.y);
+  const float2 T1X = make_float2(t1.x, t1.x), T1Y = make_float2(t1.y, -t1.y);
+  float2 pc1 = cz(), qc1 = cz(), p1 = cz(), q1 = cz(), p2 = cz(), q2 = cz();
 #pragma unroll 1
   for (int s = S - 1; s >= 0; --s) {
     const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
     if constexpr (S > 1) {
       btf_drive<K, DRIVE, true>(a, base, tw, fv, c2, t1, x, xp, b);
-#pragma unroll
-      for (int k = 0; k < K; ++k) {
-        const int64_t t = tw + k;
-        go[k] = (fv && t < a.T) ? __ldcs(a.gout + base + t * a.F) : cz();
-      }
+      btf_load_go<K>(a, base, tw, fv, true, go);
       float2 y = cz(), h = cz();
 #pragma unroll
       for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
@@ -341,33 +370,45 @@ __global__ void __launch_bounds__(NW * 32) btf_bwd_kernel(const BtfArgs a) {
       e = c_fma(lam, e, b[k]);
     }
     float2 gnext = c_fma(Grw, Ds, Xrw);
+    float2 gnsw = c_swap(gnext);
+    const bool full = fv && tw + K <= a.T;
+    int64_t idx = base + (tw + K - 1) * a.F;
 #pragma unroll
-    for (int k = K - 1; k >= 0; --k) {
+    for (int k = K - 1; k >= 0; --k, idx -= a.F) {
       const float2 g = c_fma(mu, gnext, go[k]);
-      const int64_t t = tw + k;
-      const bool in = fv && t < a.T;
+      const float2 gs = c_swap(g);
+      const float2 gx = make_float2(g.x, g.x), gy = make_float2(g.y, g.y);
+      const bool in = full || (fv && tw + k < a.T);
       if constexpr (DRIVE == kReal) {
         // grad of the real input: Re(conj(c2) g)
-        if (in) __stcs(static_cast<float *>(a.out) + base + t * a.F, c2.x * g.x + c2.y * g.y);
-        acc_1 = make_float2(fmaf(x[k].x, g.x, acc_1.x), fmaf(x[k].x, g.y, acc_1.y));
+        if (in) __stcs(static_cast<float *>(a.out) + idx, fmaf(c2.x, g.x, c2.y * g.y));
+        p1 = __ffma2_rn(make_float2(x[k].x, x[k].x), g, p1);  // conj(x) g, x real
       } else if constexpr (DRIVE == kPlain) {
-        if (in) __stcs(static_cast<float2 *>(a.out) + base + t * a.F, c_cfma(c2, g, cz()));
-        acc_1 = c_cfma(x[k], g, acc_1);
+        if (in) __stcs(static_cast<float2 *>(a.out) + idx, __ffma2_rn(C2X, g, __fmul2_rn(C2Y, gs)));
+        p1 = __ffma2_rn(x[k], gx, p1);
+        q1 = __ffma2_rn(x[k], gy, q1);
       } else {
         if (in)
-          __stcs(static_cast<float2 *>(a.out) + base + t * a.F,
-                 c_cfma(t1, gnext, c_cfma(c2, g, cz())));
-        acc_1 = c_cfma(x[k], g, acc_1);
-        acc_2 = c_cfma(k > 0 ? x[k - 1] : xp, g, acc_2);
+          __stcs(static_cast<float2 *>(a.out) + idx,
+                 __ffma2_rn(C2X, g, __ffma2_rn(C2Y, gs, __ffma2_rn(T1X, gnext,
+                                                                    __fmul2_rn(T1Y, gnsw)))));
+        p1 = __ffma2_rn(x[k], gx, p1);
+        q1 = __ffma2_rn(x[k], gy, q1);
+        const float2 xk1 = k > 0 ? x[k - 1] : xp;
+        p2 = __ffma2_rn(xk1, gx, p2);
+        q2 = __ffma2_rn(xk1, gy, q2);
       }
-      acc_c1 = c_cfma(yprev[k], g, acc_c1);
+      pc1 = __ffma2_rn(yprev[k], gx, pc1);
+      qc1 = __ffma2_rn(yprev[k], gy, qc1);
       gnext = g;
+      gnsw = gs;
     }
     Ds = c_fma(muL, Ds, s_subr[s][lane]);  // adjoint entering sub-tile s-1
   }
-  s_red[0][warp][lane] = acc_c1;
-  s_red[1][warp][lane] = acc_1;
-  s_red[2][warp][lane] = acc_2;
+  // conj(v) g = (v.x g.x + v.y g.y, v.x g.y - v.y g.x)
+  s_red[0][warp][lane] = make_float2(pc1.x + qc1.y, qc1.x - pc1.y);
+  s_red[1][warp][lane] = DRIVE == kReal ? p1 : make_float2(p1.x + q1.y, q1.x - p1.y);
+  s_red[2][warp][lane] = make_float2(p2.x + q2.y, q2.x - p2.y);
   __syncthreads();
   if (warp < 3 && fv) {
     float2 sum = cz();
