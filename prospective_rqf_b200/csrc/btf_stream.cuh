@@ -23,7 +23,8 @@
 // entry states to produce the outputs.  S (1..8) is chosen per call from the
 // number of chains.  Tickets run tile-major across chains, so resident CTAs
 // work on different chains instead of queueing behind one.
-// Backward recomputes y from the per-tile carries and fuses the adjoint with
+// The forward saves the state entering every sub-tile; the backward starts
+// each sub-tile from it, and fuses the adjoint with
 // grad_u / grad_x and the coefficient-gradient partial sums (one partial per
 // tile, reduced in fixed order afterwards).
 #pragma once
@@ -42,7 +43,8 @@ struct BtfArgs {
   const float2 *gout;  // (B,T,F) cotangent (backward)
   void *out;           // forward: y; backward: grad_x (float for REAL)
   float2 *out2;        // TBPTT backward: grad_zw
-  float2 *carries;     // (B*F, ntiles), row = b*F + f
+  float2 *carries;     // (B*F, csub), row = b*F + f: the state entering each 128-step sub-tile
+  int csub;            // saved states per row (at least the sub-tiles that start before T)
   float2 *partials;    // (B*F, ntiles, 3)
   u64 *flags;          // (B*F, ntiles, 2)
   unsigned *ticket;
@@ -188,17 +190,19 @@ __global__ void __launch_bounds__(NW * 32) btf_fwd_kernel(const BtfArgs a) {
         C = lookback_const_win(fl, j, M);
         if (has_next) flag_publish2(fl + 2 * j, c_fma(M, C, Xtile), kInclusive);
       }
-      if (a.carries) a.carries[row * a.ntiles + j] = C;
     }
     s_C[lane] = C;
   }
   __syncthreads();
 
-  // pass 2: outputs, sub-tile by sub-tile from their entry states
+  // pass 2: outputs, sub-tile by sub-tile from their entry states (saved
+  // for the backward)
   float2 es = s_C[lane];
 #pragma unroll 1
   for (int s = 0; s < S; ++s) {
     const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
+    if (warp == 0 && fv && a.carries && tile0 + (int64_t)s * L < a.T)
+      a.carries[(bi * a.F + f) * a.csub + (int64_t)j * S + s] = es;
     if constexpr (S > 1) {
       btf_drive<K, DRIVE, true>(a, base, tw, fv, c2, t1, x, xp, b);
       float2 y = cz();
@@ -235,7 +239,6 @@ __global__ void __launch_bounds__(NW * 32) btf_bwd_kernel(const BtfArgs a) {
   constexpr int L = NW * K;
   static_assert(L == kBtfSub, "sub-tile length");
   __shared__ float4 s_yh[2][NW][32];   // (forward local y, reverse local h) per warp
-  __shared__ float2 s_subf[S][32];     // forward sub-tile aggregates
   __shared__ float2 s_subr[S][32];     // reverse sub-tile aggregates
   __shared__ float2 s_red[3][NW][32];
   __shared__ float2 s_D[32];
@@ -254,7 +257,6 @@ __global__ void __launch_bounds__(NW * 32) btf_bwd_kernel(const BtfArgs a) {
   const float2 lam = fv ? a.c1[f] : cz();
   const float2 c2 = fv ? a.c2[f] : cz();
   const float2 t1 = (DRIVE == kTwoTap && fv) ? a.tap1[f] : cz();
-  const float2 C = fv ? a.carries[row * a.ntiles + j] : cz();
   const int64_t base = bi * a.T * a.F + f;
   const int64_t tile0 = (int64_t)j * S * L;
   const float2 mu = c_conj(lam);
@@ -264,33 +266,28 @@ __global__ void __launch_bounds__(NW * 32) btf_bwd_kernel(const BtfArgs a) {
   for (int w = 0; w < warp; ++w) Gw = c_mul(gK, Gw);
   for (int w = NW - 1; w > warp; --w) Grw = c_mul(muK, Grw);
 
-  // pass 1: forward and reverse sub-tile aggregates.  With one sub-tile
-  // (S == 1) the loaded values and the warp exchange stay for pass 2.
+  // pass 1: reverse sub-tile aggregates (the forward's saved entry states
+  // give each sub-tile's forward entry).  With one sub-tile (S == 1) the
+  // drive, the loaded values and the warp exchange stay for pass 2.
   float2 Xrtile = cz(), pw = cone();
   float2 x[K], xp, b[K], go[K];
 #pragma unroll 1
   for (int s = 0; s < S; ++s) {
     const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
-    btf_drive<K, DRIVE, S == 1>(a, base, tw, fv, c2, t1, x, xp, b);
-    btf_load_go<K>(a, base, tw, fv, S == 1, go);
     float2 y = cz(), h = cz();
+    if constexpr (S == 1) {
+      btf_drive<K, DRIVE, true>(a, base, tw, fv, c2, t1, x, xp, b);
 #pragma unroll
-    for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
+      for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
+    }
+    btf_load_go<K>(a, base, tw, fv, S == 1, go);
 #pragma unroll
     for (int k = K - 1; k >= 0; --k) h = c_fma(mu, h, go[k]);
     s_yh[s & 1][warp][lane] = make_float4(y.x, y.y, h.x, h.y);
     __syncthreads();
-    // sub-tile totals: forward by warp 0, reverse by warp 1 (tile total kept
-    // by warp 1 and handed to warp 0 through s_D below)
-    if (warp == 0) {
-      float2 X = cz();
-#pragma unroll
-      for (int w = 0; w < NW; ++w) {
-        const float4 q = s_yh[s & 1][w][lane];
-        X = c_fma(gK, X, make_float2(q.x, q.y));
-      }
-      s_subf[s][lane] = X;
-    } else if (warp == 1) {
+    // reverse sub-tile totals by warp 1 (the tile total handed to warp 0
+    // through s_D below)
+    if (warp == 1) {
       float2 Xr = cz();
 #pragma unroll
       for (int w = NW - 1; w >= 0; --w) {
@@ -324,12 +321,8 @@ __global__ void __launch_bounds__(NW * 32) btf_bwd_kernel(const BtfArgs a) {
   }
   __syncthreads();
 
-  // sub-tile entry states: forward C_s from the tile carry, reverse D_s (the
+  // sub-tile entry states: forward C_s saved by the forward, reverse D_s (the
   // adjoint entering sub-tile s from its right) from the look-back
-  float2 Cs[S];
-  Cs[0] = C;
-#pragma unroll
-  for (int s = 1; s < S; ++s) Cs[s] = c_fma(gL, Cs[s - 1], s_subf[s - 1][lane]);
   float2 Ds = s_D[lane];
 
   // pass 2: sub-tiles from last to first.  The element-wise products run on
@@ -362,7 +355,10 @@ __global__ void __launch_bounds__(NW * 32) btf_bwd_kernel(const BtfArgs a) {
       const float4 q = s_yh[s & 1][w][lane];
       Xrw = c_fma(muK, Xrw, make_float2(q.z, q.w));
     }
-    float2 e = c_fma(Gw, Cs[s], Xw);
+    const float2 Cs = (fv && tile0 + (int64_t)s * L < a.T)
+                          ? a.carries[row * a.csub + (int64_t)j * S + s]
+                          : cz();
+    float2 e = c_fma(Gw, Cs, Xw);
     float2 yprev[K];
 #pragma unroll
     for (int k = 0; k < K; ++k) {
@@ -419,14 +415,13 @@ __global__ void __launch_bounds__(NW * 32) btf_bwd_kernel(const BtfArgs a) {
 }
 
 // TBPTT(1) surrogate backward in (B,T,F) layout (no temporal adjoint).  One
-// CTA per (tile, chain) in blockIdx order; pass 1 forms the forward sub-tile
-// aggregates so that pass 2 can start every sub-tile from its entry state.
+// CTA per (tile, chain) in blockIdx order; every sub-tile starts from the
+// entry state the forward saved for it, so one pass suffices.
 template <int NW, int K, int S, bool FUSE_ACT>
 __global__ void __launch_bounds__(NW * 32) btf_tbptt_bwd_kernel(const BtfArgs a) {
   constexpr int L = NW * K;
   static_assert(L == kBtfSub, "sub-tile length");
   __shared__ float2 s_y[2][NW][32];
-  __shared__ float2 s_sub[S][32];
   __shared__ float2 s_first[2][NW + 1][32];
   __shared__ float2 s_red[3][NW][32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -439,49 +434,26 @@ __global__ void __launch_bounds__(NW * 32) btf_tbptt_bwd_kernel(const BtfArgs a)
   const float2 lam = fv ? a.c1[f] : cz();
   const float2 t0 = fv ? a.c2[f] : cz();
   const float2 t1 = fv ? a.tap1[f] : cz();
-  const float2 C = fv ? a.carries[row * a.ntiles + j] : cz();
   const int64_t base = bi * a.T * a.F + f;
   const int64_t tile0 = (int64_t)j * S * L;
   const float2 *xs = static_cast<const float2 *>(a.x);
   const float2 gK = c_pow2k(lam, ilog2(K));
-  const float2 gL = c_pow2k(lam, kBtfLog2Sub);
   float2 Gw = cone();
   for (int w = 0; w < warp; ++w) Gw = c_mul(gK, Gw);
 
-  // pass 1: forward sub-tile aggregates (S > 1 only)
-  if constexpr (S > 1) {
-#pragma unroll 1
-    for (int s = 0; s < S - 1; ++s) {
-      const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
-      float2 x[K], xp, b[K];
-      btf_drive<K, kTwoTap, false>(a, base, tw, fv, t0, t1, x, xp, b);
-      float2 y = cz();
-#pragma unroll
-      for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
-      s_y[s & 1][warp][lane] = y;
-      __syncthreads();
-      if (warp == 0) {
-        float2 X = cz();
-#pragma unroll
-        for (int w = 0; w < NW; ++w) X = c_fma(gK, X, s_y[s & 1][w][lane]);
-        s_sub[s][lane] = X;
-      }
-    }
-    __syncthreads();
-  }
-
-  float2 es = C;
-  float2 acc_c1 = cz(), acc_t0 = cz(), acc_t1 = cz();
+  // element-wise products on paired fp32 FMAs, as in btf_bwd_kernel
+  const float2 T0X = make_float2(t0.x, t0.x), T0Y = make_float2(t0.y, -t0.y);
+  const float2 T1X = make_float2(t1.x, t1.x), T1Y = make_float2(t1.y, -t1.y);
+  float2 pc1 = cz(), qc1 = cz(), p0 = cz(), q0 = cz(), p1 = cz(), q1 = cz();
 #pragma unroll 1
   for (int s = 0; s < S; ++s) {
     const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
+    const float2 es = (fv && tile0 + (int64_t)s * L < a.T)
+                          ? a.carries[row * a.csub + (int64_t)j * S + s]
+                          : cz();
     float2 x[K], xp, b[K], go[K];
     btf_drive<K, kTwoTap, true>(a, base, tw, fv, t0, t1, x, xp, b);
-#pragma unroll
-    for (int k = 0; k < K; ++k) {
-      const int64_t t = tw + k;
-      go[k] = (fv && t < a.T) ? __ldcs(a.gout + base + t * a.F) : cz();
-    }
+    btf_load_go<K>(a, base, tw, fv, true, go);
     float2 y = cz();
 #pragma unroll
     for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
@@ -513,27 +485,31 @@ __global__ void __launch_bounds__(NW * 32) btf_tbptt_bwd_kernel(const BtfArgs a)
     }
     __syncthreads();
     const float2 gn = s_first[s & 1][warp + 1][lane];
+    const bool full = fv && tw + K <= a.T;
+    int64_t idx = base + tw * a.F;
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
+    for (int k = 0; k < K; ++k, idx += a.F) {
       const float2 g = go[k];
       const float2 g1 = (k + 1 < K) ? go[k + 1] : gn;
-      const int64_t t = tw + k;
-      if (fv && t < a.T) {
-        __stcs(static_cast<float2 *>(a.out) + base + t * a.F, c_cfma(t0, g, cz()));
-        __stcs(a.out2 + base + t * a.F, c_cfma(t1, g1, cz()));
+      const float2 gs = c_swap(g), g1s = c_swap(g1);
+      if (full || (fv && tw + k < a.T)) {
+        __stcs(static_cast<float2 *>(a.out) + idx, __ffma2_rn(T0X, g, __fmul2_rn(T0Y, gs)));
+        __stcs(a.out2 + idx, __ffma2_rn(T1X, g1, __fmul2_rn(T1Y, g1s)));
       }
-      acc_c1 = c_cfma(yprev[k], g, acc_c1);
-      acc_t0 = c_cfma(x[k], g, acc_t0);
-      acc_t1 = c_cfma(k > 0 ? x[k - 1] : xp, g, acc_t1);
-    }
-    if (s + 1 < S) {
-      // entry of the next sub-tile: the state after this one
-      if constexpr (S > 1) es = c_fma(gL, es, s_sub[s][lane]);
+      const float2 gx = make_float2(g.x, g.x), gy = make_float2(g.y, g.y);
+      pc1 = __ffma2_rn(yprev[k], gx, pc1);
+      qc1 = __ffma2_rn(yprev[k], gy, qc1);
+      p0 = __ffma2_rn(x[k], gx, p0);
+      q0 = __ffma2_rn(x[k], gy, q0);
+      const float2 xk1 = k > 0 ? x[k - 1] : xp;
+      p1 = __ffma2_rn(xk1, gx, p1);
+      q1 = __ffma2_rn(xk1, gy, q1);
     }
   }
-  s_red[0][warp][lane] = acc_c1;
-  s_red[1][warp][lane] = acc_t0;
-  s_red[2][warp][lane] = acc_t1;
+  // conj(v) g = (v.x g.x + v.y g.y, v.x g.y - v.y g.x)
+  s_red[0][warp][lane] = make_float2(pc1.x + qc1.y, qc1.x - pc1.y);
+  s_red[1][warp][lane] = make_float2(p0.x + q0.y, q0.x - p0.y);
+  s_red[2][warp][lane] = make_float2(p1.x + q1.y, q1.x - p1.y);
   __syncthreads();
   if (warp < 3 && fv) {
     float2 sum = cz();

@@ -328,6 +328,8 @@ bs::BtfArgs btfs_args(const float *c1, const float *c2, const float *tap1, const
   a.out = out;
   a.out2 = reinterpret_cast<float2 *>(out2);
   a.carries = reinterpret_cast<float2 *>(carries);
+  a.csub = (int)btf_nsub(T);  // row stride of the carry buffer: 64-step sub-tiles, so every
+                              // 128-step one that starts before T has a slot
   a.B = B;
   a.T = T;
   a.F = F;
