@@ -78,7 +78,8 @@ int rqf_selftest_lookback_timeout(void *scratch, rqf_stream_t stream);
 /* ---- sizes of saved context and scratch ------------------------------ */
 /* BTF kernels: rows = batch * filters.  Two kernel families share the
  * buffers: a streaming one (tiles of 1..8 x 128 steps, re-read from L2 in a
- * second pass) for few chains of batch x 32 channels, and a tile-resident one
+ * second pass, entry states saved per 128-step sub-tile) for few chains of
+ * batch x 32 channels, and a tile-resident one
  * (tiles of 1..4 x 64 steps held in shared memory, entry states saved per
  * 64-step sub-tile) for many.  rqf_btf_num_tiles gives the 64-step sub-tiles
  * along time (an upper bound on the tiles of either family); size buffers
@@ -252,6 +253,17 @@ int rqf_tbptt1_two_tap_backward(int layout, const float *c1, const float *tap0,
                                 void *scratch, int64_t d0, int64_t d1,
                                 int64_t d2, int fuse_act, int path,
                                 rqf_stream_t stream);
+/* The same (F,B,T) backward writing grad_zsum = grad_z + grad_zw in place of
+ * grad_zw: the operand of the weight cotangent when both taps come from one
+ * projection (the lag source zw is the same W h as z, pure.py:184-187, so
+ * grad W = (grad_z + grad_zw) h^H), which saves the caller an element-wise
+ * pass.  grad_z is still written (the input cotangent W^H grad_z needs it). */
+int rqf_fbt_tbptt1_backward_wsum(const float *c1, const float *tap0, const float *tap1,
+                                 const float *z, const float *carries, const float *grad_out,
+                                 float *grad_z, float *grad_zsum, float *grad_c1,
+                                 float *grad_tap0, float *grad_tap1, void *scratch,
+                                 int64_t filters, int64_t batch, int64_t time, int fuse_act,
+                                 rqf_stream_t stream);
 
 /* ---- selective (input-dependent ZOH) scan, (F,B,T) layout ------------ *
  * Replaces rqf_models/ops/selective_scan_kernel.py:selective_forward (:491) /

@@ -447,14 +447,21 @@ __global__ void __launch_bounds__(NT, 3) fbt_tbptt_rows_kernel(const FbtArgs a) 
 #pragma unroll
     for (int k = 0; k < K; ++k) {
       dz[k] = c_cfma(t0c, go[k], cz());
-      dzw[k] = c_cfma(t1c, k + 1 < K ? go[k + 1] : gn, cz());
+      dzw[k] = c_cfma(t1c, k + 1 < K ? go[k + 1] : gn, a.wsum ? dz[k] : cz());
     }
-    if (tid == 0 && pc.j > 0) __stcs(a.out2 + roff + tile0 - 1, c_cfma(t1c, go[0], cz()));
+    // The lag tap of the tile before's last sample.  With wsum that tile
+    // stored its grad_z there (the same CTA, ordered by the loop's barrier),
+    // so this adds to it.
+    if (tid == 0 && pc.j > 0)
+      __stcs(a.out2 + roff + tile0 - 1,
+             c_cfma(t1c, go[0], a.wsum ? __ldcg(a.out2 + roff + tile0 - 1) : cz()));
     fbt_store_tile<K>(gbuf, dz, a.out + roff, tile0 + wofs, T, lane);
     // grad_zw staged through the z region (every warp has read its z samples
     // before the scan barrier).  The tile's last sample needs g of the next
     // tile: unless this is the row's last tile, only the first half of that
-    // pair is stored here and the next tile stores the other.
+    // pair is stored here and the next tile stores the other (with wsum the
+    // whole pair is stored, the last sample holding its grad_z, which the
+    // next tile completes).
     const int last = tile0 + L - 1;
 #pragma unroll
     for (int m = 0; m < K / 2; ++m)
@@ -466,7 +473,7 @@ __global__ void __launch_bounds__(NT, 3) fbt_tbptt_rows_kernel(const FbtArgs a) 
       const int t = tile0 + wofs + 2 * (v * 32 + lane);
       if (t >= T) continue;
       const float4 q = zbuf[swz<K>(v * 32 + lane)];
-      if (t + 1 == last && pc.j + 1 < ntiles)
+      if (t + 1 == last && pc.j + 1 < ntiles && !a.wsum)
         __stcs(a.out2 + roff + t, make_float2(q.x, q.y));
       else
         st_stream4(a.out2 + roff + t, q);

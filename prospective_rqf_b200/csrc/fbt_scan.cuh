@@ -31,7 +31,8 @@ struct FbtArgs {
   const float2 *gout;              // (rows, T) cotangent (backward)
   const float2 *skip;              // (rows, T) added to the forward output, or null
   float2 *out;                     // forward: act / raw; backward: grad_z
-  float2 *out2;                    // TBPTT backward: grad_zw
+  float2 *out2;                    // TBPTT backward: grad_zw, or grad_z + grad_zw with wsum
+  int wsum;                        // TBPTT backward: out2 = grad_z + grad_zw (the weight's operand)
   float2 *carries;                 // entry states, see kFbtSlots
   float2 *partials;                // (rows, ntiles, 3)
   u64 *flags;                      // (rows, ntiles, 2)
@@ -400,7 +401,7 @@ __global__ void __launch_bounds__(NT) fbt_tbptt_bwd_kernel(const FbtArgs a) {
     const float2 g = go[k];
     const float2 g1 = (k + 1 < K) ? go[k + 1] : gn;
     dz[k] = c_cfma(t0, g, cz());
-    dzw[k] = c_cfma(t1, g1, cz());
+    dzw[k] = c_cfma(t1, g1, a.wsum ? dz[k] : cz());
     acc_c1 = c_cfma(yprev[k], g, acc_c1);
     acc_t0 = c_cfma(z[k], g, acc_t0);
     acc_t1 = c_cfma(k > 0 ? z[k - 1] : zp, g, acc_t1);

@@ -154,6 +154,7 @@ FbtArgs fbt_args(const float *c1, const float *tap0, const float *tap1, const fl
   a.skip = nullptr;
   a.out = reinterpret_cast<float2 *>(out);
   a.out2 = reinterpret_cast<float2 *>(out2);
+  a.wsum = 0;
   a.carries = reinterpret_cast<float2 *>(carries);
   a.rows = F * B;
   a.T = T;
@@ -789,13 +790,15 @@ int rqf_fbt_prospective_backward(const float *c1, const float *tap0, const float
 }
 
 // ------------------------------------------------------------ TBPTT(1)
-int rqf_tbptt1_two_tap_backward(int layout, const float *c1, const float *tap0,
+// wsum (layout 1 only): grad_zw receives grad_z + grad_zw.
+static int tbptt1_backward_impl(int layout, const float *c1, const float *tap0,
                                 const float *tap1, const float *z, const float *carries,
                                 const float *grad_out, float *grad_z, float *grad_zw,
                                 float *grad_c1, float *grad_tap0, float *grad_tap1,
                                 void *scratch, int64_t d0, int64_t d1, int64_t d2, int fuse_act,
-                                int path, rqf_stream_t stream) {
+                                int path, rqf_stream_t stream, int wsum) {
   if (layout != 0 && layout != 1) return RQF_ERR_ARGUMENT;
+  if (wsum && layout != 1) return RQF_ERR_ARGUMENT;
   if (!btf_path_ok(path)) return RQF_ERR_ARGUMENT;
   const int64_t F = layout == 0 ? d2 : d0;
   const int64_t B = layout == 0 ? d0 : d1;
@@ -840,6 +843,7 @@ int rqf_tbptt1_two_tap_backward(int layout, const float *c1, const float *tap0,
   }
   FbtArgs a = fbt_args(c1, tap0, tap1, z, grad_out, grad_z, grad_zw, const_cast<float *>(carries),
                        scratch, F, B, T);
+  a.wsum = wsum ? 1 : 0;
   const bool vec = (T % 2 == 0) && aligned(z, 16) && aligned(grad_out, 16) &&
                    aligned(grad_z, 16) && aligned(grad_zw, 16);
   if (vec) {
@@ -877,6 +881,28 @@ int rqf_tbptt1_two_tap_backward(int layout, const float *c1, const float *tap0,
   return launch_status();
 }
 
+
+int rqf_tbptt1_two_tap_backward(int layout, const float *c1, const float *tap0,
+                                const float *tap1, const float *z, const float *carries,
+                                const float *grad_out, float *grad_z, float *grad_zw,
+                                float *grad_c1, float *grad_tap0, float *grad_tap1,
+                                void *scratch, int64_t d0, int64_t d1, int64_t d2, int fuse_act,
+                                int path, rqf_stream_t stream) {
+  return tbptt1_backward_impl(layout, c1, tap0, tap1, z, carries, grad_out, grad_z, grad_zw,
+                              grad_c1, grad_tap0, grad_tap1, scratch, d0, d1, d2, fuse_act, path,
+                              stream, 0);
+}
+
+int rqf_fbt_tbptt1_backward_wsum(const float *c1, const float *tap0, const float *tap1,
+                                 const float *z, const float *carries, const float *grad_out,
+                                 float *grad_z, float *grad_zsum, float *grad_c1,
+                                 float *grad_tap0, float *grad_tap1, void *scratch,
+                                 int64_t filters, int64_t batch, int64_t time, int fuse_act,
+                                 rqf_stream_t stream) {
+  return tbptt1_backward_impl(1, c1, tap0, tap1, z, carries, grad_out, grad_z, grad_zsum,
+                              grad_c1, grad_tap0, grad_tap1, scratch, filters, batch, time,
+                              fuse_act, 0, stream, 1);
+}
 }  // extern "C"
 
 // ------------------------------------------------------------ selective

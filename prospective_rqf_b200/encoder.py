@@ -181,29 +181,31 @@ class RQFCoefficients(nn.Module):
 
 
 class _TBPTTLayer(torch.autograd.Function):
-    """z = W @ h, then the TBPTT(1) two-tap scan in (F,B,T).  The lag-tap
+    """z = W @ h, then the TBPTT(1) two-tap scan in (F,B,T), with the skip
+    h_out = out + h fused into the scan's store when `skip`.  The lag-tap
     cotangent updates W only — the reference gets the same by feeding the lag
-    tap from a second GEMM W(x.detach()) (pure.py:184-187)."""
+    tap from a second GEMM W(x.detach()) (pure.py:184-187) — so the kernel
+    hands back gz + gzw for the weight cotangent, and the input cotangent is
+    W^H gz + g (g the skip's cotangent) in one accumulating GEMM."""
 
     @staticmethod
-    def forward(ctx, h, W, C1, tap0, tap1, fuse_act):
-        y, saved = _block_forward(W, h, C1, tap0, tap1, bool(fuse_act), None)
+    def forward(ctx, h, W, C1, tap0, tap1, fuse_act, skip=False):
+        y, saved = _block_forward(W, h, C1, tap0, tap1, bool(fuse_act), h if skip else None)
         ctx.save_for_backward(h, W, *saved)
-        ctx.fuse_act = bool(fuse_act)
+        ctx.fuse_act, ctx.skip = bool(fuse_act), bool(skip)
         return y
 
     @staticmethod
     @once_differentiable
     def backward(ctx, gy):
         h, W, *saved = ctx.saved_tensors
-        z = saved[3]
-        gc1, gt0, gt1, gz, gzw = ops._tbptt_backward(saved, "fbt", tuple(z.shape), gy,
-                                                     ctx.fuse_act)
-        F_in, B, T = h.shape
+        gc1, gt0, gt1, gz, gsum = ops._tbptt_backward_wsum(saved, gy, ctx.fuse_act)
         need = ctx.needs_input_grad
-        gh = _project(W, gz, conj_transpose=True) if need[0] else None
-        gW = _weight_grad(gz + gzw, h) if need[1] else None
-        return gh, gW, gc1, gt0, gt1, None
+        gh = None
+        if need[0]:
+            gh = _project(W, gz, conj_transpose=True, acc=ops._c64(gy) if ctx.skip else None)
+        gW = _weight_grad(gsum, h) if need[1] else None
+        return gh, gW, gc1, gt0, gt1, None, None
 
 
 class _PureBlock(torch.autograd.Function):
@@ -342,8 +344,9 @@ class _InputTBPTT(torch.autograd.Function):
     """The input projection and the first TBPTT(1) layer together, with the
     skip add (the TBPTT counterpart of _InputBlock; pure.py:184-187 for the
     lag tap).  z0 = (W w_in) x (+ W b_in) from rqf_lowrank_drive, the TBPTT(1)
-    scan, then out = y + h0.  With G = gz0 [x; 1]^T and Gw = gzw [x; 1]^T:
-      gW = (gz0 + gzw) h0^H = (G + Gw) [w_in, b_in]^T
+    scan, then out = y + h0.  With G = gz0 [x; 1]^T and Gs = (gz0 + gzw) [x; 1]^T
+    (the kernel returns gz0 + gzw):
+      gW = (gz0 + gzw) h0^H = Gs [w_in, b_in]^T
       grad [w_in, b_in] = Re(W^H G + g [x; 1]^T)   (the lag cotangent updates W only)."""
 
     @staticmethod
@@ -361,16 +364,14 @@ class _InputTBPTT(torch.autograd.Function):
     @once_differentiable
     def backward(ctx, g):
         x_cf, w_in, b_in, W, *saved = ctx.saved_tensors
-        z = saved[3]
-        gc1, gt0, gt1, gz, gzw = ops._tbptt_backward(saved, "fbt", tuple(z.shape), g,
-                                                     ctx.fuse_act)
+        gc1, gt0, gt1, gz, gsum = ops._tbptt_backward_wsum(saved, g, ctx.fuse_act)
         need = ctx.needs_input_grad
         I, has_b = w_in.shape[1], b_in is not None
         G = ops.rowdot(gz, x_cf, with_sum=has_b)
         gW = gw_in = gb_in = None
         if need[3]:
             rows = torch.cat([w_in, b_in[:, None]], dim=1) if has_b else w_in
-            gW = (G + ops.rowdot(gzw, x_cf, with_sum=has_b)) @ rows.t().to(torch.complex64)
+            gW = ops.rowdot(gsum, x_cf, with_sum=has_b) @ rows.t().to(torch.complex64)
         if need[1] or need[2]:
             gh = W.mH @ G
             if ctx.skip:
@@ -435,8 +436,7 @@ class PureRQFEncoderB200(nn.Module):
         if self.scan_grad_mode == "tbptt1":
             for i, act, skip in zip(blocks, acts, skips):
                 c1, t0, t1 = coeffs[i]
-                out = _TBPTTLayer.apply(h, self.W[i], c1, t0, t1, act)
-                h = out + h if skip else out
+                h = _TBPTTLayer.apply(h, self.W[i], c1, t0, t1, act, skip)
         elif len(blocks) > 0:
             h = _PureStack.apply(h, acts, skips, *(self.W[i] for i in blocks),
                                  *(coeffs[i][0] for i in blocks), *(coeffs[i][1] for i in blocks),

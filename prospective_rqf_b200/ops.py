@@ -591,6 +591,29 @@ def _tbptt_backward(saved, layout, dims, grad_output, fuse_act, path=0):
     return gc1, gt0, gt1, gz, gzw
 
 
+def _tbptt_backward_wsum(saved, grad_output, fuse_act):
+    """The (F,B,T) TBPTT(1) surrogate VJP with the two tap cotangents also
+    summed (rqf_fbt_tbptt1_backward_wsum): (gc1, gtap0, gtap1, gz, gz + gzw),
+    for a lag source that is the same projection as z."""
+    c1, t0, t1, z, carries = saved
+    F, B, T = z.shape
+    dev = z.device
+    gy = _c64(grad_output)
+    lib = _abi.load()
+    gz = torch.empty_like(z)
+    gsum = torch.empty_like(z)
+    gc1, gt0, gt1 = torch.empty_like(c1), torch.empty_like(t0), torch.empty_like(t1)
+    scratch = _scratch(lib.rqf_fbt_scratch_bytes(F, B, T), dev)
+    with _timing.launch("rqf_tbptt1_two_tap_backward", F * B * T, _nbytes(z, gy, gz, gsum)):
+        _abi.check(lib.rqf_fbt_tbptt1_backward_wsum(
+            _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1), _abi.ptr(z), _abi.ptr(carries),
+            _abi.ptr(gy), _abi.ptr(gz), _abi.ptr(gsum), _abi.ptr(gc1), _abi.ptr(gt0),
+            _abi.ptr(gt1), _abi.ptr(scratch), F, B, T, int(bool(fuse_act)),
+            _abi.stream_of(gy)), "rqf_fbt_tbptt1_backward_wsum")
+    _done(dev)
+    return gc1, gt0, gt1, gz, gsum
+
+
 def tbptt1_two_tap_scan(u, C1, tap0, tap1, *, delayed_u=None, layout: str = "btf",
                         fuse_act: bool = False):
     """TBPTT(1) two-tap scan: forward value of the exact recurrence

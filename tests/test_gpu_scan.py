@@ -417,6 +417,32 @@ def test_tbptt_fbt_persistent_rows_vs_oracle(T, fuse):
         assert_close(host(t.grad), r, GRAD_TOL, k)
 
 
+@pytest.mark.parametrize("F,B,T", [(40, 16, 5000), (40, 16, 4096), (3, 2, 5001), (3, 2, 2049)])
+@pytest.mark.parametrize("fuse", [False, True])
+def test_tbptt_fbt_wsum_matches_separate_outputs(F, B, T, fuse):
+    """rqf_fbt_tbptt1_backward_wsum (grad_z and grad_z + grad_zw) against
+    rqf_tbptt1_two_tap_backward on the same saved context: grad_z and the
+    coefficient gradients equal, the sum equal to the two outputs added (at
+    fp32 rounding), over the persistent row kernel (640 rows, whose tiles
+    complete the sum across their boundary) and the per-tile kernel (6 rows),
+    T cut inside a tile and T a multiple of it."""
+    from prospective_rqf_b200 import ops
+
+    rng = np.random.default_rng(4100 + F + T + int(fuse))
+    c1 = coeffs(rng, F)
+    t0, t1 = c64(crandn(rng, F, 0.5)), c64(crandn(rng, F, 0.5))
+    z = dev(c64(crandn(rng, (F, B, T))))
+    gy = dev(c64(crandn(rng, (F, B, T))))
+    c1d, t0d, t1d = dev(c1), dev(t0), dev(t1)
+    _, saved = ops._fbt_forward(c1d, t0d, t1d, z, fuse)
+    a = ops._tbptt_backward(saved, "fbt", (F, B, T), gy, fuse)
+    b = ops._tbptt_backward_wsum(saved, gy, fuse)
+    for x, y_, name in zip(a[:4], b[:4], ("gc1", "gt0", "gt1", "gz")):
+        assert torch.equal(x, y_), name
+    assert_close(host(b[4]), host(a[3]) + host(a[4]), 1e-6, "gz + gzw")
+    rqf().check_device_errors()
+
+
 # ------------------------------------------------------- edge cases
 def test_empty_shapes_give_zero_grads():
     for shape in [(0, 10, 4), (2, 0, 4)]:
