@@ -108,10 +108,10 @@ struct ProjLayout {
   static constexpr int kWarpStaging = kScan ? kScanWarpStaging : kStagingBytes / 4;
   static constexpr int kRingBytes = kScan == kScanBwd ? 4 * kRingWarpBytes : 0;
   // scan modes: staging, ring, barriers; otherwise barriers then staging
-  static constexpr int kStagingOff =
-      kScan ? kStages * kStageBytes : kStages * kStageBytes + kBarBytes;
+  // staging (1024-byte aligned for the TMA tensor stores), ring, barriers
+  static constexpr int kStagingOff = kStages * kStageBytes;
   static constexpr int kRingOff = kStages * kStageBytes + 4 * kWarpStaging;
-  static constexpr int kBarOff = kScan ? kRingOff + kRingBytes : kStages * kStageBytes;
+  static constexpr int kBarOff = kRingOff + kRingBytes;
   static constexpr int kSmemBytes =
       kStages * kStageBytes + kBarBytes + 4 * kWarpStaging + kRingBytes + 1024;  // + alignment slack
 };
@@ -146,6 +146,10 @@ struct Params {
   // Scan mode (proj_kernel<false, true>): the epilogue also runs the Pure RQF
   // block's two-tap scan along each output row (see ScanParams).
   int scan;
+  // Accumulate in place (complex X, out == acc): the epilogue adds its tile
+  // into out with a TMA reduce-add through ScanParams::tmZ (out as M rows x
+  // 2N floats) instead of loading acc, so no epilogue warp waits on it.
+  int inplace;
 };
 
 // The block scan fused into the projection's epilogue: out row j of the
@@ -271,6 +275,16 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void 
                    reinterpret_cast<uint64_t>(map)),
                "r"(smem_u32(src)), "r"(x), "r"(y)
                : "memory");
+}
+// TMA tensor reduce of a shared-memory box into global memory: element-wise
+// fp32 add (each element of the box is added once).
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, const void *src, int x,
+                                                  int y) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y)
+      : "memory");
 }
 __device__ __forceinline__ void bulk_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
@@ -1259,6 +1273,28 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       const long long jw0 = ((long long)mp * kPairM + (long long)rank * kBM + quarter * 32) >> 1;
       const int r_own = lane >> 1;
       const int iters = 16 * kpr / 32;             // 16-byte pieces per lane per chunk
+      if (p.acc != nullptr && lane < 16) {
+        // Into L2: this warp's 16 rows of acc for its next tile (and, on the
+        // pair's first tile, for this one), so that the chunk loads below hit
+        // L2 instead of waiting on HBM.
+        const int bytes = (p.real_x ? kBN : kBN / 2) * 8;
+        for (int ahead = (tile < npairs) ? 0 : 1; ahead < 2; ++ahead) {
+          const long long t2 = tile + ahead * npairs;
+          if (t2 >= p.num_tiles) break;
+          int mp2, nt2;
+          tile_coords(t2, p, mp2, nt2);
+          const long long j2 =
+              (((long long)mp2 * kPairM + (long long)rank * kBM + quarter * 32) >> 1) + lane;
+          const long long n2 = p.real_x ? (long long)nt2 * kBN : (long long)nt2 * (kBN / 2);
+          if (j2 < p.M && n2 < p.N) {
+            const long long left = (p.N - n2) * 8;
+            const int nb = (int)(left < bytes ? left : bytes);  // N is even: a multiple of 16
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.acc + j2 * p.N + n2),
+                         "r"(nb)
+                         : "memory");
+          }
+        }
+      }
 #pragma unroll 1
       for (int c = 0; c < kBN / 32; ++c) {
         const long long nbase = p.real_x ? (long long)nt * kBN + c * 32
@@ -1304,6 +1340,27 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             const float pi_im = odd ? v[16 + 2 * t + 1] : r[2 * t + 1];
             z[t] = make_float2(pr_re - pi_im, pr_im + pi_re);
           }
+          if (p.inplace) {
+            // two 2 KB halves in turn; a half is reused once the reduce that
+            // read it two chunks ago has finished reading
+            float4 *st2 = stage + (c & 1) * 128;
+            if (lane == 0) bulk_wait_read<1>();
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int k = (odd ? 4 : 0) + q;
+              st2[r_own * 8 + (k ^ (r_own & 7))] =
+                  make_float4(z[2 * q].x, z[2 * q].y, z[2 * q + 1].x, z[2 * q + 1].y);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              // a box wholly past N is skipped; a partial one is clipped by the map
+              if (jw0 < p.M && nbase < p.N) tma_reduce_add_2d(&sp.tmZ, st2, (int)(2 * nbase), (int)jw0);
+              bulk_commit();
+            }
+            continue;
+          }
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const int k = (odd ? 4 : 0) + q;
@@ -1337,7 +1394,7 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         acc_phase ^= 1u;
       }
     }
-    if constexpr (kScan) {  // the TMA stores of this warp complete before the CTA exits
+    if (kScan || p.inplace) {  // the TMA stores of this warp complete before the CTA exits
       if (lane == 0) bulk_wait<0>();
       __syncwarp();
     }

@@ -1298,6 +1298,17 @@ int projection_impl(const float *w, const float *x, const float *acc, float *out
   const long long grid = 2 * (p.num_tiles < pairs ? p.num_tiles : pairs);  // whole CTA pairs
   p.out_real = nullptr;
   p.scan = scan ? 1 : 0;
+  // out == acc (complex x): the epilogue adds into out with TMA reduces
+  // instead of loading acc
+  p.inplace = (!scan && !real_x && acc != nullptr && acc == out) ? 1 : 0;
+  proj::ScanParams plain_sp{};
+  if (p.inplace) {
+    p.acc = nullptr;
+    const uint64_t nf = 2 * (uint64_t)n;
+    if (!encode_map_2d(&plain_sp.tmZ, out, nf, (uint64_t)m, nf * sizeof(float), 32, 16,
+                       CU_TENSOR_MAP_SWIZZLE_128B))
+      return RQF_ERR_LAUNCH;
+  }
   if (scan) {
     // Every CTA pair must be resident at once: a tile's epilogue waits for
     // the tile before it along time, which another pair may hold.  The
@@ -1312,7 +1323,7 @@ int projection_impl(const float *w, const float *x, const float *acc, float *out
           <<<(unsigned)grid, proj::kThreads, proj::kScanSmemBytes, st>>>(tmA, tmX, p, sp);
   } else {
     proj::proj_kernel<false><<<(unsigned)grid, proj::kThreads, proj::kSmemBytes, st>>>(
-        tmA, tmX, p, proj::ScanParams{});
+        tmA, tmX, p, plain_sp);
   }
   return launch_status();
 }
@@ -1547,6 +1558,7 @@ int rqf_projection_real_out(const float *w, const float *x, float *out, int64_t 
   p.real_x = 0;
   const long long grid = 2 * (p.num_tiles < pairs ? p.num_tiles : pairs);
   p.scan = 0;
+  p.inplace = 0;
   proj::proj_kernel<true><<<(unsigned)grid, proj::kThreads, proj::ProjLayout<true>::kSmemBytes,
                             st>>>(tmA, tmX, p, proj::ScanParams{});
   return launch_status();

@@ -84,10 +84,12 @@ def _weight_grad(gz, h):
     return gz.reshape(gz.shape[0], -1) @ h.reshape(h.shape[0], -1).mH
 
 
-def _project(W, h, conj_transpose=False, acc=None):
-    """op(W) @ h (+ acc) over the (d, batch*time) view of an (d, B, T) tensor."""
+def _project(W, h, conj_transpose=False, acc=None, inplace=False):
+    """op(W) @ h (+ acc) over the (d, batch*time) view of an (d, B, T) tensor;
+    with `inplace` the sum may be accumulated into acc (which the caller
+    gives up)."""
     if PROJECTION == "tc" and h.is_cuda:
-        return ops.projection(W, h, conj_transpose, acc)
+        return ops.projection(W, h, conj_transpose, acc, inplace)
     d, B, T = h.shape
     opw = W.mH if conj_transpose else W
     if acc is None:
@@ -282,7 +284,8 @@ class _PureStack(torch.autograd.Function):
                 g, vjp = ops.projection_block_scan_backward(Ws[i], gz, acc, saved[i - 1],
                                                             ctx.acts[i - 1])
             elif i > 0 or need[0]:
-                g = _project(Ws[i], gz, conj_transpose=True, acc=acc)
+                # after the top block, g is this backward's own buffer: sum into it
+                g = _project(Ws[i], gz, conj_transpose=True, acc=acc, inplace=i < m - 1)
                 if i > 0:
                     vjp = ops._fbt_backward(saved[i - 1], g, ctx.acts[i - 1])
             if need[3 + i]:

@@ -1074,13 +1074,16 @@ def selective_layer_scan(x, weight, inputs, *, truncated: bool = False, activate
 
 # ------------------------------------------------ complex projection GEMM
 def projection(W: torch.Tensor, x: torch.Tensor, conj_transpose: bool = False,
-               acc: torch.Tensor | None = None) -> torch.Tensor:
+               acc: torch.Tensor | None = None, inplace: bool = False) -> torch.Tensor:
     """out = op(W) @ x (+ acc) with x (K, ...) complex64, the trailing dims
     flattened to N: the Pure RQF block projection z = W h
     (rqf_models/backbones/rqf/pure.py:223, torch.matmul on the
     (d_model, batch*time) view) when op(W) = W with W (M, K), and its input
     cotangent W^H gz when ``conj_transpose`` (W is then (K, M)).  ``acc``
-    (M, ...) is added in the epilogue (the skip cotangent).
+    (M, ...) is added in the epilogue (the skip cotangent); with ``inplace``
+    the result is accumulated into ``acc`` itself when it is a contiguous
+    complex64 tensor, by TMA reduce-adds (the epilogue reads no acc), and
+    ``acc`` is returned.
 
     Runs the split-TF32 tcgen05 GEMM of rqf_projection (fp32-comparable;
     not differentiable itself — the callers own the autograd).  An odd N,
@@ -1111,7 +1114,10 @@ def projection(W: torch.Tensor, x: torch.Tensor, conj_transpose: bool = False,
         out = (opw @ xx.reshape(K, N)).reshape(out_shape)
         return out if a is None else out.add_(a)
     lib = _abi.load()
-    out = torch.empty(out_shape, dtype=torch.complex64, device=dev)
+    if inplace and a is not None and a is acc:  # acc already contiguous complex64
+        out = a
+    else:
+        out = torch.empty(out_shape, dtype=torch.complex64, device=dev)
     ws = _scratch(lib.rqf_projection_workspace_bytes(M, K), dev)
     with _timing.launch("rqf_projection", M * N, _nbytes(xx, out, a), 8 * M * K * N):
         _abi.check(lib.rqf_projection(

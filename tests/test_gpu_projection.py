@@ -75,6 +75,36 @@ def test_projection_accumulate_and_alias(conj):
     assert_close(out.cpu().numpy().astype(np.complex128), ref, PROJ_TOL, "W x + acc")
 
 
+# (M, K, N): ragged M (rows past M in the last pair tile), ragged N (a
+# partial last tile), several tiles per pair, and the config-5 layer shape.
+INPLACE_SHAPES = [(96, 64, 3 * 700), (37, 50, 1000), (256, 256, 4 * 4096), (256, 256, 32 * 16000)]
+
+
+@pytest.mark.parametrize("M,K,N", INPLACE_SHAPES)
+@pytest.mark.parametrize("conj", [False, True])
+def test_projection_inplace_accumulate(M, K, N, conj):
+    """ops.projection(..., acc, inplace=True): the epilogue adds its tiles into
+    acc with TMA reduce-adds.  The result is the out-of-place W x + acc (one
+    fp32 add per element in either path), and acc is the tensor returned."""
+    from prospective_rqf_b200 import ops
+
+    g = torch.Generator(device="cuda").manual_seed(M + K + N + int(conj))
+    shape = (K, M) if conj else (M, K)
+    W = torch.randn(*shape, dtype=torch.complex64, device="cuda", generator=g) / np.sqrt(2 * K)
+    x = torch.randn(K, N, dtype=torch.complex64, device="cuda", generator=g)
+    acc = torch.randn(M, N, dtype=torch.complex64, device="cuda", generator=g)
+    want = ops.projection(W, x, conj, acc)
+    buf = acc.clone()
+    got = ops.projection(W, x, conj, buf, inplace=True)
+    assert got is buf
+    torch.cuda.synchronize()
+    err = rel_err(got.cpu().numpy(), want.cpu().numpy())
+    assert err <= 1e-7, f"in-place accumulate differs from W x + acc ({err:.2e})"
+    if N <= 4096:
+        assert_close(got.cpu().numpy().astype(np.complex128),
+                     _ref(W, x, conj, acc), PROJ_TOL, "in place vs fp64")
+
+
 def test_projection_full_layer_shape_vs_torch_fp32():
     """The config-5 layer shape (256 x 256, N = 32 x 16000): against an fp64
     GEMM on a column sample, and against torch's fp32 complex GEMM on all of it."""
