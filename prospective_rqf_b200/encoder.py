@@ -182,32 +182,51 @@ class RQFCoefficients(nn.Module):
         self.log_gamma.clamp_(*self._gamma_bounds)
 
 
-class _TBPTTLayer(torch.autograd.Function):
-    """z = W @ h, then the TBPTT(1) two-tap scan in (F,B,T), with the skip
-    h_out = out + h fused into the scan's store when `skip`.  The lag-tap
-    cotangent updates W only — the reference gets the same by feeding the lag
-    tap from a second GEMM W(x.detach()) (pure.py:184-187) — so the kernel
-    hands back gz + gzw for the weight cotangent, and the input cotangent is
-    W^H gz + g (g the skip's cotangent) in one accumulating GEMM."""
+class _TBPTTStack(torch.autograd.Function):
+    """Consecutive TBPTT(1) layers as one autograd node.  Each layer: z = W @ h,
+    the TBPTT(1) two-tap scan in (F,B,T), and the skip h_out = out + h fused
+    into the scan's store.  The lag-tap cotangent updates W only — the
+    reference gets the same by feeding the lag tap from a second GEMM
+    W(x.detach()) (pure.py:184-187) — so the kernel hands back gz + gzw for
+    the weight cotangent, and the input cotangent is W^H gz + g (g the skip's
+    cotangent) in one GEMM, accumulated into the backward's own cotangent
+    buffer after the top layer (ops.projection with inplace).  Arguments as
+    _PureStack's."""
 
     @staticmethod
-    def forward(ctx, h, W, C1, tap0, tap1, fuse_act, skip=False):
-        y, saved = _block_forward(W, h, C1, tap0, tap1, bool(fuse_act), h if skip else None)
-        ctx.save_for_backward(h, W, *saved)
-        ctx.fuse_act, ctx.skip = bool(fuse_act), bool(skip)
-        return y
+    def forward(ctx, h, acts, skips, *params):
+        m = len(acts)
+        Ws, c1s, t0s, t1s = (params[i * m:(i + 1) * m] for i in range(4))
+        inputs, saved = [], []
+        for i in range(m):
+            inputs.append(h)
+            h, sv = _block_forward(Ws[i], h, c1s[i], t0s[i], t1s[i], bool(acts[i]),
+                                   h if skips[i] else None)
+            saved.extend(sv)
+        ctx.save_for_backward(*inputs, *Ws, *saved)
+        ctx.acts, ctx.skips = tuple(map(bool, acts)), tuple(map(bool, skips))
+        return h
 
     @staticmethod
     @once_differentiable
-    def backward(ctx, gy):
-        h, W, *saved = ctx.saved_tensors
-        gc1, gt0, gt1, gz, gsum = ops._tbptt_backward_wsum(saved, gy, ctx.fuse_act)
+    def backward(ctx, g):
+        m = len(ctx.acts)
+        st = ctx.saved_tensors
+        inputs, Ws = st[:m], st[m:2 * m]
+        saved = [st[2 * m + 5 * i:2 * m + 5 * i + 5] for i in range(m)]
         need = ctx.needs_input_grad
-        gh = None
-        if need[0]:
-            gh = _project(W, gz, conj_transpose=True, acc=ops._c64(gy) if ctx.skip else None)
-        gW = _weight_grad(gsum, h) if need[1] else None
-        return gh, gW, gc1, gt0, gt1, None, None
+        gW, gc1, gt0, gt1 = ([None] * m for _ in range(4))
+        g = ops._c64(g)
+        for i in range(m - 1, -1, -1):
+            gc1[i], gt0[i], gt1[i], gz, gsum = ops._tbptt_backward_wsum(saved[i], g,
+                                                                        ctx.acts[i])
+            if need[3 + i]:
+                gW[i] = _weight_grad(gsum, inputs[i])
+            del gsum
+            if i > 0 or need[0]:
+                acc = g if ctx.skips[i] else None
+                g = _project(Ws[i], gz, conj_transpose=True, acc=acc, inplace=i < m - 1)
+        return (g if need[0] else None, None, None, *gW, *gc1, *gt0, *gt1)
 
 
 class _PureBlock(torch.autograd.Function):
@@ -436,14 +455,11 @@ class PureRQFEncoderB200(nn.Module):
         blocks = range(first, n)
         acts = tuple(self.final_activation or i + 1 < n for i in blocks)
         skips = tuple(self.skip and self.W[i].shape[0] == self.W[i].shape[1] for i in blocks)
-        if self.scan_grad_mode == "tbptt1":
-            for i, act, skip in zip(blocks, acts, skips):
-                c1, t0, t1 = coeffs[i]
-                h = _TBPTTLayer.apply(h, self.W[i], c1, t0, t1, act, skip)
-        elif len(blocks) > 0:
-            h = _PureStack.apply(h, acts, skips, *(self.W[i] for i in blocks),
-                                 *(coeffs[i][0] for i in blocks), *(coeffs[i][1] for i in blocks),
-                                 *(coeffs[i][2] for i in blocks))
+        if len(blocks) > 0:
+            stack = _TBPTTStack if self.scan_grad_mode == "tbptt1" else _PureStack
+            h = stack.apply(h, acts, skips, *(self.W[i] for i in blocks),
+                            *(coeffs[i][0] for i in blocks), *(coeffs[i][1] for i in blocks),
+                            *(coeffs[i][2] for i in blocks))
         return h
 
     @torch.no_grad()
