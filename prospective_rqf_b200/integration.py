@@ -18,6 +18,8 @@ Call sites served (reference paths):
   rqf_models/ops/fbt_scan_kernel.py:1005       -> fbt_layer0_real_scan (no caller in the reference)
   rqf_models/backbones/rqf/block.py:882, :904 -> TBPTT(1) fused surrogate on CUDA
   rqf_models/ops/selective_scan.py:119, :133   -> selective_forward / selective_backward
+  rqf_models/backbones/rqf/selective.py:78     -> the controller projection _SplitProjection
+                                                  (fp32 CUDA: tensor-core GEMMs)
   rqf_models/backbones/rqf/filter.py:510       -> RQF.compute_two_tap_coefficients on fp32
                                                   CUDA leaves (every caller: pure.py:225,
                                                   block.py's prospective paths, selective.py)
@@ -116,9 +118,25 @@ def _filter_coefficients(orig):
     return compute_two_tap_coefficients
 
 
+def _split_projection(orig):
+    """selective.py:_SplitProjection: fp32 CUDA operands take the tensor-core
+    form (ops._SplitProjection); others keep the reference's own Function."""
+    class _SplitProjection:
+        @staticmethod
+        def apply(v, weights, sizes):
+            if (v.is_cuda and v.dtype == torch.float32 and weights.dtype == torch.float32
+                    and v.dim() == 2 and v.shape[0] % 2 == 0):
+                return ops._SplitProjection.apply(v, weights, sizes)
+            return orig.apply(v, weights, sizes)
+
+    _SplitProjection.__wrapped__ = orig
+    return _SplitProjection
+
+
 # (module, attribute, wrapper of the original)
 _WRAPPED = [
     ("rqf_models.backbones.s5.layer", "parallel_scan", _cuda_parallel_scan),
+    ("rqf_models.backbones.rqf.selective", "_SplitProjection", _split_projection),
 ]
 
 

@@ -1312,6 +1312,47 @@ def projection_weight_grad_real(gz: torch.Tensor, x: torch.Tensor) -> torch.Tens
     return gw
 
 
+class _SplitProjection(torch.autograd.Function):
+    """The selective controller's projection (rqf_models/backbones/rqf/
+    selective.py:_SplitProjection :78-97): logits = weights @ v split into
+    the gamma / warp / write heads, with v = [Re s; Im s] (2I, N) and
+    weights (M, 2I) real.  On the split-TF32 tensor-core GEMMs in their
+    complex-as-real forms, with s = v[:I] + i v[I:] and Wr, Wi the two
+    column halves of weights:
+      logits = Re((Wr - i Wi) s)          (rqf_projection_real_out)
+      grad v = [Re u; Im u],  u = (Wr^T + i Wi^T) grad     (rqf_projection_real)
+      grad weights = [Re P, -Im P],  P = grad s^H          (rqf_projection_weight_grad_real)
+    The reference runs the three as fp32 cuBLAS GEMMs (SIMT on B200)."""
+
+    @staticmethod
+    def forward(ctx, v, weights, sizes):
+        I = v.shape[0] // 2
+        s = torch.complex(v[:I], v[I:]).contiguous()
+        wr, wi = weights[:, :I], weights[:, I:]
+        ctx.save_for_backward(s, weights)
+        ctx.sizes = sizes
+        ctx.set_materialize_grads(False)
+        out = projection_real_out(torch.complex(wr, -wi), s)
+        return out.split(sizes)
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, *grads):
+        s, weights = ctx.saved_tensors
+        I, N = s.shape
+        grad = torch.cat([g if g is not None else s.real.new_zeros((n, N))
+                          for g, n in zip(grads, ctx.sizes) if n])
+        need = ctx.needs_input_grad
+        gv = gw = None
+        if need[0]:
+            u = projection_real(torch.complex(weights[:, :I].t(), weights[:, I:].t()), grad)
+            gv = torch.cat((u.real, u.imag))
+        if need[1]:
+            P = projection_weight_grad_real(grad, s)
+            gw = torch.cat((P.real, -P.imag), dim=1)
+        return gv, gw, None
+
+
 def projection_real_out(W: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
     """Re(W @ x) as float32 (M, ...) for complex W (M, K) and x (K, ...): the
     readout hidden layer's pre-activation W1 [Re h; Im h] with W = W1[:, :F] -

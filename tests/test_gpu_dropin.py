@@ -172,6 +172,43 @@ def test_selective_pure_encoder_forward():
     x = torch.randn(2, 1024, 1, device="cuda", generator=torch.Generator("cuda").manual_seed(6))
     launched = _compare(enc, x, fwd_only=True)
     assert "rqf_selective_forward" in launched
+    assert "rqf_projection_real_out" in launched  # the controller projection
+
+
+@pytest.mark.parametrize("sizes", [(64, 4, 64), (0, 8, 96), (48, 0, 0)])
+@pytest.mark.parametrize("N", [4096, 2050])
+def test_selective_controller_projection(sizes, N):
+    """selective.py:_SplitProjection after install(): the controller logits
+    and the cotangents of v and of the stacked head weights against the
+    reference's own Function run in fp64 on the same inputs (heads of zero
+    rows included; N not a multiple of 4 takes torch's GEMMs on the GPU)."""
+    import prospective_rqf_b200 as rqf
+    from rqf_models.backbones.rqf import selective
+
+    g = torch.Generator("cuda").manual_seed(sum(sizes) + N)
+    I, M = 32, sum(sizes)
+    v = torch.randn(2 * I, N, device="cuda", generator=g)
+    w = torch.randn(M, 2 * I, device="cuda", generator=g) / np.sqrt(2 * I)
+    gys = [torch.randn(n, N, device="cuda", generator=g) for n in sizes]
+    rqf.uninstall()
+    v64, w64 = v.double().requires_grad_(True), w.double().requires_grad_(True)
+    outs = selective._SplitProjection.apply(v64, w64, sizes)
+    torch.autograd.backward([o for o in outs if o.numel()],
+                            [gy.double() for gy, o in zip(gys, outs) if o.numel()])
+    rqf.install()
+    try:
+        vv, ww = v.clone().requires_grad_(True), w.clone().requires_grad_(True)
+        got = selective._SplitProjection.apply(vv, ww, sizes)
+        torch.autograd.backward([o for o in got if o.numel()],
+                                [gy for gy, o in zip(gys, got) if o.numel()])
+    finally:
+        rqf.uninstall()
+    for o, r in zip(got, outs):
+        assert o.shape == r.shape
+        if o.numel():
+            assert rel_err(_np(o), _np(r)) <= FWD_TOL
+    assert rel_err(_np(vv.grad), _np(v64.grad)) <= GRAD_TOL
+    assert rel_err(_np(ww.grad), _np(w64.grad)) <= GRAD_TOL
 
 
 def test_sequential_scan_abs_epilogue():
