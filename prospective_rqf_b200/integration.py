@@ -18,6 +18,8 @@ Call sites served (reference paths):
   rqf_models/ops/fbt_scan_kernel.py:1005       -> fbt_layer0_real_scan (no caller in the reference)
   rqf_models/backbones/rqf/block.py:882, :904 -> TBPTT(1) fused surrogate on CUDA
   rqf_models/ops/selective_scan.py:119, :133   -> selective_forward / selective_backward
+  rqf_models/ops/selective_scan.py:107         -> _SelectiveLayerScan (its drive GEMMs on the
+                                                  tensor cores)
   rqf_models/backbones/rqf/selective.py:78     -> the controller projection _SplitProjection
                                                   (fp32 CUDA: tensor-core GEMMs)
   rqf_models/backbones/rqf/filter.py:510       -> RQF.compute_two_tap_coefficients on fp32
@@ -65,6 +67,7 @@ _BINDINGS = [
      ops._sequential_scan_multi_osc_real_forward_abs_raw),
     ("rqf_models.ops.selective_scan_kernel", "selective_forward", ops.selective_forward),
     ("rqf_models.ops.selective_scan_kernel", "selective_backward", ops.selective_backward),
+    ("rqf_models.ops.selective_scan", "_SelectiveLayerScan", ops._SelectiveLayerScan),
 ]
 
 

@@ -1019,15 +1019,15 @@ def selective_backward_bf16(z, inputs, entries, gy, gx, activate, truncated):
 
 class _SelectiveLayerScan(torch.autograd.Function):
     """Owns the drive GEMM z = W @ x so the TBPTT(1) lag cotangent reaches W
-    only (rqf_models/ops/selective_scan.py:_SelectiveLayerScan :107-170)."""
+    only (rqf_models/ops/selective_scan.py:_SelectiveLayerScan :107-170).
+    The drive GEMM and its two cotangent GEMMs run on the split-TF32
+    tensor-core projections (the reference: fp32 cuBLAS complex GEMMs)."""
 
     @staticmethod
     def forward(ctx, x, weight, *args):
         *tensors, options, truncated, activate, write_raw, chunk = args
         inputs = tuple(tensors) + (options,)
-        f_in, batch, time = x.shape
-        with torch.autocast(x.device.type, enabled=False):
-            z = (weight @ x.reshape(f_in, batch * time)).reshape(-1, batch, time)
+        z = projection(weight, x)
         raw, act, entries = selective_forward(z, inputs, activate, write_raw, chunk)
         ctx.save_for_backward(x, weight, z, entries, *[t for t in tensors if t is not None])
         ctx.none_mask = [t is None for t in tensors]
@@ -1045,10 +1045,9 @@ class _SelectiveLayerScan(torch.autograd.Function):
         inputs = tuple(tensors) + (ctx.options,)
         dx_drive, dw_drive, dg, dd, dw, dbias, dtheta = selective_backward(
             z, inputs, entries, grad_raw, grad_act, ctx.activate, ctx.truncated, ctx.chunk)
-        f_in = x.shape[0]
-        with torch.autocast(x.device.type, enabled=False):
-            dx = (weight.mH @ dx_drive.reshape(weight.shape[0], -1)).reshape_as(x)
-            dweight = dw_drive.reshape(weight.shape[0], -1) @ x.reshape(f_in, -1).mH
+        need = ctx.needs_input_grad
+        dx = projection(weight, dx_drive, conj_transpose=True) if need[0] else None
+        dweight = projection_weight_grad(dw_drive, x) if need[1] else None
         grads = (dx, dweight, dg, dd, dw, dbias, dtheta) + (None,) * 12
         return tuple(g if need else None for g, need in zip(grads, ctx.needs_input_grad))
 
