@@ -229,6 +229,35 @@ int rqf_fbt_prospective_backward(const float *c1, const float *tap0,
                                  int64_t time, int fuse_act,
                                  rqf_stream_t stream);
 
+/* ---- first block over a rank-1 input ---------------------------------- *
+ * The first Pure RQF block when the input projection has one channel
+ * (pure.py:_forward_fbt_stack :510-534 with input_dims = 1, the waveform
+ * models): its drive z = u x + beta (u = W w_in, beta = W b_in) and skip
+ * h0 = w x + bb (w = w_in, bb = b_in) are made inside the (F,B,T) row scan
+ * from x (batch, time) float32 instead of being read from HBM.  The forward
+ * equals rqf_lowrank_drive followed by rqf_fbt_block_forward on its z and h0
+ * (the same operations), writes out = act(y) (+ h0) and the (F,B,T) saved
+ * context.  The backward replays from that context and, instead of grad_z,
+ * returns its row sums gzx = [sum gz x, sum gz] and gsx = [sum g x, sum g]
+ * (complex (F, 2), over batch and time; gsx nullable; the plain sums only
+ * with with_sum), which is what the block's weight and input-projection
+ * cotangents need (rqf_rowdot of grad_z and of the output cotangent).
+ * beta, w, bb nullable (no w: no skip).  Both need the persistent row
+ * kernels and T a multiple of 4: rqf_fbt_rank1_supported; otherwise
+ * RQF_ERR_SHAPE. */
+int rqf_fbt_rank1_supported(int64_t filters, int64_t batch, int64_t time);
+size_t rqf_fbt_rank1_scratch_bytes(int64_t filters, int64_t batch, int64_t time);
+int rqf_fbt_rank1_forward(const float *u, const float *beta, const float *w, const float *bb,
+                          const float *x, const float *c1, const float *tap0, const float *tap1,
+                          float *out, float *carries, int64_t filters, int64_t batch,
+                          int64_t time, int fuse_act, rqf_stream_t stream);
+int rqf_fbt_rank1_backward(const float *u, const float *beta, const float *x, const float *c1,
+                           const float *tap0, const float *tap1, const float *carries,
+                           const float *grad_out, float *gzx, float *gsx, float *grad_c1,
+                           float *grad_tap0, float *grad_tap1, void *scratch, int64_t filters,
+                           int64_t batch, int64_t time, int fuse_act, int with_sum,
+                           rqf_stream_t stream);
+
 /* ---- TBPTT(1) two-tap surrogate backward ----------------------------- *
  * The forward value of the reference's TBPTT(1) path equals the exact scan
  * (rqf_models/backbones/rqf/block.py:_scan_two_tap_with_grad_mode :904-954),

@@ -116,6 +116,13 @@ SIGNATURES: dict[str, tuple] = {
     "rqf_projection_block_scan_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64]),
     "rqf_projection_block_scan": (
         _int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _int, _p]),
+    "rqf_fbt_rank1_supported": (_int, [_i64, _i64, _i64]),
+    "rqf_fbt_rank1_scratch_bytes": (_sz, [_i64, _i64, _i64]),
+    "rqf_fbt_rank1_forward": (
+        _int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
+    "rqf_fbt_rank1_backward": (
+        _int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int,
+               _int, _p]),
     "rqf_fbt_tbptt1_backward_wsum": (
         _int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "rqf_projection_block_scan_backward_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64]),

@@ -14,6 +14,7 @@
 #include "btf_scan.cuh"
 #include "btf_stream.cuh"
 #include "fbt_rows.cuh"
+#include "fbt_rank1.cuh"
 #include "fbt_scan.cuh"
 #include "coeffs.cuh"
 #include "lowrank.cuh"
@@ -728,6 +729,117 @@ int rqf_fbt_block_forward(const float *c1, const float *tap0, const float *tap1,
       fbt_fwd_kernel<kFbtThreads, kFbtK, false, false><<<grid, kFbtThreads, 0, stream>>>(a);
   }
   return launch_status();
+}
+
+// ------------------------------------------------ rank-1 first block
+}  // extern "C"
+
+namespace {
+
+constexpr int kRank1FwdStages = kRowsFwdStages, kRank1BwdStages = kRowsBwdStages;
+constexpr size_t kRank1FwdSmem = fbt_rows_smem_bytes<kFbtThreads, kFbtK, 1, kRank1FwdStages>();
+constexpr size_t kRank1BwdSmem = fbt_rows_smem_bytes<kFbtThreads, kFbtK, 2, kRank1BwdStages>();
+
+// Both row kernels of the rank-1 block take the shape: enough rows for every
+// resident CTA, T a multiple of 4 (16-byte x pieces), 32-bit cursors.
+bool rank1_shape_ok(int64_t F, int64_t B, int64_t T) {
+  if (fbt_dims_ok(F, B, T) != RQF_OK || F <= 0 || B <= 0 || T <= 0 || T % 4 != 0) return false;
+  if (T > 0x7fffffffLL || F * B > 0x7fffffffLL) return false;
+  const int64_t gf = resident_ctas(fbt_rank1_fwd_kernel<kFbtThreads, kFbtK, kRank1FwdStages, true>,
+                                   kFbtThreads, kRank1FwdSmem);
+  const int64_t gb = resident_ctas(
+      fbt_rank1_bwd_kernel<kFbtThreads, kFbtK, kRank1BwdStages, true, true>, kFbtThreads,
+      kRank1BwdSmem);
+  return gf > 0 && gb > 0 && F * B >= gf && F * B >= gb;
+}
+
+}  // namespace
+
+extern "C" {
+
+int rqf_fbt_rank1_supported(int64_t filters, int64_t batch, int64_t time) {
+  return rank1_shape_ok(filters, batch, time) ? 1 : 0;
+}
+
+size_t rqf_fbt_rank1_scratch_bytes(int64_t filters, int64_t batch, int64_t time) {
+  if (fbt_dims_ok(filters, batch, time) != RQF_OK) return SIZE_MAX;
+  return round256((size_t)filters * batch * 3 * sizeof(float2)) +
+         round256((size_t)filters * batch * 4 * sizeof(float2));
+}
+
+int rqf_fbt_rank1_forward(const float *u, const float *beta, const float *w, const float *bb,
+                          const float *x, const float *c1, const float *tap0, const float *tap1,
+                          float *out, float *carries, int64_t filters, int64_t batch,
+                          int64_t time, int fuse_act, rqf_stream_t stream) {
+  int st = fbt_dims_ok(filters, batch, time);
+  if (st != RQF_OK) return st;
+  if (filters == 0 || batch == 0 || time == 0) return RQF_OK;
+  if (!rank1_shape_ok(filters, batch, time)) return RQF_ERR_SHAPE;
+  if (!u || !x || !c1 || !tap0 || !tap1 || !out || !carries) return RQF_ERR_ARGUMENT;
+  if (!aligned(u, 8) || (beta && !aligned(beta, 8)) || !aligned(x, 16) || !aligned(c1, 8) ||
+      !aligned(tap0, 8) || !aligned(tap1, 8) || !aligned(out, 16) || !aligned(carries, 8))
+    return RQF_ERR_ALIGN;
+  FbtArgs a = fbt_args(c1, tap0, tap1, nullptr, nullptr, out, nullptr, carries, nullptr, filters,
+                       batch, time);
+  Rank1Args r{reinterpret_cast<const float2 *>(u), reinterpret_cast<const float2 *>(beta), w, bb, x,
+              nullptr};
+  auto kern = fuse_act ? fbt_rank1_fwd_kernel<kFbtThreads, kFbtK, kRank1FwdStages, true>
+                       : fbt_rank1_fwd_kernel<kFbtThreads, kFbtK, kRank1FwdStages, false>;
+  const int64_t g = resident_ctas(kern, kFbtThreads, kRank1FwdSmem);
+  kern<<<(unsigned)g, kFbtThreads, kRank1FwdSmem, reinterpret_cast<cudaStream_t>(stream)>>>(a, r);
+  return launch_status();
+}
+
+int rqf_fbt_rank1_backward(const float *u, const float *beta, const float *x, const float *c1,
+                           const float *tap0, const float *tap1, const float *carries,
+                           const float *grad_out, float *gzx, float *gsx, float *grad_c1,
+                           float *grad_tap0, float *grad_tap1, void *scratch, int64_t filters,
+                           int64_t batch, int64_t time, int fuse_act, int with_sum,
+                           rqf_stream_t stream) {
+  cudaStream_t sm = reinterpret_cast<cudaStream_t>(stream);
+  int st = fbt_dims_ok(filters, batch, time);
+  if (st != RQF_OK) return st;
+  if (filters == 0) return RQF_OK;
+  if (batch == 0 || time == 0) {
+    for (float *p : {grad_c1, grad_tap0, grad_tap1})
+      if ((st = zero_complex(p, filters, sm)) != RQF_OK) return st;
+    if ((st = zero_complex(gzx, 2 * filters, sm)) != RQF_OK) return st;
+    return zero_complex(gsx, 2 * filters, sm);
+  }
+  if (!rank1_shape_ok(filters, batch, time)) return RQF_ERR_SHAPE;
+  if (!u || !x || !c1 || !tap0 || !tap1 || !carries || !grad_out || !gzx || !grad_c1 ||
+      !grad_tap0 || !grad_tap1 || !scratch)
+    return RQF_ERR_ARGUMENT;
+  if (!aligned(u, 8) || (beta && !aligned(beta, 8)) || !aligned(x, 16) || !aligned(c1, 8) ||
+      !aligned(tap0, 8) || !aligned(tap1, 8) || !aligned(carries, 8) || !aligned(grad_out, 16) ||
+      !aligned(gzx, 8) || (gsx && !aligned(gsx, 8)) || !aligned(scratch, 16))
+    return RQF_ERR_ALIGN;
+  FbtArgs a = fbt_args(c1, tap0, tap1, nullptr, grad_out, nullptr, nullptr,
+                       const_cast<float *>(carries), nullptr, filters, batch, time);
+  const int64_t rows = filters * batch;
+  a.partials = static_cast<float2 *>(scratch);
+  float2 *rowsums = at<float2>(scratch, round256((size_t)rows * 3 * sizeof(float2)));
+  Rank1Args r{reinterpret_cast<const float2 *>(u), reinterpret_cast<const float2 *>(beta),
+              nullptr, nullptr, x, rowsums};
+  const bool wsum = with_sum != 0;
+  auto kern =
+      fuse_act ? (wsum ? fbt_rank1_bwd_kernel<kFbtThreads, kFbtK, kRank1BwdStages, true, true>
+                       : fbt_rank1_bwd_kernel<kFbtThreads, kFbtK, kRank1BwdStages, true, false>)
+               : (wsum ? fbt_rank1_bwd_kernel<kFbtThreads, kFbtK, kRank1BwdStages, false, true>
+                       : fbt_rank1_bwd_kernel<kFbtThreads, kFbtK, kRank1BwdStages, false, false>);
+  const int64_t g = resident_ctas(kern, kFbtThreads, kRank1BwdSmem);
+  kern<<<(unsigned)g, kFbtThreads, kRank1BwdSmem, sm>>>(a, r);
+  if ((st = launch_status()) != RQF_OK) return st;
+  reduce_partials_kernel<<<(unsigned)filters, 256, 0, sm>>>(
+      a.partials, reinterpret_cast<float2 *>(grad_c1), reinterpret_cast<float2 *>(grad_tap0),
+      reinterpret_cast<float2 *>(grad_tap1), batch, batch, 1, 1);
+  if ((st = launch_status()) != RQF_OK) return st;
+  // (F, 2) sums {gz x, gz} into gzx and {g x, g} into gsx
+  reduce_rows4_kernel<<<(unsigned)ceil_div(filters * 4, 256), 256, 0, sm>>>(
+      rowsums, reinterpret_cast<float2 *>(gzx), reinterpret_cast<float2 *>(gsx), filters,
+      (int)batch);
+  if ((st = launch_status()) != RQF_OK) return st;
+  return RQF_OK;
 }
 
 int rqf_fbt_prospective_backward(const float *c1, const float *tap0, const float *tap1,

@@ -332,12 +332,18 @@ class _InputBlock(torch.autograd.Function):
     def forward(ctx, x_cf, w_in, b_in, W, C1, tap0, tap1, fuse_act, skip, B, T):
         F = W.shape[0]
         beta = W @ b_in.to(torch.complex64) if b_in is not None else None
-        z, h0 = ops.lowrank_drive(W @ w_in.to(torch.complex64), x_cf, beta,
-                                  w_in if skip else None, b_in)
-        z = z.view(F, B, T)
-        out, saved = ops._fbt_forward(C1, tap0, tap1, z, bool(fuse_act),
-                                      h0.view(F, B, T) if skip else None)
-        ctx.save_for_backward(x_cf, w_in, b_in, W, *saved)
+        U = W @ w_in.to(torch.complex64)
+        ctx.rank1 = w_in.shape[1] == 1 and ops.rank1_supported(F, B, T)
+        if ctx.rank1:  # the drive and skip made inside the scan from x
+            out, saved = ops.rank1_block_forward(U[:, 0], beta, w_in[:, 0] if skip else None,
+                                                 b_in, x_cf.view(B, T), C1, tap0, tap1,
+                                                 bool(fuse_act))
+        else:
+            z, h0 = ops.lowrank_drive(U, x_cf, beta, w_in if skip else None, b_in)
+            out, saved = ops._fbt_forward(C1, tap0, tap1, z.view(F, B, T), bool(fuse_act),
+                                          h0.view(F, B, T) if skip else None)
+        ctx.save_for_backward(x_cf, w_in, b_in, W, *[t for t in saved if t is not None])
+        ctx.has_beta = beta is not None
         ctx.fuse_act, ctx.skip = bool(fuse_act), bool(skip)
         return out
 
@@ -345,10 +351,20 @@ class _InputBlock(torch.autograd.Function):
     @once_differentiable
     def backward(ctx, g):
         x_cf, w_in, b_in, W, *saved = ctx.saved_tensors
-        gc1, gt0, gt1, gz = ops._fbt_backward(saved, g, ctx.fuse_act)
         need = ctx.needs_input_grad
         I, has_b = w_in.shape[1], b_in is not None
-        G = ops.rowdot(gz, x_cf, with_sum=has_b)  # (F, I + has_b)
+        Gs = None
+        if ctx.rank1:
+            c1, t0, t1, u, *rest = saved
+            beta = rest.pop(0) if ctx.has_beta else None
+            xx, carries = rest
+            gc1, gt0, gt1, G, Gs = ops.rank1_block_backward(
+                (c1, t0, t1, u, beta, xx, carries), g, ctx.fuse_act, has_b, ctx.skip)
+        else:
+            gc1, gt0, gt1, gz = ops._fbt_backward(saved, g, ctx.fuse_act)
+            G = ops.rowdot(gz, x_cf, with_sum=has_b)  # (F, I + has_b)
+            if ctx.skip:
+                Gs = ops.rowdot(g, x_cf, with_sum=has_b)
         gW = gw_in = gb_in = None
         if need[3]:
             rows = torch.cat([w_in, b_in[:, None]], dim=1) if has_b else w_in
@@ -356,7 +372,7 @@ class _InputBlock(torch.autograd.Function):
         if need[1] or need[2]:
             gh = W.mH @ G
             if ctx.skip:
-                gh = gh + ops.rowdot(g, x_cf, with_sum=has_b)
+                gh = gh + Gs
             gw_in = gh[:, :I].real.contiguous() if need[1] else None
             gb_in = gh[:, I].real.contiguous() if (has_b and need[2]) else None
         return None, gw_in, gb_in, gW, gc1, gt0, gt1, None, None, None, None

@@ -1181,6 +1181,69 @@ def lowrank_drive(u: torch.Tensor, x: torch.Tensor, beta: torch.Tensor | None = 
     return z, h
 
 
+def rank1_supported(F: int, B: int, T: int) -> bool:
+    """Whether the rank-1 first-block kernels take an (F, B, T) block on the
+    current device (enough rows for the persistent row kernels, T a multiple
+    of 4)."""
+    return _abi.load().rqf_fbt_rank1_supported(int(F), int(B), int(T)) == 1
+
+
+def rank1_block_forward(u, beta, w, bb, x, C1, tap0, tap1, fuse_act: bool):
+    """The first Pure RQF block over a rank-1 input in one launch
+    (rqf_fbt_rank1_forward): z = u x + beta and, when w is given, the skip
+    h0 = w x + bb made inside the (F,B,T) row scan from x (B, T) float32;
+    returns act(y) (+ h0) as complex64 (F, B, T) and the saved context
+    (c1, tap0, tap1, u, beta, x, carries) for rank1_block_backward.  u,
+    beta (F,) complex; w, bb (F,) real (beta, bb may be None)."""
+    dev = _require_cuda(u, x, C1)
+    xx = x.detach().to(torch.float32).contiguous()
+    B, T = (int(d) for d in xx.shape)
+    uu = _c64(u)
+    F = int(uu.shape[0])
+    c1, t0, t1 = _coef(C1, F, "C1"), _coef(tap0, F, "tap0"), _coef(tap1, F, "tap1")
+    be = _c64(beta) if beta is not None else None
+    ww = w.detach().to(torch.float32).contiguous() if w is not None else None
+    bbv = bb.detach().to(torch.float32).contiguous() if (w is not None and bb is not None) else None
+    lib = _abi.load()
+    out = torch.empty((F, B, T), dtype=torch.complex64, device=dev)
+    carries = _carries(lib.rqf_fbt_carry_count(F, B, T), dev)
+    with _timing.launch("rqf_fbt_rank1_forward", F * B * T, _nbytes(xx, out)):
+        _abi.check(lib.rqf_fbt_rank1_forward(
+            _abi.ptr(uu), _abi.ptr(be), _abi.ptr(ww), _abi.ptr(bbv), _abi.ptr(xx), _abi.ptr(c1),
+            _abi.ptr(t0), _abi.ptr(t1), _abi.ptr(out), _abi.ptr(carries), F, B, T,
+            int(bool(fuse_act)), _abi.stream_of(xx)), "rqf_fbt_rank1_forward")
+    _done(dev)
+    return out, (c1, t0, t1, uu, be, xx, carries)
+
+
+def rank1_block_backward(saved, grad_output, fuse_act: bool, with_sum: bool, skip: bool):
+    """The rank-1 first block's backward (rqf_fbt_rank1_backward): the scan
+    VJP of grad_output replayed from the saved context with z made from x,
+    reduced to (gc1, gtap0, gtap1, G, Gs) where G = [sum gz x (, sum gz)] and
+    Gs = [sum g x (, sum g)] over (b, t) are complex64 (F, 1 + with_sum) —
+    what rowdot(gz, x, with_sum) and rowdot(g, x, with_sum) return — and Gs is
+    None unless ``skip``.  grad_z itself is never formed."""
+    c1, t0, t1, uu, be, xx, carries = saved
+    F = int(uu.shape[0])
+    B, T = (int(d) for d in xx.shape)
+    dev = xx.device
+    gy = _c64(grad_output)
+    lib = _abi.load()
+    gc1, gt0, gt1 = torch.empty_like(c1), torch.empty_like(t0), torch.empty_like(t1)
+    G = torch.empty((F, 2), dtype=torch.complex64, device=dev)
+    Gs = torch.empty((F, 2), dtype=torch.complex64, device=dev) if skip else None
+    scratch = _scratch(lib.rqf_fbt_rank1_scratch_bytes(F, B, T), dev)
+    with _timing.launch("rqf_fbt_rank1_backward", F * B * T, _nbytes(xx, gy)):
+        _abi.check(lib.rqf_fbt_rank1_backward(
+            _abi.ptr(uu), _abi.ptr(be), _abi.ptr(xx), _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1),
+            _abi.ptr(carries), _abi.ptr(gy), _abi.ptr(G), _abi.ptr(Gs), _abi.ptr(gc1),
+            _abi.ptr(gt0), _abi.ptr(gt1), _abi.ptr(scratch), F, B, T, int(bool(fuse_act)),
+            int(bool(with_sum)), _abi.stream_of(gy)), "rqf_fbt_rank1_backward")
+    _done(dev)
+    n = 2 if with_sum else 1
+    return gc1, gt0, gt1, G[:, :n], (Gs[:, :n] if Gs is not None else None)
+
+
 def rowdot(a: torch.Tensor, x: torch.Tensor | None, with_sum: bool = False) -> torch.Tensor:
     """out[:, j] = a @ x[j] for the real rows of x (I <= 4), then the row sums
     of a when with_sum: complex64 (F, I + with_sum), over the flattened

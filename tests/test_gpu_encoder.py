@@ -438,3 +438,44 @@ def test_readout_tc_matches_torch(per_step, monkeypatch):
     for n in res["torch"][2]:
         assert_close(_np(res["tc"][2][n].cpu()), _np(res["torch"][2][n].cpu()), GRAD_TOL,
                      f"grad {n}")
+
+
+@pytest.mark.parametrize("bias,skip,T", [(False, True, 4000), (True, True, 2000),
+                                         (False, False, 4096), (True, False, 1004)])
+def test_rank1_first_block_matches_general_path(bias, skip, T, monkeypatch):
+    """The first block over a one-channel input on the rank-1 kernels
+    (rqf_fbt_rank1_forward / _backward: drive and skip made from x inside
+    the scan, no grad_z, the row sums reduced in the backward) against the
+    same block on rqf_lowrank_drive + the (F,B,T) row kernels + rqf_rowdot:
+    the features bit-identical (the same operations), logits and every
+    parameter gradient within fp32 summation-order noise.  1024 rows, so the
+    persistent row kernels apply; T a multiple of 4 with the last tile cut."""
+    from prospective_rqf_b200 import _timing, ops
+    from prospective_rqf_b200 import encoder as E
+
+    def run(rank1):
+        if not rank1:
+            monkeypatch.setattr(ops, "rank1_supported", lambda *a: False)
+        torch.manual_seed(0)
+        enc = E.PureRQFEncoderB200(input_dims=1, hidden_dims=128, num_layers=2,
+                                   skip_connection=skip, input_proj_bias=bias, seed=4)
+        model = E.RQFClassifier(enc, 5, 32).cuda()
+        g = torch.Generator().manual_seed(6)
+        x = (0.5 * torch.randn(8, T, 1, generator=g)).clamp(-1, 1).cuda()
+        y = torch.randint(0, 5, (8,), generator=g).cuda()
+        with _timing.KernelTimer() as tm:
+            feats = model.encoder(x)
+            logits = model.readout(feats)
+            torch.nn.functional.cross_entropy(logits, y).backward()
+        grads = {n: p.grad.detach().clone() for n, p in model.named_parameters()}
+        return feats.detach().clone(), logits.detach().clone(), grads, set(tm.summary())
+
+    f1, l1, g1, k1 = run(True)
+    assert {"rqf_fbt_rank1_forward", "rqf_fbt_rank1_backward"} <= k1
+    f2, l2, g2, k2 = run(False)
+    assert "rqf_fbt_rank1_forward" not in k2
+    assert torch.equal(f1, f2), "features differ from the general first block"
+    assert rel_err(l1.cpu().numpy(), l2.cpu().numpy()) <= 1e-6
+    for n in g1:
+        e = rel_err(g1[n].cpu().numpy(), g2[n].cpu().numpy())
+        assert e <= 1e-4, f"{n}: {e:.2e}"

@@ -55,6 +55,7 @@ def _fake_reference(monkeypatch):
                                            "fbt_recompute_scan": "orig"},
         "rqf_models.ops.selective_scan_kernel": {"selective_forward": "orig",
                                                  "selective_backward": "orig"},
+        "rqf_models.ops.selective_scan": {"_SelectiveLayerScan": "orig"},
         "rqf_models.backbones": {},
         "rqf_models.backbones.rqf": {},
         "rqf_models.backbones.rqf.block": {"_triton_chunked_scan_prospective": "orig"},
@@ -147,7 +148,11 @@ def test_install_against_the_reference_tree(monkeypatch):
         assert sk.selective_forward is ops.selective_forward
         assert scan._sequential_scan_forward_abs_raw_block_f is \
             ops._sequential_scan_forward_abs_raw_block_f
-        assert len(patched) == 23
+        import rqf_models.ops.selective_scan as ss
+
+        assert ss._SelectiveLayerScan is ops._SelectiveLayerScan
+        assert "rqf_models.backbones.rqf.selective._SplitProjection" in patched
+        assert len(patched) == 25
     finally:
         integration.uninstall()
 
