@@ -30,6 +30,8 @@ Ops:
              (rqf_projection_block_scan_backward: W^H gz + acc with the lower
              block's scan VJP in the epilogue), beside the unfused pair:
              rqf_projection, then rqf_fbt_prospective_backward
+  rank1      the first Pure RQF block over a one-channel input (drive and skip
+             made from x inside the row scan; rqf_fbt_rank1_forward / _backward)
   mosc       the fused multi-oscillator scan (B,T,F) -> (B,T,F), --groups
              oscillators per filter
 
@@ -168,6 +170,17 @@ def make_case(op: str, F: int, B: int, T: int, groups: int = 8, truncated: bool 
             ops._fbt_backward(saved, gy, True)
         return run
 
+    if op == "rank1":  # the first block over a one-channel input, made inside the scan
+        x = torch.randn(B, T, generator=g).to(dev)
+        u, be = crandn(F), crandn(F)
+        w, bb = torch.randn(F, generator=g).to(dev), torch.randn(F, generator=g).to(dev)
+        gy = crandn(F, B, T)
+
+        def run():
+            out, saved = ops.rank1_block_forward(u, be, w, bb, x, c1, t0, t1, True)
+            ops.rank1_block_backward(saved, gy, True, True, True)
+        return run
+
     if op == "mosc":  # groups = oscillators per filter; F filters in and out
         n = groups
         c1m, c2m, _ = _coeffs(F * n, dev, g)
@@ -206,7 +219,7 @@ def make_case(op: str, F: int, B: int, T: int, groups: int = 8, truncated: bool 
 
 OPS = ("fbt", "fbt_raw", "fbt_skip", "tbptt_fbt", "tbptt_btf", "btf", "btf_real", "btf_pro",
        "selective", "selective_bf16", "projection", "projection_torch", "projection_real", "mosc",
-       "block_scan", "block_scan_bwd")
+       "block_scan", "block_scan_bwd", "rank1")
 
 
 def measure(op, F, B, T, iters=10, warmup=3, groups=8, truncated=False) -> dict:

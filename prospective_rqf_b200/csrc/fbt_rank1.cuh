@@ -204,10 +204,19 @@ __global__ void __launch_bounds__(NT, 3) fbt_rank1_bwd_kernel(const FbtArgs a, c
   for (int s = 0; s < S - 1; ++s) issue();
   RowCursor pc{(int)blockIdx.x, 0, 0};
   float2 dcarry = cz(), lam = cz(), t0 = cz(), t1 = cz(), lpow_r = cz(), u = cz(), be = cz();
-  // conj(v) g sums as v (g.x, g.x) and v (g.y, g.y) pairs (see fbt_bwd_rows_kernel); the row
-  // sums of a real x as (x, x) g
-  float2 acc_c1 = cz(), acc_t0 = cz(), acc_t1 = cz();
-  float2 acc_zx = cz(), acc_z1 = cz(), acc_gx = cz(), acc_g1 = cz();
+  // Running sums of the row, all linear in the adjoint d because z is rank 1
+  // in x (z = u x + beta, and z = 0 before the row's first sample):
+  //   acc_c1  sum conj(y[t-1]) d[t] as its (g.x, g.x), (g.y, g.y) pair halves
+  //   sd      sum d[t]             sxd  sum x[t] d[t]      sxpd  sum x[t-1] d[t]
+  //   sgx     sum x[t] g[t]        sg   sum g[t] (WSUM)     g the output cotangent
+  // so that, with d0 = d at the row's first sample and d past the row zero,
+  //   sum conj(z[t]) d[t]     = conj(u) sxd  + conj(beta) sd
+  //   sum conj(z[t-1]) d[t]   = conj(u) sxpd + conj(beta) (sd - d0)
+  //   sum gz x = conj(tap0) sxd + conj(tap1) sxpd     (sum x[t] d[t+1] = sxpd)
+  //   sum gz   = conj(tap0) sd  + conj(tap1) (sd - d0)
+  // with gz[t] = conj(tap0) d[t] + conj(tap1) d[t+1].
+  float2 pc1r = cz(), qc1r = cz(), sd = cz(), sxd = cz(), sxpd = cz(), sgx = cz(), sg = cz();
+  float2 d0 = cz();
   while (pc.row < rows) {
     cp_async_wait<S - 2>();
     __syncthreads();
@@ -229,17 +238,19 @@ __global__ void __launch_bounds__(NT, 3) fbt_rank1_bwd_kernel(const FbtArgs a, c
     float4 *gbuf = dsm + s * stage_sz + (NW + warp) * WSZ;
     float xv[K];
     r1_read_x<K>(xbuf, xv, lane);
-    float2 z[K], go[K];
-#pragma unroll
-    for (int k = 0; k < K; ++k) z[k] = r1_z(u, be, xv[k]);
+    float2 go[K];
     read_blocked<K>(gbuf, go, lane);
-    float2 zp = shfl_up2(z[K - 1], 1);
-    if (lane == 0)
-      zp = warp > 0 ? r1_z(u, be, r1_last_x(xbuf - WSZ))
-                    : (jt > 0 ? r1_z(u, be, s_xprev[s]) : cz());
-
+    // x before the thread's first sample (zero before the row's first)
+    float xp = __shfl_up_sync(0xffffffffu, xv[K - 1], 1);
+    if (lane == 0) xp = warp > 0 ? r1_last_x(xbuf - WSZ) : (jt > 0 ? s_xprev[s] : 0.f);
+    const bool row_start = jt == 0 && tid == 0;
     float2 b[K];
-    fbt_drive<K>(t0, t1, z, zp, b);
+    {
+      float2 z[K];
+#pragma unroll
+      for (int k = 0; k < K; ++k) z[k] = r1_z(u, be, xv[k]);
+      fbt_drive<K>(t0, t1, z, row_start ? cz() : r1_z(u, be, xp), b);
+    }
     float2 e = s_ent[s][tid];
     float2 yprev[K];
 #pragma unroll
@@ -247,6 +258,8 @@ __global__ void __launch_bounds__(NT, 3) fbt_rank1_bwd_kernel(const FbtArgs a, c
       yprev[k] = e;
       e = c_fma(lam, e, b[k]);
       b[k] = FUSE_ACT ? c_relu_mask(go[k], e) : go[k];
+      sgx = __ffma2_rn(make_float2(xv[k], xv[k]), go[k], sgx);  // go dies here
+      if constexpr (WSUM) sg = c_add(sg, go[k]);
     }
     const float2 mu = c_conj(lam);
     float2 h = cz();
@@ -255,61 +268,63 @@ __global__ void __launch_bounds__(NT, 3) fbt_rank1_bwd_kernel(const FbtArgs a, c
     float2 gnext, Art;
     cta_scan_entry_rev<NT, LK>(h, dcarry, pw, lpow_r, gnext, Art, s_warp_r);
     dcarry = Art;
-    const float2 T0X = make_float2(t0.x, t0.x), T0Y = make_float2(t0.y, -t0.y);
-    const float2 T1X = make_float2(t1.x, t1.x), T1Y = make_float2(t1.y, -t1.y);
-    float2 pc1 = cz(), qc1 = cz(), pt0 = cz(), qt0 = cz(), pt1 = cz(), qt1 = cz();
-    float2 gsw = make_float2(gnext.y, gnext.x);
+    float2 pc1 = cz(), qc1 = cz();
 #pragma unroll
     for (int k = K - 1; k >= 0; --k) {
       const float2 g = c_fma(mu, gnext, b[k]);
-      const float2 gs = make_float2(g.y, g.x);
-      const float2 gz =
-          __ffma2_rn(T0X, g, __ffma2_rn(T0Y, gs, __ffma2_rn(T1X, gnext, __fmul2_rn(T1Y, gsw))));
       const float2 xx = make_float2(xv[k], xv[k]);
-      acc_zx = __ffma2_rn(xx, gz, acc_zx);
-      acc_gx = __ffma2_rn(xx, go[k], acc_gx);
-      if constexpr (WSUM) {
-        acc_z1 = c_add(acc_z1, gz);
-        acc_g1 = c_add(acc_g1, go[k]);
-      }
-      const float2 gx = make_float2(g.x, g.x), gy = make_float2(g.y, g.y);
-      pc1 = __ffma2_rn(yprev[k], gx, pc1);
-      qc1 = __ffma2_rn(yprev[k], gy, qc1);
-      pt0 = __ffma2_rn(z[k], gx, pt0);
-      qt0 = __ffma2_rn(z[k], gy, qt0);
-      const float2 zk1 = k > 0 ? z[k - 1] : zp;
-      pt1 = __ffma2_rn(zk1, gx, pt1);
-      qt1 = __ffma2_rn(zk1, gy, qt1);
+      const float xpk = k > 0 ? xv[k - 1] : xp;
+      sd = c_add(sd, g);
+      sxd = __ffma2_rn(xx, g, sxd);
+      sxpd = __ffma2_rn(make_float2(xpk, xpk), g, sxpd);
+      pc1 = __ffma2_rn(yprev[k], make_float2(g.x, g.x), pc1);
+      qc1 = __ffma2_rn(yprev[k], make_float2(g.y, g.y), qc1);
       gnext = g;
-      gsw = gs;
     }
-    acc_c1 = c_add(acc_c1, make_float2(pc1.x + qc1.y, qc1.x - pc1.y));
-    acc_t0 = c_add(acc_t0, make_float2(pt0.x + qt0.y, qt0.x - pt0.y));
-    acc_t1 = c_add(acc_t1, make_float2(pt1.x + qt1.y, qt1.x - pt1.y));
+    if (row_start) d0 = gnext;  // d at the row's first sample
+    pc1r = c_add(pc1r, pc1);
+    qc1r = c_add(qc1r, qc1);
     if (jt == 0) {  // row finished: deterministic CTA reduction of the row's sums
       auto warp_sum = [&](float2 v, int q) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) v = c_add(v, shfl_xor2(v, o));
         if (lane == 0) s_red[q][warp] = v;
       };
-      warp_sum(acc_c1, 0);
-      warp_sum(acc_t0, 1);
-      warp_sum(acc_t1, 2);
-      warp_sum(acc_zx, 3);
-      warp_sum(acc_z1, 4);
-      warp_sum(acc_gx, 5);
-      warp_sum(acc_g1, 6);
+      warp_sum(make_float2(pc1r.x + qc1r.y, qc1r.x - pc1r.y), 0);
+      warp_sum(sd, 1);
+      warp_sum(sxd, 2);
+      warp_sum(sxpd, 3);
+      warp_sum(sgx, 4);
+      warp_sum(sg, 5);
+      if (tid == 0) s_red[6][0] = d0;
       __syncthreads();
-      if (tid < 7) {
+      if (tid < 6) {
         float2 sum = cz();
 #pragma unroll
         for (int w = 0; w < NW; ++w) sum = c_add(sum, s_red[tid][w]);
-        if (tid < 3)
-          a.partials[(size_t)pc.row * 3 + tid] = sum;
-        else
-          r.rowsums[(size_t)pc.row * 4 + (tid - 3)] = sum;
+        s_red[tid][0] = sum;  // each thread reads and writes only its own q
       }
-      acc_c1 = acc_t0 = acc_t1 = acc_zx = acc_z1 = acc_gx = acc_g1 = cz();
+      __syncthreads();
+      if (tid < 7) {
+        const float2 Sd = s_red[1][0], Sxd = s_red[2][0], Sxpd = s_red[3][0];
+        const float2 Sd1 = make_float2(Sd.x - s_red[6][0].x, Sd.y - s_red[6][0].y);  // d past t = 0
+        const float2 cu = c_conj(u), cb = c_conj(be), ct0 = c_conj(t0), ct1 = c_conj(t1);
+        float2 v;
+        switch (tid) {
+          case 0: v = s_red[0][0]; break;                                  // conj(y[t-1]) d
+          case 1: v = c_add(c_mul(cu, Sxd), c_mul(cb, Sd)); break;        // conj(z[t]) d
+          case 2: v = c_add(c_mul(cu, Sxpd), c_mul(cb, Sd1)); break;      // conj(z[t-1]) d
+          case 3: v = c_add(c_mul(ct0, Sxd), c_mul(ct1, Sxpd)); break;    // sum gz x
+          case 4: v = WSUM ? c_add(c_mul(ct0, Sd), c_mul(ct1, Sd1)) : cz(); break;  // sum gz
+          case 5: v = s_red[4][0]; break;                                  // sum g x
+          default: v = s_red[5][0]; break;                                 // sum g
+        }
+        if (tid < 3)
+          a.partials[(size_t)pc.row * 3 + tid] = v;
+        else
+          r.rowsums[(size_t)pc.row * 4 + (tid - 3)] = v;
+      }
+      pc1r = qc1r = sd = sxd = sxpd = sgx = sg = d0 = cz();
     }
     pc.advance(ntiles, G, S);
   }
