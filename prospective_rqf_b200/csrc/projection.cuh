@@ -189,7 +189,6 @@ struct ScanParams {
   int chains;                      // m_pairs * batch
   int fbt_ntiles;                  // ceil(T / 2048): tiles of the (F,B,T) saved context
   int fuse_act;
-  int two_pass;                    // forward: scan_epilogue_2p (few chains)
 };
 
 // ------------------------------------------------------------ PTX wrappers
@@ -415,36 +414,6 @@ __device__ __forceinline__ void tc_st_32x32b_x32(uint32_t taddr, const float (&v
       "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
       "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
       : "memory");
-}
-
-// 32 lanes x 16 consecutive fp32 columns, both ways (see the x32 forms).
-__device__ __forceinline__ void tc_ld_32x32b_x16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-__device__ __forceinline__ void tc_st_32x32b_x16(uint32_t taddr, const float (&v)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
-      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
-      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
-      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
-      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
-      "r"(__float_as_uint(v[15]))
-      : "memory");
-}
-__device__ __forceinline__ void tc_wait_st() {
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ float tf32_rna(float v) {
@@ -795,203 +764,6 @@ __device__ __forceinline__ bool scan_epilogue(uint32_t tbase, float4 *stage, con
   }
   scan_save_entries(ent, p, sp, jw0, bidx, pos, tfirst, lane);
 
-  return true;
-}
-
-// The same share of a tile in two passes over the chunks (sp.two_pass: few
-// chains, so that consecutive tiles of a batch row run at the same time and
-// the state chain from tile to tile along a batch row, the link records,
-// bounds the launch).  The chain then waits only on the short step between
-// the passes:
-//   pass 1   nothing from the tile before is needed.  Per chunk: z combined
-//            from the TMEM products as in the plain epilogue, staged
-//            (128-byte swizzle) and written by a TMA tensor store to p.out
-//            (the (F,B,T) backward reads it), and written back into the
-//            chunk's TMEM columns it was read from; the drive
-//            b[k] = tap0 z[k] + tap1 z[k-1] (fbt_drive, z before the tile
-//            taken as zero) and the lane's fold of its 8 drives from a zero
-//            state, A = sum_k c1^(7-k) b[k], kept in the lane's entry slot;
-//   chain    with {y, z} at the sample before the tile (the link record that
-//            the tile before it along time, tile - chains, published; zero at
-//            the start of a batch row), both lanes of a pair compose the
-//            entries of all chunks: the even lane enters with the running
-//            state E, the odd lane with c1^8 E + A_even, and E becomes
-//            c1^8 (that) + A_odd; chunk 0's A_even gains c1^7 tap1 z_before,
-//            the drive term pass 1 left out.  The tile then publishes {E, z}
-//            at its last sample for the tile after it;
-//   pass 2   per chunk: z back from TMEM, the drive again, y = c1 y + b[k]
-//            from the lane's entry (the operations that the (F,B,T) backward
-//            replays from the saved entry, so its split-ReLU mask is this
-//            one), act = split-ReLU(y) or y, plus skip, staged and written by
-//            a TMA tensor store to sp.act.
-// Each lane loads its own 8 skip samples one chunk ahead in pass 2.  The z
-// and act stores of consecutive chunks alternate between the warp's two
-// staging buffers, each reused once the bulk store before the last one has
-// finished reading it (bulk_wait_read<1>).  The entries are the saved context
-// slots of the lanes' 8 samples, written as in scan_epilogue.  False on an
-// abort.
-__device__ __forceinline__ bool scan_epilogue_2p(uint32_t tbase, float4 *stage, const Params &p,
-                                                 const ScanParams &sp, long long tile, int mp,
-                                                 int nt, int rank, int quarter, int lane,
-                                                 volatile int *abort) {
-  const bool odd = (lane & 1) != 0;
-  const int r_own = lane >> 1;
-  const long long jw0 = ((long long)mp * kPairM + (long long)rank * kBM + quarter * 32) >> 1;
-  const long long jrow = jw0 + r_own;
-  const bool row_ok = jrow < p.M;
-  const bool warp_ok = jw0 < p.M;  // some row of the warp's 16 exists
-  const int bidx = nt / sp.tiles_per_row;
-  const int pos = nt - bidx * sp.tiles_per_row;
-  const long long tfirst = (long long)pos * (kBN / 2);  // first sample in the batch row
-  const long long n0 = (long long)nt * (kBN / 2);       // first sample in N
-  const float2 lam = row_ok ? __ldg(sp.c1 + jrow) : cz();
-  const float2 tap0 = row_ok ? __ldg(sp.tap0 + jrow) : cz();
-  const float2 tap1 = row_ok ? __ldg(sp.tap1 + jrow) : cz();
-  unsigned *abort_word = sp.flags + p.num_tiles * 8;
-  const bool has_skip = sp.skip != nullptr;
-  const bool lane_skip = has_skip && row_ok;
-  // this lane's 8 skip samples of chunk c: the 64 bytes at skrow + 8 c
-  const float4 *skrow =
-      lane_skip ? reinterpret_cast<const float4 *>(sp.skip + jrow * p.N + n0 + (odd ? 8 : 0))
-                : nullptr;
-  if (has_skip && lane < 16 && jw0 + lane < p.M)  // the tile's 1 KB of each row, into L2
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], 1024;" ::"l"(sp.skip + (jw0 + lane) * p.N + n0)
-                 : "memory");
-  // staging: two buffers of 16 rows x 128 B, at stage and stage + 128
-  float2 *ent = reinterpret_cast<float2 *>(stage + 256);  // [16 rows][16 slots], swizzled
-  // this lane's slot of chunk c in ent (its partner's: slot ^ 1)
-  auto slot = [&](int c) { return r_own * 16 + ((c ^ (r_own & 7)) << 1) + (odd ? 1 : 0); };
-  // stage 16 rows x 16 samples (the lanes' 8 each) and store them to `map` at chunk c
-  auto stage_store = [&](int c, const CUtensorMap *map, const float2 (&v)[8]) {
-    float4 *buf = stage + ((c & 1) ? 128 : 0);
-    if (lane == 0) bulk_wait_read<1>();  // the store before the last one has read this buffer
-    __syncwarp();
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-      buf[r_own * 8 + (((odd ? 4 : 0) + q) ^ (r_own & 7))] =
-          make_float4(v[2 * q].x, v[2 * q].y, v[2 * q + 1].x, v[2 * q + 1].y);
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      if (warp_ok) tma_store_2d(map, buf, (int)(2 * (n0 + c * 16)), (int)jw0);
-      bulk_commit();
-    }
-  };
-
-  // pass 1: z, its store, and each lane's fold from zero
-  float2 zl = cz();  // z at the sample before the chunk (zero before the tile)
-#pragma unroll 1
-  for (int c = 0; c < kBN / 32; ++c) {
-    float v[32];
-    tc_ld_32x32b_x32(tbase + (uint32_t)(c * 32), v);
-    float r[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) r[i] = __shfl_xor_sync(0xffffffffu, odd ? v[i] : v[16 + i], 1);
-    float2 z[8];
-    float zz[16];
-#pragma unroll
-    for (int t = 0; t < 8; ++t) {
-      const float pr_re = odd ? r[2 * t] : v[2 * t];
-      const float pr_im = odd ? r[2 * t + 1] : v[2 * t + 1];
-      const float pi_re = odd ? v[16 + 2 * t] : r[2 * t];
-      const float pi_im = odd ? v[16 + 2 * t + 1] : r[2 * t + 1];
-      z[t] = make_float2(pr_re - pi_im, pr_im + pi_re);
-      zz[2 * t] = z[t].x;
-      zz[2 * t + 1] = z[t].y;
-    }
-    tc_st_32x32b_x16(tbase + (uint32_t)(c * 32), zz);  // columns already read above
-    stage_store(c, &sp.tmZ, z);
-    // drives; the odd lane's z before its first sample is the even lane's last
-    const float2 zx = shfl_xor2(z[7], 1);
-    float2 bd[8];
-    fbt_drive<8>(tap0, tap1, z, odd ? zx : zl, bd);
-    zl = odd ? z[7] : zx;  // both lanes: z at the chunk's last sample
-    float2 y = cz();
-#pragma unroll
-    for (int k = 0; k < 8; ++k) y = c_fma(lam, y, bd[k]);
-    ent[slot(c)] = y;
-  }
-  const float2 zlast = zl;  // z at the tile's last sample
-  tc_wait_st();
-
-  // chain: the entries of every lane and chunk from the state before the tile
-  float2 E = cz(), zb = cz();  // y and z at the sample before the tile
-  if (pos > 0) {
-    const long long pred = (tile - sp.chains) * 2 + rank;
-    const bool ok = scan_link_wait(sp.flags + pred * 4 + quarter, abort_word, abort);
-    if (!__all_sync(0xffffffffu, ok)) return false;
-    const float4 l = __ldcg(sp.link + pred * 64 + quarter * 16 + r_own);
-    E = make_float2(l.x, l.y);
-    zb = make_float2(l.z, l.w);
-  }
-  __syncwarp();
-  {
-    const float2 l2 = c_mul(lam, lam), l4 = c_mul(l2, l2), l8 = c_mul(l4, l4);
-    const float2 l7 = c_mul(c_mul(l4, l2), lam);
-    float2 ae[8], ao[8];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const int s0 = slot(c) & ~1;
-      ae[c] = ent[s0];
-      ao[c] = ent[s0 + 1];
-    }
-    __syncwarp();
-    ae[0] = c_fma(c_mul(l7, tap1), zb, ae[0]);
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const float2 X = c_fma(l8, E, ae[c]);
-      ent[slot(c)] = odd ? X : E;
-      E = c_fma(l8, X, ao[c]);
-    }
-  }
-
-  // publish {y, z} at the tile's last sample for the tile after it, before
-  // pass 2: the tile after it along time waits on this
-  if (pos + 1 < sp.tiles_per_row) {
-    const long long me = tile * 2 + rank;
-    if (odd) sp.link[me * 64 + quarter * 16 + r_own] = make_float4(E.x, E.y, zlast.x, zlast.y);
-    __threadfence();
-    __syncwarp();
-    if (lane == 0) st_release_u32(sp.flags + me * 4 + quarter, 1u);
-  }
-  __syncwarp();
-
-  // pass 2: outputs from the entries
-  float4 skn[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-    skn[i] = lane_skip ? __ldg(skrow + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-  zl = zb;
-#pragma unroll 1
-  for (int c = 0; c < kBN / 32; ++c) {
-    float4 sk[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) sk[i] = skn[i];
-    if (lane_skip && c + 1 < kBN / 32) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) skn[i] = __ldg(skrow + 8 * (c + 1) + i);
-    }
-    float zz[16];
-    tc_ld_32x32b_x16(tbase + (uint32_t)(c * 32), zz);
-    float2 z[8];
-#pragma unroll
-    for (int t = 0; t < 8; ++t) z[t] = make_float2(zz[2 * t], zz[2 * t + 1]);
-    const float2 zx = shfl_xor2(z[7], 1);
-    float2 bd[8];
-    fbt_drive<8>(tap0, tap1, z, odd ? zx : zl, bd);
-    zl = odd ? z[7] : zx;
-    float2 e = ent[slot(c)];
-    float2 o[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      e = c_fma(lam, e, bd[k]);
-      const float2 a = sp.fuse_act ? c_relu(e) : e;
-      const float4 s = sk[k >> 1];
-      o[k] = (k & 1) ? make_float2(a.x + s.z, a.y + s.w) : make_float2(a.x + s.x, a.y + s.y);
-    }
-    stage_store(c, &sp.tmAct, o);
-  }
-  scan_save_entries(ent, p, sp, jw0, bidx, pos, tfirst, lane);
   return true;
 }
 
@@ -1499,11 +1271,7 @@ proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           __syncwarp();
         }
       } else if constexpr (kScan == kScanFwd) {
-        const bool ok2 =
-            sp.two_pass
-                ? scan_epilogue_2p(tbase, stage, p, sp, tile, mp, nt, rank, quarter, lane, abort)
-                : scan_epilogue(tbase, stage, p, sp, tile, mp, nt, rank, quarter, lane, abort);
-        if (!ok2) break;
+        if (!scan_epilogue(tbase, stage, p, sp, tile, mp, nt, rank, quarter, lane, abort)) break;
       } else if constexpr (kScan == kScanBwd) {
         if (!scan_bwd_epilogue(tbase, stage, p, sp, tile, mp, nt, rank, quarter, lane, ring,
                                abort))

@@ -1427,12 +1427,6 @@ int projection_impl(const float *w, const float *x, const float *acc, float *out
     // persistent grid is the device's pair capacity at most.
     proj::ScanParams sp = *scan;
     sp.chains = p.m_pairs * sp.batch;
-    // Few chains (at most half the CTA pairs): consecutive tiles of a batch
-    // row run at the same time and the state chain between them bounds the
-    // forward; the two-pass epilogue cuts that chain to the step between its
-    // passes (F = 256, T = 16000: B = 16 1.21 -> 0.96 ms), while with more
-    // chains the single pass is faster (B = 32: 1.42 against 1.87 ms).
-    sp.two_pass = (scan_mode == proj::kScanFwd && 2 * (long long)sp.chains <= grid / 2) ? 1 : 0;
     if (scan_mode == proj::kScanBwd)
       proj::proj_kernel<false, proj::kScanBwd>
           <<<(unsigned)grid, proj::kThreads, proj::kScanBwdSmemBytes, st>>>(tmA, tmX, p, sp);

@@ -55,8 +55,7 @@ def _case(F, K, B, T, seed):
     return [torch.from_numpy(a).cuda() for a in (W, h, c1, t0, t1)]
 
 
-# (F, K, B, T).  The forward's epilogue runs in two passes when the chains
-# (row blocks x batch rows) are at most half the CTA pairs, else in one pass.
+# (F, K, B, T)
 SHAPES = [
     (64, 64, 2, 256),      # F below one pair tile's 128 filters
     (128, 96, 3, 2176),    # two context tiles, the second cut at 128 samples
@@ -64,8 +63,8 @@ SHAPES = [
     (96, 96, 1, 128),      # one GEMM tile per row, one chain per row block
     (200, 136, 5, 1920),   # ragged F and K, T below one context tile
     (128, 128, 1, 8192),   # a single chain: 64 tiles, each waiting on the last
-    (128, 128, 96, 256),   # more chains than CTA pairs: the single pass
-    (256, 256, 40, 256),   # two row blocks, 80 chains: the single pass
+    (128, 128, 96, 256),   # more chains than CTA pairs
+    (256, 256, 40, 256),   # two row blocks, 80 chains
 ]
 
 
@@ -120,9 +119,8 @@ def test_block_scan_vs_oracle(F, K, B, T, fuse, with_skip):
 def test_block_scan_saved_entries(T, B):
     """The saved context holds the raw state entering every 8-sample group
     (slot s of context tile j of row (f, b): y[f, b, 2048 j + 8 s - 1]), zero
-    in the slots past T, and the every-thread marker (1, 0) after the slots.
-    B = 3 runs the two-pass epilogue, B = 40 (more chains than half the CTA
-    pairs) the single pass."""
+    in the slots past T, and the every-thread marker (1, 0) after the slots,
+    with few chains (B = 3) and with more than half the CTA pairs (B = 40)."""
     from prospective_rqf_b200 import _abi, ops
 
     F, K = 128, 64
