@@ -7,7 +7,7 @@
 One step = one full training step of the Pure RQF encoder (depth 6,
 prospective two-tap input, skip connections) on one synthetic batch:
 forward, loss, backward, gradient all-reduce across ranks (N > 1), clip,
-AdamW, clamp of the filter leaves.  Default workload: BASELINE config 5 per
+AdamW, clamp of the filter leaves.  Default workload: benchmark config 5 per
 GPU (H=256, 32 samples/GPU, T=16000, full BPTT), weak scaling over N ranks.
 
 `value`  = global samples / s with inputs resident in HBM (max over ranks).
@@ -502,7 +502,7 @@ def reference_cpu_paths(cfg, threads: int):
     """The reference's own CPU PyTorch path, timed on the host cores:
     PureRQFEncoder forward+backward (per sample, at reduced T: its CPU
     backward does not finish a T=16000 sample in minutes) and config 1's
-    sequential_scan op (exact BASELINE shape)."""
+    sequential_scan op (the exact benchmark shape)."""
     PureRQFEncoder = _reference_modules()
     if PureRQFEncoder is None:
         return {"unavailable": "reference install (baseline/_ref) absent"}

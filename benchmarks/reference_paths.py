@@ -3,7 +3,7 @@ same machine:
 - its GPU path (its Triton kernels and its Pure RQF encoder) on the same B200,
   same shapes, same CUDA-event method;
 - its CPU PyTorch path on the box's host cores (config 1: sequential_scan
-  forward + backward on the exact BASELINE tensors; config-2 scale:
+  forward + backward on the exact benchmark tensors; config-2 scale:
   parallel_scan on one batch row), beside this backend's GPU op.
 
 The reference comes from its offline install:
@@ -138,7 +138,7 @@ def encoder(out):
     from prospective_rqf_b200.encoder import PureRQFEncoderB200
 
     B, T, H = 32, 16000, 256
-    # configs/model/pure_rqf_paper.yaml with BASELINE config 5's width, depth and skip
+    # configs/model/pure_rqf_paper.yaml with benchmark config 5's width, depth and skip
     ref = PureRQFEncoder(input_dims=1, output_dims=32, hidden_dims=H, num_layers=6,
                          samp_frequency=16000.0, min_freq=1.0, max_freq=8000.0, tau=0.0003125,
                          discretization="zoh", activation="split_relu", complex_weights=True,

@@ -344,8 +344,8 @@ int rqf_selective_backward(const float *z, const rqf_selective_inputs *inputs,
 /* ---- selective scan, bf16 storage mode -------------------------------- *
  * No counterpart in the reference, whose selective kernel requires fp32
  * logits and complex64 activations (rqf_models/ops/selective_scan.py:187-198):
- * the storage mode of BASELINE config 3 ("bf16 activations, fp32 complex
- * state").  Same arguments and arithmetic as rqf_selective_forward /
+ * the storage mode of the selective benchmark configuration ("bf16
+ * activations, fp32 complex state").  Same arguments and arithmetic as rqf_selective_forward /
  * _backward, except that the three logit pointers of `inputs` address bf16
  * (2-byte) elements, raw / act are written as interleaved bf16 pairs
  * (F,B,T,2), and the logit cotangents dgamma / dwarp / dwrite are written in

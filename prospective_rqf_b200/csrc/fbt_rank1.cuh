@@ -1,5 +1,5 @@
 // The first Pure RQF block over a rank-1 input (input_dims == 1: the waveform
-// models of BASELINE configs 2 and 5), with the block's drive and skip made
+// classification models, one input channel), with the block's drive and skip made
 // inside the (F,B,T) row kernels from the 4-byte input instead of read from
 // HBM (rqf_models/backbones/rqf/pure.py:_forward_fbt_stack :510-534 and
 // PureRQFBlock._forward_fbt :212-243):

@@ -1,6 +1,6 @@
 // Persistent row-sequential variant of the (F,B,T) two-tap scan, used when
-// there are at least as many rows as resident CTAs (3 and
-// 5 have 2k-8k rows of 16k samples).
+// there are at least as many rows as resident CTAs (the benchmarked waveform
+// and selective layers have 2k-8k rows of 4k-16k samples).
 //
 // Each CTA owns rows blockIdx.x, blockIdx.x + gridDim.x, ... and walks each
 // row tile by tile, keeping the recurrence carry on chip between tiles, so no

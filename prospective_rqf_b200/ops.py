@@ -958,8 +958,8 @@ def selective_backward(z, inputs, entries, gy, gx, activate, truncated, chunk=No
 
 def selective_forward_bf16(z, inputs, activate, write_raw):
     """The bf16 storage mode of selective_forward (rqf_selective_forward_bf16;
-    no reference counterpart: BASELINE config 3's "bf16 activations, fp32
-    state").  The logits of `inputs` are read as bf16 (converted if given in
+    no reference counterpart: the selective benchmark configuration's "bf16
+    activations, fp32 state").  The logits of `inputs` are read as bf16 (converted if given in
     another dtype); raw and act are returned as bf16 (F, B, T, 2) [Re, Im]
     pairs.  z, the carries and all arithmetic stay fp32."""
     dev = _require_cuda(z)

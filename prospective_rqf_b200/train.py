@@ -8,7 +8,7 @@ backward, one NCCL all-reduce of the flat parameter gradients across ranks
 shards with no exchange inside the scan), gradient clipping, AdamW, and the
 post-step clamp of the log-space filter leaves.
 
-Synthetic inputs follow BASELINE configs 2 and 5: each waveform is a sum of 3
+Synthetic inputs follow the benchmarked waveform workloads: each waveform is a sum of 3
 sinusoids (freq ~ U(50, 4000) Hz at fs = 16 kHz, amplitude ~ U(0.1, 0.5)) plus
 N(0, 0.05) noise, clipped to [-1, 1]; labels uniform over 35 classes.  The
 Speech Commands audio the reference trains on is not available here.
@@ -45,9 +45,9 @@ class StepConfig:
 
 
 WORKLOADS = {
-    # Pure RQF depth 6, H=128, [B=16, T=16000, 1], full BPTT
+    # config 2: Pure RQF depth 6, H=128, [B=16, T=16000, 1], full BPTT
     "cfg2": StepConfig(name="cfg2", batch=16, hidden=128),
-    # BASELINE config 5 per-rank shard: H=256, 32 samples per GPU, full BPTT / TBPTT(1)
+    # config 5 per-rank shard: H=256, 32 samples per GPU, full BPTT / TBPTT(1)
     "cfg5-full": StepConfig(name="cfg5-full", batch=32, hidden=256),
     "cfg5-tbptt": StepConfig(name="cfg5-tbptt", batch=32, hidden=256, scan_grad_mode="tbptt1"),
 }
@@ -55,7 +55,7 @@ WORKLOADS = {
 
 def waveform_batch(batch: int, time: int, fs: float, num_classes: int,
                    generator: torch.Generator, device="cpu"):
-    """(x (B,T,1) float32 in [-1, 1], y (B,) int64) — BASELINE config 2/5 generator.
+    """(x (B,T,1) float32 in [-1, 1], y (B,) int64) — the config 2/5 waveform generator.
 
     Drawn on the generator's device: a CUDA generator makes the whole batch on
     the GPU (no host work or copy per step); a CPU generator draws on the host

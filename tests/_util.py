@@ -8,7 +8,7 @@ import numpy as np
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
 
-# BASELINE tolerances (fp32 kernels against the fp64 oracle):
+# The benchmark's stated tolerances (fp32 kernels against the fp64 oracle):
 FWD_TOL = 1e-4   # forward: max |a - b| / max |b|
 GRAD_TOL = 1e-3  # gradients: max |a - b| / max |b|
 

@@ -15,7 +15,7 @@ Every fixture is produced by calling the REFERENCE implementation
   (TRITON_INTERPRET=1, fp32): chunked_scan_kernel._triton_chunked_scan,
   _triton_chunked_scan_prospective, fbt_scan_kernel.fbt_recompute_scan and
   fbt_prospective_scan.
-* scan.py:sequential_scan on CPU (fp32), the BASELINE config-1 entry point.
+* scan.py:sequential_scan on CPU (fp32), the config-1 benchmark entry point.
 
 Outputs: tests/golden/*.npz (small; committed).  Nothing at test time reads
 the reference tree.
@@ -96,7 +96,7 @@ def case_scan_complex(out):
 
 
 def case_scan_real_cfg1(out):
-    """BASELINE config 1 generator at reduced size: real u ~ N(0,1),
+    """Config 1 generator at reduced size: real u ~ N(0,1),
     lambda = r e^{i theta}, r ~ U(0.90, 0.999), theta ~ U(0, pi),
     b ~ CN(0,1)/sqrt(2), loss = sum |y|^2.  Reference: scan.py:sequential_scan
     on CPU (fp32) and parallel_scan with complex128 coefficients (fp64)."""

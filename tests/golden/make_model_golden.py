@@ -64,7 +64,7 @@ def _classifier_class(reference: str):
 
 
 def _waveforms(batch, time, seed):
-    """Sum of three sinusoids plus noise, clipped (the BASELINE waveform draw)."""
+    """Sum of three sinusoids plus noise, clipped (the benchmark's waveform draw)."""
     import torch
 
     g = torch.Generator().manual_seed(seed)

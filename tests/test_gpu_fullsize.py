@@ -1,4 +1,4 @@
-"""Parity at the BASELINE configurations' full sizes, against the fp64 oracle.
+"""Parity at the benchmark configurations' full sizes, against the fp64 oracle.
 
 Each test runs one full-size launch pair (forward and backward) of the shape a
 configuration times, then checks it against the oracle:

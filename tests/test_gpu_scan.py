@@ -1,7 +1,7 @@
 """GPU parity of the sm_100a scan kernels (through the C ABI) against the
 fp64 CPU oracle and the reference's golden vectors.
 
-Tolerances (written here, from the BASELINE contract): forward normwise max
+Tolerances (written here, from the benchmark's stated bounds): forward normwise max
 relative error <= 1e-4, gradients <= 1e-3, fp32 kernels vs fp64 oracle.
 """
 
@@ -340,7 +340,7 @@ def test_scan_abs_epilogue_vs_oracle(B, T, F, real, btf_path):
 
 
 def test_config1_exact_shapes(btf_path):
-    """u real [32,161,128] ~ N(0,1), lambda = r e^{i theta},
+    """Benchmark config 1: u real [32,161,128] ~ N(0,1), lambda = r e^{i theta},
     r ~ U(0.90, 0.999), theta ~ U(0, pi), b ~ CN(0,1)/sqrt(2), y0 = 0; grads of
     sum |y|^2 w.r.t. u, lambda and b."""
     g = torch.Generator().manual_seed(0)
