@@ -385,23 +385,43 @@ class _InputTBPTT(torch.autograd.Function):
     scan, then out = y + h0.  With G = gz0 [x; 1]^T and Gs = (gz0 + gzw) [x; 1]^T
     (the kernel returns gz0 + gzw):
       gW = (gz0 + gzw) h0^H = Gs [w_in, b_in]^T
-      grad [w_in, b_in] = Re(W^H G + g [x; 1]^T)   (the lag cotangent updates W only)."""
+      grad [w_in, b_in] = Re(W^H G + g [x; 1]^T)   (the lag cotangent updates W only).
+
+    The forward is the full-BPTT block's: with one input channel it runs on
+    the rank-1 kernel (z0 and the skip made from x inside the scan, the skip
+    add fused), and the backward then makes z0 again with rqf_lowrank_drive
+    (the same fmaf operations, so the TBPTT(1) kernel replays the forward's
+    states bit for bit from the saved entries)."""
 
     @staticmethod
     def forward(ctx, x_cf, w_in, b_in, W, C1, tap0, tap1, fuse_act, skip, B, T):
         F = W.shape[0]
         beta = W @ b_in.to(torch.complex64) if b_in is not None else None
-        z, h0 = ops.lowrank_drive(W @ w_in.to(torch.complex64), x_cf, beta,
-                                  w_in if skip else None, b_in)
+        U = W @ w_in.to(torch.complex64)
+        ctx.rank1 = w_in.shape[1] == 1 and ops.rank1_supported(F, B, T)
+        ctx.fuse_act, ctx.skip = bool(fuse_act), bool(skip)
+        ctx.B, ctx.T = B, T
+        if ctx.rank1:
+            out, saved = ops.rank1_block_forward(U[:, 0], beta, w_in[:, 0] if skip else None,
+                                                 b_in, x_cf.view(B, T), C1, tap0, tap1,
+                                                 bool(fuse_act))
+            c1, t0, t1, _, _, _, carries = saved
+            ctx.save_for_backward(x_cf, w_in, b_in, W, c1, t0, t1, carries)
+            return out
+        z, h0 = ops.lowrank_drive(U, x_cf, beta, w_in if skip else None, b_in)
         y, saved = ops._fbt_forward(C1, tap0, tap1, z.view(F, B, T), bool(fuse_act))
         ctx.save_for_backward(x_cf, w_in, b_in, W, *saved)
-        ctx.fuse_act, ctx.skip = bool(fuse_act), bool(skip)
         return y + h0.view(F, B, T) if skip else y
 
     @staticmethod
     @once_differentiable
     def backward(ctx, g):
         x_cf, w_in, b_in, W, *saved = ctx.saved_tensors
+        if ctx.rank1:  # z0 again, as the rank-1 forward made it
+            c1, t0, t1, carries = saved
+            beta = W @ b_in.to(torch.complex64) if b_in is not None else None
+            z, _ = ops.lowrank_drive(W @ w_in.to(torch.complex64), x_cf, beta)
+            saved = (c1, t0, t1, z.view(W.shape[0], ctx.B, ctx.T), carries)
         gc1, gt0, gt1, gz, gsum = ops._tbptt_backward_wsum(saved, g, ctx.fuse_act)
         need = ctx.needs_input_grad
         I, has_b = w_in.shape[1], b_in is not None

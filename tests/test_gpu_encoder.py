@@ -479,3 +479,41 @@ def test_rank1_first_block_matches_general_path(bias, skip, T, monkeypatch):
     for n in g1:
         e = rel_err(g1[n].cpu().numpy(), g2[n].cpu().numpy())
         assert e <= 1e-4, f"{n}: {e:.2e}"
+
+
+@pytest.mark.parametrize("bias,skip,T", [(False, True, 4000), (True, False, 1004)])
+def test_rank1_first_block_tbptt_matches_general_path(bias, skip, T, monkeypatch):
+    """The TBPTT(1) encoder's first layer over a one-channel input: its forward
+    on the rank-1 kernel (the backward makes z0 again with rqf_lowrank_drive)
+    against rqf_lowrank_drive + the row forward + the torch skip add: the
+    features bit-identical, every parameter gradient within fp32 summation-order
+    noise (the TBPTT(1) backward replays the same states)."""
+    from prospective_rqf_b200 import _timing, ops
+    from prospective_rqf_b200 import encoder as E
+
+    def run(rank1):
+        if not rank1:
+            monkeypatch.setattr(ops, "rank1_supported", lambda *a: False)
+        torch.manual_seed(0)
+        enc = E.PureRQFEncoderB200(input_dims=1, hidden_dims=128, num_layers=2,
+                                   skip_connection=skip, input_proj_bias=bias, seed=4,
+                                   scan_grad_mode="tbptt1")
+        model = E.RQFClassifier(enc, 5, 32).cuda()
+        g = torch.Generator().manual_seed(6)
+        x = (0.5 * torch.randn(8, T, 1, generator=g)).clamp(-1, 1).cuda()
+        y = torch.randint(0, 5, (8,), generator=g).cuda()
+        with _timing.KernelTimer() as tm:
+            feats = model.encoder(x)
+            logits = model.readout(feats)
+            torch.nn.functional.cross_entropy(logits, y).backward()
+        grads = {n: p.grad.detach().clone() for n, p in model.named_parameters()}
+        return feats.detach().clone(), grads, set(tm.summary())
+
+    f1, g1, k1 = run(True)
+    assert "rqf_fbt_rank1_forward" in k1
+    f2, g2, k2 = run(False)
+    assert "rqf_fbt_rank1_forward" not in k2
+    assert torch.equal(f1, f2), "features differ from the general first layer"
+    for n in g1:
+        e = rel_err(g1[n].cpu().numpy(), g2[n].cpu().numpy())
+        assert e <= 1e-4, f"{n}: {e:.2e}"
