@@ -257,6 +257,21 @@ int rqf_fbt_rank1_backward(const float *u, const float *beta, const float *x, co
                            float *grad_tap0, float *grad_tap1, void *scratch, int64_t filters,
                            int64_t batch, int64_t time, int fuse_act, int with_sum,
                            rqf_stream_t stream);
+/* The TBPTT(1) surrogate of the same block (the gradients of
+ * rqf_fbt_tbptt1_backward_wsum, rqf_models/backbones/rqf/pure.py:184-187 with
+ * the lag source the same projection as z): no adjoint recursion, d = the
+ * masked output cotangent, grad_z = conj(tap0) d, the lag cotangent
+ * conj(tap1) d[t+1].  gzx = [sum gz x, sum gz] (the input projection's
+ * term), gwx = [sum gsum x, sum gsum] with gsum = grad_z + the lag cotangent
+ * (the weight cotangent's), gsx = [sum g x, sum g] (nullable); the plain
+ * sums only with with_sum.  Same context, shapes and errors as
+ * rqf_fbt_rank1_backward. */
+int rqf_fbt_rank1_tbptt_backward(const float *u, const float *beta, const float *x,
+                                 const float *c1, const float *tap0, const float *tap1,
+                                 const float *carries, const float *grad_out, float *gzx,
+                                 float *gwx, float *gsx, float *grad_c1, float *grad_tap0,
+                                 float *grad_tap1, void *scratch, int64_t filters, int64_t batch,
+                                 int64_t time, int fuse_act, int with_sum, rqf_stream_t stream);
 
 /* ---- TBPTT(1) two-tap surrogate backward ----------------------------- *
  * The forward value of the reference's TBPTT(1) path equals the exact scan

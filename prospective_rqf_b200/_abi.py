@@ -123,6 +123,9 @@ SIGNATURES: dict[str, tuple] = {
     "rqf_fbt_rank1_backward": (
         _int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int,
                _int, _p]),
+    "rqf_fbt_rank1_tbptt_backward": (
+        _int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64,
+               _int, _int, _p]),
     "rqf_fbt_tbptt1_backward_wsum": (
         _int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "rqf_projection_block_scan_backward_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64]),

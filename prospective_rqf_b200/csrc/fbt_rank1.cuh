@@ -160,9 +160,15 @@ __global__ void __launch_bounds__(NT) fbt_rank1_fwd_kernel(const FbtArgs a, cons
 // Tiles of a row in reverse time order, as fbt_bwd_rows_kernel, with z made
 // from x and the forward's per-thread entry states (required: the forward of
 // this file saves them).  Per row: the coefficient sums into a.partials
-// (rows, 3) and the four row sums into r.rowsums (rows, 4); the two plain
-// sums (sum gz, sum g: the bias's terms) only with WSUM, zero otherwise.
-template <int NT, int K, int S, bool FUSE_ACT, bool WSUM>
+// (rows, 3) and the row sums into r.rowsums (rows, 4; rows, 6 with TRUNC);
+// the plain sums (sum gz, sum g, sum gsum: the bias's terms) only with WSUM,
+// zero otherwise.
+// TRUNC: the TBPTT(1) surrogate (the (F,B,T) TBPTT(1) kernels' gradients):
+// no adjoint recursion, d[t] = mask(y[t]) g[t]; grad_z[t] = conj(tap0) d[t]
+// and the lag tap's cotangent conj(tap1) d[t+1], whose sum with it (gsum)
+// takes the weight cotangent.  Row sums: {sum gz x, sum gz, sum g x, sum g,
+// sum gsum x, sum gsum}.
+template <int NT, int K, int S, bool FUSE_ACT, bool WSUM, bool TRUNC = false>
 __global__ void __launch_bounds__(NT, 3) fbt_rank1_bwd_kernel(const FbtArgs a, const Rank1Args r) {
   constexpr int NW = NT / 32, L = NT * K, LK = (K == 4) ? 2 : (K == 8) ? 3 : 4;
   constexpr int WSZ = 16 * K;
@@ -262,16 +268,19 @@ __global__ void __launch_bounds__(NT, 3) fbt_rank1_bwd_kernel(const FbtArgs a, c
       if constexpr (WSUM) sg = c_add(sg, go[k]);
     }
     const float2 mu = c_conj(lam);
-    float2 h = cz();
+    float2 gnext = cz();
+    if constexpr (!TRUNC) {
+      float2 h = cz();
 #pragma unroll
-    for (int k = K - 1; k >= 0; --k) h = c_fma(mu, h, b[k]);
-    float2 gnext, Art;
-    cta_scan_entry_rev<NT, LK>(h, dcarry, pw, lpow_r, gnext, Art, s_warp_r);
-    dcarry = Art;
+      for (int k = K - 1; k >= 0; --k) h = c_fma(mu, h, b[k]);
+      float2 Art;
+      cta_scan_entry_rev<NT, LK>(h, dcarry, pw, lpow_r, gnext, Art, s_warp_r);
+      dcarry = Art;
+    }
     float2 pc1 = cz(), qc1 = cz();
 #pragma unroll
     for (int k = K - 1; k >= 0; --k) {
-      const float2 g = c_fma(mu, gnext, b[k]);
+      const float2 g = TRUNC ? b[k] : c_fma(mu, gnext, b[k]);
       const float2 xx = make_float2(xv[k], xv[k]);
       const float xpk = k > 0 ? xv[k - 1] : xp;
       sd = c_add(sd, g);
@@ -305,24 +314,31 @@ __global__ void __launch_bounds__(NT, 3) fbt_rank1_bwd_kernel(const FbtArgs a, c
         s_red[tid][0] = sum;  // each thread reads and writes only its own q
       }
       __syncthreads();
-      if (tid < 7) {
+      if (tid < (TRUNC ? 9 : 7)) {
         const float2 Sd = s_red[1][0], Sxd = s_red[2][0], Sxpd = s_red[3][0];
         const float2 Sd1 = make_float2(Sd.x - s_red[6][0].x, Sd.y - s_red[6][0].y);  // d past t = 0
         const float2 cu = c_conj(u), cb = c_conj(be), ct0 = c_conj(t0), ct1 = c_conj(t1);
+        // with the adjoint recursion gz[t] = conj(tap0) d[t] + conj(tap1) d[t+1]
+        // (sum x[t] d[t+1] = sxpd); TRUNC: gz[t] = conj(tap0) d[t], and gsum has
+        // the recursion's form
+        const float2 lag_x = c_add(c_mul(ct0, Sxd), c_mul(ct1, Sxpd));
+        const float2 lag_1 = WSUM ? c_add(c_mul(ct0, Sd), c_mul(ct1, Sd1)) : cz();
         float2 v;
         switch (tid) {
           case 0: v = s_red[0][0]; break;                                  // conj(y[t-1]) d
           case 1: v = c_add(c_mul(cu, Sxd), c_mul(cb, Sd)); break;        // conj(z[t]) d
           case 2: v = c_add(c_mul(cu, Sxpd), c_mul(cb, Sd1)); break;      // conj(z[t-1]) d
-          case 3: v = c_add(c_mul(ct0, Sxd), c_mul(ct1, Sxpd)); break;    // sum gz x
-          case 4: v = WSUM ? c_add(c_mul(ct0, Sd), c_mul(ct1, Sd1)) : cz(); break;  // sum gz
+          case 3: v = TRUNC ? c_mul(ct0, Sxd) : lag_x; break;             // sum gz x
+          case 4: v = TRUNC ? (WSUM ? c_mul(ct0, Sd) : cz()) : lag_1; break;  // sum gz
           case 5: v = s_red[4][0]; break;                                  // sum g x
-          default: v = s_red[5][0]; break;                                 // sum g
+          case 6: v = s_red[5][0]; break;                                  // sum g
+          case 7: v = lag_x; break;                                        // sum gsum x
+          default: v = lag_1; break;                                       // sum gsum
         }
         if (tid < 3)
           a.partials[(size_t)pc.row * 3 + tid] = v;
         else
-          r.rowsums[(size_t)pc.row * 4 + (tid - 3)] = v;
+          r.rowsums[(size_t)pc.row * (TRUNC ? 6 : 4) + (tid - 3)] = v;
       }
       pc1r = qc1r = sd = sxd = sxpd = sgx = sg = d0 = cz();
     }
@@ -331,20 +347,24 @@ __global__ void __launch_bounds__(NT, 3) fbt_rank1_bwd_kernel(const FbtArgs a, c
   cp_async_wait<0>();
 }
 
-// The sum over the batch of rowsums[(f * batch + b) * 4 + q], in increasing
-// b, in double: q = 0, 1 into gzx[f * 2 + q], q = 2, 3 into gsx[f * 2 + q - 2]
-// (gsx may be null).  One thread per (f, q).
+// The sum over the batch of rowsums[(f * batch + b) * R + q], R = 4 or 6, in
+// increasing b, in double: q = 0, 1 into gzx[f * 2 + q], q = 2, 3 into
+// gsx[f * 2 + q - 2], q = 4, 5 into gwx[f * 2 + q - 4] (gsx, gwx may be null).
+// One thread per (f, q).
 __global__ void reduce_rows4_kernel(const float2 *__restrict__ rowsums, float2 *__restrict__ gzx,
-                                    float2 *__restrict__ gsx, long long F, int batch) {
+                                    float2 *__restrict__ gsx, float2 *__restrict__ gwx,
+                                    long long F, int batch, int R) {
   const long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-  if (e >= F * 4) return;
-  const long long f = e >> 2;
-  const int q = (int)(e & 3);
-  float2 *dst = q < 2 ? gzx + f * 2 + q : (gsx ? gsx + f * 2 + (q - 2) : nullptr);
+  if (e >= F * R) return;
+  const long long f = e / R;
+  const int q = (int)(e - f * R);
+  float2 *dst = q < 2 ? gzx + f * 2 + q
+                : q < 4 ? (gsx ? gsx + f * 2 + (q - 2) : nullptr)
+                        : (gwx ? gwx + f * 2 + (q - 4) : nullptr);
   if (!dst) return;
   double re = 0.0, im = 0.0;
   for (int b = 0; b < batch; ++b) {
-    const float2 v = rowsums[(f * batch + b) * 4 + q];
+    const float2 v = rowsums[(f * batch + b) * R + q];
     re += v.x;
     im += v.y;
   }

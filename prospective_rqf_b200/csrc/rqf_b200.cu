@@ -764,7 +764,7 @@ int rqf_fbt_rank1_supported(int64_t filters, int64_t batch, int64_t time) {
 size_t rqf_fbt_rank1_scratch_bytes(int64_t filters, int64_t batch, int64_t time) {
   if (fbt_dims_ok(filters, batch, time) != RQF_OK) return SIZE_MAX;
   return round256((size_t)filters * batch * 3 * sizeof(float2)) +
-         round256((size_t)filters * batch * 4 * sizeof(float2));
+         round256((size_t)filters * batch * 6 * sizeof(float2));
 }
 
 int rqf_fbt_rank1_forward(const float *u, const float *beta, const float *w, const float *bb,
@@ -790,13 +790,16 @@ int rqf_fbt_rank1_forward(const float *u, const float *beta, const float *w, con
   return launch_status();
 }
 
-int rqf_fbt_rank1_backward(const float *u, const float *beta, const float *x, const float *c1,
-                           const float *tap0, const float *tap1, const float *carries,
-                           const float *grad_out, float *gzx, float *gsx, float *grad_c1,
-                           float *grad_tap0, float *grad_tap1, void *scratch, int64_t filters,
-                           int64_t batch, int64_t time, int fuse_act, int with_sum,
-                           rqf_stream_t stream) {
-  cudaStream_t sm = reinterpret_cast<cudaStream_t>(stream);
+extern "C++" {
+namespace {
+// Both rank-1 backwards: TRUNC the TBPTT(1) surrogate, which also returns gwx.
+template <bool TRUNC>
+int rank1_backward_impl(const float *u, const float *beta, const float *x, const float *c1,
+                        const float *tap0, const float *tap1, const float *carries,
+                        const float *grad_out, float *gzx, float *gwx, float *gsx, float *grad_c1,
+                        float *grad_tap0, float *grad_tap1, void *scratch, int64_t filters,
+                        int64_t batch, int64_t time, int fuse_act, int with_sum,
+                        cudaStream_t sm) {
   int st = fbt_dims_ok(filters, batch, time);
   if (st != RQF_OK) return st;
   if (filters == 0) return RQF_OK;
@@ -804,15 +807,17 @@ int rqf_fbt_rank1_backward(const float *u, const float *beta, const float *x, co
     for (float *p : {grad_c1, grad_tap0, grad_tap1})
       if ((st = zero_complex(p, filters, sm)) != RQF_OK) return st;
     if ((st = zero_complex(gzx, 2 * filters, sm)) != RQF_OK) return st;
+    if ((st = zero_complex(gwx, 2 * filters, sm)) != RQF_OK) return st;
     return zero_complex(gsx, 2 * filters, sm);
   }
   if (!rank1_shape_ok(filters, batch, time)) return RQF_ERR_SHAPE;
   if (!u || !x || !c1 || !tap0 || !tap1 || !carries || !grad_out || !gzx || !grad_c1 ||
-      !grad_tap0 || !grad_tap1 || !scratch)
+      !grad_tap0 || !grad_tap1 || !scratch || (TRUNC && !gwx))
     return RQF_ERR_ARGUMENT;
   if (!aligned(u, 8) || (beta && !aligned(beta, 8)) || !aligned(x, 16) || !aligned(c1, 8) ||
       !aligned(tap0, 8) || !aligned(tap1, 8) || !aligned(carries, 8) || !aligned(grad_out, 16) ||
-      !aligned(gzx, 8) || (gsx && !aligned(gsx, 8)) || !aligned(scratch, 16))
+      !aligned(gzx, 8) || (gsx && !aligned(gsx, 8)) || (gwx && !aligned(gwx, 8)) ||
+      !aligned(scratch, 16))
     return RQF_ERR_ALIGN;
   FbtArgs a = fbt_args(c1, tap0, tap1, nullptr, grad_out, nullptr, nullptr,
                        const_cast<float *>(carries), nullptr, filters, batch, time);
@@ -822,11 +827,11 @@ int rqf_fbt_rank1_backward(const float *u, const float *beta, const float *x, co
   Rank1Args r{reinterpret_cast<const float2 *>(u), reinterpret_cast<const float2 *>(beta),
               nullptr, nullptr, x, rowsums};
   const bool wsum = with_sum != 0;
-  auto kern =
-      fuse_act ? (wsum ? fbt_rank1_bwd_kernel<kFbtThreads, kFbtK, kRank1BwdStages, true, true>
-                       : fbt_rank1_bwd_kernel<kFbtThreads, kFbtK, kRank1BwdStages, true, false>)
-               : (wsum ? fbt_rank1_bwd_kernel<kFbtThreads, kFbtK, kRank1BwdStages, false, true>
-                       : fbt_rank1_bwd_kernel<kFbtThreads, kFbtK, kRank1BwdStages, false, false>);
+  constexpr int NT = kFbtThreads, K = kFbtK, S = kRank1BwdStages;
+  auto kern = fuse_act ? (wsum ? fbt_rank1_bwd_kernel<NT, K, S, true, true, TRUNC>
+                               : fbt_rank1_bwd_kernel<NT, K, S, true, false, TRUNC>)
+                       : (wsum ? fbt_rank1_bwd_kernel<NT, K, S, false, true, TRUNC>
+                               : fbt_rank1_bwd_kernel<NT, K, S, false, false, TRUNC>);
   const int64_t g = resident_ctas(kern, kFbtThreads, kRank1BwdSmem);
   kern<<<(unsigned)g, kFbtThreads, kRank1BwdSmem, sm>>>(a, r);
   if ((st = launch_status()) != RQF_OK) return st;
@@ -834,12 +839,37 @@ int rqf_fbt_rank1_backward(const float *u, const float *beta, const float *x, co
       a.partials, reinterpret_cast<float2 *>(grad_c1), reinterpret_cast<float2 *>(grad_tap0),
       reinterpret_cast<float2 *>(grad_tap1), batch, batch, 1, 1);
   if ((st = launch_status()) != RQF_OK) return st;
-  // (F, 2) sums {gz x, gz} into gzx and {g x, g} into gsx
-  reduce_rows4_kernel<<<(unsigned)ceil_div(filters * 4, 256), 256, 0, sm>>>(
-      rowsums, reinterpret_cast<float2 *>(gzx), reinterpret_cast<float2 *>(gsx), filters,
-      (int)batch);
-  if ((st = launch_status()) != RQF_OK) return st;
-  return RQF_OK;
+  // (F, 2) sums {gz x, gz} into gzx, {g x, g} into gsx and, TRUNC, {gsum x, gsum} into gwx
+  const int R = TRUNC ? 6 : 4;
+  reduce_rows4_kernel<<<(unsigned)ceil_div(filters * R, 256), 256, 0, sm>>>(
+      rowsums, reinterpret_cast<float2 *>(gzx), reinterpret_cast<float2 *>(gsx),
+      reinterpret_cast<float2 *>(gwx), filters, (int)batch, R);
+  return launch_status();
+}
+}  // namespace
+}  // extern "C++"
+
+int rqf_fbt_rank1_backward(const float *u, const float *beta, const float *x, const float *c1,
+                           const float *tap0, const float *tap1, const float *carries,
+                           const float *grad_out, float *gzx, float *gsx, float *grad_c1,
+                           float *grad_tap0, float *grad_tap1, void *scratch, int64_t filters,
+                           int64_t batch, int64_t time, int fuse_act, int with_sum,
+                           rqf_stream_t stream) {
+  return rank1_backward_impl<false>(u, beta, x, c1, tap0, tap1, carries, grad_out, gzx, nullptr,
+                                    gsx, grad_c1, grad_tap0, grad_tap1, scratch, filters, batch,
+                                    time, fuse_act, with_sum,
+                                    reinterpret_cast<cudaStream_t>(stream));
+}
+
+int rqf_fbt_rank1_tbptt_backward(const float *u, const float *beta, const float *x,
+                                 const float *c1, const float *tap0, const float *tap1,
+                                 const float *carries, const float *grad_out, float *gzx,
+                                 float *gwx, float *gsx, float *grad_c1, float *grad_tap0,
+                                 float *grad_tap1, void *scratch, int64_t filters, int64_t batch,
+                                 int64_t time, int fuse_act, int with_sum, rqf_stream_t stream) {
+  return rank1_backward_impl<true>(u, beta, x, c1, tap0, tap1, carries, grad_out, gzx, gwx, gsx,
+                                   grad_c1, grad_tap0, grad_tap1, scratch, filters, batch, time,
+                                   fuse_act, with_sum, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int rqf_fbt_prospective_backward(const float *c1, const float *tap0, const float *tap1,

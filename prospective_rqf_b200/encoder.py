@@ -389,9 +389,9 @@ class _InputTBPTT(torch.autograd.Function):
 
     The forward is the full-BPTT block's: with one input channel it runs on
     the rank-1 kernel (z0 and the skip made from x inside the scan, the skip
-    add fused), and the backward then makes z0 again with rqf_lowrank_drive
-    (the same fmaf operations, so the TBPTT(1) kernel replays the forward's
-    states bit for bit from the saved entries)."""
+    add fused), and so does the backward (rqf_fbt_rank1_tbptt_backward: the
+    states replayed from the saved entries with z0 made from x, and G, Gs and
+    the sums of gz0 + gzw returned as row sums instead of gz0 and gz0 + gzw)."""
 
     @staticmethod
     def forward(ctx, x_cf, w_in, b_in, W, C1, tap0, tap1, fuse_act, skip, B, T):
@@ -400,13 +400,12 @@ class _InputTBPTT(torch.autograd.Function):
         U = W @ w_in.to(torch.complex64)
         ctx.rank1 = w_in.shape[1] == 1 and ops.rank1_supported(F, B, T)
         ctx.fuse_act, ctx.skip = bool(fuse_act), bool(skip)
-        ctx.B, ctx.T = B, T
         if ctx.rank1:
             out, saved = ops.rank1_block_forward(U[:, 0], beta, w_in[:, 0] if skip else None,
                                                  b_in, x_cf.view(B, T), C1, tap0, tap1,
                                                  bool(fuse_act))
-            c1, t0, t1, _, _, _, carries = saved
-            ctx.save_for_backward(x_cf, w_in, b_in, W, c1, t0, t1, carries)
+            ctx.has_beta = beta is not None
+            ctx.save_for_backward(x_cf, w_in, b_in, W, *[t for t in saved if t is not None])
             return out
         z, h0 = ops.lowrank_drive(U, x_cf, beta, w_in if skip else None, b_in)
         y, saved = ops._fbt_forward(C1, tap0, tap1, z.view(F, B, T), bool(fuse_act))
@@ -417,23 +416,27 @@ class _InputTBPTT(torch.autograd.Function):
     @once_differentiable
     def backward(ctx, g):
         x_cf, w_in, b_in, W, *saved = ctx.saved_tensors
-        if ctx.rank1:  # z0 again, as the rank-1 forward made it
-            c1, t0, t1, carries = saved
-            beta = W @ b_in.to(torch.complex64) if b_in is not None else None
-            z, _ = ops.lowrank_drive(W @ w_in.to(torch.complex64), x_cf, beta)
-            saved = (c1, t0, t1, z.view(W.shape[0], ctx.B, ctx.T), carries)
-        gc1, gt0, gt1, gz, gsum = ops._tbptt_backward_wsum(saved, g, ctx.fuse_act)
         need = ctx.needs_input_grad
         I, has_b = w_in.shape[1], b_in is not None
-        G = ops.rowdot(gz, x_cf, with_sum=has_b)
+        if ctx.rank1:
+            c1, t0, t1, u, *rest = saved
+            beta = rest.pop(0) if ctx.has_beta else None
+            xx, carries = rest
+            gc1, gt0, gt1, G, Gw, Gs = ops.rank1_tbptt_backward(
+                (c1, t0, t1, u, beta, xx, carries), g, ctx.fuse_act, has_b, ctx.skip)
+        else:
+            gc1, gt0, gt1, gz, gsum = ops._tbptt_backward_wsum(saved, g, ctx.fuse_act)
+            G = ops.rowdot(gz, x_cf, with_sum=has_b)
+            Gw = ops.rowdot(gsum, x_cf, with_sum=has_b) if need[3] else None
+            Gs = ops.rowdot(g, x_cf, with_sum=has_b) if ctx.skip else None
         gW = gw_in = gb_in = None
         if need[3]:
             rows = torch.cat([w_in, b_in[:, None]], dim=1) if has_b else w_in
-            gW = ops.rowdot(gsum, x_cf, with_sum=has_b) @ rows.t().to(torch.complex64)
+            gW = Gw @ rows.t().to(torch.complex64)
         if need[1] or need[2]:
             gh = W.mH @ G
             if ctx.skip:
-                gh = gh + ops.rowdot(g, x_cf, with_sum=has_b)
+                gh = gh + Gs
             gw_in = gh[:, :I].real.contiguous() if need[1] else None
             gb_in = gh[:, I].real.contiguous() if (has_b and need[2]) else None
         return None, gw_in, gb_in, gW, gc1, gt0, gt1, None, None, None, None

@@ -1244,6 +1244,36 @@ def rank1_block_backward(saved, grad_output, fuse_act: bool, with_sum: bool, ski
     return gc1, gt0, gt1, G[:, :n], (Gs[:, :n] if Gs is not None else None)
 
 
+def rank1_tbptt_backward(saved, grad_output, fuse_act: bool, with_sum: bool, skip: bool):
+    """The TBPTT(1) surrogate backward of the rank-1 first block
+    (rqf_fbt_rank1_tbptt_backward), from rank1_block_forward's saved context:
+    (gc1, gtap0, gtap1, G, Gw, Gs) with G = [sum gz x (, sum gz)], Gw the same
+    sums of gz + gzw (what _tbptt_backward_wsum's second output gives
+    rowdot), Gs = [sum g x (, sum g)] or None unless ``skip``; complex64
+    (F, 1 + with_sum).  Neither grad_z nor the lag cotangent is formed."""
+    c1, t0, t1, uu, be, xx, carries = saved
+    F = int(uu.shape[0])
+    B, T = (int(d) for d in xx.shape)
+    dev = xx.device
+    gy = _c64(grad_output)
+    lib = _abi.load()
+    gc1, gt0, gt1 = torch.empty_like(c1), torch.empty_like(t0), torch.empty_like(t1)
+    G = torch.empty((F, 2), dtype=torch.complex64, device=dev)
+    Gw = torch.empty((F, 2), dtype=torch.complex64, device=dev)
+    Gs = torch.empty((F, 2), dtype=torch.complex64, device=dev) if skip else None
+    scratch = _scratch(lib.rqf_fbt_rank1_scratch_bytes(F, B, T), dev)
+    with _timing.launch("rqf_fbt_rank1_tbptt_backward", F * B * T, _nbytes(xx, gy)):
+        _abi.check(lib.rqf_fbt_rank1_tbptt_backward(
+            _abi.ptr(uu), _abi.ptr(be), _abi.ptr(xx), _abi.ptr(c1), _abi.ptr(t0), _abi.ptr(t1),
+            _abi.ptr(carries), _abi.ptr(gy), _abi.ptr(G), _abi.ptr(Gw), _abi.ptr(Gs),
+            _abi.ptr(gc1), _abi.ptr(gt0), _abi.ptr(gt1), _abi.ptr(scratch), F, B, T,
+            int(bool(fuse_act)), int(bool(with_sum)), _abi.stream_of(gy)),
+            "rqf_fbt_rank1_tbptt_backward")
+    _done(dev)
+    n = 2 if with_sum else 1
+    return gc1, gt0, gt1, G[:, :n], Gw[:, :n], (Gs[:, :n] if Gs is not None else None)
+
+
 def rowdot(a: torch.Tensor, x: torch.Tensor | None, with_sum: bool = False) -> torch.Tensor:
     """out[:, j] = a @ x[j] for the real rows of x (I <= 4), then the row sums
     of a when with_sum: complex64 (F, I + with_sum), over the flattened

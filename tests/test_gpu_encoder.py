@@ -483,11 +483,12 @@ def test_rank1_first_block_matches_general_path(bias, skip, T, monkeypatch):
 
 @pytest.mark.parametrize("bias,skip,T", [(False, True, 4000), (True, False, 1004)])
 def test_rank1_first_block_tbptt_matches_general_path(bias, skip, T, monkeypatch):
-    """The TBPTT(1) encoder's first layer over a one-channel input: its forward
-    on the rank-1 kernel (the backward makes z0 again with rqf_lowrank_drive)
-    against rqf_lowrank_drive + the row forward + the torch skip add: the
-    features bit-identical, every parameter gradient within fp32 summation-order
-    noise (the TBPTT(1) backward replays the same states)."""
+    """The TBPTT(1) encoder's first layer over a one-channel input on the
+    rank-1 kernels (rqf_fbt_rank1_forward, rqf_fbt_rank1_tbptt_backward: no
+    grad_z, the row sums reduced in the backward) against rqf_lowrank_drive +
+    the row forward + the torch skip add, the (F,B,T) TBPTT(1) kernel and
+    rqf_rowdot: the features bit-identical, every parameter gradient within
+    fp32 summation-order noise."""
     from prospective_rqf_b200 import _timing, ops
     from prospective_rqf_b200 import encoder as E
 
@@ -510,7 +511,7 @@ def test_rank1_first_block_tbptt_matches_general_path(bias, skip, T, monkeypatch
         return feats.detach().clone(), grads, set(tm.summary())
 
     f1, g1, k1 = run(True)
-    assert "rqf_fbt_rank1_forward" in k1
+    assert {"rqf_fbt_rank1_forward", "rqf_fbt_rank1_tbptt_backward"} <= k1
     f2, g2, k2 = run(False)
     assert "rqf_fbt_rank1_forward" not in k2
     assert torch.equal(f1, f2), "features differ from the general first layer"
