@@ -454,6 +454,24 @@ __global__ void __launch_bounds__(NT, 3) sel_bwd_kernel(const SelArgs a) {
     for (int jr = a.ntiles - 1; jr >= 0; --jr) {
       __syncthreads();  // shared slots of the previous tile are free
       const int t0 = jr * L + tid * K;
+      if (jr > 0 && tid < 64) {
+        // The tile processed next (the one before in time, whole inside the
+        // row) into L2, one 128-byte line per thread and tensor, so its loads
+        // do not wait on HBM when it starts.
+        const size_t pt = roff + (size_t)(jr - 1) * L;
+        const size_t lb = (size_t)tid * 128;
+        auto pf = [](const void *p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); };
+        pf(reinterpret_cast<const char *>(a.z + pt) + lb);
+        if (a.gy) pf(reinterpret_cast<const char *>(a.gy + pt) + lb);
+        if (a.gx) pf(reinterpret_cast<const char *>(a.gx + pt) + lb);
+        constexpr int kLogitLines = L * (BF ? 2 : 4) / 128;
+        if (tid < kLogitLines) {
+          const size_t lo = (size_t)(jr - 1) * L * (BF ? 2 : 4) + lb;
+          if (grow) pf(static_cast<const char *>(grow) + lo);
+          if (wrow) pf(static_cast<const char *>(wrow) + lo);
+          if (drow) pf(static_cast<const char *>(drow) + lo);
+        }
+      }
       float2 z[K], e[K];
       sel_ld_c(a.z + roff, t0, T, vec, z);
       const float2 zp = sel_prev_z(a.z + roff, t0, T, z[K - 1], lane);
