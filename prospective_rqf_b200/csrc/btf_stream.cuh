@@ -125,6 +125,23 @@ __device__ __forceinline__ void btf_load_go(const BtfArgs &a, int64_t base, int6
   }
 }
 
+// Into L2: the warp's K steps starting at tw of its chain in x (ESZ bytes per
+// element), one 128-byte line per lane (a step of 32 complex channels is two
+// lines, of 32 real ones one), so that the loads issued for them after the
+// next sub-tile barrier find them in L2.  base0: element (bi, 0, first
+// channel of the chain), fb0 that channel; only lines holding channels below
+// F are touched.
+template <int K, int ESZ>
+__device__ __forceinline__ void btf_prefetch(const void *x, int64_t base0, int64_t tw,
+                                             const BtfArgs &a, int fb0, int lane) {
+  constexpr int kLines = (32 * ESZ) / 128;  // lines per step: 2 or 1
+  const int step = lane / kLines, part = lane - step * kLines;
+  const int64_t t = tw + step;
+  if (step < K && t < a.T && fb0 + part * (128 / ESZ) < a.F)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(static_cast<const char *>(x) +
+                                                 (base0 + t * a.F) * ESZ + part * 128));
+}
+
 // ------------------------------------------------------------ forward
 // ABS: write |y| (float) instead of y (rqf::btf_store_y); a null carries
 // pointer skips the saved entry states.
@@ -162,6 +179,8 @@ __global__ void __launch_bounds__(NW * 32) btf_fwd_kernel(const BtfArgs a) {
 #pragma unroll 1
   for (int s = 0; s < S; ++s) {
     const int64_t tw = tile0 + (int64_t)s * L + (int64_t)warp * K;
+    if (s + 1 < S)
+      btf_prefetch<K, DRIVE == kReal ? 4 : 8>(a.x, base - lane, tw + L, a, (int)(f - lane), lane);
     btf_drive<K, DRIVE, S == 1>(a, base, tw, fv, c2, t1, x, xp, b);
     float2 y = cz();
 #pragma unroll
@@ -280,6 +299,7 @@ __global__ void __launch_bounds__(NW * 32) btf_bwd_kernel(const BtfArgs a) {
 #pragma unroll
       for (int k = 0; k < K; ++k) y = c_fma(lam, y, b[k]);
     }
+    if (s + 1 < S) btf_prefetch<K, 8>(a.gout, base - lane, tw + L, a, (int)(f - lane), lane);
     btf_load_go<K>(a, base, tw, fv, S == 1, go);
 #pragma unroll
     for (int k = K - 1; k >= 0; --k) h = c_fma(mu, h, go[k]);
@@ -452,6 +472,10 @@ __global__ void __launch_bounds__(NW * 32) btf_tbptt_bwd_kernel(const BtfArgs a)
                           ? a.carries[row * a.csub + (int64_t)j * S + s]
                           : cz();
     float2 x[K], xp, b[K], go[K];
+    if (s + 1 < S) {
+      btf_prefetch<K, 8>(a.x, base - lane, tw + L, a, (int)(f - lane), lane);
+      btf_prefetch<K, 8>(a.gout, base - lane, tw + L, a, (int)(f - lane), lane);
+    }
     btf_drive<K, kTwoTap, true>(a, base, tw, fv, t0, t1, x, xp, b);
     btf_load_go<K>(a, base, tw, fv, true, go);
     float2 y = cz();
