@@ -18,6 +18,8 @@ configuration times, then checks it against the oracle:
   groups, sigmoid gamma and write, prospective): the full launch, checked on
   the filters of two whole groups (their group cotangent dD sums over exactly
   those filters), every batch row and time step.
+* the rank-1 first block of configs 2 and 5, against the general first block
+  on the same inputs (full BPTT and TBPTT(1)).
 
 Bounds: forward normwise max relative error <= 1e-4, gradients <= 1e-3; the
 element-wise relative error with a floor of 1e-3 x max|ref| is bounded beside
@@ -243,3 +245,48 @@ def test_selective_config3_full_launch_vs_oracle_on_two_groups():
                            ("dtheta", dtheta[fsel], rdtheta)):
         assert_close(got, ref, GRAD_TOL, name, elem_tol=GRAD_ELEM_TOL)
     assert math.isfinite(float(np.abs(dz).max()))
+
+
+@pytest.mark.parametrize("F,B", [(128, 16), (256, 32)])
+def test_rank1_first_block_full_size(F, B):
+    """The first block over a one-channel input at configs 2 and 5 (T = 16000),
+    on the rank-1 kernels against the general first block on the same inputs
+    (rqf_lowrank_drive, the row forward with the fused skip, the row backward
+    and rqf_rowdot; both already checked against the oracle): the forward bit
+    for bit (the same operations), the backward's coefficient gradients and row
+    sums, full BPTT and TBPTT(1), within fp32 summation-order noise."""
+    from prospective_rqf_b200 import ops
+
+    T = 16000
+    c1, t0, t1 = _model_coefficients(F, 11 + F)
+    g = torch.Generator(device="cuda").manual_seed(F + B)
+    x = (0.5 * torch.randn(B, T, device="cuda", generator=g)).clamp(-1, 1)
+    u = 0.2 * torch.randn(F, dtype=torch.complex64, device="cuda", generator=g)
+    beta = 0.1 * torch.randn(F, dtype=torch.complex64, device="cuda", generator=g)
+    w = torch.randn(F, device="cuda", generator=g)
+    bb = 0.1 * torch.randn(F, device="cuda", generator=g)
+    gy = torch.randn(F, B, T, dtype=torch.complex64, device="cuda", generator=g)
+    xr = x.reshape(1, -1)
+
+    out1, saved1 = ops.rank1_block_forward(u, beta, w, bb, x, c1, t0, t1, True)
+    z, h0 = ops.lowrank_drive(u[:, None], xr, beta, w[:, None], bb)
+    out2, saved2 = ops._fbt_forward(c1, t0, t1, z.view(F, B, T), True, h0.view(F, B, T))
+    assert torch.equal(out1, out2), "rank-1 forward differs from the general first block"
+    del out1, out2
+
+    tol = 1e-4
+    gc1, gt0, gt1, G, Gs = ops.rank1_block_backward(saved1, gy, True, True, True)
+    rc1, rt0, rt1, gz = ops._fbt_backward(saved2, gy, True)
+    for a, b, name in ((gc1, rc1, "gc1"), (gt0, rt0, "gtap0"), (gt1, rt1, "gtap1"),
+                       (G, ops.rowdot(gz, xr, with_sum=True), "sum gz [x; 1]"),
+                       (Gs, ops.rowdot(gy, xr, with_sum=True), "sum g [x; 1]")):
+        assert_close(_h(a), _h(b), tol, "full BPTT " + name)
+    del gz
+
+    gc1, gt0, gt1, G, Gw, Gs = ops.rank1_tbptt_backward(saved1, gy, True, True, True)
+    rc1, rt0, rt1, gz, gsum = ops._tbptt_backward_wsum(saved2, gy, True)
+    for a, b, name in ((gc1, rc1, "gc1"), (gt0, rt0, "gtap0"), (gt1, rt1, "gtap1"),
+                       (G, ops.rowdot(gz, xr, with_sum=True), "sum gz [x; 1]"),
+                       (Gw, ops.rowdot(gsum, xr, with_sum=True), "sum (gz + gzw) [x; 1]"),
+                       (Gs, ops.rowdot(gy, xr, with_sum=True), "sum g [x; 1]")):
+        assert_close(_h(a), _h(b), tol, "TBPTT(1) " + name)
