@@ -21,7 +21,10 @@
 // which it accumulates per row beside the coefficient sums (reduced over the
 // batch in a fixed order in double by reduce_rows4_kernel).  So the block
 // moves 4 bytes of input per sample plus its output (forward) or its output
-// cotangent (backward), against z, h0 and gz in the general path.
+// cotangent (backward), against z, h0 and gz in the general path.  The same
+// backward kernel also serves the block's TBPTT(1) surrogate (TRUNC: no
+// adjoint recursion, and the row sums of grad_z plus the lag cotangent for
+// the weight cotangent; pure.py:184-187).
 //
 // Tiling, pipeline and scans are those of fbt_rows.cuh (kFbtThreads threads x
 // kFbtK samples per tile); x tiles are 4 bytes per sample, staged by cp.async
