@@ -53,6 +53,7 @@ KERNELS_PER_CALL = {  # kernels each C-ABI call launches (the backward adds the 
     "rqf_fbt_rank1_forward": 1,
     "rqf_fbt_rank1_backward": 3,
     "rqf_fbt_rank1_tbptt_backward": 3,
+    "rqf_per_step_cross_entropy": 2,
     "rqf_tbptt1_two_tap_backward": 2,
 }
 SCAN_CALLS = ("rqf_fbt_prospective_forward", "rqf_fbt_block_forward",

@@ -592,6 +592,27 @@ int rqf_readout_relu_pool_backward(const uint32_t *mask, const float *scale, flo
                                    float *counts, int64_t h, int64_t batch, int64_t time,
                                    rqf_stream_t stream);
 
+/* The per-timestep classification loss of the TBPTT(1) recipe
+ * (train.py:per_step_cross_entropy :663-674: cross_entropy over the
+ * (batch*time, classes) view, batch row b's label for each of its time
+ * steps, label smoothing, mean), on the logits as the readout's output GEMM
+ * writes them: float32 (classes, batch*time), sample b*time + t.  labels
+ * int64 (batch), each in [0, classes) (else RQF_ERR_ARGUMENT is latched for
+ * rqf_read_device_error and class 0 used).  loss: one float32; the sum is
+ * taken per block in double and then over blocks in a fixed order.
+ * `scratch` needs rqf_per_step_cross_entropy_scratch_bytes (8-byte aligned).
+ * The backward writes grad_logits (classes, batch*time) for the upstream
+ * gradient *grad_loss (a device scalar): (softmax - (1 - eps) onehot(y) -
+ * eps / classes) * grad_loss / (batch*time). */
+size_t rqf_per_step_cross_entropy_scratch_bytes(int64_t batch, int64_t time);
+int rqf_per_step_cross_entropy(const float *logits, const int64_t *labels, float *loss,
+                               void *scratch, int64_t classes, int64_t batch, int64_t time,
+                               float label_smoothing, rqf_stream_t stream);
+int rqf_per_step_cross_entropy_backward(const float *logits, const int64_t *labels,
+                                        const float *grad_loss, float *grad_logits,
+                                        int64_t classes, int64_t batch, int64_t time,
+                                        float label_smoothing, rqf_stream_t stream);
+
 /* ---- RQF filter-bank coefficients (rqf_models/backbones/rqf/filter.py) -- *
  * Replaces RQF.compute_two_tap_coefficients (filter.py:510-664) with the
  * parameter reads it makes (the tau / gamma / freq properties, :402-449):

@@ -21,6 +21,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "rqf_common.cuh"
+
 namespace rqf {
 namespace readout {
 
@@ -91,6 +93,99 @@ relu_pool_backward_kernel(const uint32_t *__restrict__ mask, const float *__rest
     __syncthreads();
   }
   if (threadIdx.x == 0 && counts) counts[row] = (float)red[0];
+}
+
+// ------------------------------------------------ per-step cross entropy
+// The loss of per-timestep logits (train.py:per_step_cross_entropy :663-674:
+// torch cross_entropy over the (batch*time, classes) view, the label of batch
+// row b for each of its time steps, label smoothing eps, mean reduction),
+// read in the layout the readout's output GEMM writes: logits (C, N) with
+// sample n = b T + t.  Per sample:
+//   loss_n = lse_n - (1 - eps) l[y] - (eps / C) sum_c l[c],
+//   dl[c]  = (softmax_c - (1 - eps) [c == y] - eps / C) g / N,
+// with lse_n = m + log sum_c exp(l[c] - m) in one pass (running maximum m).
+// The sum over samples is per block in double, then over blocks in a fixed
+// order (deterministic).  A label outside [0, C) latches RQF_ERR_ARGUMENT
+// and counts as class 0.
+constexpr int kCeThreads = 256;
+
+__device__ __forceinline__ void ce_lse(const float *__restrict__ l, long long N, long long n, int C,
+                                       float &lse, float &sum) {
+  float m = -INFINITY, s = 0.f;
+  sum = 0.f;
+  for (int c = 0; c < C; ++c) {
+    const float v = l[(long long)c * N + n];
+    sum += v;
+    if (v > m) {
+      s = s * expf(m - v) + 1.f;
+      m = v;
+    } else {
+      s += expf(v - m);
+    }
+  }
+  lse = m + logf(s);
+}
+
+__device__ __forceinline__ int ce_label(const long long *labels, long long n, long long T, int C) {
+  const long long y = labels[n / T];
+  if (y < 0 || y >= C) {
+    latch_error(5);
+    return 0;
+  }
+  return (int)y;
+}
+
+__global__ void __launch_bounds__(kCeThreads) ce_forward_kernel(
+    const float *__restrict__ logits, const long long *__restrict__ labels, long long N,
+    long long T, int C, float eps, double *__restrict__ partials) {
+  const long long n = (long long)blockIdx.x * kCeThreads + threadIdx.x;
+  double loss = 0.0;
+  if (n < N) {
+    float lse, sum;
+    ce_lse(logits, N, n, C, lse, sum);
+    const int y = ce_label(labels, n, T, C);
+    loss = (double)lse - (1.0 - (double)eps) * (double)logits[(long long)y * N + n] -
+           ((double)eps / C) * (double)sum;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) loss += __shfl_xor_sync(0xffffffffu, loss, o);
+  __shared__ double s_w[kCeThreads / 32];
+  if ((threadIdx.x & 31) == 0) s_w[threadIdx.x >> 5] = loss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+#pragma unroll
+    for (int w = 0; w < kCeThreads / 32; ++w) t += s_w[w];
+    partials[blockIdx.x] = t;
+  }
+}
+
+// loss = (sum of the block partials, in block order) / N; one warp.
+__global__ void ce_finalize_kernel(const double *__restrict__ partials, long long blocks,
+                                   long long N, float *__restrict__ loss) {
+  double t = 0.0;
+  for (long long b = threadIdx.x; b < blocks; b += 32) t += partials[b];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  if (threadIdx.x == 0) *loss = (float)(t / (double)N);
+}
+
+// grad_logits (C, N) for the upstream gradient *grad_loss of the mean loss.
+__global__ void __launch_bounds__(kCeThreads) ce_backward_kernel(
+    const float *__restrict__ logits, const long long *__restrict__ labels,
+    const float *__restrict__ grad_loss, long long N, long long T, int C, float eps,
+    float *__restrict__ grad_logits) {
+  const long long n = (long long)blockIdx.x * kCeThreads + threadIdx.x;
+  if (n >= N) return;
+  float lse, sum;
+  ce_lse(logits, N, n, C, lse, sum);
+  const int y = ce_label(labels, n, T, C);
+  const float g = *grad_loss / (float)N, off = eps / (float)C;
+  for (int c = 0; c < C; ++c) {
+    const long long i = (long long)c * N + n;
+    const float p = expf(logits[i] - lse);
+    grad_logits[i] = (p - (c == y ? 1.f - eps : 0.f) - off) * g;
+  }
 }
 
 }  // namespace readout

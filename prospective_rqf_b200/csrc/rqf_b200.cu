@@ -1930,6 +1930,59 @@ int rqf_readout_relu_pool_backward(const uint32_t *mask, const float *scale, flo
   return launch_status();
 }
 
+namespace {
+int ce_dims_ok(int64_t classes, int64_t batch, int64_t time) {
+  if (classes <= 0 || batch < 0 || time < 0 || classes > 0x7fffffffLL) return RQF_ERR_SHAPE;
+  if (ceil_div(batch * time, readout::kCeThreads) > 0x7fffffffLL) return RQF_ERR_SHAPE;
+  return RQF_OK;
+}
+}  // namespace
+
+size_t rqf_per_step_cross_entropy_scratch_bytes(int64_t batch, int64_t time) {
+  if (batch <= 0 || time <= 0) return 0;
+  return round256((size_t)ceil_div(batch * time, readout::kCeThreads) * sizeof(double));
+}
+
+int rqf_per_step_cross_entropy(const float *logits, const int64_t *labels, float *loss,
+                               void *scratch, int64_t classes, int64_t batch, int64_t time,
+                               float label_smoothing, rqf_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int rc = ce_dims_ok(classes, batch, time);
+  if (rc != RQF_OK) return rc;
+  if (loss == nullptr) return RQF_ERR_ARGUMENT;
+  const int64_t n = batch * time;
+  if (n == 0)  // the mean over no samples, as torch gives it
+    return cudaMemsetAsync(loss, 0xff, sizeof(float), st) == cudaSuccess ? RQF_OK : RQF_ERR_LAUNCH;
+  if (logits == nullptr || labels == nullptr || scratch == nullptr) return RQF_ERR_ARGUMENT;
+  if (!aligned(scratch, 8)) return RQF_ERR_ALIGN;
+  const int64_t blocks = ceil_div(n, readout::kCeThreads);
+  readout::ce_forward_kernel<<<(unsigned)blocks, readout::kCeThreads, 0, st>>>(
+      logits, reinterpret_cast<const long long *>(labels), n, time, (int)classes,
+      label_smoothing, static_cast<double *>(scratch));
+  if ((rc = launch_status()) != RQF_OK) return rc;
+  readout::ce_finalize_kernel<<<1, 32, 0, st>>>(static_cast<const double *>(scratch), blocks, n,
+                                                loss);
+  return launch_status();
+}
+
+int rqf_per_step_cross_entropy_backward(const float *logits, const int64_t *labels,
+                                        const float *grad_loss, float *grad_logits,
+                                        int64_t classes, int64_t batch, int64_t time,
+                                        float label_smoothing, rqf_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int rc = ce_dims_ok(classes, batch, time);
+  if (rc != RQF_OK) return rc;
+  const int64_t n = batch * time;
+  if (n == 0) return RQF_OK;
+  if (logits == nullptr || labels == nullptr || grad_loss == nullptr || grad_logits == nullptr)
+    return RQF_ERR_ARGUMENT;
+  readout::ce_backward_kernel<<<(unsigned)ceil_div(n, readout::kCeThreads), readout::kCeThreads, 0,
+                                st>>>(logits, reinterpret_cast<const long long *>(labels),
+                                      grad_loss, n, time, (int)classes, label_smoothing,
+                                      grad_logits);
+  return launch_status();
+}
+
 }  // extern "C"
 
 // ------------------------------------------------ two-tap coefficient producer

@@ -629,3 +629,22 @@ class RQFClassifier(nn.Module):
 
     def forward(self, x: torch.Tensor, per_step: bool = False) -> torch.Tensor:
         return self.readout(self.encoder(x), per_step=per_step)
+
+    def per_step_loss(self, x: torch.Tensor, y: torch.Tensor,
+                      label_smoothing: float = 0.0) -> torch.Tensor:
+        """train.py:per_step_cross_entropy (:663-674) of forward(x, per_step=True)
+        against the batch labels y.  On the tensor-core path the logits stay in
+        the output GEMM's (classes, batch*time) layout and the loss and its
+        gradient run in one pass each (ops.per_step_cross_entropy)."""
+        h = self.encoder(x)
+        F, B, T = h.shape
+        ro = self.readout
+        if PROJECTION == "tc" and h.is_cuda:
+            hid = _ReadoutHidden.apply(h, ro.fc1.weight, ro.fc1.bias)  # (H, B, T)
+            logits = torch.addmm(ro.fc2.bias[:, None], ro.fc2.weight,
+                                 hid.reshape(hid.shape[0], B * T))     # (C, B*T)
+            return ops.per_step_cross_entropy(logits, y, B, T, label_smoothing)
+        logits = ro(h, per_step=True)
+        return torch.nn.functional.cross_entropy(
+            logits.reshape(B * T, -1), y[:, None].expand(B, T).reshape(-1),
+            label_smoothing=label_smoothing)

@@ -1299,6 +1299,60 @@ def rowdot(a: torch.Tensor, x: torch.Tensor | None, with_sum: bool = False) -> t
 
 
 # ------------------------------------------------ mean-pooled readout hidden layer
+class _PerStepCE(torch.autograd.Function):
+    """The per-timestep cross entropy (train.py:per_step_cross_entropy
+    :663-674) on logits in the readout GEMM's (classes, batch*time) layout:
+    rqf_per_step_cross_entropy forward, rqf_per_step_cross_entropy_backward
+    for the logits' gradient.  Labels and smoothing take no gradient."""
+
+    @staticmethod
+    def forward(ctx, logits, labels, batch, time, label_smoothing):
+        ll = logits.detach().contiguous()
+        yy = labels.detach().to(torch.int64).contiguous()
+        C = int(ll.shape[0])
+        dev = _require_cuda(ll, yy)
+        lib = _abi.load()
+        loss = torch.empty((), dtype=torch.float32, device=dev)
+        scratch = _scratch(lib.rqf_per_step_cross_entropy_scratch_bytes(batch, time), dev)
+        with _timing.launch("rqf_per_step_cross_entropy", batch * time, _nbytes(ll)):
+            _abi.check(lib.rqf_per_step_cross_entropy(
+                _abi.ptr(ll), _abi.ptr(yy), _abi.ptr(loss), _abi.ptr(scratch), C, batch, time,
+                float(label_smoothing), _abi.stream_of(ll)), "rqf_per_step_cross_entropy")
+        _done(dev)
+        ctx.save_for_backward(ll, yy)
+        ctx.dims = (batch, time, float(label_smoothing))
+        return loss
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_loss):
+        ll, yy = ctx.saved_tensors
+        batch, time, eps = ctx.dims
+        g = grad_loss.detach().to(torch.float32).contiguous()
+        gl = torch.empty_like(ll)
+        lib = _abi.load()
+        with _timing.launch("rqf_per_step_cross_entropy_backward", batch * time,
+                            2 * _nbytes(ll)):
+            _abi.check(lib.rqf_per_step_cross_entropy_backward(
+                _abi.ptr(ll), _abi.ptr(yy), _abi.ptr(g), _abi.ptr(gl), int(ll.shape[0]), batch,
+                time, eps, _abi.stream_of(ll)), "rqf_per_step_cross_entropy_backward")
+        _done(ll.device)
+        return gl, None, None, None, None
+
+
+def per_step_cross_entropy(logits_cn: torch.Tensor, labels: torch.Tensor, batch: int, time: int,
+                           label_smoothing: float = 0.0) -> torch.Tensor:
+    """Mean label-smoothed cross entropy of per-timestep logits given as
+    float32 (classes, batch*time), sample b*time + t, labels (batch,) int64:
+    the value of train.py:per_step_cross_entropy on the (batch, time,
+    classes) view of the same logits, in one pass and without the view."""
+    if logits_cn.dtype != torch.float32 or logits_cn.dim() != 2 or \
+            logits_cn.shape[1] != batch * time or labels.shape != (batch,):
+        raise ValueError(f"logits {tuple(logits_cn.shape)} {logits_cn.dtype}, labels "
+                         f"{tuple(labels.shape)} do not match batch={batch}, time={time}")
+    return _PerStepCE.apply(logits_cn, labels, int(batch), int(time), float(label_smoothing))
+
+
 def readout_relu_pool(z: torch.Tensor, bias: torch.Tensor | None):
     """pooled = mean_t relu(z + bias[:, None, None]) as float32 (H, B), and
     the ReLU mask as int32 words (H, B, ceil(T/32)), bit t % 32 of word t / 32,

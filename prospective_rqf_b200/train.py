@@ -164,15 +164,10 @@ class TrainStep:
     def __call__(self, x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
         cfg = self.cfg
         self.model.train()
-        per_step = cfg.scan_grad_mode == "tbptt1"
-        logits = self.model(x, per_step=per_step)
-        if per_step:  # per_step_cross_entropy (train.py:663-674)
-            B, T, C = logits.shape
-            loss = torch.nn.functional.cross_entropy(
-                logits.reshape(B * T, C), y[:, None].expand(B, T).reshape(-1),
-                label_smoothing=cfg.label_smoothing)
+        if cfg.scan_grad_mode == "tbptt1":  # per_step_cross_entropy (train.py:663-674)
+            loss = self.model.per_step_loss(x, y, cfg.label_smoothing)
         else:
-            loss = torch.nn.functional.cross_entropy(logits, y,
+            loss = torch.nn.functional.cross_entropy(self.model(x), y,
                                                      label_smoothing=cfg.label_smoothing)
         self.opt.zero_grad(set_to_none=True)
         loss.backward()

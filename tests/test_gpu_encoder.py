@@ -518,3 +518,58 @@ def test_rank1_first_block_tbptt_matches_general_path(bias, skip, T, monkeypatch
     for n in g1:
         e = rel_err(g1[n].cpu().numpy(), g2[n].cpu().numpy())
         assert e <= 1e-4, f"{n}: {e:.2e}"
+
+
+@pytest.mark.parametrize("C,B,T,eps", [(35, 4, 1000, 0.1), (35, 3, 257, 0.0), (5, 2, 64, 0.3),
+                                       (1, 2, 7, 0.1)])
+def test_per_step_cross_entropy_matches_torch(C, B, T, eps):
+    """rqf_per_step_cross_entropy and its backward against
+    torch.nn.functional.cross_entropy on the (batch*time, classes) view of the
+    same logits (train.py:per_step_cross_entropy :663-674): loss and logit
+    gradient in fp64, for an upstream gradient other than one."""
+    from prospective_rqf_b200 import ops
+
+    g = torch.Generator().manual_seed(C * 7 + B + T)
+    logits = (3.0 * torch.randn(C, B * T, generator=g)).cuda().requires_grad_(True)
+    y = torch.randint(0, C, (B,), generator=g).cuda()
+    loss = ops.per_step_cross_entropy(logits, y, B, T, eps)
+    (2.5 * loss).backward()
+    ref_l = logits.detach().double().requires_grad_(True)
+    ref = torch.nn.functional.cross_entropy(
+        ref_l.t().reshape(B, T, C).reshape(B * T, C), y[:, None].expand(B, T).reshape(-1),
+        label_smoothing=eps)
+    (2.5 * ref).backward()
+    assert abs(float(loss) - float(ref)) <= 1e-6 * max(1.0, abs(float(ref)))
+    assert_close(logits.grad.cpu().numpy().astype(np.float64), ref_l.grad.cpu().numpy(), 1e-5,
+                 "grad logits")
+
+
+def test_tbptt_step_loss_matches_torch_cross_entropy():
+    """The TBPTT(1) training step's loss through RQFClassifier.per_step_loss
+    against torch's cross entropy of forward(x, per_step=True), and the same
+    parameter gradients."""
+    from prospective_rqf_b200 import encoder as E
+
+    def run(fused):
+        torch.manual_seed(0)
+        enc = E.PureRQFEncoderB200(input_dims=1, hidden_dims=64, num_layers=2, seed=2,
+                                   scan_grad_mode="tbptt1")
+        model = E.RQFClassifier(enc, 7, 32).cuda()
+        g = torch.Generator().manual_seed(3)
+        x = (0.5 * torch.randn(4, 2048, 1, generator=g)).clamp(-1, 1).cuda()
+        y = torch.randint(0, 7, (4,), generator=g).cuda()
+        if fused:
+            loss = model.per_step_loss(x, y, 0.1)
+        else:
+            logits = model(x, per_step=True)
+            loss = torch.nn.functional.cross_entropy(
+                logits.reshape(4 * 2048, 7), y[:, None].expand(4, 2048).reshape(-1),
+                label_smoothing=0.1)
+        loss.backward()
+        return float(loss), {n: p.grad.detach().clone() for n, p in model.named_parameters()}
+
+    l1, g1 = run(True)
+    l2, g2 = run(False)
+    assert abs(l1 - l2) <= 1e-6 * max(1.0, abs(l2))
+    for n in g1:
+        assert rel_err(g1[n].cpu().numpy(), g2[n].cpu().numpy()) <= 1e-4, n
