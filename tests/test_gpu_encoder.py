@@ -539,7 +539,8 @@ def test_per_step_cross_entropy_matches_torch(C, B, T, eps):
         ref_l.t().reshape(B, T, C).reshape(B * T, C), y[:, None].expand(B, T).reshape(-1),
         label_smoothing=eps)
     (2.5 * ref).backward()
-    assert abs(float(loss) - float(ref)) <= 1e-6 * max(1.0, abs(float(ref)))
+    lv, rv = float(loss.detach()), float(ref.detach())
+    assert abs(lv - rv) <= 1e-6 * max(1.0, abs(rv))
     assert_close(logits.grad.cpu().numpy().astype(np.float64), ref_l.grad.cpu().numpy(), 1e-5,
                  "grad logits")
 
