@@ -592,6 +592,18 @@ int rqf_readout_relu_pool_backward(const uint32_t *mask, const float *scale, flo
                                    float *counts, int64_t h, int64_t batch, int64_t time,
                                    rqf_stream_t stream);
 
+/* The per-step readout's hidden layer (train.py:ComplexReadoutClassifier
+ * :74-136, Linear -> ReLU at every step, for per-step logits): in place on
+ * the real part z (float32, H x B x T, T contiguous) of the projection,
+ * z = relu(z + bias[h]) and the mask bits of rqf_readout_relu_pool (bias may
+ * be null).  Its backward: g = mask ? gy : 0 (float32, like gy) and
+ * rowsum[h, b] = sum_t g (nullable; in double, fixed order), the bias's
+ * cotangent before the sum over the batch. */
+int rqf_readout_bias_relu(float *z, const float *bias, uint32_t *mask, int64_t h, int64_t batch,
+                          int64_t time, rqf_stream_t stream);
+int rqf_readout_bias_relu_backward(const float *gy, const uint32_t *mask, float *g, float *rowsum,
+                                   int64_t h, int64_t batch, int64_t time, rqf_stream_t stream);
+
 /* The per-timestep classification loss of the TBPTT(1) recipe
  * (train.py:per_step_cross_entropy :663-674: cross_entropy over the
  * (batch*time, classes) view, batch row b's label for each of its time

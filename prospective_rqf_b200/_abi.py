@@ -150,6 +150,8 @@ SIGNATURES: dict[str, tuple] = {
         _int, [_p, _p, _p, _p, _p, _p, _p, _i64, _f64, _f64, _p]),
     "rqf_readout_relu_pool": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _p]),
     "rqf_readout_relu_pool_backward": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _p]),
+    "rqf_readout_bias_relu": (_int, [_p, _p, _p, _i64, _i64, _i64, _p]),
+    "rqf_readout_bias_relu_backward": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _p]),
     "rqf_per_step_cross_entropy_scratch_bytes": (_sz, [_i64, _i64]),
     "rqf_per_step_cross_entropy": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _f32, _p]),
     "rqf_per_step_cross_entropy_backward": (

@@ -68,6 +68,67 @@ relu_pool_kernel(const float *__restrict__ z, const float *__restrict__ bias,
   if (threadIdx.x == 0) pooled[row] = (float)(red[0] / (double)T);
 }
 
+// The per-step hidden layer's bias and ReLU in place: z[row, t] = relu(z +
+// bias[row / batch]) and its mask bits (as relu_pool_kernel writes them).
+__global__ void __launch_bounds__(kThreads)
+bias_relu_kernel(float *__restrict__ z, const float *__restrict__ bias, uint32_t *__restrict__ mask,
+                 int batch, long long T, long long words) {
+  const long long row = blockIdx.x;
+  const float bh = bias ? bias[row / batch] : 0.f;
+  float *zr = z + row * T;
+  uint32_t *mr = mask + row * words;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int kU = 4;
+  for (long long w0 = warp; w0 < words; w0 += kU * kWarps) {
+    float v[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const long long t = (w0 + u * kWarps) * 32 + lane;
+      v[u] = t < T ? zr[t] : -INFINITY;
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const long long w = w0 + u * kWarps, t = w * 32 + lane;
+      const float x = v[u] + bh;
+      const bool on = x > 0.f;
+      const uint32_t bits = __ballot_sync(0xffffffffu, on);
+      if (lane == 0 && w < words) mr[w] = bits;
+      if (t < T) zr[t] = on ? x : 0.f;
+    }
+  }
+}
+
+// Its backward: g[row, t] = mask ? gy[row, t] : 0, and rowsum[row] = sum_t g
+// (in double, fixed order): the bias's cotangent before the sum over batch.
+__global__ void __launch_bounds__(kThreads)
+bias_relu_backward_kernel(const float *__restrict__ gy, const uint32_t *__restrict__ mask,
+                          float *__restrict__ g, float *__restrict__ rowsum, long long T,
+                          long long words) {
+  const long long row = blockIdx.x;
+  const float *gr = gy + row * T;
+  float *out = g + row * T;
+  const uint32_t *mr = mask + row * words;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  double acc = 0.0;
+  for (long long w = warp; w < words; w += kWarps) {
+    const uint32_t bits = mr[w];
+    const long long t = w * 32 + lane;
+    if (t < T) {
+      const float v = ((bits >> lane) & 1u) ? gr[t] : 0.f;
+      out[t] = v;
+      acc += v;
+    }
+  }
+  __shared__ double red[kThreads];
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  for (int k = kThreads / 2; k > 0; k >>= 1) {
+    if (threadIdx.x < k) red[threadIdx.x] += red[threadIdx.x + k];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0 && rowsum) rowsum[row] = (float)red[0];
+}
+
 // g[row, t] = mask ? scale[row] : 0; counts[row] = number of set bits.
 __global__ void __launch_bounds__(kThreads)
 relu_pool_backward_kernel(const uint32_t *__restrict__ mask, const float *__restrict__ scale,

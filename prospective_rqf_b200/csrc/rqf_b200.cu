@@ -1930,6 +1930,38 @@ int rqf_readout_relu_pool_backward(const uint32_t *mask, const float *scale, flo
   return launch_status();
 }
 
+int rqf_readout_bias_relu(float *z, const float *bias, uint32_t *mask, int64_t h, int64_t batch,
+                          int64_t time, rqf_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (h < 0 || batch < 0 || time < 0) return RQF_ERR_SHAPE;
+  const int64_t rows = h * batch;
+  if (rows == 0 || time == 0) return RQF_OK;
+  if (rows > 0x7fffffffLL || batch > 0x7fffffffLL) return RQF_ERR_SHAPE;
+  if (z == nullptr || mask == nullptr) return RQF_ERR_ARGUMENT;
+  readout::bias_relu_kernel<<<(unsigned)rows, readout::kThreads, 0, st>>>(
+      z, bias, mask, (int)batch, time, ceil_div(time, 32));
+  return launch_status();
+}
+
+int rqf_readout_bias_relu_backward(const float *gy, const uint32_t *mask, float *g, float *rowsum,
+                                   int64_t h, int64_t batch, int64_t time, rqf_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (h < 0 || batch < 0 || time < 0) return RQF_ERR_SHAPE;
+  const int64_t rows = h * batch;
+  if (rows == 0) return RQF_OK;
+  if (rows > 0x7fffffffLL) return RQF_ERR_SHAPE;
+  if (time == 0) {
+    if (rowsum == nullptr) return RQF_OK;
+    return cudaMemsetAsync(rowsum, 0, (size_t)rows * sizeof(float), st) == cudaSuccess
+               ? RQF_OK
+               : RQF_ERR_LAUNCH;
+  }
+  if (gy == nullptr || mask == nullptr || g == nullptr) return RQF_ERR_ARGUMENT;
+  readout::bias_relu_backward_kernel<<<(unsigned)rows, readout::kThreads, 0, st>>>(
+      gy, mask, g, rowsum, time, ceil_div(time, 32));
+  return launch_status();
+}
+
 namespace {
 int ce_dims_ok(int64_t classes, int64_t batch, int64_t time) {
   if (classes <= 0 || batch < 0 || time < 0 || classes > 0x7fffffffLL) return RQF_ERR_SHAPE;

@@ -522,23 +522,24 @@ class _ReadoutHidden(torch.autograd.Function):
     def forward(ctx, h, W1, b1):
         F = h.shape[0]
         V = torch.complex(W1[:, :F], -W1[:, F:]).contiguous()
-        pre = ops.projection_real_out(V, h).add_(b1[:, None, None])
-        mask = pre > 0
+        # bias and ReLU in one pass over the projection, the decisions kept as bits
+        hid, mask = ops.readout_bias_relu(ops.projection_real_out(V, h), b1)
         ctx.save_for_backward(h, V, mask)
-        return pre.mul_(mask)
+        return hid
 
     @staticmethod
     @once_differentiable
     def backward(ctx, ghid):
         h, V, mask = ctx.saved_tensors
         need = ctx.needs_input_grad
-        g = ghid * mask  # real: the real-operand forms of both cotangent GEMMs
+        # real: the real-operand forms of both cotangent GEMMs
+        g, rowsum = ops.readout_bias_relu_backward(ghid, mask)
         gh = ops.projection_real(V, g, conj_transpose=True) if need[0] else None
         gW1 = None
         if need[1]:
             P = ops.projection_weight_grad_real(g, h)
             gW1 = torch.cat([P.real, -P.imag], dim=1)
-        gb1 = g.sum(dim=(1, 2)) if need[2] else None
+        gb1 = rowsum.sum(dim=1) if need[2] else None
         return gh, gW1, gb1
 
 

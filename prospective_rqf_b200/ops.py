@@ -1396,6 +1396,42 @@ def readout_relu_pool_backward(mask: torch.Tensor, scale: torch.Tensor, time: in
     return gc, counts
 
 
+def readout_bias_relu(z: torch.Tensor, bias: torch.Tensor | None):
+    """In place on z (float32, H x B x T): z = relu(z + bias[:, None, None])
+    (rqf_readout_bias_relu), the per-step hidden layer's activation; returns
+    (z, mask) with the ReLU decisions as bits (uint32 words, the layout of
+    readout_relu_pool)."""
+    dev = _require_cuda(z)
+    if z.dtype != torch.float32 or z.dim() != 3 or not z.is_contiguous():
+        raise ValueError("z must be a contiguous float32 (H, B, T) tensor")
+    H, B, T = (int(d) for d in z.shape)
+    bb = bias.detach().to(torch.float32).contiguous() if bias is not None else None
+    mask = torch.empty((H * B * ((T + 31) // 32),), dtype=torch.int32, device=dev)
+    lib = _abi.load()
+    with _timing.launch("rqf_readout_bias_relu", H * B * T, 2 * _nbytes(z)):
+        _abi.check(lib.rqf_readout_bias_relu(_abi.ptr(z), _abi.ptr(bb), _abi.ptr(mask), H, B, T,
+                                             _abi.stream_of(z)), "rqf_readout_bias_relu")
+    _done(dev)
+    return z, mask
+
+
+def readout_bias_relu_backward(gy: torch.Tensor, mask: torch.Tensor):
+    """(g, rowsum): g = gy where the ReLU passed, else 0 (float32, H x B x T),
+    and rowsum (H, B) its sums over time (rqf_readout_bias_relu_backward)."""
+    gg = gy.detach().to(torch.float32).contiguous()
+    dev = _require_cuda(gg, mask)
+    H, B, T = (int(d) for d in gg.shape)
+    g = torch.empty_like(gg)
+    rowsum = torch.empty((H, B), dtype=torch.float32, device=dev)
+    lib = _abi.load()
+    with _timing.launch("rqf_readout_bias_relu_backward", H * B * T, 2 * _nbytes(gg)):
+        _abi.check(lib.rqf_readout_bias_relu_backward(
+            _abi.ptr(gg), _abi.ptr(mask), _abi.ptr(g), _abi.ptr(rowsum), H, B, T,
+            _abi.stream_of(gg)), "rqf_readout_bias_relu_backward")
+    _done(dev)
+    return g, rowsum
+
+
 # ------------------------------------------------ real-operand projections
 def projection_real(W: torch.Tensor, x: torch.Tensor, conj_transpose: bool = False,
                     acc: torch.Tensor | None = None) -> torch.Tensor:

@@ -574,3 +574,22 @@ def test_tbptt_step_loss_matches_torch_cross_entropy():
     assert abs(l1 - l2) <= 1e-6 * max(1.0, abs(l2))
     for n in g1:
         assert rel_err(g1[n].cpu().numpy(), g2[n].cpu().numpy()) <= 1e-4, n
+
+
+@pytest.mark.parametrize("H,B,T", [(16, 3, 1000), (8, 2, 32), (5, 1, 70)])
+def test_readout_bias_relu_matches_torch(H, B, T):
+    """rqf_readout_bias_relu (in place) and its backward against
+    relu(z + b) and the masked cotangent with its sum over (b, t): exact."""
+    from prospective_rqf_b200 import ops
+
+    g = torch.Generator().manual_seed(H + B + T)
+    z = torch.randn(H, B, T, generator=g).cuda()
+    b = torch.randn(H, generator=g).cuda()
+    gy = torch.randn(H, B, T, generator=g).cuda()
+    ref = torch.relu(z + b[:, None, None])
+    hid, mask = ops.readout_bias_relu(z.clone(), b)
+    assert torch.equal(hid, ref)
+    gr, rowsum = ops.readout_bias_relu_backward(gy, mask)
+    want = gy * (z + b[:, None, None] > 0)
+    assert torch.equal(gr, want)
+    assert torch.allclose(rowsum.double(), want.double().sum(dim=2), rtol=1e-6, atol=1e-5)
