@@ -622,6 +622,43 @@ class ComplexReadout(nn.Module):
         return logits.mean(dim=2).t()  # (B, C)
 
 
+# Split of the sample reduction in the per-step output layer's weight
+# cotangent (batched GEMMs over this many sample chunks, then their sum);
+# 0: one GEMM over all samples.
+OUTPUT_GRAD_SPLITS = int(os.environ.get("RQF_B200_OUTPUT_GRAD_SPLITS", "64"))
+
+
+class _PerStepLogits(torch.autograd.Function):
+    """logits = W2 @ hid + b2 over the (H, N) samples of the per-step readout,
+    as torch.addmm; backward as addmm's, except that the weight cotangent
+    dl @ hid^T, a reduction over all N samples with only C x H outputs,
+    runs as OUTPUT_GRAD_SPLITS batched GEMMs over sample chunks and their sum
+    (one GEMM of depth N leaves most SMs idle)."""
+
+    @staticmethod
+    def forward(ctx, hid, W2, b2):
+        ctx.save_for_backward(hid, W2)
+        return torch.addmm(b2[:, None], W2, hid)
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, dl):
+        hid, W2 = ctx.saved_tensors
+        need = ctx.needs_input_grad
+        gh = W2.t() @ dl if need[0] else None
+        gW = None
+        if need[1]:
+            (C, N), H, S = dl.shape, hid.shape[0], OUTPUT_GRAD_SPLITS
+            if S > 1 and N % S == 0 and dl.is_contiguous() and hid.is_contiguous():
+                n = N // S
+                gW = torch.bmm(dl.view(C, S, n).transpose(0, 1),
+                               hid.view(H, S, n).permute(1, 2, 0)).sum(dim=0)
+            else:
+                gW = dl @ hid.t()
+        gb = dl.sum(dim=1) if need[2] else None
+        return gh, gW, gb
+
+
 class RQFClassifier(nn.Module):
     def __init__(self, encoder: PureRQFEncoderB200, num_classes: int, hidden_dims: int = 256):
         super().__init__()
@@ -642,8 +679,8 @@ class RQFClassifier(nn.Module):
         ro = self.readout
         if PROJECTION == "tc" and h.is_cuda:
             hid = _ReadoutHidden.apply(h, ro.fc1.weight, ro.fc1.bias)  # (H, B, T)
-            logits = torch.addmm(ro.fc2.bias[:, None], ro.fc2.weight,
-                                 hid.reshape(hid.shape[0], B * T))     # (C, B*T)
+            logits = _PerStepLogits.apply(hid.reshape(hid.shape[0], B * T), ro.fc2.weight,
+                                          ro.fc2.bias)                  # (C, B*T)
             return ops.per_step_cross_entropy(logits, y, B, T, label_smoothing)
         logits = ro(h, per_step=True)
         return torch.nn.functional.cross_entropy(
