@@ -34,6 +34,25 @@ def test_cpu_tensors_raise_no_fallback(fn, args):
         fn(*args)
 
 
+def test_per_step_cross_entropy_checks_its_arguments():
+    """The per-step loss refuses logits that do not match (classes,
+    batch*time) float32 or labels that are not (batch,) before any launch,
+    and CPU tensors with the no-fallback error."""
+    from prospective_rqf_b200 import ops
+
+    y = torch.zeros(2, dtype=torch.int64)
+    with pytest.raises(ValueError):
+        ops.per_step_cross_entropy(torch.zeros(5, 7), y, 2, 4)            # 7 != 2 * 4
+    with pytest.raises(ValueError):
+        ops.per_step_cross_entropy(torch.zeros(5, 8, dtype=torch.float64), y, 2, 4)
+    with pytest.raises(ValueError):
+        ops.per_step_cross_entropy(torch.zeros(5, 8), torch.zeros(3, dtype=torch.int64), 2, 4)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        ops.per_step_cross_entropy(torch.zeros(5, 8), y, 2, 4)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        ops.readout_bias_relu(torch.zeros(2, 2, 8), None)
+
+
 def test_tbptt_rejects_bad_arguments():
     with pytest.raises(ValueError):
         rqf.tbptt1_two_tap_scan(c(2, 5, 3), c(3), c(3), c(3), layout="tbf")
